@@ -1,0 +1,163 @@
+// Shared device helpers for the sm_100a eviction kernels: error words,
+// bounded mbarrier waits, bulk-tensor (TMA) loads, ldmatrix and the
+// m16n8k16 bf16 tensor-core step used by the decode kernel.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include "../../include/ce_api.h"
+
+namespace ce {
+
+// A device wait that has not completed after this many nanoseconds of
+// %globaltimer gives up, flags CE_EW_TIMEOUT and lets the kernel return.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ void flag_error(int32_t* err, int bits) {
+  if (err) atomicOr(err, bits);
+}
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier ---------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase.  Returns false (and flags the error
+// word) when the phase did not complete within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      flag_error(err, CE_EW_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// ---- TMA: 2D tiled bulk-tensor load into shared memory, no multicast --------
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int32_t x,
+                                            int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// ---- warp-level tensor-core helpers ------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                              uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D += A(16x16, rows 8..15 zero) * B(16x8); a1/a3 (the zero rows) are passed
+// as 0 so only the upper half of the tile carries query heads.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                          uint32_t b1) {
+  const uint32_t z = 0u;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Split two fp32 values into bf16 hi parts and bf16 residuals so that
+// hi + lo reproduces each value to ~2^-17 relative.
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  float2 hf = __bfloat1622float2(h);
+  __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  hi = *reinterpret_cast<uint32_t*>(&h);
+  lo = *reinterpret_cast<uint32_t*>(&l);
+}
+
+// ---- order-preserving integer keys for fp scores ------------------------------
+// Larger float -> larger unsigned key.  -0.0 is folded onto +0.0 (the reference
+// compares doubles, where they are equal) and NaN maps to the largest key.
+__device__ __forceinline__ uint64_t key_from_f32(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) == 0u) u = 0u;
+  if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return 0xffffffffull;
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return static_cast<uint64_t>(u);
+}
+
+__device__ __forceinline__ uint64_t key_from_f64(double d) {
+  uint64_t u = static_cast<uint64_t>(__double_as_longlong(d));
+  if ((u & 0x7fffffffffffffffull) == 0ull) u = 0ull;
+  if ((u & 0x7ff0000000000000ull) == 0x7ff0000000000000ull && (u & 0x000fffffffffffffull))
+    return 0xffffffffffffffffull;
+  return (u & 0x8000000000000000ull) ? ~u : (u | 0x8000000000000000ull);
+}
+
+// splitmix64 of (seed, layer, kv head, position) as in the reference's
+// reservoir_scores (runtime:358-373) and core.reservoir_score (core.py:23-30);
+// returns the top 53 bits (the double is this integer / 2^53).
+__device__ __forceinline__ uint64_t reservoir53(uint64_t seed, uint64_t layer, uint64_t head,
+                                                uint64_t pos) {
+  uint64_t x = pos * 0x9E3779B97F4A7C15ull + layer * 0xBF58476D1CE4E5B9ull +
+               head * 0x94D049BB133111EBull + seed * 0xD1B54A32D192ED03ull +
+               0x632BE59BD9B4E019ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  x = x ^ (x >> 31);
+  return x >> 11;
+}
+
+}  // namespace ce

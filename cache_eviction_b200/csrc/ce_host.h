@@ -1,0 +1,35 @@
+// Host-side helpers shared by the C-ABI entry points (no device code).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ce {
+namespace host {
+
+// Records a message for ce_status_string's companion ce_last_error and
+// returns `status` unchanged.
+int fail(int status, const char* msg);
+// Message of the last failing entry point on this host thread.
+const char* last_error();
+// Records the pending CUDA error text and returns CE_ERR_CUDA.
+int fail_cuda(const char* where);
+
+// Multiprocessor count of the current device (cached per device).
+int sm_count();
+
+// Raise a kernel's dynamic shared-memory limit once per device.
+bool set_smem_attr(const void* func, int bytes);
+template <class F>
+bool set_smem(F* func, int bytes) {
+  return set_smem_attr(reinterpret_cast<const void*>(func), bytes);
+}
+
+// 2D bf16 tensor map over `rows` rows of `cols` elements (dense), box
+// {cols, box_rows}, 128-byte swizzle, zero fill out of bounds.
+bool encode_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint32_t cols,
+                     uint32_t box_rows);
+
+}  // namespace host
+}  // namespace ce

@@ -1,0 +1,1076 @@
+// K2 (selection) and K3 (compaction) for sm_100a.
+//
+// Selection follows the reference's choose (code/cache_eviction/sglang_evict_runtime.py:376-397):
+// positions below the prefix, in the recent window or at/after the
+// sliding-window cursor are protected; the rest of the budget goes to the
+// largest keys, ties to the newer (larger) position; prefix_sliding keeps only
+// the protected set.  Instead of two argsorts per (layer, KV head) each CTA runs
+// an MSB-first 8-bit radix select on order-preserving integer keys (fp32 scores,
+// fp64 uniforms and 53-bit reservoir draws all map to unsigned integers with the
+// same order, and -0.0 folds onto +0.0 as in the reference's double compare),
+// then breaks the remaining tie with a second radix select on position.  The
+// kept set is written in ascending position order by ranking positions in a
+// shared-memory bitmap (rank = popcount prefix), which is the order _boundary
+// needs (runtime:442-446).
+//
+// Compaction follows _boundary (runtime:415-507): every head's j-th middle
+// survivor moves to the j-th non-protected candidate unit (column order).  A
+// source unit that is also some other item's target is a hazard; those sources
+// are staged in a scratch buffer by one launch and every item is written by the
+// next launch, which reproduces the reference's "gather all sources, then
+// scatter" semantics without copying the non-hazard items twice.
+#include <algorithm>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include "ce_common.cuh"
+#include "ce_host.h"
+
+namespace ce {
+namespace sel {
+
+constexpr int T = 512;
+constexpr int NW = T / 32;
+
+struct Sh {
+  int hist[256];
+  int red[NW];
+  int bc[8];
+};
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ int block_sum(int v, Sh& sh) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) sh.red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    int x = (threadIdx.x < NW) ? sh.red[threadIdx.x] : 0;
+    x = warp_sum(x);
+    if (threadIdx.x == 0) sh.bc[7] = x;
+  }
+  __syncthreads();
+  const int r = sh.bc[7];
+  __syncthreads();
+  return r;
+}
+
+// Exclusive block scan; `total` receives the block sum.
+__device__ int block_excl(int v, Sh& sh, int& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) sh.red[w] = x;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int a = (threadIdx.x < NW) ? sh.red[threadIdx.x] : 0;
+    int s = a;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (threadIdx.x >= o) s += y;
+    }
+    if (threadIdx.x < NW) sh.red[threadIdx.x] = s - a;
+    if (threadIdx.x == 31) sh.bc[6] = s;
+  }
+  __syncthreads();
+  const int r = sh.red[w] + x - v;
+  total = sh.bc[6];
+  __syncthreads();
+  return r;
+}
+
+// hist[256] holds digit counts.  Find d with sum(hist[>d]) < krem <= sum(hist[>=d]);
+// sh.bc[0] = d, bc[1] = sum(hist[>d]), bc[2] = hist[d].
+__device__ void find_digit(Sh& sh, int krem) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int c[8];
+    int s = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      c[q] = sh.hist[255 - 8 * lane - q];
+      s += c[q];
+    }
+    int incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int excl = incl - s;
+    if (excl < krem && krem <= incl) {
+      int run = excl;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (run + c[q] >= krem) {
+          sh.bc[0] = 255 - 8 * lane - q;
+          sh.bc[1] = run;
+          sh.bc[2] = c[q];
+          break;
+        }
+        run += c[q];
+      }
+    }
+  }
+  __syncthreads();
+}
+
+struct Thresh {
+  uint64_t key;
+  int pos;
+  bool none;  // k == 0: nothing selected
+};
+
+// Threshold of the k largest (key, pos) pairs among unprotected columns.
+// pv[c] < 0 marks a protected column; pv[c] & 0x7fffffff is the position.
+__device__ Thresh radix_threshold(const uint64_t* kv, const int32_t* pv, int N, int k,
+                                  int nonprot, int key_bits, Sh& sh) {
+  Thresh th{0ull, 0, false};
+  if (k <= 0) {
+    th.none = true;
+    return th;
+  }
+  if (k >= nonprot) return th;  // everything unprotected is kept
+  uint64_t prefix = 0, mask = 0;
+  int krem = k, eq = 0;
+  for (int shift = key_bits - 8; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += T) sh.hist[i] = 0;
+    __syncthreads();
+    for (int c = threadIdx.x; c < N; c += T) {
+      if (pv[c] < 0) continue;
+      const uint64_t key = kv[c];
+      if ((key & mask) == prefix) atomicAdd(&sh.hist[(key >> shift) & 255], 1);
+    }
+    __syncthreads();
+    find_digit(sh, krem);
+    const int d = sh.bc[0];
+    krem -= sh.bc[1];
+    eq = sh.bc[2];
+    prefix |= static_cast<uint64_t>(d) << shift;
+    mask |= static_cast<uint64_t>(255) << shift;
+  }
+  th.key = prefix;
+  if (krem < eq) {
+    // Among equal keys keep the krem newest positions.
+    int pp = 0, pm = 0, kr = krem;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < 256; i += T) sh.hist[i] = 0;
+      __syncthreads();
+      for (int c = threadIdx.x; c < N; c += T) {
+        const int pc = pv[c];
+        if (pc < 0 || kv[c] != prefix) continue;
+        if ((pc & pm) == pp) atomicAdd(&sh.hist[(pc >> shift) & 255], 1);
+      }
+      __syncthreads();
+      find_digit(sh, kr);
+      kr -= sh.bc[1];
+      pp |= sh.bc[0] << shift;
+      pm |= 255 << shift;
+    }
+    th.pos = pp;
+  }
+  __syncthreads();
+  return th;
+}
+
+__device__ __forceinline__ bool selected(const Thresh& th, uint64_t key, int pc) {
+  if (th.none || pc < 0) return false;
+  return key > th.key || (key == th.key && pc >= th.pos);
+}
+
+// Rank every column whose posf(c) >= 0 by ascending position using a bitmap
+// of nw words, then call emit(rank, c, pos).  Positions must be < 32*nw.
+template <class PosF, class EmitF>
+__device__ void emit_sorted(int N, int nw, uint32_t* bits, int* pre, PosF posf, EmitF emit, Sh& sh,
+                            int32_t* err) {
+  for (int w = threadIdx.x; w < nw; w += T) bits[w] = 0u;
+  __syncthreads();
+  for (int c = threadIdx.x; c < N; c += T) {
+    const int p = posf(c);
+    if (p < 0) continue;
+    if (p >= 32 * nw) {
+      flag_error(err, CE_EW_SHAPE);
+      continue;
+    }
+    atomicOr(&bits[p >> 5], 1u << (p & 31));
+  }
+  __syncthreads();
+  int carry = 0;
+  for (int base = 0; base < nw; base += T) {
+    const int w = base + threadIdx.x;
+    const int v = (w < nw) ? __popc(bits[w]) : 0;
+    int tot;
+    const int ex = block_excl(v, sh, tot);
+    if (w < nw) pre[w] = carry + ex;
+    carry += tot;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < N; c += T) {
+    const int p = posf(c);
+    if (p < 0 || p >= 32 * nw) continue;
+    const int rank = pre[p >> 5] + __popc(bits[p >> 5] & ((1u << (p & 31)) - 1u));
+    emit(rank, c, p);
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ bool is_prot(int pos, const ce_row_params& q) {
+  return pos < q.prefix || pos >= q.n - q.recent || (q.cursor >= 0 && pos >= q.cursor);
+}
+
+__device__ __forceinline__ int key_bits_of(int policy, int score_dtype) {
+  if (policy == CE_POLICY_RESERVOIR) return 64;
+  if (policy == CE_POLICY_RANDOM) return score_dtype == CE_DTYPE_F64 ? 64 : 32;
+  return 32;
+}
+
+// ============================== ce_choose ========================================
+struct ChooseParams {
+  const int32_t* pos;
+  const int32_t* ncols;
+  int n_cols;
+  const void* score;
+  int sdt;
+  const ce_row_params* params;
+  int problems, layers, heads, head_offset, nw;
+  int32_t* kept;
+  int kept_stride;
+  int32_t* status;
+  int32_t* pcount;
+  uint64_t* kv;
+  int32_t* pv;
+  int32_t* seg_info;
+  int32_t* err;
+};
+
+__device__ __forceinline__ float score_f(const void* s, int dt, int64_t idx) {
+  return dt == CE_DTYPE_F64 ? static_cast<float>(static_cast<const double*>(s)[idx])
+                            : static_cast<const float*>(s)[idx];
+}
+
+__global__ void __launch_bounds__(T) choose_seg_kernel(const ChooseParams p) {
+  extern __shared__ uint32_t dyn[];
+  __shared__ Sh sh;
+  const int segs = p.layers * p.heads;
+  const int i = blockIdx.x / segs, s = blockIdx.x % segs;
+  const int l = s / p.heads, g = s % p.heads;
+  const ce_row_params q = p.params[i];
+  const int N = p.ncols ? min(p.ncols[i], p.n_cols) : p.n_cols;
+  const int64_t base = (static_cast<int64_t>(i) * segs + s) * p.n_cols;
+  uint64_t* kv = p.kv + base;
+  int32_t* pv = p.pv + base;
+  int np = 0;
+  for (int c = threadIdx.x; c < N; c += T) {
+    const int pos = p.pos[base + c];
+    const bool pr = is_prot(pos, q);
+    pv[c] = pos | (pr ? static_cast<int>(0x80000000u) : 0);
+    np += pr;
+    if (pr) continue;
+    uint64_t key = 0;
+    switch (q.policy) {
+      case CE_POLICY_RESERVOIR:
+        key = reservoir53(q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
+        break;
+      case CE_POLICY_H2O_GLOBAL:
+        if (p.sdt == CE_DTYPE_F64) {
+          double acc = 0.0;
+          for (int gg = 0; gg < p.heads; ++gg)
+            acc += static_cast<const double*>(p.score)[(static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c];
+          key = key_from_f64(acc);
+        } else {
+          float acc = 0.f;
+          for (int gg = 0; gg < p.heads; ++gg)
+            acc += static_cast<const float*>(p.score)[(static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c];
+          key = key_from_f32(acc);
+        }
+        break;
+      case CE_POLICY_PREFIX_SLIDING:
+        break;
+      default:
+        key = (p.sdt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.score)[base + c])
+                                      : key_from_f32(static_cast<const float*>(p.score)[base + c]);
+    }
+    kv[c] = key;
+  }
+  const int nprot = block_sum(np, sh);
+  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * segs + s] = nprot;
+  if (nprot > q.budget) return;
+  int k = (q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : q.budget - nprot;
+  const int nonprot = N - nprot;
+  int bits = (q.policy == CE_POLICY_H2O_GLOBAL || q.policy == CE_POLICY_HEAD_SUM ||
+              q.policy == CE_POLICY_HEAD_MAX || q.policy == CE_POLICY_RANDOM)
+                 ? (p.sdt == CE_DTYPE_F64 ? 64 : 32)
+                 : 64;
+  const Thresh th = radix_threshold(kv, pv, N, k, nonprot, bits, sh);
+  int32_t* out = p.kept + (static_cast<int64_t>(i) * segs + s) * p.kept_stride;
+  uint32_t* bitsm = dyn;
+  int* pre = reinterpret_cast<int*>(dyn + p.nw);
+  const int stride = p.kept_stride;
+  int32_t* err = p.err;
+  emit_sorted(
+      N, p.nw, bitsm, pre,
+      [&](int c) -> int {
+        const int pc = pv[c];
+        if (pc < 0) return pc & 0x7fffffff;
+        return selected(th, kv[c], pc) ? pc : -1;
+      },
+      [&](int rank, int c, int) {
+        if (rank < stride) out[rank] = c;
+        else flag_error(err, CE_EW_CAPACITY);
+      },
+      sh, p.err);
+}
+
+__global__ void choose_status_kernel(const ChooseParams p) {
+  const int i = blockIdx.x;
+  const int segs = p.layers * p.heads;
+  if (threadIdx.x != 0) return;
+  const ce_row_params q = p.params[i];
+  const int n0 = p.seg_info[static_cast<int64_t>(i) * segs];
+  int st = 0;
+  for (int s = 1; s < segs; ++s)
+    if (p.seg_info[static_cast<int64_t>(i) * segs + s] != n0) st = 3;
+  if (st == 0 && n0 > q.budget) st = 2;
+  if (st == 3) flag_error(p.err, CE_EW_PROTECTED);
+  p.status[i] = st;
+  if (p.pcount) p.pcount[i] = n0;
+}
+
+// ============================== ce_boundary ======================================
+struct BParams {
+  int32_t* table;
+  int64_t ts;
+  int table_width;
+  int32_t* r2u;
+  int64_t rs;
+  int r2u_width;
+  int32_t* frontier;
+  int32_t* count;
+  int32_t* pos;
+  int64_t prs;
+  int pos_cap;
+  float* scores;
+  int64_t sls, shs, pool_units;
+  const uint64_t* k_layers;
+  const uint64_t* v_layers;
+  int L, G, P, head_offset;
+  int32_t* marks;
+  int epoch;
+  const int64_t* swa;
+  const int32_t* rows;
+  const ce_row_params* params;
+  int R;
+  const void* uniforms;
+  int udt;
+  const float* gscores;
+  int GH;
+  int live, max_cols, nw;
+  // workspace
+  uint64_t* kv;
+  int32_t* pv;
+  int32_t* seg_info;   // [R*L*G]
+  int32_t* mid_col;    // [R*L*G*max_cols]
+  int32_t* src_unit;
+  int32_t* new_pos;
+  float* score_scr;
+  int32_t* row_info;   // [R*8]: N, nprot, W, after, true_u, nleft, -, status
+  int32_t* cand_rank;  // [R*max_cols]
+  int32_t* new_table;  // [R*max_cols]
+  uint8_t* hazard;
+  int32_t* freed;
+  int64_t freed_stride;
+  int32_t* result;
+  int32_t* err;
+};
+
+struct RowCtx {
+  int row, cnt, fr, N;
+  ce_row_params q;
+};
+
+__device__ __forceinline__ RowCtx row_ctx(const BParams& p, int i) {
+  RowCtx r;
+  r.row = p.rows[i];
+  r.q = p.params[i];
+  r.cnt = p.count[r.row];
+  r.fr = p.frontier[r.row];
+  r.N = r.cnt + (r.q.n - r.fr);
+  return r;
+}
+
+__device__ __forceinline__ bool row_shape_ok(const BParams& p, const RowCtx& r) {
+  return r.cnt >= 0 && r.fr >= 0 && r.fr <= r.q.n && r.N >= 0 && r.N <= p.max_cols &&
+         r.q.n <= 32 * p.nw && r.q.n <= p.r2u_width && r.cnt <= p.pos_cap;
+}
+
+__device__ __forceinline__ int col_unit(const BParams& p, const RowCtx& r, int c) {
+  return c < r.cnt ? p.table[r.row * p.ts + c] : p.r2u[r.row * p.rs + r.fr + (c - r.cnt)];
+}
+
+__device__ __forceinline__ int col_pos(const BParams& p, const RowCtx& r, int lg, int c) {
+  return c < r.cnt ? p.pos[r.row * p.prs + static_cast<int64_t>(lg) * p.pos_cap + c]
+                   : r.fr + (c - r.cnt);
+}
+
+__device__ __forceinline__ float unit_score(const BParams& p, int l, int g, int unit) {
+  if (unit < 0 || unit >= p.pool_units) return 0.f;
+  return p.scores[l * p.sls + g * p.shs + unit];
+}
+
+// Segment blocks: R*L*G of them, then R row blocks.
+__global__ void __launch_bounds__(T) bsel_kernel(const BParams p) {
+  extern __shared__ uint32_t dyn[];
+  __shared__ Sh sh;
+  uint32_t* bitsm = dyn;
+  int* pre = reinterpret_cast<int*>(dyn + p.nw);
+  const int LG = p.L * p.G;
+  const int nseg = p.R * LG;
+  if (static_cast<int>(blockIdx.x) < nseg) {
+    const int i = blockIdx.x / LG, lg = blockIdx.x % LG;
+    const int l = lg / p.G, g = lg % p.G;
+    const RowCtx r = row_ctx(p, i);
+    if (!row_shape_ok(p, r) || r.N <= r.q.budget) return;
+    const int64_t base = (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
+    uint64_t* kv = p.kv + base;
+    int32_t* pv = p.pv + base;
+    int np = 0;
+    for (int c = threadIdx.x; c < r.N; c += T) {
+      const int pos = col_pos(p, r, lg, c);
+      const bool pr = is_prot(pos, r.q);
+      pv[c] = pos | (pr ? static_cast<int>(0x80000000u) : 0);
+      np += pr;
+      if (pr) continue;
+      uint64_t key = 0;
+      switch (r.q.policy) {
+        case CE_POLICY_RANDOM: {
+          const int64_t ui = (static_cast<int64_t>(i) * LG + lg) * p.max_cols + c;
+          key = (p.udt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.uniforms)[ui])
+                                        : key_from_f32(static_cast<const float*>(p.uniforms)[ui]);
+          break;
+        }
+        case CE_POLICY_RESERVOIR:
+          key = reservoir53(r.q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
+          break;
+        case CE_POLICY_HEAD_SUM:
+        case CE_POLICY_HEAD_MAX:
+          key = key_from_f32(unit_score(p, l, g, col_unit(p, r, c)));
+          break;
+        case CE_POLICY_H2O_GLOBAL: {
+          float acc = 0.f;
+          if (p.gscores) {
+            for (int gg = 0; gg < p.GH; ++gg)
+              acc += p.gscores[((static_cast<int64_t>(i) * p.L + l) * p.GH + gg) * p.max_cols + c];
+          } else {
+            const int u = col_unit(p, r, c);
+            for (int gg = 0; gg < p.G; ++gg) acc += unit_score(p, l, gg, u);
+          }
+          key = key_from_f32(acc);
+          break;
+        }
+        default:
+          break;
+      }
+      kv[c] = key;
+    }
+    const int nprot = block_sum(np, sh);
+    if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
+    if (nprot > r.q.budget) return;
+    const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
+    const int bits = key_bits_of(r.q.policy, p.udt);
+    const Thresh th = radix_threshold(kv, pv, r.N, k, r.N - nprot, bits, sh);
+    int32_t* mid = p.mid_col + base;
+    int32_t* npos = p.new_pos + base;
+    int32_t* srcu = p.src_unit + base;
+    float* ssc = p.score_scr + base;
+    const int max_cols = p.max_cols;
+    // Middle survivors in ascending position.
+    emit_sorted(
+        r.N, p.nw, bitsm, pre,
+        [&](int c) -> int {
+          const int pc = pv[c];
+          return selected(th, kv[c], pc) ? pc : -1;
+        },
+        [&](int rank, int c, int pos) {
+          if (nprot + rank >= max_cols) return;
+          mid[rank] = c;
+          npos[nprot + rank] = pos;
+          const int u = col_unit(p, r, c);
+          srcu[rank] = u;
+          ssc[rank] = unit_score(p, l, g, u);
+        },
+        sh, p.err);
+    // Protected part: this head's positions at the (0,0) head's protected
+    // columns taken in (0,0) position order (runtime:442-443,469).
+    emit_sorted(
+        r.N, p.nw, bitsm, pre,
+        [&](int c) -> int {
+          const int p00 = col_pos(p, r, 0, c);
+          return is_prot(p00, r.q) ? p00 : -1;
+        },
+        [&](int rank, int c, int) {
+          if (rank < max_cols) npos[rank] = col_pos(p, r, lg, c);
+        },
+        sh, p.err);
+  } else {
+    // ---------------- row block: table, candidates, leftovers, marks -----------
+    const int i = blockIdx.x - nseg;
+    const RowCtx r = row_ctx(p, i);
+    int32_t* info = p.row_info + i * 8;
+    if (!row_shape_ok(p, r) || r.N <= r.q.budget) return;
+    int np = 0;
+    for (int c = threadIdx.x; c < r.N; c += T) np += is_prot(col_pos(p, r, 0, c), r.q);
+    const int nprot = block_sum(np, sh);
+    if (nprot > r.q.budget) {
+      if (threadIdx.x == 0) info[1] = nprot;
+      return;
+    }
+    const int W = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
+    int32_t* ntab = p.new_table + static_cast<int64_t>(i) * p.max_cols;
+    int32_t* crank = p.cand_rank + static_cast<int64_t>(i) * p.max_cols;
+    emit_sorted(
+        r.N, p.nw, bitsm, pre,
+        [&](int c) -> int {
+          const int p00 = col_pos(p, r, 0, c);
+          return is_prot(p00, r.q) ? p00 : -1;
+        },
+        [&](int rank, int c, int) { ntab[rank] = col_unit(p, r, c); }, sh, p.err);
+    int carry = 0;
+    for (int b0 = 0; b0 < r.N; b0 += T) {
+      const int c = b0 + threadIdx.x;
+      const bool in = c < r.N;
+      const bool cand = in && !is_prot(col_pos(p, r, 0, c), r.q);
+      int tot;
+      const int ex = block_excl(cand ? 1 : 0, sh, tot);
+      if (in) {
+        if (cand) {
+          const int cr = carry + ex;
+          crank[c] = cr;
+          if (cr < W)
+            ntab[nprot + cr] = col_unit(p, r, c);
+          else if (p.live)
+            p.freed[i * p.freed_stride + (cr - W)] = col_unit(p, r, c);
+        } else {
+          crank[c] = -1;
+        }
+      }
+      carry += tot;
+    }
+    const int true_u = min(r.q.n - r.q.recent, r.q.cursor >= 0 ? r.q.cursor : r.q.n);
+    if (p.live) {
+      for (int x = max(true_u, 0) + threadIdx.x; x < r.q.n; x += T) {
+        const int u = p.r2u[r.row * p.rs + x];
+        if (u >= 0 && u < p.pool_units) p.marks[u] = p.epoch;
+      }
+    }
+    if (threadIdx.x == 0) {
+      info[0] = r.N;
+      info[1] = nprot;
+      info[2] = W;
+      info[3] = nprot + W;
+      info[4] = true_u;
+      info[5] = r.N - nprot - W;
+    }
+  }
+}
+
+__global__ void bvalidate_kernel(const BParams p) {
+  const int i = blockIdx.x;
+  if (threadIdx.x != 0) return;
+  const RowCtx r = row_ctx(p, i);
+  const int LG = p.L * p.G;
+  int32_t* info = p.row_info + i * 8;
+  int st;
+  int after = r.N;
+  if (!row_shape_ok(p, r)) {
+    st = 6;
+    flag_error(p.err, CE_EW_SHAPE);
+  } else if (r.N <= r.q.budget) {
+    st = 1;
+  } else {
+    const int n0 = info[1];
+    st = 0;
+    for (int s = 0; s < LG; ++s)
+      if (p.seg_info[static_cast<int64_t>(i) * LG + s] != n0) st = 3;
+    if (st == 3) {
+      flag_error(p.err, CE_EW_PROTECTED);
+    } else if (n0 > r.q.budget) {
+      st = 2;
+    } else {
+      after = info[3];
+      if (after > p.table_width || after > p.pos_cap) {
+        st = 6;
+        flag_error(p.err, CE_EW_CAPACITY);
+      }
+    }
+  }
+  info[7] = st;
+  int32_t* res = p.result + i * 4;
+  res[0] = st;
+  res[1] = r.N;
+  res[2] = (st == 0) ? after : r.N;
+  res[3] = 0;
+}
+
+// One warp per (row, layer-in-group, head, j) item.
+struct Item {
+  int i, l, g, j;
+  int64_t base;   // segment base in the [R, L, G, max_cols] arrays
+};
+
+__device__ __forceinline__ bool decode_item(const BParams& p, int64_t item, int l0, int nl, Item& it) {
+  const int64_t per_row = static_cast<int64_t>(nl) * p.G * p.max_cols;
+  it.i = static_cast<int>(item / per_row);
+  int64_t rem = item % per_row;
+  const int ll = static_cast<int>(rem / (static_cast<int64_t>(p.G) * p.max_cols));
+  rem %= static_cast<int64_t>(p.G) * p.max_cols;
+  it.g = static_cast<int>(rem / p.max_cols);
+  it.j = static_cast<int>(rem % p.max_cols);
+  it.l = l0 + ll;
+  it.base = (static_cast<int64_t>(it.i) * p.L * p.G + static_cast<int64_t>(it.l) * p.G + it.g) * p.max_cols;
+  const int32_t* info = p.row_info + it.i * 8;
+  return info[7] == 0 && it.j < info[2];
+}
+
+__device__ __forceinline__ bool is_hazard(const BParams& p, const Item& it, int W) {
+  const int col = p.mid_col[it.base + it.j];
+  const int cr = p.cand_rank[static_cast<int64_t>(it.i) * p.max_cols + col];
+  return cr >= 0 && cr < W && cr != it.j;
+}
+
+__device__ __forceinline__ uint8_t* unit_ptr(const uint64_t* layers, int l, int unit, int g, int G,
+                                             int P) {
+  return reinterpret_cast<uint8_t*>(layers[l]) +
+         (static_cast<int64_t>(unit) * G + g) * static_cast<int64_t>(P) * 128;
+}
+
+__device__ __forceinline__ void copy_block(uint8_t* dst, const uint8_t* src, int bytes, int lane) {
+  for (int o = lane * 16; o < bytes; o += 32 * 16)
+    *reinterpret_cast<uint4*>(dst + o) = *reinterpret_cast<const uint4*>(src + o);
+}
+
+__global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int l0, int nl) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nitems = static_cast<int64_t>(p.R) * nl * p.G * p.max_cols;
+  const int bytes = p.P * 128;
+  for (int64_t item = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; item < nitems;
+       item += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    Item it;
+    if (!decode_item(p, item, l0, nl, it)) continue;
+    const int W = p.row_info[it.i * 8 + 2];
+    if (!is_hazard(p, it, W)) continue;
+    const int src = p.src_unit[it.base + it.j];
+    if (src < 0 || src >= p.pool_units) {
+      if (lane == 0) flag_error(p.err, CE_EW_INDEX);
+      continue;
+    }
+    uint8_t* scr = p.hazard + item * 2 * bytes;
+    copy_block(scr, unit_ptr(p.k_layers, it.l, src, it.g, p.G, p.P), bytes, lane);
+    copy_block(scr + bytes, unit_ptr(p.v_layers, it.l, src, it.g, p.G, p.P), bytes, lane);
+  }
+}
+
+__global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int l0, int nl) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nitems = static_cast<int64_t>(p.R) * nl * p.G * p.max_cols;
+  const int bytes = p.P * 128;
+  for (int64_t item = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; item < nitems;
+       item += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    Item it;
+    if (!decode_item(p, item, l0, nl, it)) continue;
+    const int32_t* info = p.row_info + it.i * 8;
+    const int W = info[2], nprot = info[1];
+    const int dst = p.new_table[static_cast<int64_t>(it.i) * p.max_cols + nprot + it.j];
+    const int src = p.src_unit[it.base + it.j];
+    if (dst < 0 || dst >= p.pool_units || src < 0 || src >= p.pool_units) {
+      if (lane == 0) flag_error(p.err, CE_EW_INDEX);
+      continue;
+    }
+    if (lane == 0) p.scores[it.l * p.sls + it.g * p.shs + dst] = p.score_scr[it.base + it.j];
+    if (src == dst) continue;
+    const bool hz = is_hazard(p, it, W);
+    const uint8_t* ks = hz ? p.hazard + item * 2 * bytes : unit_ptr(p.k_layers, it.l, src, it.g, p.G, p.P);
+    const uint8_t* vs = hz ? p.hazard + item * 2 * bytes + bytes
+                           : unit_ptr(p.v_layers, it.l, src, it.g, p.G, p.P);
+    copy_block(unit_ptr(p.k_layers, it.l, dst, it.g, p.G, p.P), ks, bytes, lane);
+    copy_block(unit_ptr(p.v_layers, it.l, dst, it.g, p.G, p.P), vs, bytes, lane);
+  }
+}
+
+__global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
+  __shared__ Sh sh;
+  __shared__ int bad;
+  const int i = blockIdx.x;
+  const int32_t* info = p.row_info + i * 8;
+  if (info[7] != 0) return;
+  const RowCtx r = row_ctx(p, i);
+  const int nprot = info[1], after = info[3], true_u = info[4], nleft = info[5];
+  const int LG = p.L * p.G;
+  const int32_t* ntab = p.new_table + static_cast<int64_t>(i) * p.max_cols;
+  for (int k = threadIdx.x; k < after; k += T) p.table[r.row * p.ts + k] = ntab[k];
+  for (int lg = 0; lg < LG; ++lg) {
+    const int32_t* src = p.new_pos + (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
+    int32_t* dst = p.pos + r.row * p.prs + static_cast<int64_t>(lg) * p.pos_cap;
+    for (int k = threadIdx.x; k < after; k += T) dst[k] = src[k];
+  }
+  if (threadIdx.x == 0) {
+    p.count[r.row] = after;
+    p.frontier[r.row] = r.q.n;
+    bad = 0;
+  }
+  int32_t* res = p.result + i * 4;
+  __syncthreads();
+  if (!p.live) {
+    if (threadIdx.x == 0) res[3] = 0;
+    return;
+  }
+  const int32_t* left = p.freed + i * p.freed_stride;
+  if (p.swa) {
+    for (int k = threadIdx.x; k < nleft; k += T) {
+      const int u = left[k];
+      if (u >= 0 && u < p.pool_units && p.swa[u] != 0) bad = 1;
+    }
+    __syncthreads();
+    if (bad) {
+      if (threadIdx.x == 0) {
+        res[0] = 5;
+        flag_error(p.err, CE_EW_SWA);
+      }
+      return;
+    }
+  }
+  for (int k = threadIdx.x; k < nleft; k += T) {
+    const int u = left[k];
+    if (u < 0 || u >= p.pool_units) continue;
+    for (int l = 0; l < p.L; ++l)
+      for (int g = 0; g < p.G; ++g) p.scores[l * p.sls + g * p.shs + u] = 0.f;
+  }
+  if (threadIdx.x == 0) res[3] = nleft;
+  // Pack every owned unit that is not a real slot of [true_u, n) at the row start.
+  int np = 0;
+  for (int k = threadIdx.x; k < after; k += T) {
+    const int u = ntab[k];
+    np += !(u >= 0 && u < p.pool_units && p.marks[u] == p.epoch);
+  }
+  const int npacked = block_sum(np, sh);
+  if (npacked > true_u) {
+    if (threadIdx.x == 0) {
+      res[0] = 4;
+      flag_error(p.err, CE_EW_PACK);
+    }
+    return;
+  }
+  int32_t* rrow = p.r2u + r.row * p.rs;
+  int carry = 0;
+  for (int b0 = 0; b0 < after; b0 += T) {
+    const int k = b0 + threadIdx.x;
+    const int u = (k < after) ? ntab[k] : 0;
+    const bool keep = k < after && !(u >= 0 && u < p.pool_units && p.marks[u] == p.epoch);
+    int tot;
+    const int ex = block_excl(keep ? 1 : 0, sh, tot);
+    if (keep) rrow[carry + ex] = u;
+    carry += tot;
+  }
+  for (int x = npacked + threadIdx.x; x < min(true_u, p.r2u_width); x += T) rrow[x] = 0;
+  (void)nprot;
+}
+
+__global__ void gather_scores_kernel(const BParams p, float* out) {
+  const int LG = p.L * p.G;
+  const int i = blockIdx.x / LG, lg = blockIdx.x % LG;
+  const int l = lg / p.G, g = lg % p.G;
+  const RowCtx r = row_ctx(p, i);
+  float* o = out + (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
+  const int N = (r.N >= 0 && r.N <= p.max_cols) ? r.N : 0;
+  for (int c = threadIdx.x; c < p.max_cols; c += blockDim.x)
+    o[c] = (c < N) ? unit_score(p, l, g, col_unit(p, r, c)) : 0.f;
+}
+
+__global__ void reservoir_kernel(const int32_t* pos, int layers, int heads, int n_cols,
+                                 int head_offset, uint64_t seed, uint64_t* out) {
+  const int64_t total = static_cast<int64_t>(layers) * heads * n_cols;
+  for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total;
+       x += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int l = static_cast<int>(x / (static_cast<int64_t>(heads) * n_cols));
+    const int g = static_cast<int>((x / n_cols) % heads);
+    out[x] = reservoir53(seed, l, head_offset + g, static_cast<uint64_t>(pos[x]));
+  }
+}
+
+}  // namespace sel
+}  // namespace ce
+
+using namespace ce;
+using namespace ce::sel;
+
+namespace {
+size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct BLayout {
+  size_t kv, pv, seg, mid, src, npos, ssc, info, crank, ntab, hazard, total;
+};
+
+BLayout boundary_layout(int R, int L, int G, int max_cols, int64_t hazard_bytes) {
+  BLayout b{};
+  const size_t cells = static_cast<size_t>(R) * L * G * max_cols;
+  size_t o = 0;
+  b.kv = o; o += a256(cells * 8);
+  b.pv = o; o += a256(cells * 4);
+  b.seg = o; o += a256(static_cast<size_t>(R) * L * G * 4);
+  b.mid = o; o += a256(cells * 4);
+  b.src = o; o += a256(cells * 4);
+  b.npos = o; o += a256(cells * 4);
+  b.ssc = o; o += a256(cells * 4);
+  b.info = o; o += a256(static_cast<size_t>(R) * 8 * 4);
+  b.crank = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
+  b.ntab = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
+  b.hazard = o; o += a256(static_cast<size_t>(hazard_bytes));
+  b.total = o;
+  return b;
+}
+
+int64_t hazard_per_layer(int R, int G, int max_cols, int P) {
+  return static_cast<int64_t>(R) * G * max_cols * 2 * P * 128;
+}
+
+int sel_smem(int nw) { return nw * 8; }
+}  // namespace
+
+extern "C" int64_t ce_choose_workspace_bytes(int32_t problems, int32_t segs, int32_t n_cols) {
+  if (problems < 0 || segs <= 0 || n_cols < 0) return -1;
+  const size_t cells = static_cast<size_t>(problems) * segs * n_cols;
+  return static_cast<int64_t>(a256(cells * 8) + a256(cells * 4) +
+                              a256(static_cast<size_t>(problems) * segs * 4));
+}
+
+extern "C" int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols, const void* score,
+                         int32_t score_dtype, const ce_row_params* params, int32_t problems,
+                         int32_t max_n, int32_t layers, int32_t heads, int32_t head_offset,
+                         int32_t* kept, int32_t kept_stride, int32_t* status,
+                         int32_t* protected_count, void* workspace, int64_t workspace_bytes,
+                         int32_t* err, void* stream) {
+  if (problems < 0 || n_cols < 0 || layers <= 0 || heads <= 0 || max_n < 0 || kept_stride < 0)
+    return host::fail(CE_ERR_ARG, "bad size");
+  if (problems == 0) return CE_OK;
+  if (!pos || !params || !kept || !status || !workspace) return host::fail(CE_ERR_ARG, "null pointer");
+  if (score && score_dtype != CE_DTYPE_F32 && score_dtype != CE_DTYPE_F64)
+    return host::fail(CE_ERR_ARG, "score dtype must be f32 or f64");
+  const int segs = layers * heads;
+  const int64_t need = ce_choose_workspace_bytes(problems, segs, n_cols);
+  if (workspace_bytes < need) return host::fail(CE_ERR_WORKSPACE, "choose workspace too small");
+  const int nw = (max_n + 31) / 32;
+  if (sel_smem(nw) > 200 * 1024) return host::fail(CE_ERR_UNSUPPORTED, "max_n too large");
+  const size_t cells = static_cast<size_t>(problems) * segs * n_cols;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  ChooseParams p{};
+  p.pos = pos;
+  p.ncols = ncols;
+  p.n_cols = n_cols;
+  p.score = score;
+  p.sdt = score ? score_dtype : CE_DTYPE_F32;
+  p.params = params;
+  p.problems = problems;
+  p.layers = layers;
+  p.heads = heads;
+  p.head_offset = head_offset;
+  p.nw = nw;
+  p.kept = kept;
+  p.kept_stride = kept_stride;
+  p.status = status;
+  p.pcount = protected_count;
+  p.kv = reinterpret_cast<uint64_t*>(ws);
+  p.pv = reinterpret_cast<int32_t*>(ws + a256(cells * 8));
+  p.seg_info = reinterpret_cast<int32_t*>(ws + a256(cells * 8) + a256(cells * 4));
+  p.err = err;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int smem = sel_smem(nw);
+  if (!host::set_smem(choose_seg_kernel, smem)) return host::fail(CE_ERR_CUDA, "smem attr");
+  choose_seg_kernel<<<problems * segs, T, smem, st>>>(p);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("choose_seg_kernel");
+  choose_status_kernel<<<problems, 32, 0, st>>>(p);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("choose_status_kernel");
+  return CE_OK;
+}
+
+extern "C" int64_t ce_boundary_workspace_bytes(int32_t num_rows, int32_t layers, int32_t kv_heads,
+                                               int32_t head_dim, int32_t page_size,
+                                               int32_t max_cols, int32_t global_heads,
+                                               int64_t hazard_bytes) {
+  (void)global_heads;
+  if (num_rows < 0 || layers <= 0 || kv_heads <= 0 || head_dim != 64 || page_size <= 0 ||
+      max_cols < 0)
+    return -1;
+  const int64_t one = hazard_per_layer(num_rows, kv_heads, max_cols, page_size);
+  const int64_t hz = hazard_bytes < one ? one : hazard_bytes;
+  return static_cast<int64_t>(boundary_layout(num_rows, layers, kv_heads, max_cols, hz).total);
+}
+
+static int boundary_params(BParams& p, int32_t* table, int64_t table_stride, int32_t table_width,
+                           int32_t* req_to_unit, int64_t r2u_stride, int32_t r2u_width,
+                           int32_t* frontier, int32_t* count, int32_t* pos,
+                           int64_t pos_row_stride, int32_t pos_cap, float* scores,
+                           int64_t sls, int64_t shs, int64_t pool_units, int32_t layers,
+                           int32_t kv_heads, int32_t page_size, const int32_t* rows,
+                           const ce_row_params* params, int32_t num_rows, int32_t max_cols,
+                           int32_t max_n) {
+  p.table = table;
+  p.ts = table_stride;
+  p.table_width = table_width;
+  p.r2u = req_to_unit;
+  p.rs = r2u_stride;
+  p.r2u_width = r2u_width;
+  p.frontier = frontier;
+  p.count = count;
+  p.pos = pos;
+  p.prs = pos_row_stride;
+  p.pos_cap = pos_cap;
+  p.scores = scores;
+  p.sls = sls;
+  p.shs = shs;
+  p.pool_units = pool_units;
+  p.L = layers;
+  p.G = kv_heads;
+  p.P = page_size;
+  p.rows = rows;
+  p.params = params;
+  p.R = num_rows;
+  p.max_cols = max_cols;
+  p.nw = (max_n + 31) / 32;
+  return CE_OK;
+}
+
+extern "C" int ce_gather_row_scores(const int32_t* table, int64_t table_stride,
+                                    const int32_t* req_to_unit, int64_t r2u_stride,
+                                    const int32_t* frontier, const int32_t* count,
+                                    const float* scores, int64_t score_layer_stride,
+                                    int64_t score_head_stride, int64_t pool_units, int32_t layers,
+                                    int32_t kv_heads, const int32_t* rows,
+                                    const ce_row_params* params, int32_t num_rows,
+                                    int32_t max_cols, float* out, int32_t* err, void* stream) {
+  if (num_rows < 0 || layers <= 0 || kv_heads <= 0 || max_cols < 0)
+    return host::fail(CE_ERR_ARG, "bad size");
+  if (num_rows == 0 || max_cols == 0) return CE_OK;
+  BParams p{};
+  boundary_params(p, const_cast<int32_t*>(table), table_stride, 0,
+                  const_cast<int32_t*>(req_to_unit), r2u_stride, 0, const_cast<int32_t*>(frontier),
+                  const_cast<int32_t*>(count), nullptr, 0, 0, const_cast<float*>(scores),
+                  score_layer_stride, score_head_stride, pool_units, layers, kv_heads, 1, rows,
+                  params, num_rows, max_cols, 0);
+  p.err = err;
+  gather_scores_kernel<<<num_rows * layers * kv_heads, 256, 0, static_cast<cudaStream_t>(stream)>>>(p, out);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("gather_scores_kernel");
+  return CE_OK;
+}
+
+extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_width,
+                           int32_t* req_to_unit, int64_t r2u_stride, int32_t r2u_width,
+                           int32_t* frontier, int32_t* count, int32_t* pos,
+                           int64_t pos_row_stride, int32_t pos_cap, float* scores,
+                           int64_t score_layer_stride, int64_t score_head_stride,
+                           int64_t pool_units, const uint64_t* k_layers,
+                           const uint64_t* v_layers, int32_t layers, int32_t kv_heads,
+                           int32_t head_dim, int32_t page_size, int32_t head_offset,
+                           int32_t* marks, int32_t epoch, const int64_t* swa_mapping,
+                           const int32_t* rows, const ce_row_params* params, int32_t num_rows,
+                           const void* uniforms, int32_t uniform_dtype,
+                           const float* global_scores, int32_t global_heads, int32_t live,
+                           int32_t max_cols, int32_t max_n, int32_t* result,
+                           int32_t* freed_units, int64_t freed_stride, void* workspace,
+                           int64_t workspace_bytes, int64_t hazard_bytes, int32_t* err,
+                           void* stream) {
+  if (num_rows < 0 || layers <= 0 || kv_heads <= 0 || max_cols < 0 || max_n < 0 || page_size <= 0)
+    return host::fail(CE_ERR_ARG, "bad size");
+  if (head_dim != 64) return host::fail(CE_ERR_UNSUPPORTED, "head_dim must be 64");
+  if (num_rows == 0) return CE_OK;
+  if (!table || !req_to_unit || !frontier || !count || !pos || !scores || !k_layers || !v_layers ||
+      !rows || !params || !result || !workspace)
+    return host::fail(CE_ERR_ARG, "null pointer");
+  if (live && (!marks || !freed_units)) return host::fail(CE_ERR_ARG, "live needs marks and freed_units");
+  if (uniforms && uniform_dtype != CE_DTYPE_F32 && uniform_dtype != CE_DTYPE_F64)
+    return host::fail(CE_ERR_ARG, "uniform dtype must be f32 or f64");
+  const int nw = (max_n + 31) / 32;
+  if (sel_smem(nw) > 200 * 1024) return host::fail(CE_ERR_UNSUPPORTED, "max_n too large");
+  const int64_t one = hazard_per_layer(num_rows, kv_heads, max_cols, page_size);
+  const int64_t hz = hazard_bytes < one ? one : hazard_bytes;
+  const BLayout Lo = boundary_layout(num_rows, layers, kv_heads, max_cols, hz);
+  if (workspace_bytes < static_cast<int64_t>(Lo.total))
+    return host::fail(CE_ERR_WORKSPACE, "boundary workspace too small");
+  BParams p{};
+  boundary_params(p, table, table_stride, table_width, req_to_unit, r2u_stride, r2u_width,
+                  frontier, count, pos, pos_row_stride, pos_cap, scores, score_layer_stride,
+                  score_head_stride, pool_units, layers, kv_heads, page_size, rows, params,
+                  num_rows, max_cols, max_n);
+  p.k_layers = k_layers;
+  p.v_layers = v_layers;
+  p.head_offset = head_offset;
+  p.marks = marks;
+  p.epoch = epoch;
+  p.swa = swa_mapping;
+  p.uniforms = uniforms;
+  p.udt = uniform_dtype;
+  p.gscores = global_scores;
+  p.GH = global_heads;
+  p.live = live;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.kv = reinterpret_cast<uint64_t*>(ws + Lo.kv);
+  p.pv = reinterpret_cast<int32_t*>(ws + Lo.pv);
+  p.seg_info = reinterpret_cast<int32_t*>(ws + Lo.seg);
+  p.mid_col = reinterpret_cast<int32_t*>(ws + Lo.mid);
+  p.src_unit = reinterpret_cast<int32_t*>(ws + Lo.src);
+  p.new_pos = reinterpret_cast<int32_t*>(ws + Lo.npos);
+  p.score_scr = reinterpret_cast<float*>(ws + Lo.ssc);
+  p.row_info = reinterpret_cast<int32_t*>(ws + Lo.info);
+  p.cand_rank = reinterpret_cast<int32_t*>(ws + Lo.crank);
+  p.new_table = reinterpret_cast<int32_t*>(ws + Lo.ntab);
+  p.hazard = ws + Lo.hazard;
+  p.freed = freed_units;
+  p.freed_stride = freed_stride;
+  p.result = result;
+  p.err = err;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int smem = sel_smem(nw);
+  if (!host::set_smem(bsel_kernel, smem)) return host::fail(CE_ERR_CUDA, "smem attr");
+  if (cudaMemsetAsync(p.row_info, 0, sizeof(int32_t) * 8 * num_rows, st) != cudaSuccess)
+    return host::fail_cuda("row_info memset");
+  bsel_kernel<<<num_rows * layers * kv_heads + num_rows, T, smem, st>>>(p);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bsel_kernel");
+  bvalidate_kernel<<<num_rows, 32, 0, st>>>(p);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bvalidate_kernel");
+  const int group = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(layers, hz / one)));
+  const int nsm = host::sm_count();
+  for (int l0 = 0; l0 < layers; l0 += group) {
+    const int nl = std::min(group, layers - l0);
+    const int64_t items = static_cast<int64_t>(num_rows) * nl * kv_heads * max_cols;
+    const int64_t want = (items * 32 + 255) / 256;
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 8LL * nsm)));
+    bgather_kernel<<<blocks, 256, 0, st>>>(p, l0, nl);
+    if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bgather_kernel");
+    bscatter_kernel<<<blocks, 256, 0, st>>>(p, l0, nl);
+    if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bscatter_kernel");
+  }
+  bfinish_kernel<<<num_rows, T, 0, st>>>(p);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bfinish_kernel");
+  return CE_OK;
+}
+
+extern "C" int ce_reservoir_scores(const int32_t* pos, int32_t layers, int32_t heads, int32_t n_cols,
+                                   int32_t head_offset, uint64_t seed, uint64_t* out,
+                                   void* stream) {
+  if (layers < 0 || heads < 0 || n_cols < 0) return host::fail(CE_ERR_ARG, "bad size");
+  const int64_t total = static_cast<int64_t>(layers) * heads * n_cols;
+  if (total == 0) return CE_OK;
+  if (!pos || !out) return host::fail(CE_ERR_ARG, "null pointer");
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+  reservoir_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(pos, layers, heads, n_cols,
+                                                                            head_offset, seed, out);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("reservoir_kernel");
+  return CE_OK;
+}

@@ -1,0 +1,257 @@
+/*
+ * ce_api.h -- C ABI of the B200 (sm_100a) decode-time KV eviction path.
+ *
+ * One shared library, libce_b200.so, exports these symbols.  Every pointer
+ * argument is caller-owned DEVICE memory unless the comment says "host".
+ * Every entry point:
+ *   - enqueues its kernels on `stream` (a cudaStream_t passed as void*);
+ *   - never synchronises the device and never allocates memory; scratch comes
+ *     from the caller through (workspace, workspace_bytes), sized with the
+ *     matching *_workspace_bytes() query;
+ *   - returns CE_OK or a negative CE_ERR_* status for host-detectable errors
+ *     (bad sizes, unsupported shapes, launch failures) and never throws;
+ *   - reports data-dependent errors found on the device (an index outside the
+ *     pool, a capacity overflow, a bounded wait that gave up) by OR-ing
+ *     CE_EW_* bits into the optional device word `err` (may be NULL).
+ *
+ * Vocabulary (the reference's, at page granularity):
+ *   unit      one KV page of `page_size` tokens (page_size 1 = the reference's
+ *             token slots).  Pools hold [units, kv_heads, page_size, head_dim]
+ *             bf16 per layer; at page_size 1 that is the reference's
+ *             [slots, kv_heads, head_dim] (SGLang MHATokenToKVPool).
+ *   row       a request row (SGLang req_pool_idx).
+ *   table     [rows, width] compacted resident units of each row, shared by
+ *             every layer and KV head (reference State.table).
+ *   req_to_unit [rows, width] logical position (in units) -> pool unit
+ *             (reference req_to_token).
+ *   frontier  [rows] logical length (units) below which residents live in
+ *             `table`; count [rows] = number of compacted residents.
+ *   pos       [rows, layers, kv_heads, pos_cap] logical unit position that
+ *             column c of `table` holds for (layer, head) (reference
+ *             entry["pos"]).
+ *   scores    [layers, kv_heads, pool_units] fp32 H2O scores, one per
+ *             (layer, KV head, unit) (reference State.scores).
+ *
+ * Reference citations are file:line inside tonghuikang/cache-eviction,
+ * e.g. code/cache_eviction/sglang_evict_runtime.py:136 (written
+ * "runtime:136" below).
+ */
+#ifndef CE_API_H
+#define CE_API_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (return values) ------------------------------------- */
+#define CE_OK               0
+#define CE_ERR_ARG         -1   /* a size/pointer argument is invalid        */
+#define CE_ERR_UNSUPPORTED -2   /* shape outside what the kernels implement  */
+#define CE_ERR_CUDA        -3   /* a CUDA runtime call or launch failed      */
+#define CE_ERR_WORKSPACE   -4   /* workspace smaller than the query returned */
+
+/* ---- device error-word bits (OR-ed into *err) -------------------------- */
+#define CE_EW_INDEX      0x01  /* a unit index outside [0, pool_units)           */
+#define CE_EW_CAPACITY   0x02  /* a CSR / column / output capacity was exceeded  */
+#define CE_EW_TIMEOUT    0x04  /* a bounded device wait gave up (kernel returned) */
+#define CE_EW_MODE       0x08  /* a row's score mode had no workspace (flags)    */
+#define CE_EW_PROTECTED  0x10  /* protected counts differ between heads          */
+#define CE_EW_SWA        0x20  /* a freed unit still maps to a sliding-window slot */
+#define CE_EW_PACK       0x40  /* packed ownership overlaps the sliding-window region */
+#define CE_EW_SHAPE      0x80  /* per-row sizes inconsistent with the arguments  */
+
+/* ---- policies (reference POLICIES, runtime:45-46, plus H2O global) ----- */
+#define CE_POLICY_PREFIX_SLIDING 0  /* prefix_sliding_2048: keep exactly P u R   */
+#define CE_POLICY_RANDOM         1  /* random_2048: caller-supplied uniforms      */
+#define CE_POLICY_RESERVOIR      2  /* random_reservoir_2048: splitmix64 scores   */
+#define CE_POLICY_HEAD_SUM       3  /* head_sum_2048: per-head score buffer       */
+#define CE_POLICY_HEAD_MAX       4  /* head_max_sum_2048: per-head score buffer   */
+#define CE_POLICY_H2O_GLOBAL     5  /* h2o_global_2048: sum of all KV heads' scores */
+
+/* decode score modes per row (reference State.mode, runtime:45-46,162-164) */
+#define CE_MODE_NONE 0
+#define CE_MODE_SUM  1
+#define CE_MODE_MAX  2
+
+/* score / uniform element types */
+#define CE_DTYPE_NONE 0
+#define CE_DTYPE_F32  1
+#define CE_DTYPE_F64  2
+#define CE_DTYPE_BF16 3
+
+/* per-boundary parameters, all in units (reference _boundary cfg + n + cursor,
+ * runtime:415-437).  32 bytes, device array. */
+typedef struct ce_row_params {
+  int32_t n;        /* logical length at the boundary                         */
+  int32_t budget;   /* retained units per (layer, head)                       */
+  int32_t prefix;   /* protected prefix P                                     */
+  int32_t recent;   /* protected recent window R                              */
+  int32_t cursor;   /* sliding-window guard (pos >= cursor protected); -1 = none */
+  int32_t policy;   /* CE_POLICY_*                                            */
+  uint64_t seed;    /* reservoir seed (reference cfg["seed"])                 */
+} ce_row_params;
+
+/* ---- library info -------------------------------------------------------- */
+const char* ce_version(void);
+const char* ce_status_string(int status);
+/* Detail of the last failing call made by this host thread. */
+const char* ce_last_error(void);
+
+/* ---- K4: ragged CSR page table -------------------------------------------
+ * Replaces gstar_evict.fill (runtime:136-152) and the two
+ * create_flashinfer_kv_indices_triton launches it makes.  For batch entry b
+ * (row = rows[b], L = seq_lens[b] tokens):
+ *   kv_indptr[b+1] = kv_indptr[b] + count[row] + ceil(L/page) - frontier[row]
+ *   kv_indices     = table[row, :count[row]] ++ req_to_unit[row, frontier:ceil(L/page)]
+ *   kv_tokens[b]   = count[row]*page + L - frontier[row]*page  (valid tokens)
+ * kv_indices is int32 or int64 (indices_i64).  Entries beyond kv_capacity are
+ * dropped and flag CE_EW_CAPACITY. */
+int ce_fill(const int32_t* table, int64_t table_stride,
+            const int32_t* req_to_unit, int64_t r2u_stride,
+            const int32_t* frontier, const int32_t* count,
+            const int64_t* rows, const int64_t* seq_lens, int32_t bs,
+            int32_t page_size,
+            int32_t* kv_indptr, void* kv_indices, int32_t indices_i64,
+            int64_t kv_capacity, int32_t* kv_tokens,
+            int32_t* err, void* stream);
+
+/* ---- K1: fused paged GQA decode attention + H2O score --------------------
+ * Replaces SGLang decode_attention_fwd (stage 1 + stage 2, call shape
+ * code/tests/test_sglang_evict.py:59-61) AND gstar_evict.after_decode /
+ * _decode_scores (runtime:155-224) with one pass over K and V.
+ *   q       [bs, H, 64] bf16 (strides q_sb, q_sh in elements, last dim dense)
+ *   k_pool, v_pool  one layer, [pool_units, G, page_size, 64] bf16, dense
+ *   kv_indptr/kv_indices/kv_tokens  the CSR from ce_fill (int32 indices)
+ *   sinks   [H] fp32 natural-log sink logits, or NULL (no sink)
+ *   mode_of_row [rows] CE_MODE_* and rows [bs] (mode = mode_of_row[rows[b]]);
+ *           mode_of_row NULL = no scores for any row
+ *   scores  [G, pool_units] fp32 of this layer (stride score_sg), receives
+ *           per unit: CE_MODE_SUM  sum over tokens in the unit and over the
+ *           group's query heads of p;  CE_MODE_MAX  sum over tokens of the
+ *           max over the group's query heads of p, where
+ *           p = exp(scale*q.k - logsumexp(all logits, sink)).
+ *   zero_new  1: a unit whose first token is the newest token of the row is
+ *           overwritten instead of accumulated (the reference zeroes the new
+ *           slot's score first, runtime:211-212)
+ *   out     [bs, H, 64] bf16 (out_f32 = 0) or fp32 (out_f32 = 1)
+ *   lse_out [bs, H] fp32 natural-log normalizer incl. sink, or NULL
+ *   score_flags bit0: CE_MODE_SUM rows may occur, bit1: CE_MODE_MAX rows may
+ *           occur (sizes the workspace; a row whose mode has no workspace
+ *           flags CE_EW_MODE and gets no score)
+ * Supported: head_dim 64, H/G == 8, page_size 1 (G == 8) or 16 (any G). */
+int64_t ce_decode_workspace_bytes(int32_t bs, int64_t kv_capacity,
+                                  int32_t num_q_heads, int32_t num_kv_heads,
+                                  int32_t page_size, int32_t score_flags);
+int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh,
+                         const void* k_pool, const void* v_pool, int64_t pool_units,
+                         const int32_t* kv_indptr, const int32_t* kv_indices,
+                         const int32_t* kv_tokens, int64_t kv_capacity,
+                         const float* sinks,
+                         const int32_t* mode_of_row, const int64_t* rows,
+                         float sm_scale, int32_t bs, int32_t num_q_heads,
+                         int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                         float* scores, int64_t score_sg, int32_t zero_new,
+                         void* out, int32_t out_f32, int64_t o_sb, int64_t o_sh,
+                         float* lse_out, int32_t score_flags,
+                         void* workspace, int64_t workspace_bytes,
+                         int32_t* err, void* stream);
+
+/* ---- K2: ragged per-head selection ---------------------------------------
+ * Replaces gstar_evict.choose + _scores + reservoir_scores (runtime:358-412)
+ * for `problems` independent boundaries, each over `segs` = layers*heads
+ * segments of up to n_cols columns (ncols[i] valid, NULL = all):
+ *   pos    [problems, segs, n_cols] int32 logical unit positions (unique per segment)
+ *   score  [problems, segs, n_cols] f32/f64 (score_dtype) or NULL; ignored by
+ *          prefix_sliding and reservoir; for h2o_global the key of (l, g, c) is
+ *          the fp32 sum over the layer's heads in ascending head order
+ *   params [problems] ce_row_params
+ * protected = pos < prefix | pos >= n - recent | (cursor >= 0 & pos >= cursor);
+ * the rest of the budget goes to the largest keys, ties to the larger pos.
+ * Every position must lie in [0, max_n) with max_n >= every problem's n.
+ * Outputs: kept [problems, segs, kept_stride] columns of the kept set sorted
+ * by ascending pos (min(budget, ncols) of them; the protected count for
+ * prefix_sliding); status [problems]: 0 chosen, 2 deferred (protected >
+ * budget, kept not written), 3 protected counts differ between heads;
+ * protected_count [problems]. */
+int64_t ce_choose_workspace_bytes(int32_t problems, int32_t segs, int32_t n_cols);
+int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols,
+              const void* score, int32_t score_dtype,
+              const ce_row_params* params, int32_t problems, int32_t max_n,
+              int32_t layers, int32_t heads, int32_t head_offset,
+              int32_t* kept, int32_t kept_stride, int32_t* status,
+              int32_t* protected_count,
+              void* workspace, int64_t workspace_bytes,
+              int32_t* err, void* stream);
+
+/* ---- K2+K3: one eviction boundary for a batch of rows --------------------
+ * Replaces gstar_evict._boundary (runtime:415-507): choose per (layer, KV
+ * head), move every head's j-th middle survivor (ascending pos) into the j-th
+ * non-protected candidate unit for K, V and scores of every layer, write
+ * table/count/frontier/pos; when live != 0 also zero the leftover units'
+ * scores, pack the req_to_unit row (runtime:476-491) and return the leftover
+ * units in candidate order for the caller's allocator (free_full).
+ *   k_layers/v_layers  device arrays [layers] of pool base addresses (uint64)
+ *   marks   [pool_units] int32 scratch owned by the caller (zero-initialised
+ *           once); epoch must grow by one per call
+ *   swa_mapping [pool_units] int64 or NULL (reference
+ *           allocator.full_to_swa_index_mapping, runtime:477-479)
+ *   uniforms [num_rows, layers, heads, max_cols] f32/f64 for random rows
+ *   global_scores [num_rows, layers, global_heads, max_cols] fp32 or NULL:
+ *           dense per-column scores of ALL KV heads (tensor-parallel ranks
+ *           all-gather them); when NULL h2o_global sums the local heads
+ *   max_cols >= count[row] + n - frontier[row] for every row
+ *   max_n    >= every row's n (positions are ranked in a max_n-bit bitmap)
+ *   result  [num_rows, 4]: status (0 evicted, 1 nothing to do, 2 deferred,
+ *           3 protected mismatch, 4 packing error, 5 sliding-window error),
+ *           columns before, residents after, units freed
+ *   freed_units [num_rows, freed_stride] leftover units (live only)
+ * hazard_bytes bounds the relocation scratch; layers are processed in groups
+ * that fit it (at least one layer; query the minimum with layers = 1). */
+int64_t ce_boundary_workspace_bytes(int32_t num_rows, int32_t layers, int32_t kv_heads,
+                                    int32_t head_dim, int32_t page_size,
+                                    int32_t max_cols, int32_t global_heads,
+                                    int64_t hazard_bytes);
+int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_width,
+                int32_t* req_to_unit, int64_t r2u_stride, int32_t r2u_width,
+                int32_t* frontier, int32_t* count,
+                int32_t* pos, int64_t pos_row_stride, int32_t pos_cap,
+                float* scores, int64_t score_layer_stride, int64_t score_head_stride,
+                int64_t pool_units,
+                const uint64_t* k_layers, const uint64_t* v_layers,
+                int32_t layers, int32_t kv_heads, int32_t head_dim, int32_t page_size,
+                int32_t head_offset,
+                int32_t* marks, int32_t epoch, const int64_t* swa_mapping,
+                const int32_t* rows, const ce_row_params* params, int32_t num_rows,
+                const void* uniforms, int32_t uniform_dtype,
+                const float* global_scores, int32_t global_heads,
+                int32_t live, int32_t max_cols, int32_t max_n,
+                int32_t* result, int32_t* freed_units, int64_t freed_stride,
+                void* workspace, int64_t workspace_bytes, int64_t hazard_bytes,
+                int32_t* err, void* stream);
+
+/* Dense per-column scores of the boundary rows, [num_rows, layers, heads,
+ * max_cols] fp32 (zero beyond each row's columns), for the tensor-parallel
+ * all-gather that h2o_global needs before ce_boundary. */
+int ce_gather_row_scores(const int32_t* table, int64_t table_stride,
+                         const int32_t* req_to_unit, int64_t r2u_stride,
+                         const int32_t* frontier, const int32_t* count,
+                         const float* scores, int64_t score_layer_stride,
+                         int64_t score_head_stride, int64_t pool_units,
+                         int32_t layers, int32_t kv_heads,
+                         const int32_t* rows, const ce_row_params* params,
+                         int32_t num_rows, int32_t max_cols, float* out,
+                         int32_t* err, void* stream);
+
+/* reservoir_scores (runtime:358-373) / core.reservoir_score (core.py:23-30):
+ * out[l, g, c] = splitmix64(seed, l, head_offset + g, pos[l, g, c]) >> 11 as
+ * the 53-bit integer (divide by 2^53 for the reference's double). */
+int ce_reservoir_scores(const int32_t* pos, int32_t layers, int32_t heads,
+                        int32_t n_cols, int32_t head_offset, uint64_t seed,
+                        uint64_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CE_API_H */

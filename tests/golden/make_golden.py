@@ -1,0 +1,199 @@
+"""Generate the golden fixtures from the reference's own functions.
+
+    python tests/golden/make_golden.py [/path/to/cache-eviction]
+
+Imports tonghuikang/cache-eviction's code/cache_eviction/sglang_evict_runtime.py
+and core.py from a read-only checkout (default /root/reference) and runs them on
+CPU tensors; torch.cuda.synchronize is replaced by a no-op in this process only.
+Inputs come from tests/golden/scenarios.py (numpy, fixed seeds), so only the
+reference's outputs are stored.  The checkout is needed only to regenerate;
+tests read the .npz files.
+"""
+from __future__ import annotations
+
+import hashlib
+import importlib.util
+import sys
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parent))
+from golden import scenarios as sc  # noqa: E402
+
+
+def load_reference(root: Path):
+    torch.cuda.synchronize = lambda *a, **k: None  # CPU run: the reference syncs at boundaries
+    spec = importlib.util.spec_from_file_location(
+        "ref_gstar_evict", root / "code/cache_eviction/sglang_evict_runtime.py")
+    rt = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(rt)
+    sys.path.insert(0, str(root / "code"))
+    from cache_eviction import core
+    return rt, core
+
+
+def bf16_tensor(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
+
+
+def sha(t: torch.Tensor) -> str:
+    return hashlib.sha256(t.contiguous().view(torch.int16).numpy().tobytes()
+                          if t.dtype == torch.bfloat16 else t.contiguous().numpy().tobytes()).hexdigest()
+
+
+def gen_choose(rt):
+    out = {}
+    for i, c in enumerate(sc.choose_cases()):
+        pos = torch.from_numpy(c["pos"])
+        L, G, N = pos.shape
+        if c["name"] == "random_reservoir_2048":
+            score = rt.reservoir_scores(c["seed"], pos, torch.arange(L), torch.arange(G))
+        elif c["name"] == "h2o_global_2048":
+            score = torch.from_numpy(c["global_key"])
+        elif c["score"] is None:
+            score = torch.zeros(pos.shape, dtype=torch.float64)
+        else:
+            score = torch.from_numpy(c["score"])
+        name = "head_sum_2048" if c["name"] == "h2o_global_2048" else c["name"]
+        try:
+            keep, count = rt.choose(name, pos, c["n"], c["budget"], c["prefix"], c["recent"], score,
+                                    c["cursor"])
+            if keep is None:
+                status, kept = 2, np.zeros((L, G, 0), np.int32)
+            else:
+                status, kept = 0, np.sort(keep.numpy(), -1).astype(np.int32)
+        except RuntimeError:
+            status, kept, count = 3, np.zeros((L, G, 0), np.int32), -1
+        out[f"case{i}_status"] = np.int32(status)
+        out[f"case{i}_count"] = np.int32(count)
+        out[f"case{i}_kept"] = kept
+    np.savez_compressed(HERE / "choose.npz", **out)
+    return out
+
+
+def gen_reservoir(rt, core):
+    pos = torch.arange(1000).expand(2, 8, -1)
+    vals = {}
+    for seed in (7, 3, (1 << 63) + 5, -3):
+        s = rt.reservoir_scores(seed, pos, torch.arange(2), torch.arange(8))
+        vals[f"seed_{seed & ((1 << 64) - 1)}"] = (s[:, :, :128] * float(1 << 53)).numpy().astype(np.uint64)
+    vals["kat_7_1_5_321"] = np.float64(core.reservoir_score(7, 1, 5, 321))
+    vals["kat_runtime_7_1_5_321"] = np.float64(
+        rt.reservoir_scores(7, pos, torch.arange(2), torch.arange(8))[1, 5, 321])
+    np.savez_compressed(HERE / "reservoir.npz", **vals)
+
+
+def make_backend(setup):
+    keys = {l: bf16_tensor(setup["keys"][l]).clone() for l in range(4)}
+    values = {l: bf16_tensor(setup["values"][l]).clone() for l in range(4)}
+    pool = SimpleNamespace(layers_mapping={l: (l, l not in sc.FULL) for l in range(4)},
+                           get_key_buffer=keys.__getitem__, get_value_buffer=values.__getitem__)
+    return SimpleNamespace(token_to_kv_pool=pool, max_kv_splits=8,
+                           req_to_token_pool=SimpleNamespace(req_to_token=torch.zeros(
+                               (setup["rows"], setup["width"]), dtype=torch.int32)),
+                           kv_indptr=torch.zeros(setup["rows"] + 1, dtype=torch.int32)), keys, values
+
+
+def gen_boundaries(rt, core):
+    out = {}
+    setup = sc.boundary_setup()
+    n = setup["n"]
+    orig_scores = rt._scores
+
+    def scores_with_global(st, entry, name, pos, slots, nn):
+        if name == "h2o_global_2048":
+            s = st.scores[:, :, slots]
+            acc = torch.zeros(s.shape[0], s.shape[2], dtype=torch.float32)
+            for g in range(s.shape[1]):
+                acc = acc + s[:, g]
+            return acc[:, None, :].expand(-1, s.shape[1], -1).double()
+        return orig_scores(st, entry, name, pos, slots, nn)
+
+    rt._scores = scores_with_global
+    for name, kind in sc.BOUNDARY_NAMES:
+        rt.STATE = None
+        b, keys, values = make_backend(setup)
+        st = rt.state(b)
+        slot_of = torch.from_numpy(setup["slot_of"])
+        st.req_to_token[1, :n] = slot_of.int()
+        st.scores[:, :, slot_of] = torch.from_numpy(setup["score"])
+        cfg = sc.boundary_cfg(name)
+        if name == "h2o_global_2048":
+            entry = {"kind": kind, "key": "r", "cfg": dict(cfg, record=False), "mode": 1, "events": [],
+                     "error": None, "frontier": 0, "count": 0, "last_boundary": 0,
+                     "peak_full_entries": 0, "layer_error": []}
+        else:
+            entry = rt._live_entry(SimpleNamespace(rid="r", session=None), dict(cfg, record=False), kind)
+        freed = []
+        alloc = SimpleNamespace(free_full=lambda s: freed.append(s.clone()),
+                                full_to_swa_index_mapping=torch.zeros(setup["slots"], dtype=torch.int64))
+        policies = {(l, g): core.Policy(name if name != "h2o_global_2048" else "head_sum_2048",
+                                        cfg["budget"], cfg["prefix"], cfg["recent"], seed=4, stream=(l, g))
+                    for l in range(2) for g in range(8)}
+        key = f"{name}_{kind}"
+        for k, boundary in enumerate((2048, 4096)):
+            cursor = boundary - 200
+            if kind == "replay":
+                rt._boundary(st, 1, entry, boundary)
+            else:
+                rt._boundary(st, 1, entry, boundary, cursor, alloc)
+            cnt = entry["count"]
+            out[f"{key}_b{k}_table"] = st.table[1, :cnt].numpy().copy()
+            out[f"{key}_b{k}_pos"] = entry["pos"].numpy().astype(np.int32).copy()
+            out[f"{key}_b{k}_frontier"] = np.int32(int(st.frontier[1]))
+            out[f"{key}_b{k}_r2u"] = st.req_to_token[1, :n].numpy().copy()
+            out[f"{key}_b{k}_freed"] = (torch.cat(freed).numpy().astype(np.int32) if freed
+                                        else np.zeros(0, np.int32))
+            # the reference test's own check: kept sets equal core.Policy's
+            if name not in ("random_2048", "h2o_global_2048"):
+                for p in policies.values():
+                    for t in range(p.next_position, boundary):
+                        p.append(t)
+                for (l, g), p in policies.items():
+                    p.scores = {t: float(setup["score"][l, g, t]) for t in p.resident}
+                    p.finish()
+                for (l, g), p in policies.items():
+                    assert set(entry["pos"][l, g].tolist()) == p.resident, (name, boundary, l, g)
+        out[f"{key}_keys_sha"] = np.array([sha(keys[l]) for l in sc.FULL])
+        out[f"{key}_values_sha"] = np.array([sha(values[l]) for l in sc.FULL])
+        out[f"{key}_scores_sha"] = np.array([sha(st.scores)])
+    rt._scores = orig_scores
+    np.savez_compressed(HERE / "boundary.npz", **out)
+
+
+def gen_decode(rt):
+    d = sc.decode_setup()
+    keys = bf16_tensor(d["keys"]).float()
+    values = bf16_tensor(d["values"]).float()
+    q = bf16_tensor(d["q"]).float()
+    sinks = bf16_tensor(d["sinks"]).float()
+    out = {}
+    for i, length in enumerate(sc.DECODE_LENGTHS):
+        slots = torch.from_numpy(d["perm"][d["indptr"][i]:d["indptr"][i + 1]]).long()
+        k = keys[slots]
+        p = rt._probabilities(q[i:i + 1], k, sinks, d["scale"], sc.G, torch.tensor([length - 1]),
+                              torch.arange(length))  # [G, group, 1, len]
+        out[f"seq{i}_sum"] = p.sum(1)[:, 0].numpy().astype(np.float32)
+        out[f"seq{i}_max"] = p.amax(1)[:, 0].numpy().astype(np.float32)
+        o = torch.einsum("gjk,kgd->gjd", p[:, :, 0].double(), values[slots].double())
+        out[f"seq{i}_out"] = o.reshape(sc.H, sc.D).numpy().astype(np.float32)
+    np.savez_compressed(HERE / "decode.npz", **out)
+
+
+def main():
+    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    rt, core = load_reference(root)
+    gen_choose(rt)
+    gen_reservoir(rt, core)
+    gen_boundaries(rt, core)
+    gen_decode(rt)
+    for f in sorted(HERE.glob("*.npz")):
+        print(f.name, f.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()
