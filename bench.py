@@ -1,0 +1,427 @@
+"""Decode throughput of the eviction hot path on B200 (one JSON line on rank 0).
+
+Workload ("ragged continuous batch"): 64 sequences per GPU
+with contexts log-uniform over 2K-64K tokens in 16-token pages, per-sequence
+budgets from {2K, 4K, 8K, 16K, 32K} (P = R = B/4, recent: R = 3B/4) and
+policies mixed over full / recent / random / H2O global / H2O per-head, on the
+12 full-attention layers of a gpt-oss-20b-shaped attention (64 query heads,
+8 KV heads, head_dim 64, bf16).  Every step appends one token to every
+sequence, runs due eviction boundaries (select + compact), builds the CSR page
+table and runs the fused decode attention + H2O score kernel on each layer,
+followed by the row-parallel output projection and its NCCL all-reduce across
+ranks.  Synthetic seeded data; the KV state is larger than L2.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Tensor parallel over KV heads: rank r holds 8/N KV heads of every sequence and
+the global batch is 64*N sequences (per-GPU work fixed: weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s with per-head H2O eviction (ragged 64-seq batch, 8K-32K budgets)"
+UNIT = "tok/s"
+H_TOTAL, G_TOTAL, D, PAGE, LAYERS, HIDDEN = 64, 8, 64, 16, 12, 2880
+SEQS_PER_GPU = 64
+BUDGETS = [2048, 4096, 8192, 16384, 32768]
+POLICY_MIX = ["full", "recent", "random", "h2o_global", "h2o_per_head"]
+
+
+def workload(n_seqs: int, seed: int = 2026):
+    """Seeded per-sequence (ctx, policy, budget) of BASELINE config 3."""
+    from cache_eviction_b200.policy import EvictionConfig, canonical, sweep_split
+    rng = np.random.default_rng(seed)
+    specs = []
+    for _ in range(n_seqs):
+        ctx = int(np.exp(rng.uniform(np.log(2048), np.log(65536)))) // PAGE * PAGE
+        budget = int(rng.choice(BUDGETS))
+        pol = str(rng.choice(POLICY_MIX))
+        if pol == "full":
+            cfg = None
+        else:
+            name = canonical(pol)
+            p, r = sweep_split(budget, name)
+            cfg = EvictionConfig(name, budget, p, r, seed=int(rng.integers(0, 1 << 31)))
+        specs.append(dict(ctx=ctx, cfg=cfg, policy=pol, budget=budget))
+    return specs
+
+
+def pool_units_needed(specs, steps):
+    total = 1
+    for sp in specs:
+        cfg, ctx = sp["cfg"], sp["ctx"]
+        end = -(-(ctx + steps) // PAGE)
+        last = (ctx // 2048) * 2048
+        if cfg is not None and last > cfg.budget:
+            total += cfg.budget // PAGE + end - last // PAGE
+        else:
+            total += end
+    return total + 64
+
+
+def resident_tokens_after_steps(specs, steps):
+    """Host-side resident token count per sequence (for the CPU sample)."""
+    out = []
+    for sp in specs:
+        cfg, ctx = sp["cfg"], sp["ctx"]
+        last = (ctx // 2048) * 2048
+        if cfg is not None and last > cfg.budget:
+            out.append(cfg.budget + ctx - last)
+        else:
+            out.append(ctx)
+    return out
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_gpu{gpu_index}.csv"
+
+    def __enter__(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu),
+                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_decode_sample(specs, n_rows, layers_sample, seed, max_seconds=None, min_reps=1):
+    """Time the oracle's decode (attention + H2O scores) on a bounded sample.
+
+    Builds host pools for `n_rows` sequences of the workload (their resident
+    token counts, 16-token pages) and runs oracle.decode for `layers_sample`
+    layers.  Returns (seconds per sampled layer-step, sampled tokens).
+    """
+    from oracle import oracle
+    rng = np.random.default_rng(seed)
+    resident = resident_tokens_after_steps(specs, 0)
+    idx = rng.choice(len(specs), size=min(n_rows, len(specs)), replace=False)
+    lengths = [resident[i] for i in idx]
+    pages = [-(-n // PAGE) for n in lengths]
+    units = sum(pages) + 1
+    kp = rng.integers(0, 1 << 16, (units, G_TOTAL, PAGE, D), dtype=np.uint16) & 0xBFFF
+    vp = rng.integers(0, 1 << 16, (units, G_TOTAL, PAGE, D), dtype=np.uint16) & 0xBFFF
+    q = (rng.integers(0, 1 << 16, (len(idx), H_TOTAL, D), dtype=np.uint16) & 0x3FFF) | 0x3800
+    indptr = np.concatenate([[0], np.cumsum(pages)]).astype(np.int32)
+    indices = (rng.permutation(units - 1) + 1).astype(np.int32)[:sum(pages)]
+    tokens = np.array(lengths, np.int32)
+    modes = np.array([1 if specs[i]["cfg"] is not None and specs[i]["cfg"].score_mode else 0
+                      for i in idx], np.int32)
+    sinks = rng.standard_normal(H_TOTAL).astype(np.float32)
+    scores = np.zeros((G_TOTAL, units), np.float32)
+    times = []
+    t_all = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        for _ in range(layers_sample):
+            oracle.decode(q, kp, vp, indptr, indices, tokens, sinks, modes, 0.125, PAGE, scores)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= min_reps and (max_seconds is None or time.perf_counter() - t_all > max_seconds):
+            break
+        if max_seconds is None:
+            break
+    return statistics.median(times) / layers_sample, int(sum(lengths)), len(idx)
+
+
+def reference_arm(args, world, rank):
+    """--impl reference: the CPU restatement of the reference path on host cores."""
+    if rank != 0:
+        return 0
+    from oracle import oracle
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    specs = workload(SEQS_PER_GPU * world)
+    resident = resident_tokens_after_steps(specs, 0)
+    total_tokens = sum(resident)
+    n_sample = 4
+    step_times = []
+    sampled = None
+    for s in range(args.warmup + args.steps):
+        t, tok, nrows = cpu_decode_sample(specs, n_sample, 1, seed=100 + s)
+        full_step = t * (total_tokens / tok) * LAYERS
+        if s >= args.warmup:
+            step_times.append(full_step)
+        sampled = (tok, nrows)
+    per_step = statistics.mean(step_times)
+    value = len(specs) / per_step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic", "config": config_block(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"oracle decode (attention + H2O scores) of {sampled[1]} of "
+                                   f"{len(specs)} sequences ({sampled[0]} resident tokens), 1 of "
+                                   f"{LAYERS} layers per step, scaled by resident tokens and layers"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_block(world):
+    return {"workload": "config3 ragged continuous batch: 64 seqs/GPU, ctx log-uniform 2K-64K, "
+                        "budgets {2K..32K}, policies {full, recent, random, h2o_global, h2o_per_head}, "
+                        "12 full-attention layers, 64q/8kv heads, head_dim 64, 16-token pages",
+            "global_batch": SEQS_PER_GPU * world, "page_size": PAGE, "layers": LAYERS,
+            "kv_heads_per_gpu": G_TOTAL // world, "parallelism": f"tp{world} over KV heads",
+            "l2": "KV state far larger than L2 (no flush needed)"}
+
+
+# ---------------------------------------------------------------- our arm
+def build_engine(specs, steps_total, world, rank, group, device):
+    import torch
+    from cache_eviction_b200.engine import RaggedDecodeEngine, synth_state
+    from cache_eviction_b200 import tp
+    G, H, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    units = pool_units_needed(specs, steps_total)
+    eng = RaggedDecodeEngine(layers=LAYERS, q_heads=H, kv_heads=G, page_size=PAGE, pool_units=units,
+                             max_rows=len(specs), r2u_width=-(-(65536 + steps_total + 4096) // PAGE),
+                             pos_cap=32768 // PAGE, device=device, head_offset=off,
+                             global_kv_heads=G_TOTAL, process_group=group)
+    synth_state(eng, specs, steps_total, seed=2026 + 17)
+    torch.cuda.synchronize()
+    return eng
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=512)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-oproj", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        return reference_arm(args, world, rank)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    import torch
+    import torch.distributed as dist
+    from cache_eviction_b200 import capi, kernels, tp
+
+    group, rank, world = tp.init_from_env("nccl")
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+    capi.load()
+    specs = workload(SEQS_PER_GPU * world)
+    e2e_steps = args.e2e_steps if args.e2e_steps is not None else args.steps
+    steps_total = args.warmup + max(args.steps, e2e_steps)
+    G, H, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    B = len(specs)
+    scale = D ** -0.5
+
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    q = torch.randn((LAYERS, B, H, D), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty((LAYERS, B, H, D), dtype=torch.bfloat16, device=device)
+    sinks = [torch.randn(H, generator=gen, device=device) for _ in range(LAYERS)]
+    w_o = [(torch.randn((H * D, HIDDEN), generator=gen, device=device) * 0.02).to(torch.bfloat16)
+           for _ in range(LAYERS)] if not args.no_oproj else None
+    hidden = torch.empty((B, HIDDEN), dtype=torch.bfloat16, device=device)
+
+    def after_layer(l, o):
+        if w_o is not None:
+            tp.output_reduction(o, w_o[l], group, out=hidden)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[device.index])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ------------------------------------------------ device-resident pass
+    eng = build_engine(specs, steps_total, world, rank, group, device)
+    for _ in range(args.warmup):
+        eng.step(q, out, sinks, scale, after_layer)
+    barrier()
+    torch.cuda.synchronize()
+    ev = []   # (start, end, bytes) per fused decode launch
+    bound_before = len(eng.boundary_ms)
+    launches0 = kernels.LAUNCHES[0]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tokens_resident = []
+    with ClockSampler(device.index) as clocks:
+        start.record()
+        for s in range(args.steps):
+            eng.run_boundaries(eng.due())
+            eng.advance()
+            eng._ensure_capacity(0)
+            eng.fill()
+            res_tok = sum(eng.resident_tokens(r) for r in eng.active)
+            h2o_pages = sum(eng.resident_units(r) for r in eng.active
+                            if eng.rows[r].cfg is not None and eng.rows[r].cfg.score_mode)
+            nbytes = res_tok * G * D * 2 * 2 + 2 * B * H * D * 2 + h2o_pages * G * 8
+            tokens_resident.append(res_tok)
+            for l in range(LAYERS):
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                eng.decode_layer(l, q[l], out[l], sinks[l], scale)
+                b.record()
+                ev.append((a, b, nbytes))
+                after_layer(l, out[l])
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end))
+    launches = kernels.LAUNCHES[0] - launches0
+    eng.check_errors()
+    dur = [a.elapsed_time(b) for a, b, _ in ev]
+    avg_launch_ms = statistics.mean(dur)
+    avg_bytes = statistics.mean(x for _, _, x in ev)
+    achieved_gbs = avg_bytes / (avg_launch_ms * 1e-3) / 1e9
+    boundary_ms = eng.boundary_ms[bound_before:]
+    n_bound_rows = sum(1 for r in eng.active for e in eng.rows[r].events)
+    value = B * args.steps / (elapsed_ms * 1e-3)
+    clock_info = clocks.summary()
+    del eng
+    torch.cuda.empty_cache()
+
+    # --------------------------------------------------------- e2e pass
+    eng = build_engine(specs, steps_total, world, rank, group, device)
+    q_host = q[0].cpu().pin_memory()
+    q_host_all = torch.empty((LAYERS, B, H, D), dtype=torch.bfloat16).pin_memory()
+    q_host_all.copy_(q.cpu())
+    out_host = torch.empty((LAYERS, B, H, D), dtype=torch.bfloat16).pin_memory()
+    q_dev = torch.empty_like(q)
+    for _ in range(args.warmup):
+        q_dev.copy_(q_host_all, non_blocking=True)
+        eng.step(q_dev, out, sinks, scale, after_layer)
+        out_host.copy_(out, non_blocking=True)
+    barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(e2e_steps):
+        q_dev.copy_(q_host_all, non_blocking=True)
+        eng.step(q_dev, out, sinks, scale, after_layer)
+        out_host.copy_(out, non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2))
+    e2e_value = B * e2e_steps / (e2e_ms * 1e-3)
+    step_bytes = LAYERS * B * H * D * 2
+    del eng, q_host
+    torch.cuda.empty_cache()
+
+    peak, peak_kind = measured_peak_hbm()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_block(world),
+        "roofline": {"bound": "hbm", "kernel": "ce_decode_attn_score (attn_kernel + finalize_kernel)",
+                     "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": achieved_gbs / peak, "peak_kind": peak_kind,
+                     "bytes_per_launch": avg_bytes, "launch_ms": avg_launch_ms,
+                     "traffic": None},
+        "clocks": clock_info,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes,
+                "d2h_bytes_per_step": step_bytes,
+                "path": "pinned host q (all layers) -> device, engine.step via the C ABI, "
+                        "attention outputs -> pinned host, every step"},
+        "gpu_launches": launches,
+        "evict": {"boundary_batches": len(boundary_ms),
+                  "boundary_ms_mean": statistics.mean(boundary_ms) if boundary_ms else None,
+                  "boundary_rows": n_bound_rows},
+        "resident_tokens_mean": statistics.mean(tokens_resident),
+    }
+    if rank == 0 and world == 1:
+        from oracle import oracle
+        cores = os.cpu_count() or 1
+        oracle.set_threads(cores)
+        t, tok, nrows = cpu_decode_sample(specs, 4, 1, seed=99, max_seconds=args.cpu_seconds)
+        cpu_step = t * (statistics.mean(tokens_resident) / tok) * LAYERS
+        line["cpu_baseline"] = {
+            "value": B / cpu_step, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"oracle decode of {nrows} of {B} sequences ({tok} resident tokens), 1 layer, "
+                      f"repeated for ~{args.cpu_seconds:.0f} s, scaled by resident tokens x {LAYERS} layers"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

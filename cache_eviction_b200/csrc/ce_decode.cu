@@ -86,6 +86,14 @@ struct Params {
 
 __device__ __forceinline__ int stage_tokens(int G) { return 16 * (NCW / G); }
 
+// Partitions actually used: at least MIN_STAGES_PER_CTA stages each, so a
+// short batch is not spread thinner than the pipeline depth.
+constexpr int64_t MIN_STAGES_PER_CTA = 4;
+__device__ __forceinline__ int64_t eff_grid(int64_t S, int64_t launched) {
+  const int64_t want = (S + MIN_STAGES_PER_CTA - 1) / MIN_STAGES_PER_CTA;
+  return want < 1 ? 1 : (want < launched ? want : launched);
+}
+
 __device__ __forceinline__ int seq_tokens(const Params& p, int b, int P) {
   if (p.kv_tokens) return max(0, p.kv_tokens[b]);
   return max(0, (p.kv_indptr[b + 1] - p.kv_indptr[b]) * P);
@@ -143,11 +151,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int UNIT_ROWS = G * P;            // rows of one page (all local heads)
   const uint32_t UNIT_BYTES = UNIT_ROWS * ROW_BYTES;
 
-  // Zero the stage ring so rows that are never loaded hold finite values.
-  {
-    uint4* z = reinterpret_cast<uint4*>(smem);
-    for (int i = tid; i < NSTAGES * STAGE_BYTES / 16; i += THREADS) z[i] = make_uint4(0, 0, 0, 0);
-  }
   if (tid == 0) {
     for (int s = 0; s < NSTAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -166,8 +169,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   for (int b = lo_b; b < hi_b; ++b) local += (seq_tokens(p, b, P) + ST - 1) / ST;
   int64_t S = 0;
   const int64_t excl = block_excl_scan(local, scan_sh, S);  // includes __syncthreads
-  const int64_t k = blockIdx.x, grid = gridDim.x;
-  const int64_t S_lo = k * S / grid, S_hi = (k + 1) * S / grid;
+  const int64_t k = blockIdx.x, grid = eff_grid(S, gridDim.x);
+  const int64_t S_lo = k < grid ? k * S / grid : S, S_hi = k < grid ? (k + 1) * S / grid : S;
   if (blockIdx.x == 0) {
     int64_t run = excl;
     for (int b = lo_b; b < hi_b; ++b) {
@@ -201,20 +204,45 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == NCW) {
     // ------------------------------- producer --------------------------------
+    // Page indices are read in 32-entry windows one window ahead of use (the
+    // CTA's CSR positions only move forward), so no TMA issue waits on a
+    // dependent global load.
     int issued = 0;
     int b = b_start, base = base_start;
-    int nst = (b < bs) ? (seq_tokens(p, b, P) + ST - 1) / ST : 0;
+    int nst = 0, tok_b = 0;
+    int64_t ip_b = 0;
+    auto load_seq = [&](int bb) {
+      tok_b = seq_tokens(p, bb, P);
+      nst = (tok_b + ST - 1) / ST;
+      ip_b = p.kv_indptr[bb];
+    };
+    if (b < bs) load_seq(b);
+    auto fetch = [&](int64_t w0) -> int {
+      const int64_t c = w0 + lane;
+      return (c >= 0 && c < p.kv_capacity) ? p.kv_indices[c] : -2;
+    };
+    int64_t w0 = -1;
+    int idx_cur = -2, idx_next = -2;
     for (int64_t x = S_lo; x < S_hi; ++x) {
       while (x >= base + nst) {
         base += nst;
         ++b;
-        nst = (seq_tokens(p, b, P) + ST - 1) / ST;
+        load_seq(b);
       }
       if (*abort_flag) break;
       const int j = static_cast<int>(x - base);
-      const int tokens = seq_tokens(p, b, P);
-      const int ntok = min(ST, tokens - j * ST);
+      const int ntok = min(ST, tok_b - j * ST);
       const int nunits = (ntok + P - 1) / P;
+      const int64_t c0 = ip_b + static_cast<int64_t>(j) * UPS;
+      if (w0 < 0 || c0 < w0 || c0 + nunits > w0 + 64) {
+        w0 = c0;
+        idx_cur = fetch(w0);
+        idx_next = fetch(w0 + 32);
+      } else if (c0 >= w0 + 32) {
+        w0 += 32;
+        idx_cur = idx_next;
+        idx_next = fetch(w0 + 32);
+      }
       const int s = issued % NSTAGES;
       const uint32_t ph = (issued / NSTAGES) & 1;
       if (issued >= NSTAGES) {
@@ -226,20 +254,19 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
       }
-      // Resolve this stage's pages; a page outside the pool is skipped (its
-      // rows keep old finite data, its tokens are still masked by ntok only if
-      // past the end, so flag the error for the caller).
+      // Unit of this lane's page: window slot (c0 - w0 + lane) of cur/next.
+      const int slot = static_cast<int>(c0 - w0) + lane;
+      const int a = __shfl_sync(0xffffffffu, idx_cur, slot & 31);
+      const int bn = __shfl_sync(0xffffffffu, idx_next, slot & 31);
       int unit = -1;
-      const int64_t cpos = static_cast<int64_t>(p.kv_indptr[b]) + static_cast<int64_t>(j) * UPS + lane;
       if (lane < nunits) {
-        if (cpos < p.kv_capacity) {
-          unit = p.kv_indices[cpos];
-          if (unit < 0 || unit >= p.pool_units) {
-            flag_error(p.err, CE_EW_INDEX);
-            unit = -1;
-          }
-        } else {
+        const int v = (slot < 32) ? a : bn;
+        if (v == -2) {
           flag_error(p.err, CE_EW_CAPACITY);
+        } else if (v < 0 || v >= p.pool_units) {
+          flag_error(p.err, CE_EW_INDEX);
+        } else {
+          unit = v;
         }
       }
       const unsigned valid = __ballot_sync(0xffffffffu, unit >= 0);
@@ -292,13 +319,20 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     int it = 0;
     int b = b_start, base = base_start;
-    int nst = (b < bs) ? (seq_tokens(p, b, P) + ST - 1) / ST : 0;
+    int nst = 0, tok_b = 0;
+    int64_t ip_b = 0;
+    auto load_seq = [&](int bb) {
+      tok_b = seq_tokens(p, bb, P);
+      nst = (tok_b + ST - 1) / ST;
+      ip_b = p.kv_indptr[bb];
+    };
+    if (b < bs) load_seq(b);
     bool aborted = false;
     for (int64_t x = S_lo; x < S_hi; ++x, ++it) {
       while (x >= base + nst) {
         base += nst;
         ++b;
-        nst = (seq_tokens(p, b, P) + ST - 1) / ST;
+        load_seq(b);
       }
       if (b != cur_b) {
         if (cur_b >= 0) epilogue(cur_b);
@@ -324,8 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       const int j = static_cast<int>(x - base);
-      const int tokens = seq_tokens(p, b, P);
-      const int ntok = min(ST, tokens - j * ST);
+      const int ntok = min(ST, tok_b - j * ST);
       const int s = it % NSTAGES;
       const uint32_t ph = (it / NSTAGES) & 1;
       if (!mbar_wait(&full[s], ph, p.err)) {
@@ -411,7 +444,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         // ---- score side data ------------------------------------------------
         if (mode != CE_MODE_NONE) {
-          const int64_t cbase = static_cast<int64_t>(p.kv_indptr[b]) + static_cast<int64_t>(j) * UPS;
+          const int64_t cbase = ip_b + static_cast<int64_t>(j) * UPS;
           if (P == 1) {
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
@@ -453,6 +486,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ---- finalize: split combine + scores ------------------------------------------
 constexpr int FIN_THREADS = 256;
+constexpr int FIN_WARPS = FIN_THREADS / 32;
+constexpr int MAX_SLOTS = 160 * NCW;   // (record, sub-part) slots a sequence can span
+constexpr int UNITS_PER_TASK = 128;
 
 struct FinParams {
   Params a;
@@ -464,153 +500,202 @@ __device__ __forceinline__ int cta_of_stage(int64_t x, int64_t S, int64_t grid) 
   return static_cast<int>(((x + 1) * grid - 1) / S);
 }
 
-// log2 normaliser of query head h of sequence b over its records and the sink.
-__device__ float head_lse2(const FinParams& f, int b, int h, int k0, int k1) {
-  const Params& p = f.a;
-  const int G = p.G;
-  const int g = h / GROUP, r = h % GROUP;
-  const int subs = NCW / G;
-  float M = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
-  for (int k = k0; k <= k1; ++k) {
-    const float* rec = p.rec + static_cast<int64_t>(b + k) * REC_FLOATS;
-    for (int sb = 0; sb < subs; ++sb) {
-      const int vrow = (sb * G + g) * 8 + r;
-      M = fmaxf(M, rec[REC_ROWS * D + vrow]);
-    }
+// When there are fewer stages than CTAs some partitions are empty and leave
+// no record; a sequence's record range [k0, k1] may straddle them.
+__device__ __forceinline__ bool cta_has_work(int64_t k, int64_t S, int64_t grid) {
+  return (k * S) / grid < ((k + 1) * S) / grid;
+}
+
+__device__ __forceinline__ void seq_records(const Params& p, int b, int64_t S, int64_t grid,
+                                            int& k0, int& k1) {
+  const int64_t pre = p.prefix[b], n = p.prefix[b + 1] - pre;
+  if (n <= 0) {
+    k0 = 1;
+    k1 = 0;
+    return;
   }
-  if (M == -INFINITY) return -INFINITY;
-  float den = p.sinks ? exp2f(p.sinks[h] * LOG2E - M) : 0.f;
-  for (int k = k0; k <= k1; ++k) {
+  k0 = cta_of_stage(pre, S, grid);
+  k1 = cta_of_stage(pre + n - 1, S, grid);
+}
+
+// Warp-cooperative log2 normaliser of query head h over its (record, sub)
+// slots plus the sink.  Every lane returns M and L2 = log2 sum.
+__device__ __forceinline__ void warp_head_norm(const Params& p, int b, int h, int k0, int k1,
+                                               int64_t S, int64_t grid, float& M, float& L2) {
+  const int lane = threadIdx.x & 31;
+  const int G = p.G, g = h / GROUP, r = h % GROUP, subs = NCW / G;
+  const int nslots = (k1 - k0 + 1) * subs;
+  float m = -INFINITY;
+  for (int i = lane; i < nslots; i += 32) {
+    const int k = k0 + i / subs, sb = i % subs;
+    if (!cta_has_work(k, S, grid)) continue;
     const float* rec = p.rec + static_cast<int64_t>(b + k) * REC_FLOATS;
-    for (int sb = 0; sb < subs; ++sb) {
-      const int vrow = (sb * G + g) * 8 + r;
-      const float mk = rec[REC_ROWS * D + vrow];
-      if (mk != -INFINITY) den += rec[REC_ROWS * D + REC_ROWS + vrow] * exp2f(mk - M);
-    }
+    m = fmaxf(m, rec[REC_ROWS * D + (sb * G + g) * 8 + r]);
   }
-  return M + log2f(den);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float sink2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
+  M = fmaxf(m, sink2);
+  if (M == -INFINITY) {
+    L2 = -INFINITY;
+    return;
+  }
+  float den = 0.f;
+  for (int i = lane; i < nslots; i += 32) {
+    const int k = k0 + i / subs, sb = i % subs;
+    if (!cta_has_work(k, S, grid)) continue;
+    const float* rec = p.rec + static_cast<int64_t>(b + k) * REC_FLOATS;
+    const int vrow = (sb * G + g) * 8 + r;
+    const float mk = rec[REC_ROWS * D + vrow];
+    if (mk != -INFINITY) den += rec[REC_ROWS * D + REC_ROWS + vrow] * exp2f(mk - M);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+  if (p.sinks) den += exp2f(sink2 - M);
+  L2 = M + log2f(den);
 }
 
 __global__ void __launch_bounds__(FIN_THREADS)
     finalize_kernel(const FinParams f) {
   const Params& p = f.a;
   const int bs = p.bs, H = p.H, G = p.G, P = f.P;
-  const int64_t S = p.prefix[bs];
-  const int64_t grid = f.grid;
-  const int64_t total_units = min(static_cast<int64_t>(p.kv_indptr[bs]), p.kv_capacity);
-  const int upt = FIN_THREADS / G;  // units per score task
-  const int64_t unit_tasks = (total_units + upt - 1) / upt;
-  const int64_t ntasks = bs + unit_tasks;
-  __shared__ float sh_m[64];
-  __shared__ float sh_inv[64];
   const int subs = NCW / G;
+  const int64_t S = p.prefix[bs];
+  const int64_t grid = eff_grid(S, f.grid);
+  const int64_t total_units = min(static_cast<int64_t>(p.kv_indptr[bs]), p.kv_capacity);
+  const int hgroups = H / GROUP;
+  const int64_t combine_tasks = static_cast<int64_t>(bs) * hgroups;
+  const bool scoring = p.mode_of_row && p.scores && p.ul;
+  const int64_t unit_tasks = scoring ? (total_units + UNITS_PER_TASK - 1) / UNITS_PER_TASK : 0;
+  const int64_t ntasks = combine_tasks + unit_tasks;
+  __shared__ float wts[GROUP][MAX_SLOTS];
+  __shared__ float sh_l2[64];
+  __shared__ int sh_b;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   for (int64_t task = blockIdx.x; task < ntasks; task += gridDim.x) {
-    if (task < bs) {
-      // -------- combine the records of sequence b into out / lse ------------
-      const int b = static_cast<int>(task);
-      const int64_t pre = p.prefix[b], n = p.prefix[b + 1] - pre;
-      const int k0 = (n > 0) ? cta_of_stage(pre, S, grid) : 1;
-      const int k1 = (n > 0) ? cta_of_stage(pre + n - 1, S, grid) : 0;
-      // Pass 1: per head max and normaliser.
-      if (threadIdx.x < H) {
-        const int h = threadIdx.x;
-        const float L2 = head_lse2(f, b, h, k0, k1);
-        float M = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
-        const int g = h / GROUP, r = h % GROUP;
-        for (int k = k0; k <= k1; ++k) {
-          const float* rec = p.rec + static_cast<int64_t>(b + k) * REC_FLOATS;
-          for (int sb = 0; sb < subs; ++sb) M = fmaxf(M, rec[REC_ROWS * D + (sb * G + g) * 8 + r]);
+    if (task < combine_tasks) {
+      // -------- combine sequence b, query heads hc*8 .. hc*8+7 ---------------
+      const int b = static_cast<int>(task / hgroups), hc = static_cast<int>(task % hgroups);
+      int k0, k1;
+      seq_records(p, b, S, grid, k0, k1);
+      const int nslots = (k1 - k0 + 1) * subs;
+      const int h = hc * GROUP + warp;   // one warp per head
+      float M, L2;
+      warp_head_norm(p, b, h, k0, k1, S, grid, M, L2);
+      const int g = h / GROUP, r = h % GROUP;
+      const bool fits = nslots <= MAX_SLOTS;
+      if (fits) {
+        for (int i = lane; i < nslots; i += 32) {
+          const int k = k0 + i / subs, sb = i % subs;
+          float w = 0.f;
+          if (L2 != -INFINITY && cta_has_work(k, S, grid)) {
+            const float mk = p.rec[static_cast<int64_t>(b + k) * REC_FLOATS + REC_ROWS * D + (sb * G + g) * 8 + r];
+            if (mk != -INFINITY) w = exp2f(mk - L2);
+          }
+          wts[warp][i] = w;
         }
-        sh_m[h] = M;
-        // O = sum_k O_k 2^(m_k - M) / den, den = 2^(L2 - M)
-        sh_inv[h] = (L2 == -INFINITY) ? 0.f : exp2f(M - L2);
-        if (p.lse_out) p.lse_out[static_cast<int64_t>(b) * H + h] = L2 * LN2;
       }
-      __syncthreads();
-      for (int e = threadIdx.x; e < H * D; e += FIN_THREADS) {
-        const int h = e / D, d = e % D;
-        const int g = h / GROUP, r = h % GROUP;
-        const float M = sh_m[h];
+      if (lane == 0 && p.lse_out) p.lse_out[static_cast<int64_t>(b) * H + h] = L2 * LN2;
+      __syncwarp();
+      // Each warp writes its head's 64 outputs: O = sum_slots w_slot * O_slot.
+      for (int d = lane; d < D; d += 32) {
         float acc = 0.f;
-        if (M != -INFINITY) {
-          for (int k = k0; k <= k1; ++k) {
-            const float* rec = p.rec + static_cast<int64_t>(b + k) * REC_FLOATS;
-            for (int sb = 0; sb < subs; ++sb) {
-              const int vrow = (sb * G + g) * 8 + r;
-              const float mk = rec[REC_ROWS * D + vrow];
-              if (mk != -INFINITY) acc += rec[vrow * D + d] * exp2f(mk - M);
+        for (int i = 0; i < nslots; ++i) {
+          const int k = k0 + i / subs, sb = i % subs;
+          float w;
+          if (fits) {
+            w = wts[warp][i];
+          } else {
+            w = 0.f;
+            if (L2 != -INFINITY && cta_has_work(k, S, grid)) {
+              const float mk = p.rec[static_cast<int64_t>(b + k) * REC_FLOATS + REC_ROWS * D + (sb * G + g) * 8 + r];
+              if (mk != -INFINITY) w = exp2f(mk - L2);
             }
           }
+          if (w != 0.f) acc += w * p.rec[static_cast<int64_t>(b + k) * REC_FLOATS + ((sb * G + g) * 8 + r) * D + d];
         }
-        const float v = acc * sh_inv[h];
         const int64_t off = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh + d;
         if (p.out_f32)
-          reinterpret_cast<float*>(p.out)[off] = v;
+          reinterpret_cast<float*>(p.out)[off] = acc;
         else
-          reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v);
+          reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(acc);
       }
-      __syncthreads();
+      __syncwarp();
     } else {
-      // -------- scores of up to 32 units x G heads --------------------------
-      const int64_t u0 = (task - bs) * upt;
-      const int i = threadIdx.x;
-      const int uu = i / G, g = i % G;
-      const int64_t cpos = u0 + uu;
-      if (uu < upt && cpos < total_units && p.mode_of_row && p.scores) {
-        // sequence owning cpos: last b with kv_indptr[b] <= cpos
+      // -------- scores of UNITS_PER_TASK consecutive CSR units ----------------
+      const int64_t u0 = (task - combine_tasks) * UNITS_PER_TASK;
+      const int64_t u_end = min(u0 + UNITS_PER_TASK, total_units);
+      if (threadIdx.x == 0) {
         int lo = 0, hi = bs - 1;
         while (lo < hi) {
           const int mid = (lo + hi + 1) >> 1;
-          if (p.kv_indptr[mid] <= cpos) lo = mid; else hi = mid - 1;
+          if (p.kv_indptr[mid] <= u0) lo = mid; else hi = mid - 1;
         }
-        const int b = lo;
+        sh_b = lo;
+      }
+      __syncthreads();
+      int b = sh_b;
+      int64_t u = u0;
+      while (u < u_end && b < bs) {
+        const int64_t seg_end = min(u_end, static_cast<int64_t>(p.kv_indptr[b + 1]));
         int mode = seq_mode(p, b);
         if (mode == CE_MODE_MAX && P > 1 && !p.tl) mode = CE_MODE_NONE;
-        if ((mode == CE_MODE_SUM || mode == CE_MODE_MAX) && p.ul) {
+        if ((mode == CE_MODE_SUM || mode == CE_MODE_MAX) && seg_end > u) {
+          int k0, k1;
+          seq_records(p, b, S, grid, k0, k1);
+          for (int h = warp; h < H; h += FIN_WARPS) {
+            float M, L2;
+            warp_head_norm(p, b, h, k0, k1, S, grid, M, L2);
+            if (lane == 0) sh_l2[h] = L2;
+          }
+          __syncthreads();
           const int tokens = seq_tokens(p, b, P);
           const int npages = (tokens + P - 1) / P;
-          const int64_t jj = cpos - p.kv_indptr[b];
-          if (jj < npages) {
+          const int64_t npairs = (seg_end - u) * G;
+          for (int64_t pr = threadIdx.x; pr < npairs; pr += FIN_THREADS) {
+            const int64_t cpos = u + pr / G;
+            const int g = static_cast<int>(pr % G);
+            const int64_t jj = cpos - p.kv_indptr[b];
+            if (jj >= npages) continue;
             const int unit = p.kv_indices[cpos];
-            if (unit >= 0 && unit < p.pool_units) {
-              const int64_t pre = p.prefix[b], n = p.prefix[b + 1] - pre;
-              const int k0 = cta_of_stage(pre, S, grid);
-              const int k1 = cta_of_stage(pre + n - 1, S, grid);
-              float L2[GROUP];
+            if (unit < 0 || unit >= p.pool_units) {
+              flag_error(p.err, CE_EW_INDEX);
+              continue;
+            }
+            const float* L2 = sh_l2 + g * GROUP;
+            float contrib = 0.f;
+            if (mode == CE_MODE_SUM) {
+              const float* uv = p.ul + cpos * H + g * GROUP;
 #pragma unroll
-              for (int rr = 0; rr < GROUP; ++rr) L2[rr] = head_lse2(f, b, g * GROUP + rr, k0, k1);
-              float contrib = 0.f;
-              if (mode == CE_MODE_SUM) {
-                const float* u = p.ul + cpos * H + g * GROUP;
+              for (int rr = 0; rr < GROUP; ++rr)
+                if (uv[rr] != -INFINITY) contrib += exp2f(uv[rr] - L2[rr]);
+            } else if (P == 1) {
+              const float* uv = p.ul + cpos * H + g * GROUP;
+              float mx = 0.f;
 #pragma unroll
-                for (int rr = 0; rr < GROUP; ++rr)
-                  if (u[rr] != -INFINITY) contrib += exp2f(u[rr] - L2[rr]);
-              } else if (P == 1) {
-                const float* u = p.ul + cpos * H + g * GROUP;
+              for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
+              contrib = mx;
+            } else {
+              const int vt = (jj == npages - 1) ? tokens - static_cast<int>(jj) * P : P;
+              for (int tt = 0; tt < vt; ++tt) {
+                const float* uv = p.tl + (cpos * P + tt) * H + g * GROUP;
                 float mx = 0.f;
 #pragma unroll
-                for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(u[rr] - L2[rr]));
-                contrib = mx;
-              } else {
-                const int vt = (jj == npages - 1) ? tokens - static_cast<int>(jj) * P : P;
-                for (int tt = 0; tt < vt; ++tt) {
-                  const float* u = p.tl + (cpos * P + tt) * H + g * GROUP;
-                  float mx = 0.f;
-#pragma unroll
-                  for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(u[rr] - L2[rr]));
-                  contrib += mx;
-                }
+                for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
+                contrib += mx;
               }
-              float* sp = p.scores + g * p.score_sg + unit;
-              const bool fresh = p.zero_new && jj == npages - 1 && ((tokens - 1) % P) == 0;
-              *sp = fresh ? contrib : *sp + contrib;
-            } else {
-              flag_error(p.err, CE_EW_INDEX);
             }
+            float* sp = p.scores + g * p.score_sg + unit;
+            const bool fresh = p.zero_new && jj == npages - 1 && ((tokens - 1) % P) == 0;
+            *sp = fresh ? contrib : *sp + contrib;
           }
         }
+        __syncthreads();
+        u = max(u, seg_end);
+        ++b;
       }
+      __syncthreads();
     }
   }
 }

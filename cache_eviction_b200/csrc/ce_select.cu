@@ -616,7 +616,7 @@ __global__ void bvalidate_kernel(const BParams p) {
   int32_t* res = p.result + i * 4;
   res[0] = st;
   res[1] = r.N;
-  res[2] = (st == 0) ? after : r.N;
+  res[2] = (st == 0) ? after : (st == 2 ? info[1] : r.N);
   res[3] = 0;
 }
 

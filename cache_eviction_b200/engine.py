@@ -1,0 +1,316 @@
+"""Ragged continuous-batch decode with per-row KV eviction, on the device.
+
+The engine keeps every row of a continuous batch packed in one paged pool per
+full-attention layer and drives the four kernels through the C ABI:
+
+  * per step: ce_fill builds one CSR over all rows (compacted residents then
+    the tail, runtime:136-152), and ce_decode_attn_score runs the fused decode
+    attention + H2O score for each full layer;
+  * at boundaries (a row's length hits a multiple of 2048, runtime:692-710):
+    ce_boundary selects and compacts every due row in one batched call.
+
+Rows, their policies and lengths live on the host (like SGLang's scheduler);
+eviction state (tables, positions, scores, pools) lives on the device.  With
+tensor parallelism each rank holds kv_heads/tp heads of every row; the only
+cross-rank exchange on the eviction path is the all-gather of per-head scores
+that H2O global needs at a boundary (tp.py adds the attention-output reduction).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import capi, kernels
+from .policy import INTERVAL, EvictionConfig
+
+D = 64
+
+
+@dataclass
+class Row:
+    cfg: Optional[EvictionConfig]    # None = full cache, no eviction
+    n: int                           # tokens in the cache
+    last_boundary: int = 0
+    frontier: int = 0                # units
+    count: int = 0                   # units
+    events: list = field(default_factory=list)
+    freed: int = 0
+
+
+class RaggedDecodeEngine:
+    def __init__(self, *, layers: int, q_heads: int, kv_heads: int, page_size: int,
+                 pool_units: int, max_rows: int, r2u_width: int, pos_cap: int,
+                 device="cuda", head_offset: int = 0, global_kv_heads: Optional[int] = None,
+                 process_group=None, alloc_pools: bool = True):
+        self.L, self.H, self.G, self.P = layers, q_heads, kv_heads, page_size
+        self.units = pool_units
+        self.device = torch.device(device)
+        self.head_offset = head_offset
+        self.global_G = global_kv_heads or kv_heads
+        self.group = process_group
+        dev = self.device
+        if alloc_pools:
+            shape = (pool_units, kv_heads, page_size, D)
+            self.k = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(layers)]
+            self.v = [torch.empty(shape, dtype=torch.bfloat16, device=dev) for _ in range(layers)]
+            self.kptr = kernels.layer_pointers(self.k, dev)
+            self.vptr = kernels.layer_pointers(self.v, dev)
+        self.scores = torch.zeros((layers, kv_heads, pool_units), dtype=torch.float32, device=dev)
+        self.table = torch.zeros((max_rows, pos_cap), dtype=torch.int32, device=dev)
+        self.r2u = torch.zeros((max_rows, r2u_width), dtype=torch.int32, device=dev)
+        self.frontier = torch.zeros(max_rows, dtype=torch.int32, device=dev)
+        self.count = torch.zeros(max_rows, dtype=torch.int32, device=dev)
+        self.mode = torch.zeros(max_rows, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros((max_rows, layers, kv_heads, pos_cap), dtype=torch.int32, device=dev)
+        self.marks = torch.zeros(pool_units, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.epoch = 0
+        self.pos_cap = pos_cap
+        self.rows: dict[int, Row] = {}
+        self.active: list[int] = []
+        self.kv_indptr = torch.zeros(max_rows + 1, dtype=torch.int32, device=dev)
+        self.kv_tokens = torch.zeros(max_rows, dtype=torch.int32, device=dev)
+        self.kv_indices = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.rows_dev = torch.zeros(0, dtype=torch.int64, device=dev)
+        self.seq_lens_dev = torch.zeros(0, dtype=torch.int64, device=dev)
+        self.free_units: list = []
+        self.boundary_ms: list = []
+
+    # ------------------------------------------------------------- rows
+    def add_row(self, row: int, cfg: Optional[EvictionConfig], n: int, last_boundary: int = 0,
+                frontier_units: int = 0, count_units: int = 0):
+        self.rows[row] = Row(cfg=cfg, n=n, last_boundary=last_boundary, frontier=frontier_units,
+                             count=count_units)
+        self.mode[row] = cfg.score_mode if cfg is not None else capi.CE_MODE_NONE
+        self.frontier[row] = frontier_units
+        self.count[row] = count_units
+        if row not in self.active:
+            self.active.append(row)
+
+    def commit_rows(self):
+        """Upload the active row list and lengths (after rows were added)."""
+        self.rows_dev = torch.tensor(self.active, dtype=torch.int64, device=self.device)
+        self.seq_lens_dev = torch.tensor([self.rows[r].n for r in self.active], dtype=torch.int64,
+                                         device=self.device)
+        self._ensure_capacity()
+
+    def resident_units(self, r: int, extra_tokens: int = 0) -> int:
+        row = self.rows[r]
+        units = -(-(row.n + extra_tokens) // self.P)
+        return row.count + max(0, units - row.frontier)
+
+    def resident_tokens(self, r: int) -> int:
+        row = self.rows[r]
+        return row.count * self.P + row.n - row.frontier * self.P
+
+    def _ensure_capacity(self, extra_tokens: int = 1):
+        need = sum(self.resident_units(r, extra_tokens) for r in self.active) + 16
+        if self.kv_indices.numel() < need:
+            self.kv_indices = torch.zeros(int(need * 1.25), dtype=torch.int32, device=self.device)
+
+    # -------------------------------------------------------- boundaries
+    def due(self) -> list:
+        """Rows whose length sits on a boundary not yet taken (runtime:706)."""
+        out = []
+        for r in self.active:
+            row = self.rows[r]
+            if row.cfg is None:
+                continue
+            if row.n % INTERVAL == 0 and row.n > row.last_boundary:
+                out.append(r)
+        return out
+
+    def run_boundaries(self, rows: list, cursors: Optional[dict] = None, live: bool = True,
+                       swa: Optional[torch.Tensor] = None, hazard_bytes: int = 512 << 20):
+        """One batched ce_boundary over `rows`; returns the per-row results (host)."""
+        if not rows:
+            return []
+        P = self.P
+        params, ncols = [], []
+        for r in rows:
+            row = self.rows[r]
+            b, p, q = row.cfg.units(P)
+            n_u = row.n // P
+            cur = None if not cursors or cursors.get(r) is None else cursors[r] // P
+            params.append(dict(n=n_u, budget=b, prefix=p, recent=q, cursor=cur,
+                               policy=row.cfg.policy_id, seed=row.cfg.seed))
+            ncols.append(row.count + n_u - row.frontier)
+            row.last_boundary = row.n
+        max_cols = max(ncols)
+        max_n = max(prm["n"] for prm in params) + 1
+        dev = self.device
+        uniforms = None
+        if any(self.rows[r].cfg.name == "random_2048" for r in rows):
+            uniforms = torch.zeros((len(rows), self.L, self.G, max_cols), dtype=torch.float64, device=dev)
+            for i, r in enumerate(rows):
+                row = self.rows[r]
+                if row.cfg.name != "random_2048":
+                    continue
+                gen = torch.Generator(device=dev).manual_seed((row.cfg.seed * 1000003 + row.n) & 0x7FFFFFFF)
+                draw = torch.rand((self.L, self.global_G, ncols[i]), generator=gen, device=dev,
+                                  dtype=torch.float64)
+                h0 = self.head_offset
+                uniforms[i, :, :, :ncols[i]] = draw[:, h0:h0 + self.G]
+        rows_t = torch.tensor(rows, dtype=torch.int32, device=dev)
+        params_t = kernels.row_params(params, dev)
+        gscores = None
+        if self.group is not None and any(self.rows[r].cfg.name == "h2o_global_2048" for r in rows):
+            from . import tp
+            local = kernels.gather_row_scores(self.table, self.r2u, self.frontier, self.count,
+                                              self.scores, rows_t, params_t, max_cols, self.err)
+            gscores = tp.all_gather_heads(local, self.group)
+        self.epoch += 1
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        result, freed = kernels.boundary(
+            self.table, self.r2u, self.frontier, self.count, self.pos, self.scores, self.kptr,
+            self.vptr, self.G, P, rows_t, params_t, max_cols, max_n, live, marks=self.marks,
+            epoch=self.epoch, swa=swa, uniforms=uniforms, global_scores=gscores,
+            head_offset=self.head_offset, hazard_bytes=hazard_bytes, err=self.err)
+        end.record()
+        res = result.cpu().numpy()   # one readback per boundary batch, as the reference syncs
+        self.boundary_ms.append(start.elapsed_time(end))
+        fr = None
+        for i, r in enumerate(rows):
+            row = self.rows[r]
+            status, before, after, nfreed = (int(x) for x in res[i])
+            row.events.append(dict(boundary=row.n, status=status, before=before, after=after,
+                                   freed=nfreed))
+            if status == 0:
+                row.frontier, row.count = row.n // P, after
+                if live and nfreed:
+                    if fr is None:
+                        fr = freed.cpu().numpy()
+                    self.free_units.extend(fr[i, :nfreed].tolist())
+                    row.freed += nfreed
+            elif status not in (1, 2):
+                raise RuntimeError(f"boundary for row {r} failed with status {status}")
+        return res
+
+    # ------------------------------------------------------------ decode
+    def fill(self):
+        bs = len(self.active)
+        kernels.fill(self.table, self.r2u, self.frontier, self.count, self.rows_dev,
+                     self.seq_lens_dev, self.P, self.kv_indptr[:bs + 1], self.kv_indices,
+                     self.kv_tokens[:bs], self.err)
+
+    def decode_layer(self, layer: int, q: torch.Tensor, out: torch.Tensor, sinks, scale: float,
+                     score_flags: int = 3):
+        bs = len(self.active)
+        return kernels.decode_attn_score(
+            q, self.k[layer], self.v[layer], self.kv_indptr[:bs + 1], self.kv_indices,
+            self.kv_tokens[:bs], scale, self.P, sinks=sinks, mode_of_row=self.mode,
+            rows=self.rows_dev, scores=self.scores[layer], zero_new=True, out=out,
+            score_flags=score_flags, err=self.err)
+
+    def advance(self):
+        """Append one token to every active row (host lengths and the device copy)."""
+        for r in self.active:
+            self.rows[r].n += 1
+        self.seq_lens_dev.add_(1)
+
+    def step(self, q_layers, out_layers, sinks, scale, after_layer=None):
+        """One decode step: due boundaries, one token appended, CSR, every layer."""
+        self.run_boundaries(self.due())
+        self.advance()
+        self._ensure_capacity(0)
+        self.fill()
+        for l in range(self.L):
+            self.decode_layer(l, q_layers[l], out_layers[l], sinks[l], scale)
+            if after_layer is not None:
+                after_layer(l, out_layers[l])
+
+    def check_errors(self):
+        torch.cuda.synchronize(self.device)
+        word = int(self.err.item())
+        if word:
+            raise RuntimeError(f"device error word 0x{word:x}")
+
+
+# -------------------------------------------------------------- synthesis
+def synth_state(engine: RaggedDecodeEngine, specs: list, steps: int, seed: int,
+                score_sigma: float = 2.0, fill_pools: bool = True):
+    """Initialise rows as if every boundary up to each context had been taken.
+
+    specs: dicts with ctx (tokens), cfg (EvictionConfig or None).  Each evicting
+    row holds prefix + recent + budget-remainder residents after its last
+    evicting boundary (ascending positions, per-head middle picks for per-head
+    policies, shared picks for H2O global) and its tail since that boundary.
+    Units are drawn from a shuffled pool; the pool holds each row's future
+    pages for `steps` more tokens.  Scores of H2O rows are lognormal(0, sigma).
+    """
+    rng = np.random.default_rng(seed)
+    P, L, G = engine.P, engine.L, engine.G
+    order = rng.permutation(np.arange(1, engine.units)).astype(np.int32)
+    cursor = 0
+
+    def take(k):
+        nonlocal cursor
+        out = order[cursor:cursor + k]
+        cursor += k
+        if len(out) < k:
+            raise RuntimeError("pool too small for the synthetic state")
+        return out
+
+    table = engine.table.cpu().numpy()
+    r2u = engine.r2u.cpu().numpy()
+    pos = engine.pos.cpu().numpy()
+    scores_rows = []
+    for r, sp in enumerate(specs):
+        cfg, ctx = sp["cfg"], int(sp["ctx"])
+        end_units = -(-(ctx + steps) // P)
+        frontier = count = 0
+        last = (ctx // INTERVAL) * INTERVAL
+        if cfg is not None and last > cfg.budget:
+            b_u, p_u, r_u = cfg.units(P)
+            f_u = last // P
+            w_u = b_u - p_u - r_u
+            units = take(b_u)
+            table[r, :b_u] = units
+            recent = np.arange(f_u - r_u, f_u)
+            prefix = np.arange(p_u)
+            middle_pool = np.arange(p_u, f_u - r_u)
+            shared = cfg.name in ("h2o_global_2048", "prefix_sliding_2048")
+            if shared:
+                mid = np.sort(rng.choice(middle_pool, w_u, replace=False)) if w_u else np.zeros(0, int)
+            for l in range(L):
+                for g in range(G):
+                    if not shared:
+                        mid = np.sort(rng.choice(middle_pool, w_u, replace=False)) if w_u else np.zeros(0, int)
+                    pos[r, l, g, :b_u] = np.concatenate([prefix, recent, mid])
+            # req_to_unit: real units at the protected recent positions, the rest packed
+            true_u = f_u - r_u
+            r2u[r, true_u:f_u] = units[p_u:p_u + r_u]
+            packed = np.concatenate([units[:p_u], units[p_u + r_u:]])
+            r2u[r, :len(packed)] = packed
+            tail = take(end_units - f_u)
+            r2u[r, f_u:end_units] = tail
+            frontier, count = f_u, b_u
+            owned = np.concatenate([units, tail[:-(-(ctx - last) // P) if ctx > last else 0]])
+        else:
+            tail = take(end_units)
+            r2u[r, :end_units] = tail
+            owned = tail[:-(-ctx // P)]
+            last = last if cfg is not None else 0
+        engine.add_row(r, cfg, ctx, last_boundary=last if cfg is not None else 0,
+                       frontier_units=frontier, count_units=count)
+        if cfg is not None and cfg.score_mode != capi.CE_MODE_NONE:
+            scores_rows.append(owned)
+    engine.table.copy_(torch.from_numpy(table))
+    engine.r2u.copy_(torch.from_numpy(r2u))
+    engine.pos.copy_(torch.from_numpy(pos))
+    if scores_rows:
+        idx = torch.from_numpy(np.concatenate(scores_rows).astype(np.int64)).to(engine.device)
+        gen = torch.Generator(device=engine.device).manual_seed(seed + 7)
+        vals = torch.randn((L, G, idx.numel()), generator=gen, device=engine.device) * score_sigma
+        engine.scores[:, :, idx] = vals.exp_()
+    if fill_pools:
+        gen = torch.Generator(device=engine.device).manual_seed(seed + 11)
+        for t in engine.k + engine.v:
+            t.normal_(generator=gen)
+    engine.commit_rows()
+    return cursor + 1

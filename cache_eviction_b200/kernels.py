@@ -1,0 +1,233 @@
+"""torch-tensor front end of the C ABI (libce_b200.so).
+
+torch supplies device memory and the current CUDA stream; every call goes
+through capi (ctypes) into the sm_100a kernels.  Workspaces are cached per
+device and grown on demand from torch's caching allocator, so steady-state
+calls allocate nothing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import capi
+
+ROW_DTYPE = np.dtype([("n", "<i4"), ("budget", "<i4"), ("prefix", "<i4"), ("recent", "<i4"),
+                      ("cursor", "<i4"), ("policy", "<i4"), ("seed", "<u8")])
+POLICY_IDS = {"prefix_sliding_2048": capi.CE_POLICY_PREFIX_SLIDING,
+              "random_2048": capi.CE_POLICY_RANDOM,
+              "random_reservoir_2048": capi.CE_POLICY_RESERVOIR,
+              "head_sum_2048": capi.CE_POLICY_HEAD_SUM,
+              "head_max_sum_2048": capi.CE_POLICY_HEAD_MAX,
+              "h2o_global_2048": capi.CE_POLICY_H2O_GLOBAL}
+U64_MASK = (1 << 64) - 1
+
+
+def _p(t: Optional[torch.Tensor]):
+    if t is None:
+        return None
+    return C.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+class _Workspaces:
+    def __init__(self):
+        self._bufs: dict = {}
+
+    def get(self, device: torch.device, key: str, nbytes: int) -> torch.Tensor:
+        k = (device.index if device.index is not None else torch.cuda.current_device(), key)
+        buf = self._bufs.get(k)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(int(nbytes * 1.25), 256), dtype=torch.uint8, device=device)
+            self._bufs[k] = buf
+        return buf
+
+
+WORKSPACES = _Workspaces()
+
+# Kernel launches issued through this module (the C entry points' own
+# kernels, not torch's); bench.py reports the count over its timed region.
+LAUNCHES = [0]
+
+
+def _count(n: int) -> None:
+    LAUNCHES[0] += n
+
+
+def row_params(rows: Sequence[dict], device) -> torch.Tensor:
+    """Pack boundary parameters (units) into a device array of ce_row_params."""
+    arr = np.zeros(len(rows), dtype=ROW_DTYPE)
+    for i, r in enumerate(rows):
+        for k in ("n", "budget", "prefix", "recent"):
+            arr[i][k] = int(r[k])
+        arr[i]["cursor"] = -1 if r.get("cursor") is None else int(r["cursor"])
+        pol = r["policy"]
+        arr[i]["policy"] = POLICY_IDS[pol] if isinstance(pol, str) else int(pol)
+        arr[i]["seed"] = int(r.get("seed", 0)) & U64_MASK
+    return torch.from_numpy(arr.view(np.uint8).copy()).to(device)
+
+
+def error_word(device) -> torch.Tensor:
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def fill(table, req_to_unit, frontier, count, rows, seq_lens, page_size, kv_indptr, kv_indices,
+         kv_tokens=None, err=None):
+    """CSR of compacted residents then the tail (runtime:136-152)."""
+    lib = capi.load()
+    bs = int(rows.numel())
+    assert rows.dtype == torch.int64 and seq_lens.dtype == torch.int64
+    assert kv_indices.dtype in (torch.int32, torch.int64)
+    st = lib.ce_fill(_p(table), table.stride(0), _p(req_to_unit), req_to_unit.stride(0),
+                     _p(frontier), _p(count), _p(rows), _p(seq_lens), bs, page_size,
+                     _p(kv_indptr), _p(kv_indices), 1 if kv_indices.dtype == torch.int64 else 0,
+                     kv_indices.numel(), _p(kv_tokens), _p(err), _stream(kv_indptr.device))
+    capi.check(st, "ce_fill")
+    _count(1 if bs else 0)
+    return kv_indptr
+
+
+def decode_attn_score(q, k_pool, v_pool, kv_indptr, kv_indices, kv_tokens, sm_scale, page_size,
+                      sinks=None, mode_of_row=None, rows=None, scores=None, zero_new=True,
+                      out=None, out_f32=False, lse=None, score_flags=3, err=None):
+    """Fused decode attention + H2O score over one layer.
+
+    q [bs, H, 64] bf16; pools [units, G, page, 64] bf16; scores [G, units] fp32.
+    Returns out [bs, H, 64] (bf16, or fp32 with out_f32).
+    """
+    lib = capi.load()
+    bs, H, D = q.shape
+    G = k_pool.shape[1]
+    assert q.dtype == torch.bfloat16 and q.stride(2) == 1
+    assert k_pool.is_contiguous() and v_pool.is_contiguous()
+    assert kv_indices.dtype == torch.int32 and kv_indptr.dtype == torch.int32
+    dev = q.device
+    if out is None:
+        out = torch.empty((bs, H, D), dtype=torch.float32 if out_f32 else torch.bfloat16, device=dev)
+    if sinks is not None and sinks.dtype != torch.float32:
+        sinks = sinks.float()
+    if scores is not None:
+        assert scores.dtype == torch.float32 and scores.stride(1) == 1
+    cap = kv_indices.numel()
+    need = lib.ce_decode_workspace_bytes(bs, cap, H, G, page_size, score_flags)
+    if need < 0:
+        raise capi.CeError("ce_decode_workspace_bytes failed")
+    ws = WORKSPACES.get(dev, "decode", need)
+    st = lib.ce_decode_attn_score(
+        _p(q), q.stride(0), q.stride(1), _p(k_pool), _p(v_pool), k_pool.shape[0], _p(kv_indptr),
+        _p(kv_indices), _p(kv_tokens), cap, _p(sinks), _p(mode_of_row), _p(rows), float(sm_scale),
+        bs, H, G, D, page_size, _p(scores), scores.stride(0) if scores is not None else 0,
+        1 if zero_new else 0, _p(out), 1 if out.dtype == torch.float32 else 0, out.stride(0),
+        out.stride(1), _p(lse), score_flags, _p(ws), ws.numel(), _p(err), _stream(dev))
+    capi.check(st, "ce_decode_attn_score")
+    _count(2 if bs else 0)
+    return out
+
+
+def choose(pos, score, params: torch.Tensor, layers, heads, max_n, ncols=None, head_offset=0,
+           kept_stride=None, err=None):
+    """Kept columns [problems, segs, kept_stride] in ascending position (runtime:376-412)."""
+    lib = capi.load()
+    problems, segs, n_cols = pos.shape
+    dev = pos.device
+    kept_stride = kept_stride or n_cols
+    kept = torch.full((problems, segs, kept_stride), -1, dtype=torch.int32, device=dev)
+    status = torch.zeros(problems, dtype=torch.int32, device=dev)
+    pcount = torch.zeros(problems, dtype=torch.int32, device=dev)
+    sdt = capi.CE_DTYPE_NONE
+    if score is not None:
+        sdt = capi.CE_DTYPE_F64 if score.dtype == torch.float64 else capi.CE_DTYPE_F32
+        assert score.is_contiguous() and score.shape == pos.shape
+    need = lib.ce_choose_workspace_bytes(problems, segs, n_cols)
+    ws = WORKSPACES.get(dev, "choose", need)
+    st = lib.ce_choose(_p(pos.contiguous()), _p(ncols), n_cols, _p(score), sdt, _p(params), problems,
+                       int(max_n), layers, heads, head_offset, _p(kept), kept_stride, _p(status),
+                       _p(pcount), _p(ws), ws.numel(), _p(err), _stream(dev))
+    capi.check(st, "ce_choose")
+    _count(2 if problems else 0)
+    return kept, status, pcount
+
+
+def layer_pointers(tensors: Sequence[torch.Tensor], device) -> torch.Tensor:
+    return torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64, device=device)
+
+
+def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, kv_heads, page_size,
+             rows, params, max_cols, max_n, live, marks=None, epoch=0, swa=None, uniforms=None,
+             global_scores=None, head_offset=0, freed=None, hazard_bytes=256 << 20, err=None):
+    """One eviction boundary for a batch of rows (runtime:415-507).
+
+    Returns (result [R, 4] int32 device tensor, freed [R, max_cols] int32).
+    """
+    lib = capi.load()
+    dev = table.device
+    R = int(rows.numel())
+    L = int(k_ptrs.numel())
+    result = torch.zeros((max(R, 1), 4), dtype=torch.int32, device=dev)
+    if freed is None:
+        freed = torch.full((max(R, 1), max(max_cols, 1)), -1, dtype=torch.int32, device=dev)
+    need = lib.ce_boundary_workspace_bytes(R, L, kv_heads, 64, page_size, max_cols,
+                                           global_scores.shape[2] if global_scores is not None else 0,
+                                           hazard_bytes)
+    if need < 0:
+        raise capi.CeError("ce_boundary_workspace_bytes failed")
+    ws = WORKSPACES.get(dev, "boundary", need)
+    udt = capi.CE_DTYPE_NONE
+    if uniforms is not None:
+        udt = capi.CE_DTYPE_F64 if uniforms.dtype == torch.float64 else capi.CE_DTYPE_F32
+    st = lib.ce_boundary(
+        _p(table), table.stride(0), table.shape[1], _p(req_to_unit), req_to_unit.stride(0),
+        req_to_unit.shape[1], _p(frontier), _p(count), _p(pos), pos.stride(0), pos.shape[3],
+        _p(scores), scores.stride(0), scores.stride(1), scores.shape[2], _p(k_ptrs), _p(v_ptrs), L,
+        kv_heads, 64, page_size, head_offset, _p(marks), int(epoch), _p(swa), _p(rows), _p(params),
+        R, _p(uniforms), udt, _p(global_scores),
+        global_scores.shape[2] if global_scores is not None else 0, 1 if live else 0, max_cols,
+        int(max_n), _p(result), _p(freed), freed.stride(0), _p(ws), ws.numel(), int(hazard_bytes),
+        _p(err), _stream(dev))
+    capi.check(st, "ce_boundary")
+    if R:
+        one = R * kv_heads * max_cols * 2 * page_size * 128
+        group = max(1, min(L, max(int(hazard_bytes), one) // max(one, 1)))
+        _count(3 + 2 * ceil_div(L, group))
+    return result, freed
+
+
+def gather_row_scores(table, req_to_unit, frontier, count, scores, rows, params, max_cols, err=None):
+    lib = capi.load()
+    dev = table.device
+    R = int(rows.numel())
+    L, G, units = scores.shape
+    out = torch.zeros((R, L, G, max_cols), dtype=torch.float32, device=dev)
+    st = lib.ce_gather_row_scores(_p(table), table.stride(0), _p(req_to_unit), req_to_unit.stride(0),
+                                  _p(frontier), _p(count), _p(scores), scores.stride(0),
+                                  scores.stride(1), units, L, G, _p(rows), _p(params), R, max_cols,
+                                  _p(out), _p(err), _stream(dev))
+    capi.check(st, "ce_gather_row_scores")
+    return out
+
+
+def reservoir_scores53(pos: torch.Tensor, seed: int, head_offset: int = 0) -> torch.Tensor:
+    """splitmix64 draws as 53-bit integers [L, G, N] (int64 storage of the uint64)."""
+    lib = capi.load()
+    L, G, N = pos.shape
+    pos32 = pos.to(torch.int32).contiguous()
+    out = torch.empty((L, G, N), dtype=torch.int64, device=pos.device)
+    st = lib.ce_reservoir_scores(_p(pos32), L, G, N, head_offset, int(seed) & U64_MASK, _p(out),
+                                 _stream(pos.device))
+    capi.check(st, "ce_reservoir_scores")
+    return out
+
+
+def ceil_div(a: int, b: int) -> int:
+    return -(-a // b)
+
+
+def next_pow2(x: int) -> int:
+    return 1 << max(0, math.ceil(math.log2(max(1, x))))

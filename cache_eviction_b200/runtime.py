@@ -1,0 +1,451 @@
+"""Drop-in mirror of the overlay module ``sglang.srt.gstar_evict``.
+
+Same hook names, arguments and error behaviour as the reference's
+code/cache_eviction/sglang_evict_runtime.py ("runtime:" below), with the work
+done by the sm_100a kernels behind include/ce_api.h:
+
+  enabled()                                  runtime:53-54
+  fill(backend, bs, seq_lens, rows, kv_indices) -> kv_indptr       runtime:136-152
+  decode(backend, q, layer, forward_batch, sinks, out)   fused attention + score
+  after_decode(backend, q, layer, forward_batch, sinks, out=None)  runtime:203-224
+  after_extend(backend, q, layer, forward_batch, sinks)            runtime:277-311
+  on_extend(batch), on_decode(batch), release(req)                runtime:640-742
+  filter_holes(segments), freed(row)                               runtime:128-131, 745-747
+  choose(...), reservoir_scores(...), _scores(...), _boundary(...) runtime:358-507
+
+Backends, layers, batches, requests and allocators are the duck-typed SGLang
+objects the reference reads (fields as in code/tests/test_sglang_evict.py:19-39).
+A backend may carry ``page_size`` (units of that many tokens; default 1, the
+reference's token slots) and ``gstar_pos_cap`` (retained units per row).
+
+Differences by design: choose() returns each head's kept columns in ascending
+position order (the reference returns them in key order; the kept sets are
+identical and every caller only uses the sets), and decode() computes the
+attention output together with the scores in one pass over K and V.
+"""
+from __future__ import annotations
+
+import logging
+import os
+import time
+
+import torch
+
+from . import capi, kernels
+from .policy import INTERVAL, POLICIES, SCORE_MODE, canonical, validate
+
+logger = logging.getLogger(__name__)
+
+STATE = None
+RETRACTED: set = set()
+POS_CAP_DEFAULT = 32768
+
+
+def enabled() -> bool:
+    return os.environ.get("GSTAR_EVICT") == "1"
+
+
+# ---------------------------------------------------------------- state
+class State:
+    """Per-process eviction state on the device (runtime:89-110)."""
+
+    def __init__(self, backend):
+        self.pool = backend.token_to_kv_pool
+        self.req_to_token = backend.req_to_token_pool.req_to_token
+        rows, width = self.req_to_token.shape
+        device = self.req_to_token.device
+        self.device = device
+        self.page_size = int(getattr(backend, "page_size", 1) or 1)
+        self.full_layers = sorted(i for i, (_, swa) in self.pool.layers_mapping.items() if not swa)
+        self.index = {layer: i for i, layer in enumerate(self.full_layers)}
+        self.first_full = self.full_layers[0]
+        keys = self.pool.get_key_buffer(self.first_full)
+        self.kv_heads, self.dim = keys.shape[1], keys.shape[-1]
+        self.units = keys.shape[0]
+        self.head_offset = int(getattr(backend, "gstar_head_offset", 0))
+        self.frontier = torch.zeros(rows, dtype=torch.int32, device=device)
+        self.count = torch.zeros(rows, dtype=torch.int32, device=device)
+        self.mode = torch.zeros(rows, dtype=torch.int32, device=device)
+        self.table = torch.zeros((rows, width), dtype=torch.int32, device=device)
+        self.scores = torch.zeros((len(self.full_layers), self.kv_heads, self.units),
+                                  dtype=torch.float32, device=device)
+        self.pos_cap = int(getattr(backend, "gstar_pos_cap", min(width, POS_CAP_DEFAULT)))
+        self.pos = torch.zeros((rows, len(self.full_layers), self.kv_heads, self.pos_cap),
+                               dtype=torch.int32, device=device)
+        self.marks = torch.zeros(self.units, dtype=torch.int32, device=device)
+        self.epoch = 0
+        self.kv_tokens = torch.zeros(rows + 1, dtype=torch.int32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.entries: dict = {}
+        self.verify = os.environ.get("GSTAR_EVICT_VERIFY") == "1"
+        self._ptrs = None
+
+    def pools(self, layer_id):
+        """One layer's K and V as [units, G, page, D] views."""
+        k = self.pool.get_key_buffer(layer_id)
+        v = self.pool.get_value_buffer(layer_id)
+        shape = (k.shape[0], self.kv_heads, self.page_size, self.dim)
+        return k.view(shape), v.view(shape)
+
+    def layer_pointers(self):
+        ptrs = ([self.pool.get_key_buffer(l).data_ptr() for l in self.full_layers],
+                [self.pool.get_value_buffer(l).data_ptr() for l in self.full_layers])
+        if self._ptrs is None or self._ptrs[0] != ptrs:
+            self._ptrs = (ptrs, torch.tensor(ptrs[0], dtype=torch.int64, device=self.device),
+                          torch.tensor(ptrs[1], dtype=torch.int64, device=self.device))
+        return self._ptrs[1], self._ptrs[2]
+
+
+def state(backend=None):
+    global STATE
+    if STATE is None and backend is not None:
+        STATE = State(backend)
+        logger.info("gstar_evict (B200) active: full layers %s, %d KV heads, page %d",
+                    STATE.full_layers, STATE.kv_heads, STATE.page_size)
+    return STATE
+
+
+def _reset(st, row):
+    st.entries.pop(row, None)
+    st.mode[row] = 0
+    st.frontier[row] = 0
+    st.count[row] = 0
+
+
+def freed(row):
+    """Slots this row's evictions returned to the allocator (runtime:128-131)."""
+    entry = STATE.entries.get(row) if STATE is not None else None
+    return entry.get("freed", 0) if entry is not None else 0
+
+
+# ------------------------------------------------------- attention metadata
+def fill(backend, bs, seq_lens, req_pool_indices, kv_indices):
+    """Full-layer CSR: shared resident units below the frontier, then the tail."""
+    st = state(backend)
+    kv_indptr = backend.kv_indptr[: bs + 1]
+    rows = req_pool_indices[:bs].to(torch.int64).contiguous()
+    lens = seq_lens[:bs].to(torch.int64).contiguous()
+    kernels.fill(st.table, st.req_to_token, st.frontier, st.count, rows, lens, st.page_size,
+                 kv_indptr, kv_indices, st.kv_tokens[:bs], st.err)
+    return kv_indptr
+
+
+def _layer_is_sliding(layer):
+    return layer.sliding_window_size is not None and layer.sliding_window_size > -1
+
+
+def _decode(backend, q, layer, forward_batch, sinks, out, zero_new):
+    st = state(backend)
+    meta = backend.forward_metadata
+    heads, dim = layer.tp_q_head_num, layer.qk_head_dim
+    queries = q.view(-1, heads, dim)
+    bs = queries.shape[0]
+    kpool, vpool = st.pools(layer.layer_id)
+    indices = meta.kv_indices
+    if indices.dtype != torch.int32:
+        indices = indices.to(torch.int32)
+    tokens = None if st.page_size == 1 else st.kv_tokens[:bs]
+    rows = forward_batch.req_pool_indices.to(torch.int64)
+    scores = st.scores[st.index[layer.layer_id]]
+    o = None if out is None else out.view(bs, heads, dim)
+    result = kernels.decode_attn_score(
+        queries, kpool, vpool, meta.kv_indptr[: bs + 1].to(torch.int32), indices, tokens,
+        layer.scaling, st.page_size, sinks=sinks, mode_of_row=st.mode, rows=rows, scores=scores,
+        zero_new=zero_new, out=o, err=st.err)
+    return result
+
+
+def decode(backend, q, layer, forward_batch, sinks, out=None):
+    """Fused replacement for decode_attention_fwd + after_decode on a full layer.
+
+    Writes the attention output into ``out`` (allocated when None) and adds
+    this step's H2O mass to the layer's scores in the same pass; the unit that
+    the new token starts is zeroed first (runtime:211-212).
+    """
+    return _decode(backend, q, layer, forward_batch, sinks, out, zero_new=True)
+
+
+def after_decode(backend, q, layer, forward_batch, sinks, out=None):
+    """Scores of one decode step for a layer whose output SGLang already wrote.
+
+    Same effect on the scores as the reference hook: on the first full layer
+    every new slot's score is zeroed for all layers, then each H2O row adds
+    p summed (head_sum) or maxed (head_max) over the KV head's query heads.
+    """
+    if _layer_is_sliding(layer):
+        return
+    st = state(backend)
+    if layer.layer_id == st.first_full:
+        st.scores.index_fill_(2, forward_batch.out_cache_loc.long() // st.page_size, 0.0)
+    _decode(backend, q, layer, forward_batch, sinks, None, zero_new=False)
+
+
+def after_extend(backend, q, layer, forward_batch, sinks):
+    """Prefill scores (runtime:277-311) for H2O rows of an extend batch."""
+    if _layer_is_sliding(layer):
+        return
+    st = state(backend)
+    entries = [st.entries.get(r) for r in forward_batch.req_pool_indices.tolist()]
+    if not any(entries):
+        return
+    if layer.layer_id == st.first_full:
+        st.scores.index_fill_(2, forward_batch.out_cache_loc.long() // st.page_size, 0.0)
+    if any(e is not None and not e["error"] and e["mode"] in (1, 2) for e in entries):
+        raise NotImplementedError("prefill scoring for head_sum/head_max rows needs the prefill "
+                                  "score kernel, which this build does not have yet")
+
+
+# ------------------------------------------------------------- selection
+_MASK = (1 << 64) - 1
+
+
+def reservoir_scores(seed, pos, layers, heads):
+    """splitmix64 score per (seed, layer, KV head, position) (runtime:358-373)."""
+    L, G = int(layers.numel()), int(heads.numel())
+    if not (torch.equal(layers.cpu(), torch.arange(L)) and
+            torch.equal(heads.cpu(), torch.arange(int(heads[0]), int(heads[0]) + G))):
+        raise ValueError("reservoir_scores expects arange layers and contiguous heads")
+    p = pos.expand(L, G, pos.shape[-1]) if pos.dim() == 3 else pos
+    ints = kernels.reservoir_scores53(p.contiguous(), int(seed) & _MASK, int(heads[0]))
+    return ints.double() / float(1 << 53)
+
+
+def choose(name, pos, n, budget, prefix, recent, score, cursor=None):
+    """Survivors of one boundary for every (layer, KV head) row of pos [L, G, N].
+
+    Returns (kept columns [L, G, K] in ascending position, protected count),
+    or (None, count) when protection exceeds the budget; raises RuntimeError
+    when heads protect different counts (runtime:384-397).
+    """
+    name = canonical(name)
+    L, G, N = pos.shape
+    dev = pos.device
+    pos32 = pos.to(torch.int32).reshape(1, L * G, N).contiguous()
+    sc = None
+    if name not in ("prefix_sliding_2048", "random_reservoir_2048") and score is not None:
+        sc = score.reshape(1, L * G, N).contiguous()
+        if sc.dtype not in (torch.float32, torch.float64):
+            sc = sc.double()
+    row = dict(n=int(n), budget=int(budget), prefix=int(prefix), recent=int(recent),
+               cursor=cursor, policy=name, seed=0)
+    if name == "random_reservoir_2048" and score is not None:
+        # the caller supplied reservoir draws: rank them as explicit doubles
+        sc = score.reshape(1, L * G, N).double().contiguous()
+        row["policy"] = "random_2048"
+    max_n = max(int(n), int(pos.max().item()) + 1 if N else 1)
+    kept, status, pcount = kernels.choose(pos32, sc, kernels.row_params([row], dev), L, G, max_n)
+    st, count = int(status[0]), int(pcount[0])
+    if st == 3:
+        raise RuntimeError("protected positions differ between heads")
+    if st == 2:
+        return None, count
+    k = count if name == "prefix_sliding_2048" else min(int(budget), N)
+    return kept[0, :, :k].reshape(L, G, k).long(), count
+
+
+def _scores(st, entry, name, pos, slots, n):
+    """Per-column keys of a boundary, as the reference builds them (runtime:400-412)."""
+    device = pos.device
+    seed = int(entry["cfg"].get("seed", 0))
+    name = canonical(name)
+    if name == "random_2048":
+        generator = torch.Generator(device=device).manual_seed((seed * 1000003 + n) & 0x7FFFFFFF)
+        return torch.rand(pos.shape, generator=generator, device=device, dtype=torch.float64)
+    if name == "random_reservoir_2048":
+        return reservoir_scores(seed, pos, torch.arange(pos.shape[0], device=device),
+                                torch.arange(pos.shape[1], device=device))
+    if name in ("head_sum_2048", "head_max_sum_2048"):
+        return st.scores[:, :, slots].double()
+    if name == "h2o_global_2048":
+        s = st.scores[:, :, slots]
+        acc = torch.zeros((s.shape[0], s.shape[2]), dtype=torch.float32, device=device)
+        for g in range(s.shape[1]):
+            acc = acc + s[:, g]
+        return acc[:, None, :].expand(-1, s.shape[1], -1).double()
+    return torch.zeros(pos.shape, device=device, dtype=torch.float64)
+
+
+def _units(st, tokens, what):
+    if tokens % st.page_size:
+        raise ValueError(f"{what}={tokens} is not a multiple of the page size {st.page_size}")
+    return tokens // st.page_size
+
+
+def _boundary(st, row, entry, n, cursor=None, allocator=None):
+    """Evict at logical length n: choose per head, relocate survivors, free the rest.
+
+    With allocator=None (static replay) survivors are relocated but nothing is
+    freed and req_to_token is untouched (runtime:415-421).
+    """
+    cfg = entry["cfg"]
+    name = canonical(cfg["name"])
+    page = st.page_size
+    budget, prefix, recent = (_units(st, int(cfg[k]), k) for k in ("budget", "prefix", "recent"))
+    n_u = _units(st, int(n), "n")
+    cur_u = None if cursor is None else int(cursor) // page
+    frontier, count = entry["frontier"], entry["count"]
+    started = time.perf_counter()
+    N = count + n_u - frontier
+    entry["last_boundary"] = n
+    if N <= budget:
+        entry["events"].append({"boundary": n, "before": int(N), "after": int(N)})
+        return
+    L, G = len(st.full_layers), st.kv_heads
+    uniforms = None
+    if name == "random_2048":
+        generator = torch.Generator(device=st.device).manual_seed(
+            (int(cfg.get("seed", 0)) * 1000003 + n) & 0x7FFFFFFF)
+        draw = torch.rand((L, G, N), generator=generator, device=st.device, dtype=torch.float64)
+        uniforms = draw.reshape(1, L, G, N)
+    st.epoch += 1
+    kptr, vptr = st.layer_pointers()
+    live = allocator is not None
+    swa = getattr(allocator, "full_to_swa_index_mapping", None) if live else None
+    rows = torch.tensor([row], dtype=torch.int32, device=st.device)
+    params = kernels.row_params([dict(n=n_u, budget=budget, prefix=prefix, recent=recent,
+                                      cursor=cur_u, policy=name, seed=int(cfg.get("seed", 0)))],
+                                st.device)
+    result, leftover = kernels.boundary(
+        st.table, st.req_to_token, st.frontier, st.count, st.pos, st.scores, kptr, vptr, G, page,
+        rows, params, N, n_u + 1, live, marks=st.marks, epoch=st.epoch, swa=swa,
+        uniforms=uniforms, head_offset=st.head_offset, err=st.err)
+    res = result[0].tolist()  # synchronises, as the reference does (runtime:474, 492)
+    finished = time.perf_counter()
+    status, before, after, nfreed = res
+    if status == 2:
+        entry["events"].append({"boundary": n, "deferred": True, "protected": after})
+        return
+    if status == 3:
+        raise RuntimeError("protected positions differ between heads")
+    if status == 6:
+        raise RuntimeError(f"boundary sizes exceed the state capacity (pos_cap {st.pos_cap})")
+    entry["pos"] = st.pos[row, :, :, :after].long()
+    entry.update(frontier=n_u, count=after)
+    if status == 5:
+        raise RuntimeError("gstar_evict would free a slot that still holds a sliding-window entry")
+    if live:
+        allocator.free_full(leftover[0, :nfreed].long())
+        entry["freed"] = entry.get("freed", 0) + nfreed
+    if status == 4:
+        raise RuntimeError("packed ownership overlaps the sliding-window region")
+    elapsed = 1000 * (finished - started)
+    entry["events"].append({"boundary": n, "before": before, "after": after, "freed": nfreed,
+                            "swa_cursor": cursor, "ranking_ms": elapsed, "compaction_ms": 0.0})
+
+
+# ------------------------------------------------------------ scheduler hooks
+def _identity(req):
+    session = getattr(req, "session", None)
+    if session is not None and getattr(session, "streaming", False):
+        return f"session-{session.session_id}"
+    return req.rid
+
+
+def _live_entry(req, cfg, kind):
+    entry = {"kind": kind, "key": _identity(req), "cfg": dict(cfg),
+             "mode": POLICIES.get(canonical(str(cfg.get("name"))), 0), "events": [], "error": None,
+             "frontier": 0, "count": 0, "last_boundary": 0, "peak_full_entries": 0,
+             "layer_error": []}
+    try:
+        validate(cfg, getattr(STATE, "page_size", 1) if STATE is not None else 1)
+    except ValueError as error:
+        entry["error"], entry["mode"] = str(error), 0
+    return entry
+
+
+def on_extend(batch):
+    """Create entries from custom_params and run boundaries at chunk starts (runtime:640-689)."""
+    st = STATE
+    if st is None:
+        return
+    for req in batch.reqs:
+        row = req.kv.req_pool_idx
+        params = getattr(req.sampling_params, "custom_params", None) or {}
+        entry = st.entries.get(row)
+        if entry is not None and entry["key"] != _identity(req):
+            _reset(st, row)  # the row now belongs to another request or session
+            entry = None
+        if entry is None:
+            if "gstar_replay" in params:
+                entry = _live_entry(req, params["gstar_replay"], "replay")
+            elif "gstar_eviction" in params:
+                entry = _live_entry(req, params["gstar_eviction"], "live")
+            else:
+                continue
+            st.entries[row] = entry
+            st.mode[row] = SCORE_MODE.get(canonical(str(entry["cfg"].get("name"))), 0) \
+                if not entry["error"] else 0
+            st.frontier[row], st.count[row] = 0, 0
+        if entry["error"]:
+            continue
+        if getattr(req, "retraction_count", 0) or entry["key"] in RETRACTED:
+            # a retracted request recomputes its KV from scratch, which evicted state cannot survive
+            RETRACTED.add(entry["key"])
+            entry["error"] = "retracted"
+            st.mode[row] = 0
+            continue
+        start, length = req.extend_range.start, req.extend_range.length
+        if start < entry["frontier"] * st.page_size:
+            entry["error"] = "the session rewound below the eviction frontier"
+        elif length and start // INTERVAL != (start + length - 1) // INTERVAL:
+            entry["error"] = "prefill chunk crosses a boundary; use --chunked-prefill-size 2048"
+        if entry["error"]:
+            st.mode[row] = 0
+            continue
+        if start and start % INTERVAL == 0 and start > entry["last_boundary"]:
+            torch.cuda.synchronize()  # the previous chunk's keys and scores are complete
+            if entry["kind"] == "replay":
+                _boundary(st, row, entry, start)
+            else:
+                _boundary(st, row, entry, start, _swa_cursor(req),
+                          batch.tree_cache.token_to_kv_pool_allocator)
+
+
+def _swa_cursor(req):
+    getter = getattr(req.kv, "get_evicted_seqlen", None)
+    if getter is None:
+        return None
+    try:
+        from sglang.srt.mem_cache.unified_cache.component_type import ComponentType
+        return getter(ComponentType.SWA)
+    except ImportError:
+        return getter("swa")
+
+
+def on_decode(batch):
+    """Run due boundaries before the decode step (runtime:692-710)."""
+    st = STATE
+    if st is None or not st.entries:
+        return
+    lengths = batch.seq_lens_cpu.tolist()
+    for i, req in enumerate(batch.reqs):
+        row = req.kv.req_pool_idx
+        entry = st.entries.get(row)
+        if entry is None or entry["kind"] != "live" or entry["error"] or entry["key"] != _identity(req):
+            continue
+        n = lengths[i]
+        entry["peak_full_entries"] = max(entry["peak_full_entries"],
+                                         entry["count"] * st.page_size + n - entry["frontier"] * st.page_size)
+        if n % INTERVAL or n <= entry["last_boundary"]:
+            continue
+        torch.cuda.synchronize()  # the previous decode step wrote query n-1's key and scores
+        _boundary(st, row, entry, n, _swa_cursor(req), batch.tree_cache.token_to_kv_pool_allocator)
+
+
+def release(req):
+    """At a request's KV release drop its state unless its session keeps the row (runtime:719-742)."""
+    st = STATE
+    if st is None or not req.kv.holds_kv:
+        return
+    row = req.kv.req_pool_idx
+    entry = st.entries.get(row)
+    if entry is None or entry["key"] != _identity(req):
+        return
+    if entry["kind"] == "live" and entry["key"] != req.rid:
+        return  # the session keeps its row and eviction state for the next call
+    _reset(st, row)
+
+
+def filter_holes(segments):
+    """Holes are zero and below the sliding-window cursor, so only full-side frees see them."""
+    return [(kv[kv != 0], start) for kv, start in segments]

@@ -204,8 +204,9 @@ int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols,
  *   max_cols >= count[row] + n - frontier[row] for every row
  *   max_n    >= every row's n (positions are ranked in a max_n-bit bitmap)
  *   result  [num_rows, 4]: status (0 evicted, 1 nothing to do, 2 deferred,
- *           3 protected mismatch, 4 packing error, 5 sliding-window error),
- *           columns before, residents after, units freed
+ *           3 protected mismatch, 4 packing error, 5 sliding-window error,
+ *           6 row sizes outside max_cols/max_n/pos_cap), columns before,
+ *           residents after (the protected count when deferred), units freed
  *   freed_units [num_rows, freed_stride] leftover units (live only)
  * hazard_bytes bounds the relocation scratch; layers are processed in groups
  * that fit it (at least one layer; query the minimum with layers = 1). */

@@ -338,6 +338,7 @@ void or_boundary(int32_t* table, int64_t ts, int32_t* r2u, int64_t rs, int32_t* 
       if (np[lg] != np[0]) mismatch = 1;
     if (mismatch || np[0] > q->budget) {
       res[0] = mismatch ? 3 : 2; /* runtime:388-391 */
+      if (!mismatch) res[2] = np[0];
       free(units); free(ps); free(key); free(kept); free(nk); free(np);
       continue;
     }

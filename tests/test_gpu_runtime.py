@@ -1,0 +1,291 @@
+"""The gstar_evict mirror driven like the reference's own tests
+(code/tests/test_sglang_evict.py), on the sm_100a kernels.
+
+Where the reference test compares against core.Policy (which needs the
+reference source), these compare against the CPU oracle, which
+tests/test_oracle_golden.py pins to the reference's outputs.
+"""
+import random
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+FULL = (1, 3)
+
+
+@pytest.fixture(autouse=True)
+def _setup():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from cache_eviction_b200 import runtime as ge
+    ge.STATE = None
+    torch.manual_seed(0)
+    yield ge
+    ge.STATE = None
+
+
+def backend(rows=4, width=8192, slots=20000, kv_heads=8, dim=64, page=1):
+    """Two full layers (1, 3) and two sliding-window layers (test_sglang_evict.py:19-28)."""
+    keys = {l: torch.randn((slots, kv_heads, dim), device="cuda").to(torch.bfloat16) for l in range(4)}
+    values = {l: torch.randn((slots, kv_heads, dim), device="cuda").to(torch.bfloat16) for l in range(4)}
+    pool = SimpleNamespace(layers_mapping={l: (l, l not in FULL) for l in range(4)},
+                           get_key_buffer=keys.__getitem__, get_value_buffer=values.__getitem__)
+    return SimpleNamespace(token_to_kv_pool=pool, max_kv_splits=8, page_size=page,
+                           req_to_token_pool=SimpleNamespace(req_to_token=torch.zeros(
+                               (rows, width), dtype=torch.int32, device="cuda")),
+                           kv_indptr=torch.zeros(rows + 1, dtype=torch.int32, device="cuda"))
+
+
+def allocator(slots=20000):
+    freed = []
+    return freed, SimpleNamespace(free_full=lambda s: freed.append(s.clone()),
+                                  full_to_swa_index_mapping=torch.zeros(slots, dtype=torch.int64, device="cuda"))
+
+
+def entry(ge, name, budget, prefix, recent, seed, kind="live"):
+    cfg = {"name": name, "budget": budget, "prefix": prefix, "recent": recent, "seed": seed}
+    return ge._live_entry(SimpleNamespace(rid="r", session=None), cfg, kind)
+
+
+def test_decode_scores_are_per_kv_head(_setup):
+    """test_sglang_evict.py:48-78, with the fused kernel in place of SGLang's decode."""
+    ge = _setup
+    b = backend()
+    st = ge.state(b)
+    heads, kv_heads, dim, lengths = 64, 8, 64, [37, 1500, 3001]
+    keys, values = b.token_to_kv_pool.get_key_buffer(1), b.token_to_kv_pool.get_value_buffer(1)
+    q = torch.randn((3, heads, dim), device="cuda").to(torch.bfloat16)
+    sinks = torch.randn(heads, device="cuda").to(torch.bfloat16)
+    perm = (torch.randperm(19999, device="cuda")[:sum(lengths)] + 1).int()
+    indptr = torch.tensor([0, 37, 1537, 4538], dtype=torch.int32, device="cuda")
+    rows = torch.tensor([1, 2, 3], device="cuda")
+    b.forward_metadata = SimpleNamespace(kv_indptr=indptr, kv_indices=perm)
+    layer = SimpleNamespace(sliding_window_size=-1, tp_q_head_num=heads, tp_k_head_num=kv_heads,
+                            qk_head_dim=dim, layer_id=1, scaling=0.125)
+    for mode in (1, 2):
+        st.mode[:] = mode
+        st.scores.zero_()
+        out = torch.empty((3, heads, dim), dtype=torch.bfloat16, device="cuda")
+        ge.decode(b, q.reshape(3, -1), layer, SimpleNamespace(
+            out_cache_loc=torch.zeros(3, dtype=torch.int64, device="cuda"), req_pool_indices=rows),
+            sinks, out)
+        expected = torch.zeros_like(st.scores)
+        expected_out = torch.zeros((3, heads, dim), device="cuda")
+        for i in range(3):
+            slots = perm[indptr[i]:indptr[i + 1]].long()
+            k = keys[slots].float().repeat_interleave(heads // kv_heads, 1)
+            v = values[slots].float().repeat_interleave(heads // kv_heads, 1)
+            logits = torch.einsum("hd,khd->hk", q[i].float(), k) * 0.125
+            p = torch.softmax(torch.cat((logits, sinks.float()[:, None]), -1), -1)[:, :-1]
+            expected_out[i] = torch.einsum("hk,khd->hd", p, v)
+            p = p.view(kv_heads, 8, -1)
+            expected[0][:, slots] += p.sum(1) if mode == 1 else p.amax(1)
+        # the new slots (out_cache_loc = 0) were zeroed first, as in the reference
+        torch.testing.assert_close(st.scores, expected, rtol=2e-3, atol=1e-6)
+        rel = (out.float() - expected_out).norm() / expected_out.norm()
+        assert float(rel) < 5e-3
+
+
+def test_after_decode_matches_reference_hook_semantics(_setup):
+    ge = _setup
+    b = backend()
+    st = ge.state(b)
+    lengths = [100, 257]
+    perm = (torch.randperm(19999, device="cuda")[:sum(lengths)] + 1).int()
+    b.forward_metadata = SimpleNamespace(kv_indptr=torch.tensor([0, 100, 357], dtype=torch.int32, device="cuda"),
+                                         kv_indices=perm)
+    q = torch.randn((2, 64, 64), device="cuda").to(torch.bfloat16)
+    sinks = torch.randn(64, device="cuda")
+    layer = SimpleNamespace(sliding_window_size=-1, tp_q_head_num=64, tp_k_head_num=8, qk_head_dim=64,
+                            layer_id=1, scaling=0.125)
+    st.mode[:] = 1
+    st.scores.fill_(5.0)
+    loc = perm[[99, 356]].long()
+    ge.after_decode(b, q.reshape(2, -1), layer, SimpleNamespace(out_cache_loc=loc,
+                                                                req_pool_indices=torch.tensor([0, 1], device="cuda")), sinks)
+    s = st.scores.cpu()
+    # new slots zeroed on every full layer, then this layer's mass added
+    assert float(s[1, :, loc.cpu()].abs().max()) == 0.0
+    assert float(s[0, :, loc.cpu()].max()) < 1.0
+    sliding = SimpleNamespace(sliding_window_size=128)
+    ge.after_decode(b, q.reshape(2, -1), sliding, None, sinks)  # sliding layers are ignored
+
+
+def test_fill_reads_compact_residents_then_tail(_setup):
+    """test_sglang_evict.py:80-90 (golden vectors)."""
+    ge = _setup
+    b = backend()
+    st = ge.state(b)
+    st.req_to_token[1, :10] = torch.arange(101, 111, dtype=torch.int32)
+    st.req_to_token[2, :6] = torch.arange(201, 207, dtype=torch.int32)
+    st.table[1, :4] = torch.tensor([101, 102, 106, 107], dtype=torch.int32)
+    st.count[1], st.frontier[1] = 4, 7
+    out = torch.full((32,), -1, dtype=torch.int64, device="cuda")
+    indptr = ge.fill(b, 2, torch.tensor([10, 6], device="cuda"), torch.tensor([1, 2], device="cuda"), out)
+    assert indptr.tolist() == [0, 7, 13]
+    assert out[:13].tolist() == [101, 102, 106, 107, 108, 109, 110, 201, 202, 203, 204, 205, 206]
+
+
+def _oracle_state(st, b):
+    state = {"table": st.table.cpu().numpy(), "r2u": st.req_to_token.cpu().numpy(),
+             "frontier": st.frontier.cpu().numpy(), "count": st.count.cpu().numpy(),
+             "pos": st.pos.cpu().numpy(), "scores": st.scores.cpu().numpy()}
+    kl = [b.token_to_kv_pool.get_key_buffer(l).view(torch.int16).cpu().numpy().reshape(-1, 8, 1, 64) for l in FULL]
+    vl = [b.token_to_kv_pool.get_value_buffer(l).view(torch.int16).cpu().numpy().reshape(-1, 8, 1, 64) for l in FULL]
+    return state, [k.view(np.uint16) for k in kl], [v.view(np.uint16) for v in vl]
+
+
+def check_boundaries(ge, name, kind):
+    """test_sglang_evict.py:92-148: two boundaries with relocation, ownership and
+    freeing checks; kept sets against the oracle run on the same state."""
+    b = backend()
+    st = ge.state(b)
+    n, budget = 4096 + 300, 1024
+    prefix = budget // 4
+    recent = budget - prefix if name == "prefix_sliding_2048" else budget // 4
+    slot_of = torch.randperm(19000, device="cuda")[:n] + 1
+    st.req_to_token[1, :n] = slot_of.int()
+    original = {l: b.token_to_kv_pool.get_key_buffer(l)[slot_of].clone() for l in FULL}
+    original_v = {l: b.token_to_kv_pool.get_value_buffer(l)[slot_of].clone() for l in FULL}
+    score = torch.rand((2, 8, n), device="cuda")
+    st.scores[:, :, slot_of] = score
+    e = entry(ge, name, budget, prefix, recent, seed=4, kind=kind)
+    freed, alloc = allocator()
+    ostate, okl, ovl = _oracle_state(st, b)
+    for boundary in (2048, 4096):
+        cursor = boundary - 200
+        N = int(ostate["count"][1]) + boundary - int(ostate["frontier"][1])
+        uni = None
+        if name == "random_2048":
+            g = torch.Generator(device="cuda").manual_seed((4 * 1000003 + boundary) & 0x7FFFFFFF)
+            uni = torch.rand((2, 8, N), generator=g, device="cuda", dtype=torch.float64).cpu().numpy()[None]
+        row = dict(n=boundary, budget=budget, prefix=prefix, recent=recent,
+                   cursor=None if kind == "replay" else cursor, policy=name, seed=4)
+        oracle.boundary(ostate, okl, ovl, [1], oracle.row_params([row]), N, live=kind == "live",
+                        uniforms=uni)
+        if kind == "replay":
+            ge._boundary(st, 1, e, boundary)
+        else:
+            ge._boundary(st, 1, e, boundary, cursor, alloc)
+        table = st.table[1, :e["count"]].long()
+        assert e["count"] == (budget if name != "prefix_sliding_2048" else prefix + recent)
+        np.testing.assert_array_equal(st.table.cpu().numpy(), ostate["table"])
+        np.testing.assert_array_equal(st.pos.cpu().numpy(), ostate["pos"])
+        for index, layer in enumerate(FULL):
+            keys = b.token_to_kv_pool.get_key_buffer(layer)
+            values = b.token_to_kv_pool.get_value_buffer(layer)
+            for g in range(8):
+                held = e["pos"][index, g]
+                assert held.numel() == e["count"]
+                # relocated keys, values and scores belong to the positions the head claims
+                assert torch.equal(keys[table, g], original[layer][held, g])
+                assert torch.equal(values[table, g], original_v[layer][held, g])
+                torch.testing.assert_close(st.scores[index, g, table], score[index, g, held])
+        assert int(st.frontier[1]) == boundary
+    if kind == "replay":
+        assert torch.equal(st.req_to_token[1, :n], slot_of.int())
+        assert freed == []
+        return
+    row = st.req_to_token[1, :n].long()
+    owned = row[row != 0]
+    true = min(4096 - recent, 4096 - 200)
+    assert torch.equal(row[true:], slot_of[true:])
+    assert owned.numel() == torch.unique(owned).numel()
+    assert set(owned.tolist()) == set(st.table[1, :e["count"]].tolist()) | set(slot_of[4096:].tolist())
+    released = torch.cat(freed).tolist()
+    assert len(released) == len(set(released))
+    assert set(released) | set(owned.tolist()) == set(slot_of.tolist())
+    assert e["freed"] == len(released)
+    np.testing.assert_array_equal(st.req_to_token.cpu().numpy(), ostate["r2u"])
+
+
+@pytest.mark.parametrize("name", ["head_sum_2048", "random_reservoir_2048", "prefix_sliding_2048",
+                                  "random_2048", "h2o_global_2048"])
+def test_live_boundaries_relocate_and_free(_setup, name):
+    check_boundaries(_setup, name, "live")
+
+
+@pytest.mark.parametrize("name", ["head_max_sum_2048", "random_reservoir_2048"])
+def test_replay_boundaries_relocate_without_freeing(_setup, name):
+    check_boundaries(_setup, name, "replay")
+
+
+def test_random_redraws_but_reservoir_is_fixed(_setup):
+    """test_sglang_evict.py:160-169."""
+    ge = _setup
+    pos = torch.arange(1000, device="cuda").expand(2, 8, -1)
+    layers, heads = torch.arange(2, device="cuda"), torch.arange(8, device="cuda")
+    fixed = ge.reservoir_scores(7, pos, layers, heads)
+    assert float(fixed[1, 5, 321]) == oracle.reservoir53(7, 1, 5, 321) / float(1 << 53)
+    assert float((fixed[0, 0] - fixed[1, 3]).abs().mean()) > 0.2
+    st = SimpleNamespace(scores=None)
+    a = ge._scores(st, {"cfg": {"seed": 7}}, "random_2048", pos, None, 2048)
+    c = ge._scores(st, {"cfg": {"seed": 7}}, "random_2048", pos, None, 4096)
+    assert float((a - c).abs().mean()) > 0.2
+
+
+def test_reservoir_survival_does_not_decay_with_age(_setup):
+    """test_sglang_evict.py:171-189, through the selection kernel."""
+    ge = _setup
+    budget, total = 2048, 2048 * 16
+    layers, heads = torch.arange(1, device="cuda"), torch.arange(1, device="cuda")
+    fractions = {}
+    for name in ("random_reservoir_2048", "random_2048"):
+        resident = torch.arange(0, device="cuda", dtype=torch.long).view(1, 1, 0)
+        for n in range(2048, total + 1, 2048):
+            pos = torch.cat((resident, torch.arange(n - 2048, n, device="cuda").view(1, 1, -1)), -1)
+            if name == "random_2048":
+                g = torch.Generator(device="cuda").manual_seed(n)
+                score = torch.rand(pos.shape, generator=g, device="cuda", dtype=torch.float64)
+            else:
+                score = ge.reservoir_scores(3, pos, layers, heads)
+            keep, _ = ge.choose(name, pos, n, budget, 0, 0, score)
+            resident = torch.gather(pos, -1, keep)
+        fractions[name] = float((resident < total // 2).float().mean())
+    assert abs(fractions["random_reservoir_2048"] - 0.5) < 0.05
+    assert fractions["random_2048"] < 0.1
+
+
+def test_choose_deferred_and_mismatch(_setup):
+    ge = _setup
+    pos = torch.arange(600, device="cuda").expand(2, 8, -1).contiguous()
+    score = torch.rand((2, 8, 600), device="cuda", dtype=torch.float64)
+    keep, count = ge.choose("head_sum_2048", pos, 600, 100, 64, 64, score)
+    assert keep is None and count == 128
+    bad = pos.clone()
+    bad[1, 3, 599] = 650  # at n = 700 only this head holds a recent-window position
+    with pytest.raises(RuntimeError, match="protected positions differ"):
+        ge.choose("head_sum_2048", bad, 700, 256, 64, 64, score)
+
+
+def test_on_decode_runs_due_boundary_and_frees(_setup):
+    """The scheduler hook path: create the entry at extend, boundary at decode."""
+    ge = _setup
+    b = backend(rows=2, slots=6000)
+    st = ge.state(b)
+    n = 2048
+    slot_of = torch.randperm(5990, device="cuda")[:n] + 1
+    st.req_to_token[0, :n] = slot_of.int()
+    freed, alloc = allocator(6000)
+    req = SimpleNamespace(rid="a", session=None, kv=SimpleNamespace(req_pool_idx=0, holds_kv=True),
+                          sampling_params=SimpleNamespace(custom_params={"gstar_eviction": {
+                              "name": "random_reservoir_2048", "budget": 512, "prefix": 128,
+                              "recent": 128, "seed": 1}}),
+                          extend_range=SimpleNamespace(start=0, length=2048))
+    batch = SimpleNamespace(reqs=[req], tree_cache=SimpleNamespace(token_to_kv_pool_allocator=alloc),
+                            seq_lens_cpu=torch.tensor([n]))
+    ge.on_extend(batch)
+    e = st.entries[0]
+    assert e["error"] is None and int(st.mode[0]) == 0
+    ge.on_decode(batch)
+    assert e["count"] == 512 and e["last_boundary"] == n
+    assert sum(x.numel() for x in freed) == n - 512 == e["freed"]
+    ge.on_decode(batch)  # same length again: no second boundary
+    assert len(e["events"]) == 1
+    ge.release(req)
+    assert 0 not in st.entries
