@@ -252,6 +252,39 @@ def build_engine(specs, steps_total, world, rank, group, device):
     return eng
 
 
+def run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks, scale,
+            after_layer, barrier, max_over_ranks, e2e_steps):
+    """End-to-end pass through the public engine API from a fresh state: every
+    step copies all layers' queries from pinned host memory and reads all
+    attention outputs back into pinned host memory."""
+    import torch
+    B = len(specs)
+    eng = build_engine(specs, steps_total, world, rank, group, device)
+    q_host = torch.empty(tuple(q.shape), dtype=torch.bfloat16).pin_memory()
+    q_host.copy_(q.cpu())
+    out_host = torch.empty(tuple(out.shape), dtype=torch.bfloat16).pin_memory()
+    q_dev = torch.empty_like(q)
+    for _ in range(args.warmup):
+        q_dev.copy_(q_host, non_blocking=True)
+        eng.step(q_dev, out, sinks, scale, after_layer)
+        out_host.copy_(out, non_blocking=True)
+    barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(e2e_steps):
+        q_dev.copy_(q_host, non_blocking=True)
+        eng.step(q_dev, out, sinks, scale, after_layer)
+        out_host.copy_(out, non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2))
+    del eng
+    torch.cuda.empty_cache()
+    return B * e2e_steps / (e2e_ms * 1e-3)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -260,7 +293,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--no-oproj", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="CPU-baseline sample length (0 skips it)")
+    ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
+                    help="sequences per GPU (small cases for profiling)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -278,7 +314,7 @@ def main():
     device = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(device)
     capi.load()
-    specs = workload(SEQS_PER_GPU * world)
+    specs = workload(args.seqs * world)
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else args.steps
     steps_total = args.warmup + max(args.steps, e2e_steps)
     G, H, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
@@ -357,32 +393,10 @@ def main():
     torch.cuda.empty_cache()
 
     # --------------------------------------------------------- e2e pass
-    eng = build_engine(specs, steps_total, world, rank, group, device)
-    q_host = q[0].cpu().pin_memory()
-    q_host_all = torch.empty((LAYERS, B, H, D), dtype=torch.bfloat16).pin_memory()
-    q_host_all.copy_(q.cpu())
-    out_host = torch.empty((LAYERS, B, H, D), dtype=torch.bfloat16).pin_memory()
-    q_dev = torch.empty_like(q)
-    for _ in range(args.warmup):
-        q_dev.copy_(q_host_all, non_blocking=True)
-        eng.step(q_dev, out, sinks, scale, after_layer)
-        out_host.copy_(out, non_blocking=True)
-    barrier()
-    torch.cuda.synchronize()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(e2e_steps):
-        q_dev.copy_(q_host_all, non_blocking=True)
-        eng.step(q_dev, out, sinks, scale, after_layer)
-        out_host.copy_(out, non_blocking=True)
-    e2.record()
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2))
-    e2e_value = B * e2e_steps / (e2e_ms * 1e-3)
-    step_bytes = LAYERS * B * H * D * 2
-    del eng, q_host
-    torch.cuda.empty_cache()
+    e2e_value, step_bytes = None, LAYERS * B * H * D * 2
+    if e2e_steps > 0:
+        e2e_value = run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
+                            scale, after_layer, barrier, max_over_ranks, e2e_steps)
 
     peak, peak_kind = measured_peak_hbm()
     line = {
@@ -406,7 +420,7 @@ def main():
                   "boundary_rows": n_bound_rows},
         "resident_tokens_mean": statistics.mean(tokens_resident),
     }
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
         from oracle import oracle
         cores = os.cpu_count() or 1
         oracle.set_threads(cores)

@@ -1,0 +1,43 @@
+"""The C-ABI library loads without a GPU and exports every entry point that
+include/ce_api.h declares (no compute calls here)."""
+import ctypes as C
+import re
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_functions():
+    text = (ROOT / "include" / "ce_api.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b(ce_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    from cache_eviction_b200 import capi
+    lib = capi.load()
+    names = declared_functions()
+    assert len(names) >= 10
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) == set(capi.SIGNATURES), set(names) ^ set(capi.SIGNATURES)
+
+
+def test_version_and_status_strings_without_gpu():
+    from cache_eviction_b200 import capi
+    lib = capi.load()
+    assert b"sm_100a" in lib.ce_version()
+    assert lib.ce_status_string(capi.CE_ERR_WORKSPACE) == b"workspace too small"
+
+
+def test_workspace_queries_are_host_only():
+    from cache_eviction_b200 import capi
+    lib = capi.load()
+    assert lib.ce_choose_workspace_bytes(2, 16, 100) > 0
+    assert lib.ce_boundary_workspace_bytes(1, 2, 8, 64, 16, 100, 0, 0) > 0
+    assert lib.ce_boundary_workspace_bytes(1, 2, 8, 32, 16, 100, 0, 0) == -1  # head_dim 64 only
+
+
+def test_row_params_layout_matches_header():
+    from cache_eviction_b200 import capi, kernels
+    assert C.sizeof(capi.RowParams) == 32 and kernels.ROW_DTYPE.itemsize == 32
