@@ -39,6 +39,9 @@ CE_POLICY_H2O_GLOBAL = 5
 CE_MODE_NONE, CE_MODE_SUM, CE_MODE_MAX = 0, 1, 2
 CE_DTYPE_NONE, CE_DTYPE_F32, CE_DTYPE_F64, CE_DTYPE_BF16 = 0, 1, 2, 3
 
+# size of the static scratch behind ce_decode_attn_score_static
+CE_DECODE_STATIC_SCRATCH_BYTES = 32 << 20
+
 
 class RowParams(C.Structure):
     """ce_row_params: one boundary's sizes in units (32 bytes)."""
@@ -64,6 +67,9 @@ SIGNATURES = {
     "ce_decode_attn_score": (C.c_int, [P, I64, I64, P, P, I64, P, P, P, I64, P, P, P, F32, I32,
                                        I32, I32, I32, I32, P, I64, I32, P, I32, I64, I64, P,
                                        I32, P, I64, P, P]),
+    "ce_decode_attn_score_static": (C.c_int, [P, I64, I64, P, P, I64, P, P, P, I64, P, P, P, F32,
+                                              I32, I32, I32, I32, I32, P, I64, I32, P, I32, I64,
+                                              I64, P, I32, P, P]),
     "ce_choose_workspace_bytes": (I64, [I32, I32, I32]),
     "ce_choose": (C.c_int, [P, P, I32, P, I32, P, I32, I32, I32, I32, I32, P, I32, P, P, P,
                             I64, P, P]),

@@ -1,0 +1,83 @@
+// ce_decode_attn_score_static: the fused decode attention + H2O score for
+// callers that cannot allocate device memory.
+//
+// Some callers cannot call cudaMalloc (or any allocating routine) at the point
+// where they run a decode step: a serving process that hands all of HBM to its
+// KV-cache pool at start-up and has nothing left to carve a workspace from, a
+// plugin whose host forbids device allocations after initialisation so that
+// memory use stays fixed, or code that runs inside a CUDA graph capture in
+// global mode, where allocation calls are rejected.  ce_decode_attn_score
+// still needs such a caller to pass a workspace; this entry point does not.
+//
+// Its scratch is the file-scope array below, CE_DECODE_STATIC_SCRATCH_BYTES
+// long.  Every GPU that loads libce_b200.so holds one copy of it until the
+// process exits.  The entry point checks that the call fits the array, finds
+// the array's device address and hands it to ce_decode_attn_score as the
+// workspace; nothing else changes.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/ce_api.h"
+#include "ce_host.h"
+
+namespace {
+
+// The scratch itself.  In host code this name is only a stand-in for the
+// device array (its address is not a device address); the real address comes
+// from cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char g_decode_scratch[CE_DECODE_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+void* g_scratch_ptr[kMaxDevices] = {nullptr};
+std::mutex g_scratch_mu;
+
+// Device address of this device's copy of the scratch, looked up on the
+// first call made with that device current.
+int scratch_address(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return ce::host::fail(CE_ERR_CUDA, "ce_decode_attn_score_static: no current device");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+    if (e != cudaSuccess || !ptr)
+      return ce::host::fail(CE_ERR_CUDA, "ce_decode_attn_score_static: cudaGetSymbolAddress failed");
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
+  return CE_OK;
+}
+
+}  // namespace
+
+extern "C" int ce_decode_attn_score_static(
+    const void* q, int64_t q_sb, int64_t q_sh, const void* k_pool, const void* v_pool,
+    int64_t pool_units, const int32_t* kv_indptr, const int32_t* kv_indices,
+    const int32_t* kv_tokens, int64_t kv_capacity, const float* sinks,
+    const int32_t* mode_of_row, const int64_t* rows, float sm_scale, int32_t bs,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+    float* scores, int64_t score_sg, int32_t zero_new, void* out, int32_t out_f32, int64_t o_sb,
+    int64_t o_sh, float* lse_out, int32_t score_flags, int32_t* err, void* stream) {
+  if (bs == 0) return CE_OK;
+  const int64_t need = ce_decode_workspace_bytes(bs, kv_capacity, num_q_heads, num_kv_heads,
+                                                 page_size, score_flags);
+  if (need < 0) return ce::host::fail(CE_ERR_ARG, "ce_decode_attn_score_static: bad sizes");
+  if (need > static_cast<int64_t>(CE_DECODE_STATIC_SCRATCH_BYTES))
+    return ce::host::fail(CE_ERR_WORKSPACE,
+                          "ce_decode_attn_score_static: this batch needs more scratch than the "
+                          "static maximum (CE_DECODE_STATIC_SCRATCH_BYTES); use "
+                          "ce_decode_attn_score with a caller workspace");
+  void* scratch = nullptr;
+  const int st = scratch_address(&scratch);
+  if (st != CE_OK) return st;
+  // Nothing in the scratch has to start at zero: every byte the kernels read
+  // is written earlier in the same call, so the previous call's contents are
+  // harmless.
+  return ce_decode_attn_score(q, q_sb, q_sh, k_pool, v_pool, pool_units, kv_indptr, kv_indices,
+                              kv_tokens, kv_capacity, sinks, mode_of_row, rows, sm_scale, bs,
+                              num_q_heads, num_kv_heads, head_dim, page_size, scores, score_sg,
+                              zero_new, out, out_f32, o_sb, o_sh, lse_out, score_flags, scratch,
+                              static_cast<int64_t>(CE_DECODE_STATIC_SCRATCH_BYTES), err, stream);
+}

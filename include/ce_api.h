@@ -158,6 +158,35 @@ int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh,
                          void* workspace, int64_t workspace_bytes,
                          int32_t* err, void* stream);
 
+/* ---- K1 without a caller workspace ------------------------------------------
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory when they decode (an engine that gave all HBM to its KV pool, a host
+ * that forbids allocations after start-up, a global-mode graph capture):
+ * identical to ce_decode_attn_score except that its scratch is a static
+ * device array of CE_DECODE_STATIC_SCRATCH_BYTES inside the library, held by
+ * every GPU that loads the library until the process exits.
+ *   - A call whose ce_decode_workspace_bytes() exceeds that maximum returns
+ *     CE_ERR_WORKSPACE and launches nothing.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Every call on a device shares the one array: calls that may overlap on
+ *     the GPU (different streams without ordering) race and must be
+ *     serialised by the caller.  No part of the array needs to start at zero.
+ * Allocates nothing (no cudaMalloc/cudaFree, no allocating library call). */
+#define CE_DECODE_STATIC_SCRATCH_BYTES (32u << 20)
+int ce_decode_attn_score_static(const void* q, int64_t q_sb, int64_t q_sh,
+                                const void* k_pool, const void* v_pool, int64_t pool_units,
+                                const int32_t* kv_indptr, const int32_t* kv_indices,
+                                const int32_t* kv_tokens, int64_t kv_capacity,
+                                const float* sinks,
+                                const int32_t* mode_of_row, const int64_t* rows,
+                                float sm_scale, int32_t bs, int32_t num_q_heads,
+                                int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                                float* scores, int64_t score_sg, int32_t zero_new,
+                                void* out, int32_t out_f32, int64_t o_sb, int64_t o_sh,
+                                float* lse_out, int32_t score_flags,
+                                int32_t* err, void* stream);
+
 /* ---- K2: ragged per-head selection ---------------------------------------
  * Replaces gstar_evict.choose + _scores + reservoir_scores (runtime:358-412)
  * for `problems` independent boundaries, each over `segs` = layers*heads
