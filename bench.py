@@ -404,7 +404,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": config_block(world),
-        "roofline": {"bound": "hbm", "kernel": "ce_decode_attn_score (attn_kernel + finalize_kernel)",
+        "roofline": {"bound": "hbm", "kernel": "ce_decode_attn_score (attn_kernel + combine_kernel)",
                      "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                      "frac": achieved_gbs / peak, "peak_kind": peak_kind,
                      "bytes_per_launch": avg_bytes, "launch_ms": avg_launch_ms,

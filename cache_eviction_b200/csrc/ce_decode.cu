@@ -6,30 +6,33 @@
 // (code/cache_eviction/sglang_evict_runtime.py:155-224).
 //
 // Work split (stream-K over tokens): the concatenation of all sequences'
-// 16-token-per-warp "stages" is cut into gridDim.x equal ranges, one per
+// 16-token-per-warp "stages" is cut into equal contiguous ranges, one per
 // persistent CTA.  A CTA walks its range sequence by sequence and leaves one
 // partial record (per-warp running max m, sum l and unnormalised O) for every
 // sequence it touched.  Record (b, cta) lives at index b + cta, which is unique
-// because both walks are monotone.
+// because both walks are monotone.  combine_kernel then merges each
+// sequence's records with the sink into the output and the log-sum-exp.
 //
 // Inside a CTA: warp 8 is the producer.  It issues one 2D bulk-tensor (TMA)
 // load per KV page for K and one for V (box = the page's G*P rows of 128 B,
 // 128-byte swizzle) into a ring of shared-memory stages guarded by mbarriers.
 // Warps 0..7 consume: warp w owns KV head g = w % G and 16 tokens of the
-// stage.  S = Q K^T and O += P V run on m16n8k16 bf16 tensor-core tiles with
-// the group's 8 query heads in rows 0..7; P enters the PV product as a bf16
-// hi/lo pair so the output keeps ~fp32 accuracy.
+// stage; they copy their K and V fragments to registers and release the stage
+// before doing any math.  S^T = K Q^T and O^T += V^T P^T run on m16n8k16 bf16
+// tensor-core tiles (tokens, then head dims, as the 16-row operand; the group's
+// 8 query heads as the 8 columns); P^T is formed in registers by movmatrix and
+// enters as a bf16 hi/lo pair so the output keeps ~fp32 accuracy.
 //
-// Scores need the final normaliser, which only exists after the split
-// combine.  For H2O rows the consumer therefore stores, per KV page and query
-// head, log2 of the page's probability mass relative to the running max
-// (CE_MODE_SUM), or every token's logit (CE_MODE_MAX, which needs a max over
-// heads per token).  The finalize kernel rebuilds each head's normaliser from
-// the records plus the sink -- the same normaliser as decode stage 2 and the
-// reference score kernel (runtime:179-188) -- combines O, and adds
+// Scores need the final normaliser.  For H2O rows the consumer stores, per KV
+// page and query head, log2 of the page's probability mass relative to the
+// running max (CE_MODE_SUM), or every token's logit (CE_MODE_MAX, which needs a
+// max over heads per token).  combine_kernel, after merging a sequence, adds
 //   SUM: sum_h 2^(page_lse - LSE_h)   MAX: sum_t max_h 2^(s_t,h - LSE_h)
 // into scores[g, unit] with a plain read-modify-write: a unit appears once in
-// a batch, as in the reference kernel (runtime:199-200).
+// a batch, as in the reference kernel (runtime:199-200).  LSE_h is the same
+// normaliser as decode stage 2 and the reference score kernel
+// (runtime:179-188): every key's logit plus the sink.
+#include <algorithm>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -78,6 +81,7 @@ struct Params {
   int64_t o_sb, o_sh;
   float* lse_out;
   int32_t* prefix;   // [bs + 1] stage prefix (written by CTA 0)
+  float* lse2;       // [bs, H] log2 normaliser per query head (for scores)
   float* rec;        // [(bs + grid), REC_FLOATS]
   float* ul;         // [kv_capacity, H] unit log-mass (log2 units) or null
   float* tl;         // [kv_capacity * P, H] token logits (page_size > 1, MAX rows) or null
@@ -132,6 +136,34 @@ __device__ int64_t block_excl_scan(int64_t v, int64_t* sh, int64_t& total) {
   return res;
 }
 
+__device__ __forceinline__ int cta_of_stage(int64_t x, int64_t S, int64_t grid) {
+  return static_cast<int>(((x + 1) * grid - 1) / S);
+}
+
+// When there are fewer stages than CTAs some partitions are empty and leave
+// no record; a sequence's record range [k0, k1] may straddle them.
+__device__ __forceinline__ bool cta_has_work(int64_t k, int64_t S, int64_t grid) {
+  return (k * S) / grid < ((k + 1) * S) / grid;
+}
+
+__device__ __forceinline__ void store_out(const Params& p, int b, int h, int d, float v) {
+  const int64_t off = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh + d;
+  if (p.out_f32)
+    reinterpret_cast<float*>(p.out)[off] = v;
+  else
+    reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v);
+}
+
+// A sequence with no tokens attends only to the sink: zero output.
+__device__ void empty_sequence(const Params& p, int b) {
+  for (int h = 0; h < p.H; ++h) {
+    for (int d = 0; d < D; ++d) store_out(p, b, h, d, 0.f);
+    const float s2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
+    p.lse2[static_cast<int64_t>(b) * p.H + h] = s2;
+    if (p.lse_out) p.lse_out[static_cast<int64_t>(b) * p.H + h] = s2 * LN2;
+  }
+}
+
 template <int P>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
@@ -175,7 +207,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     int64_t run = excl;
     for (int b = lo_b; b < hi_b; ++b) {
       p.prefix[b] = static_cast<int32_t>(run);
-      run += (seq_tokens(p, b, P) + ST - 1) / ST;
+      const int64_t n = (seq_tokens(p, b, P) + ST - 1) / ST;
+      run += n;
+      if (n == 0) empty_sequence(p, b);   // no CTA will touch it
     }
     if (tid == 0) p.prefix[bs] = static_cast<int32_t>(S);
   }
@@ -288,36 +322,61 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------- consumers -------------------------------
+    // Warp w owns KV head g = w % G and tokens [16*tb, 16*tb+16) of each stage.
+    // S^T = K Q^T: the 16 tokens are the MMA rows (no padding), the group's 8
+    // query heads the columns.  Thread (r = lane/4, t = lane%4) holds tokens r
+    // and r+8 for heads 2t and 2t+1, and keeps the running max/sum of those two
+    // heads.  O^T = V^T P^T: 4 tiles of 16 dims x 8 heads; P^T comes from the
+    // S^T fragments by an in-register 8x8 transpose (movmatrix).
     const int g = warp % G;
     const int tb = warp / G;
-    const int r = lane >> 2;   // query-head row within the group
+    const int r = lane >> 2;
     const int t = lane & 3;
-    const int head = g * GROUP + r;
-    float* rec_base = p.rec;
+    const int head = g * GROUP + r;     // head whose q row this lane loads
+    const int tau0 = tb * 16;
 
-    // Row (in a stage) of token tau for this warp's KV head.
     auto row_of = [&](int tau) -> int { return (tau / P) * UNIT_ROWS + g * P + (tau % P); };
 
-    uint32_t qa[4][2];
-    float o[8][4];
-    float m = -INFINITY, l = 0.f;
+    // Swizzled shared-memory offsets of this lane's ldmatrix rows: the same in
+    // every stage, so they are computed once.
+    uint32_t koff[4], voff[4];
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int krow = row_of(tau0 + (mi & 1) * 8 + rr);
+      const int vrow = row_of(tau0 + (mi >> 1) * 8 + rr);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        koff[c] = krow * ROW_BYTES + (((c * 2 + (mi >> 1)) ^ (krow & 7)) << 4);
+        voff[c] = HALF_STAGE + vrow * ROW_BYTES + (((c * 2 + (mi & 1)) ^ (vrow & 7)) << 4);
+      }
+    }
+    const uint32_t ring = smem_addr(smem);
+
+    uint32_t qb[4][2];                  // B operand (Q^T) per k-step
+    float o[4][4];                      // O^T accumulators
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
     int cur_b = -1, mode = CE_MODE_NONE;
 
-    auto epilogue = [&](int bb) {
-      float* rec = rec_base + static_cast<int64_t>(bb + blockIdx.x) * REC_FLOATS;
-      const int vrow = warp * 8 + r;
+    auto leave = [&](int bb) {
+      float* rec = p.rec + static_cast<int64_t>(bb + blockIdx.x) * REC_FLOATS;
+      const int v0 = warp * 8 + 2 * t;   // virtual rows of heads 2t, 2t+1
 #pragma unroll
-      for (int dt = 0; dt < 8; ++dt) {
-        float2 v = make_float2(o[dt][0], o[dt][1]);
-        *reinterpret_cast<float2*>(rec + vrow * D + dt * 8 + 2 * t) = v;
+      for (int mt = 0; mt < 4; ++mt) {
+        rec[v0 * D + mt * 16 + r] = o[mt][0];
+        rec[(v0 + 1) * D + mt * 16 + r] = o[mt][1];
+        rec[v0 * D + mt * 16 + r + 8] = o[mt][2];
+        rec[(v0 + 1) * D + mt * 16 + r + 8] = o[mt][3];
       }
-      if (t == 0) {
-        rec[REC_ROWS * D + vrow] = m;
-        rec[REC_ROWS * D + REC_ROWS + vrow] = l;
+      if (r == 0) {
+        rec[REC_ROWS * D + v0] = m[0];
+        rec[REC_ROWS * D + v0 + 1] = m[1];
+        rec[REC_ROWS * D + REC_ROWS + v0] = l[0];
+        rec[REC_ROWS * D + REC_ROWS + v0 + 1] = l[1];
       }
     };
 
-    int it = 0;
+    int s = 0;
+    uint32_t ph = 0;
     int b = b_start, base = base_start;
     int nst = 0, tok_b = 0;
     int64_t ip_b = 0;
@@ -328,25 +387,25 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
     if (b < bs) load_seq(b);
     bool aborted = false;
-    for (int64_t x = S_lo; x < S_hi; ++x, ++it) {
+    for (int64_t x = S_lo; x < S_hi; ++x) {
       while (x >= base + nst) {
         base += nst;
         ++b;
         load_seq(b);
       }
       if (b != cur_b) {
-        if (cur_b >= 0) epilogue(cur_b);
+        if (cur_b >= 0) leave(cur_b);
         cur_b = b;
         const __nv_bfloat16* qrow = p.q + static_cast<int64_t>(b) * p.q_sb + static_cast<int64_t>(head) * p.q_sh;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-          qa[ks][0] = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t);
-          qa[ks][1] = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t);
+          qb[ks][0] = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t);
+          qb[ks][1] = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t);
         }
 #pragma unroll
-        for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
-        m = -INFINITY;
-        l = 0.f;
+        for (int mt = 0; mt < 4; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+        m[0] = m[1] = -INFINITY;
+        l[0] = l[1] = 0.f;
         mode = seq_mode(p, b);
         if ((mode == CE_MODE_SUM || mode == CE_MODE_MAX) && !p.ul) {
           if (lane == 0 && warp == 0) flag_error(p.err, CE_EW_MODE);
@@ -359,16 +418,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const int j = static_cast<int>(x - base);
       const int ntok = min(ST, tok_b - j * ST);
-      const int s = it % NSTAGES;
-      const uint32_t ph = (it / NSTAGES) & 1;
-      if (!mbar_wait(&full[s], ph, p.err)) {
+      const int cs = s;
+      const uint32_t cph = ph;
+      if (++s == NSTAGES) {
+        s = 0;
+        ph ^= 1u;
+      }
+      // After a timeout the warp keeps walking (so the record writes stay in
+      // step) but waits for and computes nothing more.
+      if (!aborted && !mbar_wait_or_abort(&full[cs], cph, p.err, abort_flag)) {
         *abort_flag = 1;
         aborted = true;
-        break;
       }
-      uint8_t* kst = smem + s * STAGE_BYTES;
+      if (aborted) continue;
+      uint8_t* kst = smem + cs * STAGE_BYTES;
       uint8_t* vst = kst + HALF_STAGE;
-      const int tau0 = tb * 16;
       if (ntok < tau0 + 16) {
         // Zero V rows of tokens past the end so 0-probability * garbage stays 0.
         for (int idx = lane; idx < 16 * 8; idx += 32) {
@@ -380,323 +444,293 @@ __global__ void __launch_bounds__(THREADS, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
       }
-      if (tau0 < ntok) {
-        // ---- S = Q K^T over the warp's 16 tokens -----------------------------
-        float sacc[2][4];
+      if (tau0 >= ntok) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[cs]);
+        continue;
+      }
+      // ---- copy the warp's K and V fragments out, then release the stage -----
+      const uint32_t sbase = ring + cs * STAGE_BYTES;
+      uint32_t kf[4][4], vf[4][4];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+      for (int c = 0; c < 4; ++c) ldsm_x4(sbase + koff[c], kf[c][0], kf[c][1], kf[c][2], kf[c][3]);
 #pragma unroll
-          for (int kp = 0; kp < 2; ++kp) {
-            const int mi = lane >> 3, rr = lane & 7;
-            const int row = row_of(tau0 + nt * 8 + rr);
-            const int chunk = kp * 4 + mi;
-            const uint32_t addr = smem_addr(kst) + row * ROW_BYTES + ((chunk ^ (row & 7)) << 4);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(addr, b0, b1, b2, b3);
-            mma_16816(sacc[nt], qa[2 * kp][0], qa[2 * kp][1], b0, b1);
-            mma_16816(sacc[nt], qa[2 * kp + 1][0], qa[2 * kp + 1][1], b2, b3);
+      for (int c = 0; c < 4; ++c)
+        ldsm_x4_trans(sbase + voff[c], vf[c][0], vf[c][1], vf[c][2], vf[c][3]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[cs]);   // release orders the reads above
+      // ---- S^T = K Q^T over the warp's 16 tokens: 4 MMAs ----------------------
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_16816_full(sacc, kf[ks][0], kf[ks][1], kf[ks][2], kf[ks][3], qb[ks][0], qb[ks][1]);
+      const bool v_lo = tau0 + r < ntok, v_hi = tau0 + r + 8 < ntok;
+      float sv[4];
+      sv[0] = v_lo ? sacc[0] * p.scale_log2 : -INFINITY;
+      sv[1] = v_lo ? sacc[1] * p.scale_log2 : -INFINITY;
+      sv[2] = v_hi ? sacc[2] * p.scale_log2 : -INFINITY;
+      sv[3] = v_hi ? sacc[3] * p.scale_log2 : -INFINITY;
+      float mx0 = fmaxf(sv[0], sv[2]), mx1 = fmaxf(sv[1], sv[3]);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
+      const float mu0 = (mn0 == -INFINITY) ? 0.f : mn0;
+      const float mu1 = (mn1 == -INFINITY) ? 0.f : mn1;
+      float pv[4];
+      pv[0] = exp2f(sv[0] - mu0);
+      pv[1] = exp2f(sv[1] - mu1);
+      pv[2] = exp2f(sv[2] - mu0);
+      pv[3] = exp2f(sv[3] - mu1);
+      float rs0 = pv[0] + pv[2], rs1 = pv[1] + pv[3];
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        rs0 += __shfl_xor_sync(0xffffffffu, rs0, off);
+        rs1 += __shfl_xor_sync(0xffffffffu, rs1, off);
+      }
+      // Rescale the running state only when some head's max moved.
+      if (__any_sync(0xffffffffu, (mn0 != m[0]) || (mn1 != m[1]))) {
+        const float al0 = exp2f(m[0] - mu0), al1 = exp2f(m[1] - mu1);
+        l[0] *= al0;
+        l[1] *= al1;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          o[mt][0] *= al0;
+          o[mt][1] *= al1;
+          o[mt][2] *= al0;
+          o[mt][3] *= al1;
+        }
+        m[0] = mn0;
+        m[1] = mn1;
+      }
+      l[0] += rs0;
+      l[1] += rs1;
+      // ---- O^T += V^T P^T, P^T as bf16 hi + lo via movmatrix ------------------
+      uint32_t h01, l01, h23, l23;
+      split_bf16x2(pv[0], pv[1], h01, l01);
+      split_bf16x2(pv[2], pv[3], h23, l23);
+      const uint32_t bh0 = movmatrix_trans(h01), bh1 = movmatrix_trans(h23);
+      const uint32_t bl0 = movmatrix_trans(l01), bl1 = movmatrix_trans(l23);
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        mma_16816_full(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], bh0, bh1);
+        mma_16816_full(o[mt], vf[mt][0], vf[mt][1], vf[mt][2], vf[mt][3], bl0, bl1);
+      }
+      // ---- score side data --------------------------------------------------
+      if (mode != CE_MODE_NONE) {
+        const int64_t cbase = ip_b + static_cast<int64_t>(j) * UPS;
+        const int hcol = g * GROUP + 2 * t;
+        if (P == 1) {
+          if (v_lo) {
+            const int64_t cpos = cbase + tau0 + r;
+            if (cpos < p.kv_capacity)
+              *reinterpret_cast<float2*>(p.ul + cpos * H + hcol) = make_float2(sv[0], sv[1]);
           }
-        }
-        float sv[4];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const int tau = tau0 + nt * 8 + 2 * t + i;
-            sv[nt * 2 + i] = (tau < ntok) ? sacc[nt][i] * p.scale_log2 : -INFINITY;
+          if (v_hi) {
+            const int64_t cpos = cbase + tau0 + r + 8;
+            if (cpos < p.kv_capacity)
+              *reinterpret_cast<float2*>(p.ul + cpos * H + hcol) = make_float2(sv[2], sv[3]);
           }
-        float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m, mx);
-        const float mu = (m_new == -INFINITY) ? 0.f : m_new;
-        const float alpha = exp2f(m - mu);
-        float pv[4];
+        } else if (mode == CE_MODE_SUM) {
+          // P == 16: the warp's 16 tokens are exactly one page.
+          if (r == 0) {
+            const int64_t cpos = cbase + tb;
+            if (cpos < p.kv_capacity)
+              *reinterpret_cast<float2*>(p.ul + cpos * H + hcol) =
+                  make_float2(rs0 > 0.f ? mu0 + __log2f(rs0) : -INFINITY,
+                              rs1 > 0.f ? mu1 + __log2f(rs1) : -INFINITY);
+          }
+        } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) pv[i] = exp2f(sv[i] - mu);
-        float rs = (pv[0] + pv[1]) + (pv[2] + pv[3]);
-        rs += __shfl_xor_sync(0xffffffffu, rs, 1);
-        rs += __shfl_xor_sync(0xffffffffu, rs, 2);
-        l = l * alpha + rs;
-        m = m_new;
-#pragma unroll
-        for (int dt = 0; dt < 8; ++dt) {
-          o[dt][0] *= alpha;
-          o[dt][1] *= alpha;
-        }
-        // ---- O += P V (P as bf16 hi + lo) ------------------------------------
-        uint32_t ph0, pl0, ph2, pl2;
-        split_bf16x2(pv[0], pv[1], ph0, pl0);
-        split_bf16x2(pv[2], pv[3], ph2, pl2);
-#pragma unroll
-        for (int dp = 0; dp < 4; ++dp) {
-          const int mi = lane >> 3, rr = lane & 7;
-          const int row = row_of(tau0 + (mi & 1) * 8 + rr);
-          const int chunk = dp * 2 + (mi >> 1);
-          const uint32_t addr = smem_addr(vst) + row * ROW_BYTES + ((chunk ^ (row & 7)) << 4);
-          uint32_t v0, v1, v2, v3;
-          ldsm_x4_trans(addr, v0, v1, v2, v3);
-          mma_16816(o[2 * dp], ph0, ph2, v0, v1);
-          mma_16816(o[2 * dp], pl0, pl2, v0, v1);
-          mma_16816(o[2 * dp + 1], ph0, ph2, v2, v3);
-          mma_16816(o[2 * dp + 1], pl0, pl2, v2, v3);
-        }
-        // ---- score side data ------------------------------------------------
-        if (mode != CE_MODE_NONE) {
-          const int64_t cbase = ip_b + static_cast<int64_t>(j) * UPS;
-          if (P == 1) {
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-              for (int i = 0; i < 2; ++i) {
-                const int tau = tau0 + nt * 8 + 2 * t + i;
-                if (tau < ntok) {
-                  const int64_t cpos = cbase + tau;
-                  if (cpos < p.kv_capacity) p.ul[cpos * H + head] = sv[nt * 2 + i];
-                }
-              }
-          } else if (mode == CE_MODE_SUM) {
-            // P == 16: the warp's 16 tokens are exactly one page.
-            if (t == 0) {
-              const int64_t cpos = cbase + tb;
-              if (cpos < p.kv_capacity) p.ul[cpos * H + head] = (rs > 0.f) ? mu + log2f(rs) : -INFINITY;
+          for (int half = 0; half < 2; ++half) {
+            const int tau = tau0 + r + 8 * half;
+            if (tau < ntok) {
+              const int64_t cpos = cbase + tau / P;
+              if (cpos < p.kv_capacity)
+                *reinterpret_cast<float2*>(p.tl + (cpos * P + tau % P) * H + hcol) =
+                    make_float2(sv[2 * half], sv[2 * half + 1]);
             }
-          } else {
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-              for (int i = 0; i < 2; ++i) {
-                const int tau = tau0 + nt * 8 + 2 * t + i;
-                if (tau < ntok) {
-                  const int64_t cpos = cbase + tau / P;
-                  if (cpos < p.kv_capacity) p.tl[(cpos * P + tau % P) * H + head] = sv[nt * 2 + i];
-                }
-              }
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
     }
-    if (!aborted && cur_b >= 0) epilogue(cur_b);
+    if (cur_b >= 0) leave(cur_b);
   }
   __syncthreads();
 }
 
-// ---- finalize: split combine + scores ------------------------------------------
-constexpr int FIN_THREADS = 256;
-constexpr int FIN_WARPS = FIN_THREADS / 32;
-constexpr int MAX_SLOTS = 160 * NCW;   // (record, sub-part) slots a sequence can span
-constexpr int UNITS_PER_TASK = 128;
+// ---- combine: records of a sequence + sink -> output, lse ----------------------
+constexpr int CB_THREADS = 256;
+constexpr int MAX_SLOTS = 160 * NCW;   // (record, sub-part) slots one sequence can span
 
-struct FinParams {
+struct CombineParams {
   Params a;
+  int grid;   // CTAs the attention kernel was launched with
   int P;
-  int grid;   // attention grid (partition count)
 };
 
-__device__ __forceinline__ int cta_of_stage(int64_t x, int64_t S, int64_t grid) {
-  return static_cast<int>(((x + 1) * grid - 1) / S);
-}
-
-// When there are fewer stages than CTAs some partitions are empty and leave
-// no record; a sequence's record range [k0, k1] may straddle them.
-__device__ __forceinline__ bool cta_has_work(int64_t k, int64_t S, int64_t grid) {
-  return (k * S) / grid < ((k + 1) * S) / grid;
-}
-
-__device__ __forceinline__ void seq_records(const Params& p, int b, int64_t S, int64_t grid,
-                                            int& k0, int& k1) {
-  const int64_t pre = p.prefix[b], n = p.prefix[b + 1] - pre;
-  if (n <= 0) {
-    k0 = 1;
-    k1 = 0;
-    return;
-  }
-  k0 = cta_of_stage(pre, S, grid);
-  k1 = cta_of_stage(pre + n - 1, S, grid);
-}
-
-// Warp-cooperative log2 normaliser of query head h over its (record, sub)
-// slots plus the sink.  Every lane returns M and L2 = log2 sum.
-__device__ __forceinline__ void warp_head_norm(const Params& p, int b, int h, int k0, int k1,
-                                               int64_t S, int64_t grid, float& M, float& L2) {
-  const int lane = threadIdx.x & 31;
-  const int G = p.G, g = h / GROUP, r = h % GROUP, subs = NCW / G;
-  const int nslots = (k1 - k0 + 1) * subs;
-  float m = -INFINITY;
-  for (int i = lane; i < nslots; i += 32) {
-    const int k = k0 + i / subs, sb = i % subs;
-    if (!cta_has_work(k, S, grid)) continue;
-    const float* rec = p.rec + static_cast<int64_t>(b + k) * REC_FLOATS;
-    m = fmaxf(m, rec[REC_ROWS * D + (sb * G + g) * 8 + r]);
-  }
+// Add sequence b's page masses for KV head g into scores[g, unit]:
+//   SUM: sum_h 2^(page_lse - LSE_h)   MAX: sum_t max_h 2^(s_t,h - LSE_h)
+// L2 holds the group's 8 log2 normalisers.  Each thread takes 4 pages per
+// round and issues all their loads before any store.
+__device__ void score_pages(const Params& p, int b, int g, int mode, int P, const float* L2s) {
+  const int H = p.H;
+  const int tokens = seq_tokens(p, b, P);
+  const int npages = (tokens + P - 1) / P;
+  const int64_t ip = p.kv_indptr[b];
+  float L2[GROUP];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  const float sink2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
-  M = fmaxf(m, sink2);
-  if (M == -INFINITY) {
-    L2 = -INFINITY;
-    return;
-  }
-  float den = 0.f;
-  for (int i = lane; i < nslots; i += 32) {
-    const int k = k0 + i / subs, sb = i % subs;
-    if (!cta_has_work(k, S, grid)) continue;
-    const float* rec = p.rec + static_cast<int64_t>(b + k) * REC_FLOATS;
-    const int vrow = (sb * G + g) * 8 + r;
-    const float mk = rec[REC_ROWS * D + vrow];
-    if (mk != -INFINITY) den += rec[REC_ROWS * D + REC_ROWS + vrow] * exp2f(mk - M);
-  }
+  for (int rr = 0; rr < GROUP; ++rr) L2[rr] = L2s[rr];
+  const bool fresh_tail = p.zero_new && ((tokens - 1) % P) == 0;
+  const int32_t* __restrict__ kvi = p.kv_indices;
+  const float* __restrict__ ul = p.ul;
+  float* __restrict__ sc = p.scores + g * p.score_sg;
+  constexpr int BATCH = 4;
+  for (int j0 = threadIdx.x * BATCH; j0 < npages; j0 += CB_THREADS * BATCH) {
+    int unit[BATCH];
+    float contrib[BATCH], old[BATCH];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-  if (p.sinks) den += exp2f(sink2 - M);
-  L2 = M + log2f(den);
+    for (int q = 0; q < BATCH; ++q) {
+      const int jj = j0 + q;
+      unit[q] = -1;
+      if (jj < npages && ip + jj < p.kv_capacity) unit[q] = kvi[ip + jj];
+    }
+#pragma unroll
+    for (int q = 0; q < BATCH; ++q) {
+      const int jj = j0 + q;
+      contrib[q] = 0.f;
+      old[q] = 0.f;
+      if (unit[q] < 0 || unit[q] >= p.pool_units) continue;
+      old[q] = sc[unit[q]];
+      const int64_t cpos = ip + jj;
+      if (mode == CE_MODE_SUM) {
+        const float4* u4 = reinterpret_cast<const float4*>(ul + cpos * H + g * GROUP);
+        const float4 a = u4[0], c = u4[1];
+        const float uv[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int rr = 0; rr < GROUP; ++rr)
+          if (uv[rr] != -INFINITY) contrib[q] += exp2f(uv[rr] - L2[rr]);
+      } else if (P == 1) {
+        const float* uv = ul + cpos * H + g * GROUP;
+        float mx = 0.f;
+#pragma unroll
+        for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
+        contrib[q] = mx;
+      } else {
+        const int vt = (jj == npages - 1) ? tokens - jj * P : P;
+        for (int tt = 0; tt < vt; ++tt) {
+          const float* uv = p.tl + (cpos * P + tt) * H + g * GROUP;
+          float mx = 0.f;
+#pragma unroll
+          for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
+          contrib[q] += mx;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < BATCH; ++q) {
+      const int jj = j0 + q;
+      if (jj >= npages) continue;
+      if (unit[q] < 0 || unit[q] >= p.pool_units) {
+        if (ip + jj < p.kv_capacity) flag_error(p.err, CE_EW_INDEX);
+        continue;
+      }
+      const bool fresh = fresh_tail && jj == npages - 1;
+      sc[unit[q]] = fresh ? contrib[q] : old[q] + contrib[q];
+    }
+  }
 }
 
-__global__ void __launch_bounds__(FIN_THREADS)
-    finalize_kernel(const FinParams f) {
-  const Params& p = f.a;
-  const int bs = p.bs, H = p.H, G = p.G, P = f.P;
+// One task per (sequence b, group of 8 query heads): warp w handles head
+// hc*8 + w.  Its lanes first reduce the head's max and sum over the record
+// slots (plus the sink), then split as 8 dim groups x 4 slot groups to
+// accumulate the 64 outputs, so a sequence spread over many CTAs costs a few
+// rounds of independent loads rather than one chain per slot.
+__global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams cp) {
+  const Params& p = cp.a;
+  const int bs = p.bs, H = p.H, G = p.G;
   const int subs = NCW / G;
   const int64_t S = p.prefix[bs];
-  const int64_t grid = eff_grid(S, f.grid);
-  const int64_t total_units = min(static_cast<int64_t>(p.kv_indptr[bs]), p.kv_capacity);
+  const int64_t grid = eff_grid(S, cp.grid);
   const int hgroups = H / GROUP;
-  const int64_t combine_tasks = static_cast<int64_t>(bs) * hgroups;
-  const bool scoring = p.mode_of_row && p.scores && p.ul;
-  const int64_t unit_tasks = scoring ? (total_units + UNITS_PER_TASK - 1) / UNITS_PER_TASK : 0;
-  const int64_t ntasks = combine_tasks + unit_tasks;
+  const int64_t ntasks = static_cast<int64_t>(bs) * hgroups;
   __shared__ float wts[GROUP][MAX_SLOTS];
-  __shared__ float sh_l2[64];
-  __shared__ int sh_b;
+  __shared__ float sh_l2[GROUP];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
   for (int64_t task = blockIdx.x; task < ntasks; task += gridDim.x) {
-    if (task < combine_tasks) {
-      // -------- combine sequence b, query heads hc*8 .. hc*8+7 ---------------
-      const int b = static_cast<int>(task / hgroups), hc = static_cast<int>(task % hgroups);
-      int k0, k1;
-      seq_records(p, b, S, grid, k0, k1);
-      const int nslots = (k1 - k0 + 1) * subs;
-      const int h = hc * GROUP + warp;   // one warp per head
-      float M, L2;
-      warp_head_norm(p, b, h, k0, k1, S, grid, M, L2);
-      const int g = h / GROUP, r = h % GROUP;
-      const bool fits = nslots <= MAX_SLOTS;
-      if (fits) {
-        for (int i = lane; i < nslots; i += 32) {
-          const int k = k0 + i / subs, sb = i % subs;
-          float w = 0.f;
-          if (L2 != -INFINITY && cta_has_work(k, S, grid)) {
-            const float mk = p.rec[static_cast<int64_t>(b + k) * REC_FLOATS + REC_ROWS * D + (sb * G + g) * 8 + r];
-            if (mk != -INFINITY) w = exp2f(mk - L2);
-          }
-          wts[warp][i] = w;
-        }
-      }
-      if (lane == 0 && p.lse_out) p.lse_out[static_cast<int64_t>(b) * H + h] = L2 * LN2;
-      __syncwarp();
-      // Each warp writes its head's 64 outputs: O = sum_slots w_slot * O_slot.
-      for (int d = lane; d < D; d += 32) {
-        float acc = 0.f;
-        for (int i = 0; i < nslots; ++i) {
-          const int k = k0 + i / subs, sb = i % subs;
-          float w;
-          if (fits) {
-            w = wts[warp][i];
-          } else {
-            w = 0.f;
-            if (L2 != -INFINITY && cta_has_work(k, S, grid)) {
-              const float mk = p.rec[static_cast<int64_t>(b + k) * REC_FLOATS + REC_ROWS * D + (sb * G + g) * 8 + r];
-              if (mk != -INFINITY) w = exp2f(mk - L2);
-            }
-          }
-          if (w != 0.f) acc += w * p.rec[static_cast<int64_t>(b + k) * REC_FLOATS + ((sb * G + g) * 8 + r) * D + d];
-        }
-        const int64_t off = static_cast<int64_t>(b) * p.o_sb + static_cast<int64_t>(h) * p.o_sh + d;
-        if (p.out_f32)
-          reinterpret_cast<float*>(p.out)[off] = acc;
-        else
-          reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(acc);
-      }
-      __syncwarp();
-    } else {
-      // -------- scores of UNITS_PER_TASK consecutive CSR units ----------------
-      const int64_t u0 = (task - combine_tasks) * UNITS_PER_TASK;
-      const int64_t u_end = min(u0 + UNITS_PER_TASK, total_units);
-      if (threadIdx.x == 0) {
-        int lo = 0, hi = bs - 1;
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if (p.kv_indptr[mid] <= u0) lo = mid; else hi = mid - 1;
-        }
-        sh_b = lo;
-      }
-      __syncthreads();
-      int b = sh_b;
-      int64_t u = u0;
-      while (u < u_end && b < bs) {
-        const int64_t seg_end = min(u_end, static_cast<int64_t>(p.kv_indptr[b + 1]));
-        int mode = seq_mode(p, b);
-        if (mode == CE_MODE_MAX && P > 1 && !p.tl) mode = CE_MODE_NONE;
-        if ((mode == CE_MODE_SUM || mode == CE_MODE_MAX) && seg_end > u) {
-          int k0, k1;
-          seq_records(p, b, S, grid, k0, k1);
-          for (int h = warp; h < H; h += FIN_WARPS) {
-            float M, L2;
-            warp_head_norm(p, b, h, k0, k1, S, grid, M, L2);
-            if (lane == 0) sh_l2[h] = L2;
-          }
-          __syncthreads();
-          const int tokens = seq_tokens(p, b, P);
-          const int npages = (tokens + P - 1) / P;
-          const int64_t npairs = (seg_end - u) * G;
-          for (int64_t pr = threadIdx.x; pr < npairs; pr += FIN_THREADS) {
-            const int64_t cpos = u + pr / G;
-            const int g = static_cast<int>(pr % G);
-            const int64_t jj = cpos - p.kv_indptr[b];
-            if (jj >= npages) continue;
-            const int unit = p.kv_indices[cpos];
-            if (unit < 0 || unit >= p.pool_units) {
-              flag_error(p.err, CE_EW_INDEX);
-              continue;
-            }
-            const float* L2 = sh_l2 + g * GROUP;
-            float contrib = 0.f;
-            if (mode == CE_MODE_SUM) {
-              const float* uv = p.ul + cpos * H + g * GROUP;
+    const int b = static_cast<int>(task / hgroups), hc = static_cast<int>(task % hgroups);
+    const int64_t pre = p.prefix[b], n = p.prefix[b + 1] - pre;
+    if (n <= 0) continue;   // empty sequences were written by the attention kernel
+    const int k0 = cta_of_stage(pre, S, grid), k1 = cta_of_stage(pre + n - 1, S, grid);
+    const int nslots = (k1 - k0 + 1) * subs;
+    const int h = hc * GROUP + warp, g = h / GROUP, r = h % GROUP;
+    auto rec_of = [&](int i) -> const float* {
+      return p.rec + static_cast<int64_t>(b + k0 + i / subs) * REC_FLOATS;
+    };
+    auto vrow = [&](int i) -> int { return ((i % subs) * G + g) * 8 + r; };
+    auto live = [&](int i) -> bool { return cta_has_work(k0 + i / subs, S, grid); };
+    float M = -INFINITY;
+    for (int i = lane; i < nslots; i += 32)
+      if (live(i)) M = fmaxf(M, rec_of(i)[REC_ROWS * D + vrow(i)]);
 #pragma unroll
-              for (int rr = 0; rr < GROUP; ++rr)
-                if (uv[rr] != -INFINITY) contrib += exp2f(uv[rr] - L2[rr]);
-            } else if (P == 1) {
-              const float* uv = p.ul + cpos * H + g * GROUP;
-              float mx = 0.f;
-#pragma unroll
-              for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
-              contrib = mx;
-            } else {
-              const int vt = (jj == npages - 1) ? tokens - static_cast<int>(jj) * P : P;
-              for (int tt = 0; tt < vt; ++tt) {
-                const float* uv = p.tl + (cpos * P + tt) * H + g * GROUP;
-                float mx = 0.f;
-#pragma unroll
-                for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
-                contrib += mx;
-              }
-            }
-            float* sp = p.scores + g * p.score_sg + unit;
-            const bool fresh = p.zero_new && jj == npages - 1 && ((tokens - 1) % P) == 0;
-            *sp = fresh ? contrib : *sp + contrib;
-          }
-        }
-        __syncthreads();
-        u = max(u, seg_end);
-        ++b;
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float sink2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
+    M = fmaxf(M, sink2);
+    float den = 0.f;
+    if (M != -INFINITY)
+      for (int i = lane; i < nslots; i += 32) {
+        if (!live(i)) continue;
+        const float mk = rec_of(i)[REC_ROWS * D + vrow(i)];
+        if (mk != -INFINITY) den += rec_of(i)[REC_ROWS * D + REC_ROWS + vrow(i)] * exp2f(mk - M);
       }
-      __syncthreads();
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (p.sinks && M != -INFINITY) den += exp2f(sink2 - M);
+    const float L2 = (M == -INFINITY) ? -INFINITY : M + log2f(den);
+    const bool fits = nslots <= MAX_SLOTS;
+    auto weight = [&](int i) -> float {
+      if (L2 == -INFINITY || !live(i)) return 0.f;
+      const float mk = rec_of(i)[REC_ROWS * D + vrow(i)];
+      return mk == -INFINITY ? 0.f : exp2f(mk - L2);
+    };
+    if (fits)
+      for (int i = lane; i < nslots; i += 32) wts[warp][i] = weight(i);
+    __syncwarp();
+    // lane = dim group (8 dims) x slot group (4): sg = lane % 4, dg = lane / 4
+    const int sg = lane & 3, dg = lane >> 2;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+    for (int i = sg; i < nslots; i += 4) {
+      const float w = fits ? wts[warp][i] : weight(i);
+      if (w == 0.f) continue;
+      const float4* src = reinterpret_cast<const float4*>(rec_of(i) + vrow(i) * D + dg * 8);
+      const float4 a = src[0], c = src[1];
+      acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
+      acc[4] += w * c.x; acc[5] += w * c.y; acc[6] += w * c.z; acc[7] += w * c.w;
     }
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+      acc[d] += __shfl_xor_sync(0xffffffffu, acc[d], 1);
+      acc[d] += __shfl_xor_sync(0xffffffffu, acc[d], 2);
+    }
+    if (sg == 0) {
+#pragma unroll
+      for (int d = 0; d < 8; ++d) store_out(p, b, h, dg * 8 + d, acc[d]);
+    }
+    if (lane == 0) {
+      sh_l2[warp] = L2;
+      if (p.lse_out) p.lse_out[static_cast<int64_t>(b) * H + h] = L2 * LN2;
+    }
+    __syncthreads();
+    // The task's 8 heads are exactly KV head g's group: add this sequence's
+    // page masses for KV head g (pages in independent batches of 4).
+    int mode = (p.mode_of_row && p.scores && p.ul) ? seq_mode(p, b) : CE_MODE_NONE;
+    if (mode == CE_MODE_MAX && cp.P > 1 && !p.tl) mode = CE_MODE_NONE;
+    if (mode == CE_MODE_SUM || mode == CE_MODE_MAX)
+      score_pages(p, b, hc, mode, cp.P, sh_l2);
+    __syncthreads();
   }
 }
 
@@ -711,7 +745,7 @@ namespace {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct DecodeLayout {
-  size_t prefix, rec, ul, tl, total;
+  size_t prefix, lse2, rec, ul, tl, total;
 };
 
 DecodeLayout decode_layout(int bs, int64_t cap, int H, int P, int flags, int grid) {
@@ -719,6 +753,8 @@ DecodeLayout decode_layout(int bs, int64_t cap, int H, int P, int flags, int gri
   size_t off = 0;
   L.prefix = off;
   off += align256(sizeof(int32_t) * (bs + 1));
+  L.lse2 = off;
+  off += align256(sizeof(float) * (size_t)bs * H);
   L.rec = off;
   off += align256(sizeof(float) * (size_t)(bs + grid) * REC_FLOATS);
   L.ul = off;
@@ -807,6 +843,7 @@ extern "C" int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh, c
   p.lse_out = lse_out;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.prefix = reinterpret_cast<int32_t*>(ws + L.prefix);
+  p.lse2 = reinterpret_cast<float*>(ws + L.lse2);
   p.rec = reinterpret_cast<float*>(ws + L.rec);
   p.ul = (score_flags & 3) ? reinterpret_cast<float*>(ws + L.ul) : nullptr;
   p.tl = ((score_flags & 2) && page_size > 1) ? reinterpret_cast<float*>(ws + L.tl) : nullptr;
@@ -821,8 +858,10 @@ extern "C" int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh, c
     attn_kernel<1><<<grid, THREADS, SMEM_BYTES, st>>>(kmap, vmap, p);
   }
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("attn_kernel launch");
-  FinParams f{p, page_size, grid};
-  finalize_kernel<<<2 * grid, FIN_THREADS, 0, st>>>(f);
-  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("finalize_kernel launch");
+  CombineParams cp{p, grid, page_size};
+  const int cb_grid = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP), 4LL * grid)));
+  combine_kernel<<<cb_grid, CB_THREADS, 0, st>>>(cp);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("combine_kernel launch");
   return CE_OK;
 }
