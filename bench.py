@@ -37,6 +37,11 @@ METRIC = "decode tok/s with per-head H2O eviction (ragged 64-seq batch, 8K-32K b
 UNIT = "tok/s"
 H_TOTAL, G_TOTAL, D, PAGE, LAYERS, HIDDEN = 64, 8, 64, 16, 12, 2880
 SEQS_PER_GPU = 64
+# DRAM bytes (read + write, attn_kernel + combine_kernel) per resident token
+# from one ncu capture of the 8-sequence config-3 case
+# (profiles/decode_kernels_config3_8seq.md); the traffic of this streaming
+# kernel grows with resident tokens, so a full launch scales by its tokens.
+TRAFFIC_BYTES_PER_RESIDENT_TOKEN = 2174.0
 BUDGETS = [2048, 4096, 8192, 16384, 32768]
 POLICY_MIX = ["full", "recent", "random", "h2o_global", "h2o_per_head"]
 
@@ -408,7 +413,10 @@ def main():
                      "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                      "frac": achieved_gbs / peak, "peak_kind": peak_kind,
                      "bytes_per_launch": avg_bytes, "launch_ms": avg_launch_ms,
-                     "traffic": None},
+                     "traffic": TRAFFIC_BYTES_PER_RESIDENT_TOKEN * statistics.mean(tokens_resident)
+                                * G / G_TOTAL,
+                     "traffic_source": "ncu dram__bytes_read+write of an 8-sequence capture, "
+                                       "scaled by resident tokens"},
         "clocks": clock_info,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": step_bytes,
                 "d2h_bytes_per_step": step_bytes,
