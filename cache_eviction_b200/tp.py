@@ -49,10 +49,11 @@ def shard(kv_heads: int, q_heads: int, rank: int, world: int):
 def all_gather_heads(local: torch.Tensor, group) -> torch.Tensor:
     """[R, L, G_local, C] per rank -> [R, L, G_local*world, C], heads in rank order."""
     world = dist.get_world_size(group)
-    buf = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
-    dist.all_gather_into_tensor(buf, local.contiguous(), group=group)
     R, L, G, C = local.shape
-    return buf.permute(1, 2, 0, 3, 4).reshape(R, L, world * G, C).contiguous()
+    # ranks concatenated along dim 0 (the layout every backend accepts)
+    buf = torch.empty((world * R, L, G, C), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(buf, local.contiguous(), group=group)
+    return buf.view(world, R, L, G, C).permute(1, 2, 0, 3, 4).reshape(R, L, world * G, C).contiguous()
 
 
 def output_reduction(attn_out: torch.Tensor, w_slice: torch.Tensor, group, out=None):
