@@ -290,6 +290,81 @@ def run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
     return B * e2e_steps / (e2e_ms * 1e-3)
 
 
+def evict_microbench(world, rank, device, reps=3):
+    """one eviction step (select + compaction) over 32 rows x
+    this rank's KV heads x 4096 pages (65,536-token contexts), fp32 scores
+    lognormal(0, 2), P = R = B/4, for H2O global / H2O per-head / random at
+    budgets 2K..32K tokens.  Device time of ce_boundary and of ce_choose alone
+    (CUDA events, state restored outside the timed window), moved pages and
+    algorithmic GB/s."""
+    import torch
+    from cache_eviction_b200 import kernels, tp
+    G, _, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    R, N = 32, 4096
+    units = R * N + 1
+    gen = torch.Generator(device=device).manual_seed(55)
+    kp = torch.randn((units, G, PAGE, D), generator=gen, device=device).to(torch.bfloat16)
+    vp = torch.randn((units, G, PAGE, D), generator=gen, device=device).to(torch.bfloat16)
+    kptr, vptr = kernels.layer_pointers([kp], device), kernels.layer_pointers([vp], device)
+    scores0 = torch.randn((1, G, units), generator=gen, device=device).mul_(2.0).exp_()
+    perm = torch.randperm(units - 1, generator=gen, device=device).int() + 1
+    r2u0 = perm[:R * N].view(R, N).contiguous()
+    rows = torch.arange(R, dtype=torch.int32, device=device)
+    marks = torch.zeros(units, dtype=torch.int32, device=device)
+    uni = torch.rand((R, 1, G, N), generator=gen, device=device, dtype=torch.float64)
+    pos_fresh = torch.arange(N, dtype=torch.int32, device=device).expand(R, G, N).contiguous()
+    out = {}
+    epoch = 0
+    for pol in ("h2o_global_2048", "head_sum_2048", "random_2048"):
+        for budget in BUDGETS:
+            b = budget // PAGE
+            params = [dict(n=N, budget=b, prefix=b // 4, recent=b // 4, cursor=None, policy=pol, seed=i)
+                      for i in range(R)]
+            prm = kernels.row_params(params, device)
+            table = torch.zeros((R, N), dtype=torch.int32, device=device)
+            frontier = torch.zeros(R, dtype=torch.int32, device=device)
+            count = torch.zeros(R, dtype=torch.int32, device=device)
+            pos = torch.zeros((R, 1, G, b), dtype=torch.int32, device=device)
+            r2u, scores = r2u0.clone(), scores0.clone()
+            times, sel_times = [], []
+            for it in range(reps + 1):
+                r2u.copy_(r2u0), scores.copy_(scores0), frontier.zero_(), count.zero_()
+                epoch += 1
+                a = torch.cuda.Event(enable_timing=True)
+                e = torch.cuda.Event(enable_timing=True)
+                a.record()
+                res, _ = kernels.boundary(table, r2u, frontier, count, pos, scores, kptr, vptr, G, PAGE,
+                                          rows, prm, N, N + 1, True, marks=marks, epoch=epoch,
+                                          uniforms=uni if pol == "random_2048" else None,
+                                          head_offset=off, hazard_bytes=1 << 30, max_width=b)
+                e.record()
+                sc = scores0[0].gather(1, r2u0.view(1, -1).expand(G, -1).long()).view(G, R, N)
+                sc = sc.permute(1, 0, 2).contiguous()
+                a2 = torch.cuda.Event(enable_timing=True)
+                e2 = torch.cuda.Event(enable_timing=True)
+                a2.record()
+                kernels.choose(pos_fresh, uni.view(R, G, N) if pol == "random_2048" else sc, prm, 1, G,
+                               max_n=N + 1, kept_stride=b)
+                e2.record()
+                torch.cuda.synchronize()
+                if it:
+                    times.append(a.elapsed_time(e) * 1e3)
+                    sel_times.append(a2.elapsed_time(e2) * 1e3)
+            status = res[:, 0].cpu()
+            assert bool((status == 0).all()), status
+            p_u, mid = b // 4, b - 2 * (b // 4)
+            mpos = pos[:, 0, :, p_u:p_u + mid]
+            moved = int((mpos != (torch.arange(mid, device=device, dtype=torch.int32) + p_u)).sum())
+            nbytes = R * G * N * 4 + (R * G * N * 8 if pol == "random_2048" else 0) + R * G * b * 4 \
+                + moved * (2 * 2 * PAGE * D * 2 + 8)
+            us = statistics.median(times)
+            out[f"{pol}_{budget}"] = {"evict_step_us": us, "select_us": statistics.median(sel_times),
+                                      "moved_pages": moved, "gbs": nbytes / (us * 1e-6) / 1e9}
+    del kp, vp
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -300,6 +375,8 @@ def main():
     ap.add_argument("--no-oproj", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="CPU-baseline sample length (0 skips it)")
+    ap.add_argument("--no-evict-bench", action="store_true",
+                    help="skip the config-5 eviction-step leg")
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (small cases for profiling)")
     args = ap.parse_args()
@@ -403,6 +480,12 @@ def main():
         e2e_value = run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
                             scale, after_layer, barrier, max_over_ranks, e2e_steps)
 
+    evict5 = None
+    if not args.no_evict_bench:
+        evict5 = evict_microbench(world, rank, device)
+        if world > 1:
+            for k in evict5:
+                evict5[k]["evict_step_us"] = max_over_ranks(evict5[k]["evict_step_us"])
     peak, peak_kind = measured_peak_hbm()
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -427,6 +510,7 @@ def main():
                   "boundary_ms_mean": statistics.mean(boundary_ms) if boundary_ms else None,
                   "boundary_rows": n_bound_rows},
         "resident_tokens_mean": statistics.mean(tokens_resident),
+        "evict_config5": evict5,
     }
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         from oracle import oracle

@@ -130,10 +130,50 @@ struct Thresh {
   bool none;  // k == 0: nothing selected
 };
 
-// Threshold of the k largest (key, pos) pairs among unprotected columns.
-// pv[c] < 0 marks a protected column; pv[c] & 0x7fffffff is the position.
-__device__ Thresh radix_threshold(const uint64_t* kv, const int32_t* pv, int N, int k,
-                                  int nonprot, int key_bits, Sh& sh) {
+// Column sets a CTA selects over.  pv < 0 marks a protected column (position
+// in the low 31 bits); pv == -1 marks a slot past the end (no column).
+//
+// RegCols: up to ITEMS columns per thread held in registers (column
+// c = threadIdx.x + i*T) -- every pass of the select is then register work.
+// MemCols: any number of columns in a global workspace (L2-resident).
+constexpr int32_t kAbsent = -1;
+
+template <int ITEMS>
+struct RegCols {
+  uint64_t key[ITEMS];
+  int32_t pv[ITEMS];
+  template <class F>
+  __device__ __forceinline__ void each(F f) const {
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i)
+      if (pv[i] != kAbsent) f(static_cast<int>(threadIdx.x) + i * T, key[i], pv[i]);
+  }
+};
+
+struct MemCols {
+  const uint64_t* kv;
+  const int32_t* pv;
+  int N;
+  template <class F>
+  __device__ __forceinline__ void each(F f) const {
+    for (int c = threadIdx.x; c < N; c += T) f(c, kv[c], pv[c]);
+  }
+};
+
+// Plain column range [0, N) for ranks that do not need keys.
+struct RangeCols {
+  int N;
+  template <class F>
+  __device__ __forceinline__ void each(F f) const {
+    for (int c = threadIdx.x; c < N; c += T) f(c, 0ull, 0);
+  }
+};
+
+// Threshold of the k largest (key, pos) pairs among unprotected columns:
+// MSB-first 8-bit radix select on the key, then on the position among the
+// columns equal to the threshold key (newer wins).
+template <class Cols>
+__device__ Thresh radix_threshold(const Cols& cols, int k, int nonprot, int key_bits, Sh& sh) {
   Thresh th{0ull, 0, false};
   if (k <= 0) {
     th.none = true;
@@ -145,11 +185,9 @@ __device__ Thresh radix_threshold(const uint64_t* kv, const int32_t* pv, int N, 
   for (int shift = key_bits - 8; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += T) sh.hist[i] = 0;
     __syncthreads();
-    for (int c = threadIdx.x; c < N; c += T) {
-      if (pv[c] < 0) continue;
-      const uint64_t key = kv[c];
-      if ((key & mask) == prefix) atomicAdd(&sh.hist[(key >> shift) & 255], 1);
-    }
+    cols.each([&](int, uint64_t key, int32_t pc) {
+      if (pc >= 0 && (key & mask) == prefix) atomicAdd(&sh.hist[(key >> shift) & 255], 1);
+    });
     __syncthreads();
     find_digit(sh, krem);
     const int d = sh.bc[0];
@@ -165,11 +203,9 @@ __device__ Thresh radix_threshold(const uint64_t* kv, const int32_t* pv, int N, 
     for (int shift = 24; shift >= 0; shift -= 8) {
       for (int i = threadIdx.x; i < 256; i += T) sh.hist[i] = 0;
       __syncthreads();
-      for (int c = threadIdx.x; c < N; c += T) {
-        const int pc = pv[c];
-        if (pc < 0 || kv[c] != prefix) continue;
-        if ((pc & pm) == pp) atomicAdd(&sh.hist[(pc >> shift) & 255], 1);
-      }
+      cols.each([&](int, uint64_t key, int32_t pc) {
+        if (pc >= 0 && key == prefix && (pc & pm) == pp) atomicAdd(&sh.hist[(pc >> shift) & 255], 1);
+      });
       __syncthreads();
       find_digit(sh, kr);
       kr -= sh.bc[1];
@@ -187,22 +223,22 @@ __device__ __forceinline__ bool selected(const Thresh& th, uint64_t key, int pc)
   return key > th.key || (key == th.key && pc >= th.pos);
 }
 
-// Rank every column whose posf(c) >= 0 by ascending position using a bitmap
-// of nw words, then call emit(rank, c, pos).  Positions must be < 32*nw.
-template <class PosF, class EmitF>
-__device__ void emit_sorted(int N, int nw, uint32_t* bits, int* pre, PosF posf, EmitF emit, Sh& sh,
-                            int32_t* err) {
+// Rank every column whose posf(c, key, pv) >= 0 by ascending position using a
+// bitmap of nw words, then call emit(rank, c, pos).  Positions must be < 32*nw.
+template <class Cols, class PosF, class EmitF>
+__device__ void emit_sorted(const Cols& cols, int nw, uint32_t* bits, int* pre, PosF posf, EmitF emit,
+                            Sh& sh, int32_t* err) {
   for (int w = threadIdx.x; w < nw; w += T) bits[w] = 0u;
   __syncthreads();
-  for (int c = threadIdx.x; c < N; c += T) {
-    const int p = posf(c);
-    if (p < 0) continue;
+  cols.each([&](int c, uint64_t key, int32_t pc) {
+    const int p = posf(c, key, pc);
+    if (p < 0) return;
     if (p >= 32 * nw) {
       flag_error(err, CE_EW_SHAPE);
-      continue;
+      return;
     }
     atomicOr(&bits[p >> 5], 1u << (p & 31));
-  }
+  });
   __syncthreads();
   int carry = 0;
   for (int base = 0; base < nw; base += T) {
@@ -214,14 +250,17 @@ __device__ void emit_sorted(int N, int nw, uint32_t* bits, int* pre, PosF posf, 
     carry += tot;
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < N; c += T) {
-    const int p = posf(c);
-    if (p < 0 || p >= 32 * nw) continue;
+  cols.each([&](int c, uint64_t key, int32_t pc) {
+    const int p = posf(c, key, pc);
+    if (p < 0 || p >= 32 * nw) return;
     const int rank = pre[p >> 5] + __popc(bits[p >> 5] & ((1u << (p & 31)) - 1u));
     emit(rank, c, p);
-  }
+  });
   __syncthreads();
 }
+
+// Register path for segments of up to REG_ITEMS * T columns.
+constexpr int REG_ITEMS = 16;
 
 __device__ __forceinline__ bool is_prot(int pos, const ce_row_params& q) {
   return pos < q.prefix || pos >= q.n - q.recent || (q.cursor >= 0 && pos >= q.cursor);
@@ -257,6 +296,68 @@ __device__ __forceinline__ float score_f(const void* s, int dt, int64_t idx) {
                             : static_cast<const float*>(s)[idx];
 }
 
+// Key of column c for ce_choose; returns whether the column is protected.
+__device__ __forceinline__ bool choose_column(const ChooseParams& p, int i, int l, int g, int64_t base,
+                                              const ce_row_params& q, int c, uint64_t& key,
+                                              int32_t& pv) {
+  const int segs = p.layers * p.heads;
+  const int pos = p.pos[base + c];
+  const bool pr = is_prot(pos, q);
+  pv = pos | (pr ? static_cast<int>(0x80000000u) : 0);
+  key = 0;
+  if (pr) return true;
+  switch (q.policy) {
+    case CE_POLICY_RESERVOIR:
+      key = reservoir53(q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
+      break;
+    case CE_POLICY_H2O_GLOBAL:
+      if (p.sdt == CE_DTYPE_F64) {
+        double acc = 0.0;
+        for (int gg = 0; gg < p.heads; ++gg)
+          acc += static_cast<const double*>(p.score)[(static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c];
+        key = key_from_f64(acc);
+      } else {
+        float acc = 0.f;
+        for (int gg = 0; gg < p.heads; ++gg)
+          acc += static_cast<const float*>(p.score)[(static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c];
+        key = key_from_f32(acc);
+      }
+      break;
+    case CE_POLICY_PREFIX_SLIDING:
+      break;
+    default:
+      key = (p.sdt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.score)[base + c])
+                                    : key_from_f32(static_cast<const float*>(p.score)[base + c]);
+  }
+  return false;
+}
+
+template <class Cols>
+__device__ void choose_body(const ChooseParams& p, const Cols& cols, int np, int i, int s, int N,
+                            const ce_row_params& q, Sh& sh, uint32_t* dyn) {
+  const int segs = p.layers * p.heads;
+  const int nprot = block_sum(np, sh);
+  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * segs + s] = nprot;
+  if (nprot > q.budget) return;
+  const int k = (q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : q.budget - nprot;
+  const int bits = (q.policy == CE_POLICY_RESERVOIR) ? 64 : (p.sdt == CE_DTYPE_F64 ? 64 : 32);
+  const Thresh th = radix_threshold(cols, k, N - nprot, bits, sh);
+  int32_t* out = p.kept + (static_cast<int64_t>(i) * segs + s) * p.kept_stride;
+  const int stride = p.kept_stride;
+  int32_t* err = p.err;
+  emit_sorted(
+      cols, p.nw, dyn, reinterpret_cast<int*>(dyn + p.nw),
+      [&](int, uint64_t key, int32_t pc) -> int {
+        if (pc < 0) return pc & 0x7fffffff;
+        return selected(th, key, pc) ? pc : -1;
+      },
+      [&](int rank, int c, int) {
+        if (rank < stride) out[rank] = c;
+        else flag_error(err, CE_EW_CAPACITY);
+      },
+      sh, p.err);
+}
+
 __global__ void __launch_bounds__(T) choose_seg_kernel(const ChooseParams p) {
   extern __shared__ uint32_t dyn[];
   __shared__ Sh sh;
@@ -266,68 +367,24 @@ __global__ void __launch_bounds__(T) choose_seg_kernel(const ChooseParams p) {
   const ce_row_params q = p.params[i];
   const int N = p.ncols ? min(p.ncols[i], p.n_cols) : p.n_cols;
   const int64_t base = (static_cast<int64_t>(i) * segs + s) * p.n_cols;
-  uint64_t* kv = p.kv + base;
-  int32_t* pv = p.pv + base;
   int np = 0;
-  for (int c = threadIdx.x; c < N; c += T) {
-    const int pos = p.pos[base + c];
-    const bool pr = is_prot(pos, q);
-    pv[c] = pos | (pr ? static_cast<int>(0x80000000u) : 0);
-    np += pr;
-    if (pr) continue;
-    uint64_t key = 0;
-    switch (q.policy) {
-      case CE_POLICY_RESERVOIR:
-        key = reservoir53(q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
-        break;
-      case CE_POLICY_H2O_GLOBAL:
-        if (p.sdt == CE_DTYPE_F64) {
-          double acc = 0.0;
-          for (int gg = 0; gg < p.heads; ++gg)
-            acc += static_cast<const double*>(p.score)[(static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c];
-          key = key_from_f64(acc);
-        } else {
-          float acc = 0.f;
-          for (int gg = 0; gg < p.heads; ++gg)
-            acc += static_cast<const float*>(p.score)[(static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c];
-          key = key_from_f32(acc);
-        }
-        break;
-      case CE_POLICY_PREFIX_SLIDING:
-        break;
-      default:
-        key = (p.sdt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.score)[base + c])
-                                      : key_from_f32(static_cast<const float*>(p.score)[base + c]);
+  if (N <= REG_ITEMS * T) {
+    RegCols<REG_ITEMS> cols;
+#pragma unroll
+    for (int it = 0; it < REG_ITEMS; ++it) {
+      const int c = threadIdx.x + it * T;
+      cols.pv[it] = kAbsent;
+      cols.key[it] = 0;
+      if (c < N) np += choose_column(p, i, l, g, base, q, c, cols.key[it], cols.pv[it]);
     }
-    kv[c] = key;
+    choose_body(p, cols, np, i, s, N, q, sh, dyn);
+  } else {
+    uint64_t* kv = p.kv + base;
+    int32_t* pv = p.pv + base;
+    for (int c = threadIdx.x; c < N; c += T) np += choose_column(p, i, l, g, base, q, c, kv[c], pv[c]);
+    __syncthreads();
+    choose_body(p, MemCols{kv, pv, N}, np, i, s, N, q, sh, dyn);
   }
-  const int nprot = block_sum(np, sh);
-  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * segs + s] = nprot;
-  if (nprot > q.budget) return;
-  int k = (q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : q.budget - nprot;
-  const int nonprot = N - nprot;
-  int bits = (q.policy == CE_POLICY_H2O_GLOBAL || q.policy == CE_POLICY_HEAD_SUM ||
-              q.policy == CE_POLICY_HEAD_MAX || q.policy == CE_POLICY_RANDOM)
-                 ? (p.sdt == CE_DTYPE_F64 ? 64 : 32)
-                 : 64;
-  const Thresh th = radix_threshold(kv, pv, N, k, nonprot, bits, sh);
-  int32_t* out = p.kept + (static_cast<int64_t>(i) * segs + s) * p.kept_stride;
-  uint32_t* bitsm = dyn;
-  int* pre = reinterpret_cast<int*>(dyn + p.nw);
-  const int stride = p.kept_stride;
-  int32_t* err = p.err;
-  emit_sorted(
-      N, p.nw, bitsm, pre,
-      [&](int c) -> int {
-        const int pc = pv[c];
-        if (pc < 0) return pc & 0x7fffffff;
-        return selected(th, kv[c], pc) ? pc : -1;
-      },
-      [&](int rank, int c, int) {
-        if (rank < stride) out[rank] = c;
-        else flag_error(err, CE_EW_CAPACITY);
-      },
-      sh, p.err);
 }
 
 __global__ void choose_status_kernel(const ChooseParams p) {
@@ -373,7 +430,7 @@ struct BParams {
   int udt;
   const float* gscores;
   int GH;
-  int live, max_cols, nw;
+  int live, max_cols, max_width, nw;
   // workspace
   uint64_t* kv;
   int32_t* pv;
@@ -426,6 +483,92 @@ __device__ __forceinline__ float unit_score(const BParams& p, int l, int g, int 
   return p.scores[l * p.sls + g * p.shs + unit];
 }
 
+// Key of boundary column c for segment (i, lg); returns whether the column is
+// protected.  Keys follow _scores (runtime:400-412).
+__device__ __forceinline__ bool bsel_column(const BParams& p, const RowCtx& r, int i, int lg, int c,
+                                            uint64_t& key, int32_t& pv) {
+  const int LG = p.L * p.G;
+  const int l = lg / p.G, g = lg % p.G;
+  const int pos = col_pos(p, r, lg, c);
+  const bool pr = is_prot(pos, r.q);
+  pv = pos | (pr ? static_cast<int>(0x80000000u) : 0);
+  key = 0;
+  if (pr) return true;
+  switch (r.q.policy) {
+    case CE_POLICY_RANDOM: {
+      const int64_t ui = (static_cast<int64_t>(i) * LG + lg) * p.max_cols + c;
+      key = (p.udt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.uniforms)[ui])
+                                    : key_from_f32(static_cast<const float*>(p.uniforms)[ui]);
+      break;
+    }
+    case CE_POLICY_RESERVOIR:
+      key = reservoir53(r.q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
+      break;
+    case CE_POLICY_HEAD_SUM:
+    case CE_POLICY_HEAD_MAX:
+      key = key_from_f32(unit_score(p, l, g, col_unit(p, r, c)));
+      break;
+    case CE_POLICY_H2O_GLOBAL: {
+      float acc = 0.f;
+      if (p.gscores) {
+        for (int gg = 0; gg < p.GH; ++gg)
+          acc += p.gscores[((static_cast<int64_t>(i) * p.L + l) * p.GH + gg) * p.max_cols + c];
+      } else {
+        const int u = col_unit(p, r, c);
+        for (int gg = 0; gg < p.G; ++gg) acc += unit_score(p, l, gg, u);
+      }
+      key = key_from_f32(acc);
+      break;
+    }
+    default:
+      break;
+  }
+  return false;
+}
+
+template <class Cols>
+__device__ void bsel_body(const BParams& p, const RowCtx& r, const Cols& cols, int np, int i, int lg,
+                          int64_t base, Sh& sh, uint32_t* bitsm, int* pre) {
+  const int LG = p.L * p.G;
+  const int l = lg / p.G, g = lg % p.G;
+  const int nprot = block_sum(np, sh);
+  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
+  if (nprot > r.q.budget) return;
+  const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
+  const int bits = key_bits_of(r.q.policy, p.udt);
+  const Thresh th = radix_threshold(cols, k, r.N - nprot, bits, sh);
+  int32_t* mid = p.mid_col + base;
+  int32_t* npos = p.new_pos + base;
+  int32_t* srcu = p.src_unit + base;
+  float* ssc = p.score_scr + base;
+  const int max_cols = p.max_cols;
+  // Middle survivors in ascending position.
+  emit_sorted(
+      cols, p.nw, bitsm, pre,
+      [&](int, uint64_t key, int32_t pc) -> int { return selected(th, key, pc) ? pc : -1; },
+      [&](int rank, int c, int pos) {
+        if (nprot + rank >= max_cols) return;
+        mid[rank] = c;
+        npos[nprot + rank] = pos;
+        const int u = col_unit(p, r, c);
+        srcu[rank] = u;
+        ssc[rank] = unit_score(p, l, g, u);
+      },
+      sh, p.err);
+  // Protected part: this head's positions at the (0,0) head's protected
+  // columns taken in (0,0) position order (runtime:442-443,469).
+  emit_sorted(
+      RangeCols{r.N}, p.nw, bitsm, pre,
+      [&](int c, uint64_t, int32_t) -> int {
+        const int p00 = col_pos(p, r, 0, c);
+        return is_prot(p00, r.q) ? p00 : -1;
+      },
+      [&](int rank, int c, int) {
+        if (rank < max_cols) npos[rank] = col_pos(p, r, lg, c);
+      },
+      sh, p.err);
+}
+
 // Segment blocks: R*L*G of them, then R row blocks.
 __global__ void __launch_bounds__(T) bsel_kernel(const BParams p) {
   extern __shared__ uint32_t dyn[];
@@ -436,90 +579,27 @@ __global__ void __launch_bounds__(T) bsel_kernel(const BParams p) {
   const int nseg = p.R * LG;
   if (static_cast<int>(blockIdx.x) < nseg) {
     const int i = blockIdx.x / LG, lg = blockIdx.x % LG;
-    const int l = lg / p.G, g = lg % p.G;
     const RowCtx r = row_ctx(p, i);
     if (!row_shape_ok(p, r) || r.N <= r.q.budget) return;
     const int64_t base = (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
-    uint64_t* kv = p.kv + base;
-    int32_t* pv = p.pv + base;
     int np = 0;
-    for (int c = threadIdx.x; c < r.N; c += T) {
-      const int pos = col_pos(p, r, lg, c);
-      const bool pr = is_prot(pos, r.q);
-      pv[c] = pos | (pr ? static_cast<int>(0x80000000u) : 0);
-      np += pr;
-      if (pr) continue;
-      uint64_t key = 0;
-      switch (r.q.policy) {
-        case CE_POLICY_RANDOM: {
-          const int64_t ui = (static_cast<int64_t>(i) * LG + lg) * p.max_cols + c;
-          key = (p.udt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.uniforms)[ui])
-                                        : key_from_f32(static_cast<const float*>(p.uniforms)[ui]);
-          break;
-        }
-        case CE_POLICY_RESERVOIR:
-          key = reservoir53(r.q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
-          break;
-        case CE_POLICY_HEAD_SUM:
-        case CE_POLICY_HEAD_MAX:
-          key = key_from_f32(unit_score(p, l, g, col_unit(p, r, c)));
-          break;
-        case CE_POLICY_H2O_GLOBAL: {
-          float acc = 0.f;
-          if (p.gscores) {
-            for (int gg = 0; gg < p.GH; ++gg)
-              acc += p.gscores[((static_cast<int64_t>(i) * p.L + l) * p.GH + gg) * p.max_cols + c];
-          } else {
-            const int u = col_unit(p, r, c);
-            for (int gg = 0; gg < p.G; ++gg) acc += unit_score(p, l, gg, u);
-          }
-          key = key_from_f32(acc);
-          break;
-        }
-        default:
-          break;
+    if (r.N <= REG_ITEMS * T) {
+      RegCols<REG_ITEMS> cols;
+#pragma unroll
+      for (int it = 0; it < REG_ITEMS; ++it) {
+        const int c = threadIdx.x + it * T;
+        cols.pv[it] = kAbsent;
+        cols.key[it] = 0;
+        if (c < r.N) np += bsel_column(p, r, i, lg, c, cols.key[it], cols.pv[it]);
       }
-      kv[c] = key;
+      bsel_body(p, r, cols, np, i, lg, base, sh, bitsm, pre);
+    } else {
+      uint64_t* kv = p.kv + base;
+      int32_t* pv = p.pv + base;
+      for (int c = threadIdx.x; c < r.N; c += T) np += bsel_column(p, r, i, lg, c, kv[c], pv[c]);
+      __syncthreads();
+      bsel_body(p, r, MemCols{kv, pv, r.N}, np, i, lg, base, sh, bitsm, pre);
     }
-    const int nprot = block_sum(np, sh);
-    if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
-    if (nprot > r.q.budget) return;
-    const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
-    const int bits = key_bits_of(r.q.policy, p.udt);
-    const Thresh th = radix_threshold(kv, pv, r.N, k, r.N - nprot, bits, sh);
-    int32_t* mid = p.mid_col + base;
-    int32_t* npos = p.new_pos + base;
-    int32_t* srcu = p.src_unit + base;
-    float* ssc = p.score_scr + base;
-    const int max_cols = p.max_cols;
-    // Middle survivors in ascending position.
-    emit_sorted(
-        r.N, p.nw, bitsm, pre,
-        [&](int c) -> int {
-          const int pc = pv[c];
-          return selected(th, kv[c], pc) ? pc : -1;
-        },
-        [&](int rank, int c, int pos) {
-          if (nprot + rank >= max_cols) return;
-          mid[rank] = c;
-          npos[nprot + rank] = pos;
-          const int u = col_unit(p, r, c);
-          srcu[rank] = u;
-          ssc[rank] = unit_score(p, l, g, u);
-        },
-        sh, p.err);
-    // Protected part: this head's positions at the (0,0) head's protected
-    // columns taken in (0,0) position order (runtime:442-443,469).
-    emit_sorted(
-        r.N, p.nw, bitsm, pre,
-        [&](int c) -> int {
-          const int p00 = col_pos(p, r, 0, c);
-          return is_prot(p00, r.q) ? p00 : -1;
-        },
-        [&](int rank, int c, int) {
-          if (rank < max_cols) npos[rank] = col_pos(p, r, lg, c);
-        },
-        sh, p.err);
   } else {
     // ---------------- row block: table, candidates, leftovers, marks -----------
     const int i = blockIdx.x - nseg;
@@ -537,8 +617,8 @@ __global__ void __launch_bounds__(T) bsel_kernel(const BParams p) {
     int32_t* ntab = p.new_table + static_cast<int64_t>(i) * p.max_cols;
     int32_t* crank = p.cand_rank + static_cast<int64_t>(i) * p.max_cols;
     emit_sorted(
-        r.N, p.nw, bitsm, pre,
-        [&](int c) -> int {
+        RangeCols{r.N}, p.nw, bitsm, pre,
+        [&](int c, uint64_t, int32_t) -> int {
           const int p00 = col_pos(p, r, 0, c);
           return is_prot(p00, r.q) ? p00 : -1;
         },
@@ -606,7 +686,7 @@ __global__ void bvalidate_kernel(const BParams p) {
       st = 2;
     } else {
       after = info[3];
-      if (after > p.table_width || after > p.pos_cap) {
+      if (after > p.table_width || after > p.pos_cap || info[2] > p.max_width) {
         st = 6;
         flag_error(p.err, CE_EW_CAPACITY);
       }
@@ -627,13 +707,13 @@ struct Item {
 };
 
 __device__ __forceinline__ bool decode_item(const BParams& p, int64_t item, int l0, int nl, Item& it) {
-  const int64_t per_row = static_cast<int64_t>(nl) * p.G * p.max_cols;
+  const int64_t per_row = static_cast<int64_t>(nl) * p.G * p.max_width;
   it.i = static_cast<int>(item / per_row);
   int64_t rem = item % per_row;
-  const int ll = static_cast<int>(rem / (static_cast<int64_t>(p.G) * p.max_cols));
-  rem %= static_cast<int64_t>(p.G) * p.max_cols;
-  it.g = static_cast<int>(rem / p.max_cols);
-  it.j = static_cast<int>(rem % p.max_cols);
+  const int ll = static_cast<int>(rem / (static_cast<int64_t>(p.G) * p.max_width));
+  rem %= static_cast<int64_t>(p.G) * p.max_width;
+  it.g = static_cast<int>(rem / p.max_width);
+  it.j = static_cast<int>(rem % p.max_width);
   it.l = l0 + ll;
   it.base = (static_cast<int64_t>(it.i) * p.L * p.G + static_cast<int64_t>(it.l) * p.G + it.g) * p.max_cols;
   const int32_t* info = p.row_info + it.i * 8;
@@ -659,7 +739,7 @@ __device__ __forceinline__ void copy_block(uint8_t* dst, const uint8_t* src, int
 
 __global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int l0, int nl) {
   const int lane = threadIdx.x & 31;
-  const int64_t nitems = static_cast<int64_t>(p.R) * nl * p.G * p.max_cols;
+  const int64_t nitems = static_cast<int64_t>(p.R) * nl * p.G * p.max_width;
   const int bytes = p.P * 128;
   for (int64_t item = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; item < nitems;
        item += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
@@ -680,7 +760,7 @@ __global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int l0, i
 
 __global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int l0, int nl) {
   const int lane = threadIdx.x & 31;
-  const int64_t nitems = static_cast<int64_t>(p.R) * nl * p.G * p.max_cols;
+  const int64_t nitems = static_cast<int64_t>(p.R) * nl * p.G * p.max_width;
   const int bytes = p.P * 128;
   for (int64_t item = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; item < nitems;
        item += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
@@ -837,8 +917,8 @@ BLayout boundary_layout(int R, int L, int G, int max_cols, int64_t hazard_bytes)
   return b;
 }
 
-int64_t hazard_per_layer(int R, int G, int max_cols, int P) {
-  return static_cast<int64_t>(R) * G * max_cols * 2 * P * 128;
+int64_t hazard_per_layer(int R, int G, int max_width, int P) {
+  return static_cast<int64_t>(R) * G * max_width * 2 * P * 128;
 }
 
 int sel_smem(int nw) { return nw * 8; }
@@ -902,13 +982,14 @@ extern "C" int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_col
 
 extern "C" int64_t ce_boundary_workspace_bytes(int32_t num_rows, int32_t layers, int32_t kv_heads,
                                                int32_t head_dim, int32_t page_size,
-                                               int32_t max_cols, int32_t global_heads,
-                                               int64_t hazard_bytes) {
+                                               int32_t max_cols, int32_t max_width,
+                                               int32_t global_heads, int64_t hazard_bytes) {
   (void)global_heads;
   if (num_rows < 0 || layers <= 0 || kv_heads <= 0 || head_dim != 64 || page_size <= 0 ||
       max_cols < 0)
     return -1;
-  const int64_t one = hazard_per_layer(num_rows, kv_heads, max_cols, page_size);
+  const int width = (max_width > 0 && max_width < max_cols) ? max_width : max_cols;
+  const int64_t one = hazard_per_layer(num_rows, kv_heads, width, page_size);
   const int64_t hz = hazard_bytes < one ? one : hazard_bytes;
   return static_cast<int64_t>(boundary_layout(num_rows, layers, kv_heads, max_cols, hz).total);
 }
@@ -982,7 +1063,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
                            const int32_t* rows, const ce_row_params* params, int32_t num_rows,
                            const void* uniforms, int32_t uniform_dtype,
                            const float* global_scores, int32_t global_heads, int32_t live,
-                           int32_t max_cols, int32_t max_n, int32_t* result,
+                           int32_t max_cols, int32_t max_width, int32_t max_n, int32_t* result,
                            int32_t* freed_units, int64_t freed_stride, void* workspace,
                            int64_t workspace_bytes, int64_t hazard_bytes, int32_t* err,
                            void* stream) {
@@ -998,7 +1079,8 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
     return host::fail(CE_ERR_ARG, "uniform dtype must be f32 or f64");
   const int nw = (max_n + 31) / 32;
   if (sel_smem(nw) > 200 * 1024) return host::fail(CE_ERR_UNSUPPORTED, "max_n too large");
-  const int64_t one = hazard_per_layer(num_rows, kv_heads, max_cols, page_size);
+  const int width = (max_width > 0 && max_width < max_cols) ? max_width : max_cols;
+  const int64_t one = hazard_per_layer(num_rows, kv_heads, width, page_size);
   const int64_t hz = hazard_bytes < one ? one : hazard_bytes;
   const BLayout Lo = boundary_layout(num_rows, layers, kv_heads, max_cols, hz);
   if (workspace_bytes < static_cast<int64_t>(Lo.total))
@@ -1008,6 +1090,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
                   frontier, count, pos, pos_row_stride, pos_cap, scores, score_layer_stride,
                   score_head_stride, pool_units, layers, kv_heads, page_size, rows, params,
                   num_rows, max_cols, max_n);
+  p.max_width = width;
   p.k_layers = k_layers;
   p.v_layers = v_layers;
   p.head_offset = head_offset;
@@ -1048,7 +1131,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   const int nsm = host::sm_count();
   for (int l0 = 0; l0 < layers; l0 += group) {
     const int nl = std::min(group, layers - l0);
-    const int64_t items = static_cast<int64_t>(num_rows) * nl * kv_heads * max_cols;
+    const int64_t items = static_cast<int64_t>(num_rows) * nl * kv_heads * width;
     const int64_t want = (items * 32 + 255) / 256;
     const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 8LL * nsm)));
     bgather_kernel<<<blocks, 256, 0, st>>>(p, l0, nl);

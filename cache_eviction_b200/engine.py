@@ -170,7 +170,8 @@ class RaggedDecodeEngine:
             self.table, self.r2u, self.frontier, self.count, self.pos, self.scores, self.kptr,
             self.vptr, self.G, P, rows_t, params_t, max_cols, max_n, live, marks=self.marks,
             epoch=self.epoch, swa=swa, uniforms=uniforms, global_scores=gscores,
-            head_offset=self.head_offset, hazard_bytes=hazard_bytes, err=self.err)
+            head_offset=self.head_offset, hazard_bytes=hazard_bytes, err=self.err,
+            max_width=max(prm["budget"] for prm in params))
         end.record()
         res = result.cpu().numpy()   # one readback per boundary batch, as the reference syncs
         self.boundary_ms.append(start.elapsed_time(end))

@@ -161,7 +161,8 @@ def layer_pointers(tensors: Sequence[torch.Tensor], device) -> torch.Tensor:
 
 def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, kv_heads, page_size,
              rows, params, max_cols, max_n, live, marks=None, epoch=0, swa=None, uniforms=None,
-             global_scores=None, head_offset=0, freed=None, hazard_bytes=256 << 20, err=None):
+             global_scores=None, head_offset=0, freed=None, hazard_bytes=256 << 20, err=None,
+             max_width=0):
     """One eviction boundary for a batch of rows (runtime:415-507).
 
     Returns (result [R, 4] int32 device tensor, freed [R, max_cols] int32).
@@ -173,7 +174,7 @@ def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, k
     result = torch.zeros((max(R, 1), 4), dtype=torch.int32, device=dev)
     if freed is None:
         freed = torch.full((max(R, 1), max(max_cols, 1)), -1, dtype=torch.int32, device=dev)
-    need = lib.ce_boundary_workspace_bytes(R, L, kv_heads, 64, page_size, max_cols,
+    need = lib.ce_boundary_workspace_bytes(R, L, kv_heads, 64, page_size, max_cols, int(max_width),
                                            global_scores.shape[2] if global_scores is not None else 0,
                                            hazard_bytes)
     if need < 0:
@@ -189,11 +190,12 @@ def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, k
         kv_heads, 64, page_size, head_offset, _p(marks), int(epoch), _p(swa), _p(rows), _p(params),
         R, _p(uniforms), udt, _p(global_scores),
         global_scores.shape[2] if global_scores is not None else 0, 1 if live else 0, max_cols,
-        int(max_n), _p(result), _p(freed), freed.stride(0), _p(ws), ws.numel(), int(hazard_bytes),
+        int(max_width), int(max_n), _p(result), _p(freed), freed.stride(0), _p(ws), ws.numel(), int(hazard_bytes),
         _p(err), _stream(dev))
     capi.check(st, "ce_boundary")
     if R:
-        one = R * kv_heads * max_cols * 2 * page_size * 128
+        width = max_width if 0 < max_width < max_cols else max_cols
+        one = R * kv_heads * width * 2 * page_size * 128
         group = max(1, min(L, max(int(hazard_bytes), one) // max(one, 1)))
         _count(3 + 2 * ceil_div(L, group))
     return result, freed

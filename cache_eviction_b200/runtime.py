@@ -308,7 +308,7 @@ def _boundary(st, row, entry, n, cursor=None, allocator=None):
     result, leftover = kernels.boundary(
         st.table, st.req_to_token, st.frontier, st.count, st.pos, st.scores, kptr, vptr, G, page,
         rows, params, N, n_u + 1, live, marks=st.marks, epoch=st.epoch, swa=swa,
-        uniforms=uniforms, head_offset=st.head_offset, err=st.err)
+        uniforms=uniforms, head_offset=st.head_offset, err=st.err, max_width=budget)
     res = result[0].tolist()  # synchronises, as the reference does (runtime:474, 492)
     finished = time.perf_counter()
     status, before, after, nfreed = res

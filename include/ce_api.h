@@ -231,6 +231,8 @@ int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols,
  *           dense per-column scores of ALL KV heads (tensor-parallel ranks
  *           all-gather them); when NULL h2o_global sums the local heads
  *   max_cols >= count[row] + n - frontier[row] for every row
+ *   max_width >= every row's middle width (budget - protected; <= 0 means
+ *            max_cols): sizes the relocation scratch and the item space
  *   max_n    >= every row's n (positions are ranked in a max_n-bit bitmap)
  *   result  [num_rows, 4]: status (0 evicted, 1 nothing to do, 2 deferred,
  *           3 protected mismatch, 4 packing error, 5 sliding-window error,
@@ -241,8 +243,8 @@ int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols,
  * that fit it (at least one layer; query the minimum with layers = 1). */
 int64_t ce_boundary_workspace_bytes(int32_t num_rows, int32_t layers, int32_t kv_heads,
                                     int32_t head_dim, int32_t page_size,
-                                    int32_t max_cols, int32_t global_heads,
-                                    int64_t hazard_bytes);
+                                    int32_t max_cols, int32_t max_width,
+                                    int32_t global_heads, int64_t hazard_bytes);
 int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_width,
                 int32_t* req_to_unit, int64_t r2u_stride, int32_t r2u_width,
                 int32_t* frontier, int32_t* count,
@@ -256,7 +258,7 @@ int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_width,
                 const int32_t* rows, const ce_row_params* params, int32_t num_rows,
                 const void* uniforms, int32_t uniform_dtype,
                 const float* global_scores, int32_t global_heads,
-                int32_t live, int32_t max_cols, int32_t max_n,
+                int32_t live, int32_t max_cols, int32_t max_width, int32_t max_n,
                 int32_t* result, int32_t* freed_units, int64_t freed_stride,
                 void* workspace, int64_t workspace_bytes, int64_t hazard_bytes,
                 int32_t* err, void* stream);

@@ -34,8 +34,12 @@ def test_workspace_queries_are_host_only():
     from cache_eviction_b200 import capi
     lib = capi.load()
     assert lib.ce_choose_workspace_bytes(2, 16, 100) > 0
-    assert lib.ce_boundary_workspace_bytes(1, 2, 8, 64, 16, 100, 0, 0) > 0
-    assert lib.ce_boundary_workspace_bytes(1, 2, 8, 32, 16, 100, 0, 0) == -1  # head_dim 64 only
+    # the relocation scratch scales with the widest middle set, not the column count
+    wide = lib.ce_boundary_workspace_bytes(32, 1, 8, 64, 16, 4096, 0, 0, 0)
+    narrow = lib.ce_boundary_workspace_bytes(32, 1, 8, 64, 16, 4096, 256, 0, 0)
+    assert narrow < wide
+    assert lib.ce_boundary_workspace_bytes(1, 2, 8, 64, 16, 100, 0, 0, 0) > 0
+    assert lib.ce_boundary_workspace_bytes(1, 2, 8, 32, 16, 100, 0, 0, 0) == -1  # head_dim 64 only
 
 
 def test_row_params_layout_matches_header():

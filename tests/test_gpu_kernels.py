@@ -281,7 +281,7 @@ def _gpu_state(state, kl, vl):
 
 
 def _gpu_boundary(g, rows, params, max_cols, max_n, live, epoch, uniforms=None, swa=None,
-                  hazard_bytes=256 << 20, page=1):
+                  hazard_bytes=256 << 20, page=1, max_width=0):
     kern = K()
     err = kern.error_word(DEV)
     res, freed = kern.boundary(g["table"], g["r2u"], g["frontier"], g["count"], g["pos"], g["scores"],
@@ -289,7 +289,7 @@ def _gpu_boundary(g, rows, params, max_cols, max_n, live, epoch, uniforms=None, 
                                torch.tensor(rows, dtype=torch.int32, device=DEV),
                                kern.row_params(params, DEV), max_cols, max_n, live, marks=g["marks"],
                                epoch=epoch, uniforms=uniforms, swa=swa, hazard_bytes=hazard_bytes,
-                               err=err)
+                               err=err, max_width=max_width)
     torch.cuda.synchronize()
     return res.cpu().numpy(), freed.cpu().numpy(), int(err.item())
 
@@ -370,7 +370,7 @@ def test_boundary_paged_multirow_vs_oracle(policy):
         epoch += 1
         res_g, fr_g, err = _gpu_boundary(g, list(range(rows)), params, max_cols, n + 1, True, epoch,
                                          uniforms=None if uni is None else torch.from_numpy(uni).to(DEV),
-                                         page=page)
+                                         page=page, max_width=max(budgets), hazard_bytes=1)
         assert err == 0, hex(err)
         np.testing.assert_array_equal(res_g, res_c)
         for r in range(rows):
