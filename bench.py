@@ -44,6 +44,7 @@ SEQS_PER_GPU = 64
 TRAFFIC_BYTES_PER_RESIDENT_TOKEN = 2174.0
 BUDGETS = [2048, 4096, 8192, 16384, 32768]
 POLICY_MIX = ["full", "recent", "random", "h2o_global", "h2o_per_head"]
+SLEEP_CYCLES = 2_000_000   # ~1 ms spin ahead of a timed call
 
 
 def workload(n_seqs: int, seed: int = 2026):
@@ -290,6 +291,34 @@ def run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
     return B * e2e_steps / (e2e_ms * 1e-3)
 
 
+def run_no_score(args, specs, steps_total, world, rank, group, device, q, out, sinks, scale,
+                 after_layer, barrier, max_over_ranks):
+    """The device-resident pass again from a fresh state with H2O scoring off for
+    every row (mode NONE) and the same boundaries, so the resident KV matches the
+    scored pass step for step: the full-cache decode rate at the same resident
+    size, which the scored rate is compared against."""
+    import torch
+    from cache_eviction_b200 import capi
+    B = len(specs)
+    eng = build_engine(specs, steps_total, world, rank, group, device)
+    eng.mode.fill_(capi.CE_MODE_NONE)
+    for _ in range(args.warmup):
+        eng.step(q, out, sinks, scale, after_layer)
+    barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        eng.step(q, out, sinks, scale, after_layer)
+    e2.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(s2.elapsed_time(e2))
+    del eng
+    torch.cuda.empty_cache()
+    return B * args.steps / (ms * 1e-3)
+
+
 def evict_microbench(world, rank, device, reps=3):
     """one eviction step (select + compaction) over 32 rows x
     this rank's KV heads x 4096 pages (65,536-token contexts), fp32 scores
@@ -332,6 +361,9 @@ def evict_microbench(world, rank, device, reps=3):
                 epoch += 1
                 a = torch.cuda.Event(enable_timing=True)
                 e = torch.cuda.Event(enable_timing=True)
+                # Keep the GPU busy while the host prepares the call, so the
+                # events bracket device time only.
+                torch.cuda._sleep(SLEEP_CYCLES)
                 a.record()
                 res, _ = kernels.boundary(table, r2u, frontier, count, pos, scores, kptr, vptr, G, PAGE,
                                           rows, prm, N, N + 1, True, marks=marks, epoch=epoch,
@@ -342,6 +374,7 @@ def evict_microbench(world, rank, device, reps=3):
                 sc = sc.permute(1, 0, 2).contiguous()
                 a2 = torch.cuda.Event(enable_timing=True)
                 e2 = torch.cuda.Event(enable_timing=True)
+                torch.cuda._sleep(SLEEP_CYCLES)
                 a2.record()
                 kernels.choose(pos_fresh, uni.view(R, G, N) if pol == "random_2048" else sc, prm, 1, G,
                                max_n=N + 1, kept_stride=b)
@@ -480,6 +513,9 @@ def main():
         e2e_value = run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
                             scale, after_layer, barrier, max_over_ranks, e2e_steps)
 
+    no_score = run_no_score(args, specs, steps_total, world, rank, group, device, q, out, sinks,
+                            scale, after_layer, barrier, max_over_ranks)
+
     evict5 = None
     if not args.no_evict_bench:
         evict5 = evict_microbench(world, rank, device)
@@ -510,6 +546,10 @@ def main():
                   "boundary_ms_mean": statistics.mean(boundary_ms) if boundary_ms else None,
                   "boundary_rows": n_bound_rows},
         "resident_tokens_mean": statistics.mean(tokens_resident),
+        "no_score_same_resident": {"value": no_score, "unit": UNIT,
+                                   "scored_over_no_score": value / no_score,
+                                   "what": "same rows, steps and boundaries with H2O scoring off "
+                                           "(full-cache decode at the same resident KV)"},
         "evict_config5": evict5,
     }
     if rank == 0 and world == 1 and args.cpu_seconds > 0:

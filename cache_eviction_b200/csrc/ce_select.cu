@@ -260,7 +260,9 @@ __device__ void emit_sorted(const Cols& cols, int nw, uint32_t* bits, int* pre, 
 }
 
 // Register path for segments of up to REG_ITEMS * T columns.
-constexpr int REG_ITEMS = 16;
+// Eight columns per thread keep the register path at <= 64 registers, so two
+// 512-thread blocks fit on an SM and a 256-segment select runs in one wave.
+constexpr int REG_ITEMS = 8;
 
 __device__ __forceinline__ bool is_prot(int pos, const ce_row_params& q) {
   return pos < q.prefix || pos >= q.n - q.recent || (q.cursor >= 0 && pos >= q.cursor);
@@ -358,7 +360,7 @@ __device__ void choose_body(const ChooseParams& p, const Cols& cols, int np, int
       sh, p.err);
 }
 
-__global__ void __launch_bounds__(T) choose_seg_kernel(const ChooseParams p) {
+__global__ void __launch_bounds__(T, 2) choose_seg_kernel(const ChooseParams p) {
   extern __shared__ uint32_t dyn[];
   __shared__ Sh sh;
   const int segs = p.layers * p.heads;
@@ -570,7 +572,7 @@ __device__ void bsel_body(const BParams& p, const RowCtx& r, const Cols& cols, i
 }
 
 // Segment blocks: R*L*G of them, then R row blocks.
-__global__ void __launch_bounds__(T) bsel_kernel(const BParams p) {
+__global__ void __launch_bounds__(T, 2) bsel_kernel(const BParams p) {
   extern __shared__ uint32_t dyn[];
   __shared__ Sh sh;
   uint32_t* bitsm = dyn;
@@ -732,9 +734,32 @@ __device__ __forceinline__ uint8_t* unit_ptr(const uint64_t* layers, int l, int 
          (static_cast<int64_t>(unit) * G + g) * static_cast<int64_t>(P) * 128;
 }
 
-__device__ __forceinline__ void copy_block(uint8_t* dst, const uint8_t* src, int bytes, int lane) {
-  for (int o = lane * 16; o < bytes; o += 32 * 16)
-    *reinterpret_cast<uint4*>(dst + o) = *reinterpret_cast<const uint4*>(src + o);
+// Copy one head slice of K and of V (bytes each) with the warp: every lane
+// issues all of its loads (up to 4 x 16 B of K and of V) before its first
+// store, so a warp keeps a whole 2 KB + 2 KB page pair in flight.  Sources are
+// never written by the launch that reads them (hazard sources are staged by
+// the previous launch), so the loads take the non-coherent path.
+__device__ __forceinline__ void copy_pair(uint8_t* dk, uint8_t* dv, const uint8_t* sk, const uint8_t* sv,
+                                          int bytes, int lane) {
+  for (int o = lane * 16; o < bytes; o += 4 * 32 * 16) {
+    uint4 a[4], b[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int x = o + u * 32 * 16;
+      if (x < bytes) {
+        a[u] = __ldg(reinterpret_cast<const uint4*>(sk + x));
+        b[u] = __ldg(reinterpret_cast<const uint4*>(sv + x));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int x = o + u * 32 * 16;
+      if (x < bytes) {
+        *reinterpret_cast<uint4*>(dk + x) = a[u];
+        *reinterpret_cast<uint4*>(dv + x) = b[u];
+      }
+    }
+  }
 }
 
 __global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int l0, int nl) {
@@ -753,8 +778,8 @@ __global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int l0, i
       continue;
     }
     uint8_t* scr = p.hazard + item * 2 * bytes;
-    copy_block(scr, unit_ptr(p.k_layers, it.l, src, it.g, p.G, p.P), bytes, lane);
-    copy_block(scr + bytes, unit_ptr(p.v_layers, it.l, src, it.g, p.G, p.P), bytes, lane);
+    copy_pair(scr, scr + bytes, unit_ptr(p.k_layers, it.l, src, it.g, p.G, p.P),
+              unit_ptr(p.v_layers, it.l, src, it.g, p.G, p.P), bytes, lane);
   }
 }
 
@@ -780,8 +805,8 @@ __global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int l0, 
     const uint8_t* ks = hz ? p.hazard + item * 2 * bytes : unit_ptr(p.k_layers, it.l, src, it.g, p.G, p.P);
     const uint8_t* vs = hz ? p.hazard + item * 2 * bytes + bytes
                            : unit_ptr(p.v_layers, it.l, src, it.g, p.G, p.P);
-    copy_block(unit_ptr(p.k_layers, it.l, dst, it.g, p.G, p.P), ks, bytes, lane);
-    copy_block(unit_ptr(p.v_layers, it.l, dst, it.g, p.G, p.P), vs, bytes, lane);
+    copy_pair(unit_ptr(p.k_layers, it.l, dst, it.g, p.G, p.P), unit_ptr(p.v_layers, it.l, dst, it.g, p.G, p.P),
+              ks, vs, bytes, lane);
   }
 }
 

@@ -44,7 +44,8 @@ class RaggedDecodeEngine:
     def __init__(self, *, layers: int, q_heads: int, kv_heads: int, page_size: int,
                  pool_units: int, max_rows: int, r2u_width: int, pos_cap: int,
                  device="cuda", head_offset: int = 0, global_kv_heads: Optional[int] = None,
-                 process_group=None, alloc_pools: bool = True):
+                 process_group=None, alloc_pools: bool = True, boundary_rows: int = 8,
+                 hazard_bytes: int = 512 << 20):
         self.L, self.H, self.G, self.P = layers, q_heads, kv_heads, page_size
         self.units = pool_units
         self.device = torch.device(device)
@@ -78,6 +79,15 @@ class RaggedDecodeEngine:
         self.seq_lens_dev = torch.zeros(0, dtype=torch.int64, device=dev)
         self.free_units: list = []
         self.boundary_ms: list = []
+        # The boundary workspace is sized up front for batches of up to
+        # `boundary_rows` rows, so no device allocation falls inside the decode
+        # loop (a larger batch grows it once).
+        self.hazard_bytes = hazard_bytes
+        self.r2u_width = r2u_width
+        if alloc_pools:
+            kernels.reserve_boundary(dev, min(max_rows, boundary_rows), layers, kv_heads, page_size,
+                                     r2u_width, pos_cap,
+                                     self.global_G if process_group is not None else 0, hazard_bytes)
 
     # ------------------------------------------------------------- rows
     def add_row(self, row: int, cfg: Optional[EvictionConfig], n: int, last_boundary: int = 0,
@@ -124,11 +134,12 @@ class RaggedDecodeEngine:
         return out
 
     def run_boundaries(self, rows: list, cursors: Optional[dict] = None, live: bool = True,
-                       swa: Optional[torch.Tensor] = None, hazard_bytes: int = 512 << 20):
+                       swa: Optional[torch.Tensor] = None, hazard_bytes: Optional[int] = None):
         """One batched ce_boundary over `rows`; returns the per-row results (host)."""
         if not rows:
             return []
         P = self.P
+        hazard_bytes = self.hazard_bytes if hazard_bytes is None else hazard_bytes
         params, ncols = [], []
         for r in rows:
             row = self.rows[r]

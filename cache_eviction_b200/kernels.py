@@ -201,6 +201,16 @@ def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, k
     return result, freed
 
 
+def reserve_boundary(device, rows, layers, kv_heads, page_size, max_cols, max_width, global_heads,
+                     hazard_bytes):
+    """Allocate the ce_boundary workspace for the given batch bounds ahead of use."""
+    need = capi.load().ce_boundary_workspace_bytes(rows, layers, kv_heads, 64, page_size, max_cols,
+                                                   max_width, global_heads, hazard_bytes)
+    if need < 0:
+        raise capi.CeError("ce_boundary_workspace_bytes failed")
+    return WORKSPACES.get(torch.device(device), "boundary", need)
+
+
 def gather_row_scores(table, req_to_unit, frontier, count, scores, rows, params, max_cols, err=None):
     lib = capi.load()
     dev = table.device
