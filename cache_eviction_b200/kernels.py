@@ -131,6 +131,42 @@ def decode_attn_score(q, k_pool, v_pool, kv_indptr, kv_indices, kv_tokens, sm_sc
     return out
 
 
+def prefill_scores(q, k_pool, qo_indptr, kv_indptr, kv_indices, kv_tokens, sm_scale, page_size,
+                   max_q, max_tokens, sinks=None, mode_of_row=None, rows=None, scores=None,
+                   zero_new=True, err=None):
+    """Prefill / extend H2O scores of one layer (runtime:314-340) into `scores`.
+
+    q [total_q, H, 64] bf16; k_pool [units, G, page, 64] bf16; scores [G, units]
+    fp32; qo_indptr/kv_indptr/kv_indices/kv_tokens int32 as ce_prefill_scores
+    documents; max_q / max_tokens bound the chunk and list lengths (host ints).
+    """
+    lib = capi.load()
+    total_q, H, D = q.shape
+    G = k_pool.shape[1]
+    assert q.dtype == torch.bfloat16 and q.stride(2) == 1
+    assert k_pool.is_contiguous() and scores is not None and scores.dtype == torch.float32
+    assert scores.stride(1) == 1
+    for t in (qo_indptr, kv_indptr, kv_indices, kv_tokens):
+        assert t.dtype == torch.int32
+    dev = q.device
+    if sinks is not None and sinks.dtype != torch.float32:
+        sinks = sinks.float()
+    bs = int(kv_tokens.numel())
+    need = lib.ce_prefill_workspace_bytes(total_q, H)
+    if need < 0:
+        raise capi.CeError("ce_prefill_workspace_bytes failed")
+    ws = WORKSPACES.get(dev, "prefill", need)
+    st = lib.ce_prefill_scores(
+        _p(q), q.stride(0), q.stride(1), _p(k_pool), k_pool.shape[0], _p(qo_indptr), _p(kv_indptr),
+        _p(kv_indices), _p(kv_tokens), kv_indices.numel(), _p(sinks), _p(mode_of_row), _p(rows),
+        float(sm_scale), bs, H, G, D, page_size, total_q, int(max_q), int(max_tokens), _p(scores),
+        scores.stride(0), 1 if zero_new else 0, _p(ws), ws.numel(), _p(err), _stream(dev))
+    capi.check(st, "ce_prefill_scores")
+    if bs and max_q and mode_of_row is not None and total_q:
+        _count(2 if max_tokens else 1)
+    return scores
+
+
 def choose(pos, score, params: torch.Tensor, layers, heads, max_n, ncols=None, head_offset=0,
            kept_stride=None, err=None):
     """Kept columns [problems, segs, kept_stride] in ascending position (runtime:376-412)."""

@@ -176,23 +176,79 @@ def after_decode(backend, q, layer, forward_batch, sinks, out=None):
         return
     st = state(backend)
     if layer.layer_id == st.first_full:
-        st.scores.index_fill_(2, forward_batch.out_cache_loc.long() // st.page_size, 0.0)
+        st.scores.index_fill_(2, _new_units(st, forward_batch.out_cache_loc.long()), 0.0)
     _decode(backend, q, layer, forward_batch, sinks, None, zero_new=False)
 
 
+def _new_units(st, loc):
+    """Units that tokens at pool locations `loc` start (loc % page == 0); other
+    tokens map to unit 0, SGLang's padding slot, so the result keeps its shape
+    and needs no host sync."""
+    P = st.page_size
+    if P == 1:
+        return loc
+    return torch.where(loc % P == 0, loc // P, torch.zeros_like(loc))
+
+
 def after_extend(backend, q, layer, forward_batch, sinks):
-    """Prefill scores (runtime:277-311) for H2O rows of an extend batch."""
+    """Prefill scores (runtime:277-311) for H2O rows of an extend batch.
+
+    On the first full layer every unit that a new token starts is zeroed for
+    all layers (runtime:293-294); then ce_prefill_scores adds each head_sum /
+    head_max row's chunk probabilities over its resident prefix and the chunk
+    itself (_prefill_scores, runtime:327-340).  Replay and diagnostic entries
+    are not part of this path (their scoring is the reference's offline
+    tooling) and raise.
+    """
     if _layer_is_sliding(layer):
         return
     st = state(backend)
-    entries = [st.entries.get(r) for r in forward_batch.req_pool_indices.tolist()]
+    rows = forward_batch.req_pool_indices.tolist()
+    entries = [st.entries.get(r) for r in rows]
     if not any(entries):
         return
+    loc = forward_batch.out_cache_loc.long()
     if layer.layer_id == st.first_full:
-        st.scores.index_fill_(2, forward_batch.out_cache_loc.long() // st.page_size, 0.0)
-    if any(e is not None and not e["error"] and e["mode"] in (1, 2) for e in entries):
-        raise NotImplementedError("prefill scoring for head_sum/head_max rows needs the prefill "
-                                  "score kernel, which this build does not have yet")
+        st.scores.index_fill_(2, _new_units(st, loc), 0.0)
+    scored = [i for i, e in enumerate(entries) if e is not None and not e["error"] and e["mode"] in (1, 2)]
+    if not scored:
+        return
+    if any(entries[i]["kind"] != "live" for i in scored):
+        raise NotImplementedError("replay/diagnostic entries are outside the decode-time eviction path")
+    meta = backend.forward_metadata
+    heads, dim = layer.tp_q_head_num, layer.qk_head_dim
+    queries = q.view(-1, heads, dim)
+    qo, kv = meta.qo_indptr.tolist(), meta.kv_indptr.tolist()
+    P = st.page_size
+    starts = forward_batch.extend_prefix_lens_cpu
+    parts, indptr, tokens, modes = [], [0], [], []
+    for i, e in enumerate(entries):
+        nnew = qo[i + 1] - qo[i]
+        if i not in scored:
+            tokens.append(nnew)         # an empty list: skipped by mode 0
+            modes.append(0)
+            indptr.append(indptr[-1])
+            continue
+        start = int(starts[i])
+        resident = e["count"] * P + start - e["frontier"] * P   # prefix tokens in the CSR
+        prefix = meta.kv_indices[kv[i]:kv[i + 1]].to(torch.int32)
+        new = loc[qo[i]:qo[i + 1]]
+        if P > 1:
+            first = (torch.arange(start, start + nnew, device=new.device) % P) == 0
+            new = new[first] // P
+        parts += [prefix, new.to(torch.int32)]
+        indptr.append(indptr[-1] + prefix.numel() + new.numel())
+        tokens.append(resident + nnew)
+        modes.append(e["mode"])
+    dev = queries.device
+    kpool, _ = st.pools(layer.layer_id)
+    kernels.prefill_scores(
+        queries, kpool, meta.qo_indptr[: len(rows) + 1].to(torch.int32),
+        torch.tensor(indptr, dtype=torch.int32, device=dev), torch.cat(parts),
+        torch.tensor(tokens, dtype=torch.int32, device=dev), layer.scaling, P,
+        max_q=max(qo[i + 1] - qo[i] for i in range(len(rows))), max_tokens=max(tokens),
+        sinks=sinks, mode_of_row=torch.tensor(modes, dtype=torch.int32, device=dev),
+        scores=st.scores[st.index[layer.layer_id]], zero_new=False, err=st.err)
 
 
 # ------------------------------------------------------------- selection

@@ -187,6 +187,53 @@ int ce_decode_attn_score_static(const void* q, int64_t q_sb, int64_t q_sh,
                                 float* lse_out, int32_t score_flags,
                                 int32_t* err, void* stream);
 
+/* ---- K5: prefill / extend H2O scores --------------------------------------
+ * Replaces the scoring in gstar_evict.after_extend (runtime:277-311):
+ * _prefill_scores with _probabilities (runtime:314-340), for a ragged batch
+ * of extend chunks of one layer.
+ *   q       [total_q, H, 64] bf16 (strides q_st, q_sh in elements, multiples
+ *           of 8; last dim dense); entry b's chunk is rows
+ *           qo_indptr[b] .. qo_indptr[b+1]  (nq_b queries)
+ *   k_pool  [pool_units, G, page_size, 64] bf16 of this layer, dense
+ *   kv_indptr/kv_indices/kv_tokens  entry b's key list: units
+ *           kv_indices[kv_indptr[b] ..] holding kv_tokens[b] tokens, the
+ *           resident prefix then the chunk's own tokens (the reference's
+ *           prefix ++ new slots, runtime:330); kv_tokens[b] >= nq_b and the
+ *           list has at least ceil(kv_tokens[b] / page_size) entries below
+ *           kv_capacity
+ *   mask    list token t is visible to chunk query i iff
+ *           t <= kv_tokens[b] - nq_b + i  (key_pos > query_pos masked,
+ *           runtime:334-336)
+ *   sinks   [H] fp32 natural-log sink logits, or NULL
+ *   mode_of_row, rows  as for ce_decode_attn_score (rows NULL: mode_of_row
+ *           is indexed by b); entries whose mode is not SUM/MAX are skipped
+ *   scores  [G, pool_units] fp32 of this layer (stride score_sg): per unit
+ *           += sum over its tokens of sum over the chunk's queries of
+ *           (sum (SUM) or max (MAX) over the group's query heads of p),
+ *           p = exp(scale*q.k - logaddexp(logsumexp(visible logits), sink));
+ *           zero_new 1: a unit whose first token is one of the chunk's is
+ *           written instead of accumulated (the reference zeroes new slots
+ *           first, runtime:293-294)
+ *   total_q  rows of q (workspace size); max_q, max_tokens  host bounds on
+ *           nq_b and kv_tokens[b] (grid sizes); an entry above either, or
+ *           with ranges outside total_q / kv_capacity, flags CE_EW_SHAPE
+ *           and is skipped
+ * Supported: head_dim 64, H == 8*G, page_size dividing 64.  No scratch
+ * beyond the workspace ([total_q, H] fp32 row normalizers). */
+int64_t ce_prefill_workspace_bytes(int32_t total_q, int32_t num_q_heads);
+int ce_prefill_scores(const void* q, int64_t q_st, int64_t q_sh,
+                      const void* k_pool, int64_t pool_units,
+                      const int32_t* qo_indptr, const int32_t* kv_indptr,
+                      const int32_t* kv_indices, const int32_t* kv_tokens,
+                      int64_t kv_capacity, const float* sinks,
+                      const int32_t* mode_of_row, const int64_t* rows,
+                      float sm_scale, int32_t bs, int32_t num_q_heads,
+                      int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                      int32_t total_q, int32_t max_q, int32_t max_tokens,
+                      float* scores, int64_t score_sg, int32_t zero_new,
+                      void* workspace, int64_t workspace_bytes,
+                      int32_t* err, void* stream);
+
 /* ---- K2: ragged per-head selection ---------------------------------------
  * Replaces gstar_evict.choose + _scores + reservoir_scores (runtime:358-412)
  * for `problems` independent boundaries, each over `segs` = layers*heads

@@ -148,6 +148,75 @@ typedef struct {
 
 /* Descending key, ties to the newer (larger) position: the reference's
  * stable argsort over a newest-first pre-order.  NaN sorts above everything. */
+/* Prefill / extend scores: _prefill_scores with _probabilities
+ * (runtime:314-340).  Entry b's chunk q[qo_indptr[b] .. qo_indptr[b+1])
+ * attends to its list of tokens[b] tokens (units indices[indptr[b] ..], page
+ * P); list token t is visible to chunk query i when t <= tokens[b] - nq + i
+ * (runtime:334-336).  p = exp(s - logaddexp(logsumexp(s), sink_h)) in
+ * double; per token: sum over queries of (sum over the group's heads (mode 1)
+ * or max (mode 2)); per unit: sum over its tokens, added to scores[g, unit]
+ * (or written, for a unit whose first token is in the chunk when zero_new). */
+void or_prefill(const uint16_t* q, int64_t q_st, int64_t q_sh, const uint16_t* kpool,
+                const int32_t* qo_indptr, const int32_t* indptr, const int32_t* indices,
+                const int32_t* tokens, const float* sinks, const int32_t* modes, float scale,
+                int bs, int H, int G, int D, int P, float* scores, int64_t score_sg,
+                int zero_new) {
+  const int grp = H / G;
+#pragma omp parallel for schedule(dynamic) collapse(2)
+  for (int b = 0; b < bs; ++b) {
+    for (int g = 0; g < G; ++g) {
+      const int mode = modes ? modes[b] : 0;
+      if (mode != 1 && mode != 2) continue;
+      const int q0 = qo_indptr[b], nq = qo_indptr[b + 1] - q0, ntok = tokens[b];
+      const int prefix = ntok - nq;
+      if (nq <= 0 || prefix < 0) continue;
+      double* contrib = (double*)calloc((size_t)ntok, sizeof(double));
+      double* s = (double*)malloc(sizeof(double) * (size_t)ntok * grp);
+      for (int i = 0; i < nq; ++i) {
+        const int vis = prefix + i + 1; /* tokens [0, vis) */
+        for (int r = 0; r < grp; ++r) {
+          const int h = g * grp + r;
+          const uint16_t* qh = q + (int64_t)(q0 + i) * q_st + (int64_t)h * q_sh;
+          double m = -INFINITY;
+          for (int t = 0; t < vis; ++t) {
+            const int unit = indices[indptr[b] + t / P];
+            const uint16_t* kr = kpool + (((int64_t)unit * G + g) * P + t % P) * D;
+            double acc = 0.0;
+            for (int d = 0; d < D; ++d) acc += (double)bf16f(qh[d]) * (double)bf16f(kr[d]);
+            s[(int64_t)r * ntok + t] = acc * (double)scale;
+            if (s[(int64_t)r * ntok + t] > m) m = s[(int64_t)r * ntok + t];
+          }
+          double mm = m;
+          if (sinks && (double)sinks[h] > mm) mm = (double)sinks[h];
+          double den = sinks ? exp((double)sinks[h] - mm) : 0.0;
+          for (int t = 0; t < vis; ++t) den += exp(s[(int64_t)r * ntok + t] - mm);
+          const double norm = mm + log(den);
+          for (int t = 0; t < vis; ++t) s[(int64_t)r * ntok + t] = exp(s[(int64_t)r * ntok + t] - norm);
+        }
+        for (int t = 0; t < vis; ++t) {
+          double agg = 0.0;
+          for (int r = 0; r < grp; ++r) {
+            const double pt = s[(int64_t)r * ntok + t];
+            if (mode == 1) agg += pt;
+            else if (pt > agg) agg = pt;
+          }
+          contrib[t] += agg;
+        }
+      }
+      const int npages = (ntok + P - 1) / P;
+      for (int j = 0; j < npages; ++j) {
+        double c = 0.0;
+        for (int t = j * P; t < (j + 1) * P && t < ntok; ++t) c += contrib[t];
+        const int unit = indices[indptr[b] + j];
+        float* sp = scores + (int64_t)g * score_sg + unit;
+        *sp = (zero_new && j * P >= prefix) ? (float)c : (float)((double)*sp + c);
+      }
+      free(s);
+      free(contrib);
+    }
+  }
+}
+
 static int cmp_item(const void* a, const void* b) {
   const or_item* x = (const or_item*)a;
   const or_item* y = (const or_item*)b;

@@ -49,8 +49,7 @@ _lib = None
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:
-        if not LIB.exists():
-            build()
+        build()  # no-op when the library is newer than its source
         _lib = C.CDLL(str(LIB))
         _lib.or_reservoir53.restype = C.c_uint64
         _lib.or_reservoir53.argtypes = [C.c_uint64] * 4
@@ -139,6 +138,30 @@ def decode(q_bits, k_bits, v_bits, indptr, indices, tokens, sinks, modes, scale,
                     C.c_int64(scores.shape[1] if scores is not None else 0),
                     C.c_int(1 if zero_new else 0), _p(out), _p(lse))
     return out, lse
+
+
+def prefill(q_bits, k_bits, qo_indptr, indptr, indices, tokens, sinks, modes, scale, page,
+            scores, zero_new=True):
+    """Prefill / extend H2O scores in float64 (runtime:314-340).
+
+    q_bits [total_q, H, D] uint16; k_bits [units, G, P, D] uint16; scores
+    [G, units] float32 updated in place (see or_prefill)."""
+    q_bits = np.ascontiguousarray(q_bits, np.uint16)
+    k_bits = np.ascontiguousarray(k_bits, np.uint16)
+    total_q, H, D = q_bits.shape
+    units, G, P, D2 = k_bits.shape
+    assert D == D2 and P == page and scores.dtype == np.float32 and scores.flags.c_contiguous
+    qo_indptr = np.ascontiguousarray(qo_indptr, np.int32)
+    indptr = np.ascontiguousarray(indptr, np.int32)
+    indices = np.ascontiguousarray(indices, np.int32)
+    tokens = np.ascontiguousarray(tokens, np.int32)
+    modes = np.ascontiguousarray(modes, np.int32)
+    sinks = None if sinks is None else np.ascontiguousarray(sinks, np.float32)
+    lib().or_prefill(_p(q_bits), C.c_int64(H * D), C.c_int64(D), _p(k_bits), _p(qo_indptr),
+                     _p(indptr), _p(indices), _p(tokens), _p(sinks), _p(modes), C.c_float(scale),
+                     C.c_int(len(tokens)), C.c_int(H), C.c_int(G), C.c_int(D), C.c_int(P),
+                     _p(scores), C.c_int64(scores.shape[1]), C.c_int(1 if zero_new else 0))
+    return scores
 
 
 def choose(pos, score, params, layers, heads, ncols=None, head_offset=0, kept_stride=None,

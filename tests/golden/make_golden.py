@@ -184,6 +184,25 @@ def gen_decode(rt):
     np.savez_compressed(HERE / "decode.npz", **out)
 
 
+def gen_prefill(rt):
+    """_prefill_scores (runtime:327-340) on each entry of the prefill scenario,
+    from zero scores, for head_sum (mode 1) and head_max (mode 2)."""
+    d = sc.prefill_setup()
+    keys = bf16_tensor(d["keys"])
+    q = bf16_tensor(d["q"])
+    sinks = bf16_tensor(d["sinks"])
+    layer = SimpleNamespace(tp_q_head_num=sc.H, tp_k_head_num=sc.G, scaling=d["scale"])
+    out = {}
+    for mode in (1, 2):
+        for i, (prefix, nq) in enumerate(sc.PREFILL_ENTRIES):
+            st = SimpleNamespace(scores=torch.zeros((1, sc.G, d["slots"]), dtype=torch.float32))
+            lst = torch.from_numpy(d["lists"][i]).long()
+            chunk = q[d["qo_indptr"][i]:d["qo_indptr"][i + 1]]
+            rt._prefill_scores(st, 0, mode, layer, chunk, keys, sinks, lst[:prefix], lst[prefix:])
+            out[f"mode{mode}_entry{i}"] = st.scores[0][:, lst].numpy()  # [G, prefix + nq]
+    np.savez_compressed(HERE / "prefill.npz", **out)
+
+
 def main():
     root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
     rt, core = load_reference(root)
@@ -191,6 +210,7 @@ def main():
     gen_reservoir(rt, core)
     gen_boundaries(rt, core)
     gen_decode(rt)
+    gen_prefill(rt)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

@@ -150,3 +150,29 @@ def decode_setup(seed: int = 5):
     indptr = np.concatenate([[0], np.cumsum(DECODE_LENGTHS)]).astype(np.int32)
     return dict(keys=keys, values=values, q=q, sinks=sinks, perm=perm, indptr=indptr,
                 scale=0.125, slots=slots)
+
+
+# -------------------------------------------------------------- prefill scenario
+# (prefix tokens, chunk queries) per entry: a chunk after a prefix, a fresh
+# prompt, and a one-query chunk.
+PREFILL_ENTRIES = ((150, 70), (0, 90), (333, 1))
+
+
+def prefill_setup(seed: int = 11):
+    """Extend chunks over scattered token slots, scored as _prefill_scores
+    does (runtime:327-340): each entry's key list is its prefix slots followed
+    by its chunk's new slots."""
+    rng = np.random.default_rng(seed)
+    slots = 1200
+    keys = bf16_bits(rng.standard_normal((slots, G, D), dtype=np.float32))
+    total_q = sum(nq for _, nq in PREFILL_ENTRIES)
+    q = bf16_bits(rng.standard_normal((total_q, H, D), dtype=np.float32))
+    sinks = bf16_bits(rng.standard_normal(H, dtype=np.float32))
+    perm = rng.permutation(slots - 1) + 1
+    lists, k = [], 0
+    for prefix, nq in PREFILL_ENTRIES:
+        lists.append(perm[k:k + prefix + nq].astype(np.int32))
+        k += prefix + nq
+    qo_indptr = np.concatenate([[0], np.cumsum([nq for _, nq in PREFILL_ENTRIES])]).astype(np.int32)
+    return dict(keys=keys, q=q, sinks=sinks, lists=lists, qo_indptr=qo_indptr, scale=0.125,
+                slots=slots)

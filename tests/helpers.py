@@ -60,3 +60,33 @@ def paged(keys_tok: np.ndarray, slot_lists, page: int):
             pool[us[t // page], :, t % page, :] = keys_tok[slot]
         out.append(us.astype(np.int32))
     return pool, out
+
+
+def prefill_inputs(page):
+    """The prefill scenario as pools/lists at `page` tokens per unit."""
+    d = sc.prefill_setup()
+    lists = d["lists"]
+    if page == 1:
+        kpool = d["keys"].reshape(-1, sc.G, 1, sc.D)
+        units = lists
+    else:
+        kpool, units = paged(d["keys"], lists, page)
+    indptr = np.concatenate([[0], np.cumsum([len(u) for u in units])]).astype(np.int32)
+    tokens = np.array([p + n for p, n in sc.PREFILL_ENTRIES], np.int32)
+    return d, kpool, units, indptr, np.concatenate(units).astype(np.int32), tokens
+
+
+def prefill_want(z, mode, page, units, init):
+    """Expected [G, units] scores: the reference's per-token scores summed per
+    page, added to `init` except on units that start inside the chunk."""
+    want = init.copy()
+    for i, (prefix, nq) in enumerate(sc.PREFILL_ENTRIES):
+        tok = z[f"mode{mode}_entry{i}"]  # [G, prefix + nq]
+        ntok = prefix + nq
+        pad = np.zeros((sc.G, len(units[i]) * page), np.float64)
+        pad[:, :ntok] = tok
+        per_unit = pad.reshape(sc.G, -1, page).sum(-1)
+        for j, u in enumerate(units[i]):
+            base = 0.0 if j * page >= prefix else want[:, u]
+            want[:, u] = base + per_unit[:, j]
+    return want

@@ -23,6 +23,16 @@ def test_library_exports_every_declared_symbol():
     assert set(names) == set(capi.SIGNATURES), set(names) ^ set(capi.SIGNATURES)
 
 
+def test_binding_argument_counts_match_header():
+    from cache_eviction_b200 import capi
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "ce_api.h").read_text(), flags=re.S)
+    for name, (_, args) in capi.SIGNATURES.items():
+        m = re.search(r"\b" + name + r"\s*\(([^)]*)\)\s*;", text)
+        assert m, name
+        params = [a for a in m.group(1).split(",") if a.strip() and a.strip() != "void"]
+        assert len(params) == len(args), (name, len(params), len(args))
+
+
 def test_version_and_status_strings_without_gpu():
     from cache_eviction_b200 import capi
     lib = capi.load()
@@ -34,6 +44,8 @@ def test_workspace_queries_are_host_only():
     from cache_eviction_b200 import capi
     lib = capi.load()
     assert lib.ce_choose_workspace_bytes(2, 16, 100) > 0
+    assert lib.ce_prefill_workspace_bytes(2048, 64) >= 2048 * 64 * 4
+    assert lib.ce_prefill_workspace_bytes(-1, 64) == -1
     # the relocation scratch scales with the widest middle set, not the column count
     wide = lib.ce_boundary_workspace_bytes(32, 1, 8, 64, 16, 4096, 0, 0, 0)
     narrow = lib.ce_boundary_workspace_bytes(32, 1, 8, 64, 16, 4096, 256, 0, 0)

@@ -289,3 +289,60 @@ def test_on_decode_runs_due_boundary_and_frees(_setup):
     assert len(e["events"]) == 1
     ge.release(req)
     assert 0 not in st.entries
+
+
+def test_after_extend_scores_h2o_rows(_setup):
+    """after_extend (runtime:277-311): new slots zeroed on every full layer,
+    then each head_sum / head_max row adds its chunk's exact probabilities
+    over prefix ++ chunk with the causal mask and sinks (_probabilities,
+    runtime:314-324, in plain torch here)."""
+    ge = _setup
+    b = backend()
+    st = ge.state(b)
+    heads, kv_heads, dim = 64, 8, 64
+    # row: (policy or None, prefix tokens, chunk tokens)
+    spec = [("head_sum_2048", 300, 120), (None, 50, 17), ("head_max_sum_2048", 0, 64),
+            ("random_2048", 10, 5)]
+    for r, (name, _, _) in enumerate(spec):
+        if name is not None:
+            st.entries[r] = entry(ge, name, 1024, 256, 256, 7)
+            st.mode[r] = st.entries[r]["mode"]
+    perm = (torch.randperm(19999, device="cuda") + 1).long()
+    prefixes, news, k = [], [], 0
+    for _, p, n in spec:
+        prefixes.append(perm[k:k + p])
+        news.append(perm[k + p:k + p + n])
+        k += p + n
+    kv_indptr = torch.tensor([0] + list(np.cumsum([p for _, p, _ in spec])), dtype=torch.int32, device="cuda")
+    qo_indptr = torch.tensor([0] + list(np.cumsum([n for _, _, n in spec])), dtype=torch.int32, device="cuda")
+    b.forward_metadata = SimpleNamespace(kv_indptr=kv_indptr, kv_indices=torch.cat(prefixes),
+                                         qo_indptr=qo_indptr)
+    total = int(qo_indptr[-1])
+    q = torch.randn((total, heads, dim), device="cuda").to(torch.bfloat16)
+    sinks = torch.randn(heads, device="cuda").to(torch.bfloat16)
+    batch = SimpleNamespace(out_cache_loc=torch.cat(news), req_pool_indices=torch.arange(4, device="cuda"),
+                            extend_prefix_lens_cpu=[p for _, p, _ in spec])
+    st.scores.fill_(5.0)
+    expected = torch.full_like(st.scores, 5.0)
+    expected[:, :, batch.out_cache_loc] = 0.0
+    for layer_id in FULL:
+        layer = SimpleNamespace(sliding_window_size=-1, tp_q_head_num=heads, tp_k_head_num=kv_heads,
+                                qk_head_dim=dim, layer_id=layer_id, scaling=0.125)
+        ge.after_extend(b, q.reshape(total, -1), layer, batch, sinks)
+        keys = b.token_to_kv_pool.get_key_buffer(layer_id)
+        for r, (name, p, n) in enumerate(spec):
+            mode = st.entries[r]["mode"] if r in st.entries else 0
+            if mode not in (1, 2):
+                continue
+            slots = torch.cat((prefixes[r], news[r]))
+            kk = keys[slots].float().repeat_interleave(heads // kv_heads, 1)     # [T, H, D]
+            qq = q[int(qo_indptr[r]):int(qo_indptr[r + 1])].float()             # [n, H, D]
+            logits = torch.einsum("qhd,khd->hqk", qq, kk) * 0.125
+            causal = torch.arange(p + n, device="cuda")[None, :] > (p + torch.arange(n, device="cuda"))[:, None]
+            logits = logits.masked_fill(causal[None], -torch.inf)
+            sink = sinks.float()[:, None, None].expand(heads, n, 1)
+            prob = torch.softmax(torch.cat((logits, sink), -1), -1)[..., :-1].view(kv_heads, 8, n, -1)
+            red = (prob.sum(1) if mode == 1 else prob.amax(1)).sum(1)             # [G, T]
+            expected[FULL.index(layer_id)][:, slots] += red
+    torch.testing.assert_close(st.scores, expected, rtol=1e-3, atol=1e-5)
+    assert int(st.err.item()) == 0

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 from golden import scenarios as sc
-from helpers import boundary_row, boundary_state, paged, sha16, sha_bytes
+from helpers import boundary_row, boundary_state, paged, prefill_inputs, prefill_want, sha16, sha_bytes
 from oracle import oracle
 
 GOLD = Path(__file__).resolve().parent / "golden"
@@ -118,6 +118,19 @@ def test_decode_matches_reference(page, mode):
             want = pad.reshape(sc.G, npg, page).sum(-1)
             got = scores[:, units[i]]
         np.testing.assert_allclose(got, want, rtol=2e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("page", [1, 16])
+@pytest.mark.parametrize("mode", [1, 2])
+def test_prefill_matches_reference(page, mode):
+    z = np.load(GOLD / "prefill.npz")
+    d, kpool, units, indptr, indices, tokens = prefill_inputs(page)
+    init = np.random.default_rng(3).random((sc.G, kpool.shape[0])).astype(np.float32)
+    scores = init.copy()
+    oracle.prefill(d["q"], kpool, d["qo_indptr"], indptr, indices, tokens, sc.bits_to_f32(d["sinks"]),
+                   np.full(len(tokens), mode, np.int32), d["scale"], page, scores, zero_new=True)
+    want = prefill_want(z, mode, page, units, init.astype(np.float64))
+    np.testing.assert_allclose(scores, want, rtol=2e-5, atol=1e-6)
 
 
 def test_fill_reference_golden():
