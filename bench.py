@@ -319,6 +319,75 @@ def run_no_score(args, specs, steps_total, world, rank, group, device, q, out, s
     return B * args.steps / (ms * 1e-3)
 
 
+PREFILL_CHUNK = 2048
+PREFILL_PREFIXES = (0, 8192, 26624)   # resident tokens before a chunk; 26,624 + 2,048 = config 4's cache
+
+
+def prefill_microbench(world, rank, device, reps=5, cpu=False):
+    """one 2,048-token prefill chunk of one layer scored by
+    ce_prefill_scores against a resident prefix of 0 / 8,192 / 26,624 tokens
+    (16-token pages, this rank's KV heads, no eviction inside the chunk).
+    Algorithmic work per call: two Q.K^T passes over the visible (query, key)
+    pairs, 4 * 64 * H * pairs FLOP, and one exp2 per pair and query head in
+    each pass.  Device time by CUDA events around the call (the GPU is kept
+    busy while the host prepares it)."""
+    import torch
+    from cache_eviction_b200 import capi, kernels, tp
+    G, H, _ = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    out = {}
+    gen = torch.Generator(device=device).manual_seed(77)
+    nq = PREFILL_CHUNK
+    q = torch.randn((nq, H, D), generator=gen, device=device).to(torch.bfloat16)
+    sinks = torch.randn(H, generator=gen, device=device)
+    for prefix in PREFILL_PREFIXES:
+        ntok = prefix + nq
+        units = ntok // PAGE
+        kpool = torch.randn((units + 1, G, PAGE, D), generator=gen, device=device).to(torch.bfloat16)
+        idx = (torch.randperm(units, generator=gen, device=device) + 1).int()
+        scores = torch.zeros((G, units + 1), dtype=torch.float32, device=device)
+        meta = [torch.tensor(v, dtype=torch.int32, device=device) for v in ([0, nq], [0, units], [ntok])]
+        pairs = nq * prefix + nq * (nq + 1) // 2
+        for mode in (capi.CE_MODE_SUM, capi.CE_MODE_MAX):
+            mo = torch.tensor([mode], dtype=torch.int32, device=device)
+            ts = []
+            for it in range(reps + 1):
+                a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda._sleep(SLEEP_CYCLES)
+                a.record()
+                kernels.prefill_scores(q, kpool, meta[0], meta[1], idx, meta[2], D ** -0.5, PAGE, nq, ntok,
+                                       sinks=sinks, mode_of_row=mo, scores=scores, zero_new=True)
+                e.record()
+                torch.cuda.synchronize()
+                if it:
+                    ts.append(a.elapsed_time(e) * 1e3)
+            us = statistics.median(ts)
+            out[f"prefix{prefix}_{'sum' if mode == capi.CE_MODE_SUM else 'max'}"] = {
+                "us": us, "tflops": 4 * D * H * pairs / (us * 1e-6) / 1e12,
+                "gexp2_per_s": 2 * H * pairs / (us * 1e-6) / 1e9, "visible_pairs": pairs}
+        del kpool, scores
+    if cpu:
+        from oracle import oracle
+        import numpy as np
+        rng = np.random.default_rng(3)
+        nq_s, prefix = 8, PREFILL_PREFIXES[-1]
+        ntok = prefix + nq_s
+        units = -(-ntok // PAGE)
+        kb = rng.integers(0, 1 << 16, (units + 1, G, PAGE, D), dtype=np.uint16) & 0xBFFF
+        qb = rng.integers(0, 1 << 16, (nq_s, H, D), dtype=np.uint16) & 0xBFFF
+        sc = np.zeros((G, units + 1), np.float32)
+        t0 = time.perf_counter()
+        oracle.prefill(qb, kb, np.array([0, nq_s]), np.array([0, units]), np.arange(1, units + 1),
+                       np.array([ntok]), None, np.array([1]), D ** -0.5, PAGE, sc)
+        dt = time.perf_counter() - t0
+        pairs_s = nq_s * prefix + nq_s * (nq_s + 1) // 2
+        pairs = nq * prefix + nq * (nq + 1) // 2
+        out["cpu_baseline"] = {"us": dt * 1e6 * pairs / pairs_s, "cores": oracle.threads(),
+                               "kind": "port",
+                               "sample": f"oracle prefill scores of {nq_s} queries over {prefix} prefix "
+                                         f"tokens, scaled to the {nq}-query chunk by visible pairs"}
+    return out
+
+
 def evict_microbench(world, rank, device, reps=3):
     """one eviction step (select + compaction) over 32 rows x
     this rank's KV heads x 4096 pages (65,536-token contexts), fp32 scores
@@ -513,6 +582,7 @@ def main():
         e2e_value = run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
                             scale, after_layer, barrier, max_over_ranks, e2e_steps)
 
+    prefill4 = prefill_microbench(world, rank, device, cpu=(rank == 0 and args.cpu_seconds > 0))
     no_score = run_no_score(args, specs, steps_total, world, rank, group, device, q, out, sinks,
                             scale, after_layer, barrier, max_over_ranks)
 
@@ -551,6 +621,7 @@ def main():
                                    "what": "same rows, steps and boundaries with H2O scoring off "
                                            "(full-cache decode at the same resident KV)"},
         "evict_config5": evict5,
+        "prefill_config4": prefill4,
     }
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         from oracle import oracle

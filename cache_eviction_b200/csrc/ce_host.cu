@@ -66,29 +66,43 @@ bool set_smem_attr(const void* func, int bytes) {
   return true;
 }
 
+static bool encoder() {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return false;
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  return true;
+}
+
+bool encode_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                const uint64_t* dims, const uint64_t* strides, const uint32_t* box, bool swizzle128) {
+  if (rank < 1 || rank > 5 || !encoder()) return false;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) st[i] = strides[i];
+  CUresult r = g_encode(map, dtype, rank, const_cast<void*>(base), d, st, b, e,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool encode_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint32_t cols,
                      uint32_t box_rows) {
-  {
-    std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_encode) {
-      void* fn = nullptr;
-      cudaDriverEntryPointQueryResult q;
-      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
-              cudaSuccess ||
-          q != cudaDriverEntryPointSuccess || !fn)
-        return false;
-      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
-    }
-  }
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
-  cuuint32_t box[2] = {cols, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  const uint64_t dims[2] = {cols, rows};
+  const uint64_t strides[1] = {static_cast<uint64_t>(cols) * 2};
+  const uint32_t box[2] = {cols, box_rows};
+  return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, true);
 }
 
 }  // namespace host

@@ -26,6 +26,12 @@ bool set_smem(F* func, int bytes) {
   return set_smem_attr(reinterpret_cast<const void*>(func), bytes);
 }
 
+// Tiled tensor map of `rank` dims (innermost first): dims, byte strides of
+// dims 1..rank-1, box sizes; element strides 1, zero fill out of bounds,
+// 128-byte swizzle or none.
+bool encode_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                const uint64_t* dims, const uint64_t* strides, const uint32_t* box, bool swizzle128);
+
 // 2D bf16 tensor map over `rows` rows of `cols` elements (dense), box
 // {cols, box_rows}, 128-byte swizzle, zero fill out of bounds.
 bool encode_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint32_t cols,

@@ -14,22 +14,29 @@
 // At page granularity a unit's score is the sum over its tokens, which is the
 // reference's token-slot score summed over the page.
 //
-// The work is two tensor-core passes over S = Q K^T per (batch entry, KV head)
-// with mma.sync m16n8k16 (bf16 in, fp32 accumulate); rows of S are
-// (query, head-in-group) pairs so the 8 query heads that share a KV head share
-// every K fragment:
-//   lse_kernel     CTA = 32 queries x 8 heads (256 rows), K streamed in
-//                  64-key tiles through a cp.async double buffer; online
-//                  log2-domain logsumexp per row, folded with the sink, into a
+// Two passes over S = Q K^T per (batch entry, KV head) on the 5th-generation
+// tensor cores.  Each CTA has four epilogue warps (one TMEM lane = one row of
+// the accumulator per thread), a load warp and an MMA warp whose elected lane
+// issues tcgen05.mma into one of two 128-column TMEM accumulators while the
+// epilogue drains the other:
+//   lse_kernel     M = 128 rows = 16 queries x the group's 8 query heads
+//                  (Q tile by TMA), N = 128 keys per step streamed through a
+//                  4-stage ring; each thread keeps its row's online log2
+//                  logsumexp and writes it, folded with the sink, to a
 //                  [total_q, H] workspace.
-//   colsum_kernel  CTA = 256 keys (64 per warp, held as B fragments in
-//                  registers); Q streamed in 8-query blocks through a cp.async
-//                  double buffer; p = exp2(s - lse) reduced over the group's
-//                  heads (sum or max) and summed over queries in registers, so
-//                  every column total is formed inside one warp and written
-//                  once per unit without atomics.
-// Both passes spend one exp2 per (row, key), so the kernel is bounded by the
-// SFU exp2 rate as much as by the tensor pipe.
+//   colsum_kernel  M = 128 keys (loaded once), N = 16 queries x 8 heads per
+//                  step (Q block and its 128 normalizers by TMA through the
+//                  ring): D = K Q^T, so each thread owns one key and sums
+//                  p = exp2(s - lse) over its row -- over all 8 heads (SUM) or
+//                  the max of each query's 8 adjacent columns (MAX) -- with no
+//                  cross-thread reduction; unit sums are written once, no atomics.
+// Key rows come from the paged pool one page per TMA load when a page is at
+// least 8 rows (1 KB); smaller pages are gathered with cp.async and published
+// to the tensor cores with a proxy fence.  Every wait is bounded;
+// a wait that gives up flags CE_EW_TIMEOUT, tells the other roles to stop, and
+// the CTA still drains its copies and frees its tensor memory.
+// Both passes spend one exp2 per (row, key) on the SFU (ex2.approx), which
+// bounds the kernel; the tensor cores run asynchronously beside it.
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -44,15 +51,17 @@ constexpr int D = 64;
 constexpr int GROUP = 8;
 constexpr float LOG2E = 1.4426950408889634f;
 
-constexpr int KT = 64;            // keys per K tile (both passes)
-constexpr int L_THREADS = 256;    // lse_kernel: 8 warps x 32 rows
-constexpr int L_QT = 32;          // queries per lse CTA
-constexpr int C_THREADS = 128;    // colsum_kernel: 4 warps x 64 keys
-constexpr int C_KT = 256;         // keys per colsum CTA
-constexpr int C_QB = 8;           // queries per Q block (4 m-tiles of 2 queries)
-constexpr int TILE_BYTES = KT * D * 2;         // 8 KB: 64 rows of 128 B
-constexpr int C_SMEM = 4 * TILE_BYTES + 2 * TILE_BYTES + 2 * C_QB * GROUP * 4;
-constexpr int L_SMEM = L_QT * GROUP * 128 + 2 * TILE_BYTES;   // 48 KB
+constexpr int BM = 128;                  // accumulator rows (TMEM lanes)
+constexpr int BN = 128;                  // accumulator columns per step
+constexpr int QT = BM / GROUP;           // 16 queries per pass-1 CTA / per pass-2 step
+constexpr int TILE = 128 * 128;          // a 128-row K-major bf16 tile, 128 B per row
+constexpr int NS = 5;                    // ring stages
+constexpr int LAG = 3;                   // cp.async key tiles in flight before one is published
+constexpr int THREADS = 192;             // warps 0-3 epilogue, 4 loads, 5 MMA
+constexpr int LOAD_WARP = 4, MMA_WARP = 5;
+constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr uint32_t IDESC = f16_idesc(BM, BN);
+constexpr int LSE_BLOCK = QT * GROUP * 4;  // 512 B of normalizers per pass-2 step
 
 struct Params {
   const __nv_bfloat16* q;
@@ -74,6 +83,16 @@ struct Params {
   int total_q, max_q, max_tokens;
   int64_t kv_capacity;
   int32_t* err;
+};
+
+// Barriers and flags after the tiles in shared memory.
+struct Sync {
+  uint64_t full[NS], empty[NS];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t once;       // Q tile (pass 1) / key tile (pass 2)
+  uint64_t mma_done;
+  uint32_t tmem;
+  int abort;
 };
 
 // Entry b's query range [qbeg, qbeg + nq) and key list (ntok tokens starting
@@ -99,8 +118,9 @@ __device__ __forceinline__ int entry_mode(const Params& p, int b) {
   return p.mode_of_row[p.rows ? p.rows[b] : b];
 }
 
-// 128-byte rows of eight 16-byte chunks; chunk c of row r lives at c ^ (r & 7)
-// so the 8 rows an ldmatrix phase reads fall in 8 different bank groups.
+// 128-byte rows of eight 16-byte chunks in 1024-byte atoms; chunk c of row r
+// lives at c ^ (r & 7) (the layout TMA's 128-byte swizzle writes and the
+// tcgen05 SWIZZLE_128B K-major descriptor reads).
 __device__ __forceinline__ uint32_t swz(int r, int c) {
   return static_cast<uint32_t>((r * 8 + (c ^ (r & 7))) * 16);
 }
@@ -115,164 +135,255 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
-// Address of chunk c (8 elements) of list token t of entry b, head g; nullptr
-// (and CE_EW_INDEX) for a unit outside the pool.
-__device__ __forceinline__ const __nv_bfloat16* key_chunk(const Params& p, int list0, int t, int g,
-                                                          int c) {
+// 2^x with the SFU's approximate exp2 (PTX ex2.approx.ftz.f32): relative
+// error near 2^-22, -inf -> +0, results below the normal range flush to 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Unit holding list token t of the entry, or -1 past ntok / -2 outside the pool
+// (flagged).
+__device__ __forceinline__ int token_unit(const Params& p, int list0, int ntok, int t) {
+  if (t >= ntok) return -1;
   const int unit = p.kv_indices[list0 + t / p.P];
-  if (unit < 0 || unit >= p.pool_units) {
-    flag_error(p.err, CE_EW_INDEX);
-    return nullptr;
-  }
-  return p.k + ((static_cast<int64_t>(unit) * p.G + g) * p.P + t % p.P) * D + c * 8;
+  if (unit >= 0 && unit < p.pool_units) return unit;
+  flag_error(p.err, CE_EW_INDEX);
+  return -2;
 }
 
-// Stage keys [t0, t0 + rows) of (b, g) into a swizzled tile; tokens at or
-// past ntok are zero-filled.  `nthreads` threads cooperate from `tid`.
-__device__ __forceinline__ void load_keys(const Params& p, uint32_t tile, int list0, int ntok, int t0,
-                                          int rows, int g, int tid, int nthreads) {
-  for (int id = tid; id < rows * 8; id += nthreads) {
-    const int r = id >> 3, c = id & 7;
+// page_size >= 8: keys [t0, t0 + 128) of (b, g) as 128 / P page loads by TMA
+// (pool viewed as [units * G * P, 64] rows; each page lands on a 1024-byte
+// boundary of the tile), completing on `bar`.  Pages past ntok are not loaded
+// (their rows are masked by every reader).
+__device__ __forceinline__ void tma_key_tile(const Params& p, const CUtensorMap* kmap, uint8_t* tile,
+                                             uint64_t* bar, int list0, int ntok, int t0, int g,
+                                             int lane) {
+  const int pages = BN / p.P;
+  const int unit = lane < pages ? token_unit(p, list0, ntok, t0 + lane * p.P) : -1;
+  const unsigned valid = __ballot_sync(0xffffffffu, unit >= 0);
+  if (lane == 0) mbar_arrive_expect_tx(bar, __popc(valid) * p.P * 128);
+  __syncwarp();
+  if (unit >= 0) tma_load_2d(tile + lane * p.P * 128, kmap, 0, (unit * p.G + g) * p.P, bar);
+}
+
+// page_size < 8: one warp copies keys [t0, t0 + 128) into the tile with
+// cp.async (tokens past ntok zero-filled).  The 128 unit indices are read in
+// one batch (lane l: rows l, l+32, l+64, l+96) and passed around by shuffles;
+// lanes 8i..8i+7 then copy the eight chunks of rows i, i+4, i+8, ...
+__device__ __forceinline__ void copy_key_tile(const Params& p, uint32_t tile, int list0, int ntok,
+                                              int t0, int g, int lane) {
+  int u[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) u[k] = token_unit(p, list0, ntok, t0 + lane + 32 * k);
+  const int c = lane & 7;
+#pragma unroll
+  for (int j = 0; j < BM / 4; ++j) {
+    const int r = (lane >> 3) + 4 * j;
+    const int unit = __shfl_sync(0xffffffffu, u[j >> 3], r & 31);
     const int t = t0 + r;
-    const __nv_bfloat16* src = (t < ntok) ? key_chunk(p, list0, t, g, c) : nullptr;
-    cp_async16(tile + swz(r, c), src ? static_cast<const void*>(src) : static_cast<const void*>(p.k),
-               src != nullptr);
+    const bool ok = unit >= 0;
+    const __nv_bfloat16* src =
+        ok ? p.k + ((static_cast<int64_t>(unit) * p.G + g) * p.P + t % p.P) * D + c * 8 : p.k;
+    cp_async16(tile + swz(r, c), src, ok);
   }
 }
 
-__device__ __forceinline__ uint32_t ld_u32(const __nv_bfloat16* a) {
-  return *reinterpret_cast<const uint32_t*>(a);
+// Wait by one lane of a warp, result broadcast to the warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_t* err,
+                                          volatile int* abort, int lane) {
+  bool ok = true;
+  if (lane == 0) ok = mbar_wait_or_abort(bar, parity, err, abort);
+  return __shfl_sync(0xffffffffu, ok, 0);
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Initialise the barriers and allocate the two TMEM accumulators; returns the
+// TMEM base address (all threads).
+__device__ __forceinline__ uint32_t setup(Sync* sy, uint32_t empty_count) {
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&sy->full[s], 1);
+      mbar_init(&sy->empty[s], empty_count);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sy->acc_full[b], 1);
+      mbar_init(&sy->acc_empty[b], 4);
+    }
+    mbar_init(&sy->once, 1);
+    mbar_init(&sy->mma_done, 1);
+    sy->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == MMA_WARP) tmem_alloc(&sy->tmem, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  return sy->tmem;
+}
+
+// MMA warp epilogue of the role loop: every issued MMA completes before the
+// accumulators may be freed.
+__device__ __forceinline__ void mma_drain(Sync* sy, int32_t* err, bool issued) {
+  if (!issued) return;
+  tc_commit(&sy->mma_done);
+  mbar_wait(&sy->mma_done, 0, err);
+}
+
+__device__ __forceinline__ void teardown(Sync* sy, uint32_t tmem) {
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if ((threadIdx.x >> 5) == MMA_WARP) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // ---------------------------------------------------------------- pass 1
-// Row r of m-tile mt of warp w: query q0 + 4w + 2mt + (r >> 3), head g*8 + (r & 7).
-__global__ void __launch_bounds__(L_THREADS, 2) lse_kernel(const Params p) {
+// CTA (query tile x, KV head g, entry b); accumulator row r = query
+// 16x + r / 8, head g*8 + r % 8.
+__global__ void __launch_bounds__(THREADS, 1) lse_kernel(const Params p,
+                                                          const __grid_constant__ CUtensorMap qmap,
+                                                          const __grid_constant__ CUtensorMap kmap) {
   const int b = blockIdx.z, g = blockIdx.y;
   const int mode = entry_mode(p, b);
   if (mode != CE_MODE_SUM && mode != CE_MODE_MAX) return;
   int qbeg, nq, ntok, list0;
   if (!entry_ok(p, b, qbeg, nq, ntok, list0)) return;
-  const int q0 = blockIdx.x * L_QT;
+  const int q0 = blockIdx.x * QT;
   if (q0 >= nq) return;
   const int prefix = ntok - nq;
-  const int kend = prefix + min(nq - 1, q0 + L_QT - 1) + 1;  // keys [0, kend) are visible to some row
-  const int ntiles = (kend + KT - 1) / KT;
+  const int kend = prefix + min(nq, q0 + QT);   // keys [0, kend) are visible to some row
+  const int ntiles = (kend + BN - 1) / BN;
 
-  // Q rows of the CTA (32 queries x 8 heads, row = 8 * query + head) and a
-  // double-buffered K tile, all swizzled 128-byte rows.
-  extern __shared__ __align__(128) uint8_t lsm_dyn[];
-  const uint32_t qs = smem_addr(lsm_dyn);
-  const uint32_t kb0 = qs + L_QT * GROUP * 128, kb1 = kb0 + TILE_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const uint32_t qtile = smem_addr(sm);
+  const uint32_t ring = qtile + TILE;
+  Sync* sy = reinterpret_cast<Sync*>(sm + TILE + NS * TILE);
+  volatile int* abort = &sy->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int quad = lane >> 2, qc = lane & 3;
+  const uint32_t tmem = setup(sy, 1);
 
-  for (int id = threadIdx.x; id < L_QT * GROUP * 8; id += L_THREADS) {
-    const int r = id >> 3, c = id & 7;
-    const int q = q0 + (r >> 3);
-    const bool v = q < nq;
-    cp_async16(qs + swz(r, c),
-               p.q + (qbeg + (v ? q : 0)) * p.q_st + (g * GROUP + (r & 7)) * p.q_sh + c * 8, v);
-  }
-  int qrow[2][2];
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) qrow[mt][hf] = q0 + warp * 4 + mt * 2 + hf;
-
-  float m[2][2], l[2][2];
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      m[mt][hf] = -INFINITY;
-      l[mt][hf] = 0.f;
+  if (warp == LOAD_WARP) {
+    // ------------------------------------------------------------ loads
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&sy->once, TILE);
+      tma_load_3d(sm, &qmap, 0, g * GROUP, qbeg + q0, &sy->once);
     }
-
-  load_keys(p, kb0, list0, ntok, 0, KT, g, threadIdx.x, L_THREADS);
-  cp_async_commit();  // group 0: Q rows + K tile 0
-  for (int it = 0; it < ntiles; ++it) {
-    if (it + 1 < ntiles) {
-      load_keys(p, (it & 1) ? kb0 : kb1, list0, ntok, (it + 1) * KT, KT, g, threadIdx.x, L_THREADS);
+    const bool tma = p.P >= 8;
+    int t = 0;
+    for (; t < ntiles; ++t) {
+      const int s = t % NS;
+      if (t >= NS && !warp_wait(&sy->empty[s], ((t / NS) & 1) ^ 1, p.err, abort, lane)) {
+        *abort = 1;
+        break;
+      }
+      if (tma) {
+        tma_key_tile(p, &kmap, sm + TILE + s * TILE, &sy->full[s], list0, ntok, t * BN, g, lane);
+        continue;
+      }
+      copy_key_tile(p, ring + s * TILE, list0, ntok, t * BN, g, lane);
       cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+      if (t >= LAG) {
+        cp_async_wait<LAG>();
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sy->full[(t - LAG) % NS]);
+      }
     }
-    __syncthreads();
-    const uint32_t kb = (it & 1) ? kb1 : kb0;
-    float acc[2][8][4];
+    if (!tma) {
+      cp_async_wait<0>();
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0 && !*abort)
+        for (int u = max(0, t - LAG); u < t; ++u) mbar_arrive(&sy->full[u % NS]);
+    }
+    if (lane == 0) {
+      // Every issued load lands before the CTA may exit.
+      if (tma)
+        for (int u = max(0, t - NS); u < t; ++u) mbar_wait(&sy->full[u % NS], (u / NS) & 1, p.err);
+      mbar_wait(&sy->once, 0, p.err);
+    }
+  } else if (warp == MMA_WARP) {
+    // ------------------------------------------------------------- MMA
+    bool issued = false;
+    if (lane == 0 && mbar_wait_or_abort(&sy->once, 0, p.err, abort)) {
+      tc_fence_after();
+      const uint64_t adesc = sw128_desc(qtile);
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % NS, buf = t & 1;
+        if ((t >= 2 && !mbar_wait_or_abort(&sy->acc_empty[buf], ((t >> 1) & 1) ^ 1, p.err, abort)) ||
+            !mbar_wait_or_abort(&sy->full[s], (t / NS) & 1, p.err, abort)) {
+          *abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t bdesc = sw128_desc(ring + s * TILE);
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc_mma(tmem + buf * BN, adesc + 2 * kk, bdesc + 2 * kk, IDESC, kk > 0);
+        tc_commit(&sy->empty[s]);
+        tc_commit(&sy->acc_full[buf]);
+        issued = true;
+      }
+    } else if (lane == 0) {
+      *abort = 1;
+    }
+    if (lane == 0) mma_drain(sy, p.err, issued);
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------- epilogue
+    const int r = threadIdx.x;                 // accumulator row = TMEM lane
+    const int q = q0 + r / GROUP;
+    const int h = g * GROUP + r % GROUP;
+    const int lim = prefix + min(q, nq - 1);   // last visible list token of this row
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      const int buf = t & 1;
+      ok = warp_wait(&sy->acc_full[buf], (t >> 1) & 1, p.err, abort, lane);
+      if (!ok) {
+        *abort = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        __syncwarp();  // tcgen05.ld is warp-collective
+        tmem_ld32(taddr + c * 32, v);
+        const int kb = t * BN + c * 32;
+        if (kb + 31 > lim) {
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+          for (int i = 0; i < 32; ++i) v[i] = (kb + i <= lim) ? v[i] : -INFINITY;
+        }
+        float mx = v[0];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[mt][n][e] = 0.f;
+        for (int i = 1; i < 32; ++i) mx = fmaxf(mx, v[i]);
+        const float mn = fmaxf(m, mx * p.scale2);  // scale2 > 0 keeps the order
+        if (mn != -INFINITY) {
+          float sum = 0.f;
 #pragma unroll
-    for (int k2 = 0; k2 < 2; ++k2) {
-      // A fragments of both m-tiles for k-steps 2*k2 and 2*k2 + 1.
-      uint32_t a[2][2][4];
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          ldsm_x4(qs + swz(warp * 32 + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8,
-                           (2 * k2 + h) * 2 + (lane >> 4)),
-                  a[mt][h][0], a[mt][h][1], a[mt][h][2], a[mt][h][3]);
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kb + swz(n * 8 + (lane & 7), k2 * 4 + (lane >> 3)), b0, b1, b2, b3);
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          mma_16816_full(acc[mt][n], a[mt][0][0], a[mt][0][1], a[mt][0][2], a[mt][0][3], b0, b1);
-          mma_16816_full(acc[mt][n], a[mt][1][0], a[mt][1][1], a[mt][1][2], a[mt][1][3], b2, b3);
+          for (int i = 0; i < 32; ++i) sum += fast_exp2(fmaf(v[i], p.scale2, -mn));
+          l = l * fast_exp2(m - mn) + sum;
+          m = mn;
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sy->acc_empty[buf]);
     }
-    const int kbase = it * KT;
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int lim = min(prefix + qrow[mt][hf], ntok - 1);  // last visible list token
-        float mx = -INFINITY;
-#pragma unroll
-        for (int n = 0; n < 8; ++n)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int key = kbase + n * 8 + qc * 2 + e;
-            float& v = acc[mt][n][hf * 2 + e];
-            v = (key <= lim) ? v * p.scale2 : -INFINITY;
-            mx = fmaxf(mx, v);
-          }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float mn = fmaxf(m[mt][hf], mx);
-        if (mn == -INFINITY) continue;  // nothing visible yet (uniform over the quad)
-        float sum = 0.f;
-#pragma unroll
-        for (int n = 0; n < 8; ++n)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) sum += exp2f(acc[mt][n][hf * 2 + e] - mn);
-        l[mt][hf] = l[mt][hf] * exp2f(m[mt][hf] - mn) + sum;
-        m[mt][hf] = mn;
-      }
-    }
-    __syncthreads();  // the next iteration refills the buffer just read
-  }
-
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      float lt = l[mt][hf];
-      lt += __shfl_xor_sync(0xffffffffu, lt, 1);
-      lt += __shfl_xor_sync(0xffffffffu, lt, 2);
-      const int q = qrow[mt][hf];
-      if (qc != 0 || q >= nq) continue;
-      const int h = g * GROUP + quad;
-      float lse = m[mt][hf] + log2f(lt);
+    if (ok && q < nq) {
+      float lse = m + log2f(l);
       if (p.sinks) {
         const float s2 = p.sinks[h] * LOG2E;
         const float mxs = fmaxf(lse, s2);
@@ -281,149 +392,167 @@ __global__ void __launch_bounds__(L_THREADS, 2) lse_kernel(const Params p) {
       p.lse2[static_cast<int64_t>(qbeg + q) * p.H + h] = lse;
     }
   }
+  teardown(sy, tmem);
 }
 
 // ---------------------------------------------------------------- pass 2
-__global__ void __launch_bounds__(C_THREADS) colsum_kernel(const Params p) {
+// CTA (key tile x, KV head g, entry b); accumulator row r = key 128x + r,
+// column c of step j = query qfirst + 16j + c / 8, head g*8 + c % 8.
+__global__ void __launch_bounds__(THREADS, 1) colsum_kernel(const Params p,
+                                                             const __grid_constant__ CUtensorMap qmap,
+                                                             const __grid_constant__ CUtensorMap lmap,
+                                                             const __grid_constant__ CUtensorMap kmap) {
   const int b = blockIdx.z, g = blockIdx.y;
   const int mode = entry_mode(p, b);
   if (mode != CE_MODE_SUM && mode != CE_MODE_MAX) return;
   int qbeg, nq, ntok, list0;
   if (!entry_ok(p, b, qbeg, nq, ntok, list0)) return;
   const int prefix = ntok - nq;
-  const int k0 = blockIdx.x * C_KT;
+  const int k0 = blockIdx.x * BM;
   if (nq <= 0 || k0 >= ntok) return;
+  const int qfirst = max(0, k0 - prefix);   // first query that sees key k0
+  const int nblk = (nq - qfirst + QT - 1) / QT;
 
-  extern __shared__ __align__(128) uint8_t dyn[];
-  uint8_t* ksm = dyn;                                  // 4 x 8 KB, one 64-key slice per warp
-  uint8_t* qsm = dyn + 4 * TILE_BYTES;                 // 2 x 8 KB Q blocks (64 rows)
-  float* lsm = reinterpret_cast<float*>(qsm + 2 * TILE_BYTES);  // 2 x 64 row normalizers
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024(smem_raw);
+  const uint32_t ktile = smem_addr(sm);
+  const uint32_t ring = ktile + TILE;
+  float* lring = reinterpret_cast<float*>(sm + TILE + NS * TILE);           // NS x 128
+  float* tot = lring + NS * QT * GROUP;                                     // 128
+  Sync* sy = reinterpret_cast<Sync*>(tot + BM);
+  volatile int* abort = &sy->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int quad = lane >> 2, qc = lane & 3;
-  const int kw = k0 + warp * KT;                       // this warp's first key
+  const uint32_t tmem = setup(sy, 5);   // a stage is free after its MMA and the 4 epilogue warps
 
-  const int qfirst = max(0, k0 - prefix);              // first query that sees key k0
-  const int nblk = (nq - qfirst + C_QB - 1) / C_QB;
-  const uint32_t kbase = smem_addr(ksm), qb0 = smem_addr(qsm), qb1 = qb0 + TILE_BYTES;
-
-  auto load_q = [&](int blk, uint32_t dst, float* ldst) {
-    const int qb = qfirst + blk * C_QB;
-    for (int id = threadIdx.x; id < C_QB * GROUP * 8; id += C_THREADS) {
-      const int r = id >> 3, c = id & 7;
-      const int q = qb + (r >> 3);
-      const bool v = q < nq;
-      const __nv_bfloat16* src =
-          p.q + (qbeg + (v ? q : 0)) * p.q_st + (g * GROUP + (r & 7)) * p.q_sh + c * 8;
-      cp_async16(dst + swz(r, c), src, v);
-    }
-    if (threadIdx.x < C_QB * GROUP) {
-      const int r = threadIdx.x, q = qb + (r >> 3);
-      ldst[r] = (q < nq) ? p.lse2[static_cast<int64_t>(qbeg + q) * p.H + g * GROUP + (r & 7)]
-                         : INFINITY;
-    }
-  };
-
-  load_keys(p, kbase, list0, ntok, k0, C_KT, g, threadIdx.x, C_THREADS);
-  load_q(0, qb0, lsm);
-  cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
-
-  // B fragments of this warp's 64 keys: [n-tile][k-step][2].
-  uint32_t bf[8][4][2];
-  const uint32_t kt = kbase + warp * TILE_BYTES;
-#pragma unroll
-  for (int n = 0; n < 8; ++n)
-#pragma unroll
-    for (int k2 = 0; k2 < 2; ++k2)
-      ldsm_x4(kt + swz(n * 8 + (lane & 7), k2 * 4 + (lane >> 3)), bf[n][2 * k2][0], bf[n][2 * k2][1],
-              bf[n][2 * k2 + 1][0], bf[n][2 * k2 + 1][1]);
-
-  float col[8][2];
-#pragma unroll
-  for (int n = 0; n < 8; ++n) col[n][0] = col[n][1] = 0.f;
-
-  for (int blk = 0; blk < nblk; ++blk) {
-    const uint32_t qcur = (blk & 1) ? qb1 : qb0;
-    const float* lcur = lsm + (blk & 1) * C_QB * GROUP;
-    if (blk + 1 < nblk) {
-      load_q(blk + 1, (blk & 1) ? qb0 : qb1, lsm + ((blk + 1) & 1) * C_QB * GROUP);
+  if (warp == LOAD_WARP) {
+    // ------------------------------------------------------------ loads
+    const bool tma = p.P >= 8;
+    if (tma) {
+      tma_key_tile(p, &kmap, sm, &sy->once, list0, ntok, k0, g, lane);
+    } else {
+      copy_key_tile(p, ktile, list0, ntok, k0, g, lane);
       cp_async_commit();
     }
-    const int qb = qfirst + blk * C_QB;
-#pragma unroll 1
-    for (int mt = 0; mt < 4; ++mt) {
-      uint32_t a[4][4];
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        ldsm_x4(qcur + swz(mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, kk * 2 + (lane >> 4)),
-                a[kk][0], a[kk][1], a[kk][2], a[kk][3]);
-      float acc[8][4];
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_16816_full(acc[n], a[kk][0], a[kk][1], a[kk][2], a[kk][3], bf[n][kk][0], bf[n][kk][1]);
+    int j = 0;
+    for (; j < nblk; ++j) {
+      const int s = j % NS;
+      if (j >= NS && !warp_wait(&sy->empty[s], ((j / NS) & 1) ^ 1, p.err, abort, lane)) {
+        *abort = 1;
+        break;
       }
-      const int qa = qb + mt * 2;
-      const float l0 = lcur[mt * 16 + quad], l1 = lcur[mt * 16 + 8 + quad];
-      const int lim0 = (qa < nq) ? min(prefix + qa, ntok - 1) : -1;
-      const int lim1 = (qa + 1 < nq) ? min(prefix + qa + 1, ntok - 1) : -1;
-      const bool full = kw + KT - 1 <= lim0;  // both rows see every key of the slice
+      if (lane == 0) {
+        const int z = qbeg + qfirst + j * QT;
+        mbar_arrive_expect_tx(&sy->full[s], TILE + LSE_BLOCK);
+        tma_load_3d(sm + TILE + s * TILE, &qmap, 0, g * GROUP, z, &sy->full[s]);
+        tma_load_2d(lring + s * QT * GROUP, &lmap, g * GROUP, z, &sy->full[s]);
+      }
+      if (j == 0 && !tma) {
+        cp_async_wait<0>();
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sy->once);
+      }
+    }
+    if (j == 0 && !tma) {  // no step issued: still publish the key tile
+      cp_async_wait<0>();
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sy->once);
+    }
+    // Every issued load lands before the CTA may exit.
+    if (lane == 0) {
+      for (int u = max(0, j - NS); u < j; ++u) mbar_wait(&sy->full[u % NS], (u / NS) & 1, p.err);
+      if (tma) mbar_wait(&sy->once, 0, p.err);
+    }
+  } else if (warp == MMA_WARP) {
+    // ------------------------------------------------------------- MMA
+    bool issued = false;
+    if (lane == 0 && mbar_wait_or_abort(&sy->once, 0, p.err, abort)) {
+      tc_fence_after();
+      const uint64_t adesc = sw128_desc(ktile);
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % NS, buf = j & 1;
+        if ((j >= 2 && !mbar_wait_or_abort(&sy->acc_empty[buf], ((j >> 1) & 1) ^ 1, p.err, abort)) ||
+            !mbar_wait_or_abort(&sy->full[s], (j / NS) & 1, p.err, abort)) {
+          *abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t bdesc = sw128_desc(ring + s * TILE);
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc_mma(tmem + buf * BN, adesc + 2 * kk, bdesc + 2 * kk, IDESC, kk > 0);
+        tc_commit(&sy->empty[s]);
+        tc_commit(&sy->acc_full[buf]);
+        issued = true;
+      }
+    } else if (lane == 0) {
+      *abort = 1;
+    }
+    if (lane == 0) mma_drain(sy, p.err, issued);
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------- epilogue
+    const int r = threadIdx.x;
+    const int key = k0 + r;
+    float acc = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk && ok; ++j) {
+      const int s = j % NS, buf = j & 1;
+      // The stage's normalizers came by TMA: observe its completion here too
+      // (already complete once the accumulator is).
+      ok = warp_wait(&sy->acc_full[buf], (j >> 1) & 1, p.err, abort, lane) &&
+           warp_wait(&sy->full[s], (j / NS) & 1, p.err, abort, lane);
+      if (!ok) {
+        *abort = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + buf * BN;
+      const float* lse = lring + s * QT * GROUP;
+      const int qb = qfirst + j * QT;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        __syncwarp();  // tcgen05.ld is warp-collective
+        tmem_ld32(taddr + c * 32, v);
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = kw + n * 8 + qc * 2 + e;
-          float p0 = exp2f(fmaf(acc[n][e], p.scale2, -l0));
-          float p1 = exp2f(fmaf(acc[n][2 + e], p.scale2, -l1));
-          if (!full) {
-            p0 = (key <= lim0) ? p0 : 0.f;
-            p1 = (key <= lim1) ? p1 : 0.f;
-          }
+        for (int u = 0; u < 4; ++u) {
+          const int qq = qb + c * 4 + u;
+          const bool vis = qq < nq && key <= prefix + qq;
+          const float* lq = lse + (c * 4 + u) * GROUP;
           if (mode == CE_MODE_SUM) {
-            col[n][e] += p0 + p1;
-          } else {
+            float sum = 0.f;
 #pragma unroll
-            for (int o = 4; o < 32; o <<= 1) {
-              p0 = fmaxf(p0, __shfl_xor_sync(0xffffffffu, p0, o));
-              p1 = fmaxf(p1, __shfl_xor_sync(0xffffffffu, p1, o));
-            }
-            col[n][e] += p0 + p1;
+            for (int x = 0; x < GROUP; ++x) sum += fast_exp2(fmaf(v[u * 8 + x], p.scale2, -lq[x]));
+            acc += vis ? sum : 0.f;
+          } else {
+            float mx = 0.f;
+#pragma unroll
+            for (int x = 0; x < GROUP; ++x)
+              mx = fmaxf(mx, fast_exp2(fmaf(v[u * 8 + x], p.scale2, -lq[x])));
+            acc += vis ? mx : 0.f;
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sy->acc_empty[buf]);
+        mbar_arrive(&sy->empty[s]);  // done with this stage's normalizers
+      }
     }
-    if (blk + 1 < nblk) cp_async_wait<0>();
-    __syncthreads();  // next Q block landed; the block just read may be refilled
+    tot[r] = (ok && key < ntok) ? acc : 0.f;
   }
-
-  if (mode == CE_MODE_SUM) {
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 2; ++e)
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) col[n][e] += __shfl_xor_sync(0xffffffffu, col[n][e], o);
-  }
-  // Column totals of this warp's 64 keys -> its K slice's shared memory (no
-  // longer needed), then per-unit sums.
-  float* tot = reinterpret_cast<float*>(ksm + warp * TILE_BYTES);
-  __syncwarp();
-  if (quad == 0) {
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) tot[n * 8 + qc * 2 + e] = col[n][e];
-  }
-  __syncwarp();
-  const int per = KT / p.P;  // units in this warp's slice
-  for (int j = lane; j < per; j += 32) {
-    const int t = kw + j * p.P;  // first token of the unit
+  teardown(sy, tmem);
+  if (*abort) return;
+  // Per-unit sums of the CTA's 128 keys (page_size divides 128).
+  const int per = BM / p.P;
+  for (int u = threadIdx.x; u < per; u += THREADS) {
+    const int t = k0 + u * p.P;  // first token of the unit
     if (t >= ntok) continue;
     float s = 0.f;
-    for (int x = 0; x < p.P; ++x) s += tot[j * p.P + x];
+    for (int x = 0; x < p.P; ++x) s += tot[u * p.P + x];
     const int unit = p.kv_indices[list0 + t / p.P];
     if (unit < 0 || unit >= p.pool_units) {
       flag_error(p.err, CE_EW_INDEX);
@@ -433,6 +562,13 @@ __global__ void __launch_bounds__(C_THREADS) colsum_kernel(const Params p) {
     *sp = (p.zero_new && t >= prefix) ? s : *sp + s;
   }
 }
+
+// Dynamic shared memory: 1 KB alignment slack + tiles + barriers.
+constexpr int L_SMEM = 1024 + TILE + NS * TILE + static_cast<int>(sizeof(Sync));
+constexpr int C_SMEM = 1024 + TILE + NS * TILE + NS * LSE_BLOCK + BM * 4 + static_cast<int>(sizeof(Sync));
+// At most two CTAs fit on an SM (2 x 256 TMEM columns = all 512): tcgen05.alloc never waits.
+static_assert(3 * L_SMEM > 227 * 1024 && 3 * C_SMEM > 227 * 1024, "a third CTA per SM would oversubscribe TMEM");
+static_assert(2 * C_SMEM <= 227 * 1024, "two CTAs per SM");
 
 }  // namespace prefill
 }  // namespace ce
@@ -457,9 +593,10 @@ extern "C" int ce_prefill_scores(const void* q, int64_t q_st, int64_t q_sh, cons
   using namespace ce::prefill;
   if (bs < 0 || total_q < 0 || max_q < 0 || max_tokens < 0 || pool_units <= 0 || kv_capacity < 0)
     return host::fail(CE_ERR_ARG, "ce_prefill_scores: negative size");
+  if (!(sm_scale > 0.f)) return host::fail(CE_ERR_ARG, "ce_prefill_scores: sm_scale must be positive");
   if (head_dim != D || num_kv_heads <= 0 || num_q_heads != GROUP * num_kv_heads)
     return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill_scores: needs head_dim 64 and 8 query heads per KV head");
-  if (page_size <= 0 || page_size > KT || KT % page_size != 0)
+  if (page_size <= 0 || page_size > 64 || 64 % page_size != 0)
     return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill_scores: page_size must divide 64");
   if (q_sh % 8 != 0 || q_st % 8 != 0 || q_sh < D || q_st < static_cast<int64_t>(num_q_heads) * q_sh)
     return host::fail(CE_ERR_ARG, "ce_prefill_scores: q strides must be multiples of 8 elements");
@@ -469,12 +606,38 @@ extern "C" int ce_prefill_scores(const void* q, int64_t q_st, int64_t q_sh, cons
   if (score_sg < pool_units)
     return host::fail(CE_ERR_ARG, "ce_prefill_scores: score head stride below pool_units");
   if (bs > 65535) return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill_scores: more than 65535 entries");
+  if (pool_units * num_kv_heads * page_size > INT32_MAX)
+    return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill_scores: pool rows exceed 2^31");
   const int64_t need = ce_prefill_workspace_bytes(total_q, num_q_heads);
   if (!workspace || workspace_bytes < need)
     return host::fail(CE_ERR_WORKSPACE, "ce_prefill_scores: workspace too small");
   if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(k_pool) & 15) ||
       (reinterpret_cast<uintptr_t>(workspace) & 15))
     return host::fail(CE_ERR_ARG, "ce_prefill_scores: q, k_pool and workspace need 16-byte alignment");
+
+  // Q as [total_q][H][64] with byte strides; box = 16 queries x 8 heads x 64.
+  CUtensorMap qmap, lmap;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(num_q_heads),
+                              static_cast<uint64_t>(total_q)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(q_sh) * 2, static_cast<uint64_t>(q_st) * 2};
+    const uint32_t box[3] = {static_cast<uint32_t>(D), GROUP, QT};
+    if (!host::encode_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims, strides, box, true))
+      return host::fail(CE_ERR_CUDA, "ce_prefill_scores: query tensor map");
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(num_q_heads), static_cast<uint64_t>(total_q)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(num_q_heads) * 4};
+    const uint32_t box[2] = {GROUP, QT};
+    if (!host::encode_map(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, workspace, dims, strides, box, false))
+      return host::fail(CE_ERR_CUDA, "ce_prefill_scores: normalizer tensor map");
+  }
+
+  // K pool as [units * G * page, 64] rows; box = one page of one head.
+  CUtensorMap kmap;
+  if (!host::encode_rows_map(&kmap, k_pool, static_cast<uint64_t>(pool_units) * num_kv_heads * page_size,
+                             D, static_cast<uint32_t>(page_size)))
+    return host::fail(CE_ERR_CUDA, "ce_prefill_scores: key tensor map");
 
   Params p;
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -503,14 +666,14 @@ extern "C" int ce_prefill_scores(const void* q, int64_t q_st, int64_t q_sh, cons
   p.kv_capacity = kv_capacity;
   p.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const dim3 g1((max_q + L_QT - 1) / L_QT, num_kv_heads, bs);
-  if (!host::set_smem(lse_kernel, L_SMEM)) return host::fail(CE_ERR_CUDA, "prefill smem attr");
-  lse_kernel<<<g1, L_THREADS, L_SMEM, st>>>(p);
+  if (!host::set_smem(lse_kernel, L_SMEM) || !host::set_smem(colsum_kernel, C_SMEM))
+    return host::fail(CE_ERR_CUDA, "prefill smem attr");
+  const dim3 g1((max_q + QT - 1) / QT, num_kv_heads, bs);
+  lse_kernel<<<g1, THREADS, L_SMEM, st>>>(p, qmap, kmap);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("prefill lse_kernel");
   if (max_tokens == 0) return CE_OK;
-  if (!host::set_smem(colsum_kernel, C_SMEM)) return host::fail(CE_ERR_CUDA, "prefill smem attr");
-  const dim3 g2((max_tokens + C_KT - 1) / C_KT, num_kv_heads, bs);
-  colsum_kernel<<<g2, C_THREADS, C_SMEM, st>>>(p);
+  const dim3 g2((max_tokens + BM - 1) / BM, num_kv_heads, bs);
+  colsum_kernel<<<g2, THREADS, C_SMEM, st>>>(p, qmap, lmap, kmap);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("prefill colsum_kernel");
   return CE_OK;
 }

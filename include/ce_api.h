@@ -218,8 +218,8 @@ int ce_decode_attn_score_static(const void* q, int64_t q_sb, int64_t q_sh,
  *           nq_b and kv_tokens[b] (grid sizes); an entry above either, or
  *           with ranges outside total_q / kv_capacity, flags CE_EW_SHAPE
  *           and is skipped
- * Supported: head_dim 64, H == 8*G, page_size dividing 64.  No scratch
- * beyond the workspace ([total_q, H] fp32 row normalizers). */
+ * Supported: head_dim 64, H == 8*G, page_size dividing 64, sm_scale > 0.
+ * No scratch beyond the workspace ([total_q, H] fp32 row normalizers). */
 int64_t ce_prefill_workspace_bytes(int32_t total_q, int32_t num_q_heads);
 int ce_prefill_scores(const void* q, int64_t q_st, int64_t q_sh,
                       const void* k_pool, int64_t pool_units,
