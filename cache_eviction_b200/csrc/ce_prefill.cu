@@ -15,8 +15,9 @@
 // reference's token-slot score summed over the page.
 //
 // Two passes over S = Q K^T per (batch entry, KV head) on the 5th-generation
-// tensor cores.  Each CTA has four epilogue warps (one TMEM lane = one row of
-// the accumulator per thread), a load warp and an MMA warp whose elected lane
+// tensor cores.  Each CTA has eight epilogue warps (one TMEM lane = one row of
+// the accumulator per thread, two warps per row splitting its columns), a
+// load warp and an MMA warp whose elected lane
 // issues tcgen05.mma into one of two 128-column TMEM accumulators while the
 // epilogue drains the other:
 //   lse_kernel     M = 128 rows = 16 queries x the group's 8 query heads
@@ -57,8 +58,9 @@ constexpr int QT = BM / GROUP;           // 16 queries per pass-1 CTA / per pass
 constexpr int TILE = 128 * 128;          // a 128-row K-major bf16 tile, 128 B per row
 constexpr int NS = 5;                    // ring stages
 constexpr int LAG = 3;                   // cp.async key tiles in flight before one is published
-constexpr int THREADS = 192;             // warps 0-3 epilogue, 4 loads, 5 MMA
-constexpr int LOAD_WARP = 4, MMA_WARP = 5;
+constexpr int EPI_WARPS = 8;             // two per TMEM lane quarter, 64 columns each
+constexpr int THREADS = 32 * (EPI_WARPS + 2);   // warps 0-7 epilogue, 8 loads, 9 MMA
+constexpr int LOAD_WARP = EPI_WARPS, MMA_WARP = EPI_WARPS + 1;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr uint32_t IDESC = f16_idesc(BM, BN);
 constexpr int LSE_BLOCK = QT * GROUP * 4;  // 512 B of normalizers per pass-2 step
@@ -93,6 +95,7 @@ struct Sync {
   uint64_t mma_done;
   uint32_t tmem;
   int abort;
+  float part[2][BM];   // the second column half's partial results, per row
 };
 
 // Entry b's query range [qbeg, qbeg + nq) and key list (ntok tokens starting
@@ -202,6 +205,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_
   return __shfl_sync(0xffffffffu, ok, 0);
 }
 
+// Barrier of the epilogue warps only (named barrier 1).
+__device__ __forceinline__ void named_barrier_epi() {
+  asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+}
+
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
@@ -217,7 +225,7 @@ __device__ __forceinline__ uint32_t setup(Sync* sy, uint32_t empty_count) {
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sy->acc_full[b], 1);
-      mbar_init(&sy->acc_empty[b], 4);
+      mbar_init(&sy->acc_empty[b], EPI_WARPS);
     }
     mbar_init(&sy->once, 1);
     mbar_init(&sy->mma_done, 1);
@@ -249,7 +257,7 @@ __device__ __forceinline__ void teardown(Sync* sy, uint32_t tmem) {
 // ---------------------------------------------------------------- pass 1
 // CTA (query tile x, KV head g, entry b); accumulator row r = query
 // 16x + r / 8, head g*8 + r % 8.
-__global__ void __launch_bounds__(THREADS, 1) lse_kernel(const Params p,
+__global__ void __launch_bounds__(THREADS, 2) lse_kernel(const Params p,
                                                           const __grid_constant__ CUtensorMap qmap,
                                                           const __grid_constant__ CUtensorMap kmap) {
   const int b = blockIdx.z, g = blockIdx.y;
@@ -341,49 +349,62 @@ __global__ void __launch_bounds__(THREADS, 1) lse_kernel(const Params p,
     __syncwarp();
   } else {
     // -------------------------------------------------------- epilogue
-    const int r = threadIdx.x;                 // accumulator row = TMEM lane
+    // Warp e reads TMEM lanes 32 (e % 4) .. +31 (its rows), columns
+    // 64 (e / 4) .. +63 of each accumulator; the two halves of a row merge at
+    // the end.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;         // accumulator row = TMEM lane
     const int q = q0 + r / GROUP;
     const int h = g * GROUP + r % GROUP;
     const int lim = prefix + min(q, nq - 1);   // last visible list token of this row
     float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int t = 0; t < ntiles && ok; ++t) {
+    for (int t = 0; t < ntiles; ++t) {
       const int buf = t & 1;
-      ok = warp_wait(&sy->acc_full[buf], (t >> 1) & 1, p.err, abort, lane);
-      if (!ok) {
+      if (!warp_wait(&sy->acc_full[buf], (t >> 1) & 1, p.err, abort, lane)) {
         *abort = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + buf * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        __syncwarp();  // tcgen05.ld is warp-collective
-        tmem_ld32(taddr + c * 32, v);
-        const int kb = t * BN + c * 32;
-        if (kb + 31 > lim) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = (kb + i <= lim) ? v[i] : -INFINITY;
-        }
-        float mx = v[0];
-#pragma unroll
-        for (int i = 1; i < 32; ++i) mx = fmaxf(mx, v[i]);
-        const float mn = fmaxf(m, mx * p.scale2);  // scale2 > 0 keeps the order
-        if (mn != -INFINITY) {
-          float sum = 0.f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sum += fast_exp2(fmaf(v[i], p.scale2, -mn));
-          l = l * fast_exp2(m - mn) + sum;
-          m = mn;
-        }
-      }
+      float v[64];
+      __syncwarp();  // tcgen05.ld is warp-collective
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + half * 64;
+      tmem_ld32_async(taddr, v);
+      tmem_ld32_async(taddr + 32, v + 32);
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sy->acc_empty[buf]);
+      if (lane == 0) mbar_arrive(&sy->acc_empty[buf]);  // the values are in registers
+      const int kb = t * BN + half * 64;
+      if (kb + 63 > lim) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = (kb + i <= lim) ? v[i] : -INFINITY;
+      }
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = v[i];
+#pragma unroll
+      for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], v[i]);
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float mn = fmaxf(m, mt * p.scale2);  // scale2 > 0 keeps the order
+      if (mn != -INFINITY) {
+        float sm4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 64; ++i) sm4[i & 3] += fast_exp2(fmaf(v[i], p.scale2, -mn));
+        l = l * fast_exp2(m - mn) + ((sm4[0] + sm4[1]) + (sm4[2] + sm4[3]));
+        m = mn;
+      }
     }
-    if (ok && q < nq) {
-      float lse = m + log2f(l);
+    if (half == 1) {
+      sy->part[0][r] = m;
+      sy->part[1][r] = l;
+    }
+    named_barrier_epi();
+    if (half == 0 && !*abort && q < nq) {
+      const float m1 = sy->part[0][r], l1 = sy->part[1][r];
+      const float M = fmaxf(m, m1);  // finite: key 0 is in every row's first half
+      const float L = l * fast_exp2(m - M) + l1 * fast_exp2(m1 - M);
+      float lse = M + log2f(L);
       if (p.sinks) {
         const float s2 = p.sinks[h] * LOG2E;
         const float mxs = fmaxf(lse, s2);
@@ -398,7 +419,7 @@ __global__ void __launch_bounds__(THREADS, 1) lse_kernel(const Params p,
 // ---------------------------------------------------------------- pass 2
 // CTA (key tile x, KV head g, entry b); accumulator row r = key 128x + r,
 // column c of step j = query qfirst + 16j + c / 8, head g*8 + c % 8.
-__global__ void __launch_bounds__(THREADS, 1) colsum_kernel(const Params p,
+__global__ void __launch_bounds__(THREADS, 2) colsum_kernel(const Params p,
                                                              const __grid_constant__ CUtensorMap qmap,
                                                              const __grid_constant__ CUtensorMap lmap,
                                                              const __grid_constant__ CUtensorMap kmap) {
@@ -422,7 +443,7 @@ __global__ void __launch_bounds__(THREADS, 1) colsum_kernel(const Params p,
   Sync* sy = reinterpret_cast<Sync*>(tot + BM);
   volatile int* abort = &sy->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t tmem = setup(sy, 5);   // a stage is free after its MMA and the 4 epilogue warps
+  const uint32_t tmem = setup(sy, 1 + EPI_WARPS);   // a stage is free after its MMA and the epilogue
 
   if (warp == LOAD_WARP) {
     // ------------------------------------------------------------ loads
@@ -493,56 +514,55 @@ __global__ void __launch_bounds__(THREADS, 1) colsum_kernel(const Params p,
     __syncwarp();
   } else {
     // -------------------------------------------------------- epilogue
-    const int r = threadIdx.x;
+    // Warp e: TMEM lanes 32 (e % 4) .. +31 (its keys), columns 64 (e / 4) ..
+    // +63 = queries 8 (e / 4) .. +7 of each step; halves merge at the end.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
     const int key = k0 + r;
-    float acc = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nblk && ok; ++j) {
+    float acc[2] = {0.f, 0.f};
+    for (int j = 0; j < nblk; ++j) {
       const int s = j % NS, buf = j & 1;
       // The stage's normalizers came by TMA: observe its completion here too
       // (already complete once the accumulator is).
-      ok = warp_wait(&sy->acc_full[buf], (j >> 1) & 1, p.err, abort, lane) &&
-           warp_wait(&sy->full[s], (j / NS) & 1, p.err, abort, lane);
-      if (!ok) {
+      if (!warp_wait(&sy->acc_full[buf], (j >> 1) & 1, p.err, abort, lane) ||
+          !warp_wait(&sy->full[s], (j / NS) & 1, p.err, abort, lane)) {
         *abort = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + buf * BN;
-      const float* lse = lring + s * QT * GROUP;
-      const int qb = qfirst + j * QT;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        __syncwarp();  // tcgen05.ld is warp-collective
-        tmem_ld32(taddr + c * 32, v);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int qq = qb + c * 4 + u;
-          const bool vis = qq < nq && key <= prefix + qq;
-          const float* lq = lse + (c * 4 + u) * GROUP;
-          if (mode == CE_MODE_SUM) {
-            float sum = 0.f;
-#pragma unroll
-            for (int x = 0; x < GROUP; ++x) sum += fast_exp2(fmaf(v[u * 8 + x], p.scale2, -lq[x]));
-            acc += vis ? sum : 0.f;
-          } else {
-            float mx = 0.f;
-#pragma unroll
-            for (int x = 0; x < GROUP; ++x)
-              mx = fmaxf(mx, fast_exp2(fmaf(v[u * 8 + x], p.scale2, -lq[x])));
-            acc += vis ? mx : 0.f;
-          }
-        }
-      }
+      float v[64];
+      __syncwarp();  // tcgen05.ld is warp-collective
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN + half * 64;
+      tmem_ld32_async(taddr, v);
+      tmem_ld32_async(taddr + 32, v + 32);
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sy->acc_empty[buf]);
-        mbar_arrive(&sy->empty[s]);  // done with this stage's normalizers
+      if (lane == 0) mbar_arrive(&sy->acc_empty[buf]);  // the values are in registers
+      const float* lse = lring + s * QT * GROUP + half * 64;
+      const int qb = qfirst + j * QT + half * 8;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int qq = qb + u;
+        const bool vis = qq < nq && key <= prefix + qq;
+        const float* lq = lse + u * GROUP;
+        float e[GROUP];
+#pragma unroll
+        for (int x = 0; x < GROUP; ++x) e[x] = fast_exp2(fmaf(v[u * 8 + x], p.scale2, -lq[x]));
+        float red;
+        if (mode == CE_MODE_SUM)
+          red = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+        else
+          red = fmaxf(fmaxf(fmaxf(e[0], e[1]), fmaxf(e[2], e[3])),
+                      fmaxf(fmaxf(e[4], e[5]), fmaxf(e[6], e[7])));
+        acc[u & 1] += vis ? red : 0.f;
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sy->empty[s]);  // done with this stage's normalizers
     }
-    tot[r] = (ok && key < ntok) ? acc : 0.f;
+    if (half == 1) sy->part[0][r] = acc[0] + acc[1];
+    named_barrier_epi();
+    if (half == 0) tot[r] = (key < ntok) ? (acc[0] + acc[1]) + sy->part[0][r] : 0.f;
   }
   teardown(sy, tmem);
   if (*abort) return;
