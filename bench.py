@@ -323,7 +323,7 @@ PREFILL_CHUNK = 2048
 PREFILL_PREFIXES = (0, 8192, 26624)   # resident tokens before a chunk; 26,624 + 2,048 = config 4's cache
 
 
-def prefill_microbench(world, rank, device, reps=5, cpu=False):
+def prefill_microbench(world, rank, device, reps=5, cpu=False, prefixes=PREFILL_PREFIXES):
     """one 2,048-token prefill chunk of one layer scored by
     ce_prefill_scores against a resident prefix of 0 / 8,192 / 26,624 tokens
     (16-token pages, this rank's KV heads, no eviction inside the chunk).
@@ -339,7 +339,7 @@ def prefill_microbench(world, rank, device, reps=5, cpu=False):
     nq = PREFILL_CHUNK
     q = torch.randn((nq, H, D), generator=gen, device=device).to(torch.bfloat16)
     sinks = torch.randn(H, generator=gen, device=device)
-    for prefix in PREFILL_PREFIXES:
+    for prefix in prefixes:
         ntok = prefix + nq
         units = ntok // PAGE
         kpool = torch.randn((units + 1, G, PAGE, D), generator=gen, device=device).to(torch.bfloat16)
@@ -388,7 +388,7 @@ def prefill_microbench(world, rank, device, reps=5, cpu=False):
     return out
 
 
-def evict_microbench(world, rank, device, reps=3):
+def evict_microbench(world, rank, device, reps=3, rows=32):
     """one eviction step (select + compaction) over 32 rows x
     this rank's KV heads x 4096 pages (65,536-token contexts), fp32 scores
     lognormal(0, 2), P = R = B/4, for H2O global / H2O per-head / random at
@@ -398,7 +398,7 @@ def evict_microbench(world, rank, device, reps=3):
     import torch
     from cache_eviction_b200 import kernels, tp
     G, _, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
-    R, N = 32, 4096
+    R, N = rows, 4096
     units = R * N + 1
     gen = torch.Generator(device=device).manual_seed(55)
     kp = torch.randn((units, G, PAGE, D), generator=gen, device=device).to(torch.bfloat16)
@@ -481,7 +481,15 @@ def main():
                     help="skip the config-5 eviction-step leg")
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (small cases for profiling)")
+    ap.add_argument("--legs", default="decode,e2e,noscore,prefill4,evict5",
+                    help="legs to run; without 'decode' only the listed microbenchmarks run "
+                         "and one JSON line with their results is printed (profiling)")
+    ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
+    ap.add_argument("--prefill-prefixes", default=",".join(map(str, PREFILL_PREFIXES)),
+                    help="resident prefixes of the config-4 leg")
     args = ap.parse_args()
+    legs = set(args.legs.split(","))
+    prefixes = tuple(int(x) for x in args.prefill_prefixes.split(","))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
@@ -498,6 +506,17 @@ def main():
     device = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(device)
     capi.load()
+    if "decode" not in legs:
+        res = {}
+        if "prefill4" in legs:
+            res["prefill_config4"] = prefill_microbench(world, rank, device, prefixes=prefixes)
+        if "evict5" in legs:
+            res["evict_config5"] = evict_microbench(world, rank, device, rows=args.evict_rows)
+        if rank == 0:
+            print(json.dumps({"profile_legs": res}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
     specs = workload(args.seqs * world)
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else args.steps
     steps_total = args.warmup + max(args.steps, e2e_steps)
@@ -578,17 +597,22 @@ def main():
 
     # --------------------------------------------------------- e2e pass
     e2e_value, step_bytes = None, LAYERS * B * H * D * 2
-    if e2e_steps > 0:
+    if e2e_steps > 0 and "e2e" in legs:
         e2e_value = run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
                             scale, after_layer, barrier, max_over_ranks, e2e_steps)
 
-    prefill4 = prefill_microbench(world, rank, device, cpu=(rank == 0 and args.cpu_seconds > 0))
-    no_score = run_no_score(args, specs, steps_total, world, rank, group, device, q, out, sinks,
-                            scale, after_layer, barrier, max_over_ranks)
+    prefill4 = None
+    if "prefill4" in legs:
+        prefill4 = prefill_microbench(world, rank, device, cpu=(rank == 0 and args.cpu_seconds > 0),
+                                      prefixes=prefixes)
+    no_score = None
+    if "noscore" in legs:
+        no_score = run_no_score(args, specs, steps_total, world, rank, group, device, q, out, sinks,
+                                scale, after_layer, barrier, max_over_ranks)
 
     evict5 = None
-    if not args.no_evict_bench:
-        evict5 = evict_microbench(world, rank, device)
+    if not args.no_evict_bench and "evict5" in legs:
+        evict5 = evict_microbench(world, rank, device, rows=args.evict_rows)
         if world > 1:
             for k in evict5:
                 evict5[k]["evict_step_us"] = max_over_ranks(evict5[k]["evict_step_us"])
@@ -616,7 +640,8 @@ def main():
                   "boundary_ms_mean": statistics.mean(boundary_ms) if boundary_ms else None,
                   "boundary_rows": n_bound_rows},
         "resident_tokens_mean": statistics.mean(tokens_resident),
-        "no_score_same_resident": {"value": no_score, "unit": UNIT,
+        "no_score_same_resident": None if no_score is None else {
+                                   "value": no_score, "unit": UNIT,
                                    "scored_over_no_score": value / no_score,
                                    "what": "same rows, steps and boundaries with H2O scoring off "
                                            "(full-cache decode at the same resident KV)"},
