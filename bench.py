@@ -388,6 +388,43 @@ def prefill_microbench(world, rank, device, reps=5, cpu=False, prefixes=PREFILL_
     return out
 
 
+def select_token_microbench(world, rank, device, reps=3, rows=32):
+    """Config 5's page-size-1 stress variant of selection: ce_choose over
+    32 rows x this rank's KV heads x 65,536 token columns (fp32 scores
+    lognormal(0, 2); float64 uniforms for random), budgets 2K-32K tokens with
+    prefix = recent = budget / 4.  Algorithmic bytes: positions + scores
+    (+ uniforms) read once, kept indices written."""
+    import torch
+    from cache_eviction_b200 import kernels, tp
+    G, _, _ = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    R, N = rows, 65536
+    gen = torch.Generator(device=device).manual_seed(56)
+    pos = torch.arange(N, dtype=torch.int32, device=device).expand(R, G, N).contiguous()
+    sc = torch.randn((R, G, N), generator=gen, device=device).mul_(2.0).exp_()
+    uni = torch.rand((R, G, N), generator=gen, device=device, dtype=torch.float64)
+    out = {}
+    for pol in ("h2o_global_2048", "head_sum_2048", "random_2048"):
+        for budget in BUDGETS:
+            prm = kernels.row_params([dict(n=N, budget=budget, prefix=budget // 4, recent=budget // 4,
+                                           cursor=None, policy=pol, seed=i) for i in range(R)], device)
+            key = uni if pol == "random_2048" else sc
+            ts = []
+            for it in range(reps + 1):
+                a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda._sleep(SLEEP_CYCLES)
+                a.record()
+                _, status, _ = kernels.choose(pos, key, prm, 1, G, max_n=N + 1, kept_stride=budget)
+                e.record()
+                torch.cuda.synchronize()
+                if it:
+                    ts.append(a.elapsed_time(e) * 1e3)
+            assert bool((status == 0).all()), status
+            us = statistics.median(ts)
+            nbytes = R * G * N * (4 + key.element_size()) + R * G * budget * 4
+            out[f"{pol}_{budget}"] = {"us": us, "gbs": nbytes / (us * 1e-6) / 1e9}
+    return out
+
+
 def evict_microbench(world, rank, device, reps=3, rows=32):
     """one eviction step (select + compaction) over 32 rows x
     this rank's KV heads x 4096 pages (65,536-token contexts), fp32 scores
@@ -481,7 +518,7 @@ def main():
                     help="skip the config-5 eviction-step leg")
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (small cases for profiling)")
-    ap.add_argument("--legs", default="decode,e2e,noscore,prefill4,evict5",
+    ap.add_argument("--legs", default="decode,e2e,noscore,prefill4,evict5,select1",
                     help="legs to run; without 'decode' only the listed microbenchmarks run "
                          "and one JSON line with their results is printed (profiling)")
     ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
@@ -512,6 +549,8 @@ def main():
             res["prefill_config4"] = prefill_microbench(world, rank, device, prefixes=prefixes)
         if "evict5" in legs:
             res["evict_config5"] = evict_microbench(world, rank, device, rows=args.evict_rows)
+        if "select1" in legs:
+            res["select_token_config5"] = select_token_microbench(world, rank, device, rows=args.evict_rows)
         if rank == 0:
             print(json.dumps({"profile_legs": res}), flush=True)
         if world > 1:
@@ -613,6 +652,9 @@ def main():
     evict5 = None
     if not args.no_evict_bench and "evict5" in legs:
         evict5 = evict_microbench(world, rank, device, rows=args.evict_rows)
+    select1 = None
+    if not args.no_evict_bench and "select1" in legs:
+        select1 = select_token_microbench(world, rank, device, rows=args.evict_rows)
         if world > 1:
             for k in evict5:
                 evict5[k]["evict_step_us"] = max_over_ranks(evict5[k]["evict_step_us"])
@@ -646,6 +688,7 @@ def main():
                                    "what": "same rows, steps and boundaries with H2O scoring off "
                                            "(full-cache decode at the same resident KV)"},
         "evict_config5": evict5,
+        "select_token_config5": select1,
         "prefill_config4": prefill4,
     }
     if rank == 0 and world == 1 and args.cpu_seconds > 0:

@@ -274,6 +274,256 @@ __device__ __forceinline__ int key_bits_of(int policy, int score_dtype) {
   return 32;
 }
 
+// ---- large segments: REG_ITEMS*T+1 .. LARGE_MAX columns ------------------------
+// One pass over the inputs keeps a 16-bit monotone prefix of every unprotected
+// key in shared memory and a 4,096-bin histogram of its top 12 bits.  The
+// k-th largest key's prefix is then found in shared memory (the 12-bit bin,
+// then its 16 sub-bins), and only the columns sharing that prefix -- the
+// candidates, typically tens -- have their full keys computed again to settle
+// the exact threshold (key, then newer position) with the radix select above.
+// Positions are read once more, for kept columns only, when the kept set is
+// ranked.  So the inputs cross HBM about once, instead of once per radix pass.
+// A segment whose candidates overflow the buffer (e.g. thousands of equal
+// scores) returns false and takes the general path.
+constexpr int LARGE_MAX = 65536;
+constexpr int LHIST = 4096;
+constexpr int LCAND = 2048;
+constexpr int LARGE_BYTES = LARGE_MAX * 2 + 2 * (LARGE_MAX / 8) + LCAND * 16;  // 176 KB
+static_assert(LHIST == 8 * T, "one thread scans 8 bins");
+enum BinKind { BIN_K32 = 0, BIN_K64 = 1, BIN_R53 = 2, BIN_U64 = 3 };
+
+__device__ __forceinline__ double f64_from_key(uint64_t k) {
+  const uint64_t u = (k & 0x8000000000000000ull) ? (k & 0x7fffffffffffffffull) : ~k;
+  return __longlong_as_double(static_cast<long long>(u));
+}
+
+// 16-bit prefix, non-decreasing in the key: the top 16 bits of 32-bit, 64-bit
+// and 53-bit keys; f64 uniforms map linearly from [0, 1) (their top bits are
+// nearly all exponent).
+__device__ __forceinline__ uint32_t bin16_of(uint64_t key, int kind) {
+  switch (kind) {
+    case BIN_K32:
+      return static_cast<uint32_t>(key >> 16) & 0xFFFFu;
+    case BIN_K64:
+      return static_cast<uint32_t>(key >> 48);
+    case BIN_R53:
+      return static_cast<uint32_t>(key >> 37) & 0xFFFFu;
+    default: {
+      const double d = f64_from_key(key);
+      if (!(d == d) || d >= 1.0) return 0xFFFFu;
+      if (d <= 0.0) return 0u;
+      return min(0xFFFFu, static_cast<uint32_t>(d * 65536.0));
+    }
+  }
+}
+
+struct LargeBuf {
+  uint16_t* bin;   // [LARGE_MAX] key prefix of unprotected columns
+  uint32_t* prot;  // [LARGE_MAX / 32] protected columns
+  uint32_t* pick;  // [LARGE_MAX / 32] candidates that made the cut
+  int* hist;       // [LHIST], shares storage with the candidate arrays
+  uint64_t* ckey;  // [LCAND]
+  int* ccol;       // [LCAND]
+  int32_t* cpv;    // [LCAND]
+};
+
+__device__ __forceinline__ LargeBuf large_buf(uint32_t* base) {
+  LargeBuf b;
+  uint8_t* q = reinterpret_cast<uint8_t*>(base);
+  b.bin = reinterpret_cast<uint16_t*>(q);
+  q += LARGE_MAX * 2;
+  b.prot = reinterpret_cast<uint32_t*>(q);
+  q += LARGE_MAX / 8;
+  b.pick = reinterpret_cast<uint32_t*>(q);
+  q += LARGE_MAX / 8;
+  b.hist = reinterpret_cast<int*>(q);
+  b.ckey = reinterpret_cast<uint64_t*>(q);
+  q += LCAND * 8;
+  b.ccol = reinterpret_cast<int*>(q);
+  q += LCAND * 4;
+  b.cpv = reinterpret_cast<int32_t*>(q);
+  return b;
+}
+
+struct LargeSel {
+  int t16;      // unprotected columns with a larger prefix are kept
+  bool all_eq;  // every column with prefix t16 is kept (no candidate round)
+  bool none;    // no unprotected column is kept
+  bool all;     // every unprotected column is kept
+};
+
+__device__ __forceinline__ bool is_bit(const uint32_t* m, int c) { return (m[c >> 5] >> (c & 31)) & 1u; }
+
+// Pass over the inputs: prefixes, protected bits, histogram; returns this
+// thread's protected count (the caller reduces it).
+template <class ColFn>
+__device__ int large_scan(ColFn colfn, int N, int kind, const LargeBuf& lb) {
+  for (int i = threadIdx.x; i < LHIST; i += T) lb.hist[i] = 0;
+  for (int i = threadIdx.x; i < (N + 31) / 32; i += T) {
+    lb.prot[i] = 0u;
+    lb.pick[i] = 0u;
+  }
+  __syncthreads();
+  // Batches of LB columns per thread: every column's loads are issued before
+  // the first one is used.
+  constexpr int LB = 8;
+  int np = 0;
+  for (int c0 = threadIdx.x; c0 < N; c0 += LB * T) {
+    uint64_t key[LB];
+    int32_t pv[LB];
+    bool pr[LB];
+#pragma unroll
+    for (int u = 0; u < LB; ++u) {
+      const int c = c0 + u * T;
+      pr[u] = c < N ? colfn(c, key[u], pv[u]) : false;
+    }
+#pragma unroll
+    for (int u = 0; u < LB; ++u) {
+      const int c = c0 + u * T;
+      if (c >= N) continue;
+      if (pr[u]) {
+        ++np;
+        atomicOr(&lb.prot[c >> 5], 1u << (c & 31));
+        lb.bin[c] = 0;
+      } else {
+        const uint32_t b = bin16_of(key[u], kind);
+        lb.bin[c] = static_cast<uint16_t>(b);
+        atomicAdd(&lb.hist[b >> 4], 1);
+      }
+    }
+  }
+  return np;
+}
+
+// The k largest of the nonprot unprotected columns (0 < k < nonprot handled
+// here; the caller covers k <= 0 and k >= nonprot).  Returns false on
+// candidate overflow.
+template <class ColFn>
+__device__ bool large_select(ColFn colfn, int N, int k, int nonprot, int kind, const LargeBuf& lb,
+                             Sh& sh, LargeSel& r) {
+  r = LargeSel{0, false, false, false};
+  if (k <= 0) {
+    r.none = true;
+    return true;
+  }
+  if (k >= nonprot) {
+    r.all = true;
+    return true;
+  }
+  // 12-bit bin from the top: thread t owns bins 4095-8t .. 4088-8t.
+  int c8[8];
+  int s8 = 0;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    c8[q] = lb.hist[LHIST - 1 - 8 * threadIdx.x - q];
+    s8 += c8[q];
+  }
+  int total;
+  const int ex = block_excl(s8, sh, total);
+  if (ex < k && k <= ex + s8) {
+    int run = ex;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (run + c8[q] >= k) {
+        sh.bc[0] = LHIST - 1 - 8 * threadIdx.x - q;
+        sh.bc[1] = run;
+        break;
+      }
+      run += c8[q];
+    }
+  }
+  __syncthreads();
+  const int t12 = sh.bc[0], above12 = sh.bc[1];
+  __syncthreads();
+  // Its 16 sub-bins.
+  if (threadIdx.x < 16) lb.hist[threadIdx.x] = 0;
+  __syncthreads();
+  for (int c = threadIdx.x; c < N; c += T) {
+    const uint32_t b = lb.bin[c];
+    if ((b >> 4) == static_cast<uint32_t>(t12) && !is_bit(lb.prot, c)) atomicAdd(&lb.hist[b & 15], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = above12;
+    for (int d = 15; d >= 0; --d) {
+      if (run + lb.hist[d] >= k) {
+        sh.bc[0] = (t12 << 4) | d;
+        sh.bc[1] = run;
+        sh.bc[2] = lb.hist[d];
+        break;
+      }
+      run += lb.hist[d];
+    }
+    sh.bc[5] = 0;
+  }
+  __syncthreads();
+  const int t16 = sh.bc[0], above16 = sh.bc[1], eq16 = sh.bc[2];
+  r.t16 = t16;
+  const int krem = k - above16;
+  if (krem >= eq16) {
+    r.all_eq = true;
+    return true;
+  }
+  if (eq16 > LCAND) return false;
+  // Candidates: full keys of the columns with prefix t16 (hist is dead now).
+  for (int c = threadIdx.x; c < N; c += T) {
+    if (lb.bin[c] != t16 || is_bit(lb.prot, c)) continue;
+    uint64_t key;
+    int32_t pv;
+    colfn(c, key, pv);
+    const int idx = atomicAdd(&sh.bc[5], 1);
+    if (idx < LCAND) {
+      lb.ckey[idx] = key;
+      lb.cpv[idx] = pv;
+      lb.ccol[idx] = c;
+    }
+  }
+  __syncthreads();
+  const int bits = (kind == BIN_K32) ? 32 : 64;
+  const Thresh th = radix_threshold(MemCols{lb.ckey, lb.cpv, eq16}, krem, eq16, bits, sh);
+  for (int i = threadIdx.x; i < eq16; i += T)
+    if (selected(th, lb.ckey[i], lb.cpv[i])) atomicOr(&lb.pick[lb.ccol[i] >> 5], 1u << (lb.ccol[i] & 31));
+  __syncthreads();
+  return true;
+}
+
+__device__ __forceinline__ bool large_kept(const LargeBuf& lb, const LargeSel& r, int c) {
+  if (r.none) return false;
+  if (r.all) return true;
+  const int b = lb.bin[c];
+  return b > r.t16 || (b == r.t16 && (r.all_eq || is_bit(lb.pick, c)));
+}
+
+// Columns whose keep(c) holds, each with its position pos(c) (read only for
+// kept columns), as emit_sorted's column set.
+template <class KeepF, class PosF>
+struct KeptCols {
+  int N;
+  KeepF keep;
+  PosF pos;
+  template <class F>
+  __device__ __forceinline__ void each(F f) const {
+    constexpr int LB = 8;   // positions of a batch of kept columns load together
+    for (int c0 = threadIdx.x; c0 < N; c0 += LB * T) {
+      bool kp[LB];
+      int32_t ps[LB];
+#pragma unroll
+      for (int u = 0; u < LB; ++u) {
+        const int c = c0 + u * T;
+        kp[u] = c < N && keep(c);
+        ps[u] = kp[u] ? pos(c) : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < LB; ++u)
+        if (kp[u]) f(c0 + u * T, 0ull, ps[u]);
+    }
+  }
+};
+template <class KeepF, class PosF>
+__device__ __forceinline__ KeptCols<KeepF, PosF> kept_cols(int N, KeepF keep, PosF pos) {
+  return KeptCols<KeepF, PosF>{N, keep, pos};
+}
+
 // ============================== ce_choose ========================================
 struct ChooseParams {
   const int32_t* pos;
@@ -283,6 +533,7 @@ struct ChooseParams {
   int sdt;
   const ce_row_params* params;
   int problems, layers, heads, head_offset, nw;
+  int large;   // the launch carries the large-segment shared-memory buffer
   int32_t* kept;
   int kept_stride;
   int32_t* status;
@@ -304,34 +555,36 @@ __device__ __forceinline__ bool choose_column(const ChooseParams& p, int i, int 
                                               int32_t& pv) {
   const int segs = p.layers * p.heads;
   const int pos = p.pos[base + c];
-  const bool pr = is_prot(pos, q);
-  pv = pos | (pr ? static_cast<int>(0x80000000u) : 0);
-  key = 0;
-  if (pr) return true;
+  // The score loads do not wait for the protection test, so a batch of
+  // columns has all its loads in flight at once.
+  uint64_t k = 0;
   switch (q.policy) {
     case CE_POLICY_RESERVOIR:
-      key = reservoir53(q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
+      k = reservoir53(q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
       break;
     case CE_POLICY_H2O_GLOBAL:
       if (p.sdt == CE_DTYPE_F64) {
         double acc = 0.0;
         for (int gg = 0; gg < p.heads; ++gg)
           acc += static_cast<const double*>(p.score)[(static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c];
-        key = key_from_f64(acc);
+        k = key_from_f64(acc);
       } else {
         float acc = 0.f;
         for (int gg = 0; gg < p.heads; ++gg)
           acc += static_cast<const float*>(p.score)[(static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c];
-        key = key_from_f32(acc);
+        k = key_from_f32(acc);
       }
       break;
     case CE_POLICY_PREFIX_SLIDING:
       break;
     default:
-      key = (p.sdt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.score)[base + c])
-                                    : key_from_f32(static_cast<const float*>(p.score)[base + c]);
+      k = (p.sdt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.score)[base + c])
+                                  : key_from_f32(static_cast<const float*>(p.score)[base + c]);
   }
-  return false;
+  const bool pr = is_prot(pos, q);
+  pv = pos | (pr ? static_cast<int>(0x80000000u) : 0);
+  key = pr ? 0 : k;
+  return pr;
 }
 
 template <class Cols>
@@ -360,6 +613,39 @@ __device__ void choose_body(const ChooseParams& p, const Cols& cols, int np, int
       sh, p.err);
 }
 
+// Large segments (see large_select); false = candidate overflow, nothing emitted.
+__device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, int64_t base,
+                             const ce_row_params& q, int N, Sh& sh, uint32_t* dyn) {
+  const int segs = p.layers * p.heads;
+  const LargeBuf lb = large_buf(dyn + 2 * p.nw);
+  const int kind = q.policy == CE_POLICY_RESERVOIR ? BIN_R53
+                   : p.sdt == CE_DTYPE_F64 ? (q.policy == CE_POLICY_RANDOM ? BIN_U64 : BIN_K64)
+                                           : BIN_K32;
+  auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool {
+    return choose_column(p, i, l, g, base, q, c, key, pv);
+  };
+  const int nprot = block_sum(large_scan(colfn, N, kind, lb), sh);
+  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * segs + s] = nprot;
+  if (nprot > q.budget) return true;
+  const int k = (q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : q.budget - nprot;
+  LargeSel sel;
+  if (!large_select(colfn, N, k, N - nprot, kind, lb, sh, sel)) return false;
+  int32_t* out = p.kept + (static_cast<int64_t>(i) * segs + s) * p.kept_stride;
+  const int stride = p.kept_stride;
+  int32_t* err = p.err;
+  const int32_t* pos = p.pos + base;
+  emit_sorted(
+      kept_cols(N, [&](int c) { return is_bit(lb.prot, c) || large_kept(lb, sel, c); },
+                [&](int c) { return pos[c]; }),
+      p.nw, dyn, reinterpret_cast<int*>(dyn + p.nw), [](int, uint64_t, int32_t pc) -> int { return pc; },
+      [&](int rank, int c, int) {
+        if (rank < stride) out[rank] = c;
+        else flag_error(err, CE_EW_CAPACITY);
+      },
+      sh, p.err);
+  return true;
+}
+
 __global__ void __launch_bounds__(T, 2) choose_seg_kernel(const ChooseParams p) {
   extern __shared__ uint32_t dyn[];
   __shared__ Sh sh;
@@ -380,6 +666,7 @@ __global__ void __launch_bounds__(T, 2) choose_seg_kernel(const ChooseParams p) 
       if (c < N) np += choose_column(p, i, l, g, base, q, c, cols.key[it], cols.pv[it]);
     }
     choose_body(p, cols, np, i, s, N, q, sh, dyn);
+  } else if (p.large && N <= LARGE_MAX && choose_large(p, i, l, g, s, base, q, N, sh, dyn)) {
   } else {
     uint64_t* kv = p.kv + base;
     int32_t* pv = p.pv + base;
@@ -433,6 +720,7 @@ struct BParams {
   const float* gscores;
   int GH;
   int live, max_cols, max_width, nw;
+  int large;   // the launch carries the large-segment shared-memory buffer
   // workspace
   uint64_t* kv;
   int32_t* pv;
@@ -492,23 +780,21 @@ __device__ __forceinline__ bool bsel_column(const BParams& p, const RowCtx& r, i
   const int LG = p.L * p.G;
   const int l = lg / p.G, g = lg % p.G;
   const int pos = col_pos(p, r, lg, c);
-  const bool pr = is_prot(pos, r.q);
-  pv = pos | (pr ? static_cast<int>(0x80000000u) : 0);
-  key = 0;
-  if (pr) return true;
+  // Score loads are issued before the protection test (see choose_column).
+  uint64_t k = 0;
   switch (r.q.policy) {
     case CE_POLICY_RANDOM: {
       const int64_t ui = (static_cast<int64_t>(i) * LG + lg) * p.max_cols + c;
-      key = (p.udt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.uniforms)[ui])
-                                    : key_from_f32(static_cast<const float*>(p.uniforms)[ui]);
+      k = (p.udt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.uniforms)[ui])
+                                  : key_from_f32(static_cast<const float*>(p.uniforms)[ui]);
       break;
     }
     case CE_POLICY_RESERVOIR:
-      key = reservoir53(r.q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
+      k = reservoir53(r.q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos));
       break;
     case CE_POLICY_HEAD_SUM:
     case CE_POLICY_HEAD_MAX:
-      key = key_from_f32(unit_score(p, l, g, col_unit(p, r, c)));
+      k = key_from_f32(unit_score(p, l, g, col_unit(p, r, c)));
       break;
     case CE_POLICY_H2O_GLOBAL: {
       float acc = 0.f;
@@ -519,35 +805,32 @@ __device__ __forceinline__ bool bsel_column(const BParams& p, const RowCtx& r, i
         const int u = col_unit(p, r, c);
         for (int gg = 0; gg < p.G; ++gg) acc += unit_score(p, l, gg, u);
       }
-      key = key_from_f32(acc);
+      k = key_from_f32(acc);
       break;
     }
     default:
       break;
   }
-  return false;
+  const bool pr = is_prot(pos, r.q);
+  pv = pos | (pr ? static_cast<int>(0x80000000u) : 0);
+  key = pr ? 0 : k;
+  return pr;
 }
 
-template <class Cols>
-__device__ void bsel_body(const BParams& p, const RowCtx& r, const Cols& cols, int np, int i, int lg,
-                          int64_t base, Sh& sh, uint32_t* bitsm, int* pre) {
-  const int LG = p.L * p.G;
+// Middle survivors (cols with posf(c, key, pv) >= 0) in ascending position,
+// then the protected part: this head's positions at the (0,0) head's
+// protected columns taken in (0,0) position order (runtime:442-443,469).
+template <class Cols, class PosF>
+__device__ void bsel_emit(const BParams& p, const RowCtx& r, const Cols& cols, PosF posf, int nprot,
+                          int i, int lg, int64_t base, Sh& sh, uint32_t* bitsm, int* pre) {
   const int l = lg / p.G, g = lg % p.G;
-  const int nprot = block_sum(np, sh);
-  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
-  if (nprot > r.q.budget) return;
-  const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
-  const int bits = key_bits_of(r.q.policy, p.udt);
-  const Thresh th = radix_threshold(cols, k, r.N - nprot, bits, sh);
   int32_t* mid = p.mid_col + base;
   int32_t* npos = p.new_pos + base;
   int32_t* srcu = p.src_unit + base;
   float* ssc = p.score_scr + base;
   const int max_cols = p.max_cols;
-  // Middle survivors in ascending position.
   emit_sorted(
-      cols, p.nw, bitsm, pre,
-      [&](int, uint64_t key, int32_t pc) -> int { return selected(th, key, pc) ? pc : -1; },
+      cols, p.nw, bitsm, pre, posf,
       [&](int rank, int c, int pos) {
         if (nprot + rank >= max_cols) return;
         mid[rank] = c;
@@ -557,8 +840,6 @@ __device__ void bsel_body(const BParams& p, const RowCtx& r, const Cols& cols, i
         ssc[rank] = unit_score(p, l, g, u);
       },
       sh, p.err);
-  // Protected part: this head's positions at the (0,0) head's protected
-  // columns taken in (0,0) position order (runtime:442-443,469).
   emit_sorted(
       RangeCols{r.N}, p.nw, bitsm, pre,
       [&](int c, uint64_t, int32_t) -> int {
@@ -569,6 +850,42 @@ __device__ void bsel_body(const BParams& p, const RowCtx& r, const Cols& cols, i
         if (rank < max_cols) npos[rank] = col_pos(p, r, lg, c);
       },
       sh, p.err);
+}
+
+template <class Cols>
+__device__ void bsel_body(const BParams& p, const RowCtx& r, const Cols& cols, int np, int i, int lg,
+                          int64_t base, Sh& sh, uint32_t* bitsm, int* pre) {
+  const int LG = p.L * p.G;
+  const int nprot = block_sum(np, sh);
+  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
+  if (nprot > r.q.budget) return;
+  const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
+  const int bits = key_bits_of(r.q.policy, p.udt);
+  const Thresh th = radix_threshold(cols, k, r.N - nprot, bits, sh);
+  bsel_emit(p, r, cols, [&](int, uint64_t key, int32_t pc) -> int { return selected(th, key, pc) ? pc : -1; },
+            nprot, i, lg, base, sh, bitsm, pre);
+}
+
+// Large segments (see large_select); false = candidate overflow, nothing emitted.
+__device__ bool bsel_large(const BParams& p, const RowCtx& r, int i, int lg, int64_t base, Sh& sh,
+                           uint32_t* bitsm, int* pre) {
+  const int LG = p.L * p.G;
+  const LargeBuf lb = large_buf(bitsm + 2 * p.nw);
+  const int kind = r.q.policy == CE_POLICY_RESERVOIR ? BIN_R53
+                   : (r.q.policy == CE_POLICY_RANDOM && p.udt == CE_DTYPE_F64) ? BIN_U64
+                                                                              : BIN_K32;
+  auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool { return bsel_column(p, r, i, lg, c, key, pv); };
+  const int nprot = block_sum(large_scan(colfn, r.N, kind, lb), sh);
+  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
+  if (nprot > r.q.budget) return true;
+  const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
+  LargeSel sel;
+  if (!large_select(colfn, r.N, k, r.N - nprot, kind, lb, sh, sel)) return false;
+  bsel_emit(p, r,
+            kept_cols(r.N, [&](int c) { return !is_bit(lb.prot, c) && large_kept(lb, sel, c); },
+                      [&](int c) { return col_pos(p, r, lg, c); }),
+            [](int, uint64_t, int32_t pc) -> int { return pc; }, nprot, i, lg, base, sh, bitsm, pre);
+  return true;
 }
 
 // Segment blocks: R*L*G of them, then R row blocks.
@@ -595,6 +912,7 @@ __global__ void __launch_bounds__(T, 2) bsel_kernel(const BParams p) {
         if (c < r.N) np += bsel_column(p, r, i, lg, c, cols.key[it], cols.pv[it]);
       }
       bsel_body(p, r, cols, np, i, lg, base, sh, bitsm, pre);
+    } else if (p.large && r.N <= LARGE_MAX && bsel_large(p, r, i, lg, base, sh, bitsm, pre)) {
     } else {
       uint64_t* kv = p.kv + base;
       int32_t* pv = p.pv + base;
@@ -947,6 +1265,7 @@ int64_t hazard_per_layer(int R, int G, int max_width, int P) {
 }
 
 int sel_smem(int nw) { return nw * 8; }
+constexpr int kLargeSmemMax = 220 * 1024;   // dynamic shared memory a large-segment launch may use
 }  // namespace
 
 extern "C" int64_t ce_choose_workspace_bytes(int32_t problems, int32_t segs, int32_t n_cols) {
@@ -996,7 +1315,8 @@ extern "C" int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_col
   p.seg_info = reinterpret_cast<int32_t*>(ws + a256(cells * 8) + a256(cells * 4));
   p.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int smem = sel_smem(nw);
+  p.large = n_cols > REG_ITEMS * T && sel_smem(nw) + LARGE_BYTES <= kLargeSmemMax;
+  const int smem = sel_smem(nw) + (p.large ? LARGE_BYTES : 0);
   if (!host::set_smem(choose_seg_kernel, smem)) return host::fail(CE_ERR_CUDA, "smem attr");
   choose_seg_kernel<<<problems * segs, T, smem, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("choose_seg_kernel");
@@ -1144,7 +1464,8 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   p.result = result;
   p.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int smem = sel_smem(nw);
+  p.large = max_cols > REG_ITEMS * T && sel_smem(nw) + LARGE_BYTES <= kLargeSmemMax;
+  const int smem = sel_smem(nw) + (p.large ? LARGE_BYTES : 0);
   if (!host::set_smem(bsel_kernel, smem)) return host::fail(CE_ERR_CUDA, "smem attr");
   if (cudaMemsetAsync(p.row_info, 0, sizeof(int32_t) * 8 * num_rows, st) != cudaSuccess)
     return host::fail_cuda("row_info memset");
