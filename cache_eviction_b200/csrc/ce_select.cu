@@ -289,6 +289,10 @@ constexpr int LARGE_MAX = 65536;
 constexpr int LHIST = 4096;
 constexpr int LCAND = 2048;
 constexpr int LARGE_BYTES = LARGE_MAX * 2 + 2 * (LARGE_MAX / 8) + LCAND * 16;  // 176 KB
+// Columns per thread whose loads are in flight together.  Large segments run
+// one CTA per SM (shared memory), so their kernel instance may use 128
+// registers and deep batches.
+constexpr int LARGE_LB = 16;
 static_assert(LHIST == 8 * T, "one thread scans 8 bins");
 enum BinKind { BIN_K32 = 0, BIN_K64 = 1, BIN_R53 = 2, BIN_U64 = 3 };
 
@@ -355,20 +359,55 @@ struct LargeSel {
 __device__ __forceinline__ bool is_bit(const uint32_t* m, int c) { return (m[c >> 5] >> (c & 31)) & 1u; }
 
 // Pass over the inputs: prefixes, protected bits, histogram; returns this
-// thread's protected count (the caller reduces it).
-template <class ColFn>
-__device__ int large_scan(ColFn colfn, int N, int kind, const LargeBuf& lb) {
+// thread's protected count (the caller reduces it).  With `vec`, col4fn
+// fills four consecutive columns from 16-byte loads (a quarter of the memory
+// requests of per-column loads, which is what bounds this pass); the tail
+// and the general case use colfn.
+constexpr int LQ = 4;   // quads per thread per batch
+template <class ColFn, class Col4Fn>
+__device__ int large_scan(ColFn colfn, Col4Fn col4fn, bool vec, int N, int kind, const LargeBuf& lb) {
   for (int i = threadIdx.x; i < LHIST; i += T) lb.hist[i] = 0;
   for (int i = threadIdx.x; i < (N + 31) / 32; i += T) {
     lb.prot[i] = 0u;
     lb.pick[i] = 0u;
   }
   __syncthreads();
-  // Batches of LB columns per thread: every column's loads are issued before
-  // the first one is used.
-  constexpr int LB = 8;
   int np = 0;
-  for (int c0 = threadIdx.x; c0 < N; c0 += LB * T) {
+  int cstart = 0;
+  if (vec) {
+    const int nq = N / 4;
+    for (int q0 = threadIdx.x; q0 < nq; q0 += LQ * T) {
+      uint64_t key[LQ][4];
+      int32_t pv[LQ][4];
+      bool pr[LQ][4];
+#pragma unroll
+      for (int u = 0; u < LQ; ++u)
+        if (q0 + u * T < nq) col4fn(4 * (q0 + u * T), key[u], pv[u], pr[u]);
+#pragma unroll
+      for (int u = 0; u < LQ; ++u) {
+        const int q = q0 + u * T;
+        if (q >= nq) continue;
+        uint32_t pm = 0u;
+        uint64_t packed = 0ull;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (pr[u][e]) {
+            ++np;
+            pm |= 1u << e;
+          } else {
+            const uint32_t b = bin16_of(key[u][e], kind);
+            packed |= static_cast<uint64_t>(b) << (16 * e);
+            atomicAdd(&lb.hist[b >> 4], 1);
+          }
+        }
+        *reinterpret_cast<uint64_t*>(lb.bin + 4 * q) = packed;
+        if (pm) atomicOr(&lb.prot[q >> 3], pm << (4 * (q & 7)));
+      }
+    }
+    cstart = 4 * nq;
+  }
+  constexpr int LB = LARGE_LB;
+  for (int c0 = cstart + threadIdx.x; c0 < N; c0 += LB * T) {
     uint64_t key[LB];
     int32_t pv[LB];
     bool pr[LB];
@@ -495,16 +534,45 @@ __device__ __forceinline__ bool large_kept(const LargeBuf& lb, const LargeSel& r
 }
 
 // Columns whose keep(c) holds, each with its position pos(c) (read only for
-// kept columns), as emit_sorted's column set.
-template <class KeepF, class PosF>
+// kept columns), as emit_sorted's column set.  With pos4 (vec), positions of
+// four consecutive columns come from one 16-byte load.
+template <class KeepF, class PosF, class Pos4F>
 struct KeptCols {
   int N;
   KeepF keep;
   PosF pos;
+  Pos4F pos4;
+  bool vec;
   template <class F>
   __device__ __forceinline__ void each(F f) const {
-    constexpr int LB = 8;   // positions of a batch of kept columns load together
-    for (int c0 = threadIdx.x; c0 < N; c0 += LB * T) {
+    int cstart = 0;
+    if (vec) {
+      const int nq = N / 4;
+      for (int q0 = threadIdx.x; q0 < nq; q0 += LQ * T) {
+        uint32_t km[LQ];
+        int4 ps[LQ];
+#pragma unroll
+        for (int u = 0; u < LQ; ++u) {
+          const int q = q0 + u * T;
+          km[u] = 0u;
+          if (q < nq)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) km[u] |= keep(4 * q + e) ? (1u << e) : 0u;
+          ps[u] = km[u] ? pos4(4 * q) : make_int4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < LQ; ++u) {
+          const int c = 4 * (q0 + u * T);
+          if (km[u] & 1u) f(c, 0ull, ps[u].x);
+          if (km[u] & 2u) f(c + 1, 0ull, ps[u].y);
+          if (km[u] & 4u) f(c + 2, 0ull, ps[u].z);
+          if (km[u] & 8u) f(c + 3, 0ull, ps[u].w);
+        }
+      }
+      cstart = 4 * nq;
+    }
+    constexpr int LB = LARGE_LB;   // positions of a batch of kept columns load together
+    for (int c0 = cstart + threadIdx.x; c0 < N; c0 += LB * T) {
       bool kp[LB];
       int32_t ps[LB];
 #pragma unroll
@@ -519,9 +587,10 @@ struct KeptCols {
     }
   }
 };
-template <class KeepF, class PosF>
-__device__ __forceinline__ KeptCols<KeepF, PosF> kept_cols(int N, KeepF keep, PosF pos) {
-  return KeptCols<KeepF, PosF>{N, keep, pos};
+template <class KeepF, class PosF, class Pos4F>
+__device__ __forceinline__ KeptCols<KeepF, PosF, Pos4F> kept_cols(int N, KeepF keep, PosF pos, Pos4F pos4,
+                                                                 bool vec) {
+  return KeptCols<KeepF, PosF, Pos4F>{N, keep, pos, pos4, vec};
 }
 
 // ============================== ce_choose ========================================
@@ -533,7 +602,7 @@ struct ChooseParams {
   int sdt;
   const ce_row_params* params;
   int problems, layers, heads, head_offset, nw;
-  int large;   // the launch carries the large-segment shared-memory buffer
+  int vec4;   // pos and score rows allow 16-byte loads of 4 columns
   int32_t* kept;
   int kept_stride;
   int32_t* status;
@@ -587,6 +656,62 @@ __device__ __forceinline__ bool choose_column(const ChooseParams& p, int i, int 
   return pr;
 }
 
+// Columns c..c+3 of the segment from 16-byte loads (c % 4 == 0; the caller
+// checked alignment): same keys as choose_column.
+__device__ __forceinline__ void choose_column4(const ChooseParams& p, int i, int l, int g, int64_t base,
+                                               const ce_row_params& q, int c, uint64_t (&key)[4],
+                                               int32_t (&pv)[4], bool (&pr)[4]) {
+  const int segs = p.layers * p.heads;
+  const int4 pp = *reinterpret_cast<const int4*>(p.pos + base + c);
+  const int pos[4] = {pp.x, pp.y, pp.z, pp.w};
+  uint64_t k[4] = {0ull, 0ull, 0ull, 0ull};
+  switch (q.policy) {
+    case CE_POLICY_RESERVOIR:
+#pragma unroll
+      for (int e = 0; e < 4; ++e) k[e] = reservoir53(q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos[e]));
+      break;
+    case CE_POLICY_H2O_GLOBAL:
+      if (p.sdt == CE_DTYPE_F64) {
+        double a[4] = {0.0, 0.0, 0.0, 0.0};
+        for (int gg = 0; gg < p.heads; ++gg) {
+          const double2* s2 = reinterpret_cast<const double2*>(
+              static_cast<const double*>(p.score) + (static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c);
+          const double2 x = s2[0], y = s2[1];
+          a[0] += x.x; a[1] += x.y; a[2] += y.x; a[3] += y.y;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) k[e] = key_from_f64(a[e]);
+      } else {
+        float a[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int gg = 0; gg < p.heads; ++gg) {
+          const float4 x = *reinterpret_cast<const float4*>(
+              static_cast<const float*>(p.score) + (static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c);
+          a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) k[e] = key_from_f32(a[e]);
+      }
+      break;
+    case CE_POLICY_PREFIX_SLIDING:
+      break;
+    default:
+      if (p.sdt == CE_DTYPE_F64) {
+        const double2* s2 = reinterpret_cast<const double2*>(static_cast<const double*>(p.score) + base + c);
+        const double2 x = s2[0], y = s2[1];
+        k[0] = key_from_f64(x.x); k[1] = key_from_f64(x.y); k[2] = key_from_f64(y.x); k[3] = key_from_f64(y.y);
+      } else {
+        const float4 x = *reinterpret_cast<const float4*>(static_cast<const float*>(p.score) + base + c);
+        k[0] = key_from_f32(x.x); k[1] = key_from_f32(x.y); k[2] = key_from_f32(x.z); k[3] = key_from_f32(x.w);
+      }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    pr[e] = is_prot(pos[e], q);
+    pv[e] = pos[e] | (pr[e] ? static_cast<int>(0x80000000u) : 0);
+    key[e] = pr[e] ? 0 : k[e];
+  }
+}
+
 template <class Cols>
 __device__ void choose_body(const ChooseParams& p, const Cols& cols, int np, int i, int s, int N,
                             const ce_row_params& q, Sh& sh, uint32_t* dyn) {
@@ -624,7 +749,10 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
   auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool {
     return choose_column(p, i, l, g, base, q, c, key, pv);
   };
-  const int nprot = block_sum(large_scan(colfn, N, kind, lb), sh);
+  auto col4fn = [&](int c, uint64_t(&key)[4], int32_t(&pv)[4], bool(&pr)[4]) {
+    choose_column4(p, i, l, g, base, q, c, key, pv, pr);
+  };
+  const int nprot = block_sum(large_scan(colfn, col4fn, p.vec4 != 0, N, kind, lb), sh);
   if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * segs + s] = nprot;
   if (nprot > q.budget) return true;
   const int k = (q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : q.budget - nprot;
@@ -636,7 +764,8 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
   const int32_t* pos = p.pos + base;
   emit_sorted(
       kept_cols(N, [&](int c) { return is_bit(lb.prot, c) || large_kept(lb, sel, c); },
-                [&](int c) { return pos[c]; }),
+                [&](int c) { return pos[c]; },
+                [&](int c) { return *reinterpret_cast<const int4*>(pos + c); }, p.vec4 != 0),
       p.nw, dyn, reinterpret_cast<int*>(dyn + p.nw), [](int, uint64_t, int32_t pc) -> int { return pc; },
       [&](int rank, int c, int) {
         if (rank < stride) out[rank] = c;
@@ -646,7 +775,11 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
   return true;
 }
 
-__global__ void __launch_bounds__(T, 2) choose_seg_kernel(const ChooseParams p) {
+// LARGE: the launch carries the large-segment shared-memory buffer (one CTA
+// per SM); otherwise two CTAs share an SM and large segments take the
+// general path.
+template <bool LARGE>
+__global__ void __launch_bounds__(T, LARGE ? 1 : 2) choose_seg_kernel(const ChooseParams p) {
   extern __shared__ uint32_t dyn[];
   __shared__ Sh sh;
   const int segs = p.layers * p.heads;
@@ -666,8 +799,12 @@ __global__ void __launch_bounds__(T, 2) choose_seg_kernel(const ChooseParams p) 
       if (c < N) np += choose_column(p, i, l, g, base, q, c, cols.key[it], cols.pv[it]);
     }
     choose_body(p, cols, np, i, s, N, q, sh, dyn);
-  } else if (p.large && N <= LARGE_MAX && choose_large(p, i, l, g, s, base, q, N, sh, dyn)) {
-  } else {
+    return;
+  }
+  if constexpr (LARGE) {
+    if (N <= LARGE_MAX && choose_large(p, i, l, g, s, base, q, N, sh, dyn)) return;
+  }
+  {
     uint64_t* kv = p.kv + base;
     int32_t* pv = p.pv + base;
     for (int c = threadIdx.x; c < N; c += T) np += choose_column(p, i, l, g, base, q, c, kv[c], pv[c]);
@@ -720,7 +857,6 @@ struct BParams {
   const float* gscores;
   int GH;
   int live, max_cols, max_width, nw;
-  int large;   // the launch carries the large-segment shared-memory buffer
   // workspace
   uint64_t* kv;
   int32_t* pv;
@@ -875,7 +1011,8 @@ __device__ bool bsel_large(const BParams& p, const RowCtx& r, int i, int lg, int
                    : (r.q.policy == CE_POLICY_RANDOM && p.udt == CE_DTYPE_F64) ? BIN_U64
                                                                               : BIN_K32;
   auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool { return bsel_column(p, r, i, lg, c, key, pv); };
-  const int nprot = block_sum(large_scan(colfn, r.N, kind, lb), sh);
+  auto col4fn = [](int, uint64_t(&)[4], int32_t(&)[4], bool(&)[4]) {};
+  const int nprot = block_sum(large_scan(colfn, col4fn, false, r.N, kind, lb), sh);
   if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
   if (nprot > r.q.budget) return true;
   const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
@@ -883,13 +1020,15 @@ __device__ bool bsel_large(const BParams& p, const RowCtx& r, int i, int lg, int
   if (!large_select(colfn, r.N, k, r.N - nprot, kind, lb, sh, sel)) return false;
   bsel_emit(p, r,
             kept_cols(r.N, [&](int c) { return !is_bit(lb.prot, c) && large_kept(lb, sel, c); },
-                      [&](int c) { return col_pos(p, r, lg, c); }),
+                      [&](int c) { return col_pos(p, r, lg, c); },
+                      [](int) { return make_int4(0, 0, 0, 0); }, false),
             [](int, uint64_t, int32_t pc) -> int { return pc; }, nprot, i, lg, base, sh, bitsm, pre);
   return true;
 }
 
 // Segment blocks: R*L*G of them, then R row blocks.
-__global__ void __launch_bounds__(T, 2) bsel_kernel(const BParams p) {
+template <bool LARGE>
+__global__ void __launch_bounds__(T, LARGE ? 1 : 2) bsel_kernel(const BParams p) {
   extern __shared__ uint32_t dyn[];
   __shared__ Sh sh;
   uint32_t* bitsm = dyn;
@@ -912,8 +1051,12 @@ __global__ void __launch_bounds__(T, 2) bsel_kernel(const BParams p) {
         if (c < r.N) np += bsel_column(p, r, i, lg, c, cols.key[it], cols.pv[it]);
       }
       bsel_body(p, r, cols, np, i, lg, base, sh, bitsm, pre);
-    } else if (p.large && r.N <= LARGE_MAX && bsel_large(p, r, i, lg, base, sh, bitsm, pre)) {
-    } else {
+      return;
+    }
+    if constexpr (LARGE) {
+      if (r.N <= LARGE_MAX && bsel_large(p, r, i, lg, base, sh, bitsm, pre)) return;
+    }
+    {
       uint64_t* kv = p.kv + base;
       int32_t* pv = p.pv + base;
       for (int c = threadIdx.x; c < r.N; c += T) np += bsel_column(p, r, i, lg, c, kv[c], pv[c]);
@@ -1315,10 +1458,17 @@ extern "C" int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_col
   p.seg_info = reinterpret_cast<int32_t*>(ws + a256(cells * 8) + a256(cells * 4));
   p.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  p.large = n_cols > REG_ITEMS * T && sel_smem(nw) + LARGE_BYTES <= kLargeSmemMax;
-  const int smem = sel_smem(nw) + (p.large ? LARGE_BYTES : 0);
-  if (!host::set_smem(choose_seg_kernel, smem)) return host::fail(CE_ERR_CUDA, "smem attr");
-  choose_seg_kernel<<<problems * segs, T, smem, st>>>(p);
+  const bool large = n_cols > REG_ITEMS * T && sel_smem(nw) + LARGE_BYTES <= kLargeSmemMax;
+  const int smem = sel_smem(nw) + (large ? LARGE_BYTES : 0);
+  p.vec4 = (n_cols % 4 == 0) && (reinterpret_cast<uintptr_t>(pos) % 16 == 0) &&
+           (reinterpret_cast<uintptr_t>(score) % 16 == 0);
+  if (large) {
+    if (!host::set_smem(choose_seg_kernel<true>, smem)) return host::fail(CE_ERR_CUDA, "smem attr");
+    choose_seg_kernel<true><<<problems * segs, T, smem, st>>>(p);
+  } else {
+    if (!host::set_smem(choose_seg_kernel<false>, smem)) return host::fail(CE_ERR_CUDA, "smem attr");
+    choose_seg_kernel<false><<<problems * segs, T, smem, st>>>(p);
+  }
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("choose_seg_kernel");
   choose_status_kernel<<<problems, 32, 0, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("choose_status_kernel");
@@ -1464,12 +1614,16 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   p.result = result;
   p.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  p.large = max_cols > REG_ITEMS * T && sel_smem(nw) + LARGE_BYTES <= kLargeSmemMax;
-  const int smem = sel_smem(nw) + (p.large ? LARGE_BYTES : 0);
-  if (!host::set_smem(bsel_kernel, smem)) return host::fail(CE_ERR_CUDA, "smem attr");
+  const bool large = max_cols > REG_ITEMS * T && sel_smem(nw) + LARGE_BYTES <= kLargeSmemMax;
+  const int smem = sel_smem(nw) + (large ? LARGE_BYTES : 0);
+  if (!host::set_smem(bsel_kernel<false>, smem) || !host::set_smem(bsel_kernel<true>, smem))
+    return host::fail(CE_ERR_CUDA, "smem attr");
   if (cudaMemsetAsync(p.row_info, 0, sizeof(int32_t) * 8 * num_rows, st) != cudaSuccess)
     return host::fail_cuda("row_info memset");
-  bsel_kernel<<<num_rows * layers * kv_heads + num_rows, T, smem, st>>>(p);
+  if (large)
+    bsel_kernel<true><<<num_rows * layers * kv_heads + num_rows, T, smem, st>>>(p);
+  else
+    bsel_kernel<false><<<num_rows * layers * kv_heads + num_rows, T, smem, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bsel_kernel");
   bvalidate_kernel<<<num_rows, 32, 0, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bvalidate_kernel");
