@@ -79,7 +79,7 @@ SIGNATURES = {
     "ce_boundary_workspace_bytes": (I64, [I32, I32, I32, I32, I32, I32, I32, I32, I64]),
     "ce_boundary": (C.c_int, [P, I64, I32, P, I64, I32, P, P, P, I64, I32, P, I64, I64, I64,
                               P, P, I32, I32, I32, I32, I32, P, I32, P, P, P, I32, P, I32, P,
-                              I32, I32, I32, I32, I32, P, P, I64, P, I64, I64, P, P]),
+                              I32, I32, I32, I32, I32, P, P, I64, P, I64, I64, P, I64, P, P, P]),
     "ce_gather_row_scores": (C.c_int, [P, I64, P, I64, P, P, P, I64, I64, I64, I32, I32, P,
                                        P, I32, I32, P, P, P]),
     "ce_reservoir_scores": (C.c_int, [P, I32, I32, I32, I32, U64, P, P]),

@@ -872,6 +872,9 @@ struct BParams {
   int32_t* freed;
   int64_t freed_stride;
   int32_t* result;
+  uint32_t* rec_delta;   // retention record or NULL
+  int64_t rec_stride;
+  int32_t* rec_counts;
   int32_t* err;
 };
 
@@ -1161,6 +1164,66 @@ __global__ void bvalidate_kernel(const BParams p) {
   res[1] = r.N;
   res[2] = (st == 0) ? after : (st == 2 ? info[1] : r.N);
   res[3] = 0;
+}
+
+// Retention record (runtime:465-467, 500-507): per (row, layer, KV head) the
+// positions of the columns this boundary evicts -- neither protected for this
+// head nor among its middle survivors -- in ascending order and delta-coded
+// (the first value is the position itself).  Runs after selection and before
+// bfinish rewrites the positions.  One block per segment.
+__global__ void __launch_bounds__(T) brecord_kernel(const BParams p) {
+  extern __shared__ uint32_t dyn[];
+  __shared__ Sh sh;
+  const int LG = p.L * p.G;
+  const int i = blockIdx.x / LG, lg = blockIdx.x % LG;
+  const int32_t* info = p.row_info + i * 8;
+  int32_t* cnt_out = p.rec_counts + static_cast<int64_t>(i) * LG + lg;
+  if (info[7] != 0) {
+    if (threadIdx.x == 0) *cnt_out = 0;
+    return;
+  }
+  const RowCtx r = row_ctx(p, i);
+  const int nprot = info[1], W = info[2];
+  const int64_t base = (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
+  uint32_t* bits = dyn;
+  int* pre = reinterpret_cast<int*>(dyn + p.nw);
+  uint32_t* kept = dyn + 2 * p.nw;
+  for (int w = threadIdx.x; w < (r.N + 31) / 32; w += T) kept[w] = 0u;
+  __syncthreads();
+  for (int c = threadIdx.x; c < r.N; c += T)
+    if (is_prot(col_pos(p, r, lg, c), r.q)) atomicOr(&kept[c >> 5], 1u << (c & 31));
+  for (int j = threadIdx.x; j < W; j += T) {
+    const int c = p.mid_col[base + j];
+    if (c >= 0 && c < r.N) atomicOr(&kept[c >> 5], 1u << (c & 31));
+  }
+  __syncthreads();
+  uint32_t* out = p.rec_delta + (static_cast<int64_t>(i) * LG + lg) * p.rec_stride;
+  const int64_t stride = p.rec_stride;
+  int32_t* err = p.err;
+  emit_sorted(
+      RangeCols{r.N}, p.nw, bits, pre,
+      [&](int c, uint64_t, int32_t) -> int { return is_bit(kept, c) ? -1 : col_pos(p, r, lg, c); },
+      [&](int rank, int, int pos) {
+        if (rank < stride) out[rank] = static_cast<uint32_t>(pos);
+        else flag_error(err, CE_EW_CAPACITY);
+      },
+      sh, p.err);
+  const int64_t nv64 = static_cast<int64_t>(r.N - nprot - W);
+  const int nv = static_cast<int>(nv64 < stride ? nv64 : stride);
+  if (threadIdx.x == 0) *cnt_out = nv;
+  // Delta-code in place, top chunk first, so every out[j - 1] is read before
+  // its own chunk is rewritten.
+  for (int top = nv; top > 0; top -= T) {
+    const int j = top - T + static_cast<int>(threadIdx.x);
+    uint32_t cur = 0u, prev = 0u;
+    if (j >= 0) {
+      cur = out[j];
+      prev = j ? out[j - 1] : 0u;
+    }
+    __syncthreads();
+    if (j >= 0) out[j] = cur - prev;
+    __syncthreads();
+  }
 }
 
 // One warp per (row, layer-in-group, head, j) item.
@@ -1560,10 +1623,13 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
                            const float* global_scores, int32_t global_heads, int32_t live,
                            int32_t max_cols, int32_t max_width, int32_t max_n, int32_t* result,
                            int32_t* freed_units, int64_t freed_stride, void* workspace,
-                           int64_t workspace_bytes, int64_t hazard_bytes, int32_t* err,
+                           int64_t workspace_bytes, int64_t hazard_bytes, uint32_t* record_delta,
+                           int64_t record_stride, int32_t* record_counts, int32_t* err,
                            void* stream) {
   if (num_rows < 0 || layers <= 0 || kv_heads <= 0 || max_cols < 0 || max_n < 0 || page_size <= 0)
     return host::fail(CE_ERR_ARG, "bad size");
+  if (record_delta && (!record_counts || record_stride < max_cols))
+    return host::fail(CE_ERR_ARG, "retention record needs counts and a row stride >= max_cols");
   if (head_dim != 64) return host::fail(CE_ERR_UNSUPPORTED, "head_dim must be 64");
   if (num_rows == 0) return CE_OK;
   if (!table || !req_to_unit || !frontier || !count || !pos || !scores || !k_layers || !v_layers ||
@@ -1612,6 +1678,9 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   p.freed = freed_units;
   p.freed_stride = freed_stride;
   p.result = result;
+  p.rec_delta = record_delta;
+  p.rec_stride = record_stride;
+  p.rec_counts = record_counts;
   p.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool large = max_cols > REG_ITEMS * T && sel_smem(nw) + LARGE_BYTES <= kLargeSmemMax;
@@ -1627,6 +1696,12 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bsel_kernel");
   bvalidate_kernel<<<num_rows, 32, 0, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bvalidate_kernel");
+  if (record_delta) {
+    const int rsmem = sel_smem(nw) + ((max_cols + 31) / 32) * 4;
+    if (!host::set_smem(brecord_kernel, rsmem)) return host::fail(CE_ERR_CUDA, "smem attr");
+    brecord_kernel<<<num_rows * layers * kv_heads, T, rsmem, st>>>(p);
+    if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("brecord_kernel");
+  }
   const int group = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(layers, hz / one)));
   const int nsm = host::sm_count();
   for (int l0 = 0; l0 < layers; l0 += group) {

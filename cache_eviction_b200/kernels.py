@@ -198,9 +198,12 @@ def layer_pointers(tensors: Sequence[torch.Tensor], device) -> torch.Tensor:
 def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, kv_heads, page_size,
              rows, params, max_cols, max_n, live, marks=None, epoch=0, swa=None, uniforms=None,
              global_scores=None, head_offset=0, freed=None, hazard_bytes=256 << 20, err=None,
-             max_width=0):
+             max_width=0, record=None):
     """One eviction boundary for a batch of rows (runtime:415-507).
 
+    record: None, or (delta [R * L * G, >= max_cols] int32 device tensor,
+    counts [R * L * G] int32) to receive the retention record
+    (runtime:465-467, 500-507; deltas are uint32 bit patterns).
     Returns (result [R, 4] int32 device tensor, freed [R, max_cols] int32).
     """
     lib = capi.load()
@@ -227,13 +230,14 @@ def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, k
         R, _p(uniforms), udt, _p(global_scores),
         global_scores.shape[2] if global_scores is not None else 0, 1 if live else 0, max_cols,
         int(max_width), int(max_n), _p(result), _p(freed), freed.stride(0), _p(ws), ws.numel(), int(hazard_bytes),
-        _p(err), _stream(dev))
+        _p(record[0]) if record else None, record[0].stride(0) if record else 0,
+        _p(record[1]) if record else None, _p(err), _stream(dev))
     capi.check(st, "ce_boundary")
     if R:
         width = max_width if 0 < max_width < max_cols else max_cols
         one = R * kv_heads * width * 2 * page_size * 128
         group = max(1, min(L, max(int(hazard_bytes), one) // max(one, 1)))
-        _count(3 + 2 * ceil_div(L, group))
+        _count(3 + 2 * ceil_div(L, group) + (1 if record else 0))
     return result, freed
 
 

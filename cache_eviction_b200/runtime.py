@@ -25,10 +25,15 @@ attention output together with the scores in one pass over K and V.
 """
 from __future__ import annotations
 
+import base64
+import gzip
+import json
 import logging
 import os
 import time
+from pathlib import Path
 
+import numpy as np
 import torch
 
 from . import capi, kernels
@@ -43,6 +48,27 @@ POS_CAP_DEFAULT = 32768
 
 def enabled() -> bool:
     return os.environ.get("GSTAR_EVICT") == "1"
+
+
+# ------------------------------------------------------------- payloads
+# The retention record's file format (runtime:59-73): gzip'd JSON with base64
+# arrays, one file per key, written atomically.  Serving the files over HTTP
+# is outside this path.
+def payload_dir() -> Path:
+    return Path(os.environ.get("GSTAR_PAYLOAD_DIR", "/tmp/gstar-payload"))
+
+
+def array(values, dtype):
+    data = np.ascontiguousarray(np.asarray(values, dtype=dtype))
+    return {"dtype": dtype, "shape": list(data.shape), "data": base64.b64encode(data.tobytes()).decode()}
+
+
+def write_payload(key, obj):
+    directory = payload_dir()
+    directory.mkdir(parents=True, exist_ok=True)
+    temporary = directory / f".{key}.tmp"
+    temporary.write_bytes(gzip.compress(json.dumps({"format": "gstar-payload-1", "key": key, **obj}).encode()))
+    temporary.rename(directory / f"{key}.json.gz")
 
 
 # ---------------------------------------------------------------- state
@@ -361,10 +387,14 @@ def _boundary(st, row, entry, n, cursor=None, allocator=None):
     params = kernels.row_params([dict(n=n_u, budget=budget, prefix=prefix, recent=recent,
                                       cursor=cur_u, policy=name, seed=int(cfg.get("seed", 0)))],
                                 st.device)
+    record = None
+    if cfg.get("record"):
+        record = (torch.empty((L * G, N), dtype=torch.int32, device=st.device),
+                  torch.empty(L * G, dtype=torch.int32, device=st.device))
     result, leftover = kernels.boundary(
         st.table, st.req_to_token, st.frontier, st.count, st.pos, st.scores, kptr, vptr, G, page,
         rows, params, N, n_u + 1, live, marks=st.marks, epoch=st.epoch, swa=swa,
-        uniforms=uniforms, head_offset=st.head_offset, err=st.err, max_width=budget)
+        uniforms=uniforms, head_offset=st.head_offset, err=st.err, max_width=budget, record=record)
     res = result[0].tolist()  # synchronises, as the reference does (runtime:474, 492)
     finished = time.perf_counter()
     status, before, after, nfreed = res
@@ -387,6 +417,30 @@ def _boundary(st, row, entry, n, cursor=None, allocator=None):
     elapsed = 1000 * (finished - started)
     entry["events"].append({"boundary": n, "before": before, "after": after, "freed": nfreed,
                             "swa_cursor": cursor, "ranking_ms": elapsed, "compaction_ms": 0.0})
+    if record is not None:
+        _write_record(st, entry, cfg, n, record)
+
+
+def _write_record(st, entry, cfg, n, record):
+    """Retention payload of one boundary (runtime:465-467, 500-507): victims
+    per (full layer, KV head), ascending, delta-coded.  With pages of P tokens
+    an evicted page stands for its P token positions (boundaries fall on
+    page multiples), so the record keeps the reference's token positions."""
+    counts = record[1].cpu().numpy()
+    delta = record[0].cpu().numpy().view(np.uint32)
+    P = st.page_size
+    lengths, deltas = [], []
+    for s, c in enumerate(counts):
+        victims = np.cumsum(delta[s, :c].astype(np.int64))
+        if P > 1:
+            victims = (victims[:, None] * P + np.arange(P)).ravel()
+        lengths.append(len(victims))
+        deltas.append(np.diff(victims, prepend=0))
+    write_payload(f"{entry['key']}-b{n}", {
+        "kind": "retention", "boundary": n, "cfg": cfg, "layers": st.full_layers,
+        "kv_heads": st.kv_heads,
+        "evicted_delta": array(np.concatenate(deltas) if deltas else np.zeros(0), "uint32"),
+        "evicted_counts": array(lengths, "int32")})
 
 
 # ------------------------------------------------------------ scheduler hooks

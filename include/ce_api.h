@@ -286,6 +286,14 @@ int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols,
  *           6 row sizes outside max_cols/max_n/pos_cap), columns before,
  *           residents after (the protected count when deferred), units freed
  *   freed_units [num_rows, freed_stride] leftover units (live only)
+ *   record_delta, record_counts  retention record (runtime:465-467, 500-507),
+ *           or NULL: for every evicted row and (layer, head) the positions of
+ *           the columns this boundary evicts, ascending and delta-coded (the
+ *           first value is the position itself), at
+ *           record_delta[(row * layers + layer) * kv_heads + head][...]
+ *           (row stride record_stride >= max_cols), and their number in
+ *           record_counts[(row * layers + layer) * kv_heads + head] (0 for
+ *           rows that did not evict)
  * hazard_bytes bounds the relocation scratch; layers are processed in groups
  * that fit it (at least one layer; query the minimum with layers = 1). */
 int64_t ce_boundary_workspace_bytes(int32_t num_rows, int32_t layers, int32_t kv_heads,
@@ -308,6 +316,7 @@ int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_width,
                 int32_t live, int32_t max_cols, int32_t max_width, int32_t max_n,
                 int32_t* result, int32_t* freed_units, int64_t freed_stride,
                 void* workspace, int64_t workspace_bytes, int64_t hazard_bytes,
+                uint32_t* record_delta, int64_t record_stride, int32_t* record_counts,
                 int32_t* err, void* stream);
 
 /* Dense per-column scores of the boundary rows, [num_rows, layers, heads,

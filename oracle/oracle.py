@@ -164,6 +164,28 @@ def prefill(q_bits, k_bits, qo_indptr, indptr, indices, tokens, sinks, modes, sc
     return scores
 
 
+def retention_record(pos_before, count_before, frontier_before, n, pos_after, count_after):
+    """Retention record of one row's boundary (runtime:465-467, 500-507).
+
+    pos_* [L, G, cap] int (the row's compacted positions before and after);
+    the columns before the boundary are the count_before compacted ones then
+    positions frontier_before .. n-1.  Victims of (layer, head) = positions
+    it held before and does not hold after, ascending; returns (deltas
+    uint32 concatenated over layer-major heads, first value of each head the
+    position itself; counts int32 [L * G])."""
+    L, G = pos_before.shape[:2]
+    tail = np.arange(frontier_before, n, dtype=np.int64)
+    deltas, counts = [], []
+    for l in range(L):
+        for g in range(G):
+            before = np.concatenate([np.asarray(pos_before[l, g, :count_before], np.int64), tail])
+            v = np.setdiff1d(before, np.asarray(pos_after[l, g, :count_after], np.int64))
+            counts.append(len(v))
+            deltas.append(np.diff(v, prepend=0))
+    d = np.concatenate(deltas) if deltas else np.zeros(0, np.int64)
+    return d.astype(np.uint32), np.array(counts, np.int32)
+
+
 def choose(pos, score, params, layers, heads, ncols=None, head_offset=0, kept_stride=None,
            score_is_f32=False):
     """ce_choose restated (runtime:376-412): returns (kept cols, status, protected_count)."""

@@ -165,6 +165,44 @@ def gen_boundaries(rt, core):
     np.savez_compressed(HERE / "boundary.npz", **out)
 
 
+RECORD_NAMES = ("head_sum_2048", "random_reservoir_2048", "random_2048", "prefix_sliding_2048")
+
+
+def gen_records(rt, core):
+    """Retention records (runtime:465-467, 500-507) of the check_boundaries
+    scenario with record=True, captured from the reference's write_payload."""
+    import base64
+    out = {}
+    setup = sc.boundary_setup()
+    n = setup["n"]
+    captured = []
+    orig_write = rt.write_payload
+    rt.write_payload = lambda key, obj: captured.append((key, obj))
+    for name in RECORD_NAMES:
+        rt.STATE = None
+        b, keys, values = make_backend(setup)
+        st = rt.state(b)
+        slot_of = torch.from_numpy(setup["slot_of"])
+        st.req_to_token[1, :n] = slot_of.int()
+        st.scores[:, :, slot_of] = torch.from_numpy(setup["score"])
+        cfg = dict(sc.boundary_cfg(name), record=True)
+        entry = rt._live_entry(SimpleNamespace(rid="r", session=None), cfg, "live")
+        alloc = SimpleNamespace(free_full=lambda s_: None,
+                                full_to_swa_index_mapping=torch.zeros(setup["slots"], dtype=torch.int64))
+        captured.clear()
+        for k, boundary in enumerate((2048, 4096)):
+            rt._boundary(st, 1, entry, boundary, boundary - 200, alloc)
+        assert [key for key, _ in captured] == ["r-b2048", "r-b4096"], captured
+        for k, (_, obj) in enumerate(captured):
+            assert obj["kind"] == "retention" and obj["kv_heads"] == 8 and obj["layers"] == list(sc.FULL)
+            for field, dt in (("evicted_delta", np.uint32), ("evicted_counts", np.int32)):
+                a = obj[field]
+                assert a["dtype"] == np.dtype(dt).name
+                out[f"{name}_b{k}_{field}"] = np.frombuffer(base64.b64decode(a["data"]), dt).copy()
+    rt.write_payload = orig_write
+    np.savez_compressed(HERE / "records.npz", **out)
+
+
 def gen_decode(rt):
     d = sc.decode_setup()
     keys = bf16_tensor(d["keys"]).float()
@@ -209,6 +247,7 @@ def main():
     gen_choose(rt)
     gen_reservoir(rt, core)
     gen_boundaries(rt, core)
+    gen_records(rt, core)
     gen_decode(rt)
     gen_prefill(rt)
     for f in sorted(HERE.glob("*.npz")):

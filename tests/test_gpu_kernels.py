@@ -281,7 +281,7 @@ def _gpu_state(state, kl, vl):
 
 
 def _gpu_boundary(g, rows, params, max_cols, max_n, live, epoch, uniforms=None, swa=None,
-                  hazard_bytes=256 << 20, page=1, max_width=0):
+                  hazard_bytes=256 << 20, page=1, max_width=0, record=None):
     kern = K()
     err = kern.error_word(DEV)
     res, freed = kern.boundary(g["table"], g["r2u"], g["frontier"], g["count"], g["pos"], g["scores"],
@@ -289,9 +289,49 @@ def _gpu_boundary(g, rows, params, max_cols, max_n, live, epoch, uniforms=None, 
                                torch.tensor(rows, dtype=torch.int32, device=DEV),
                                kern.row_params(params, DEV), max_cols, max_n, live, marks=g["marks"],
                                epoch=epoch, uniforms=uniforms, swa=swa, hazard_bytes=hazard_bytes,
-                               err=err, max_width=max_width)
+                               err=err, max_width=max_width, record=record)
     torch.cuda.synchronize()
     return res.cpu().numpy(), freed.cpu().numpy(), int(err.item())
+
+
+def _record_buffers(rows, L, G, max_cols):
+    return (torch.full((rows * L * G, max_cols), -1, dtype=torch.int32, device=DEV),
+            torch.full((rows * L * G,), -1, dtype=torch.int32, device=DEV))
+
+
+def _record_of_row(record, r, L, G):
+    """(deltas uint32 concatenated over layer-major heads, counts) of row r."""
+    delta, counts = record[0].cpu().numpy().view(np.uint32), record[1].cpu().numpy()
+    segs = range(r * L * G, (r + 1) * L * G)
+    return (np.concatenate([delta[s, :counts[s]] for s in segs]), counts[r * L * G:(r + 1) * L * G])
+
+
+RECORD_NAMES = ("head_sum_2048", "random_reservoir_2048", "random_2048", "prefix_sliding_2048")
+
+
+@pytest.mark.parametrize("name", RECORD_NAMES)
+def test_boundary_record_reference_golden(name):
+    """Retention records of the reference test's scenario (record=True),
+    bit for bit against the records the reference itself wrote."""
+    rec = np.load(GOLD / "records.npz")
+    setup = sc.boundary_setup()
+    state, kl, vl = boundary_state(setup)
+    g = _gpu_state(state, kl, vl)
+    max_cols = 4096
+    for k, b in enumerate((2048, 4096)):
+        N = int(g["count"][1]) + b - int(g["frontier"][1])
+        uni = None
+        if name == "random_2048":
+            u = np.zeros((1, 2, sc.G, max_cols))
+            u[0, :, :, :N] = sc.random_uniforms(4, b, (2, sc.G, N))
+            uni = torch.from_numpy(u).to(DEV)
+        record = _record_buffers(1, 2, sc.G, max_cols)
+        res, _, err = _gpu_boundary(g, [1], [boundary_row(name, b)], max_cols, setup["n"] + 1, True,
+                                    epoch=k + 1, uniforms=uni, record=record)
+        assert err == 0 and res[0, 0] == 0, (res, hex(err))
+        d, c = _record_of_row(record, 0, 2, sc.G)
+        np.testing.assert_array_equal(c, rec[f"{name}_b{k}_evicted_counts"])
+        np.testing.assert_array_equal(d, rec[f"{name}_b{k}_evicted_delta"])
 
 
 @pytest.mark.parametrize("name,kind", sc.BOUNDARY_NAMES)
@@ -365,14 +405,26 @@ def test_boundary_paged_multirow_vs_oracle(policy):
         if policy == "random_2048":
             u = rng.random((rows, L, G, max_cols))
             uni = u
+        before = {k: state[k].copy() for k in ("pos", "count", "frontier")}
         res_c, fr_c = oracle.boundary(state, kl, vl, list(range(rows)), oracle.row_params(params),
                                       max_cols, live=True, uniforms=uni)
         epoch += 1
+        record = _record_buffers(rows, L, G, max_cols)
         res_g, fr_g, err = _gpu_boundary(g, list(range(rows)), params, max_cols, n + 1, True, epoch,
                                          uniforms=None if uni is None else torch.from_numpy(uni).to(DEV),
-                                         page=page, max_width=max(budgets), hazard_bytes=1)
+                                         page=page, max_width=max(budgets), hazard_bytes=1, record=record)
         assert err == 0, hex(err)
         np.testing.assert_array_equal(res_g, res_c)
+        for r in range(rows):
+            d, c = _record_of_row(record, r, L, G)
+            if res_c[r, 0] != 0:
+                assert not c.any()
+                continue
+            dw, cw = oracle.retention_record(before["pos"][r], int(before["count"][r]),
+                                             int(before["frontier"][r]), n, state["pos"][r],
+                                             int(state["count"][r]))
+            np.testing.assert_array_equal(c, cw)
+            np.testing.assert_array_equal(d, dw)
         for r in range(rows):
             np.testing.assert_array_equal(fr_g[r, :res_c[r, 3]], fr_c[r, :res_c[r, 3]])
         for key in ("table", "r2u", "frontier", "count", "pos", "scores"):

@@ -346,3 +346,49 @@ def test_after_extend_scores_h2o_rows(_setup):
             expected[FULL.index(layer_id)][:, slots] += red
     torch.testing.assert_close(st.scores, expected, rtol=1e-3, atol=1e-5)
     assert int(st.err.item()) == 0
+
+
+def _read_payload(directory, key):
+    import base64
+    import gzip
+    import json
+    obj = json.loads(gzip.decompress((directory / f"{key}.json.gz").read_bytes()))
+    dec = lambda a: np.frombuffer(base64.b64decode(a["data"]), a["dtype"])
+    return obj, dec(obj["evicted_delta"]), dec(obj["evicted_counts"])
+
+
+@pytest.mark.parametrize("name", ["head_sum_2048", "random_reservoir_2048", "random_2048"])
+def test_retention_records_are_written_and_decode_to_the_kept_sets(_setup, name, tmp_path, monkeypatch):
+    """cfg record=True (runtime:465-467, 500-507): one payload per evicting
+    boundary; replaying the records like the reference's client
+    (sglang_client.py:115-133) rebuilds every head's held positions."""
+    monkeypatch.setenv("GSTAR_PAYLOAD_DIR", str(tmp_path))
+    ge = _setup
+    b = backend()
+    st = ge.state(b)
+    n, budget = 4096 + 300, 1024
+    slot_of = torch.randperm(19000, device="cuda")[:n] + 1
+    st.req_to_token[1, :n] = slot_of.int()
+    st.scores[:, :, slot_of] = torch.rand((2, 8, n), device="cuda")
+    cfg = {"name": name, "budget": budget, "prefix": budget // 4, "recent": budget // 4, "seed": 4,
+           "record": True}
+    e = ge._live_entry(SimpleNamespace(rid="req7", session=None), cfg, "live")
+    freed, alloc = allocator()
+    held, last = None, 0
+    for boundary in (2048, 4096):
+        before = (st.pos[1].cpu().numpy().copy(), e["count"], e["frontier"])
+        ge._boundary(st, 1, e, boundary, boundary - 200, alloc)
+        obj, delta, counts = _read_payload(tmp_path, f"req7-b{boundary}")
+        assert obj["kind"] == "retention" and obj["boundary"] == boundary and obj["kv_heads"] == 8
+        assert obj["format"] == "gstar-payload-1" and obj["cfg"]["record"] is True
+        dw, cw = oracle.retention_record(before[0], before[1], before[2], boundary,
+                                         st.pos[1].cpu().numpy(), e["count"])
+        np.testing.assert_array_equal(counts, cw)
+        np.testing.assert_array_equal(delta, dw)
+        evicted = np.split(delta.astype(np.int64), np.cumsum(counts)[:-1])
+        new = np.arange(last, boundary)
+        held = [new.copy() for _ in counts] if held is None else [np.concatenate((h, new)) for h in held]
+        held = [np.setdiff1d(h, np.cumsum(v), assume_unique=True) for h, v in zip(held, evicted)]
+        last = boundary
+        for s, h in enumerate(held):
+            np.testing.assert_array_equal(np.sort(e["pos"][s // 8, s % 8].cpu().numpy()), h)

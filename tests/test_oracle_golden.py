@@ -133,6 +133,25 @@ def test_prefill_matches_reference(page, mode):
     np.testing.assert_allclose(scores, want, rtol=2e-5, atol=1e-6)
 
 
+RECORD_NAMES = ("head_sum_2048", "random_reservoir_2048", "random_2048", "prefix_sliding_2048")
+
+
+@pytest.mark.parametrize("name", RECORD_NAMES)
+def test_retention_record_matches_reference(name):
+    """The oracle's record, rebuilt from the reference's own positions before
+    and after each boundary, equals the record the reference wrote."""
+    rec = np.load(GOLD / "records.npz")
+    bnd = np.load(GOLD / "boundary.npz")
+    key = f"{name}_live"
+    prev, prev_count, prev_frontier = np.zeros((2, sc.G, 0), np.int32), 0, 0
+    for k, b in enumerate((2048, 4096)):
+        after = bnd[f"{key}_b{k}_pos"]
+        d, c = oracle.retention_record(prev, prev_count, prev_frontier, b, after, after.shape[-1])
+        np.testing.assert_array_equal(c, rec[f"{name}_b{k}_evicted_counts"])
+        np.testing.assert_array_equal(d, rec[f"{name}_b{k}_evicted_delta"])
+        prev, prev_count, prev_frontier = after, after.shape[-1], b
+
+
 def test_fill_reference_golden():
     # code/tests/test_sglang_evict.py:80-90
     table = np.zeros((4, 16), np.int32)
