@@ -73,6 +73,8 @@ SIGNATURES = {
     "ce_prefill_workspace_bytes": (I64, [I32, I32]),
     "ce_prefill_scores": (C.c_int, [P, I64, I64, P, I64, P, P, P, P, I64, P, P, P, F32, I32, I32,
                                     I32, I32, I32, I32, I32, I32, P, I64, I32, P, I64, P, P]),
+    "ce_prefill_lost": (C.c_int, [P, I64, I64, P, I64, P, P, P, P, I64, P, F32, I32, I32, I32, I32,
+                                  I32, I32, I32, P, I32, I64, P, I64, F32, P, I64, P, P]),
     "ce_choose_workspace_bytes": (I64, [I32, I32, I32]),
     "ce_choose": (C.c_int, [P, P, I32, P, I32, P, I32, I32, I32, I32, I32, P, I32, P, P, P,
                             I64, P, P]),

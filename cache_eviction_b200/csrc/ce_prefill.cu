@@ -84,8 +84,18 @@ struct Params {
   float* lse2;    // [total_q, H] log2-domain normalizer incl. sink
   int total_q, max_q, max_tokens;
   int64_t kv_capacity;
+  // lost-mass pass: evicted bits [S][G][lost_words] (bit set = key evicted by
+  // spec s for KV head g), lost [S][lost_stride] accumulated per query
+  const uint32_t* lost_bits;
+  int64_t lost_words, lost_stride;
+  int S;
+  float lost_scale;
+  float* lost;
+  int all_entries;   // run every entry regardless of its score mode
   int32_t* err;
 };
+
+constexpr int MAX_SPECS = 8;
 
 // Barriers and flags after the tiles in shared memory.
 struct Sync {
@@ -257,12 +267,17 @@ __device__ __forceinline__ void teardown(Sync* sy, uint32_t tmem) {
 // ---------------------------------------------------------------- pass 1
 // CTA (query tile x, KV head g, entry b); accumulator row r = query
 // 16x + r / 8, head g*8 + r % 8.
+// LOST = false: row normalisers into p.lse2.  LOST = true (the lost-mass
+// diagnostic, runtime:587-613): the same S tiles again with the normalisers
+// known; each row sums p over the keys every spec evicted, the 8 rows of a
+// query are reduced, and lost[s][query] += that sum * lost_scale.
+template <bool LOST>
 __global__ void __launch_bounds__(THREADS, 2) lse_kernel(const Params p,
                                                           const __grid_constant__ CUtensorMap qmap,
                                                           const __grid_constant__ CUtensorMap kmap) {
   const int b = blockIdx.z, g = blockIdx.y;
   const int mode = entry_mode(p, b);
-  if (mode != CE_MODE_SUM && mode != CE_MODE_MAX) return;
+  if (!LOST && !p.all_entries && mode != CE_MODE_SUM && mode != CE_MODE_MAX) return;
   int qbeg, nq, ntok, list0;
   if (!entry_ok(p, b, qbeg, nq, ntok, list0)) return;
   const int q0 = blockIdx.x * QT;
@@ -358,6 +373,13 @@ __global__ void __launch_bounds__(THREADS, 2) lse_kernel(const Params p,
     const int h = g * GROUP + r % GROUP;
     const int lim = prefix + min(q, nq - 1);   // last visible list token of this row
     float m = -INFINITY, l = 0.f;
+    float lost[MAX_SPECS];
+    float lse_row = INFINITY;
+    if constexpr (LOST) {
+#pragma unroll
+      for (int x = 0; x < MAX_SPECS; ++x) lost[x] = 0.f;
+      if (q < nq) lse_row = p.lse2[static_cast<int64_t>(qbeg + q) * p.H + h];
+    }
     for (int t = 0; t < ntiles; ++t) {
       const int buf = t & 1;
       if (!warp_wait(&sy->acc_full[buf], (t >> 1) & 1, p.err, abort, lane)) {
@@ -375,6 +397,25 @@ __global__ void __launch_bounds__(THREADS, 2) lse_kernel(const Params p,
       __syncwarp();
       if (lane == 0) mbar_arrive(&sy->acc_empty[buf]);  // the values are in registers
       const int kb = t * BN + half * 64;
+      if constexpr (LOST) {
+        // kb is a multiple of 64: the 64 keys are two whole mask words per spec
+#pragma unroll
+        for (int x = 0; x < MAX_SPECS; ++x) {
+          if (x >= p.S) break;
+          const uint32_t* w = p.lost_bits + (static_cast<int64_t>(x) * p.G + g) * p.lost_words + kb / 32;
+          const uint32_t w0 = (kb / 32 < p.lost_words) ? w[0] : 0u;
+          const uint32_t w1 = (kb / 32 + 1 < p.lost_words) ? w[1] : 0u;
+          if (!(w0 | w1)) continue;
+          float acc = 0.f;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            const bool ev = ((i < 32 ? w0 >> i : w1 >> (i - 32)) & 1u) && kb + i <= lim;
+            acc += ev ? fast_exp2(fmaf(v[i], p.scale2, -lse_row)) : 0.f;
+          }
+          lost[x] += acc;
+        }
+        continue;
+      }
       if (kb + 63 > lim) {
 #pragma unroll
         for (int i = 0; i < 64; ++i) v[i] = (kb + i <= lim) ? v[i] : -INFINITY;
@@ -395,12 +436,25 @@ __global__ void __launch_bounds__(THREADS, 2) lse_kernel(const Params p,
         m = mn;
       }
     }
-    if (half == 1) {
+    if constexpr (LOST) {
+      // The 8 rows of a query are 8 consecutive lanes of this warp.
+#pragma unroll
+      for (int x = 0; x < MAX_SPECS; ++x) {
+        if (x >= p.S) break;
+        float v = lost[x];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        if ((lane & 7) == 0 && q < nq && !*abort)
+          atomicAdd(p.lost + static_cast<int64_t>(x) * p.lost_stride + q, v * p.lost_scale);
+      }
+    }
+    if (LOST || half == 1) {
       sy->part[0][r] = m;
       sy->part[1][r] = l;
     }
     named_barrier_epi();
-    if (half == 0 && !*abort && q < nq) {
+    if (!LOST && half == 0 && !*abort && q < nq) {
       const float m1 = sy->part[0][r], l1 = sy->part[1][r];
       const float M = fmaxf(m, m1);  // finite: key 0 is in every row's first half
       const float L = l * fast_exp2(m - M) + l1 * fast_exp2(m1 - M);
@@ -600,66 +654,60 @@ extern "C" int64_t ce_prefill_workspace_bytes(int32_t total_q, int32_t num_q_hea
   return static_cast<int64_t>(total_q > 0 ? total_q : 1) * num_q_heads * 4 + 256;
 }
 
-extern "C" int ce_prefill_scores(const void* q, int64_t q_st, int64_t q_sh, const void* k_pool,
-                                 int64_t pool_units, const int32_t* qo_indptr,
-                                 const int32_t* kv_indptr, const int32_t* kv_indices,
-                                 const int32_t* kv_tokens, int64_t kv_capacity, const float* sinks,
-                                 const int32_t* mode_of_row, const int64_t* rows, float sm_scale,
-                                 int32_t bs, int32_t num_q_heads, int32_t num_kv_heads,
-                                 int32_t head_dim, int32_t page_size, int32_t total_q,
-                                 int32_t max_q, int32_t max_tokens, float* scores,
-                                 int64_t score_sg, int32_t zero_new, void* workspace,
-                                 int64_t workspace_bytes, int32_t* err, void* stream) {
+namespace {
+
+// Validation, tensor maps and parameters shared by the two entry points.
+int prefill_prepare(const void* q, int64_t q_st, int64_t q_sh, const void* k_pool, int64_t pool_units,
+                    const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
+                    const int32_t* kv_tokens, int64_t kv_capacity, const float* sinks,
+                    const int32_t* mode_of_row, const int64_t* rows, float sm_scale, int32_t bs,
+                    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                    int32_t total_q, int32_t max_q, int32_t max_tokens, float* scores, int64_t score_sg,
+                    int32_t zero_new, void* workspace, int64_t workspace_bytes, int32_t* err,
+                    ce::prefill::Params& p, CUtensorMap& qmap, CUtensorMap& lmap, CUtensorMap& kmap) {
   using namespace ce::prefill;
   if (bs < 0 || total_q < 0 || max_q < 0 || max_tokens < 0 || pool_units <= 0 || kv_capacity < 0)
-    return host::fail(CE_ERR_ARG, "ce_prefill_scores: negative size");
-  if (!(sm_scale > 0.f)) return host::fail(CE_ERR_ARG, "ce_prefill_scores: sm_scale must be positive");
+    return host::fail(CE_ERR_ARG, "ce_prefill: negative size");
+  if (!(sm_scale > 0.f)) return host::fail(CE_ERR_ARG, "ce_prefill: sm_scale must be positive");
   if (head_dim != D || num_kv_heads <= 0 || num_q_heads != GROUP * num_kv_heads)
-    return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill_scores: needs head_dim 64 and 8 query heads per KV head");
+    return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill: needs head_dim 64 and 8 query heads per KV head");
   if (page_size <= 0 || page_size > 64 || 64 % page_size != 0)
-    return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill_scores: page_size must divide 64");
+    return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill: page_size must divide 64");
   if (q_sh % 8 != 0 || q_st % 8 != 0 || q_sh < D || q_st < static_cast<int64_t>(num_q_heads) * q_sh)
-    return host::fail(CE_ERR_ARG, "ce_prefill_scores: q strides must be multiples of 8 elements");
-  if (bs == 0 || max_q == 0 || mode_of_row == nullptr || total_q == 0) return CE_OK;
-  if (!q || !k_pool || !qo_indptr || !kv_indptr || !kv_indices || !kv_tokens || !scores)
-    return host::fail(CE_ERR_ARG, "ce_prefill_scores: null pointer");
-  if (score_sg < pool_units)
-    return host::fail(CE_ERR_ARG, "ce_prefill_scores: score head stride below pool_units");
-  if (bs > 65535) return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill_scores: more than 65535 entries");
+    return host::fail(CE_ERR_ARG, "ce_prefill: q strides must be multiples of 8 elements");
+  if (bs == 0 || max_q == 0 || total_q == 0) return 1;   // nothing to do
+  if (!q || !k_pool || !qo_indptr || !kv_indptr || !kv_indices || !kv_tokens)
+    return host::fail(CE_ERR_ARG, "ce_prefill: null pointer");
+  if (bs > 65535) return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill: more than 65535 entries");
   if (pool_units * num_kv_heads * page_size > INT32_MAX)
-    return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill_scores: pool rows exceed 2^31");
+    return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill: pool rows exceed 2^31");
   const int64_t need = ce_prefill_workspace_bytes(total_q, num_q_heads);
   if (!workspace || workspace_bytes < need)
-    return host::fail(CE_ERR_WORKSPACE, "ce_prefill_scores: workspace too small");
+    return host::fail(CE_ERR_WORKSPACE, "ce_prefill: workspace too small");
   if ((reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(k_pool) & 15) ||
       (reinterpret_cast<uintptr_t>(workspace) & 15))
-    return host::fail(CE_ERR_ARG, "ce_prefill_scores: q, k_pool and workspace need 16-byte alignment");
-
-  // Q as [total_q][H][64] with byte strides; box = 16 queries x 8 heads x 64.
-  CUtensorMap qmap, lmap;
+    return host::fail(CE_ERR_ARG, "ce_prefill: q, k_pool and workspace need 16-byte alignment");
   {
+    // Q as [total_q][H][64] with byte strides; box = 16 queries x 8 heads x 64.
     const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(num_q_heads),
                               static_cast<uint64_t>(total_q)};
     const uint64_t strides[2] = {static_cast<uint64_t>(q_sh) * 2, static_cast<uint64_t>(q_st) * 2};
     const uint32_t box[3] = {static_cast<uint32_t>(D), GROUP, QT};
     if (!host::encode_map(&qmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims, strides, box, true))
-      return host::fail(CE_ERR_CUDA, "ce_prefill_scores: query tensor map");
+      return host::fail(CE_ERR_CUDA, "ce_prefill: query tensor map");
   }
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(num_q_heads), static_cast<uint64_t>(total_q)};
     const uint64_t strides[1] = {static_cast<uint64_t>(num_q_heads) * 4};
     const uint32_t box[2] = {GROUP, QT};
     if (!host::encode_map(&lmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, workspace, dims, strides, box, false))
-      return host::fail(CE_ERR_CUDA, "ce_prefill_scores: normalizer tensor map");
+      return host::fail(CE_ERR_CUDA, "ce_prefill: normalizer tensor map");
   }
-
   // K pool as [units * G * page, 64] rows; box = one page of one head.
-  CUtensorMap kmap;
   if (!host::encode_rows_map(&kmap, k_pool, static_cast<uint64_t>(pool_units) * num_kv_heads * page_size,
                              D, static_cast<uint32_t>(page_size)))
-    return host::fail(CE_ERR_CUDA, "ce_prefill_scores: key tensor map");
-
-  Params p;
+    return host::fail(CE_ERR_CUDA, "ce_prefill: key tensor map");
+  p = Params{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.q_st = q_st;
   p.q_sh = q_sh;
@@ -685,15 +733,82 @@ extern "C" int ce_prefill_scores(const void* q, int64_t q_st, int64_t q_sh, cons
   p.max_tokens = max_tokens;
   p.kv_capacity = kv_capacity;
   p.err = err;
+  if (!host::set_smem(lse_kernel<false>, L_SMEM) || !host::set_smem(lse_kernel<true>, L_SMEM) ||
+      !host::set_smem(colsum_kernel, C_SMEM))
+    return host::fail(CE_ERR_CUDA, "ce_prefill: smem attr");
+  return CE_OK;
+}
+
+}  // namespace
+
+extern "C" int ce_prefill_scores(const void* q, int64_t q_st, int64_t q_sh, const void* k_pool,
+                                 int64_t pool_units, const int32_t* qo_indptr,
+                                 const int32_t* kv_indptr, const int32_t* kv_indices,
+                                 const int32_t* kv_tokens, int64_t kv_capacity, const float* sinks,
+                                 const int32_t* mode_of_row, const int64_t* rows, float sm_scale,
+                                 int32_t bs, int32_t num_q_heads, int32_t num_kv_heads,
+                                 int32_t head_dim, int32_t page_size, int32_t total_q,
+                                 int32_t max_q, int32_t max_tokens, float* scores,
+                                 int64_t score_sg, int32_t zero_new, void* workspace,
+                                 int64_t workspace_bytes, int32_t* err, void* stream) {
+  using namespace ce::prefill;
+  Params p;
+  CUtensorMap qmap, lmap, kmap;
+  if (mode_of_row == nullptr) return CE_OK;
+  if (scores == nullptr || score_sg < pool_units)
+    return host::fail(CE_ERR_ARG, "ce_prefill_scores: scores missing or head stride below pool_units");
+  const int st0 = prefill_prepare(q, q_st, q_sh, k_pool, pool_units, qo_indptr, kv_indptr, kv_indices,
+                                  kv_tokens, kv_capacity, sinks, mode_of_row, rows, sm_scale, bs,
+                                  num_q_heads, num_kv_heads, head_dim, page_size, total_q, max_q,
+                                  max_tokens, scores, score_sg, zero_new, workspace, workspace_bytes,
+                                  err, p, qmap, lmap, kmap);
+  if (st0 != CE_OK) return st0 > 0 ? CE_OK : st0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (!host::set_smem(lse_kernel, L_SMEM) || !host::set_smem(colsum_kernel, C_SMEM))
-    return host::fail(CE_ERR_CUDA, "prefill smem attr");
   const dim3 g1((max_q + QT - 1) / QT, num_kv_heads, bs);
-  lse_kernel<<<g1, THREADS, L_SMEM, st>>>(p, qmap, kmap);
+  lse_kernel<false><<<g1, THREADS, L_SMEM, st>>>(p, qmap, kmap);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("prefill lse_kernel");
   if (max_tokens == 0) return CE_OK;
   const dim3 g2((max_tokens + BM - 1) / BM, num_kv_heads, bs);
   colsum_kernel<<<g2, THREADS, C_SMEM, st>>>(p, qmap, lmap, kmap);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("prefill colsum_kernel");
+  return CE_OK;
+}
+
+extern "C" int ce_prefill_lost(const void* q, int64_t q_st, int64_t q_sh, const void* k_pool,
+                               int64_t pool_units, const int32_t* qo_indptr, const int32_t* kv_indptr,
+                               const int32_t* kv_indices, const int32_t* kv_tokens, int64_t kv_capacity,
+                               const float* sinks, float sm_scale, int32_t num_q_heads,
+                               int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                               int32_t total_q, int32_t max_q, int32_t max_tokens,
+                               const uint32_t* evicted_bits, int32_t num_specs, int64_t bits_words,
+                               float* lost, int64_t lost_stride, float lost_scale, void* workspace,
+                               int64_t workspace_bytes, int32_t* err, void* stream) {
+  using namespace ce::prefill;
+  if (num_specs < 0 || num_specs > MAX_SPECS)
+    return host::fail(CE_ERR_UNSUPPORTED, "ce_prefill_lost: at most 8 specs");
+  if (num_specs == 0) return CE_OK;
+  if (!evicted_bits || !lost || bits_words * 32 < max_tokens || lost_stride < max_q)
+    return host::fail(CE_ERR_ARG, "ce_prefill_lost: evicted bits or lost buffer too small");
+  Params p;
+  CUtensorMap qmap, lmap, kmap;
+  const int st0 = prefill_prepare(q, q_st, q_sh, k_pool, pool_units, qo_indptr, kv_indptr, kv_indices,
+                                  kv_tokens, kv_capacity, sinks, nullptr, nullptr, sm_scale, 1,
+                                  num_q_heads, num_kv_heads, head_dim, page_size, total_q, max_q,
+                                  max_tokens, nullptr, 0, 0, workspace, workspace_bytes, err, p, qmap,
+                                  lmap, kmap);
+  if (st0 != CE_OK) return st0 > 0 ? CE_OK : st0;
+  p.lost_bits = evicted_bits;
+  p.lost_words = bits_words;
+  p.lost_stride = lost_stride;
+  p.S = num_specs;
+  p.lost_scale = lost_scale;
+  p.lost = lost;
+  p.all_entries = 1;   // the normalisers pass runs for the entry whatever its score mode
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 g1((max_q + QT - 1) / QT, num_kv_heads, 1);
+  lse_kernel<false><<<g1, THREADS, L_SMEM, st>>>(p, qmap, kmap);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("prefill lse_kernel");
+  lse_kernel<true><<<g1, THREADS, L_SMEM, st>>>(p, qmap, kmap);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("prefill lost pass");
   return CE_OK;
 }

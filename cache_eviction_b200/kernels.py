@@ -167,6 +167,32 @@ def prefill_scores(q, k_pool, qo_indptr, kv_indptr, kv_indices, kv_tokens, sm_sc
     return scores
 
 
+def prefill_lost(q, k_pool, qo_indptr, kv_indptr, kv_indices, kv_tokens, sm_scale, page_size, max_q,
+                 max_tokens, evicted_bits, lost, lost_scale, sinks=None, err=None):
+    """Lost-mass diagnostic of one entry's chunk (runtime:587-613), accumulated
+    into lost [S, >= max_q]; evicted_bits [S, G, words] int32 bit masks."""
+    lib = capi.load()
+    total_q, H, D = q.shape
+    G = k_pool.shape[1]
+    assert q.dtype == torch.bfloat16 and q.stride(2) == 1 and k_pool.is_contiguous()
+    assert evicted_bits.dtype == torch.int32 and evicted_bits.is_contiguous()
+    assert lost.dtype == torch.float32 and lost.stride(1) == 1
+    S = int(evicted_bits.shape[0])
+    dev = q.device
+    if sinks is not None and sinks.dtype != torch.float32:
+        sinks = sinks.float()
+    need = lib.ce_prefill_workspace_bytes(total_q, H)
+    ws = WORKSPACES.get(dev, "prefill", need)
+    st = lib.ce_prefill_lost(
+        _p(q), q.stride(0), q.stride(1), _p(k_pool), k_pool.shape[0], _p(qo_indptr), _p(kv_indptr),
+        _p(kv_indices), _p(kv_tokens), kv_indices.numel(), _p(sinks), float(sm_scale), H, G, D, page_size,
+        total_q, int(max_q), int(max_tokens), _p(evicted_bits), S, evicted_bits.shape[2], _p(lost),
+        lost.stride(0), float(lost_scale), _p(ws), ws.numel(), _p(err), _stream(dev))
+    capi.check(st, "ce_prefill_lost")
+    _count(2 if S and total_q else 0)
+    return lost
+
+
 def choose(pos, score, params: torch.Tensor, layers, heads, max_n, ncols=None, head_offset=0,
            kept_stride=None, err=None):
     """Kept columns [problems, segs, kept_stride] in ascending position (runtime:376-412)."""

@@ -236,12 +236,21 @@ def after_extend(backend, q, layer, forward_batch, sinks):
     loc = forward_batch.out_cache_loc.long()
     if layer.layer_id == st.first_full:
         st.scores.index_fill_(2, _new_units(st, loc), 0.0)
-    scored = [i for i, e in enumerate(entries) if e is not None and not e["error"] and e["mode"] in (1, 2)]
+    meta = backend.forward_metadata
+    for i, e in enumerate(entries):
+        if e is not None and e["kind"] == "diagnostic" and not e["error"]:
+            qo, kv = meta.qo_indptr.tolist(), meta.kv_indptr.tolist()
+            chunk = q.view(-1, layer.tp_q_head_num, layer.qk_head_dim)[qo[i]:qo[i + 1]]
+            prefix = meta.kv_indices[kv[i]:kv[i + 1]].long()
+            _diagnose(st, e, st.index[layer.layer_id], layer, chunk,
+                      backend.token_to_kv_pool.get_key_buffer(layer.layer_id), sinks,
+                      torch.cat((prefix, loc[qo[i]:qo[i + 1]])), forward_batch.extend_prefix_lens_cpu[i])
+    scored = [i for i, e in enumerate(entries) if e is not None and not e["error"] and e["mode"] in (1, 2)
+              and e["kind"] != "diagnostic"]
     if not scored:
         return
     if any(entries[i]["kind"] != "live" for i in scored):
-        raise NotImplementedError("replay/diagnostic entries are outside the decode-time eviction path")
-    meta = backend.forward_metadata
+        raise NotImplementedError("replay entries are outside the decode-time eviction path")
     heads, dim = layer.tp_q_head_num, layer.qk_head_dim
     queries = q.view(-1, heads, dim)
     qo, kv = meta.qo_indptr.tolist(), meta.kv_indptr.tolist()
@@ -275,6 +284,92 @@ def after_extend(backend, q, layer, forward_batch, sinks):
         max_q=max(qo[i + 1] - qo[i] for i in range(len(rows))), max_tokens=max(tokens),
         sinks=sinks, mode_of_row=torch.tensor(modes, dtype=torch.int32, device=dev),
         scores=st.scores[st.index[layer.layer_id]], zero_new=False, err=st.err)
+
+
+# ------------------------------------------------------ regret diagnostic
+def _diagnostic_entry(req, cfg, device, layers, heads):
+    """A prefill-only entry that scores several eviction specs against the
+    unevicted cache (runtime:549-560): per spec a resident mask, per-token
+    head_sum / head_max tables, and the per-query lost mass."""
+    specs = []
+    for item in str(cfg["policies"]).split(","):
+        name, budget, prefix, recent = item.split(":")
+        specs.append((name, int(budget), int(prefix), int(recent)))
+    length = len(req.origin_input_ids)
+    return {"kind": "diagnostic", "key": _identity(req), "mode": 0, "specs": specs, "error": None, "frontier": 0,
+            "seed": int(cfg.get("seed", 0)),
+            "resident": torch.ones((len(specs), layers, heads, length), dtype=torch.bool, device=device),
+            "score_sum": torch.zeros((layers, heads, length), device=device),
+            "score_max": torch.zeros((layers, heads, length), device=device),
+            "lost": torch.zeros((len(specs), length), device=device), "layers_seen": set()}
+
+
+def _diagnostic_boundary(entry, n):
+    """Every spec's per-head boundary at n, scored by the unevicted reference (runtime:563-584)."""
+    layers, heads = entry["resident"].shape[1:3]
+    device = entry["resident"].device
+    for j, (name, budget, prefix, recent) in enumerate(entry["specs"]):
+        resident = entry["resident"][j, :, :, :n]
+        count = int(resident[0, 0].sum())
+        if count <= budget:
+            continue
+        pos = resident.nonzero()[:, -1].view(layers, heads, count)
+        if name == "random_2048":
+            generator = torch.Generator(device=device).manual_seed(
+                (entry["seed"] * 1000003 + n * 31 + j) & 0x7FFFFFFF)
+            score = torch.rand(pos.shape, generator=generator, device=device, dtype=torch.float64)
+        elif name == "random_reservoir_2048":
+            score = reservoir_scores(entry["seed"], pos, torch.arange(layers, device=device),
+                                     torch.arange(heads, device=device))
+        else:
+            table = entry["score_max" if name == "head_max_sum_2048" else "score_sum"][..., :n]
+            score = torch.gather(table, -1, pos).double()
+        keep, _ = choose(name, pos, n, budget, prefix, recent, score)
+        entry["resident"][j, :, :, :n] = torch.zeros_like(resident).scatter_(
+            -1, torch.gather(pos, -1, keep), True)
+    entry["frontier"] = n
+
+
+def _pack_bits(mask):
+    """[..., T] bool -> [..., ceil(T/32)] int32 bit words (bit t of word t/32)."""
+    T = mask.shape[-1]
+    W = max(1, -(-T // 32))
+    padded = torch.zeros(mask.shape[:-1] + (W * 32,), dtype=torch.int64, device=mask.device)
+    padded[..., :T] = mask.to(torch.int64)
+    words = (padded.view(mask.shape[:-1] + (W, 32)) << torch.arange(32, device=mask.device)).sum(-1)
+    return torch.where(words >= 1 << 31, words - (1 << 32), words).to(torch.int32).contiguous()
+
+
+def _diagnose(st, entry, index, layer, queries, keys, sinks, slots, start):
+    """One full layer of one prefill chunk (runtime:587-613): the exact
+    per-token head_sum / head_max tables (ce_prefill_scores over the whole
+    unevicted prefix) and each spec's lost mass (ce_prefill_lost)."""
+    count = queries.shape[0]
+    end = start + count
+    if start // INTERVAL != (end - 1) // INTERVAL:
+        entry["error"] = "prefill chunk crosses a boundary; use --chunked-prefill-size 2048 and run alone"
+        return
+    if st.page_size != 1:
+        raise NotImplementedError("the regret diagnostic works on token slots (page size 1)")
+    if layer.layer_id == st.first_full and start % INTERVAL == 0 and start > entry["frontier"]:
+        _diagnostic_boundary(entry, start)
+    heads, kv_heads = layer.tp_q_head_num, layer.tp_k_head_num
+    dev = queries.device
+    kpool = keys.view(keys.shape[0], kv_heads, 1, keys.shape[-1])
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)
+    qo, kvp, tok = i32([0, count]), i32([0, end]), i32([end])
+    idx = slots.to(torch.int32).contiguous()
+    q = queries.contiguous()
+    for table, mode in (("score_sum", capi.CE_MODE_SUM), ("score_max", capi.CE_MODE_MAX)):
+        scratch = torch.zeros((kv_heads, kpool.shape[0]), dtype=torch.float32, device=dev)
+        kernels.prefill_scores(q, kpool, qo, kvp, idx, tok, layer.scaling, 1, count, end, sinks=sinks,
+                               mode_of_row=i32([mode]), scores=scratch, zero_new=False, err=st.err)
+        entry[table][index, :, :end] += scratch[:, slots.long()]
+    evicted = _pack_bits(~entry["resident"][:, index, :, :end])
+    kernels.prefill_lost(q, kpool, qo, kvp, idx, tok, layer.scaling, 1, count, end, evicted,
+                         entry["lost"][:, start:end], 1.0 / (heads * len(st.full_layers)),
+                         sinks=sinks, err=st.err)
+    entry["layers_seen"].add(layer.layer_id)
 
 
 # ------------------------------------------------------------- selection
@@ -476,17 +571,20 @@ def on_extend(batch):
             _reset(st, row)  # the row now belongs to another request or session
             entry = None
         if entry is None:
-            if "gstar_replay" in params:
+            if "gstar_diagnostic" in params:
+                entry = _diagnostic_entry(req, params["gstar_diagnostic"], st.req_to_token.device,
+                                          len(st.full_layers), st.kv_heads)
+            elif "gstar_replay" in params:
                 entry = _live_entry(req, params["gstar_replay"], "replay")
             elif "gstar_eviction" in params:
                 entry = _live_entry(req, params["gstar_eviction"], "live")
             else:
                 continue
             st.entries[row] = entry
-            st.mode[row] = SCORE_MODE.get(canonical(str(entry["cfg"].get("name"))), 0) \
-                if not entry["error"] else 0
+            st.mode[row] = 0 if entry["kind"] == "diagnostic" or entry["error"] else \
+                SCORE_MODE.get(canonical(str(entry["cfg"].get("name"))), 0)
             st.frontier[row], st.count[row] = 0, 0
-        if entry["error"]:
+        if entry["kind"] == "diagnostic" or entry["error"]:
             continue
         if getattr(req, "retraction_count", 0) or entry["key"] in RETRACTED:
             # a retracted request recomputes its KV from scratch, which evicted state cannot survive
@@ -551,7 +649,11 @@ def release(req):
     entry = st.entries.get(row)
     if entry is None or entry["key"] != _identity(req):
         return
-    if entry["kind"] == "live" and entry["key"] != req.rid:
+    if entry["kind"] == "diagnostic":
+        lost = entry["lost"][:, :len(req.origin_input_ids)].cpu().numpy()
+        write_payload(req.rid, {"kind": "diagnostic", "error": entry["error"], "specs": entry["specs"],
+                                "layers": sorted(entry["layers_seen"]), "lost": array(lost, "float32")})
+    elif entry["kind"] == "live" and entry["key"] != req.rid:
         return  # the session keeps its row and eviction state for the next call
     _reset(st, row)
 

@@ -234,6 +234,30 @@ int ce_prefill_scores(const void* q, int64_t q_st, int64_t q_sh,
                       void* workspace, int64_t workspace_bytes,
                       int32_t* err, void* stream);
 
+/* ---- K5 variant: lost-mass diagnostic --------------------------------------
+ * The reference's regret diagnostic (_diagnose, runtime:587-613): for ONE
+ * entry's prefill chunk (qo_indptr/kv_indptr/kv_indices/kv_tokens as for
+ * ce_prefill_scores, bs = 1, all keys visible to the causal mask) and
+ * S <= 8 eviction specs, lost[s][i] += lost_scale * sum over the group's query
+ * heads h and the keys t the spec evicted for head g of
+ *   p = exp(scale*q_i,h . k_t - logaddexp(logsumexp(visible logits), sink_h)).
+ * evicted_bits [S][G][bits_words] uint32, bit t set = key t evicted by spec s
+ * for KV head g (bits_words * 32 >= max_tokens); lost [S][lost_stride] fp32
+ * (lost_stride >= max_q), accumulated (atomically, over calls and KV heads).
+ * The reference averages over query heads and layers: lost_scale =
+ * 1 / (H * full layers).  Same workspace and shapes as ce_prefill_scores. */
+int ce_prefill_lost(const void* q, int64_t q_st, int64_t q_sh,
+                    const void* k_pool, int64_t pool_units,
+                    const int32_t* qo_indptr, const int32_t* kv_indptr,
+                    const int32_t* kv_indices, const int32_t* kv_tokens,
+                    int64_t kv_capacity, const float* sinks, float sm_scale,
+                    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                    int32_t page_size, int32_t total_q, int32_t max_q, int32_t max_tokens,
+                    const uint32_t* evicted_bits, int32_t num_specs, int64_t bits_words,
+                    float* lost, int64_t lost_stride, float lost_scale,
+                    void* workspace, int64_t workspace_bytes,
+                    int32_t* err, void* stream);
+
 /* ---- K2: ragged per-head selection ---------------------------------------
  * Replaces gstar_evict.choose + _scores + reservoir_scores (runtime:358-412)
  * for `problems` independent boundaries, each over `segs` = layers*heads

@@ -203,6 +203,22 @@ def gen_records(rt, core):
     np.savez_compressed(HERE / "records.npz", **out)
 
 
+def gen_diagnostic(rt):
+    """Lost mass, score tables and resident masks of the reference's regret
+    diagnostic (_diagnose / _diagnostic_boundary, runtime:549-613)."""
+    d = sc.diagnostic_setup()
+    keys, q = bf16_tensor(d["keys"]), bf16_tensor(d["q"])
+    sinks = torch.from_numpy(d["sinks"])
+    st = SimpleNamespace(first_full=1, full_layers=[1])
+    layer = SimpleNamespace(layer_id=1, tp_q_head_num=sc.DIAG_H, tp_k_head_num=sc.DIAG_G, scaling=d["scale"])
+    req = SimpleNamespace(rid="r", session=None, origin_input_ids=[0] * sc.DIAG_LEN)
+    e = rt._diagnostic_entry(req, {"seed": d["seed"], "policies": d["policies"]}, "cpu", 1, sc.DIAG_G)
+    for lo, hi in sc.DIAG_CHUNKS:
+        rt._diagnose(st, e, 0, layer, q[lo:hi], keys, sinks, torch.arange(1, hi + 1), lo)
+    np.savez_compressed(HERE / "diagnostic.npz", lost=e["lost"].numpy(), score_sum=e["score_sum"].numpy(),
+                        score_max=e["score_max"].numpy(), resident=e["resident"].numpy())
+
+
 def gen_decode(rt):
     d = sc.decode_setup()
     keys = bf16_tensor(d["keys"]).float()
@@ -248,6 +264,7 @@ def main():
     gen_reservoir(rt, core)
     gen_boundaries(rt, core)
     gen_records(rt, core)
+    gen_diagnostic(rt)
     gen_decode(rt)
     gen_prefill(rt)
     for f in sorted(HERE.glob("*.npz")):

@@ -176,3 +176,22 @@ def prefill_setup(seed: int = 11):
     qo_indptr = np.concatenate([[0], np.cumsum([nq for _, nq in PREFILL_ENTRIES])]).astype(np.int32)
     return dict(keys=keys, q=q, sinks=sinks, lists=lists, qo_indptr=qo_indptr, scale=0.125,
                 slots=slots)
+
+
+# ------------------------------------------------------- diagnostic scenario
+DIAG_SPECS = (("head_sum_2048", 900, 16, 64), ("head_max_sum_2048", 900, 16, 64),
+              ("prefix_sliding_2048", 900, 16, 884), ("random_reservoir_2048", 900, 16, 64))
+DIAG_H, DIAG_G, DIAG_LEN = 16, 2, 2200
+DIAG_CHUNKS = ((0, 2048), (2048, 2200))
+
+
+def diagnostic_setup(seed: int = 21):
+    """The reference test's lost-mass scenario (test_sglang_evict.py:191-221)
+    at head_dim 64: one full layer, GQA 8:1, a 2,200-token prompt in two
+    chunks (the spec boundaries fall at 2,048), keys in slots 1..2200."""
+    rng = np.random.default_rng(seed)
+    keys = bf16_bits(rng.standard_normal((DIAG_LEN + 1, DIAG_G, D), dtype=np.float32) * 2)
+    q = bf16_bits(rng.standard_normal((DIAG_LEN, DIAG_H, D), dtype=np.float32) * 2)
+    sinks = rng.standard_normal(DIAG_H).astype(np.float32)
+    policies = ",".join(f"{n}:{b}:{p}:{r}" for n, b, p, r in DIAG_SPECS)
+    return dict(keys=keys, q=q, sinks=sinks, policies=policies, seed=5, scale=0.125)
