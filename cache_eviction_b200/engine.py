@@ -225,13 +225,19 @@ class RaggedDecodeEngine:
             self.rows[r].n += 1
         self.seq_lens_dev.add_(1)
 
-    def step(self, q_layers, out_layers, sinks, scale, after_layer=None):
-        """One decode step: due boundaries, one token appended, CSR, every layer."""
+    def step(self, q_layers, out_layers, sinks, scale, after_layer=None, before_layer=None):
+        """One decode step: due boundaries, one token appended, CSR, every layer.
+
+        before_layer(l) / after_layer(l, out) run on the host around layer l's
+        launches (e.g. to make the compute stream wait for layer l's query
+        upload, or to queue layer l's output download on another stream)."""
         self.run_boundaries(self.due())
         self.advance()
         self._ensure_capacity(0)
         self.fill()
         for l in range(self.L):
+            if before_layer is not None:
+                before_layer(l)
             self.decode_layer(l, q_layers[l], out_layers[l], sinks[l], scale)
             if after_layer is not None:
                 after_layer(l, out_layers[l])
