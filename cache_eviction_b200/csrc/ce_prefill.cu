@@ -36,8 +36,9 @@
 // to the tensor cores with a proxy fence.  Every wait is bounded;
 // a wait that gives up flags CE_EW_TIMEOUT, tells the other roles to stop, and
 // the CTA still drains its copies and frees its tensor memory.
-// Both passes spend one exp2 per (row, key) on the SFU (ex2.approx), which
-// bounds the kernel; the tensor cores run asynchronously beside it.
+// Both passes spend one exp2 per (row, key): three quarters on the SFU
+// (ex2.approx) and a quarter as a polynomial on the FMA pipe, which together
+// bound the kernel; the tensor cores run asynchronously beside them.
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -158,6 +159,22 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA/ALU pipes, for a share of the exponentials so the SFU is not
+// the only unit doing them: x = n + f with n = round(x) (adding 1.5 * 2^23
+// leaves round(x) in the low mantissa bits), f in [-0.5, 0.5]; 2^f from a
+// degree-3 polynomial (coefficients fitted for minimal relative error on
+// [-0.5, 0.5], max relative error 7.6e-5) and 2^n added to the exponent
+// field ((bits(t) << 23) == n << 23 because bits(1.5 * 2^23) end in 23 zero
+// bits).  Arguments are clamped at -126 (the result is then a denormal
+// near 0, like ex2.approx.ftz's 0); the callers' arguments are <= ~0.
+__device__ __forceinline__ float poly_exp2(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.055174146f, f, 0.24261758f), f, 0.69326109f), f, 0.99992758f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // Unit holding list token t of the entry, or -1 past ntok / -2 outside the pool
@@ -431,7 +448,10 @@ __global__ void __launch_bounds__(THREADS, 2) lse_kernel(const Params p,
       if (mn != -INFINITY) {
         float sm4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int i = 0; i < 64; ++i) sm4[i & 3] += fast_exp2(fmaf(v[i], p.scale2, -mn));
+        for (int i = 0; i < 64; ++i) {
+          const float a = fmaf(v[i], p.scale2, -mn);
+          sm4[i & 3] += (i & 3) == 3 ? poly_exp2(a) : fast_exp2(a);
+        }
         l = l * fast_exp2(m - mn) + ((sm4[0] + sm4[1]) + (sm4[2] + sm4[3]));
         m = mn;
       }
@@ -602,7 +622,10 @@ __global__ void __launch_bounds__(THREADS, 2) colsum_kernel(const Params p,
         const float* lq = lse + u * GROUP;
         float e[GROUP];
 #pragma unroll
-        for (int x = 0; x < GROUP; ++x) e[x] = fast_exp2(fmaf(v[u * 8 + x], p.scale2, -lq[x]));
+        for (int x = 0; x < GROUP; ++x) {
+          const float a = fmaf(v[u * 8 + x], p.scale2, -lq[x]);
+          e[x] = x >= 6 ? poly_exp2(a) : fast_exp2(a);   // a quarter on the FMA pipe
+        }
         float red;
         if (mode == CE_MODE_SUM)
           red = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
