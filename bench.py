@@ -397,6 +397,34 @@ def prefill_microbench(world, rank, device, reps=5, cpu=False, prefixes=PREFILL_
                 "us": us, "tflops": 4 * D * H * pairs / (us * 1e-6) / 1e12,
                 "gexp2_per_s": 2 * H * pairs / (us * 1e-6) / 1e9, "visible_pairs": pairs}
         del kpool, scores
+        # Replay layer error of the same chunk (ce_replay_error): shadow K/V by
+        # position, a quarter of each head's prefix evicted.  Tensor work per
+        # visible pair and query head: Q.K^T twice plus four P.V products
+        # (hi/lo parts of P_a and P_d), 12 * 64 FLOP; one exp2 in each pass.
+        ks = torch.randn((ntok, G, D), generator=gen, device=device).to(torch.bfloat16)
+        vs = torch.randn((ntok, G, D), generator=gen, device=device).to(torch.bfloat16)
+        vis = torch.rand((G, ntok), generator=gen, device=device) < 0.75
+        vis[:, prefix:] = True
+        words = -(-ntok // 32)
+        pad = torch.zeros((G, words * 32), dtype=torch.int64, device=device)
+        pad[:, :ntok] = vis.to(torch.int64)
+        bits = (pad.view(G, words, 32) << torch.arange(32, device=device)).sum(-1)
+        bits = torch.where(bits >= 1 << 31, bits - (1 << 32), bits).to(torch.int32).contiguous()
+        ts = []
+        for it in range(reps + 1):
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(SLEEP_CYCLES)
+            a.record()
+            kernels.replay_error(q, ks, vs, prefix, D ** -0.5, visible_bits=bits, sinks=sinks)
+            e.record()
+            torch.cuda.synchronize()
+            if it:
+                ts.append(a.elapsed_time(e) * 1e3)
+        us = statistics.median(ts)
+        out[f"prefix{prefix}_replay"] = {"us": us, "tflops": 12 * D * H * pairs / (us * 1e-6) / 1e12,
+                                         "gexp2_per_s": 2 * H * pairs / (us * 1e-6) / 1e9,
+                                         "visible_pairs": pairs}
+        del ks, vs
     if cpu:
         from oracle import oracle
         import numpy as np

@@ -75,6 +75,9 @@ SIGNATURES = {
                                     I32, I32, I32, I32, I32, I32, P, I64, I32, P, I64, P, P]),
     "ce_prefill_lost": (C.c_int, [P, I64, I64, P, I64, P, P, P, P, I64, P, F32, I32, I32, I32, I32,
                                   I32, I32, I32, P, I32, I64, P, I64, F32, P, I64, P, P]),
+    "ce_replay_workspace_bytes": (I64, [I32, I32]),
+    "ce_replay_error": (C.c_int, [P, I64, I64, P, P, I64, P, I64, P, F32, I32, I32, I32, I32, I32, P, P,
+                                  P, I64, P, P]),
     "ce_choose_workspace_bytes": (I64, [I32, I32, I32]),
     "ce_choose": (C.c_int, [P, P, I32, P, I32, P, I32, I32, I32, I32, I32, P, I32, P, P, P,
                             I64, P, P]),

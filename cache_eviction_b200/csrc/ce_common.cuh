@@ -249,6 +249,18 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]^T, issued by one thread: A (M x K, K-major)
+// lives in tensor memory, row m in lane m, two 16-bit K elements per 32-bit
+// column (the lower K index in the low half).
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                          bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
 // Arrive on *bar once every tcgen05.mma this thread issued so far has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
@@ -273,6 +285,99 @@ __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, float* v) {
 }
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane, waited for.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  tmem_ld32_async(taddr, v);
+  tmem_ld_wait();
+}
+// Store 16 consecutive 32-bit columns of this thread's TMEM lane (32x32b
+// shape, x16); complete after tmem_st_wait().
+__device__ __forceinline__ void tmem_st16_async(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of an MN-major bf16 operand in the same
+// 128-byte-swizzled 1024-byte atoms: each 128-byte row holds 64 consecutive
+// MN elements of one K index, 8 K indices per atom.  Atoms follow each other
+// along K every 1024 B (stride offset); an operand of at most 64 MN elements
+// has a single column of atoms, and the leading offset (the step between
+// 64-element MN blocks) is given the same 1024 B so that it stays inside the
+// tile either way.  K-steps of 16 elements advance the start by 2048 bytes.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (64ull << 16) | (64ull << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+// The instruction descriptor's B-operand major-ness bit: B is MN-major.
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
+
+// ---- tiles shared by the tcgen05 kernels -----------------------------------------
+// 128-byte rows of eight 16-byte chunks in 1024-byte atoms; chunk c of row r
+// lives at c ^ (r & 7) (the layout TMA's 128-byte swizzle writes and the
+// tcgen05 SWIZZLE_128B descriptors read).
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return static_cast<uint32_t>((r * 8 + (c ^ (r & 7))) * 16);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;  // 0: zero-fill, nothing read
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Generic-proxy writes to shared memory become visible to the async proxy
+// (TMA, tcgen05.mma operand reads).
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Wait by one lane of a warp, result broadcast to the warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_t* err,
+                                          volatile int* abort, int lane) {
+  bool ok = true;
+  if (lane == 0) ok = mbar_wait_or_abort(bar, parity, err, abort);
+  return __shfl_sync(0xffffffffu, ok, 0);
+}
+
+// ---- exponentials ------------------------------------------------------------------
+// 2^x with the SFU's approximate exp2 (PTX ex2.approx.ftz.f32): relative
+// error near 2^-22, -inf -> +0, results below the normal range flush to 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x on the FMA/ALU pipes, for a share of the exponentials so the SFU is not
+// the only unit doing them: x = n + f with n = round(x) (adding 1.5 * 2^23
+// leaves round(x) in the low mantissa bits), f in [-0.5, 0.5]; 2^f from a
+// degree-3 polynomial (coefficients fitted for minimal relative error on
+// [-0.5, 0.5], max relative error 7.6e-5) and 2^n added to the exponent
+// field ((bits(t) << 23) == n << 23 because bits(1.5 * 2^23) end in 23 zero
+// bits).  Arguments are clamped at -126 (the result is then a denormal
+// near 0, like ex2.approx.ftz's 0); the callers' arguments are <= ~0.
+__device__ __forceinline__ float poly_exp2(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.055174146f, f, 0.24261758f), f, 0.69326109f), f, 0.99992758f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 }  // namespace ce

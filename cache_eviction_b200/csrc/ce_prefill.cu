@@ -132,51 +132,6 @@ __device__ __forceinline__ int entry_mode(const Params& p, int b) {
   return p.mode_of_row[p.rows ? p.rows[b] : b];
 }
 
-// 128-byte rows of eight 16-byte chunks in 1024-byte atoms; chunk c of row r
-// lives at c ^ (r & 7) (the layout TMA's 128-byte swizzle writes and the
-// tcgen05 SWIZZLE_128B K-major descriptor reads).
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-  return static_cast<uint32_t>((r * 8 + (c ^ (r & 7))) * 16);
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;  // 0: zero-fill, nothing read
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// 2^x with the SFU's approximate exp2 (PTX ex2.approx.ftz.f32): relative
-// error near 2^-22, -inf -> +0, results below the normal range flush to 0.
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// 2^x on the FMA/ALU pipes, for a share of the exponentials so the SFU is not
-// the only unit doing them: x = n + f with n = round(x) (adding 1.5 * 2^23
-// leaves round(x) in the low mantissa bits), f in [-0.5, 0.5]; 2^f from a
-// degree-3 polynomial (coefficients fitted for minimal relative error on
-// [-0.5, 0.5], max relative error 7.6e-5) and 2^n added to the exponent
-// field ((bits(t) << 23) == n << 23 because bits(1.5 * 2^23) end in 23 zero
-// bits).  Arguments are clamped at -126 (the result is then a denormal
-// near 0, like ex2.approx.ftz's 0); the callers' arguments are <= ~0.
-__device__ __forceinline__ float poly_exp2(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.055174146f, f, 0.24261758f), f, 0.69326109f), f, 0.99992758f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 // Unit holding list token t of the entry, or -1 past ntok / -2 outside the pool
 // (flagged).
 __device__ __forceinline__ int token_unit(const Params& p, int list0, int ntok, int t) {
@@ -224,21 +179,9 @@ __device__ __forceinline__ void copy_key_tile(const Params& p, uint32_t tile, in
   }
 }
 
-// Wait by one lane of a warp, result broadcast to the warp.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_t* err,
-                                          volatile int* abort, int lane) {
-  bool ok = true;
-  if (lane == 0) ok = mbar_wait_or_abort(bar, parity, err, abort);
-  return __shfl_sync(0xffffffffu, ok, 0);
-}
-
 // Barrier of the epilogue warps only (named barrier 1).
 __device__ __forceinline__ void named_barrier_epi() {
   asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
-}
-
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
 // Initialise the barriers and allocate the two TMEM accumulators; returns the

@@ -193,6 +193,38 @@ def prefill_lost(q, k_pool, qo_indptr, kv_indptr, kv_indices, kv_tokens, sm_scal
     return lost
 
 
+def replay_error(q, k_shadow, v_shadow, start, sm_scale, visible_bits=None, sinks=None, out_masked=None,
+                 err=None):
+    """Per-query relative output error of eviction (runtime:520-546) for one
+    chunk: q [count, H, 64] bf16 at positions start.., k/v shadows
+    [>= start + count, G, 64] bf16 by position, visible_bits [G, words] int32
+    (None = all visible).  Returns error [count] fp32; fills out_masked
+    [count, H, 64] fp32 with the masked output when given."""
+    lib = capi.load()
+    count, H, D = q.shape
+    G = k_shadow.shape[1]
+    assert q.dtype == torch.bfloat16 and q.stride(2) == 1
+    assert k_shadow.is_contiguous() and v_shadow.is_contiguous() and k_shadow.shape == v_shadow.shape
+    if visible_bits is not None:
+        assert visible_bits.dtype == torch.int32 and visible_bits.is_contiguous() and visible_bits.shape[0] == G
+    if out_masked is not None:
+        assert out_masked.dtype == torch.float32 and out_masked.is_contiguous()
+        assert tuple(out_masked.shape) == (count, H, D)
+    dev = q.device
+    if sinks is not None and sinks.dtype != torch.float32:
+        sinks = sinks.float()
+    error = torch.empty(count, dtype=torch.float32, device=dev)
+    need = lib.ce_replay_workspace_bytes(count, H)
+    ws = WORKSPACES.get(dev, "replay", need)
+    words = 0 if visible_bits is None else visible_bits.shape[1]
+    st = lib.ce_replay_error(_p(q), q.stride(0), q.stride(1), _p(k_shadow), _p(v_shadow), k_shadow.shape[0],
+                             _p(visible_bits), words, _p(sinks), float(sm_scale), H, G, D, int(start), count,
+                             _p(error), _p(out_masked), _p(ws), ws.numel(), _p(err), _stream(dev))
+    capi.check(st, "ce_replay_error")
+    _count(3 if count else 0)
+    return error
+
+
 def choose(pos, score, params: torch.Tensor, layers, heads, max_n, ncols=None, head_offset=0,
            kept_stride=None, err=None):
     """Kept columns [problems, segs, kept_stride] in ascending position (runtime:376-412)."""

@@ -174,10 +174,14 @@ def _decode(backend, q, layer, forward_batch, sinks, out, zero_new):
     rows = forward_batch.req_pool_indices.to(torch.int64)
     scores = st.scores[st.index[layer.layer_id]]
     o = None if out is None else out.view(bs, heads, dim)
+    if o is None and st.verify and layer.layer_id == st.first_full:
+        o = torch.empty((bs, heads, dim), dtype=torch.bfloat16, device=queries.device)
     result = kernels.decode_attn_score(
         queries, kpool, vpool, meta.kv_indptr[: bs + 1].to(torch.int32), indices, tokens,
         layer.scaling, st.page_size, sinks=sinks, mode_of_row=st.mode, rows=rows, scores=scores,
         zero_new=zero_new, out=o, err=st.err)
+    if st.verify and layer.layer_id == st.first_full:
+        _verify_decode(st, queries, result, layer, forward_batch, sinks)
     return result
 
 
@@ -220,11 +224,13 @@ def after_extend(backend, q, layer, forward_batch, sinks):
     """Prefill scores (runtime:277-311) for H2O rows of an extend batch.
 
     On the first full layer every unit that a new token starts is zeroed for
-    all layers (runtime:293-294); then ce_prefill_scores adds each head_sum /
-    head_max row's chunk probabilities over its resident prefix and the chunk
-    itself (_prefill_scores, runtime:327-340).  Replay and diagnostic entries
-    are not part of this path (their scoring is the reference's offline
-    tooling) and raise.
+    all layers (runtime:293-294); replay entries (and live ones under
+    GSTAR_EVICT_VERIFY=1) copy the chunk's keys and values into their shadow
+    by logical position, and replay entries record the layer error of the
+    chunk (runtime:301-306).  Diagnostic entries run _diagnose.  Then
+    ce_prefill_scores adds each head_sum / head_max row's chunk probabilities
+    over its resident prefix and the chunk itself (_prefill_scores,
+    runtime:327-340).
     """
     if _layer_is_sliding(layer):
         return
@@ -237,20 +243,32 @@ def after_extend(backend, q, layer, forward_batch, sinks):
     if layer.layer_id == st.first_full:
         st.scores.index_fill_(2, _new_units(st, loc), 0.0)
     meta = backend.forward_metadata
+    qo_host = None
     for i, e in enumerate(entries):
-        if e is not None and e["kind"] == "diagnostic" and not e["error"]:
-            qo, kv = meta.qo_indptr.tolist(), meta.kv_indptr.tolist()
-            chunk = q.view(-1, layer.tp_q_head_num, layer.qk_head_dim)[qo[i]:qo[i + 1]]
+        if e is None or e["error"]:
+            continue
+        if qo_host is None:
+            qo_host = meta.qo_indptr.tolist()
+        lo, hi = qo_host[i], qo_host[i + 1]
+        start = int(forward_batch.extend_prefix_lens_cpu[i])
+        chunk = q.view(-1, layer.tp_q_head_num, layer.qk_head_dim)[lo:hi]
+        if layer.layer_id == st.first_full and (e["kind"] == "replay" or st.verify and e["kind"] == "live"):
+            kpool, vpool = st.pools(layer.layer_id)
+            shadow_k, shadow_v = _shadow(st, e, start + hi - lo)
+            shadow_k[start:start + hi - lo] = _token_rows(kpool, loc[lo:hi], st.page_size)
+            shadow_v[start:start + hi - lo] = _token_rows(vpool, loc[lo:hi], st.page_size)
+            if e["kind"] == "replay":
+                _replay_layer_difference(st, e, chunk, layer, sinks, start)
+        if e["kind"] == "diagnostic":
+            kv = meta.kv_indptr.tolist()
             prefix = meta.kv_indices[kv[i]:kv[i + 1]].long()
             _diagnose(st, e, st.index[layer.layer_id], layer, chunk,
                       backend.token_to_kv_pool.get_key_buffer(layer.layer_id), sinks,
-                      torch.cat((prefix, loc[qo[i]:qo[i + 1]])), forward_batch.extend_prefix_lens_cpu[i])
+                      torch.cat((prefix, loc[lo:hi])), start)
     scored = [i for i, e in enumerate(entries) if e is not None and not e["error"] and e["mode"] in (1, 2)
               and e["kind"] != "diagnostic"]
     if not scored:
         return
-    if any(entries[i]["kind"] != "live" for i in scored):
-        raise NotImplementedError("replay entries are outside the decode-time eviction path")
     heads, dim = layer.tp_q_head_num, layer.qk_head_dim
     queries = q.view(-1, heads, dim)
     qo, kv = meta.qo_indptr.tolist(), meta.kv_indptr.tolist()
@@ -284,6 +302,101 @@ def after_extend(backend, q, layer, forward_batch, sinks):
         max_q=max(qo[i + 1] - qo[i] for i in range(len(rows))), max_tokens=max(tokens),
         sinks=sinks, mode_of_row=torch.tensor(modes, dtype=torch.int32, device=dev),
         scores=st.scores[st.index[layer.layer_id]], zero_new=False, err=st.err)
+
+
+# ------------------------------------------- static replay and verification
+def _token_rows(pool, loc, page):
+    """[n, G, D] rows of the tokens at pool slots `loc` from a [units, G, page, D] pool."""
+    if page == 1:
+        return pool[loc, :, 0]
+    return pool[loc // page, :, loc % page]
+
+
+def _shadow(st, entry, length):
+    """First full layer keys and values by logical position (runtime:227-238),
+    grown by doubling; the checks that need the unevicted cache read them."""
+    current = entry["shadow_k"].shape[0] if "shadow_k" in entry else 0
+    if current < length:
+        grown = max(length, 2 * current)
+        for name in ("shadow_k", "shadow_v"):
+            new = torch.zeros((grown, st.kv_heads, st.dim), dtype=torch.bfloat16, device=st.device)
+            if name in entry:
+                new[:current] = entry[name]
+            entry[name] = new
+    return entry["shadow_k"], entry["shadow_v"]
+
+
+def _visible(st, entry, end):
+    """Per-KV-head visibility of logical tokens [0, end) as [G, words] int32
+    bit words (runtime:241-247): each head's survivors below the frontier
+    (their pages' tokens at page sizes > 1), then the tail; None when nothing
+    was evicted yet."""
+    if not entry["count"]:
+        return None
+    P = st.page_size
+    visible = torch.zeros((st.kv_heads, end), dtype=torch.bool, device=st.device)
+    visible[:, entry["frontier"] * P:] = True
+    # kept units lie below the frontier, so their tokens lie below end
+    tokens = (entry["pos"][0][..., None] * P + torch.arange(P, device=st.device)).reshape(st.kv_heads, -1)
+    visible.scatter_(1, tokens, True)
+    return _pack_bits(visible)
+
+
+def _replay_layer_difference(st, entry, queries, layer, sinks, start):
+    """Per-token relative L2 error of the first full layer's attention output,
+    evicted against full (runtime:520-546), by ce_replay_error over the
+    shadow: both outputs use the unevicted keys, the evicted one restricted to
+    each head's visible positions."""
+    end = start + queries.shape[0]
+    shadow_k, shadow_v = entry["shadow_k"], entry["shadow_v"]
+    error = kernels.replay_error(queries, shadow_k, shadow_v, start, layer.scaling,
+                                 visible_bits=_visible(st, entry, end), sinks=sinks, err=st.err)
+    entry["layer_error"].append(error)
+
+
+def _verify_decode(st, queries, out, layer, forward_batch, sinks):
+    """GSTAR_EVICT_VERIFY=1, eager only (runtime:250-274): the first full
+    layer's output of every live row with a shadow equals attention over each
+    head's claimed positions; the largest absolute difference is kept."""
+    heads, dim = layer.tp_q_head_num, layer.qk_head_dim
+    kpool, vpool = st.pools(st.first_full)
+    loc = forward_batch.out_cache_loc.long()
+    positions = forward_batch.positions.tolist()
+    o = out.view(-1, heads, dim)
+    for i, row in enumerate(forward_batch.req_pool_indices.tolist()):
+        entry = st.entries.get(row)
+        if entry is None or entry["kind"] != "live" or "shadow_k" not in entry:
+            continue
+        end = positions[i] + 1
+        shadow_k, shadow_v = _shadow(st, entry, end)
+        shadow_k[end - 1] = _token_rows(kpool, loc[i:i + 1], st.page_size)[0]
+        shadow_v[end - 1] = _token_rows(vpool, loc[i:i + 1], st.page_size)[0]
+        expected = torch.empty((1, heads, dim), dtype=torch.float32, device=st.device)
+        kernels.replay_error(queries[i:i + 1], shadow_k, shadow_v, end - 1, layer.scaling,
+                             visible_bits=_visible(st, entry, end), sinks=sinks, out_masked=expected, err=st.err)
+        error = float((o[i].float() - expected[0]).abs().max())
+        entry["verify_max_error"] = max(entry.get("verify_max_error", 0.0), error)
+        entry["verify_steps"] = entry.get("verify_steps", 0) + 1
+
+
+def _relocation_ok(st, entry, table):
+    """Each head's keys at the table's units equal the unevicted keys of the
+    positions it claims (runtime:510-515), token by token."""
+    P = st.page_size
+    kpool, _ = st.pools(st.first_full)
+    pos = entry["pos"][0]                                             # [G, count] units
+    heads = torch.arange(st.kv_heads, device=st.device)[:, None]
+    stored = kpool[table.long()[None, :].expand(st.kv_heads, -1), heads]   # [G, count, P, D]
+    tokens = pos[..., None] * P + torch.arange(P, device=st.device)       # [G, count, P]
+    want = entry["shadow_k"][tokens, heads[..., None]]                       # [G, count, P, D]
+    return bool(torch.equal(stored, want))
+
+
+def _events(entry, req):
+    """A live request's event payload (runtime:712-716)."""
+    keys = ("cfg", "error", "events", "peak_full_entries", "freed", "verify_max_error", "verify_steps")
+    return {"kind": "events", **{k: entry.get(k) for k in keys},
+            "length": len(req.origin_input_ids) + len(req.output_ids), "retracted": entry["key"] in RETRACTED}
 
 
 # ------------------------------------------------------ regret diagnostic
@@ -510,8 +623,11 @@ def _boundary(st, row, entry, n, cursor=None, allocator=None):
     if status == 4:
         raise RuntimeError("packed ownership overlaps the sliding-window region")
     elapsed = 1000 * (finished - started)
-    entry["events"].append({"boundary": n, "before": before, "after": after, "freed": nfreed,
-                            "swa_cursor": cursor, "ranking_ms": elapsed, "compaction_ms": 0.0})
+    event = {"boundary": n, "before": before, "after": after, "freed": nfreed,
+             "swa_cursor": cursor, "ranking_ms": elapsed, "compaction_ms": 0.0}
+    if st.verify and "shadow_k" in entry:
+        event["relocation_ok"] = _relocation_ok(st, entry, st.table[row, :after])
+    entry["events"].append(event)
     if record is not None:
         _write_record(st, entry, cfg, n, record)
 
@@ -590,6 +706,7 @@ def on_extend(batch):
             # a retracted request recomputes its KV from scratch, which evicted state cannot survive
             RETRACTED.add(entry["key"])
             entry["error"] = "retracted"
+            write_payload(f"{entry['key']}-retracted", {"kind": "retracted", "cfg": entry["cfg"]})
             st.mode[row] = 0
             continue
         start, length = req.extend_range.start, req.extend_range.length
@@ -653,8 +770,16 @@ def release(req):
         lost = entry["lost"][:, :len(req.origin_input_ids)].cpu().numpy()
         write_payload(req.rid, {"kind": "diagnostic", "error": entry["error"], "specs": entry["specs"],
                                 "layers": sorted(entry["layers_seen"]), "lost": array(lost, "float32")})
-    elif entry["kind"] == "live" and entry["key"] != req.rid:
-        return  # the session keeps its row and eviction state for the next call
+    elif entry["kind"] == "replay":
+        error = torch.cat(entry["layer_error"]).cpu().numpy() if entry["layer_error"] else np.zeros(0)
+        write_payload(req.rid, {"kind": "replay", "cfg": entry["cfg"], "error": entry["error"],
+                                "events": entry["events"], "layer": st.first_full,
+                                "layer_error": array(error, "float32")})
+    else:
+        session = entry["key"] != req.rid
+        write_payload(f"{entry['key']}-events" if session else req.rid, _events(entry, req))
+        if session:
+            return  # the session keeps its row and eviction state for the next call
     _reset(st, row)
 
 

@@ -258,6 +258,32 @@ int ce_prefill_lost(const void* q, int64_t q_st, int64_t q_sh,
                     void* workspace, int64_t workspace_bytes,
                     int32_t* err, void* stream);
 
+/* ---- K5 variant: replay layer error ---------------------------------------
+ * Replaces the reference's _replay_layer_difference (runtime:520-546) with
+ * _visible (241-247): one prefill chunk of one request, queries at logical
+ * positions start .. start+count-1 attending causally to the unevicted
+ * keys/values 0 .. start+count-1 kept by position (the reference's shadow,
+ * 227-238).  With a_i the full attention output of query i and b_i the
+ * output restricted to each KV head's visible positions (both with the sink
+ * in the normaliser),
+ *   error[i] = ||b_i - a_i|| / max(||a_i||, 1e-12)   over all H x 64 values.
+ *   q          [count, H, 64] bf16, strides q_st, q_sh (elements, multiples of 8)
+ *   k, v       [kv_rows, G, 64] bf16 by position, kv_rows >= start + count
+ *   visible    [G, bits_words] uint32, bit t of row g = position t visible to
+ *              KV head g (bits_words * 32 >= start + count); NULL = all visible
+ *   error      [count] fp32, written
+ *   out_masked NULL or [count, H, 64] fp32: b (the masked output), written
+ * Workspace: ce_replay_workspace_bytes(count, H). */
+int64_t ce_replay_workspace_bytes(int32_t count, int32_t num_q_heads);
+int ce_replay_error(const void* q, int64_t q_st, int64_t q_sh,
+                    const void* k, const void* v, int64_t kv_rows,
+                    const uint32_t* visible, int64_t bits_words,
+                    const float* sinks, float sm_scale,
+                    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                    int32_t start, int32_t count, float* error, float* out_masked,
+                    void* workspace, int64_t workspace_bytes,
+                    int32_t* err, void* stream);
+
 /* ---- K2: ragged per-head selection ---------------------------------------
  * Replaces gstar_evict.choose + _scores + reservoir_scores (runtime:358-412)
  * for `problems` independent boundaries, each over `segs` = layers*heads

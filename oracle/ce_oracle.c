@@ -236,6 +236,74 @@ static inline int prot(int pos, const or_row_params* q) {
   return pos < q->prefix || pos >= q->n - q->recent || (q->cursor >= 0 && pos >= q->cursor);
 }
 
+/* Replay layer error: _replay_layer_difference (runtime:520-546) with
+ * _probabilities (314-324) and _visible (241-247).  Query i of the chunk sits
+ * at position start + i and sees keys 0 .. start + i of the shadow k/v
+ * ([positions, G, D] bf16 bits).  Per head: a = softmax_full V,
+ * b = softmax over the head's visible keys V (visible [G, start + count]
+ * bytes, NULL = all), both with the sink in the normaliser
+ * (logaddexp(logsumexp, sink), so no visible key and a sink give b = 0);
+ * error[i] = ||b - a|| / max(||a||, 1e-12) over all H x D values, in double.
+ * out_masked (optional) [count, H, D] receives b. */
+void or_replay_error(const uint16_t* q, int64_t q_st, int64_t q_sh, const uint16_t* k,
+                     const uint16_t* v, const uint8_t* visible, const float* sinks, float scale,
+                     int H, int G, int D, int start, int count, double* error,
+                     double* out_masked) {
+  const int grp = H / G;
+  const int end = start + count;
+#pragma omp parallel for schedule(dynamic)
+  for (int i = 0; i < count; ++i) {
+    const int nk = start + i + 1;
+    double* s = (double*)malloc(sizeof(double) * (size_t)nk);
+    double* a = (double*)malloc(sizeof(double) * (size_t)D);
+    double* b = (double*)malloc(sizeof(double) * (size_t)D);
+    double num = 0.0, den = 0.0;
+    for (int h = 0; h < H; ++h) {
+      const int g = h / grp;
+      const uint16_t* qh = q + (int64_t)i * q_st + (int64_t)h * q_sh;
+      const uint8_t* vis = visible ? visible + (int64_t)g * end : NULL;
+      double m = -INFINITY, mv = -INFINITY;
+      for (int t = 0; t < nk; ++t) {
+        const uint16_t* kr = k + ((int64_t)t * G + g) * D;
+        double acc = 0.0;
+        for (int d = 0; d < D; ++d) acc += (double)bf16f(qh[d]) * (double)bf16f(kr[d]);
+        s[t] = acc * (double)scale;
+        if (s[t] > m) m = s[t];
+        if ((!vis || vis[t]) && s[t] > mv) mv = s[t];
+      }
+      const double sink = sinks ? (double)sinks[h] : -INFINITY;
+      if (sink > m) m = sink;
+      if (sink > mv) mv = sink;
+      double z = sinks ? exp(sink - m) : 0.0, zv = (sinks && mv > -INFINITY) ? exp(sink - mv) : 0.0;
+      for (int t = 0; t < nk; ++t) {
+        z += exp(s[t] - m);
+        if (!vis || vis[t]) zv += exp(s[t] - mv);
+      }
+      for (int d = 0; d < D; ++d) a[d] = b[d] = 0.0;
+      for (int t = 0; t < nk; ++t) {
+        const double pa = exp(s[t] - m) / z;
+        const double pb = (!vis || vis[t]) ? exp(s[t] - mv) / zv : 0.0;
+        const uint16_t* vr = v + ((int64_t)t * G + g) * D;
+        for (int d = 0; d < D; ++d) {
+          const double x = (double)bf16f(vr[d]);
+          a[d] += pa * x;
+          b[d] += pb * x;
+        }
+      }
+      for (int d = 0; d < D; ++d) {
+        num += (b[d] - a[d]) * (b[d] - a[d]);
+        den += a[d] * a[d];
+        if (out_masked) out_masked[((int64_t)i * H + h) * D + d] = b[d];
+      }
+    }
+    const double na = sqrt(den);
+    error[i] = sqrt(num) / (na > 1e-12 ? na : 1e-12);
+    free(s);
+    free(a);
+    free(b);
+  }
+}
+
 /* One segment: kept columns (protected + chosen) sorted by ascending pos.
  * key[c] is the reference's double key for unprotected columns.  Returns
  * the number kept, or -1 if the protected count exceeds the budget. */

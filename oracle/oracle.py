@@ -164,6 +164,30 @@ def prefill(q_bits, k_bits, qo_indptr, indptr, indices, tokens, sinks, modes, sc
     return scores
 
 
+def replay_error(q_bits, k_bits, v_bits, start, scale, visible=None, sinks=None, want_out=False):
+    """Replay layer error of one chunk in float64 (runtime:520-546).
+
+    q_bits [count, H, D] uint16 at positions start..; k_bits / v_bits
+    [>= start + count, G, D] uint16 by position; visible [G, start + count]
+    bool or None.  Returns error [count] (and the masked output [count, H, D]
+    with want_out); see or_replay_error."""
+    q_bits = np.ascontiguousarray(q_bits, np.uint16)
+    k_bits = np.ascontiguousarray(k_bits, np.uint16)
+    v_bits = np.ascontiguousarray(v_bits, np.uint16)
+    count, H, D = q_bits.shape
+    G = k_bits.shape[1]
+    end = start + count
+    assert k_bits.shape[0] >= end and v_bits.shape == k_bits.shape
+    vis = None if visible is None else np.ascontiguousarray(np.asarray(visible)[:, :end], np.uint8)
+    sinks = None if sinks is None else np.ascontiguousarray(sinks, np.float32)
+    error = np.zeros(count, np.float64)
+    out = np.zeros((count, H, D), np.float64) if want_out else None
+    lib().or_replay_error(_p(q_bits), C.c_int64(H * D), C.c_int64(D), _p(k_bits), _p(v_bits), _p(vis),
+                          _p(sinks), C.c_float(scale), C.c_int(H), C.c_int(G), C.c_int(D), C.c_int(start),
+                          C.c_int(count), _p(error), _p(out))
+    return (error, out) if want_out else error
+
+
 def retention_record(pos_before, count_before, frontier_before, n, pos_after, count_after):
     """Retention record of one row's boundary (runtime:465-467, 500-507).
 

@@ -219,6 +219,24 @@ def gen_diagnostic(rt):
                         score_max=e["score_max"].numpy(), resident=e["resident"].numpy())
 
 
+def gen_replay(rt):
+    """Per-token layer error of the reference's static replay
+    (_replay_layer_difference, runtime:520-546) for three chunks: one before
+    any eviction (count 0: everything visible) and two after the boundary."""
+    d = sc.replay_setup()
+    layer = SimpleNamespace(tp_q_head_num=sc.REPLAY_H, tp_k_head_num=sc.REPLAY_G, scaling=d["scale"])
+    sinks = torch.from_numpy(d["sinks"])
+    q = bf16_tensor(d["q"])
+    out = {}
+    for i, (lo, hi, evicted) in enumerate(sc.REPLAY_CHUNKS):
+        entry = {"shadow_k": bf16_tensor(d["keys"]), "shadow_v": bf16_tensor(d["values"]), "layer_error": [],
+                 "count": sc.REPLAY_KEEP if evicted else 0, "frontier": sc.REPLAY_FRONTIER if evicted else 0,
+                 "pos": torch.from_numpy(d["pos"])[None]}
+        rt._replay_layer_difference(None, entry, q[lo:hi], layer, sinks, lo)
+        out[f"chunk{i}"] = torch.cat(entry["layer_error"]).numpy()
+    np.savez_compressed(HERE / "replay.npz", **out)
+
+
 def gen_decode(rt):
     d = sc.decode_setup()
     keys = bf16_tensor(d["keys"]).float()
@@ -265,6 +283,7 @@ def main():
     gen_boundaries(rt, core)
     gen_records(rt, core)
     gen_diagnostic(rt)
+    gen_replay(rt)
     gen_decode(rt)
     gen_prefill(rt)
     for f in sorted(HERE.glob("*.npz")):

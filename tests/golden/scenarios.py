@@ -195,3 +195,38 @@ def diagnostic_setup(seed: int = 21):
     sinks = rng.standard_normal(DIAG_H).astype(np.float32)
     policies = ",".join(f"{n}:{b}:{p}:{r}" for n, b, p, r in DIAG_SPECS)
     return dict(keys=keys, q=q, sinks=sinks, policies=policies, seed=5, scale=0.125)
+
+
+# ---------------------------------------------------------- replay scenario
+REPLAY_H, REPLAY_G, REPLAY_LEN = 16, 2, 2400
+REPLAY_CHUNKS = ((0, 300, False), (2048, 2200, True), (2200, 2400, True))  # (start, end, evicted)
+REPLAY_FRONTIER, REPLAY_KEEP = 2048, 900
+
+
+def replay_setup(seed: int = 23):
+    """Shadow keys/values of one request by position and, for the chunks after
+    its boundary at 2,048, each KV head's kept positions (prefix 16, recent 64,
+    a random middle; 900 per head), the state _replay_layer_difference reads
+    (runtime:520-546).  Keys are scaled so attention is peaked and evicted
+    mass is not negligible."""
+    rng = np.random.default_rng(seed)
+    keys = bf16_bits(rng.standard_normal((REPLAY_LEN, REPLAY_G, D), dtype=np.float32) * 2)
+    values = bf16_bits(rng.standard_normal((REPLAY_LEN, REPLAY_G, D), dtype=np.float32))
+    q = bf16_bits(rng.standard_normal((REPLAY_LEN, REPLAY_H, D), dtype=np.float32) * 2)
+    sinks = rng.standard_normal(REPLAY_H).astype(np.float32)
+    F, K = REPLAY_FRONTIER, REPLAY_KEEP
+    pos = np.empty((REPLAY_G, K), np.int64)
+    for g in range(REPLAY_G):
+        mid = np.sort(rng.choice(np.arange(16, F - 64), K - 80, replace=False))
+        pos[g] = np.concatenate([np.arange(16), mid, np.arange(F - 64, F)])
+    return dict(keys=keys, values=values, q=q, sinks=sinks, pos=pos, scale=0.125)
+
+
+def replay_visible(pos, frontier, end):
+    """_visible (runtime:241-247) as [G, end] bool: each head's kept positions
+    below the frontier, everything from the frontier on."""
+    vis = np.zeros((pos.shape[0], end), bool)
+    vis[:, frontier:] = True
+    for g in range(pos.shape[0]):
+        vis[g, pos[g]] = True
+    return vis

@@ -30,9 +30,11 @@ def _setup():
 
 
 def backend(rows=4, width=8192, slots=20000, kv_heads=8, dim=64, page=1):
-    """Two full layers (1, 3) and two sliding-window layers (test_sglang_evict.py:19-28)."""
-    keys = {l: torch.randn((slots, kv_heads, dim), device="cuda").to(torch.bfloat16) for l in range(4)}
-    values = {l: torch.randn((slots, kv_heads, dim), device="cuda").to(torch.bfloat16) for l in range(4)}
+    """Two full layers (1, 3) and two sliding-window layers (test_sglang_evict.py:19-28).
+    With page > 1 the pools are [slots / page, kv_heads, page, dim]."""
+    shape = (slots, kv_heads, dim) if page == 1 else (slots // page, kv_heads, page, dim)
+    keys = {l: torch.randn(shape, device="cuda").to(torch.bfloat16) for l in range(4)}
+    values = {l: torch.randn(shape, device="cuda").to(torch.bfloat16) for l in range(4)}
     pool = SimpleNamespace(layers_mapping={l: (l, l not in FULL) for l in range(4)},
                            get_key_buffer=keys.__getitem__, get_value_buffer=values.__getitem__)
     return SimpleNamespace(token_to_kv_pool=pool, max_kv_splits=8, page_size=page,
@@ -263,8 +265,10 @@ def test_choose_deferred_and_mismatch(_setup):
         ge.choose("head_sum_2048", bad, 700, 256, 64, 64, score)
 
 
-def test_on_decode_runs_due_boundary_and_frees(_setup):
-    """The scheduler hook path: create the entry at extend, boundary at decode."""
+def test_on_decode_runs_due_boundary_and_frees(_setup, tmp_path, monkeypatch):
+    """The scheduler hook path: create the entry at extend, boundary at decode;
+    release writes the request's event payload."""
+    monkeypatch.setenv("GSTAR_PAYLOAD_DIR", str(tmp_path))
     ge = _setup
     b = backend(rows=2, slots=6000)
     st = ge.state(b)
@@ -276,7 +280,8 @@ def test_on_decode_runs_due_boundary_and_frees(_setup):
                           sampling_params=SimpleNamespace(custom_params={"gstar_eviction": {
                               "name": "random_reservoir_2048", "budget": 512, "prefix": 128,
                               "recent": 128, "seed": 1}}),
-                          extend_range=SimpleNamespace(start=0, length=2048))
+                          extend_range=SimpleNamespace(start=0, length=2048),
+                          origin_input_ids=[0] * 2000, output_ids=[0] * 48)
     batch = SimpleNamespace(reqs=[req], tree_cache=SimpleNamespace(token_to_kv_pool_allocator=alloc),
                             seq_lens_cpu=torch.tensor([n]))
     ge.on_extend(batch)
@@ -289,6 +294,11 @@ def test_on_decode_runs_due_boundary_and_frees(_setup):
     assert len(e["events"]) == 1
     ge.release(req)
     assert 0 not in st.entries
+    import gzip
+    import json
+    obj = json.loads(gzip.decompress((tmp_path / "a.json.gz").read_bytes()))
+    assert obj["kind"] == "events" and obj["length"] == n and obj["freed"] == n - 512
+    assert [ev["boundary"] for ev in obj["events"]] == [n] and obj["peak_full_entries"] == n
 
 
 def test_after_extend_scores_h2o_rows(_setup):
@@ -392,3 +402,158 @@ def test_retention_records_are_written_and_decode_to_the_kept_sets(_setup, name,
         last = boundary
         for s, h in enumerate(held):
             np.testing.assert_array_equal(np.sort(e["pos"][s // 8, s % 8].cpu().numpy()), h)
+
+
+def _bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def _chunk(b, st, ge, row, start, count, slot_of, page):
+    """Extend metadata of one chunk: the row's CSR for its prefix (built by
+    fill, as SGLang's backend does) and the chunk's token slots."""
+    kv_indptr = torch.zeros(2, dtype=torch.int32, device="cuda")
+    b.kv_indptr = kv_indptr
+    kv_indices = torch.zeros(8192, dtype=torch.int32, device="cuda")
+    ge.fill(b, 1, torch.tensor([start], device="cuda"), torch.tensor([row], device="cuda"), kv_indices)
+    b.forward_metadata = SimpleNamespace(kv_indptr=kv_indptr, kv_indices=kv_indices[:int(kv_indptr[1])],
+                                         qo_indptr=torch.tensor([0, count], dtype=torch.int32, device="cuda"))
+    return SimpleNamespace(out_cache_loc=slot_of[start:start + count], req_pool_indices=torch.tensor([row], device="cuda"),
+                           extend_prefix_lens_cpu=[start], positions=torch.arange(start, start + count, device="cuda"))
+
+
+def _layout(st, n, page, row=0):
+    """Random units for the row's pages; returns the token slot of every logical position."""
+    units = -(-n // page)
+    unit_of = (torch.randperm(st.units - 1, device="cuda")[:units] + 1).int()
+    st.req_to_token[row, :units] = unit_of
+    t = torch.arange(n, device="cuda")
+    return unit_of[t // page].long() * page + t % page
+
+
+def _layer(layer_id):
+    return SimpleNamespace(sliding_window_size=-1, tp_q_head_num=64, tp_k_head_num=8, qk_head_dim=64,
+                           layer_id=layer_id, scaling=0.125)
+
+
+def _visible_np(e, page, end):
+    vis = np.zeros((8, end), bool)
+    vis[:, e["frontier"] * page:] = True
+    pos = e["pos"][0].cpu().numpy()
+    for g in range(8):
+        for u in pos[g]:
+            vis[g, u * page:(u + 1) * page] = True
+    return vis
+
+
+@pytest.mark.parametrize("page", [1, 16])
+def test_replay_entry_records_layer_error(_setup, page, tmp_path, monkeypatch):
+    """Static replay (runtime:301-306, 520-546, 685-686, 732-736): the first
+    full layer's chunks are copied into the shadow by position, the boundary
+    at 2,048 relocates survivors without freeing, the chunk after it records
+    each query's layer error against the unevicted keys, and release writes
+    the replay payload.  Expected errors from the CPU oracle over the keys
+    and values as they were written, with the entry's kept positions."""
+    import base64
+    import gzip
+    import json
+    monkeypatch.setenv("GSTAR_PAYLOAD_DIR", str(tmp_path))
+    ge = _setup
+    b = backend(page=page)
+    st = ge.state(b)
+    n0, n1 = 2048, 152
+    slot_of = _layout(st, n0 + n1, page)
+    cfg = {"name": "head_sum_2048", "budget": 1024, "prefix": 256, "recent": 256, "seed": 3}
+    req = SimpleNamespace(rid="rep1", session=None, kv=SimpleNamespace(req_pool_idx=0, holds_kv=True),
+                          sampling_params=SimpleNamespace(custom_params={"gstar_replay": cfg}),
+                          extend_range=SimpleNamespace(start=0, length=n0), origin_input_ids=[0] * (n0 + n1),
+                          output_ids=[])
+    batch = SimpleNamespace(reqs=[req])
+    q = torch.randn((n0 + n1, 64, 64), device="cuda").mul_(1.5).to(torch.bfloat16)
+    sinks = torch.randn(64, device="cuda").to(torch.bfloat16)
+    kpool, vpool = st.pools(1)
+    orig_k = ge._token_rows(kpool, slot_of, page).clone()
+    orig_v = ge._token_rows(vpool, slot_of, page).clone()
+    ge.on_extend(batch)
+    e = st.entries[0]
+    assert e["kind"] == "replay" and e["error"] is None
+    fb = _chunk(b, st, ge, 0, 0, n0, slot_of, page)
+    for layer_id in FULL:
+        ge.after_extend(b, q[:n0].reshape(n0, -1), _layer(layer_id), fb, sinks)
+    req.extend_range = SimpleNamespace(start=n0, length=n1)
+    ge.on_extend(batch)                        # static boundary at 2,048: nothing freed
+    assert e["count"] == 1024 // page and e["events"][-1]["freed"] == 0
+    fb = _chunk(b, st, ge, 0, n0, n1, slot_of, page)
+    for layer_id in FULL:
+        ge.after_extend(b, q[n0:].reshape(n1, -1), _layer(layer_id), fb, sinks)
+    torch.cuda.synchronize()
+    assert int(st.err.item()) == 0
+    vis = _visible_np(e, page, n0 + n1)
+    want = oracle.replay_error(_bits(q[n0:]), _bits(orig_k), _bits(orig_v), n0, 0.125, vis,
+                               sinks.float().cpu().numpy())
+    ge.release(req)
+    obj = json.loads(gzip.decompress((tmp_path / "rep1.json.gz").read_bytes()))
+    assert obj["kind"] == "replay" and obj["layer"] == 1 and obj["cfg"] == cfg and obj["error"] is None
+    assert [ev["boundary"] for ev in obj["events"]] == [n0]
+    err = np.frombuffer(base64.b64decode(obj["layer_error"]["data"]), np.float32)
+    assert err.shape == (n0 + n1,)
+    assert not err[:n0].any()                  # nothing evicted before the boundary
+    assert (err[n0:] > 0).all()
+    np.testing.assert_allclose(err[n0:], want, rtol=1e-3, atol=1e-6)
+
+
+@pytest.mark.parametrize("page", [1, 16])
+def test_verify_mode_checks_decode_and_relocation(_setup, page, tmp_path, monkeypatch):
+    """GSTAR_EVICT_VERIFY=1 (runtime:110, 213-214, 250-274, 497-498, 510-515):
+    live entries keep a shadow; the boundary event reports that every head's
+    relocated keys equal the unevicted keys of its claimed positions, and a
+    decode step's first-full-layer output matches attention over those
+    positions."""
+    monkeypatch.setenv("GSTAR_PAYLOAD_DIR", str(tmp_path))
+    monkeypatch.setenv("GSTAR_EVICT_VERIFY", "1")
+    ge = _setup
+    b = backend(page=page)
+    st = ge.state(b)
+    assert st.verify
+    n0, n1 = 2048, 160
+    slot_of = _layout(st, n0 + n1 + 1, page)
+    cfg = {"name": "head_sum_2048", "budget": 1024, "prefix": 256, "recent": 256, "seed": 3}
+    req = SimpleNamespace(rid="v1", session=None, kv=SimpleNamespace(req_pool_idx=0, holds_kv=True),
+                          sampling_params=SimpleNamespace(custom_params={"gstar_eviction": cfg}),
+                          extend_range=SimpleNamespace(start=0, length=n0), origin_input_ids=[0] * (n0 + n1),
+                          output_ids=[5])
+    freed, alloc = allocator()
+    batch = SimpleNamespace(reqs=[req], tree_cache=SimpleNamespace(token_to_kv_pool_allocator=alloc))
+    q = torch.randn((n0 + n1 + 1, 64, 64), device="cuda").to(torch.bfloat16)
+    sinks = torch.randn(64, device="cuda").to(torch.bfloat16)
+    ge.on_extend(batch)
+    e = st.entries[0]
+    fb = _chunk(b, st, ge, 0, 0, n0, slot_of, page)
+    for layer_id in FULL:
+        ge.after_extend(b, q[:n0].reshape(n0, -1), _layer(layer_id), fb, sinks)
+    req.extend_range = SimpleNamespace(start=n0, length=n1)
+    ge.on_extend(batch)                        # live boundary at 2,048
+    ev = e["events"][-1]
+    assert ev["boundary"] == n0 and ev["freed"] > 0 and ev["relocation_ok"] is True
+    fb = _chunk(b, st, ge, 0, n0, n1, slot_of, page)
+    for layer_id in FULL:
+        ge.after_extend(b, q[n0:n0 + n1].reshape(n1, -1), _layer(layer_id), fb, sinks)
+    # one decode step for the token at position n0 + n1
+    n = n0 + n1 + 1
+    kv_indptr = torch.zeros(2, dtype=torch.int32, device="cuda")
+    b.kv_indptr = kv_indptr
+    kv_indices = torch.zeros(8192, dtype=torch.int32, device="cuda")
+    ge.fill(b, 1, torch.tensor([n], device="cuda"), torch.tensor([0], device="cuda"), kv_indices)
+    b.forward_metadata = SimpleNamespace(kv_indptr=kv_indptr, kv_indices=kv_indices[:int(kv_indptr[1])])
+    dfb = SimpleNamespace(out_cache_loc=slot_of[n - 1:n], req_pool_indices=torch.tensor([0], device="cuda"),
+                          positions=torch.tensor([n - 1], device="cuda"))
+    out = torch.empty((1, 64, 64), dtype=torch.bfloat16, device="cuda")
+    ge.decode(b, q[n - 1:n].reshape(1, -1), _layer(1), dfb, sinks, out)
+    torch.cuda.synchronize()
+    assert int(st.err.item()) == 0
+    assert e["verify_steps"] == 1 and e["verify_max_error"] < 2e-2
+    ge.release(req)
+    import gzip
+    import json
+    obj = json.loads(gzip.decompress((tmp_path / "v1.json.gz").read_bytes()))
+    assert obj["kind"] == "events" and obj["verify_steps"] == 1 and obj["length"] == n0 + n1 + 1
+    assert obj["events"][0]["relocation_ok"] is True

@@ -165,3 +165,19 @@ def test_fill_reference_golden():
     assert indptr.tolist() == [0, 7, 13]
     assert indices.tolist() == [101, 102, 106, 107, 108, 109, 110, 201, 202, 203, 204, 205, 206]
     assert tokens.tolist() == [7, 6]
+
+
+@pytest.mark.parametrize("chunk", range(len(sc.REPLAY_CHUNKS)))
+def test_replay_error_matches_reference(chunk):
+    """Per-token layer error of the reference's static replay
+    (_replay_layer_difference, runtime:520-546) for a chunk before any
+    eviction (all zeros) and two chunks after a boundary."""
+    z = np.load(GOLD / "replay.npz")
+    d = sc.replay_setup()
+    lo, hi, evicted = sc.REPLAY_CHUNKS[chunk]
+    vis = sc.replay_visible(d["pos"], sc.REPLAY_FRONTIER, hi) if evicted else None
+    got = oracle.replay_error(d["q"][lo:hi], d["keys"], d["values"], lo, d["scale"], vis, d["sinks"])
+    want = z[f"chunk{chunk}"]
+    if not evicted:
+        assert not got.any() and not want.any()
+    np.testing.assert_allclose(got, want, rtol=5e-6, atol=1e-7)

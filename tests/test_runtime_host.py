@@ -20,7 +20,8 @@ def cpu_backend(rows=4, width=64, slots=100):
 
 
 @pytest.fixture(autouse=True)
-def fresh():
+def fresh(tmp_path, monkeypatch):
+    monkeypatch.setenv("GSTAR_PAYLOAD_DIR", str(tmp_path))
     ge.STATE = None
     ge.RETRACTED.clear()
     yield
@@ -29,9 +30,18 @@ def fresh():
 
 def req(rid="r", row=0, params=None, start=0, length=10, retraction=0, session=None):
     return SimpleNamespace(rid=rid, session=session, retraction_count=retraction,
+                           origin_input_ids=[0] * 12, output_ids=[1, 2],
                            kv=SimpleNamespace(req_pool_idx=row, holds_kv=True),
                            sampling_params=SimpleNamespace(custom_params=params),
                            extend_range=SimpleNamespace(start=start, length=length))
+
+
+def read_payload(key):
+    import gzip
+    import json
+    import os
+    from pathlib import Path
+    return json.loads(gzip.decompress((Path(os.environ["GSTAR_PAYLOAD_DIR"]) / f"{key}.json.gz").read_bytes()))
 
 
 CFG = {"name": "head_sum_2048", "budget": 1024, "prefix": 256, "recent": 256, "seed": 3}
@@ -83,6 +93,8 @@ def test_retraction_disables_the_entry():
     ge.on_extend(SimpleNamespace(reqs=[req(params={"gstar_eviction": CFG})]))
     ge.on_extend(SimpleNamespace(reqs=[req(params={"gstar_eviction": CFG}, retraction=1)]))
     assert ge.STATE.entries[0]["error"] == "retracted" and "r" in ge.RETRACTED
+    assert read_payload("r-retracted") == {"format": "gstar-payload-1", "key": "r-retracted", "kind": "retracted",
+                                           "cfg": CFG}
 
 
 def test_rewind_below_frontier_is_an_error():
@@ -110,6 +122,12 @@ def test_release_keeps_session_rows_and_resets_others():
     ge.on_extend(SimpleNamespace(reqs=[req(rid="b", row=1, params={"gstar_eviction": CFG})]))
     ge.release(req(rid="b", row=1))
     assert 1 not in ge.STATE.entries and int(ge.STATE.mode[1]) == 0
+    # the reference's event payloads (runtime:712-716, 738-741): the session's
+    # under "<key>-events", a plain request's under its rid
+    for key in ("session-s1-events", "b"):
+        ev = read_payload(key)
+        assert ev["kind"] == "events" and ev["cfg"] == CFG and ev["events"] == [] and ev["length"] == 14
+        assert ev["retracted"] is False and ev["verify_steps"] is None and ev["peak_full_entries"] == 0
 
 
 def test_filter_holes_and_freed():
