@@ -13,12 +13,15 @@
 // (16-query tile, KV head), M = 128 accumulator rows = 16 queries x the
 // group's 8 query heads:
 //
-//   split_lse_kernel  S = Q K^T streamed over key tiles; each row keeps two
-//                     online log2 sums, one over its visible keys and one over
-//                     its evicted keys (each key is exactly one of the two, so
-//                     one exp2 per element), and writes the full normaliser
-//                     lse_a (with the sink) and r = (evicted mass) / (visible
-//                     mass + sink), i.e. p_b = p_a (1 + r) on visible keys.
+//   split_lse_kernel  S = Q K^T streamed over key tiles; each row keeps one
+//                     running max and two online log2 sums under it, one over
+//                     its visible keys and one over its evicted keys (each key
+//                     is exactly one of the two, so one exp2 per element), and
+//                     writes the full normaliser lse_a (with the sink) and
+//                     r = (evicted mass) / (visible mass + sink), i.e.
+//                     p_b = p_a (1 + r) on visible keys; r comes from two
+//                     directly accumulated sums, not from the difference of
+//                     two normalisers.
 //   pv_kernel         S again; p_a = 2^(s - lse_a) and the difference
 //                     d = p_b - p_a (p_a r on visible keys, -p_a on evicted
 //                     ones), each split into a bf16 high part and a bf16
@@ -64,6 +67,11 @@ constexpr uint32_t TMEM1 = 2 * BN;       // two S accumulators
 constexpr uint32_t TMEM2 = 512;
 constexpr uint32_t OA_COL = 128, OD_COL = 192;
 constexpr uint32_t PAH_COL = 256, PAL_COL = 320, PDH_COL = 384, PDL_COL = 448;
+// Pass 2 runs sixteen epilogue warps: four per TMEM lane quarter, 32 keys of
+// each tile apiece.
+constexpr int EPI2 = 16;
+constexpr int THREADS2 = 32 * (EPI2 + 2);
+constexpr int LOAD2 = EPI2, MMA2 = EPI2 + 1;
 constexpr uint32_t IDESC_S = f16_idesc(BM, BN);
 constexpr uint32_t IDESC_PV = f16_idesc(BM, D) | kIdescBMajorMN;
 
@@ -101,14 +109,6 @@ __device__ __forceinline__ void named_barrier_epi() {
   asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
 }
 
-// (m, l) online pairs in log2 units: the sum of 2^m * l.
-__device__ __forceinline__ void merge(float& m, float& l, float m1, float l1) {
-  const float M = fmaxf(m, m1);
-  if (M == -INFINITY) return;
-  l = l * exp2f(m - M) + l1 * exp2f(m1 - M);
-  m = M;
-}
-
 // ---------------------------------------------------------------- pass 1
 struct Sync1 {
   uint64_t full[NS1], empty[NS1];
@@ -116,7 +116,7 @@ struct Sync1 {
   uint64_t once, mma_done;
   uint32_t tmem;
   int abort;
-  float part[4][BM];
+  float part[3][BM];
 };
 
 // CTA (16-query tile x, KV head g); accumulator row r = query 16x + r / 8,
@@ -217,7 +217,10 @@ __global__ void __launch_bounds__(THREADS, 2) split_lse_kernel(const Params p,
     const int q = q0 + r / GROUP;
     const int h = g * GROUP + r % GROUP;
     const int lim = p.start + min(q, p.count - 1);   // last causal key of this row
-    float mv = -INFINITY, lv = 0.f, me = -INFINITY, le = 0.f;
+    // One running max over all causal keys; the visible and the evicted
+    // sums share it, so each element costs one exponential whose value goes
+    // to exactly one of the two sums (the bit as an integer mask).
+    float m = -INFINITY, lv = 0.f, le = 0.f;
     for (int t = 0; t < ntiles; ++t) {
       const int buf = t & 1;
       if (!warp_wait(&sy->acc_full[buf], (t >> 1) & 1, p.err, abort, lane)) {
@@ -235,49 +238,55 @@ __global__ void __launch_bounds__(THREADS, 2) split_lse_kernel(const Params p,
       __syncwarp();
       if (lane == 0) mbar_arrive(&sy->acc_empty[buf]);
       const int kb = t * BN + half * 64;
-      uint32_t w0, w1;
-      vis_words(p, g, kb, w0, w1);
-      float xv = -INFINITY, xe = -INFINITY;
+      if (kb + 63 > lim) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = (kb + i <= lim) ? v[i] : -INFINITY;
+      }
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = v[i];
+#pragma unroll
+      for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], v[i]);
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float mn = fmaxf(m, mt * p.scale2);
+      if (mn == -INFINITY) continue;   // no causal key yet
+      uint32_t w[2];
+      vis_words(p, g, kb, w[0], w[1]);
+      float sv[2] = {0.f, 0.f}, se[2] = {0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
-        const bool ok = kb + i <= lim;
-        const bool b = bit_of(w0, w1, i);
-        xv = (ok && b) ? fmaxf(xv, v[i]) : xv;
-        xe = (ok && !b) ? fmaxf(xe, v[i]) : xe;
+        const float a = fmaf(v[i], p.scale2, -mn);
+        const float e = (i & 3) == 3 ? poly_exp2(a) : fast_exp2(a);
+        // all ones when bit i is set
+        const uint32_t bm = static_cast<uint32_t>(static_cast<int32_t>(w[i >> 5] << (31 - (i & 31))) >> 31);
+        const float ev = __uint_as_float(__float_as_uint(e) & bm);
+        sv[i & 1] += ev;
+        se[i & 1] += e - ev;
       }
-      const float mvn = fmaxf(mv, xv * p.scale2), men = fmaxf(me, xe * p.scale2);
-      float sv = 0.f, se = 0.f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const bool ok = kb + i <= lim;
-        const bool b = bit_of(w0, w1, i);
-        const float e = fast_exp2(fmaf(v[i], p.scale2, -(b ? mvn : men)));
-        sv += (ok && b) ? e : 0.f;
-        se += (ok && !b) ? e : 0.f;
-      }
-      if (mvn != -INFINITY) lv = lv * fast_exp2(mv - mvn) + sv;
-      if (men != -INFINITY) le = le * fast_exp2(me - men) + se;
-      mv = mvn;
-      me = men;
+      const float c = fast_exp2(m - mn);   // 0 while m is -inf
+      lv = lv * c + (sv[0] + sv[1]);
+      le = le * c + (se[0] + se[1]);
+      m = mn;
     }
     if (half == 1) {
-      sy->part[0][r] = mv;
+      sy->part[0][r] = m;
       sy->part[1][r] = lv;
-      sy->part[2][r] = me;
-      sy->part[3][r] = le;
+      sy->part[2][r] = le;
     }
     named_barrier_epi();
     if (half == 0 && !*abort && q < p.count) {
-      merge(mv, lv, sy->part[0][r], sy->part[1][r]);
-      merge(me, le, sy->part[2][r], sy->part[3][r]);
-      // Visible normaliser with the sink, then the full one.
-      float Mv = mv, Lv = lv;
-      if (p.sinks) merge(Mv, Lv, p.sinks[h] * LOG2E, 1.f);
-      float Ma = Mv, La = Lv;
-      merge(Ma, La, me, le);
+      const float m1 = sy->part[0][r];
+      const float M = fmaxf(m, m1);      // finite: key 0 is causal for every row
+      const float c0 = exp2f(m - M), c1 = exp2f(m1 - M);
+      float Lv = lv * c0 + sy->part[1][r] * c1;
+      const float Le = le * c0 + sy->part[2][r] * c1;
+      if (p.sinks) Lv += exp2f(p.sinks[h] * LOG2E - M);
       const int64_t o = static_cast<int64_t>(q) * p.H + h;
-      p.lse2[o] = Ma + log2f(La);
-      p.ratio[o] = (le == 0.f) ? 0.f : (Lv == 0.f ? INFINITY : le * exp2f(me - Mv) / Lv);
+      p.lse2[o] = M + log2f(Lv + Le);
+      // p_b = p_a (1 + r) on visible keys; a row with no visible mass left
+      // (nothing visible, no sink) has no visible key to scale.
+      p.ratio[o] = Lv > 0.f ? fminf(Le / Lv, 1e30f) : 0.f;
     }
   }
   tc_fence_before();
@@ -303,7 +312,7 @@ static_assert(SMEM2 <= 227 * 1024 && 2 * SMEM2 > 228 * 1024, "pass 2: one CTA pe
 static_assert(2 * SMEM1 <= 227 * 1024, "two pass-1 CTAs per SM");
 static_assert(3 * SMEM1 > 227 * 1024, "a third pass-1 CTA would oversubscribe TMEM");
 
-__global__ void __launch_bounds__(THREADS, 1) pv_kernel(const Params p, const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(THREADS2, 1) pv_kernel(const Params p, const __grid_constant__ CUtensorMap qmap,
                                                          const __grid_constant__ CUtensorMap kmap,
                                                          const __grid_constant__ CUtensorMap vmap) {
   const int g = blockIdx.y;
@@ -325,8 +334,8 @@ __global__ void __launch_bounds__(THREADS, 1) pv_kernel(const Params p, const __
       mbar_init(&sy->empty[s], 1);
     }
     mbar_init(&sy->sfull, 1);
-    mbar_init(&sy->sempty, EPI_WARPS);
-    mbar_init(&sy->pfull, EPI_WARPS);
+    mbar_init(&sy->sempty, EPI2);
+    mbar_init(&sy->pfull, EPI2);
     mbar_init(&sy->pempty, 1);
     mbar_init(&sy->once, 1);
     mbar_init(&sy->odone, 1);
@@ -334,13 +343,13 @@ __global__ void __launch_bounds__(THREADS, 1) pv_kernel(const Params p, const __
     sy->abort = 0;
     fence_mbar_init();
   }
-  if (warp == MMA_WARP) tmem_alloc(&sy->tmem, TMEM2);
+  if (warp == MMA2) tmem_alloc(&sy->tmem, TMEM2);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sy->tmem;
 
-  if (warp == LOAD_WARP) {
+  if (warp == LOAD2) {
     int t = 0;
     if (lane == 0) {
       mbar_arrive_expect_tx(&sy->once, TILE);
@@ -363,7 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1) pv_kernel(const Params p, const __
       for (int u = max(0, t - NS2); u < t; ++u) mbar_wait(&sy->full[u % NS2], (u / NS2) & 1, p.err);
       mbar_wait(&sy->once, 0, p.err);
     }
-  } else if (warp == MMA_WARP) {
+  } else if (warp == MMA2) {
     // Order: S(0), S(1), PV(0), S(2), PV(1), ... so the epilogue turns S(t+1)
     // into P while the tensor cores run PV(t).
     bool issued = false;
@@ -419,7 +428,9 @@ __global__ void __launch_bounds__(THREADS, 1) pv_kernel(const Params p, const __
     }
     __syncwarp();
   } else {
-    const int quarter = warp & 3, half = warp >> 2;
+    // Warp e: TMEM lanes 32 (e % 4) .. +31, keys 32 (e / 4) .. +31 of each
+    // tile = columns 16 (e / 4) .. +15 of each P tile and of O.
+    const int quarter = warp & 3, part = warp >> 2;
     const int r = quarter * 32 + lane;
     const int q = q0 + r / GROUP;
     const int h = g * GROUP + r % GROUP;
@@ -436,45 +447,42 @@ __global__ void __launch_bounds__(THREADS, 1) pv_kernel(const Params p, const __
         break;
       }
       tc_fence_after();
-      float v[64];
+      float v[32];
       __syncwarp();
-      tmem_ld32_async(tmem + lane_base + half * 64, v);
-      tmem_ld32_async(tmem + lane_base + half * 64 + 32, v + 32);
-      tmem_ld_wait();
+      tmem_ld32(tmem + lane_base + part * 32, v);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sy->sempty);
-      const int kb = t * BN + half * 64;
-      uint32_t w0, w1;
-      vis_words(p, g, kb, w0, w1);
+      const int kb = t * BN + part * 32;
+      uint32_t w, w_unused;
+      vis_words(p, g, kb, w, w_unused);
       if (t >= 1 && !warp_wait(&sy->pempty, (t - 1) & 1, p.err, abort, lane)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // Keys kb .. kb + 63 = 32 columns of each P tile, in two halves of 16.
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t ah[16], al[16], dh[16], dl[16];
+      for (int hh = 0; hh < 2; ++hh) {   // keys 16 hh .. +15 of this warp's 32
+        uint32_t ah[8], al[8], dh[8], dl[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < 8; ++j) {
           float e[2], d[2];
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
-            const int i = hh * 32 + 2 * j + x;
+            const int i = hh * 16 + 2 * j + x;
             const bool in = qv && kb + i <= lim;
             const float y = in ? fast_exp2(fmaf(v[i], p.scale2, -lse)) : 0.f;
             e[x] = y;
-            d[x] = bit_of(w0, w1, i) ? y * rr : -y;
+            d[x] = ((w >> i) & 1u) ? y * rr : -y;
           }
           split_bf16x2(e[0], e[1], ah[j], al[j]);
           split_bf16x2(d[0], d[1], dh[j], dl[j]);
         }
-        const uint32_t col = lane_base + half * 32 + hh * 16;
-        tmem_st16_async(tmem + col + PAH_COL, ah);
-        tmem_st16_async(tmem + col + PAL_COL, al);
-        tmem_st16_async(tmem + col + PDH_COL, dh);
-        tmem_st16_async(tmem + col + PDL_COL, dl);
+        const uint32_t col = lane_base + part * 16 + hh * 8;
+        tmem_st8_async(tmem + col + PAH_COL, ah);
+        tmem_st8_async(tmem + col + PAL_COL, al);
+        tmem_st8_async(tmem + col + PDH_COL, dh);
+        tmem_st8_async(tmem + col + PDL_COL, dl);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -484,21 +492,21 @@ __global__ void __launch_bounds__(THREADS, 1) pv_kernel(const Params p, const __
     if (!ok) *abort = 1;
     if (ok && warp_wait(&sy->odone, 0, p.err, abort, lane)) {
       tc_fence_after();
-      float a[32], d[32];
+      float a[16], d[16];
       __syncwarp();
-      tmem_ld32_async(tmem + lane_base + OA_COL + half * 32, a);
-      tmem_ld32_async(tmem + lane_base + OD_COL + half * 32, d);
+      tmem_ld16_async(tmem + lane_base + OA_COL + part * 16, a);
+      tmem_ld16_async(tmem + lane_base + OD_COL + part * 16, d);
       tmem_ld_wait();
       float sa = 0.f, sd = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         sa = fmaf(a[i], a[i], sa);
         sd = fmaf(d[i], d[i], sd);
       }
       if (p.out && qv) {
-        float4* dst = reinterpret_cast<float4*>(p.out + (o * D + half * 32));
+        float4* dst = reinterpret_cast<float4*>(p.out + (o * D + part * 16));
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 4; ++i)
           dst[i] = make_float4(a[4 * i] + d[4 * i], a[4 * i + 1] + d[4 * i + 1], a[4 * i + 2] + d[4 * i + 2],
                                a[4 * i + 3] + d[4 * i + 3]);
       }
@@ -517,7 +525,7 @@ __global__ void __launch_bounds__(THREADS, 1) pv_kernel(const Params p, const __
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == MMA_WARP) tmem_dealloc(tmem, TMEM2);
+  if (warp == MMA2) tmem_dealloc(tmem, TMEM2);
 }
 
 __global__ void finish_kernel(const Params p) {
@@ -612,7 +620,7 @@ extern "C" int ce_replay_error(const void* q, int64_t q_st, int64_t q_sh, const 
   const dim3 grid((count + QT - 1) / QT, num_kv_heads);
   split_lse_kernel<<<grid, THREADS, SMEM1, st>>>(p, qmap, kmap);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("replay split_lse_kernel");
-  pv_kernel<<<grid, THREADS, SMEM2, st>>>(p, qmap, kmap, vmap);
+  pv_kernel<<<grid, THREADS2, SMEM2, st>>>(p, qmap, kmap, vmap);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("replay pv_kernel");
   finish_kernel<<<(count + 255) / 256, 256, 0, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("replay finish_kernel");
