@@ -358,54 +358,70 @@ struct LargeSel {
 
 __device__ __forceinline__ bool is_bit(const uint32_t* m, int c) { return (m[c >> 5] >> (c & 31)) & 1u; }
 
-// Pass over the inputs: prefixes, protected bits, histogram; returns this
-// thread's protected count (the caller reduces it).  With `vec`, col4fn
-// fills four consecutive columns from 16-byte loads (a quarter of the memory
-// requests of per-column loads, which is what bounds this pass); the tail
-// and the general case use colfn.
-constexpr int LQ = 4;   // quads per thread per batch
-template <class ColFn, class Col4Fn>
-__device__ int large_scan(ColFn colfn, Col4Fn col4fn, bool vec, int N, int kind, const LargeBuf& lb) {
+// Pass over the inputs: prefixes, protected bits, histogram.  large_init
+// clears the buffers; scan_quads takes four consecutive columns per 16-byte
+// load (a quarter of the memory requests of per-column loads, which is what
+// bounds this pass), issuing a whole batch of loads before it computes any
+// key so that many loads are in flight per thread; large_tail takes single
+// columns (the tail of a quad scan, or every column) through colfn.  Both
+// return this thread's protected count (the caller reduces it).
+__device__ __forceinline__ void large_init(int N, const LargeBuf& lb) {
   for (int i = threadIdx.x; i < LHIST; i += T) lb.hist[i] = 0;
   for (int i = threadIdx.x; i < (N + 31) / 32; i += T) {
     lb.prot[i] = 0u;
     lb.pick[i] = 0u;
   }
   __syncthreads();
+}
+
+// Bins, histogram and protected bits of one quad (columns 4q .. 4q + 3).
+__device__ __forceinline__ int large_quad(int q, const uint64_t (&key)[4], const bool (&pr)[4], int kind,
+                                          const LargeBuf& lb) {
   int np = 0;
-  int cstart = 0;
-  if (vec) {
-    const int nq = N / 4;
-    for (int q0 = threadIdx.x; q0 < nq; q0 += LQ * T) {
-      uint64_t key[LQ][4];
-      int32_t pv[LQ][4];
-      bool pr[LQ][4];
+  uint32_t pm = 0u;
+  uint64_t packed = 0ull;
 #pragma unroll
-      for (int u = 0; u < LQ; ++u)
-        if (q0 + u * T < nq) col4fn(4 * (q0 + u * T), key[u], pv[u], pr[u]);
-#pragma unroll
-      for (int u = 0; u < LQ; ++u) {
-        const int q = q0 + u * T;
-        if (q >= nq) continue;
-        uint32_t pm = 0u;
-        uint64_t packed = 0ull;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (pr[u][e]) {
-            ++np;
-            pm |= 1u << e;
-          } else {
-            const uint32_t b = bin16_of(key[u][e], kind);
-            packed |= static_cast<uint64_t>(b) << (16 * e);
-            atomicAdd(&lb.hist[b >> 4], 1);
-          }
-        }
-        *reinterpret_cast<uint64_t*>(lb.bin + 4 * q) = packed;
-        if (pm) atomicOr(&lb.prot[q >> 3], pm << (4 * (q & 7)));
-      }
+  for (int e = 0; e < 4; ++e) {
+    if (pr[e]) {
+      ++np;
+      pm |= 1u << e;
+    } else {
+      const uint32_t b = bin16_of(key[e], kind);
+      packed |= static_cast<uint64_t>(b) << (16 * e);
+      atomicAdd(&lb.hist[b >> 4], 1);
     }
-    cstart = 4 * nq;
   }
+  *reinterpret_cast<uint64_t*>(lb.bin + 4 * q) = packed;
+  if (pm) atomicOr(&lb.prot[q >> 3], pm << (4 * (q & 7)));
+  return np;
+}
+
+// Qd supplies Raw (the loaded words of a quad), load(c, raw) (loads only) and
+// make(raw, key, pr) (keys and protection from the loaded words).
+template <int LQN, class Qd>
+__device__ int scan_quads(const Qd& qd, int nq, int kind, const LargeBuf& lb) {
+  int np = 0;
+  for (int q0 = threadIdx.x; q0 < nq; q0 += LQN * T) {
+    typename Qd::Raw raw[LQN];
+#pragma unroll
+    for (int u = 0; u < LQN; ++u)
+      if (q0 + u * T < nq) qd.load(4 * (q0 + u * T), raw[u]);
+#pragma unroll
+    for (int u = 0; u < LQN; ++u) {
+      const int q = q0 + u * T;
+      if (q >= nq) continue;
+      uint64_t key[4];
+      bool pr[4];
+      qd.make(raw[u], key, pr);
+      np += large_quad(q, key, pr, kind, lb);
+    }
+  }
+  return np;
+}
+
+template <class ColFn>
+__device__ int large_tail(ColFn colfn, int cstart, int N, int kind, const LargeBuf& lb) {
+  int np = 0;
   constexpr int LB = LARGE_LB;
   for (int c0 = cstart + threadIdx.x; c0 < N; c0 += LB * T) {
     uint64_t key[LB];
@@ -432,6 +448,24 @@ __device__ int large_scan(ColFn colfn, Col4Fn col4fn, bool vec, int N, int kind,
     }
   }
   return np;
+}
+
+// Columns 32 w .. 32 w + 31 that exist (w < (N + 31) / 32).
+__device__ __forceinline__ uint32_t valid_bits(int w, int N) {
+  const int n = N - 32 * w;
+  return n >= 32 ? ~0u : ((1u << n) - 1u);
+}
+
+// The 16-bit prefixes of columns 32 w .. 32 w + 31 as eight 8-byte shared
+// loads: element 4 j + e of the word is bits 16 (e & 1) of bb[j][e >> 1].
+__device__ __forceinline__ void bins32(const LargeBuf& lb, int w, uint2 (&bb)[8]) {
+  const uint2* b2 = reinterpret_cast<const uint2*>(lb.bin + 32 * w);   // 8-byte aligned
+#pragma unroll
+  for (int j = 0; j < 8; ++j) bb[j] = b2[j];
+}
+__device__ __forceinline__ uint32_t bin_at(const uint2 (&bb)[8], int i) {
+  const uint32_t v = (i & 2) ? bb[i >> 2].y : bb[i >> 2].x;
+  return (i & 1) ? (v >> 16) : (v & 0xFFFFu);
 }
 
 // The k largest of the nonprot unprotected columns (0 < k < nonprot handled
@@ -477,9 +511,16 @@ __device__ bool large_select(ColFn colfn, int N, int k, int nonprot, int kind, c
   // Its 16 sub-bins.
   if (threadIdx.x < 16) lb.hist[threadIdx.x] = 0;
   __syncthreads();
-  for (int c = threadIdx.x; c < N; c += T) {
-    const uint32_t b = lb.bin[c];
-    if ((b >> 4) == static_cast<uint32_t>(t12) && !is_bit(lb.prot, c)) atomicAdd(&lb.hist[b & 15], 1);
+  const int nw = (N + 31) / 32;
+  for (int w = threadIdx.x; w < nw; w += T) {
+    const uint32_t unprot = ~lb.prot[w] & valid_bits(w, N);
+    uint2 bb[8];
+    bins32(lb, w, bb);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const uint32_t b = bin_at(bb, i);
+      if (((unprot >> i) & 1u) && (b >> 4) == static_cast<uint32_t>(t12)) atomicAdd(&lb.hist[b & 15], 1);
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -505,16 +546,26 @@ __device__ bool large_select(ColFn colfn, int N, int k, int nonprot, int kind, c
   }
   if (eq16 > LCAND) return false;
   // Candidates: full keys of the columns with prefix t16 (hist is dead now).
-  for (int c = threadIdx.x; c < N; c += T) {
-    if (lb.bin[c] != t16 || is_bit(lb.prot, c)) continue;
-    uint64_t key;
-    int32_t pv;
-    colfn(c, key, pv);
-    const int idx = atomicAdd(&sh.bc[5], 1);
-    if (idx < LCAND) {
-      lb.ckey[idx] = key;
-      lb.cpv[idx] = pv;
-      lb.ccol[idx] = c;
+  for (int w = threadIdx.x; w < nw; w += T) {
+    const uint32_t unprot = ~lb.prot[w] & valid_bits(w, N);
+    uint2 bb[8];
+    bins32(lb, w, bb);
+    uint32_t hit = 0u;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) hit |= (bin_at(bb, i) == static_cast<uint32_t>(t16)) ? (1u << i) : 0u;
+    hit &= unprot;
+    while (hit) {
+      const int c = 32 * w + __ffs(hit) - 1;
+      hit &= hit - 1;
+      uint64_t key;
+      int32_t pv;
+      colfn(c, key, pv);
+      const int idx = atomicAdd(&sh.bc[5], 1);
+      if (idx < LCAND) {
+        lb.ckey[idx] = key;
+        lb.cpv[idx] = pv;
+        lb.ccol[idx] = c;
+      }
     }
   }
   __syncthreads();
@@ -526,71 +577,119 @@ __device__ bool large_select(ColFn colfn, int N, int k, int nonprot, int kind, c
   return true;
 }
 
-__device__ __forceinline__ bool large_kept(const LargeBuf& lb, const LargeSel& r, int c) {
-  if (r.none) return false;
-  if (r.all) return true;
-  const int b = lb.bin[c];
-  return b > r.t16 || (b == r.t16 && (r.all_eq || is_bit(lb.pick, c)));
+// Kept columns of a large segment as a bitmap kb[(N + 31) / 32] (shared
+// memory), one pass of 8-byte prefix loads: the chosen unprotected columns
+// (prefix above the threshold's, or equal to it and picked), plus the
+// protected ones when WITH_PROT.
+template <bool WITH_PROT>
+__device__ void large_kept_bits(const LargeBuf& lb, const LargeSel& r, int N, uint32_t* kb) {
+  const int nw = (N + 31) / 32;
+  for (int w = threadIdx.x; w < nw; w += T) {
+    const uint32_t prot = lb.prot[w];
+    uint32_t sel = 0u;
+    if (r.all) {
+      sel = ~0u;
+    } else if (!r.none) {
+      const uint32_t pick = r.all_eq ? ~0u : lb.pick[w];
+      uint2 bb[8];
+      bins32(lb, w, bb);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint32_t b = bin_at(bb, i);
+        const bool k = b > static_cast<uint32_t>(r.t16) || (b == static_cast<uint32_t>(r.t16) && ((pick >> i) & 1u));
+        sel |= k ? (1u << i) : 0u;
+      }
+    }
+    sel &= ~prot & valid_bits(w, N);
+    kb[w] = WITH_PROT ? (sel | prot) : sel;
+  }
+  __syncthreads();
 }
 
-// Columns whose keep(c) holds, each with its position pos(c) (read only for
-// kept columns), as emit_sorted's column set.  With pos4 (vec), positions of
-// four consecutive columns come from one 16-byte load.
-template <class KeepF, class PosF, class Pos4F>
-struct KeptCols {
+// The columns set in kb, each with its position pos(c) (read only for kept
+// columns), as emit_sorted's column set.  With pos4 (vec), positions of four
+// consecutive columns come from one 16-byte load.  Each thread marks which of
+// its next 32 quads (columns) hold a kept column, then loads the positions of
+// the marked ones eight at a time, so a pass costs one load latency per eight
+// kept quads of a thread.
+template <class PosF, class Pos4F>
+struct KeptBits {
   int N;
-  KeepF keep;
+  const uint32_t* kb;
   PosF pos;
   Pos4F pos4;
   bool vec;
+  static constexpr int B = 8;
   template <class F>
   __device__ __forceinline__ void each(F f) const {
     int cstart = 0;
     if (vec) {
       const int nq = N / 4;
-      for (int q0 = threadIdx.x; q0 < nq; q0 += LQ * T) {
-        uint32_t km[LQ];
-        int4 ps[LQ];
-#pragma unroll
-        for (int u = 0; u < LQ; ++u) {
-          const int q = q0 + u * T;
-          km[u] = 0u;
-          if (q < nq)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) km[u] |= keep(4 * q + e) ? (1u << e) : 0u;
-          ps[u] = km[u] ? pos4(4 * q) : make_int4(0, 0, 0, 0);
+      for (int j0 = 0; j0 * T < nq; j0 += 32) {
+        uint32_t m = 0u;   // bit jj: quad threadIdx.x + (j0 + jj) T holds a kept column
+#pragma unroll 4
+        for (int jj = 0; jj < 32; ++jj) {
+          const int q = threadIdx.x + (j0 + jj) * T;
+          if (q < nq && ((kb[q >> 3] >> (4 * (q & 7))) & 15u)) m |= 1u << jj;
         }
+        while (m) {
+          int qs[B];
+          int4 ps[B];
 #pragma unroll
-        for (int u = 0; u < LQ; ++u) {
-          const int c = 4 * (q0 + u * T);
-          if (km[u] & 1u) f(c, 0ull, ps[u].x);
-          if (km[u] & 2u) f(c + 1, 0ull, ps[u].y);
-          if (km[u] & 4u) f(c + 2, 0ull, ps[u].z);
-          if (km[u] & 8u) f(c + 3, 0ull, ps[u].w);
+          for (int b = 0; b < B; ++b) {
+            qs[b] = -1;
+            ps[b] = make_int4(0, 0, 0, 0);
+            if (m) {
+              qs[b] = threadIdx.x + (j0 + __ffs(m) - 1) * T;
+              m &= m - 1;
+              ps[b] = pos4(4 * qs[b]);
+            }
+          }
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            if (qs[b] < 0) continue;
+            const int c = 4 * qs[b];
+            const uint32_t km = (kb[qs[b] >> 3] >> (4 * (qs[b] & 7))) & 15u;
+            if (km & 1u) f(c, 0ull, ps[b].x);
+            if (km & 2u) f(c + 1, 0ull, ps[b].y);
+            if (km & 4u) f(c + 2, 0ull, ps[b].z);
+            if (km & 8u) f(c + 3, 0ull, ps[b].w);
+          }
         }
       }
       cstart = 4 * nq;
     }
-    constexpr int LB = LARGE_LB;   // positions of a batch of kept columns load together
-    for (int c0 = cstart + threadIdx.x; c0 < N; c0 += LB * T) {
-      bool kp[LB];
-      int32_t ps[LB];
-#pragma unroll
-      for (int u = 0; u < LB; ++u) {
-        const int c = c0 + u * T;
-        kp[u] = c < N && keep(c);
-        ps[u] = kp[u] ? pos(c) : 0;
+    for (int j0 = 0; cstart + j0 * T < N; j0 += 32) {
+      uint32_t m = 0u;     // bit jj: column cstart + threadIdx.x + (j0 + jj) T is kept
+#pragma unroll 4
+      for (int jj = 0; jj < 32; ++jj) {
+        const int c = cstart + threadIdx.x + (j0 + jj) * T;
+        if (c < N && ((kb[c >> 5] >> (c & 31)) & 1u)) m |= 1u << jj;
       }
+      while (m) {
+        int cs[B];
+        int32_t ps[B];
 #pragma unroll
-      for (int u = 0; u < LB; ++u)
-        if (kp[u]) f(c0 + u * T, 0ull, ps[u]);
+        for (int b = 0; b < B; ++b) {
+          cs[b] = -1;
+          ps[b] = 0;
+          if (m) {
+            cs[b] = cstart + threadIdx.x + (j0 + __ffs(m) - 1) * T;
+            m &= m - 1;
+            ps[b] = pos(cs[b]);
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+          if (cs[b] >= 0) f(cs[b], 0ull, ps[b]);
+      }
     }
   }
 };
-template <class KeepF, class PosF, class Pos4F>
-__device__ __forceinline__ KeptCols<KeepF, PosF, Pos4F> kept_cols(int N, KeepF keep, PosF pos, Pos4F pos4,
-                                                                 bool vec) {
-  return KeptCols<KeepF, PosF, Pos4F>{N, keep, pos, pos4, vec};
+template <class PosF, class Pos4F>
+__device__ __forceinline__ KeptBits<PosF, Pos4F> kept_bits(int N, const uint32_t* kb, PosF pos, Pos4F pos4,
+                                                           bool vec) {
+  return KeptBits<PosF, Pos4F>{N, kb, pos, pos4, vec};
 }
 
 // ============================== ce_choose ========================================
@@ -656,61 +755,70 @@ __device__ __forceinline__ bool choose_column(const ChooseParams& p, int i, int 
   return pr;
 }
 
-// Columns c..c+3 of the segment from 16-byte loads (c % 4 == 0; the caller
-// checked alignment): same keys as choose_column.
-__device__ __forceinline__ void choose_column4(const ChooseParams& p, int i, int l, int g, int64_t base,
-                                               const ce_row_params& q, int c, uint64_t (&key)[4],
-                                               int32_t (&pv)[4], bool (&pr)[4]) {
-  const int segs = p.layers * p.heads;
-  const int4 pp = *reinterpret_cast<const int4*>(p.pos + base + c);
-  const int pos[4] = {pp.x, pp.y, pp.z, pp.w};
-  uint64_t k[4] = {0ull, 0ull, 0ull, 0ull};
-  switch (q.policy) {
-    case CE_POLICY_RESERVOIR:
-#pragma unroll
-      for (int e = 0; e < 4; ++e) k[e] = reservoir53(q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos[e]));
-      break;
-    case CE_POLICY_H2O_GLOBAL:
-      if (p.sdt == CE_DTYPE_F64) {
-        double a[4] = {0.0, 0.0, 0.0, 0.0};
-        for (int gg = 0; gg < p.heads; ++gg) {
-          const double2* s2 = reinterpret_cast<const double2*>(
-              static_cast<const double*>(p.score) + (static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c);
-          const double2 x = s2[0], y = s2[1];
-          a[0] += x.x; a[1] += x.y; a[2] += y.x; a[3] += y.y;
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) k[e] = key_from_f64(a[e]);
-      } else {
-        float a[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int gg = 0; gg < p.heads; ++gg) {
-          const float4 x = *reinterpret_cast<const float4*>(
-              static_cast<const float*>(p.score) + (static_cast<int64_t>(i) * segs + l * p.heads + gg) * p.n_cols + c);
-          a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) k[e] = key_from_f32(a[e]);
+// Columns c..c+3 of a ce_choose segment from 16-byte loads (c % 4 == 0; the
+// host checked alignment), for scan_quads: the same keys as choose_column.
+// SRC fixes where the key comes from, so load() is straight-line loads.
+enum QuadSrc { QS_POS = 0, QS_F32 = 1, QS_F64 = 2, QS_H2O_F32 = 3, QS_H2O_F64 = 4 };
+template <int SRC>
+struct ChooseQuads {
+  const ChooseParams* p;
+  int64_t base, hbase;   // this segment's columns; head 0 of its layer (H2O global)
+  ce_row_params q;
+  uint64_t head;          // global KV head index (reservoir draws)
+  int l;
+  struct Raw {
+    int4 pos;
+    float4 f;
+    double2 d0, d1;
+  };
+  __device__ __forceinline__ void load(int c, Raw& r) const {
+    r.pos = *reinterpret_cast<const int4*>(p->pos + base + c);
+    if constexpr (SRC == QS_F32) {
+      r.f = *reinterpret_cast<const float4*>(static_cast<const float*>(p->score) + base + c);
+    } else if constexpr (SRC == QS_F64) {
+      const double2* s2 = reinterpret_cast<const double2*>(static_cast<const double*>(p->score) + base + c);
+      r.d0 = s2[0];
+      r.d1 = s2[1];
+    } else if constexpr (SRC == QS_H2O_F32) {
+      // fp32 sum over the layer's heads in ascending head order
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int gg = 0; gg < p->heads; ++gg) {
+        const float4 x = *reinterpret_cast<const float4*>(static_cast<const float*>(p->score) + hbase +
+                                                           static_cast<int64_t>(gg) * p->n_cols + c);
+        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
       }
-      break;
-    case CE_POLICY_PREFIX_SLIDING:
-      break;
-    default:
-      if (p.sdt == CE_DTYPE_F64) {
-        const double2* s2 = reinterpret_cast<const double2*>(static_cast<const double*>(p.score) + base + c);
+      r.f = a;
+    } else if constexpr (SRC == QS_H2O_F64) {
+      double2 a0 = make_double2(0.0, 0.0), a1 = make_double2(0.0, 0.0);
+      for (int gg = 0; gg < p->heads; ++gg) {
+        const double2* s2 = reinterpret_cast<const double2*>(static_cast<const double*>(p->score) + hbase +
+                                                             static_cast<int64_t>(gg) * p->n_cols + c);
         const double2 x = s2[0], y = s2[1];
-        k[0] = key_from_f64(x.x); k[1] = key_from_f64(x.y); k[2] = key_from_f64(y.x); k[3] = key_from_f64(y.y);
-      } else {
-        const float4 x = *reinterpret_cast<const float4*>(static_cast<const float*>(p.score) + base + c);
-        k[0] = key_from_f32(x.x); k[1] = key_from_f32(x.y); k[2] = key_from_f32(x.z); k[3] = key_from_f32(x.w);
+        a0.x += x.x; a0.y += x.y; a1.x += y.x; a1.y += y.y;
       }
+      r.d0 = a0;
+      r.d1 = a1;
+    }
   }
+  __device__ __forceinline__ void make(const Raw& r, uint64_t (&key)[4], bool (&pr)[4]) const {
+    const int pos[4] = {r.pos.x, r.pos.y, r.pos.z, r.pos.w};
+    uint64_t k[4] = {0ull, 0ull, 0ull, 0ull};
+    if constexpr (SRC == QS_POS) {
+      if (q.policy == CE_POLICY_RESERVOIR)
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    pr[e] = is_prot(pos[e], q);
-    pv[e] = pos[e] | (pr[e] ? static_cast<int>(0x80000000u) : 0);
-    key[e] = pr[e] ? 0 : k[e];
+        for (int e = 0; e < 4; ++e) k[e] = reservoir53(q.seed, l, head, static_cast<uint64_t>(pos[e]));
+    } else if constexpr (SRC == QS_F32 || SRC == QS_H2O_F32) {
+      k[0] = key_from_f32(r.f.x); k[1] = key_from_f32(r.f.y); k[2] = key_from_f32(r.f.z); k[3] = key_from_f32(r.f.w);
+    } else {
+      k[0] = key_from_f64(r.d0.x); k[1] = key_from_f64(r.d0.y); k[2] = key_from_f64(r.d1.x); k[3] = key_from_f64(r.d1.y);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      pr[e] = is_prot(pos[e], q);
+      key[e] = pr[e] ? 0 : k[e];
+    }
   }
-}
+};
 
 template <class Cols>
 __device__ void choose_body(const ChooseParams& p, const Cols& cols, int np, int i, int s, int N,
@@ -749,10 +857,25 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
   auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool {
     return choose_column(p, i, l, g, base, q, c, key, pv);
   };
-  auto col4fn = [&](int c, uint64_t(&key)[4], int32_t(&pv)[4], bool(&pr)[4]) {
-    choose_column4(p, i, l, g, base, q, c, key, pv, pr);
-  };
-  const int nprot = block_sum(large_scan(colfn, col4fn, p.vec4 != 0, N, kind, lb), sh);
+  large_init(N, lb);
+  int np = 0, cstart = 0;
+  if (p.vec4) {
+    // Quads per thread per batch, by the registers a quad's loaded words take.
+    const int nq = N / 4;
+    const int64_t hbase = (static_cast<int64_t>(i) * segs + l * p.heads) * p.n_cols;
+    const uint64_t head = static_cast<uint64_t>(p.head_offset + g);
+    if (q.policy == CE_POLICY_RESERVOIR || q.policy == CE_POLICY_PREFIX_SLIDING)
+      np = scan_quads<16>(ChooseQuads<QS_POS>{&p, base, hbase, q, head, l}, nq, kind, lb);
+    else if (q.policy == CE_POLICY_H2O_GLOBAL)
+      np = p.sdt == CE_DTYPE_F64 ? scan_quads<2>(ChooseQuads<QS_H2O_F64>{&p, base, hbase, q, head, l}, nq, kind, lb)
+                                 : scan_quads<4>(ChooseQuads<QS_H2O_F32>{&p, base, hbase, q, head, l}, nq, kind, lb);
+    else
+      np = p.sdt == CE_DTYPE_F64 ? scan_quads<6>(ChooseQuads<QS_F64>{&p, base, hbase, q, head, l}, nq, kind, lb)
+                                 : scan_quads<8>(ChooseQuads<QS_F32>{&p, base, hbase, q, head, l}, nq, kind, lb);
+    cstart = 4 * nq;
+  }
+  np += large_tail(colfn, cstart, N, kind, lb);
+  const int nprot = block_sum(np, sh);
   if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * segs + s] = nprot;
   if (nprot > q.budget) return true;
   const int k = (q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : q.budget - nprot;
@@ -762,9 +885,11 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
   const int stride = p.kept_stride;
   int32_t* err = p.err;
   const int32_t* pos = p.pos + base;
+  // kept bitmap in the histogram's storage (dead once the threshold is known)
+  uint32_t* kb = reinterpret_cast<uint32_t*>(lb.hist);
+  large_kept_bits<true>(lb, sel, N, kb);
   emit_sorted(
-      kept_cols(N, [&](int c) { return is_bit(lb.prot, c) || large_kept(lb, sel, c); },
-                [&](int c) { return pos[c]; },
+      kept_bits(N, kb, [&](int c) { return pos[c]; },
                 [&](int c) { return *reinterpret_cast<const int4*>(pos + c); }, p.vec4 != 0),
       p.nw, dyn, reinterpret_cast<int*>(dyn + p.nw), [](int, uint64_t, int32_t pc) -> int { return pc; },
       [&](int rank, int c, int) {
@@ -1014,16 +1139,17 @@ __device__ bool bsel_large(const BParams& p, const RowCtx& r, int i, int lg, int
                    : (r.q.policy == CE_POLICY_RANDOM && p.udt == CE_DTYPE_F64) ? BIN_U64
                                                                               : BIN_K32;
   auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool { return bsel_column(p, r, i, lg, c, key, pv); };
-  auto col4fn = [](int, uint64_t(&)[4], int32_t(&)[4], bool(&)[4]) {};
-  const int nprot = block_sum(large_scan(colfn, col4fn, false, r.N, kind, lb), sh);
+  large_init(r.N, lb);
+  const int nprot = block_sum(large_tail(colfn, 0, r.N, kind, lb), sh);
   if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
   if (nprot > r.q.budget) return true;
   const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
   LargeSel sel;
   if (!large_select(colfn, r.N, k, r.N - nprot, kind, lb, sh, sel)) return false;
+  uint32_t* kb = reinterpret_cast<uint32_t*>(lb.hist);
+  large_kept_bits<false>(lb, sel, r.N, kb);
   bsel_emit(p, r,
-            kept_cols(r.N, [&](int c) { return !is_bit(lb.prot, c) && large_kept(lb, sel, c); },
-                      [&](int c) { return col_pos(p, r, lg, c); },
+            kept_bits(r.N, kb, [&](int c) { return col_pos(p, r, lg, c); },
                       [](int) { return make_int4(0, 0, 0, 0); }, false),
             [](int, uint64_t, int32_t pc) -> int { return pc; }, nprot, i, lg, base, sh, bitsm, pre);
   return true;

@@ -232,9 +232,12 @@ def choose(pos, score, params: torch.Tensor, layers, heads, max_n, ncols=None, h
     problems, segs, n_cols = pos.shape
     dev = pos.device
     kept_stride = kept_stride or n_cols
-    kept = torch.full((problems, segs, kept_stride), -1, dtype=torch.int32, device=dev)
-    status = torch.zeros(problems, dtype=torch.int32, device=dev)
-    pcount = torch.zeros(problems, dtype=torch.int32, device=dev)
+    # ce_choose writes every status and protected count and the first
+    # min(budget, ncols) kept columns of each chosen segment; the rest of
+    # `kept` is left as allocated.
+    kept = torch.empty((problems, segs, kept_stride), dtype=torch.int32, device=dev)
+    status = torch.empty(problems, dtype=torch.int32, device=dev)
+    pcount = torch.empty(problems, dtype=torch.int32, device=dev)
     sdt = capi.CE_DTYPE_NONE
     if score is not None:
         sdt = capi.CE_DTYPE_F64 if score.dtype == torch.float64 else capi.CE_DTYPE_F32
