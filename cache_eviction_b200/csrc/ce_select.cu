@@ -1352,30 +1352,48 @@ __global__ void __launch_bounds__(T) brecord_kernel(const BParams p) {
   }
 }
 
-// One warp per (row, layer-in-group, head, j) item.
-struct Item {
-  int i, l, g, j;
-  int64_t base;   // segment base in the [R, L, G, max_cols] arrays
+// One warp per chunk of CH consecutive middle survivors j of one (row,
+// layer-in-group, head): lane k < CH holds item j0 + k.  The chunk index is
+// decoded once with 32-bit arithmetic (the host checks that the count fits),
+// the lanes load their items' metadata in parallel, and the warp then copies
+// the chunk's items one after another; CH is small enough that a launch has
+// thousands of warps, each with a 4 KB copy in flight.
+constexpr int CH = 8;
+struct Chunk {
+  int i, l, g, j;         // this lane's item
+  int W, nprot;
+  int64_t base;           // segment base in the [R, L, G, max_cols] arrays
+  int64_t item;           // flat item index within the launch (hazard scratch slot)
+  bool valid;
 };
 
-__device__ __forceinline__ bool decode_item(const BParams& p, int64_t item, int l0, int nl, Item& it) {
-  const int64_t per_row = static_cast<int64_t>(nl) * p.G * p.max_width;
-  it.i = static_cast<int>(item / per_row);
-  int64_t rem = item % per_row;
-  const int ll = static_cast<int>(rem / (static_cast<int64_t>(p.G) * p.max_width));
-  rem %= static_cast<int64_t>(p.G) * p.max_width;
-  it.g = static_cast<int>(rem / p.max_width);
-  it.j = static_cast<int>(rem % p.max_width);
-  it.l = l0 + ll;
-  it.base = (static_cast<int64_t>(it.i) * p.L * p.G + static_cast<int64_t>(it.l) * p.G + it.g) * p.max_cols;
-  const int32_t* info = p.row_info + it.i * 8;
-  return info[7] == 0 && it.j < info[2];
+__device__ __forceinline__ int chunks_per_seg(const BParams& p) { return (p.max_width + CH - 1) / CH; }
+
+__device__ __forceinline__ Chunk decode_chunk(const BParams& p, uint32_t wi, int r0, int l0, int nl, int lane) {
+  Chunk c;
+  const uint32_t cps = static_cast<uint32_t>(chunks_per_seg(p));
+  const uint32_t seg = wi / cps, jc = wi - seg * cps;
+  const uint32_t lg = static_cast<uint32_t>(nl * p.G);
+  const int ir = static_cast<int>(seg / lg);   // row within the launch
+  c.i = r0 + ir;
+  const uint32_t rem = seg - static_cast<uint32_t>(ir) * lg;
+  const int ll = static_cast<int>(rem / static_cast<uint32_t>(p.G));
+  c.g = static_cast<int>(rem) - ll * p.G;
+  c.l = l0 + ll;
+  c.j = static_cast<int>(jc) * CH + lane;
+  const int32_t* info = p.row_info + c.i * 8;
+  c.W = info[2];
+  c.nprot = info[1];
+  c.valid = lane < CH && info[7] == 0 && c.j < c.W;
+  c.base = (static_cast<int64_t>(c.i) * p.L * p.G + static_cast<int64_t>(c.l) * p.G + c.g) * p.max_cols;
+  c.item = ((static_cast<int64_t>(ir) * nl + ll) * p.G + c.g) * p.max_width + c.j;
+  return c;
 }
 
-__device__ __forceinline__ bool is_hazard(const BParams& p, const Item& it, int W) {
-  const int col = p.mid_col[it.base + it.j];
-  const int cr = p.cand_rank[static_cast<int64_t>(it.i) * p.max_cols + col];
-  return cr >= 0 && cr < W && cr != it.j;
+__device__ __forceinline__ bool chunk_hazard(const BParams& p, const Chunk& c) {
+  const int col = p.mid_col[c.base + c.j];
+  const int cr = p.cand_rank[static_cast<int64_t>(c.i) * p.max_cols + col];
+  return cr >= 0 && cr < c.W && cr != c.j;
 }
 
 __device__ __forceinline__ uint8_t* unit_ptr(const uint64_t* layers, int l, int unit, int g, int G,
@@ -1412,51 +1430,73 @@ __device__ __forceinline__ void copy_pair(uint8_t* dk, uint8_t* dv, const uint8_
   }
 }
 
-__global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int l0, int nl) {
+__device__ __forceinline__ uint32_t launch_chunks(const BParams& p, int nr, int nl) {
+  return static_cast<uint32_t>(nr) * static_cast<uint32_t>(nl * p.G) * static_cast<uint32_t>(chunks_per_seg(p));
+}
+
+// Stage every hazard source of the group's layers (a unit that some other
+// item of its row overwrites) in the scratch buffer.
+__global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int r0, int nr, int l0, int nl) {
   const int lane = threadIdx.x & 31;
-  const int64_t nitems = static_cast<int64_t>(p.R) * nl * p.G * p.max_width;
+  const uint32_t nchunks = launch_chunks(p, nr, nl);
+  const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
   const int bytes = p.P * 128;
-  for (int64_t item = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; item < nitems;
-       item += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
-    Item it;
-    if (!decode_item(p, item, l0, nl, it)) continue;
-    const int W = p.row_info[it.i * 8 + 2];
-    if (!is_hazard(p, it, W)) continue;
-    const int src = p.src_unit[it.base + it.j];
-    if (src < 0 || src >= p.pool_units) {
-      if (lane == 0) flag_error(p.err, CE_EW_INDEX);
-      continue;
+  for (uint32_t wi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi < nchunks; wi += nwarps) {
+    const Chunk c = decode_chunk(p, wi, r0, l0, nl, lane);
+    int src = -1;
+    bool hz = false;
+    if (c.valid) {
+      hz = chunk_hazard(p, c);
+      src = p.src_unit[c.base + c.j];
+      if (hz && (src < 0 || src >= p.pool_units)) {
+        flag_error(p.err, CE_EW_INDEX);
+        hz = false;
+      }
     }
-    uint8_t* scr = p.hazard + item * 2 * bytes;
-    copy_pair(scr, scr + bytes, unit_ptr(p.k_layers, it.l, src, it.g, p.G, p.P),
-              unit_ptr(p.v_layers, it.l, src, it.g, p.G, p.P), bytes, lane);
+    for (unsigned todo = __ballot_sync(0xffffffffu, hz); todo; todo &= todo - 1) {
+      const int k = __ffs(todo) - 1;
+      const int s = __shfl_sync(0xffffffffu, src, k);
+      const int64_t it = __shfl_sync(0xffffffffu, c.item, k);
+      uint8_t* scr = p.hazard + it * 2 * bytes;
+      copy_pair(scr, scr + bytes, unit_ptr(p.k_layers, c.l, s, c.g, p.G, p.P),
+                unit_ptr(p.v_layers, c.l, s, c.g, p.G, p.P), bytes, lane);
+    }
   }
 }
 
-__global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int l0, int nl) {
+// Write every middle survivor of the group's layers to its target unit (from
+// the scratch copy when its source is a hazard) and move its score.
+__global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int r0, int nr, int l0, int nl) {
   const int lane = threadIdx.x & 31;
-  const int64_t nitems = static_cast<int64_t>(p.R) * nl * p.G * p.max_width;
+  const uint32_t nchunks = launch_chunks(p, nr, nl);
+  const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
   const int bytes = p.P * 128;
-  for (int64_t item = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; item < nitems;
-       item += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
-    Item it;
-    if (!decode_item(p, item, l0, nl, it)) continue;
-    const int32_t* info = p.row_info + it.i * 8;
-    const int W = info[2], nprot = info[1];
-    const int dst = p.new_table[static_cast<int64_t>(it.i) * p.max_cols + nprot + it.j];
-    const int src = p.src_unit[it.base + it.j];
-    if (dst < 0 || dst >= p.pool_units || src < 0 || src >= p.pool_units) {
-      if (lane == 0) flag_error(p.err, CE_EW_INDEX);
-      continue;
+  for (uint32_t wi = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wi < nchunks; wi += nwarps) {
+    const Chunk c = decode_chunk(p, wi, r0, l0, nl, lane);
+    int src = -1, dst = -1;
+    bool move = false, hz = false;
+    if (c.valid) {
+      dst = p.new_table[static_cast<int64_t>(c.i) * p.max_cols + c.nprot + c.j];
+      src = p.src_unit[c.base + c.j];
+      if (dst < 0 || dst >= p.pool_units || src < 0 || src >= p.pool_units) {
+        flag_error(p.err, CE_EW_INDEX);
+      } else {
+        p.scores[c.l * p.sls + c.g * p.shs + dst] = p.score_scr[c.base + c.j];
+        move = src != dst;
+        hz = move && chunk_hazard(p, c);
+      }
     }
-    if (lane == 0) p.scores[it.l * p.sls + it.g * p.shs + dst] = p.score_scr[it.base + it.j];
-    if (src == dst) continue;
-    const bool hz = is_hazard(p, it, W);
-    const uint8_t* ks = hz ? p.hazard + item * 2 * bytes : unit_ptr(p.k_layers, it.l, src, it.g, p.G, p.P);
-    const uint8_t* vs = hz ? p.hazard + item * 2 * bytes + bytes
-                           : unit_ptr(p.v_layers, it.l, src, it.g, p.G, p.P);
-    copy_pair(unit_ptr(p.k_layers, it.l, dst, it.g, p.G, p.P), unit_ptr(p.v_layers, it.l, dst, it.g, p.G, p.P),
-              ks, vs, bytes, lane);
+    for (unsigned todo = __ballot_sync(0xffffffffu, move); todo; todo &= todo - 1) {
+      const int k = __ffs(todo) - 1;
+      const int s = __shfl_sync(0xffffffffu, src, k);
+      const int d = __shfl_sync(0xffffffffu, dst, k);
+      const bool h = __shfl_sync(0xffffffffu, hz, k);
+      const int64_t it = __shfl_sync(0xffffffffu, c.item, k);
+      const uint8_t* ks = h ? p.hazard + it * 2 * bytes : unit_ptr(p.k_layers, c.l, s, c.g, p.G, p.P);
+      const uint8_t* vs = h ? p.hazard + it * 2 * bytes + bytes : unit_ptr(p.v_layers, c.l, s, c.g, p.G, p.P);
+      copy_pair(unit_ptr(p.k_layers, c.l, d, c.g, p.G, p.P), unit_ptr(p.v_layers, c.l, d, c.g, p.G, p.P), ks, vs,
+                bytes, lane);
+    }
   }
 }
 
@@ -1673,7 +1713,7 @@ extern "C" int64_t ce_boundary_workspace_bytes(int32_t num_rows, int32_t layers,
       max_cols < 0)
     return -1;
   const int width = (max_width > 0 && max_width < max_cols) ? max_width : max_cols;
-  const int64_t one = hazard_per_layer(num_rows, kv_heads, width, page_size);
+  const int64_t one = hazard_per_layer(1, kv_heads, width, page_size);   // one row of one layer
   const int64_t hz = hazard_bytes < one ? one : hazard_bytes;
   return static_cast<int64_t>(boundary_layout(num_rows, layers, kv_heads, max_cols, hz).total);
 }
@@ -1767,7 +1807,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   const int nw = (max_n + 31) / 32;
   if (sel_smem(nw) > 200 * 1024) return host::fail(CE_ERR_UNSUPPORTED, "max_n too large");
   const int width = (max_width > 0 && max_width < max_cols) ? max_width : max_cols;
-  const int64_t one = hazard_per_layer(num_rows, kv_heads, width, page_size);
+  const int64_t one = hazard_per_layer(1, kv_heads, width, page_size);   // one row of one layer
   const int64_t hz = hazard_bytes < one ? one : hazard_bytes;
   const BLayout Lo = boundary_layout(num_rows, layers, kv_heads, max_cols, hz);
   if (workspace_bytes < static_cast<int64_t>(Lo.total))
@@ -1828,17 +1868,29 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
     brecord_kernel<<<num_rows * layers * kv_heads, T, rsmem, st>>>(p);
     if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("brecord_kernel");
   }
-  const int group = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(layers, hz / one)));
+  // Launch groups of rows x layers that fit the hazard workspace (all rows
+  // of as many layers as fit, or fewer rows of one layer).  Splitting further
+  // to keep the staged copies in L2 was measured slower: the extra launches
+  // cost more than the DRAM round trip they save.
+  const int64_t row_layer = hazard_per_layer(1, kv_heads, width, page_size);
+  const int rows_per = static_cast<int>(std::min<int64_t>(num_rows, std::max<int64_t>(1, hz / row_layer)));
+  const int group = static_cast<int>(
+      std::min<int64_t>(layers, std::max<int64_t>(1, hz / (static_cast<int64_t>(rows_per) * row_layer))));
   const int nsm = host::sm_count();
-  for (int l0 = 0; l0 < layers; l0 += group) {
-    const int nl = std::min(group, layers - l0);
-    const int64_t items = static_cast<int64_t>(num_rows) * nl * kv_heads * width;
-    const int64_t want = (items * 32 + 255) / 256;
-    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 8LL * nsm)));
-    bgather_kernel<<<blocks, 256, 0, st>>>(p, l0, nl);
-    if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bgather_kernel");
-    bscatter_kernel<<<blocks, 256, 0, st>>>(p, l0, nl);
-    if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bscatter_kernel");
+  for (int r0 = 0; r0 < num_rows; r0 += rows_per) {
+    const int nr = std::min(rows_per, num_rows - r0);
+    for (int l0 = 0; l0 < layers; l0 += group) {
+      const int nl = std::min(group, layers - l0);
+      // one warp per chunk of CH middle survivors of a (row, layer, head)
+      const int64_t chunks = static_cast<int64_t>(nr) * nl * kv_heads * ((width + CH - 1) / CH);
+      if (chunks > INT32_MAX) return host::fail(CE_ERR_UNSUPPORTED, "ce_boundary: too many rows x layers x heads");
+      const int64_t want = (chunks * 32 + 255) / 256;
+      const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 8LL * nsm)));
+      bgather_kernel<<<blocks, 256, 0, st>>>(p, r0, nr, l0, nl);
+      if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bgather_kernel");
+      bscatter_kernel<<<blocks, 256, 0, st>>>(p, r0, nr, l0, nl);
+      if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bscatter_kernel");
+    }
   }
   bfinish_kernel<<<num_rows, T, 0, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bfinish_kernel");

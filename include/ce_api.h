@@ -344,8 +344,8 @@ int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols,
  *           (row stride record_stride >= max_cols), and their number in
  *           record_counts[(row * layers + layer) * kv_heads + head] (0 for
  *           rows that did not evict)
- * hazard_bytes bounds the relocation scratch; layers are processed in groups
- * that fit it (at least one layer; query the minimum with layers = 1). */
+ * hazard_bytes bounds the relocation scratch; rows and layers are processed
+ * in groups that fit it (at least one row of one layer, the minimum). */
 int64_t ce_boundary_workspace_bytes(int32_t num_rows, int32_t layers, int32_t kv_heads,
                                     int32_t head_dim, int32_t page_size,
                                     int32_t max_cols, int32_t max_width,
