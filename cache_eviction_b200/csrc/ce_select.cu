@@ -259,6 +259,45 @@ __device__ void emit_sorted(const Cols& cols, int nw, uint32_t* bits, int* pre, 
   __syncthreads();
 }
 
+// Ranks by ascending position of the items a thread holds in a register
+// layout (item it = column threadIdx.x + it * T): posv[it] is the position to
+// rank, or -1 for an item that is not in the set; rank[it] receives its rank
+// (-1 when not in the set).  Same bitmap method as emit_sorted, without
+// calling back per column, so the caller can batch its loads afterwards.
+template <int ITEMS>
+__device__ void rank_sorted(const int32_t (&posv)[ITEMS], int nw, uint32_t* bits, int* pre, int (&rank)[ITEMS],
+                            Sh& sh, int32_t* err) {
+  for (int w = threadIdx.x; w < nw; w += T) bits[w] = 0u;
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int q = posv[it];
+    if (q < 0) continue;
+    if (q >= 32 * nw) {
+      flag_error(err, CE_EW_SHAPE);
+      continue;
+    }
+    atomicOr(&bits[q >> 5], 1u << (q & 31));
+  }
+  __syncthreads();
+  int carry = 0;
+  for (int base = 0; base < nw; base += T) {
+    const int w = base + threadIdx.x;
+    const int v = (w < nw) ? __popc(bits[w]) : 0;
+    int tot;
+    const int ex = block_excl(v, sh, tot);
+    if (w < nw) pre[w] = carry + ex;
+    carry += tot;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int q = posv[it];
+    rank[it] = (q < 0 || q >= 32 * nw) ? -1 : pre[q >> 5] + __popc(bits[q >> 5] & ((1u << (q & 31)) - 1u));
+  }
+  __syncthreads();
+}
+
 // Register path for segments of up to REG_ITEMS * T columns.
 // Eight columns per thread keep the register path at <= 64 registers, so two
 // 512-thread blocks fit on an SM and a 256-segment select runs in one wave.
@@ -1130,6 +1169,58 @@ __device__ void bsel_body(const BParams& p, const RowCtx& r, const Cols& cols, i
             nprot, i, lg, base, sh, bitsm, pre);
 }
 
+// Register path of the boundary selection: the same outputs as bsel_emit,
+// with ranks computed first and every global load (units, scores, the (0,0)
+// head's positions) issued for all of a thread's columns at once.
+__device__ void bsel_body(const BParams& p, const RowCtx& r, const RegCols<REG_ITEMS>& cols, int np, int i,
+                          int lg, int64_t base, Sh& sh, uint32_t* bitsm, int* pre) {
+  const int LG = p.L * p.G;
+  const int nprot = block_sum(np, sh);
+  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
+  if (nprot > r.q.budget) return;
+  const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
+  const int bits = key_bits_of(r.q.policy, p.udt);
+  const Thresh th = radix_threshold(cols, k, r.N - nprot, bits, sh);
+  const int l = lg / p.G, g = lg % p.G;
+  const int max_cols = p.max_cols;
+  // middle survivors, ranked by position (runtime:444-446)
+  int32_t posv[REG_ITEMS];
+  int rank[REG_ITEMS];
+#pragma unroll
+  for (int it = 0; it < REG_ITEMS; ++it)
+    posv[it] = (cols.pv[it] != kAbsent && selected(th, cols.key[it], cols.pv[it])) ? cols.pv[it] : -1;
+  rank_sorted(posv, p.nw, bitsm, pre, rank, sh, p.err);
+  int unit[REG_ITEMS];
+#pragma unroll
+  for (int it = 0; it < REG_ITEMS; ++it)
+    unit[it] = rank[it] >= 0 ? col_unit(p, r, static_cast<int>(threadIdx.x) + it * T) : -1;
+  float sc[REG_ITEMS];
+#pragma unroll
+  for (int it = 0; it < REG_ITEMS; ++it) sc[it] = rank[it] >= 0 ? unit_score(p, l, g, unit[it]) : 0.f;
+#pragma unroll
+  for (int it = 0; it < REG_ITEMS; ++it) {
+    const int rk = rank[it];
+    if (rk < 0 || nprot + rk >= max_cols) continue;
+    p.mid_col[base + rk] = static_cast<int>(threadIdx.x) + it * T;
+    p.new_pos[base + nprot + rk] = posv[it];
+    p.src_unit[base + rk] = unit[it];
+    p.score_scr[base + rk] = sc[it];
+  }
+  // protected part: this head's positions at the (0,0) head's protected
+  // columns, in (0,0) position order (runtime:442-443, 469)
+#pragma unroll
+  for (int it = 0; it < REG_ITEMS; ++it) {
+    const int c = static_cast<int>(threadIdx.x) + it * T;
+    posv[it] = c < r.N ? col_pos(p, r, 0, c) : -1;
+  }
+#pragma unroll
+  for (int it = 0; it < REG_ITEMS; ++it) posv[it] = (posv[it] >= 0 && is_prot(posv[it], r.q)) ? posv[it] : -1;
+  rank_sorted(posv, p.nw, bitsm, pre, rank, sh, p.err);
+#pragma unroll
+  for (int it = 0; it < REG_ITEMS; ++it)
+    if (rank[it] >= 0 && rank[it] < max_cols) p.new_pos[base + rank[it]] = cols.pv[it] & 0x7fffffff;
+}
+
 // Large segments (see large_select); false = candidate overflow, nothing emitted.
 __device__ bool bsel_large(const BParams& p, const RowCtx& r, int i, int lg, int64_t base, Sh& sh,
                            uint32_t* bitsm, int* pre) {
@@ -1500,6 +1591,10 @@ __global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int r0, 
   }
 }
 
+// Grid (rows, 1 + L * G).  Block (i, 0): table, count, frontier, the
+// sliding-window guard and the req_to_unit packing of row i.  Block (i, 1 + s):
+// the new positions of segment s = (layer, head) and, for a live boundary that
+// passes the guard, zero scores of that (layer, head) at every freed unit.
 __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
   __shared__ Sh sh;
   __shared__ int bad;
@@ -1507,46 +1602,50 @@ __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
   const int32_t* info = p.row_info + i * 8;
   if (info[7] != 0) return;
   const RowCtx r = row_ctx(p, i);
-  const int nprot = info[1], after = info[3], true_u = info[4], nleft = info[5];
+  const int after = info[3], true_u = info[4], nleft = info[5];
   const int LG = p.L * p.G;
   const int32_t* ntab = p.new_table + static_cast<int64_t>(i) * p.max_cols;
-  for (int k = threadIdx.x; k < after; k += T) p.table[r.row * p.ts + k] = ntab[k];
-  for (int lg = 0; lg < LG; ++lg) {
-    const int32_t* src = p.new_pos + (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
-    int32_t* dst = p.pos + r.row * p.prs + static_cast<int64_t>(lg) * p.pos_cap;
-    for (int k = threadIdx.x; k < after; k += T) dst[k] = src[k];
-  }
-  if (threadIdx.x == 0) {
-    p.count[r.row] = after;
-    p.frontier[r.row] = r.q.n;
-    bad = 0;
-  }
-  int32_t* res = p.result + i * 4;
-  __syncthreads();
-  if (!p.live) {
-    if (threadIdx.x == 0) res[3] = 0;
-    return;
-  }
   const int32_t* left = p.freed + i * p.freed_stride;
-  if (p.swa) {
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  // The guard (runtime:477-479): no freed unit may still map to a sliding-window slot.
+  if (p.live && p.swa) {
     for (int k = threadIdx.x; k < nleft; k += T) {
       const int u = left[k];
       if (u >= 0 && u < p.pool_units && p.swa[u] != 0) bad = 1;
     }
-    __syncthreads();
-    if (bad) {
-      if (threadIdx.x == 0) {
-        res[0] = 5;
-        flag_error(p.err, CE_EW_SWA);
-      }
-      return;
-    }
   }
-  for (int k = threadIdx.x; k < nleft; k += T) {
-    const int u = left[k];
-    if (u < 0 || u >= p.pool_units) continue;
-    for (int l = 0; l < p.L; ++l)
-      for (int g = 0; g < p.G; ++g) p.scores[l * p.sls + g * p.shs + u] = 0.f;
+  __syncthreads();
+  if (blockIdx.y > 0) {
+    const int lg = static_cast<int>(blockIdx.y) - 1;
+    if (lg >= LG) return;
+    const int32_t* src = p.new_pos + (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
+    int32_t* dst = p.pos + r.row * p.prs + static_cast<int64_t>(lg) * p.pos_cap;
+    for (int k = threadIdx.x; k < after; k += T) dst[k] = src[k];
+    if (!p.live || bad) return;
+    float* sc = p.scores + (lg / p.G) * p.sls + (lg % p.G) * p.shs;
+    for (int k = threadIdx.x; k < nleft; k += T) {
+      const int u = left[k];
+      if (u >= 0 && u < p.pool_units) sc[u] = 0.f;
+    }
+    return;
+  }
+  for (int k = threadIdx.x; k < after; k += T) p.table[r.row * p.ts + k] = ntab[k];
+  int32_t* res = p.result + i * 4;
+  if (threadIdx.x == 0) {
+    p.count[r.row] = after;
+    p.frontier[r.row] = r.q.n;
+  }
+  if (!p.live) {
+    if (threadIdx.x == 0) res[3] = 0;
+    return;
+  }
+  if (bad) {
+    if (threadIdx.x == 0) {
+      res[0] = 5;
+      flag_error(p.err, CE_EW_SWA);
+    }
+    return;
   }
   if (threadIdx.x == 0) res[3] = nleft;
   // Pack every owned unit that is not a real slot of [true_u, n) at the row start.
@@ -1575,7 +1674,6 @@ __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
     carry += tot;
   }
   for (int x = npacked + threadIdx.x; x < min(true_u, p.r2u_width); x += T) rrow[x] = 0;
-  (void)nprot;
 }
 
 __global__ void gather_scores_kernel(const BParams p, float* out) {
@@ -1892,7 +1990,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
       if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bscatter_kernel");
     }
   }
-  bfinish_kernel<<<num_rows, T, 0, st>>>(p);
+  bfinish_kernel<<<dim3(num_rows, 1 + layers * kv_heads), T, 0, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bfinish_kernel");
   return CE_OK;
 }
