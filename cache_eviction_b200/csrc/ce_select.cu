@@ -1120,6 +1120,80 @@ __device__ __forceinline__ bool bsel_column(const BParams& p, const RowCtx& r, i
   return pr;
 }
 
+// The register path's columns (item it = column threadIdx.x + it * T) with
+// the keys of bsel_column, loaded in phases so that each phase's loads for
+// all of a thread's columns are in flight together: positions and units,
+// then the scores the policy needs, then keys and protection.  Returns this
+// thread's protected count.
+__device__ int bsel_reg_columns(const BParams& p, const RowCtx& r, int i, int lg, RegCols<REG_ITEMS>& cols) {
+  const int LG = p.L * p.G;
+  const int l = lg / p.G, g = lg % p.G;
+  int pos[REG_ITEMS], unit[REG_ITEMS];
+  bool in[REG_ITEMS];
+#pragma unroll
+  for (int it = 0; it < REG_ITEMS; ++it) {
+    const int c = static_cast<int>(threadIdx.x) + it * T;
+    in[it] = c < r.N;
+    pos[it] = in[it] ? col_pos(p, r, lg, c) : 0;
+    unit[it] = in[it] ? col_unit(p, r, c) : -1;
+  }
+  float f[REG_ITEMS];
+  uint64_t k[REG_ITEMS];
+  const int policy = r.q.policy;
+  if (policy == CE_POLICY_HEAD_SUM || policy == CE_POLICY_HEAD_MAX) {
+#pragma unroll
+    for (int it = 0; it < REG_ITEMS; ++it) f[it] = in[it] ? unit_score(p, l, g, unit[it]) : 0.f;
+#pragma unroll
+    for (int it = 0; it < REG_ITEMS; ++it) k[it] = key_from_f32(f[it]);
+  } else if (policy == CE_POLICY_H2O_GLOBAL) {
+    // fp32 sum over the layer's heads in ascending head order
+#pragma unroll
+    for (int it = 0; it < REG_ITEMS; ++it) f[it] = 0.f;
+    if (p.gscores) {
+      const float* gs = p.gscores + (static_cast<int64_t>(i) * p.L + l) * p.GH * p.max_cols;
+      for (int gg = 0; gg < p.GH; ++gg)
+#pragma unroll
+        for (int it = 0; it < REG_ITEMS; ++it)
+          if (in[it]) f[it] += gs[static_cast<int64_t>(gg) * p.max_cols + threadIdx.x + it * T];
+    } else {
+      for (int gg = 0; gg < p.G; ++gg)
+#pragma unroll
+        for (int it = 0; it < REG_ITEMS; ++it)
+          if (in[it]) f[it] += unit_score(p, l, gg, unit[it]);
+    }
+#pragma unroll
+    for (int it = 0; it < REG_ITEMS; ++it) k[it] = key_from_f32(f[it]);
+  } else if (policy == CE_POLICY_RANDOM) {
+    const int64_t ub = (static_cast<int64_t>(i) * LG + lg) * p.max_cols + threadIdx.x;
+#pragma unroll
+    for (int it = 0; it < REG_ITEMS; ++it) {
+      const int64_t ui = ub + it * T;
+      k[it] = !in[it] ? 0ull
+              : (p.udt == CE_DTYPE_F64) ? key_from_f64(static_cast<const double*>(p.uniforms)[ui])
+                                        : key_from_f32(static_cast<const float*>(p.uniforms)[ui]);
+    }
+  } else if (policy == CE_POLICY_RESERVOIR) {
+#pragma unroll
+    for (int it = 0; it < REG_ITEMS; ++it)
+      k[it] = reservoir53(r.q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos[it]));
+  } else {
+#pragma unroll
+    for (int it = 0; it < REG_ITEMS; ++it) k[it] = 0ull;
+  }
+  int np = 0;
+#pragma unroll
+  for (int it = 0; it < REG_ITEMS; ++it) {
+    cols.pv[it] = kAbsent;
+    cols.key[it] = 0;
+    if (!in[it]) continue;
+    const bool pr = is_prot(pos[it], r.q);
+    cols.pv[it] = pos[it] | (pr ? static_cast<int>(0x80000000u) : 0);
+    cols.key[it] = pr ? 0 : k[it];
+    np += pr;
+  }
+  return np;
+}
+
 // Middle survivors (cols with posf(c, key, pv) >= 0) in ascending position,
 // then the protected part: this head's positions at the (0,0) head's
 // protected columns taken in (0,0) position order (runtime:442-443,469).
@@ -1263,13 +1337,7 @@ __global__ void __launch_bounds__(T, LARGE ? 1 : 2) bsel_kernel(const BParams p)
     int np = 0;
     if (r.N <= REG_ITEMS * T) {
       RegCols<REG_ITEMS> cols;
-#pragma unroll
-      for (int it = 0; it < REG_ITEMS; ++it) {
-        const int c = threadIdx.x + it * T;
-        cols.pv[it] = kAbsent;
-        cols.key[it] = 0;
-        if (c < r.N) np += bsel_column(p, r, i, lg, c, cols.key[it], cols.pv[it]);
-      }
+      np = bsel_reg_columns(p, r, i, lg, cols);
       bsel_body(p, r, cols, np, i, lg, base, sh, bitsm, pre);
       return;
     }
