@@ -1413,6 +1413,24 @@ __global__ void __launch_bounds__(T, LARGE ? 1 : 2) bsel_kernel(const BParams p)
   }
 }
 
+// H2O global keys of every boundary column, once per (row, layer) instead of
+// once per KV-head segment: the fp32 sum of the layer's KV heads' unit
+// scores in ascending head order (the same additions the selection would
+// make).  Grid (column blocks, rows); rows of other policies are skipped.
+__global__ void hsum_kernel(const BParams p, float* gsum) {
+  const int i = blockIdx.y;
+  const RowCtx r = row_ctx(p, i);
+  if (r.q.policy != CE_POLICY_H2O_GLOBAL || !row_shape_ok(p, r) || r.N <= r.q.budget) return;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < r.N; c += gridDim.x * blockDim.x) {
+    const int u = col_unit(p, r, c);
+    for (int l = 0; l < p.L; ++l) {
+      float acc = 0.f;
+      for (int gg = 0; gg < p.G; ++gg) acc += unit_score(p, l, gg, u);
+      gsum[(static_cast<int64_t>(i) * p.L + l) * p.max_cols + c] = acc;
+    }
+  }
+}
+
 __global__ void bvalidate_kernel(const BParams p) {
   const int i = blockIdx.x;
   if (threadIdx.x != 0) return;
@@ -1776,7 +1794,7 @@ namespace {
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct BLayout {
-  size_t kv, pv, seg, mid, src, npos, ssc, info, crank, ntab, hazard, total;
+  size_t kv, pv, seg, mid, src, npos, ssc, info, crank, ntab, hsum, hazard, total;
 };
 
 BLayout boundary_layout(int R, int L, int G, int max_cols, int64_t hazard_bytes) {
@@ -1793,6 +1811,7 @@ BLayout boundary_layout(int R, int L, int G, int max_cols, int64_t hazard_bytes)
   b.info = o; o += a256(static_cast<size_t>(R) * 8 * 4);
   b.crank = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
   b.ntab = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
+  b.hsum = o; o += a256(static_cast<size_t>(R) * L * max_cols * 4);
   b.hazard = o; o += a256(static_cast<size_t>(hazard_bytes));
   b.total = o;
   return b;
@@ -2007,6 +2026,10 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   p.cand_rank = reinterpret_cast<int32_t*>(ws + Lo.crank);
   p.new_table = reinterpret_cast<int32_t*>(ws + Lo.ntab);
   p.hazard = ws + Lo.hazard;
+  if (!global_scores) {   // H2O global rows sum their heads once, in hsum_kernel
+    p.gscores = reinterpret_cast<float*>(ws + Lo.hsum);
+    p.GH = 1;
+  }
   p.freed = freed_units;
   p.freed_stride = freed_stride;
   p.result = result;
@@ -2021,6 +2044,10 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
     return host::fail(CE_ERR_CUDA, "smem attr");
   if (cudaMemsetAsync(p.row_info, 0, sizeof(int32_t) * 8 * num_rows, st) != cudaSuccess)
     return host::fail_cuda("row_info memset");
+  if (!global_scores) {
+    hsum_kernel<<<dim3((max_cols + 255) / 256, num_rows), 256, 0, st>>>(p, const_cast<float*>(p.gscores));
+    if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("hsum_kernel");
+  }
   if (large)
     bsel_kernel<true><<<num_rows * layers * kv_heads + num_rows, T, smem, st>>>(p);
   else

@@ -295,10 +295,15 @@ def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, k
         _p(record[1]) if record else None, _p(err), _stream(dev))
     capi.check(st, "ce_boundary")
     if R:
+        # bsel, bvalidate, bfinish; hsum without global scores; a gather and a
+        # scatter per launch group (rows x layers fitting the hazard scratch)
         width = max_width if 0 < max_width < max_cols else max_cols
-        one = R * kv_heads * width * 2 * page_size * 128
-        group = max(1, min(L, max(int(hazard_bytes), one) // max(one, 1)))
-        _count(3 + 2 * ceil_div(L, group) + (1 if record else 0))
+        row_layer = max(1, kv_heads * width * 2 * page_size * 128)
+        hz = max(int(hazard_bytes), row_layer)
+        rows_per = min(R, max(1, hz // row_layer))
+        group = min(L, max(1, hz // (rows_per * row_layer)))
+        _count(3 + (1 if global_scores is None else 0) + 2 * ceil_div(R, rows_per) * ceil_div(L, group)
+               + (1 if record else 0))
     return result, freed
 
 
