@@ -78,6 +78,7 @@ SIGNATURES = {
     "ce_replay_workspace_bytes": (I64, [I32, I32]),
     "ce_replay_error": (C.c_int, [P, I64, I64, P, P, I64, P, I64, P, F32, I32, I32, I32, I32, I32, P, P,
                                   P, I64, P, P]),
+    "ce_selftest_wait": (C.c_int, [I32, I64, P, P, P]),
     "ce_choose_workspace_bytes": (I64, [I32, I32, I32]),
     "ce_choose": (C.c_int, [P, P, I32, P, I32, P, I32, I32, I32, I32, I32, P, I32, P, P, P,
                             I64, P, P]),

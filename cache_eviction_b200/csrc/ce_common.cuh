@@ -62,13 +62,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait on an mbarrier phase.  Returns false (and flags the error
-// word) when the phase did not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
+// word) when the phase did not complete within limit_ns (kWaitLimitNs for
+// every kernel; the self-test passes a shorter one).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t* err,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       flag_error(err, CE_EW_TIMEOUT);
       return false;
     }
@@ -78,13 +80,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
 // Bounded wait that also gives up as soon as another warp of the CTA has set
 // *abort (polled only on the slow path, so a ready stage costs one try_wait).
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int32_t* err,
-                                                   volatile int* abort) {
+                                                   volatile int* abort,
+                                                   unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       flag_error(err, CE_EW_TIMEOUT);
       return false;
     }

@@ -389,6 +389,17 @@ int ce_reservoir_scores(const int32_t* pos, int32_t layers, int32_t heads,
                         int32_t n_cols, int32_t head_offset, uint64_t seed,
                         uint64_t* out, void* stream);
 
+/* ---- self-test of the bounded device waits --------------------------------
+ * Every pipelined kernel waits on mbarrier phases with a bound (2 s): a wait
+ * that runs out flags CE_EW_TIMEOUT, tells the CTA's other warps to stop and
+ * lets the kernel return.  This entry point runs that machinery alone: with
+ * complete = 0 one warp waits limit_ns ([1 us, 2 s]) on a phase nothing
+ * completes and a second warp waits on the same phase polling the abort flag;
+ * status [3] int32 (device) receives {first wait gave up, second left through
+ * the abort, block reached its end}.  With complete = 1 the phase completes
+ * and status = {0, 0, 1}.  No reference counterpart. */
+int ce_selftest_wait(int32_t complete, int64_t limit_ns, int32_t* err, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
