@@ -360,6 +360,16 @@ __device__ __forceinline__ uint32_t bin16_of(uint64_t key, int kind) {
   }
 }
 
+// bin16_of with the key kind fixed at compile time, for the scan loops (a
+// runtime switch there repeats every kind's code once per unrolled column).
+template <int KIND>
+__device__ __forceinline__ uint32_t bin16_k(uint64_t key) {
+  if constexpr (KIND == BIN_K32) return static_cast<uint32_t>(key >> 16) & 0xFFFFu;
+  else if constexpr (KIND == BIN_K64) return static_cast<uint32_t>(key >> 48);
+  else if constexpr (KIND == BIN_R53) return static_cast<uint32_t>(key >> 37) & 0xFFFFu;
+  else return bin16_of(key, BIN_U64);
+}
+
 struct LargeBuf {
   uint16_t* bin;   // [LARGE_MAX] key prefix of unprotected columns
   uint32_t* prot;  // [LARGE_MAX / 32] protected columns
@@ -414,7 +424,8 @@ __device__ __forceinline__ void large_init(int N, const LargeBuf& lb) {
 }
 
 // Bins, histogram and protected bits of one quad (columns 4q .. 4q + 3).
-__device__ __forceinline__ int large_quad(int q, const uint64_t (&key)[4], const bool (&pr)[4], int kind,
+template <int KIND>
+__device__ __forceinline__ int large_quad(int q, const uint64_t (&key)[4], const bool (&pr)[4],
                                           const LargeBuf& lb) {
   int np = 0;
   uint32_t pm = 0u;
@@ -425,7 +436,7 @@ __device__ __forceinline__ int large_quad(int q, const uint64_t (&key)[4], const
       ++np;
       pm |= 1u << e;
     } else {
-      const uint32_t b = bin16_of(key[e], kind);
+      const uint32_t b = bin16_k<KIND>(key[e]);
       packed |= static_cast<uint64_t>(b) << (16 * e);
       atomicAdd(&lb.hist[b >> 4], 1);
     }
@@ -437,8 +448,8 @@ __device__ __forceinline__ int large_quad(int q, const uint64_t (&key)[4], const
 
 // Qd supplies Raw (the loaded words of a quad), load(c, raw) (loads only) and
 // make(raw, key, pr) (keys and protection from the loaded words).
-template <int LQN, class Qd>
-__device__ int scan_quads(const Qd& qd, int nq, int kind, const LargeBuf& lb) {
+template <int LQN, int KIND, class Qd>
+__device__ int scan_quads(const Qd& qd, int nq, const LargeBuf& lb) {
   int np = 0;
   for (int q0 = threadIdx.x; q0 < nq; q0 += LQN * T) {
     typename Qd::Raw raw[LQN];
@@ -452,14 +463,14 @@ __device__ int scan_quads(const Qd& qd, int nq, int kind, const LargeBuf& lb) {
       uint64_t key[4];
       bool pr[4];
       qd.make(raw[u], key, pr);
-      np += large_quad(q, key, pr, kind, lb);
+      np += large_quad<KIND>(q, key, pr, lb);
     }
   }
   return np;
 }
 
-template <class ColFn>
-__device__ int large_tail(ColFn colfn, int cstart, int N, int kind, const LargeBuf& lb) {
+template <int KIND, class ColFn>
+__device__ int large_tail(ColFn colfn, int cstart, int N, const LargeBuf& lb) {
   int np = 0;
   constexpr int LB = LARGE_LB;
   for (int c0 = cstart + threadIdx.x; c0 < N; c0 += LB * T) {
@@ -480,7 +491,7 @@ __device__ int large_tail(ColFn colfn, int cstart, int N, int kind, const LargeB
         atomicOr(&lb.prot[c >> 5], 1u << (c & 31));
         lb.bin[c] = 0;
       } else {
-        const uint32_t b = bin16_of(key[u], kind);
+        const uint32_t b = bin16_k<KIND>(key[u]);
         lb.bin[c] = static_cast<uint16_t>(b);
         atomicAdd(&lb.hist[b >> 4], 1);
       }
@@ -903,17 +914,26 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
     const int nq = N / 4;
     const int64_t hbase = (static_cast<int64_t>(i) * segs + l * p.heads) * p.n_cols;
     const uint64_t head = static_cast<uint64_t>(p.head_offset + g);
-    if (q.policy == CE_POLICY_RESERVOIR || q.policy == CE_POLICY_PREFIX_SLIDING)
-      np = scan_quads<16>(ChooseQuads<QS_POS>{&p, base, hbase, q, head, l}, nq, kind, lb);
+    // (loader, key kind) pairs; prefix_sliding keys are all 0, whose bin is 0 in every kind
+    if (q.policy == CE_POLICY_RESERVOIR)
+      np = scan_quads<16, BIN_R53>(ChooseQuads<QS_POS>{&p, base, hbase, q, head, l}, nq, lb);
+    else if (q.policy == CE_POLICY_PREFIX_SLIDING)
+      np = scan_quads<16, BIN_K32>(ChooseQuads<QS_POS>{&p, base, hbase, q, head, l}, nq, lb);
     else if (q.policy == CE_POLICY_H2O_GLOBAL)
-      np = p.sdt == CE_DTYPE_F64 ? scan_quads<2>(ChooseQuads<QS_H2O_F64>{&p, base, hbase, q, head, l}, nq, kind, lb)
-                                 : scan_quads<4>(ChooseQuads<QS_H2O_F32>{&p, base, hbase, q, head, l}, nq, kind, lb);
+      np = p.sdt == CE_DTYPE_F64
+               ? scan_quads<2, BIN_K64>(ChooseQuads<QS_H2O_F64>{&p, base, hbase, q, head, l}, nq, lb)
+               : scan_quads<4, BIN_K32>(ChooseQuads<QS_H2O_F32>{&p, base, hbase, q, head, l}, nq, lb);
+    else if (p.sdt == CE_DTYPE_F64)
+      np = kind == BIN_U64 ? scan_quads<6, BIN_U64>(ChooseQuads<QS_F64>{&p, base, hbase, q, head, l}, nq, lb)
+                           : scan_quads<6, BIN_K64>(ChooseQuads<QS_F64>{&p, base, hbase, q, head, l}, nq, lb);
     else
-      np = p.sdt == CE_DTYPE_F64 ? scan_quads<6>(ChooseQuads<QS_F64>{&p, base, hbase, q, head, l}, nq, kind, lb)
-                                 : scan_quads<8>(ChooseQuads<QS_F32>{&p, base, hbase, q, head, l}, nq, kind, lb);
+      np = scan_quads<8, BIN_K32>(ChooseQuads<QS_F32>{&p, base, hbase, q, head, l}, nq, lb);
     cstart = 4 * nq;
   }
-  np += large_tail(colfn, cstart, N, kind, lb);
+  np += kind == BIN_K32   ? large_tail<BIN_K32>(colfn, cstart, N, lb)
+        : kind == BIN_K64 ? large_tail<BIN_K64>(colfn, cstart, N, lb)
+        : kind == BIN_R53 ? large_tail<BIN_R53>(colfn, cstart, N, lb)
+                          : large_tail<BIN_U64>(colfn, cstart, N, lb);
   const int nprot = block_sum(np, sh);
   if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * segs + s] = nprot;
   if (nprot > q.budget) return true;
@@ -1305,7 +1325,10 @@ __device__ bool bsel_large(const BParams& p, const RowCtx& r, int i, int lg, int
                                                                               : BIN_K32;
   auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool { return bsel_column(p, r, i, lg, c, key, pv); };
   large_init(r.N, lb);
-  const int nprot = block_sum(large_tail(colfn, 0, r.N, kind, lb), sh);
+  const int nprot = block_sum(kind == BIN_K32   ? large_tail<BIN_K32>(colfn, 0, r.N, lb)
+                             : kind == BIN_R53 ? large_tail<BIN_R53>(colfn, 0, r.N, lb)
+                                               : large_tail<BIN_U64>(colfn, 0, r.N, lb),
+                             sh);
   if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
   if (nprot > r.q.budget) return true;
   const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
