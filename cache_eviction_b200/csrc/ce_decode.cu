@@ -671,32 +671,53 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams
     };
     auto vrow = [&](int i) -> int { return ((i % subs) * G + g) * 8 + r; };
     auto live = [&](int i) -> bool { return cta_has_work(k0 + i / subs, S, grid); };
-    float M = -INFINITY;
-    for (int i = lane; i < nslots; i += 32)
-      if (live(i)) M = fmaxf(M, rec_of(i)[REC_ROWS * D + vrow(i)]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    const float sink2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
-    M = fmaxf(M, sink2);
-    float den = 0.f;
-    if (M != -INFINITY)
-      for (int i = lane; i < nslots; i += 32) {
-        if (!live(i)) continue;
-        const float mk = rec_of(i)[REC_ROWS * D + vrow(i)];
-        if (mk != -INFINITY) den += rec_of(i)[REC_ROWS * D + REC_ROWS + vrow(i)] * exp2f(mk - M);
-      }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    if (p.sinks && M != -INFINITY) den += exp2f(sink2 - M);
-    const float L2 = (M == -INFINITY) ? -INFINITY : M + log2f(den);
+    // One pass over the slots: each lane keeps an online (max, sum) of its
+    // slots and caches their maxima in wts, from which the weights are formed
+    // once the normaliser is known (no second or third read of the records).
     const bool fits = nslots <= MAX_SLOTS;
+    float m = -INFINITY, l = 0.f;
+    for (int i = lane; i < nslots; i += 32) {
+      float mk = -INFINITY, lk = 0.f;
+      if (live(i)) {
+        const float* st = rec_of(i) + REC_ROWS * D;
+        mk = st[vrow(i)];
+        lk = st[REC_ROWS + vrow(i)];
+      }
+      if (fits) wts[warp][i] = mk;
+      if (mk != -INFINITY) {
+        const float mn = fmaxf(m, mk);
+        l = l * exp2f(m - mn) + lk * exp2f(mk - mn);
+        m = mn;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
+      const float mn = fmaxf(m, m2);
+      if (mn != -INFINITY) {
+        l = l * exp2f(m - mn) + l2 * exp2f(m2 - mn);
+        m = mn;
+      }
+    }
+    const float sink2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
+    const float M = fmaxf(m, sink2);
+    float den = 0.f;
+    if (M != -INFINITY) {
+      den = (m == -INFINITY) ? 0.f : l * exp2f(m - M);
+      if (p.sinks) den += exp2f(sink2 - M);
+    }
+    const float L2 = (M == -INFINITY) ? -INFINITY : M + log2f(den);
     auto weight = [&](int i) -> float {
       if (L2 == -INFINITY || !live(i)) return 0.f;
       const float mk = rec_of(i)[REC_ROWS * D + vrow(i)];
       return mk == -INFINITY ? 0.f : exp2f(mk - L2);
     };
+    __syncwarp();
     if (fits)
-      for (int i = lane; i < nslots; i += 32) wts[warp][i] = weight(i);
+      for (int i = lane; i < nslots; i += 32) {
+        const float mk = wts[warp][i];
+        wts[warp][i] = (L2 == -INFINITY || mk == -INFINITY) ? 0.f : exp2f(mk - L2);
+      }
     __syncwarp();
     // lane = dim group (8 dims) x slot group (4): sg = lane % 4, dg = lane / 4
     const int sg = lane & 3, dg = lane >> 2;
