@@ -149,11 +149,6 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return y;
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
 // Split two fp32 values into bf16 hi parts and bf16 residuals so that
 // hi + lo reproduces each value to ~2^-17 relative.
 __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
@@ -294,16 +289,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   tmem_ld32_async(taddr, v);
   tmem_ld_wait();
 }
-// Store 16 consecutive 32-bit columns of this thread's TMEM lane (32x32b
-// shape, x16); complete after tmem_st_wait().
-__device__ __forceinline__ void tmem_st16_async(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-      "%15,%16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
+// Store 8 consecutive 32-bit columns of this thread's TMEM lane (32x32b
+// shape, x8); complete after tmem_st_wait().
 __device__ __forceinline__ void tmem_st8_async(uint32_t taddr, const uint32_t* r) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
                "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
