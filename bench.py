@@ -712,12 +712,12 @@ def main():
     evict5 = None
     if not args.no_evict_bench and "evict5" in legs:
         evict5 = evict_microbench(world, rank, device, rows=args.evict_rows)
+        if world > 1:   # every rank runs its shard; report the slowest (same collectives on every rank)
+            for k in evict5:
+                evict5[k]["evict_step_us"] = max_over_ranks(evict5[k]["evict_step_us"])
     select1 = None
     if not args.no_evict_bench and "select1" in legs:
         select1 = select_token_microbench(world, rank, device, rows=args.evict_rows)
-        if world > 1:
-            for k in evict5:
-                evict5[k]["evict_step_us"] = max_over_ranks(evict5[k]["evict_step_us"])
     peak, peak_kind = measured_peak_hbm()
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
