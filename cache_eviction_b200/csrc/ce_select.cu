@@ -169,6 +169,56 @@ struct RangeCols {
   }
 };
 
+// Column range [0, N) whose per-column loads (load(c, key, pv): loads only)
+// are issued for B columns of a thread before any of them is used, so a pass
+// over a long range costs one load latency per B columns of a thread.
+template <class LoadF>
+struct LoadedRange {
+  int N;
+  LoadF load;
+  static constexpr int B = 8;
+  template <class F>
+  __device__ __forceinline__ void each(F f) const {
+    for (int c0 = threadIdx.x; c0 < N; c0 += B * T) {
+      uint64_t k[B];
+      int32_t v[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        k[b] = 0ull;
+        v[b] = 0;
+        if (c0 + b * T < N) load(c0 + b * T, k[b], v[b]);
+      }
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+        if (c0 + b * T < N) f(c0 + b * T, k[b], v[b]);
+    }
+  }
+};
+template <class LoadF>
+__device__ __forceinline__ LoadedRange<LoadF> loaded_range(int N, LoadF load) {
+  return LoadedRange<LoadF>{N, load};
+}
+
+// for (k = threadIdx.x; k < n; k += T) with the loads of B iterations in
+// flight together: a = l1(k), then b = l2(k, a) (a load that needs a), then
+// use(k, a, b), each stage for all B iterations before the next.
+template <int B, class L1, class L2, class U>
+__device__ __forceinline__ void batched(int n, L1 l1, L2 l2, U use) {
+  using A = decltype(l1(0));
+  using V = decltype(l2(0, A{}));
+  for (int k0 = threadIdx.x; k0 < n; k0 += B * T) {
+    A a[B];
+    V v[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) a[b] = (k0 + b * T < n) ? l1(k0 + b * T) : A{};
+#pragma unroll
+    for (int b = 0; b < B; ++b) v[b] = (k0 + b * T < n) ? l2(k0 + b * T, a[b]) : V{};
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+      if (k0 + b * T < n) use(k0 + b * T, a[b], v[b]);
+  }
+}
+
 // Threshold of the k largest (key, pos) pairs among unprotected columns:
 // MSB-first 8-bit radix select on the key, then on the position among the
 // columns equal to the threshold key (newer wins).
@@ -224,10 +274,11 @@ __device__ __forceinline__ bool selected(const Thresh& th, uint64_t key, int pc)
 }
 
 // Rank every column whose posf(c, key, pv) >= 0 by ascending position using a
-// bitmap of nw words, then call emit(rank, c, pos).  Positions must be < 32*nw.
+// bitmap of nw words, then call emit(rank, c, pos, key).  Positions must be
+// < 32*nw.  Returns the number of ranked columns.
 template <class Cols, class PosF, class EmitF>
-__device__ void emit_sorted(const Cols& cols, int nw, uint32_t* bits, int* pre, PosF posf, EmitF emit,
-                            Sh& sh, int32_t* err) {
+__device__ int emit_sorted(const Cols& cols, int nw, uint32_t* bits, int* pre, PosF posf, EmitF emit,
+                           Sh& sh, int32_t* err) {
   for (int w = threadIdx.x; w < nw; w += T) bits[w] = 0u;
   __syncthreads();
   cols.each([&](int c, uint64_t key, int32_t pc) {
@@ -254,9 +305,10 @@ __device__ void emit_sorted(const Cols& cols, int nw, uint32_t* bits, int* pre, 
     const int p = posf(c, key, pc);
     if (p < 0 || p >= 32 * nw) return;
     const int rank = pre[p >> 5] + __popc(bits[p >> 5] & ((1u << (p & 31)) - 1u));
-    emit(rank, c, p);
+    emit(rank, c, p, key);
   });
   __syncthreads();
+  return carry;
 }
 
 // Ranks by ascending position of the items a thread holds in a register
@@ -889,7 +941,7 @@ __device__ void choose_body(const ChooseParams& p, const Cols& cols, int np, int
         if (pc < 0) return pc & 0x7fffffff;
         return selected(th, key, pc) ? pc : -1;
       },
-      [&](int rank, int c, int) {
+      [&](int rank, int c, int, uint64_t) {
         if (rank < stride) out[rank] = c;
         else flag_error(err, CE_EW_CAPACITY);
       },
@@ -951,7 +1003,7 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
       kept_bits(N, kb, [&](int c) { return pos[c]; },
                 [&](int c) { return *reinterpret_cast<const int4*>(pos + c); }, p.vec4 != 0),
       p.nw, dyn, reinterpret_cast<int*>(dyn + p.nw), [](int, uint64_t, int32_t pc) -> int { return pc; },
-      [&](int rank, int c, int) {
+      [&](int rank, int c, int, uint64_t) {
         if (rank < stride) out[rank] = c;
         else flag_error(err, CE_EW_CAPACITY);
       },
@@ -1013,6 +1065,9 @@ __global__ void choose_status_kernel(const ChooseParams p) {
 }
 
 // ============================== ce_boundary ======================================
+// Per-row record the selection leaves for the later kernels (row_info).
+constexpr int RI = 16;
+
 struct BParams {
   int32_t* table;
   int64_t ts;
@@ -1041,6 +1096,7 @@ struct BParams {
   const float* gscores;
   int GH;
   int live, max_cols, max_width, nw;
+  int ch;   // middle survivors per compaction chunk (chunk_items)
   // workspace
   uint64_t* kv;
   int32_t* pv;
@@ -1049,9 +1105,11 @@ struct BParams {
   int32_t* src_unit;
   int32_t* new_pos;
   float* score_scr;
-  int32_t* row_info;   // [R*8]: N, nprot, W, after, true_u, nleft, -, status
+  int32_t* row_info;   // [R*RI]: N, nprot, W, after, true_u, nleft, count, status, swa_bad, npacked
   int32_t* cand_rank;  // [R*max_cols]
   int32_t* new_table;  // [R*max_cols]
+  int32_t* prot_col;   // [R*max_cols] the (0,0) head's protected columns in its position order
+  int32_t* pack;       // [R*max_cols] the row's packed req_to_unit prefix (live)
   uint8_t* hazard;
   int32_t* freed;
   int64_t freed_stride;
@@ -1077,9 +1135,11 @@ __device__ __forceinline__ RowCtx row_ctx(const BParams& p, int i) {
   return r;
 }
 
+// Row sizes within the arguments, and the uniforms a random row draws from present.
 __device__ __forceinline__ bool row_shape_ok(const BParams& p, const RowCtx& r) {
   return r.cnt >= 0 && r.fr >= 0 && r.fr <= r.q.n && r.N >= 0 && r.N <= p.max_cols &&
-         r.q.n <= 32 * p.nw && r.q.n <= p.r2u_width && r.cnt <= p.pos_cap;
+         r.q.n <= 32 * p.nw && r.q.n <= p.r2u_width && r.cnt <= p.pos_cap &&
+         (r.q.policy != CE_POLICY_RANDOM || p.uniforms != nullptr);
 }
 
 __device__ __forceinline__ int col_unit(const BParams& p, const RowCtx& r, int c) {
@@ -1214,9 +1274,10 @@ __device__ int bsel_reg_columns(const BParams& p, const RowCtx& r, int i, int lg
   return np;
 }
 
-// Middle survivors (cols with posf(c, key, pv) >= 0) in ascending position,
-// then the protected part: this head's positions at the (0,0) head's
-// protected columns taken in (0,0) position order (runtime:442-443,469).
+// Middle survivors (cols with posf(c, key, pv) >= 0) in ascending position
+// after the nprot protected slots (runtime:444-446); their units and scores
+// are loaded after the ranking, eight survivors of a thread at a time.  The
+// protected slots are filled by bfinish_kernel.
 template <class Cols, class PosF>
 __device__ void bsel_emit(const BParams& p, const RowCtx& r, const Cols& cols, PosF posf, int nprot,
                           int i, int lg, int64_t base, Sh& sh, uint32_t* bitsm, int* pre) {
@@ -1226,27 +1287,21 @@ __device__ void bsel_emit(const BParams& p, const RowCtx& r, const Cols& cols, P
   int32_t* srcu = p.src_unit + base;
   float* ssc = p.score_scr + base;
   const int max_cols = p.max_cols;
-  emit_sorted(
+  const int nmid = emit_sorted(
       cols, p.nw, bitsm, pre, posf,
-      [&](int rank, int c, int pos) {
+      [&](int rank, int c, int pos, uint64_t) {
         if (nprot + rank >= max_cols) return;
         mid[rank] = c;
         npos[nprot + rank] = pos;
-        const int u = col_unit(p, r, c);
-        srcu[rank] = u;
-        ssc[rank] = unit_score(p, l, g, u);
       },
       sh, p.err);
-  emit_sorted(
-      RangeCols{r.N}, p.nw, bitsm, pre,
-      [&](int c, uint64_t, int32_t) -> int {
-        const int p00 = col_pos(p, r, 0, c);
-        return is_prot(p00, r.q) ? p00 : -1;
-      },
-      [&](int rank, int c, int) {
-        if (rank < max_cols) npos[rank] = col_pos(p, r, lg, c);
-      },
-      sh, p.err);
+  batched<8>(
+      min(nmid, max_cols - nprot), [&](int j) { return col_unit(p, r, mid[j]); },
+      [&](int, int u) { return unit_score(p, l, g, u); },
+      [&](int j, int u, float sc) {
+        srcu[j] = u;
+        ssc[j] = sc;
+      });
 }
 
 template <class Cols>
@@ -1264,8 +1319,8 @@ __device__ void bsel_body(const BParams& p, const RowCtx& r, const Cols& cols, i
 }
 
 // Register path of the boundary selection: the same outputs as bsel_emit,
-// with ranks computed first and every global load (units, scores, the (0,0)
-// head's positions) issued for all of a thread's columns at once.
+// with ranks computed first and every global load (units, scores) issued for
+// all of a thread's columns at once.
 __device__ void bsel_body(const BParams& p, const RowCtx& r, const RegCols<REG_ITEMS>& cols, int np, int i,
                           int lg, int64_t base, Sh& sh, uint32_t* bitsm, int* pre) {
   const int LG = p.L * p.G;
@@ -1300,19 +1355,133 @@ __device__ void bsel_body(const BParams& p, const RowCtx& r, const RegCols<REG_I
     p.src_unit[base + rk] = unit[it];
     p.score_scr[base + rk] = sc[it];
   }
-  // protected part: this head's positions at the (0,0) head's protected
-  // columns, in (0,0) position order (runtime:442-443, 469)
+}
+
+// Pass over a large boundary segment (large_tail's outputs) with the key
+// source fixed at compile time, so that each batch of LARGE_LB columns of a
+// thread is straight-line code: positions and units of the batch, then the
+// scores or uniforms they select, then keys, bins and protection.  Keys are
+// those of bsel_column.  The kept columns [0, count) and the new ones
+// [count, N) run as two ranges (KEPT), so neither tests which one a column
+// is in, and a new column's position is arithmetic.
+enum BselSrc { BS_NONE = 0, BS_SCORE = 1, BS_H2O = 2, BS_U32 = 3, BS_U64 = 4, BS_RES = 5 };
+template <int SRC, int KIND, bool KEPT>
+__device__ int bsel_scan_range(const BParams& p, const RowCtx& r, int i, int lg, int cb, int ce,
+                               const LargeBuf& lb) {
+  constexpr int B = LARGE_LB;
+  const int LG = p.L * p.G;
+  const int l = lg / p.G, g = lg % p.G;
+  // row-relative bases: column c's position, unit, uniform and H2O sum
+  const int32_t* posr = p.pos + r.row * p.prs + static_cast<int64_t>(lg) * p.pos_cap;
+  const int32_t* unitr = KEPT ? p.table + r.row * p.ts : p.r2u + r.row * p.rs + (r.fr - r.cnt);
+  const float* sc = p.scores + l * p.sls + g * p.shs;
+  const int64_t ub = (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
+  const float* gs = p.gscores + (static_cast<int64_t>(i) * p.L + l) * p.GH * p.max_cols;
+  const int pos0 = r.fr - r.cnt;   // position of new column c: pos0 + c
+  const int64_t pool = p.pool_units;
+  int np = 0;
+  for (int c0 = cb + static_cast<int>(threadIdx.x); c0 < ce; c0 += B * T) {
+    int pos[B];
+    uint64_t key[B];
 #pragma unroll
-  for (int it = 0; it < REG_ITEMS; ++it) {
-    const int c = static_cast<int>(threadIdx.x) + it * T;
-    posv[it] = c < r.N ? col_pos(p, r, 0, c) : -1;
+    for (int b = 0; b < B; ++b) {
+      const int c = c0 + b * T;
+      pos[b] = KEPT ? (c < ce ? posr[c] : 0) : pos0 + c;
+    }
+    if constexpr (SRC == BS_SCORE) {
+      int unit[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) unit[b] = c0 + b * T < ce ? unitr[c0 + b * T] : -1;
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+        key[b] = key_from_f32((unit[b] >= 0 && unit[b] < pool) ? sc[unit[b]] : 0.f);
+    } else if constexpr (SRC == BS_H2O) {
+      float f[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) f[b] = 0.f;
+      for (int gg = 0; gg < p.GH; ++gg)
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+          if (c0 + b * T < ce) f[b] += gs[static_cast<int64_t>(gg) * p.max_cols + c0 + b * T];
+#pragma unroll
+      for (int b = 0; b < B; ++b) key[b] = key_from_f32(f[b]);
+    } else if constexpr (SRC == BS_U32) {
+      const float* u = static_cast<const float*>(p.uniforms) + ub;
+#pragma unroll
+      for (int b = 0; b < B; ++b) key[b] = c0 + b * T < ce ? key_from_f32(u[c0 + b * T]) : 0ull;
+    } else if constexpr (SRC == BS_U64) {
+      const double* u = static_cast<const double*>(p.uniforms) + ub;
+#pragma unroll
+      for (int b = 0; b < B; ++b) key[b] = c0 + b * T < ce ? key_from_f64(u[c0 + b * T]) : 0ull;
+    } else if constexpr (SRC == BS_RES) {
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+        key[b] = reservoir53(r.q.seed, l, p.head_offset + g, static_cast<uint64_t>(pos[b]));
+    } else {
+#pragma unroll
+      for (int b = 0; b < B; ++b) key[b] = 0ull;
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int c = c0 + b * T;
+      if (c >= ce) continue;
+      if (is_prot(pos[b], r.q)) {
+        ++np;
+        atomicOr(&lb.prot[c >> 5], 1u << (c & 31));
+        lb.bin[c] = 0;
+      } else {
+        const uint32_t bn = bin16_k<KIND>(key[b]);
+        lb.bin[c] = static_cast<uint16_t>(bn);
+        atomicAdd(&lb.hist[bn >> 4], 1);
+      }
+    }
   }
+  return np;
+}
+
+template <int SRC, int KIND>
+__device__ int bsel_scan(const BParams& p, const RowCtx& r, int i, int lg, const LargeBuf& lb) {
+  return bsel_scan_range<SRC, KIND, true>(p, r, i, lg, 0, r.cnt, lb) +
+         bsel_scan_range<SRC, KIND, false>(p, r, i, lg, r.cnt, r.N, lb);
+}
+
+// The columns set in kb[0 .. nwc) (shared memory) with their positions
+// pos(c), as emit_sorted's column set: each thread takes whole words and
+// loads the positions of their set bits eight at a time, so a pass costs a
+// few shared loads per thread plus one load latency per eight kept columns.
+template <class PosF>
+struct KeptWords {
+  int nwc;
+  const uint32_t* kb;
+  PosF pos;
+  static constexpr int B = 8;
+  template <class F>
+  __device__ __forceinline__ void each(F f) const {
+    for (int w = threadIdx.x; w < nwc; w += T) {
+      uint32_t m = kb[w];
+      while (m) {
+        int cs[B];
+        int32_t ps[B];
 #pragma unroll
-  for (int it = 0; it < REG_ITEMS; ++it) posv[it] = (posv[it] >= 0 && is_prot(posv[it], r.q)) ? posv[it] : -1;
-  rank_sorted(posv, p.nw, bitsm, pre, rank, sh, p.err);
+        for (int b = 0; b < B; ++b) {
+          cs[b] = -1;
+          ps[b] = 0;
+          if (m) {
+            cs[b] = 32 * w + __ffs(m) - 1;
+            m &= m - 1;
+            ps[b] = pos(cs[b]);
+          }
+        }
 #pragma unroll
-  for (int it = 0; it < REG_ITEMS; ++it)
-    if (rank[it] >= 0 && rank[it] < max_cols) p.new_pos[base + rank[it]] = cols.pv[it] & 0x7fffffff;
+        for (int b = 0; b < B; ++b)
+          if (cs[b] >= 0) f(cs[b], 0ull, ps[b]);
+      }
+    }
+  }
+};
+template <class PosF>
+__device__ __forceinline__ KeptWords<PosF> kept_words(int N, const uint32_t* kb, PosF pos) {
+  return KeptWords<PosF>{(N + 31) / 32, kb, pos};
 }
 
 // Large segments (see large_select); false = candidate overflow, nothing emitted.
@@ -1325,10 +1494,26 @@ __device__ bool bsel_large(const BParams& p, const RowCtx& r, int i, int lg, int
                                                                               : BIN_K32;
   auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool { return bsel_column(p, r, i, lg, c, key, pv); };
   large_init(r.N, lb);
-  const int nprot = block_sum(kind == BIN_K32   ? large_tail<BIN_K32>(colfn, 0, r.N, lb)
-                             : kind == BIN_R53 ? large_tail<BIN_R53>(colfn, 0, r.N, lb)
-                                               : large_tail<BIN_U64>(colfn, 0, r.N, lb),
-                             sh);
+  int np;
+  switch (r.q.policy) {
+    case CE_POLICY_HEAD_SUM:
+    case CE_POLICY_HEAD_MAX:
+      np = bsel_scan<BS_SCORE, BIN_K32>(p, r, i, lg, lb);
+      break;
+    case CE_POLICY_H2O_GLOBAL:
+      np = p.gscores ? bsel_scan<BS_H2O, BIN_K32>(p, r, i, lg, lb) : large_tail<BIN_K32>(colfn, 0, r.N, lb);
+      break;
+    case CE_POLICY_RANDOM:
+      np = p.udt == CE_DTYPE_F64 ? bsel_scan<BS_U64, BIN_U64>(p, r, i, lg, lb)
+                                 : bsel_scan<BS_U32, BIN_K32>(p, r, i, lg, lb);
+      break;
+    case CE_POLICY_RESERVOIR:
+      np = bsel_scan<BS_RES, BIN_R53>(p, r, i, lg, lb);
+      break;
+    default:
+      np = bsel_scan<BS_NONE, BIN_K32>(p, r, i, lg, lb);
+  }
+  const int nprot = block_sum(np, sh);
   if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * LG + lg] = nprot;
   if (nprot > r.q.budget) return true;
   const int k = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
@@ -1336,14 +1521,58 @@ __device__ bool bsel_large(const BParams& p, const RowCtx& r, int i, int lg, int
   if (!large_select(colfn, r.N, k, r.N - nprot, kind, lb, sh, sel)) return false;
   uint32_t* kb = reinterpret_cast<uint32_t*>(lb.hist);
   large_kept_bits<false>(lb, sel, r.N, kb);
-  bsel_emit(p, r,
-            kept_bits(r.N, kb, [&](int c) { return col_pos(p, r, lg, c); },
-                      [](int) { return make_int4(0, 0, 0, 0); }, false),
+  bsel_emit(p, r, kept_words(r.N, kb, [&](int c) { return col_pos(p, r, lg, c); }),
             [](int, uint64_t, int32_t pc) -> int { return pc; }, nprot, i, lg, base, sh, bitsm, pre);
   return true;
 }
 
-// Segment blocks: R*L*G of them, then R row blocks.
+// A row's new columns [cnt, N) hold the consecutive positions [fr, n)
+// (column c: pos0 + c).  By is_prot, the protected ones are [fr, a1) (under
+// the prefix) and [b0, n) (the recent window and the cursor guard), and the
+// candidates are [a1, b0).
+struct RowSplit {
+  int pos0, a1, b0;
+};
+__device__ __forceinline__ RowSplit row_split(const RowCtx& r) {
+  const int n = r.q.n;
+  const int lo = r.q.cursor >= 0 ? min(n - r.q.recent, r.q.cursor) : n - r.q.recent;
+  RowSplit s;
+  s.pos0 = r.fr - r.cnt;
+  s.a1 = min(max(r.q.prefix, r.fr), n);
+  s.b0 = min(max(lo, s.a1), n);
+  return s;
+}
+
+// The (0,0) head's protected columns of a row as emit_sorted's column set
+// (key = unit, pv = position): the kept columns through their loaded
+// positions, then the new columns at positions [fr, a1) and [b0, n).
+struct RowProtCols {
+  const BParams* p;
+  RowCtx r;
+  RowSplit sp;
+  template <class F>
+  __device__ __forceinline__ void each(F f) const {
+    const BParams& pp = *p;
+    const RowCtx& rr = r;
+    loaded_range(rr.cnt, [&](int c, uint64_t& key, int32_t& pv) {
+      pv = col_pos(pp, rr, 0, c);
+      key = static_cast<uint32_t>(pp.table[rr.row * pp.ts + c]);
+    }).each(f);
+    const int32_t* r2u_row = pp.r2u + rr.row * pp.rs;
+    const int pos0 = sp.pos0;
+    auto fresh = [&](int x0, int x1) {
+      batched<8>(
+          x1 - x0, [&](int k) { return r2u_row[x0 + k]; }, [](int, int) { return 0; },
+          [&](int k, int u, int) { f(x0 + k - pos0, static_cast<uint64_t>(static_cast<uint32_t>(u)), x0 + k); });
+    };
+    fresh(rr.fr, sp.a1);
+    fresh(sp.b0, rr.q.n);
+  }
+};
+
+// R row blocks, then R*L*G segment blocks.  Row blocks come first so that
+// when the segments take more than one wave, the row blocks (a full pass
+// over each row's columns) run beside the first wave instead of after it.
 template <bool LARGE>
 __global__ void __launch_bounds__(T, LARGE ? 1 : 2) bsel_kernel(const BParams p) {
   extern __shared__ uint32_t dyn[];
@@ -1351,9 +1580,9 @@ __global__ void __launch_bounds__(T, LARGE ? 1 : 2) bsel_kernel(const BParams p)
   uint32_t* bitsm = dyn;
   int* pre = reinterpret_cast<int*>(dyn + p.nw);
   const int LG = p.L * p.G;
-  const int nseg = p.R * LG;
-  if (static_cast<int>(blockIdx.x) < nseg) {
-    const int i = blockIdx.x / LG, lg = blockIdx.x % LG;
+  if (static_cast<int>(blockIdx.x) >= p.R) {
+    const int sb = static_cast<int>(blockIdx.x) - p.R;
+    const int i = sb / LG, lg = sb % LG;
     const RowCtx r = row_ctx(p, i);
     if (!row_shape_ok(p, r) || r.N <= r.q.budget) return;
     const int64_t base = (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
@@ -1376,13 +1605,18 @@ __global__ void __launch_bounds__(T, LARGE ? 1 : 2) bsel_kernel(const BParams p)
     }
   } else {
     // ---------------- row block: table, candidates, leftovers, marks -----------
-    const int i = blockIdx.x - nseg;
+    const int i = blockIdx.x;
     const RowCtx r = row_ctx(p, i);
-    int32_t* info = p.row_info + i * 8;
+    int32_t* info = p.row_info + i * RI;
     if (!row_shape_ok(p, r) || r.N <= r.q.budget) return;
+    // Kept columns [0, cnt) are counted and ranked through the (0,0) head's
+    // loaded positions; new columns hold consecutive positions, so theirs
+    // follow from the split (row_split) without loads.
+    const RowSplit sp = row_split(r);
     int np = 0;
-    for (int c = threadIdx.x; c < r.N; c += T) np += is_prot(col_pos(p, r, 0, c), r.q);
-    const int nprot = block_sum(np, sh);
+    loaded_range(r.cnt, [&](int c, uint64_t&, int32_t& pos) { pos = col_pos(p, r, 0, c); })
+        .each([&](int, uint64_t, int32_t pos) { np += is_prot(pos, r.q); });
+    const int nprot = block_sum(np, sh) + (sp.a1 - r.fr) + (r.q.n - sp.b0);
     if (nprot > r.q.budget) {
       if (threadIdx.x == 0) info[1] = nprot;
       return;
@@ -1390,48 +1624,155 @@ __global__ void __launch_bounds__(T, LARGE ? 1 : 2) bsel_kernel(const BParams p)
     const int W = (r.q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : r.q.budget - nprot;
     int32_t* ntab = p.new_table + static_cast<int64_t>(i) * p.max_cols;
     int32_t* crank = p.cand_rank + static_cast<int64_t>(i) * p.max_cols;
+    int32_t* pcol = p.prot_col + static_cast<int64_t>(i) * p.max_cols;
+    const int32_t* r2u_row = p.r2u + r.row * p.rs;
+    // protected units first, in (0,0) position order (key = unit, pv = position),
+    // and their columns for the protected slots of every head (bfinish_kernel)
     emit_sorted(
-        RangeCols{r.N}, p.nw, bitsm, pre,
-        [&](int c, uint64_t, int32_t) -> int {
-          const int p00 = col_pos(p, r, 0, c);
-          return is_prot(p00, r.q) ? p00 : -1;
+        RowProtCols{&p, r, sp}, p.nw, bitsm, pre,
+        [&](int, uint64_t, int32_t p00) -> int { return is_prot(p00, r.q) ? p00 : -1; },
+        [&](int rank, int c, int, uint64_t key) {
+          ntab[rank] = static_cast<int32_t>(key);
+          pcol[rank] = c;
         },
-        [&](int rank, int c, int) { ntab[rank] = col_unit(p, r, c); }, sh, p.err);
+        sh, p.err);
+    // Candidates (columns the (0,0) head does not protect) ranked in column
+    // order.  Kept columns: tiles of 8 words of 32 columns per warp, each lane
+    // loading its column of every word; the ballots give the candidate words
+    // and one block scan per tile offsets the warps.
     int carry = 0;
-    for (int b0 = 0; b0 < r.N; b0 += T) {
-      const int c = b0 + threadIdx.x;
-      const bool in = c < r.N;
-      const bool cand = in && !is_prot(col_pos(p, r, 0, c), r.q);
-      int tot;
-      const int ex = block_excl(cand ? 1 : 0, sh, tot);
-      if (in) {
-        if (cand) {
-          const int cr = carry + ex;
-          crank[c] = cr;
-          if (cr < W)
-            ntab[nprot + cr] = col_unit(p, r, c);
-          else if (p.live)
-            p.freed[i * p.freed_stride + (cr - W)] = col_unit(p, r, c);
-        } else {
-          crank[c] = -1;
+    int swa_bad = 0;   // a freed unit still maps to a sliding-window slot (runtime:477-479)
+    auto swa_of = [&](int u) -> int64_t { return (p.swa && u >= 0 && u < p.pool_units) ? p.swa[u] : 0; };
+    {
+      constexpr int WW = 8;
+      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+      const uint32_t below = (1u << lane) - 1u;
+      for (int t0 = 0; t0 < r.cnt; t0 += NW * WW * 32) {
+        const int cw = t0 + warp * WW * 32 + lane;
+        int pos[WW], unit[WW];
+#pragma unroll
+        for (int j = 0; j < WW; ++j) {
+          const int c = cw + 32 * j;
+          pos[j] = c < r.cnt ? col_pos(p, r, 0, c) : 0;
+          unit[j] = c < r.cnt ? col_unit(p, r, c) : 0;
         }
+        uint32_t word[WW];
+        int wtot = 0;
+#pragma unroll
+        for (int j = 0; j < WW; ++j) {
+          word[j] = __ballot_sync(0xffffffffu, cw + 32 * j < r.cnt && !is_prot(pos[j], r.q));
+          wtot += __popc(word[j]);
+        }
+        int tot;
+        const int ex = block_excl(lane == 0 ? wtot : 0, sh, tot);
+        int run = carry + __shfl_sync(0xffffffffu, ex, 0);
+        int cr[WW];   // candidate rank, -1 for a protected column
+#pragma unroll
+        for (int j = 0; j < WW; ++j) {
+          cr[j] = ((word[j] >> lane) & 1u) ? run + __popc(word[j] & below) : -1;
+          run += __popc(word[j]);
+        }
+        if (p.live && p.swa) {
+#pragma unroll
+          for (int j = 0; j < WW; ++j) swa_bad |= cr[j] >= W && swa_of(unit[j]) != 0;
+        }
+#pragma unroll
+        for (int j = 0; j < WW; ++j) {
+          const int c = cw + 32 * j;
+          if (c >= r.cnt) continue;
+          crank[c] = cr[j];
+          if (cr[j] < 0) continue;
+          if (cr[j] < W)
+            ntab[nprot + cr[j]] = unit[j];
+          else if (p.live)
+            p.freed[i * p.freed_stride + (cr[j] - W)] = unit[j];
+        }
+        carry += tot;
       }
-      carry += tot;
     }
+    // New columns: the candidates are the positions [a1, b0), after the kept ones.
+    batched<8>(
+        r.N - r.cnt,
+        [&](int k) {
+          const int x = r.fr + k;
+          return (x >= sp.a1 && x < sp.b0) ? r2u_row[x] : 0;
+        },
+        [&](int k, int u) -> int64_t {
+          const int x = r.fr + k;
+          return (p.live && x >= sp.a1 && x < sp.b0 && carry + (x - sp.a1) >= W) ? swa_of(u) : 0;
+        },
+        [&](int k, int u, int64_t m) {
+          const int x = r.fr + k, c = r.cnt + k;
+          swa_bad |= m != 0;
+          if (x >= sp.a1 && x < sp.b0) {
+            const int cr = carry + (x - sp.a1);
+            crank[c] = cr;
+            if (cr < W)
+              ntab[nprot + cr] = u;
+            else if (p.live)
+              p.freed[i * p.freed_stride + (cr - W)] = u;
+          } else {
+            crank[c] = -1;
+          }
+        });
+    swa_bad = block_sum(swa_bad, sh);
     const int true_u = min(r.q.n - r.q.recent, r.q.cursor >= 0 ? r.q.cursor : r.q.n);
     if (p.live) {
-      for (int x = max(true_u, 0) + threadIdx.x; x < r.q.n; x += T) {
-        const int u = p.r2u[r.row * p.rs + x];
-        if (u >= 0 && u < p.pool_units) p.marks[u] = p.epoch;
+      const int x0 = max(true_u, 0);
+      batched<8>(
+          r.q.n - x0, [&](int k) { return p.r2u[r.row * p.rs + x0 + k]; }, [](int, int) { return 0; },
+          [&](int, int u, int) {
+            if (u >= 0 && u < p.pool_units) p.marks[u] = p.epoch;
+          });
+    }
+    // The packed req_to_unit prefix (runtime:484-491): every unit of the new
+    // table that is not a real slot of [true_u, n), in table order.  The table
+    // and the marks are this block's own writes; bfinish_kernel copies the
+    // list into the row once the other blocks no longer read it.
+    int npacked = 0;
+    if (p.live) {
+      __syncthreads();
+      const int after = nprot + W;
+      int32_t* plist = p.pack + static_cast<int64_t>(i) * p.max_cols;
+      constexpr int WW = 8;
+      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+      const uint32_t below = (1u << lane) - 1u;
+      for (int t0 = 0; t0 < after; t0 += NW * WW * 32) {
+        const int kw = t0 + warp * WW * 32 + lane;
+        int u[WW], m[WW];
+#pragma unroll
+        for (int j = 0; j < WW; ++j) u[j] = kw + 32 * j < after ? ntab[kw + 32 * j] : -1;
+#pragma unroll
+        for (int j = 0; j < WW; ++j) m[j] = (u[j] >= 0 && u[j] < p.pool_units) ? p.marks[u[j]] : 0;
+        uint32_t word[WW];
+        int wtot = 0;
+#pragma unroll
+        for (int j = 0; j < WW; ++j) {
+          const bool real = u[j] >= 0 && u[j] < p.pool_units && m[j] == p.epoch;
+          word[j] = __ballot_sync(0xffffffffu, kw + 32 * j < after && !real);
+          wtot += __popc(word[j]);
+        }
+        int tot;
+        const int ex = block_excl(lane == 0 ? wtot : 0, sh, tot);
+        int run = npacked + __shfl_sync(0xffffffffu, ex, 0);
+#pragma unroll
+        for (int j = 0; j < WW; ++j) {
+          if ((word[j] >> lane) & 1u) plist[run + __popc(word[j] & below)] = u[j];
+          run += __popc(word[j]);
+        }
+        npacked += tot;
       }
     }
     if (threadIdx.x == 0) {
+      info[9] = npacked;
       info[0] = r.N;
       info[1] = nprot;
       info[2] = W;
       info[3] = nprot + W;
       info[4] = true_u;
       info[5] = r.N - nprot - W;
+      info[6] = r.cnt;
+      info[8] = swa_bad > 0;
     }
   }
 }
@@ -1459,7 +1800,7 @@ __global__ void bvalidate_kernel(const BParams p) {
   if (threadIdx.x != 0) return;
   const RowCtx r = row_ctx(p, i);
   const int LG = p.L * p.G;
-  int32_t* info = p.row_info + i * 8;
+  int32_t* info = p.row_info + i * RI;
   int st;
   int after = r.N;
   if (!row_shape_ok(p, r)) {
@@ -1502,7 +1843,7 @@ __global__ void __launch_bounds__(T) brecord_kernel(const BParams p) {
   __shared__ Sh sh;
   const int LG = p.L * p.G;
   const int i = blockIdx.x / LG, lg = blockIdx.x % LG;
-  const int32_t* info = p.row_info + i * 8;
+  const int32_t* info = p.row_info + i * RI;
   int32_t* cnt_out = p.rec_counts + static_cast<int64_t>(i) * LG + lg;
   if (info[7] != 0) {
     if (threadIdx.x == 0) *cnt_out = 0;
@@ -1529,7 +1870,7 @@ __global__ void __launch_bounds__(T) brecord_kernel(const BParams p) {
   emit_sorted(
       RangeCols{r.N}, p.nw, bits, pre,
       [&](int c, uint64_t, int32_t) -> int { return is_bit(kept, c) ? -1 : col_pos(p, r, lg, c); },
-      [&](int rank, int, int pos) {
+      [&](int rank, int, int pos, uint64_t) {
         if (rank < stride) out[rank] = static_cast<uint32_t>(pos);
         else flag_error(err, CE_EW_CAPACITY);
       },
@@ -1552,13 +1893,17 @@ __global__ void __launch_bounds__(T) brecord_kernel(const BParams p) {
   }
 }
 
-// One warp per chunk of CH consecutive middle survivors j of one (row,
-// layer-in-group, head): lane k < CH holds item j0 + k.  The chunk index is
-// decoded once with 32-bit arithmetic (the host checks that the count fits),
-// the lanes load their items' metadata in parallel, and the warp then copies
-// the chunk's items one after another; CH is small enough that a launch has
-// thousands of warps, each with a 4 KB copy in flight.
-constexpr int CH = 8;
+// One warp per chunk of p.ch consecutive middle survivors j of one (row,
+// layer-in-group, head): lane k < p.ch holds item j0 + k.  The chunk index is
+// decoded once with 32-bit arithmetic (the host checks that the count fits)
+// and the lanes load their items' metadata in parallel.  Slices of 2 KB and
+// more (page size >= 16) take chunks of 8 items copied one after another,
+// each a 4 KB K + V pair in flight; smaller slices take chunks of 32 items
+// copied together (copy_items).
+constexpr int CH_PAGED = 8;
+constexpr int CH_SMALL = 32;
+__host__ __device__ __forceinline__ int chunk_items(int P) { return P * 128 >= 2048 ? CH_PAGED : CH_SMALL; }
+
 struct Chunk {
   int i, l, g, j;         // this lane's item
   int W, nprot;
@@ -1567,7 +1912,7 @@ struct Chunk {
   bool valid;
 };
 
-__device__ __forceinline__ int chunks_per_seg(const BParams& p) { return (p.max_width + CH - 1) / CH; }
+__device__ __forceinline__ int chunks_per_seg(const BParams& p) { return (p.max_width + p.ch - 1) / p.ch; }
 
 __device__ __forceinline__ Chunk decode_chunk(const BParams& p, uint32_t wi, int r0, int l0, int nl, int lane) {
   Chunk c;
@@ -1580,11 +1925,11 @@ __device__ __forceinline__ Chunk decode_chunk(const BParams& p, uint32_t wi, int
   const int ll = static_cast<int>(rem / static_cast<uint32_t>(p.G));
   c.g = static_cast<int>(rem) - ll * p.G;
   c.l = l0 + ll;
-  c.j = static_cast<int>(jc) * CH + lane;
-  const int32_t* info = p.row_info + c.i * 8;
+  c.j = static_cast<int>(jc) * p.ch + lane;
+  const int32_t* info = p.row_info + c.i * RI;
   c.W = info[2];
   c.nprot = info[1];
-  c.valid = lane < CH && info[7] == 0 && c.j < c.W;
+  c.valid = lane < p.ch && info[7] == 0 && c.j < c.W;
   c.base = (static_cast<int64_t>(c.i) * p.L * p.G + static_cast<int64_t>(c.l) * p.G + c.g) * p.max_cols;
   c.item = ((static_cast<int64_t>(ir) * nl + ll) * p.G + c.g) * p.max_width + c.j;
   return c;
@@ -1630,6 +1975,48 @@ __device__ __forceinline__ void copy_pair(uint8_t* dk, uint8_t* dv, const uint8_
   }
 }
 
+// Copy the K and V slices (bytes each, under 2 KB) of every item whose bit is
+// set in todo (warp-uniform, from a ballot) with the whole warp at once: the
+// (item, 16-byte vector) pairs are spread over the lanes, four per lane in
+// flight, so a chunk costs about one load latency instead of one per item.
+// addr(k, sk, sv, dk, dv) gives item k's addresses; it shuffles from lane k,
+// so every lane calls it, for items that are skipped too.
+template <class AddrF>
+__device__ __forceinline__ void copy_items(unsigned todo, int bytes, int lane, AddrF addr) {
+  if (!todo) return;
+  const int vecs = bytes >> 4;
+  const int total = (32 - __clz(static_cast<int>(todo))) * vecs;
+  for (int f0 = 0; f0 < total; f0 += 4 * 32) {
+    uint4 a[4], b[4];
+    uint8_t* dk[4];
+    uint8_t* dv[4];
+    bool ok[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int f = f0 + u * 32 + lane;
+      const int k = min(f / vecs, 31);
+      const uint8_t* sk;
+      const uint8_t* sv;
+      addr(k, sk, sv, dk[u], dv[u]);
+      ok[u] = f < total && ((todo >> k) & 1u);
+      if (ok[u]) {
+        const int x = (f - k * vecs) * 16;
+        a[u] = __ldg(reinterpret_cast<const uint4*>(sk + x));
+        b[u] = __ldg(reinterpret_cast<const uint4*>(sv + x));
+        dk[u] += x;
+        dv[u] += x;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (ok[u]) {
+        *reinterpret_cast<uint4*>(dk[u]) = a[u];
+        *reinterpret_cast<uint4*>(dv[u]) = b[u];
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t launch_chunks(const BParams& p, int nr, int nl) {
   return static_cast<uint32_t>(nr) * static_cast<uint32_t>(nl * p.G) * static_cast<uint32_t>(chunks_per_seg(p));
 }
@@ -1653,7 +2040,21 @@ __global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int r0, i
         hz = false;
       }
     }
-    for (unsigned todo = __ballot_sync(0xffffffffu, hz); todo; todo &= todo - 1) {
+    const unsigned hmask = __ballot_sync(0xffffffffu, hz);
+    if (bytes < 2048) {
+      // c.l, c.g and c.item - lane are the same on every lane of the chunk
+      const int64_t item0 = c.item - lane;
+      copy_items(hmask, bytes, lane,
+                 [&](int k, const uint8_t*& sk, const uint8_t*& sv, uint8_t*& dk, uint8_t*& dv) {
+                   const int s = max(__shfl_sync(0xffffffffu, src, k), 0);
+                   sk = unit_ptr(p.k_layers, c.l, s, c.g, p.G, p.P);
+                   sv = unit_ptr(p.v_layers, c.l, s, c.g, p.G, p.P);
+                   dk = p.hazard + (item0 + k) * 2 * bytes;
+                   dv = dk + bytes;
+                 });
+      continue;
+    }
+    for (unsigned todo = hmask; todo; todo &= todo - 1) {
       const int k = __ffs(todo) - 1;
       const int s = __shfl_sync(0xffffffffu, src, k);
       const int64_t it = __shfl_sync(0xffffffffu, c.item, k);
@@ -1686,7 +2087,23 @@ __global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int r0, 
         hz = move && chunk_hazard(p, c);
       }
     }
-    for (unsigned todo = __ballot_sync(0xffffffffu, move); todo; todo &= todo - 1) {
+    const unsigned mmask = __ballot_sync(0xffffffffu, move);
+    if (bytes < 2048) {
+      const int64_t item0 = c.item - lane;
+      copy_items(mmask, bytes, lane,
+                 [&](int k, const uint8_t*& sk, const uint8_t*& sv, uint8_t*& dk, uint8_t*& dv) {
+                   const int s = max(__shfl_sync(0xffffffffu, src, k), 0);
+                   const int d = max(__shfl_sync(0xffffffffu, dst, k), 0);
+                   const bool h = __shfl_sync(0xffffffffu, hz, k);
+                   const uint8_t* scr = p.hazard + (item0 + k) * 2 * bytes;
+                   sk = h ? scr : unit_ptr(p.k_layers, c.l, s, c.g, p.G, p.P);
+                   sv = h ? scr + bytes : unit_ptr(p.v_layers, c.l, s, c.g, p.G, p.P);
+                   dk = unit_ptr(p.k_layers, c.l, d, c.g, p.G, p.P);
+                   dv = unit_ptr(p.v_layers, c.l, d, c.g, p.G, p.P);
+                 });
+      continue;
+    }
+    for (unsigned todo = mmask; todo; todo &= todo - 1) {
       const int k = __ffs(todo) - 1;
       const int s = __shfl_sync(0xffffffffu, src, k);
       const int d = __shfl_sync(0xffffffffu, dst, k);
@@ -1700,46 +2117,63 @@ __global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int r0, 
   }
 }
 
-// Grid (rows, 1 + L * G).  Block (i, 0): table, count, frontier, the
-// sliding-window guard and the req_to_unit packing of row i.  Block (i, 1 + s):
-// the new positions of segment s = (layer, head) and, for a live boundary that
-// passes the guard, zero scores of that (layer, head) at every freed unit.
+// Grid (rows, 1 + L * G, Z).  Block (i, 0, 0): table, count, frontier and
+// the req_to_unit packing of row i.  Block (i, 1 + s, 0): the new positions of
+// segment s = (layer, head) -- its protected slots gathered here, its middle
+// survivors from the selection.  Blocks (i, 1 + s, z), for a live boundary
+// that passed the sliding-window guard: zero that (layer, head)'s scores at
+// the z-th of Z chunks of the row's freed units (scattered stores, spread
+// over Z blocks so that more SMs issue them).
 __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
-  __shared__ Sh sh;
-  __shared__ int bad;
   const int i = blockIdx.x;
-  const int32_t* info = p.row_info + i * 8;
+  const int32_t* info = p.row_info + i * RI;
   if (info[7] != 0) return;
-  const RowCtx r = row_ctx(p, i);
+  // The row as the selection saw it (block (i, 0) rewrites count and frontier).
+  RowCtx r;
+  r.row = p.rows[i];
+  r.q = p.params[i];
+  r.N = info[0];
+  r.cnt = info[6];
+  r.fr = r.cnt + r.q.n - r.N;
   const int after = info[3], true_u = info[4], nleft = info[5];
+  const bool bad = info[8] != 0;   // guard of runtime:477-479, checked by the row block
   const int LG = p.L * p.G;
   const int32_t* ntab = p.new_table + static_cast<int64_t>(i) * p.max_cols;
   const int32_t* left = p.freed + i * p.freed_stride;
-  if (threadIdx.x == 0) bad = 0;
-  __syncthreads();
-  // The guard (runtime:477-479): no freed unit may still map to a sliding-window slot.
-  if (p.live && p.swa) {
-    for (int k = threadIdx.x; k < nleft; k += T) {
-      const int u = left[k];
-      if (u >= 0 && u < p.pool_units && p.swa[u] != 0) bad = 1;
-    }
-  }
-  __syncthreads();
+  const int z = blockIdx.z;
   if (blockIdx.y > 0) {
     const int lg = static_cast<int>(blockIdx.y) - 1;
     if (lg >= LG) return;
-    const int32_t* src = p.new_pos + (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
-    int32_t* dst = p.pos + r.row * p.prs + static_cast<int64_t>(lg) * p.pos_cap;
-    for (int k = threadIdx.x; k < after; k += T) dst[k] = src[k];
-    if (!p.live || bad) return;
-    float* sc = p.scores + (lg / p.G) * p.sls + (lg % p.G) * p.shs;
-    for (int k = threadIdx.x; k < nleft; k += T) {
-      const int u = left[k];
-      if (u >= 0 && u < p.pool_units) sc[u] = 0.f;
+    if (z == 0) {
+      int32_t* src = p.new_pos + (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
+      int32_t* dst = p.pos + r.row * p.prs + static_cast<int64_t>(lg) * p.pos_cap;
+      // Protected slots: this head's positions at the (0,0) head's protected
+      // columns, in (0,0) position order (runtime:442-443, 469).  Every read
+      // of the old positions ends before the copy below overwrites them.
+      const int32_t* pcol = p.prot_col + static_cast<int64_t>(i) * p.max_cols;
+      batched<8>(
+          info[1], [&](int k) { return pcol[k]; }, [&](int, int c) { return col_pos(p, r, lg, c); },
+          [&](int k, int, int v) { src[k] = v; });
+      __syncthreads();
+      batched<8>(
+          after, [&](int k) { return src[k]; }, [](int, int) { return 0; },
+          [&](int k, int v, int) { dst[k] = v; });
     }
+    if (!p.live || bad) return;
+    const int per = (nleft + gridDim.z - 1) / gridDim.z;
+    const int k0 = min(nleft, z * per), k1 = min(nleft, k0 + per);
+    float* sc = p.scores + (lg / p.G) * p.sls + (lg % p.G) * p.shs;
+    batched<8>(
+        k1 - k0, [&](int k) { return left[k0 + k]; }, [](int, int) { return 0; },
+        [&](int, int u, int) {
+          if (u >= 0 && u < p.pool_units) sc[u] = 0.f;
+        });
     return;
   }
-  for (int k = threadIdx.x; k < after; k += T) p.table[r.row * p.ts + k] = ntab[k];
+  if (z != 0) return;
+  batched<8>(
+      after, [&](int k) { return ntab[k]; }, [](int, int) { return 0; },
+      [&](int k, int u, int) { p.table[r.row * p.ts + k] = u; });
   int32_t* res = p.result + i * 4;
   if (threadIdx.x == 0) {
     p.count[r.row] = after;
@@ -1757,13 +2191,8 @@ __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
     return;
   }
   if (threadIdx.x == 0) res[3] = nleft;
-  // Pack every owned unit that is not a real slot of [true_u, n) at the row start.
-  int np = 0;
-  for (int k = threadIdx.x; k < after; k += T) {
-    const int u = ntab[k];
-    np += !(u >= 0 && u < p.pool_units && p.marks[u] == p.epoch);
-  }
-  const int npacked = block_sum(np, sh);
+  // The packed prefix the row block listed (runtime:484-491), then zeros up to true_u.
+  const int npacked = info[9];
   if (npacked > true_u) {
     if (threadIdx.x == 0) {
       res[0] = 4;
@@ -1772,16 +2201,10 @@ __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
     return;
   }
   int32_t* rrow = p.r2u + r.row * p.rs;
-  int carry = 0;
-  for (int b0 = 0; b0 < after; b0 += T) {
-    const int k = b0 + threadIdx.x;
-    const int u = (k < after) ? ntab[k] : 0;
-    const bool keep = k < after && !(u >= 0 && u < p.pool_units && p.marks[u] == p.epoch);
-    int tot;
-    const int ex = block_excl(keep ? 1 : 0, sh, tot);
-    if (keep) rrow[carry + ex] = u;
-    carry += tot;
-  }
+  const int32_t* plist = p.pack + static_cast<int64_t>(i) * p.max_cols;
+  batched<8>(
+      npacked, [&](int k) { return plist[k]; }, [](int, int) { return 0; },
+      [&](int k, int u, int) { rrow[k] = u; });
   for (int x = npacked + threadIdx.x; x < min(true_u, p.r2u_width); x += T) rrow[x] = 0;
 }
 
@@ -1817,7 +2240,7 @@ namespace {
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct BLayout {
-  size_t kv, pv, seg, mid, src, npos, ssc, info, crank, ntab, hsum, hazard, total;
+  size_t kv, pv, seg, mid, src, npos, ssc, info, crank, ntab, pcol, pack, hsum, hazard, total;
 };
 
 BLayout boundary_layout(int R, int L, int G, int max_cols, int64_t hazard_bytes) {
@@ -1831,9 +2254,11 @@ BLayout boundary_layout(int R, int L, int G, int max_cols, int64_t hazard_bytes)
   b.src = o; o += a256(cells * 4);
   b.npos = o; o += a256(cells * 4);
   b.ssc = o; o += a256(cells * 4);
-  b.info = o; o += a256(static_cast<size_t>(R) * 8 * 4);
+  b.info = o; o += a256(static_cast<size_t>(R) * RI * 4);
   b.crank = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
   b.ntab = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
+  b.pcol = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
+  b.pack = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
   b.hsum = o; o += a256(static_cast<size_t>(R) * L * max_cols * 4);
   b.hazard = o; o += a256(static_cast<size_t>(hazard_bytes));
   b.total = o;
@@ -2026,6 +2451,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
                   score_head_stride, pool_units, layers, kv_heads, page_size, rows, params,
                   num_rows, max_cols, max_n);
   p.max_width = width;
+  p.ch = chunk_items(page_size);
   p.k_layers = k_layers;
   p.v_layers = v_layers;
   p.head_offset = head_offset;
@@ -2048,6 +2474,8 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   p.row_info = reinterpret_cast<int32_t*>(ws + Lo.info);
   p.cand_rank = reinterpret_cast<int32_t*>(ws + Lo.crank);
   p.new_table = reinterpret_cast<int32_t*>(ws + Lo.ntab);
+  p.prot_col = reinterpret_cast<int32_t*>(ws + Lo.pcol);
+  p.pack = reinterpret_cast<int32_t*>(ws + Lo.pack);
   p.hazard = ws + Lo.hazard;
   if (!global_scores) {   // H2O global rows sum their heads once, in hsum_kernel
     p.gscores = reinterpret_cast<float*>(ws + Lo.hsum);
@@ -2065,7 +2493,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   const int smem = sel_smem(nw) + (large ? LARGE_BYTES : 0);
   if (!host::set_smem(bsel_kernel<false>, smem) || !host::set_smem(bsel_kernel<true>, smem))
     return host::fail(CE_ERR_CUDA, "smem attr");
-  if (cudaMemsetAsync(p.row_info, 0, sizeof(int32_t) * 8 * num_rows, st) != cudaSuccess)
+  if (cudaMemsetAsync(p.row_info, 0, sizeof(int32_t) * RI * num_rows, st) != cudaSuccess)
     return host::fail_cuda("row_info memset");
   if (!global_scores) {
     hsum_kernel<<<dim3((max_cols + 255) / 256, num_rows), 256, 0, st>>>(p, const_cast<float*>(p.gscores));
@@ -2097,8 +2525,8 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
     const int nr = std::min(rows_per, num_rows - r0);
     for (int l0 = 0; l0 < layers; l0 += group) {
       const int nl = std::min(group, layers - l0);
-      // one warp per chunk of CH middle survivors of a (row, layer, head)
-      const int64_t chunks = static_cast<int64_t>(nr) * nl * kv_heads * ((width + CH - 1) / CH);
+      // one warp per chunk of p.ch middle survivors of a (row, layer, head)
+      const int64_t chunks = static_cast<int64_t>(nr) * nl * kv_heads * ((width + p.ch - 1) / p.ch);
       if (chunks > INT32_MAX) return host::fail(CE_ERR_UNSUPPORTED, "ce_boundary: too many rows x layers x heads");
       const int64_t want = (chunks * 32 + 255) / 256;
       const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 8LL * nsm)));
@@ -2108,7 +2536,13 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
       if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bscatter_kernel");
     }
   }
-  bfinish_kernel<<<dim3(num_rows, 1 + layers * kv_heads), T, 0, st>>>(p);
+  // Score-zeroing chunks per (row, layer, head): enough blocks for about
+  // four per SM, each chunk at least 4,096 freed units.
+  const int zc = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>((4LL * nsm + int64_t(num_rows) * layers * kv_heads - 1) /
+                               (int64_t(num_rows) * layers * kv_heads),
+                           (max_cols + 4095) / 4096)));
+  bfinish_kernel<<<dim3(num_rows, 1 + layers * kv_heads, zc), T, 0, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bfinish_kernel");
   return CE_OK;
 }

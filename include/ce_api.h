@@ -324,6 +324,7 @@ int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols,
  *   swa_mapping [pool_units] int64 or NULL (reference
  *           allocator.full_to_swa_index_mapping, runtime:477-479)
  *   uniforms [num_rows, layers, heads, max_cols] f32/f64 for random rows
+ *           (a random row without them gets status 6)
  *   global_scores [num_rows, layers, global_heads, max_cols] fp32 or NULL:
  *           dense per-column scores of ALL KV heads (tensor-parallel ranks
  *           all-gather them); when NULL h2o_global sums the local heads
@@ -333,7 +334,8 @@ int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols,
  *   max_n    >= every row's n (positions are ranked in a max_n-bit bitmap)
  *   result  [num_rows, 4]: status (0 evicted, 1 nothing to do, 2 deferred,
  *           3 protected mismatch, 4 packing error, 5 sliding-window error,
- *           6 row sizes outside max_cols/max_n/pos_cap), columns before,
+ *           6 row sizes outside max_cols/max_n/pos_cap, or no uniforms for a
+ *           random row), columns before,
  *           residents after (the protected count when deferred), units freed
  *   freed_units [num_rows, freed_stride] leftover units (live only)
  *   record_delta, record_counts  retention record (runtime:465-467, 500-507),

@@ -454,6 +454,25 @@ def test_boundary_noop_deferred_and_mismatch():
         assert int(g["frontier"][r]) == 0
 
 
+def test_boundary_random_row_without_uniforms_is_rejected():
+    """A random row needs the caller's uniforms: without them the row gets
+    status 6 and CE_EW_SHAPE, and nothing of it changes."""
+    rng = np.random.default_rng(5)
+    state, kl, vl = _paged_state(rng, 2, 1, 8, 16, 400, 256, 256)
+    for r in range(2):
+        state["r2u"][r, :150] = np.arange(1 + 150 * r, 151 + 150 * r)
+    g = _gpu_state(state, kl, vl)
+    params = [dict(n=128, budget=64, prefix=16, recent=16, cursor=None, policy="random_2048"),
+              dict(n=128, budget=64, prefix=16, recent=16, cursor=None, policy="head_sum_2048")]
+    before = {k: v.clone() for k, v in g.items() if isinstance(v, torch.Tensor)}
+    res, _, err = _gpu_boundary(g, [0, 1], params, 128, 129, True, 1, page=16)
+    assert res[0, 0] == 6 and res[1, 0] == 0, res
+    from cache_eviction_b200 import capi
+    assert err & capi.CE_EW_SHAPE
+    for key in ("table", "r2u", "pos", "frontier", "count"):
+        assert torch.equal(g[key][0], before[key][0]), key
+
+
 def test_boundary_sliding_window_guard_error():
     rng = np.random.default_rng(8)
     state, kl, vl = _paged_state(rng, 1, 1, 8, 16, 400, 256, 256)

@@ -103,17 +103,16 @@ def test_choose_large_vs_oracle(policy, skind, compacted, N):
                                           err_msg=f"row {r} budget {budget}")
 
 
-@pytest.mark.parametrize("policy", ["head_sum_2048", "h2o_global_2048", "random_reservoir_2048",
-                                    "random_2048", "prefix_sliding_2048"])
-def test_boundary_large_segments_vs_oracle(policy):
-    """Two rows at page size 1, two successive boundaries with 5,000-8,000
-    columns per (row, layer, head), against the oracle."""
-    rng = np.random.default_rng(41)
-    rows, L, G, page = 2, 2, 8, 1
-    n0, n1 = 8000, 10048
-    units, width, pos_cap = rows * n1 + 1, n1 + 64, 4096
-    kl = [sc.bf16_bits(rng.standard_normal((units, G, page, sc.D), dtype=np.float32)) for _ in range(L)]
-    vl = [sc.bf16_bits(rng.standard_normal((units, G, page, sc.D), dtype=np.float32)) for _ in range(L)]
+def _two_boundaries(policy, rows, L, n0, n1, budgets, seed, hazard_bytes=256 << 20):
+    """Two successive page-size-1 boundaries of `rows` rows (n0 then n1
+    positions), the GPU against the oracle after each: results, freed units,
+    tables, positions, scores and the K/V pools bit for bit."""
+    rng = np.random.default_rng(seed)
+    G, page = 8, 1
+    units, width, pos_cap = rows * n1 + 1, n1 + 64, max(budgets)
+    # the boundary moves K/V bytes without reading them: any 16-bit patterns do
+    kl = [rng.integers(0, 1 << 16, (units, G, page, sc.D), dtype=np.uint16) for _ in range(L)]
+    vl = [rng.integers(0, 1 << 16, (units, G, page, sc.D), dtype=np.uint16) for _ in range(L)]
     state = {"table": np.zeros((rows, width), np.int32), "r2u": np.zeros((rows, width), np.int32),
              "frontier": np.zeros(rows, np.int32), "count": np.zeros(rows, np.int32),
              "pos": np.zeros((rows, L, G, pos_cap), np.int32),
@@ -127,7 +126,6 @@ def test_boundary_large_segments_vs_oracle(policy):
     kern = K()
     kp, vp = kern.layer_pointers(gk, DEV), kern.layer_pointers(gv, DEV)
     marks = torch.zeros(units, dtype=torch.int32, device=DEV)
-    budgets = [3000, 2000]
     for step, n in enumerate((n0, n1)):
         params = []
         for r in range(rows):
@@ -145,7 +143,7 @@ def test_boundary_large_segments_vs_oracle(policy):
                                     kp, vp, G, page, torch.arange(rows, dtype=torch.int32, device=DEV),
                                     kern.row_params(params, DEV), max_cols, n + 1, True, marks=marks,
                                     epoch=step + 1, uniforms=None if uni is None else dt(uni), err=err,
-                                    max_width=max(budgets))
+                                    max_width=max(budgets), hazard_bytes=hazard_bytes)
         torch.cuda.synchronize()
         assert int(err.item()) == 0, hex(int(err.item()))
         np.testing.assert_array_equal(res_g.cpu().numpy(), res_c)
@@ -156,3 +154,23 @@ def test_boundary_large_segments_vs_oracle(policy):
         for l in range(L):
             np.testing.assert_array_equal(gk[l].view(torch.int16).cpu().numpy(), kl[l].view(np.int16))
             np.testing.assert_array_equal(gv[l].view(torch.int16).cpu().numpy(), vl[l].view(np.int16))
+
+
+@pytest.mark.parametrize("policy", ["head_sum_2048", "h2o_global_2048", "random_reservoir_2048",
+                                    "random_2048", "prefix_sliding_2048"])
+def test_boundary_large_segments_vs_oracle(policy):
+    """Two rows at page size 1, two successive boundaries with 5,000-8,000
+    columns per (row, layer, head), against the oracle."""
+    _two_boundaries(policy, rows=2, L=2, n0=8000, n1=10048, budgets=[3000, 2000], seed=41)
+
+
+@pytest.mark.parametrize("policy", ["head_sum_2048", "h2o_global_2048", "random_2048"])
+def test_boundary_page1_full_width_vs_oracle(policy):
+    """Four rows at page size 1 with 65,536 columns per (row, head) -- the
+    largest segment of the shared-memory path -- and budgets of 8K-40K
+    tokens, so the candidate ranking, the packing and the compaction all run
+    over many tiles and chunks; then a second boundary over the kept columns
+    plus 9,000 new ones, with the hazard workspace forcing one row per copy
+    launch.  The GPU against the oracle, bit for bit."""
+    _two_boundaries(policy, rows=4, L=1, n0=65536, n1=74536, budgets=[40000, 8192, 20000, 32768], seed=43,
+                    hazard_bytes=1)
