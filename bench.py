@@ -485,21 +485,22 @@ def select_token_microbench(world, rank, device, reps=3, rows=32):
     return out
 
 
-def evict_microbench(world, rank, device, reps=3, rows=32):
+def evict_microbench(world, rank, device, reps=3, rows=32, page=PAGE):
     """one eviction step (select + compaction) over 32 rows x
-    this rank's KV heads x 4096 pages (65,536-token contexts), fp32 scores
-    lognormal(0, 2), P = R = B/4, for H2O global / H2O per-head / random at
-    budgets 2K..32K tokens.  Device time of ce_boundary and of ce_choose alone
-    (CUDA events, state restored outside the timed window), moved pages and
+    this rank's KV heads x 65,536-token contexts (4096 pages of 16 tokens, or
+    with page=1 the reference's own token slots), fp32 scores lognormal(0, 2),
+    P = R = B/4, for H2O global / H2O per-head / random at budgets 2K..32K
+    tokens.  Device time of ce_boundary and (pages of 16) of ce_choose alone
+    (CUDA events, state restored outside the timed window), moved units and
     algorithmic GB/s."""
     import torch
     from cache_eviction_b200 import kernels, tp
     G, _, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
-    R, N = rows, 4096
+    R, N = rows, 65536 // page
     units = R * N + 1
     gen = torch.Generator(device=device).manual_seed(55)
-    kp = torch.randn((units, G, PAGE, D), generator=gen, device=device).to(torch.bfloat16)
-    vp = torch.randn((units, G, PAGE, D), generator=gen, device=device).to(torch.bfloat16)
+    kp = torch.randn((units, G, page, D), generator=gen, device=device).to(torch.bfloat16)
+    vp = torch.randn((units, G, page, D), generator=gen, device=device).to(torch.bfloat16)
     kptr, vptr = kernels.layer_pointers([kp], device), kernels.layer_pointers([vp], device)
     scores0 = torch.randn((1, G, units), generator=gen, device=device).mul_(2.0).exp_()
     perm = torch.randperm(units - 1, generator=gen, device=device).int() + 1
@@ -512,7 +513,7 @@ def evict_microbench(world, rank, device, reps=3, rows=32):
     epoch = 0
     for pol in ("h2o_global_2048", "head_sum_2048", "random_2048"):
         for budget in BUDGETS:
-            b = budget // PAGE
+            b = budget // page
             params = [dict(n=N, budget=b, prefix=b // 4, recent=b // 4, cursor=None, policy=pol, seed=i)
                       for i in range(R)]
             prm = kernels.row_params(params, device)
@@ -531,34 +532,37 @@ def evict_microbench(world, rank, device, reps=3, rows=32):
                 # events bracket device time only.
                 torch.cuda._sleep(SLEEP_CYCLES)
                 a.record()
-                res, _ = kernels.boundary(table, r2u, frontier, count, pos, scores, kptr, vptr, G, PAGE,
+                res, _ = kernels.boundary(table, r2u, frontier, count, pos, scores, kptr, vptr, G, page,
                                           rows, prm, N, N + 1, True, marks=marks, epoch=epoch,
                                           uniforms=uni if pol == "random_2048" else None,
                                           head_offset=off, hazard_bytes=1 << 30, max_width=b)
                 e.record()
-                sc = scores0[0].gather(1, r2u0.view(1, -1).expand(G, -1).long()).view(G, R, N)
-                sc = sc.permute(1, 0, 2).contiguous()
-                a2 = torch.cuda.Event(enable_timing=True)
-                e2 = torch.cuda.Event(enable_timing=True)
-                torch.cuda._sleep(SLEEP_CYCLES)
-                a2.record()
-                kernels.choose(pos_fresh, uni.view(R, G, N) if pol == "random_2048" else sc, prm, 1, G,
-                               max_n=N + 1, kept_stride=b)
-                e2.record()
+                if page == PAGE:
+                    sc = scores0[0].gather(1, r2u0.view(1, -1).expand(G, -1).long()).view(G, R, N)
+                    sc = sc.permute(1, 0, 2).contiguous()
+                    a2 = torch.cuda.Event(enable_timing=True)
+                    e2 = torch.cuda.Event(enable_timing=True)
+                    torch.cuda._sleep(SLEEP_CYCLES)
+                    a2.record()
+                    kernels.choose(pos_fresh, uni.view(R, G, N) if pol == "random_2048" else sc, prm, 1, G,
+                                   max_n=N + 1, kept_stride=b)
+                    e2.record()
                 torch.cuda.synchronize()
                 if it:
                     times.append(a.elapsed_time(e) * 1e3)
-                    sel_times.append(a2.elapsed_time(e2) * 1e3)
+                    if page == PAGE:
+                        sel_times.append(a2.elapsed_time(e2) * 1e3)
             status = res[:, 0].cpu()
             assert bool((status == 0).all()), status
             p_u, mid = b // 4, b - 2 * (b // 4)
             mpos = pos[:, 0, :, p_u:p_u + mid]
             moved = int((mpos != (torch.arange(mid, device=device, dtype=torch.int32) + p_u)).sum())
             nbytes = R * G * N * 4 + (R * G * N * 8 if pol == "random_2048" else 0) + R * G * b * 4 \
-                + moved * (2 * 2 * PAGE * D * 2 + 8)
+                + moved * (2 * 2 * page * D * 2 + 8)
             us = statistics.median(times)
-            out[f"{pol}_{budget}"] = {"evict_step_us": us, "select_us": statistics.median(sel_times),
-                                      "moved_pages": moved, "gbs": nbytes / (us * 1e-6) / 1e9}
+            out[f"{pol}_{budget}"] = {"evict_step_us": us,
+                                      "select_us": statistics.median(sel_times) if sel_times else None,
+                                      "moved_units": moved, "gbs": nbytes / (us * 1e-6) / 1e9}
     del kp, vp
     torch.cuda.empty_cache()
     return out
@@ -578,7 +582,7 @@ def main():
                     help="skip the config-5 eviction-step leg")
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (small cases for profiling)")
-    ap.add_argument("--legs", default="decode,e2e,noscore,prefill4,evict5,select1",
+    ap.add_argument("--legs", default="decode,e2e,noscore,prefill4,evict5,select1,evict1",
                     help="legs to run; without 'decode' only the listed microbenchmarks run "
                          "and one JSON line with their results is printed (profiling)")
     ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
@@ -611,6 +615,8 @@ def main():
             res["evict_config5"] = evict_microbench(world, rank, device, rows=args.evict_rows)
         if "select1" in legs:
             res["select_token_config5"] = select_token_microbench(world, rank, device, rows=args.evict_rows)
+        if "evict1" in legs:
+            res["evict_token_config5"] = evict_microbench(world, rank, device, rows=args.evict_rows, page=1)
         if rank == 0:
             print(json.dumps({"profile_legs": res}), flush=True)
         if world > 1:
@@ -718,6 +724,12 @@ def main():
     select1 = None
     if not args.no_evict_bench and "select1" in legs:
         select1 = select_token_microbench(world, rank, device, rows=args.evict_rows)
+    evict1 = None
+    if not args.no_evict_bench and "evict1" in legs:
+        evict1 = evict_microbench(world, rank, device, rows=args.evict_rows, page=1)
+        if world > 1:
+            for k in evict1:
+                evict1[k]["evict_step_us"] = max_over_ranks(evict1[k]["evict_step_us"])
     peak, peak_kind = measured_peak_hbm()
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -750,6 +762,7 @@ def main():
                                            "(full-cache decode at the same resident KV)"},
         "evict_config5": evict5,
         "select_token_config5": select1,
+        "evict_token_config5": evict1,
         "prefill_config4": prefill4,
     }
     if rank == 0 and world == 1 and args.cpu_seconds > 0:

@@ -1105,6 +1105,7 @@ struct BParams {
   int32_t* src_unit;
   int32_t* new_pos;
   float* score_scr;
+  uint8_t* hflag;      // [R*L*G*max_cols] middle survivor whose source is staged (bgather)
   int32_t* row_info;   // [R*RI]: N, nprot, W, after, true_u, nleft, count, status, swa_bad, npacked
   int32_t* cand_rank;  // [R*max_cols]
   int32_t* new_table;  // [R*max_cols]
@@ -1977,22 +1978,24 @@ __device__ __forceinline__ void copy_pair(uint8_t* dk, uint8_t* dv, const uint8_
 
 // Copy the K and V slices (bytes each, under 2 KB) of every item whose bit is
 // set in todo (warp-uniform, from a ballot) with the whole warp at once: the
-// (item, 16-byte vector) pairs are spread over the lanes, four per lane in
-// flight, so a chunk costs about one load latency instead of one per item.
-// addr(k, sk, sv, dk, dv) gives item k's addresses; it shuffles from lane k,
-// so every lane calls it, for items that are skipped too.
+// (item, 16-byte vector) pairs are spread over the lanes, two per lane in
+// flight (few registers, so that many warps fit an SM), so a chunk costs
+// about one load latency instead of one per item.  addr(k, sk, sv, dk, dv)
+// gives item k's addresses; it shuffles from lane k, so every lane calls it,
+// for items that are skipped too.
 template <class AddrF>
 __device__ __forceinline__ void copy_items(unsigned todo, int bytes, int lane, AddrF addr) {
   if (!todo) return;
+  constexpr int DEPTH = 2;
   const int vecs = bytes >> 4;
   const int total = (32 - __clz(static_cast<int>(todo))) * vecs;
-  for (int f0 = 0; f0 < total; f0 += 4 * 32) {
-    uint4 a[4], b[4];
-    uint8_t* dk[4];
-    uint8_t* dv[4];
-    bool ok[4];
+  for (int f0 = 0; f0 < total; f0 += DEPTH * 32) {
+    uint4 a[DEPTH], b[DEPTH];
+    uint8_t* dk[DEPTH];
+    uint8_t* dv[DEPTH];
+    bool ok[DEPTH];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < DEPTH; ++u) {
       const int f = f0 + u * 32 + lane;
       const int k = min(f / vecs, 31);
       const uint8_t* sk;
@@ -2008,7 +2011,7 @@ __device__ __forceinline__ void copy_items(unsigned todo, int bytes, int lane, A
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < DEPTH; ++u) {
       if (ok[u]) {
         *reinterpret_cast<uint4*>(dk[u]) = a[u];
         *reinterpret_cast<uint4*>(dv[u]) = b[u];
@@ -2023,7 +2026,10 @@ __device__ __forceinline__ uint32_t launch_chunks(const BParams& p, int nr, int 
 
 // Stage every hazard source of the group's layers (a unit that some other
 // item of its row overwrites) in the scratch buffer.
-__global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int r0, int nr, int l0, int nl) {
+// SMALL: slices under 2 KB (copy_items); otherwise one page pair at a time.
+template <bool SMALL>
+__global__ void __launch_bounds__(256, SMALL ? 4 : 2) bgather_kernel(const BParams p, int r0, int nr, int l0,
+                                                                     int nl) {
   const int lane = threadIdx.x & 31;
   const uint32_t nchunks = launch_chunks(p, nr, nl);
   const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
@@ -2039,9 +2045,10 @@ __global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int r0, i
         flag_error(p.err, CE_EW_INDEX);
         hz = false;
       }
+      p.hflag[c.base + c.j] = hz;
     }
     const unsigned hmask = __ballot_sync(0xffffffffu, hz);
-    if (bytes < 2048) {
+    if constexpr (SMALL) {
       // c.l, c.g and c.item - lane are the same on every lane of the chunk
       const int64_t item0 = c.item - lane;
       copy_items(hmask, bytes, lane,
@@ -2067,7 +2074,9 @@ __global__ void __launch_bounds__(256) bgather_kernel(const BParams p, int r0, i
 
 // Write every middle survivor of the group's layers to its target unit (from
 // the scratch copy when its source is a hazard) and move its score.
-__global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int r0, int nr, int l0, int nl) {
+template <bool SMALL>
+__global__ void __launch_bounds__(256, SMALL ? 4 : 2) bscatter_kernel(const BParams p, int r0, int nr, int l0,
+                                                                      int nl) {
   const int lane = threadIdx.x & 31;
   const uint32_t nchunks = launch_chunks(p, nr, nl);
   const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
@@ -2079,16 +2088,18 @@ __global__ void __launch_bounds__(256) bscatter_kernel(const BParams p, int r0, 
     if (c.valid) {
       dst = p.new_table[static_cast<int64_t>(c.i) * p.max_cols + c.nprot + c.j];
       src = p.src_unit[c.base + c.j];
+      const float sc = p.score_scr[c.base + c.j];
+      const bool staged = p.hflag[c.base + c.j] != 0;
       if (dst < 0 || dst >= p.pool_units || src < 0 || src >= p.pool_units) {
         flag_error(p.err, CE_EW_INDEX);
       } else {
-        p.scores[c.l * p.sls + c.g * p.shs + dst] = p.score_scr[c.base + c.j];
+        p.scores[c.l * p.sls + c.g * p.shs + dst] = sc;
         move = src != dst;
-        hz = move && chunk_hazard(p, c);
+        hz = move && staged;
       }
     }
     const unsigned mmask = __ballot_sync(0xffffffffu, move);
-    if (bytes < 2048) {
+    if constexpr (SMALL) {
       const int64_t item0 = c.item - lane;
       copy_items(mmask, bytes, lane,
                  [&](int k, const uint8_t*& sk, const uint8_t*& sv, uint8_t*& dk, uint8_t*& dv) {
@@ -2240,7 +2251,7 @@ namespace {
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct BLayout {
-  size_t kv, pv, seg, mid, src, npos, ssc, info, crank, ntab, pcol, pack, hsum, hazard, total;
+  size_t kv, pv, seg, mid, src, npos, ssc, hflag, info, crank, ntab, pcol, pack, hsum, hazard, total;
 };
 
 BLayout boundary_layout(int R, int L, int G, int max_cols, int64_t hazard_bytes) {
@@ -2254,6 +2265,7 @@ BLayout boundary_layout(int R, int L, int G, int max_cols, int64_t hazard_bytes)
   b.src = o; o += a256(cells * 4);
   b.npos = o; o += a256(cells * 4);
   b.ssc = o; o += a256(cells * 4);
+  b.hflag = o; o += a256(cells);
   b.info = o; o += a256(static_cast<size_t>(R) * RI * 4);
   b.crank = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
   b.ntab = o; o += a256(static_cast<size_t>(R) * max_cols * 4);
@@ -2471,6 +2483,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   p.src_unit = reinterpret_cast<int32_t*>(ws + Lo.src);
   p.new_pos = reinterpret_cast<int32_t*>(ws + Lo.npos);
   p.score_scr = reinterpret_cast<float*>(ws + Lo.ssc);
+  p.hflag = ws + Lo.hflag;
   p.row_info = reinterpret_cast<int32_t*>(ws + Lo.info);
   p.cand_rank = reinterpret_cast<int32_t*>(ws + Lo.crank);
   p.new_table = reinterpret_cast<int32_t*>(ws + Lo.ntab);
@@ -2521,6 +2534,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   const int group = static_cast<int>(
       std::min<int64_t>(layers, std::max<int64_t>(1, hz / (static_cast<int64_t>(rows_per) * row_layer))));
   const int nsm = host::sm_count();
+  const bool small = chunk_items(page_size) == CH_SMALL;   // matches the kernels' copy path
   for (int r0 = 0; r0 < num_rows; r0 += rows_per) {
     const int nr = std::min(rows_per, num_rows - r0);
     for (int l0 = 0; l0 < layers; l0 += group) {
@@ -2530,9 +2544,17 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
       if (chunks > INT32_MAX) return host::fail(CE_ERR_UNSUPPORTED, "ce_boundary: too many rows x layers x heads");
       const int64_t want = (chunks * 32 + 255) / 256;
       const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 8LL * nsm)));
-      bgather_kernel<<<blocks, 256, 0, st>>>(p, r0, nr, l0, nl);
+      if (small) {
+        bgather_kernel<true><<<blocks, 256, 0, st>>>(p, r0, nr, l0, nl);
+      } else {
+        bgather_kernel<false><<<blocks, 256, 0, st>>>(p, r0, nr, l0, nl);
+      }
       if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bgather_kernel");
-      bscatter_kernel<<<blocks, 256, 0, st>>>(p, r0, nr, l0, nl);
+      if (small) {
+        bscatter_kernel<true><<<blocks, 256, 0, st>>>(p, r0, nr, l0, nl);
+      } else {
+        bscatter_kernel<false><<<blocks, 256, 0, st>>>(p, r0, nr, l0, nl);
+      }
       if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bscatter_kernel");
     }
   }
