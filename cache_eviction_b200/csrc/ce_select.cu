@@ -2128,13 +2128,12 @@ __global__ void __launch_bounds__(256, SMALL ? 4 : 2) bscatter_kernel(const BPar
   }
 }
 
-// Grid (rows, 1 + L * G, Z).  Block (i, 0, 0): table, count, frontier and
-// the req_to_unit packing of row i.  Block (i, 1 + s, 0): the new positions of
-// segment s = (layer, head) -- its protected slots gathered here, its middle
-// survivors from the selection.  Blocks (i, 1 + s, z), for a live boundary
-// that passed the sliding-window guard: zero that (layer, head)'s scores at
-// the z-th of Z chunks of the row's freed units (scattered stores, spread
-// over Z blocks so that more SMs issue them).
+// Grid (rows, 1 + L * G).  Block (i, 0): table, count, frontier, the
+// req_to_unit packing of row i and, for a live boundary that passed the
+// sliding-window guard, the tag -epoch in marks[] on every freed unit of the
+// row (bzero_kernel then zeroes their scores).  Block (i, 1 + s): the new
+// positions of segment s = (layer, head) -- its protected slots gathered
+// here, its middle survivors from the selection.
 __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
   const int i = blockIdx.x;
   const int32_t* info = p.row_info + i * RI;
@@ -2151,37 +2150,24 @@ __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
   const int LG = p.L * p.G;
   const int32_t* ntab = p.new_table + static_cast<int64_t>(i) * p.max_cols;
   const int32_t* left = p.freed + i * p.freed_stride;
-  const int z = blockIdx.z;
   if (blockIdx.y > 0) {
     const int lg = static_cast<int>(blockIdx.y) - 1;
     if (lg >= LG) return;
-    if (z == 0) {
-      int32_t* src = p.new_pos + (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
-      int32_t* dst = p.pos + r.row * p.prs + static_cast<int64_t>(lg) * p.pos_cap;
-      // Protected slots: this head's positions at the (0,0) head's protected
-      // columns, in (0,0) position order (runtime:442-443, 469).  Every read
-      // of the old positions ends before the copy below overwrites them.
-      const int32_t* pcol = p.prot_col + static_cast<int64_t>(i) * p.max_cols;
-      batched<8>(
-          info[1], [&](int k) { return pcol[k]; }, [&](int, int c) { return col_pos(p, r, lg, c); },
-          [&](int k, int, int v) { src[k] = v; });
-      __syncthreads();
-      batched<8>(
-          after, [&](int k) { return src[k]; }, [](int, int) { return 0; },
-          [&](int k, int v, int) { dst[k] = v; });
-    }
-    if (!p.live || bad) return;
-    const int per = (nleft + gridDim.z - 1) / gridDim.z;
-    const int k0 = min(nleft, z * per), k1 = min(nleft, k0 + per);
-    float* sc = p.scores + (lg / p.G) * p.sls + (lg % p.G) * p.shs;
+    int32_t* src = p.new_pos + (static_cast<int64_t>(i) * LG + lg) * p.max_cols;
+    int32_t* dst = p.pos + r.row * p.prs + static_cast<int64_t>(lg) * p.pos_cap;
+    // Protected slots: this head's positions at the (0,0) head's protected
+    // columns, in (0,0) position order (runtime:442-443, 469).  Every read
+    // of the old positions ends before the copy below overwrites them.
+    const int32_t* pcol = p.prot_col + static_cast<int64_t>(i) * p.max_cols;
     batched<8>(
-        k1 - k0, [&](int k) { return left[k0 + k]; }, [](int, int) { return 0; },
-        [&](int, int u, int) {
-          if (u >= 0 && u < p.pool_units) sc[u] = 0.f;
-        });
+        info[1], [&](int k) { return pcol[k]; }, [&](int, int c) { return col_pos(p, r, lg, c); },
+        [&](int k, int, int v) { src[k] = v; });
+    __syncthreads();
+    batched<8>(
+        after, [&](int k) { return src[k]; }, [](int, int) { return 0; },
+        [&](int k, int v, int) { dst[k] = v; });
     return;
   }
-  if (z != 0) return;
   batched<8>(
       after, [&](int k) { return ntab[k]; }, [](int, int) { return 0; },
       [&](int k, int u, int) { p.table[r.row * p.ts + k] = u; });
@@ -2202,6 +2188,14 @@ __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
     return;
   }
   if (threadIdx.x == 0) res[3] = nleft;
+  // Freed units: their scores are zeroed at every (layer, head) (runtime:481)
+  // by bzero_kernel, which finds them by this tag.  A freed unit is never a
+  // real slot of [true_u, n) (those are protected), so the tags do not meet.
+  batched<8>(
+      nleft, [&](int k) { return left[k]; }, [](int, int) { return 0; },
+      [&](int, int u, int) {
+        if (u >= 0 && u < p.pool_units) p.marks[u] = -p.epoch;
+      });
   // The packed prefix the row block listed (runtime:484-491), then zeros up to true_u.
   const int npacked = info[9];
   if (npacked > true_u) {
@@ -2217,6 +2211,18 @@ __global__ void __launch_bounds__(T) bfinish_kernel(const BParams p) {
       npacked, [&](int k) { return plist[k]; }, [](int, int) { return 0; },
       [&](int k, int u, int) { rrow[k] = u; });
   for (int x = npacked + threadIdx.x; x < min(true_u, p.r2u_width); x += T) rrow[x] = 0;
+}
+
+// Zero the scores of every unit bfinish_kernel tagged as freed, at every
+// (layer, head): one thread per pool unit, so each warp's stores cover 32
+// consecutive units of one (layer, head) row -- coalesced, where zeroing
+// from the rows' freed lists would scatter one 4-byte store per (unit,
+// layer, head).
+__global__ void bzero_kernel(const BParams p) {
+  const int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (u >= p.pool_units || p.marks[u] != -p.epoch) return;
+  for (int l = 0; l < p.L; ++l)
+    for (int g = 0; g < p.G; ++g) p.scores[l * p.sls + g * p.shs + u] = 0.f;
 }
 
 __global__ void gather_scores_kernel(const BParams p, float* out) {
@@ -2447,6 +2453,7 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
       !rows || !params || !result || !workspace)
     return host::fail(CE_ERR_ARG, "null pointer");
   if (live && (!marks || !freed_units)) return host::fail(CE_ERR_ARG, "live needs marks and freed_units");
+  if (live && epoch <= 0) return host::fail(CE_ERR_ARG, "live needs epoch >= 1");
   if (uniforms && uniform_dtype != CE_DTYPE_F32 && uniform_dtype != CE_DTYPE_F64)
     return host::fail(CE_ERR_ARG, "uniform dtype must be f32 or f64");
   const int nw = (max_n + 31) / 32;
@@ -2558,14 +2565,12 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
       if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bscatter_kernel");
     }
   }
-  // Score-zeroing chunks per (row, layer, head): enough blocks for about
-  // four per SM, each chunk at least 4,096 freed units.
-  const int zc = static_cast<int>(std::max<int64_t>(
-      1, std::min<int64_t>((4LL * nsm + int64_t(num_rows) * layers * kv_heads - 1) /
-                               (int64_t(num_rows) * layers * kv_heads),
-                           (max_cols + 4095) / 4096)));
-  bfinish_kernel<<<dim3(num_rows, 1 + layers * kv_heads, zc), T, 0, st>>>(p);
+  bfinish_kernel<<<dim3(num_rows, 1 + layers * kv_heads), T, 0, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bfinish_kernel");
+  if (live && pool_units > 0) {
+    bzero_kernel<<<static_cast<unsigned>((pool_units + 255) / 256), 256, 0, st>>>(p);
+    if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("bzero_kernel");
+  }
   return CE_OK;
 }
 

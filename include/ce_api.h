@@ -320,7 +320,8 @@ int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_cols,
  * units in candidate order for the caller's allocator (free_full).
  *   k_layers/v_layers  device arrays [layers] of pool base addresses (uint64)
  *   marks   [pool_units] int32 scratch owned by the caller (zero-initialised
- *           once); epoch must grow by one per call
+ *           once); epoch >= 1 must grow by one per call (the call tags real
+ *           slots with epoch and freed units with -epoch)
  *   swa_mapping [pool_units] int64 or NULL (reference
  *           allocator.full_to_swa_index_mapping, runtime:477-479)
  *   uniforms [num_rows, layers, heads, max_cols] f32/f64 for random rows

@@ -57,3 +57,30 @@ def test_workspace_queries_are_host_only():
 def test_row_params_layout_matches_header():
     from cache_eviction_b200 import capi, kernels
     assert C.sizeof(capi.RowParams) == 32 and kernels.ROW_DTYPE.itemsize == 32
+
+
+def test_live_boundary_needs_a_positive_epoch():
+    """ce_boundary tags real slots with epoch and freed units with -epoch in
+    the caller's zero-initialised marks, so a live call with epoch 0 is
+    refused on the host, before any device work (the pointers below are never
+    dereferenced)."""
+    from cache_eviction_b200 import capi
+    lib = capi.load()
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "ce_api.h").read_text(), flags=re.S)
+    params = re.search(r"\bce_boundary\s*\(([^)]*)\)\s*;", text).group(1).split(",")
+    names = [re.findall(r"\w+", p)[-1] for p in params]
+    ints = {"table_width": 16, "r2u_width": 16, "pos_cap": 16, "pool_units": 64, "layers": 1,
+            "kv_heads": 8, "head_dim": 64, "page_size": 1, "num_rows": 1, "live": 1, "max_cols": 16,
+            "max_n": 16, "epoch": 0}
+    args = []
+    for name, p in zip(names, params):
+        if "*" in p:
+            null = name in ("swa_mapping", "uniforms", "global_scores", "record_delta", "record_counts",
+                            "err", "stream")
+            args.append(None if null else C.c_void_p(4096))
+        else:
+            args.append(ints.get(name, 16 if "stride" in name else 0))
+    args[names.index("workspace_bytes")] = 1 << 40
+    args[names.index("hazard_bytes")] = 1 << 20
+    assert lib.ce_boundary(*args) == capi.CE_ERR_ARG
+    assert b"epoch" in lib.ce_last_error()
