@@ -103,10 +103,11 @@ def test_choose_large_vs_oracle(policy, skind, compacted, N):
                                           err_msg=f"row {r} budget {budget}")
 
 
-def _two_boundaries(policy, rows, L, n0, n1, budgets, seed, hazard_bytes=256 << 20):
+def _two_boundaries(policy, rows, L, n0, n1, budgets, seed, hazard_bytes=256 << 20, record=False):
     """Two successive page-size-1 boundaries of `rows` rows (n0 then n1
     positions), the GPU against the oracle after each: results, freed units,
-    tables, positions, scores and the K/V pools bit for bit."""
+    tables, positions, scores and the K/V pools bit for bit, and with record
+    the retention record of every evicted row."""
     rng = np.random.default_rng(seed)
     G, page = 8, 1
     units, width, pos_cap = rows * n1 + 1, n1 + 64, max(budgets)
@@ -136,6 +137,11 @@ def _two_boundaries(policy, rows, L, n0, n1, budgets, seed, hazard_bytes=256 << 
         max_cols = max(int(state["count"][r]) + n - int(state["frontier"][r]) for r in range(rows))
         assert max_cols > 4096
         uni = rng.random((rows, L, G, max_cols)) if policy == "random_2048" else None
+        before = {k: state[k].copy() for k in ("pos", "count", "frontier")}
+        rec = None
+        if record:
+            rec = (torch.full((rows * L * G, max_cols), -1, dtype=torch.int32, device=DEV),
+                   torch.full((rows * L * G,), -1, dtype=torch.int32, device=DEV))
         res_c, fr_c = oracle.boundary(state, kl, vl, list(range(rows)), oracle.row_params(params),
                                       max_cols, live=True, uniforms=uni)
         err = kern.error_word(DEV)
@@ -143,7 +149,7 @@ def _two_boundaries(policy, rows, L, n0, n1, budgets, seed, hazard_bytes=256 << 
                                     kp, vp, G, page, torch.arange(rows, dtype=torch.int32, device=DEV),
                                     kern.row_params(params, DEV), max_cols, n + 1, True, marks=marks,
                                     epoch=step + 1, uniforms=None if uni is None else dt(uni), err=err,
-                                    max_width=max(budgets), hazard_bytes=hazard_bytes)
+                                    max_width=max(budgets), hazard_bytes=hazard_bytes, record=rec)
         torch.cuda.synchronize()
         assert int(err.item()) == 0, hex(int(err.item()))
         np.testing.assert_array_equal(res_g.cpu().numpy(), res_c)
@@ -154,6 +160,18 @@ def _two_boundaries(policy, rows, L, n0, n1, budgets, seed, hazard_bytes=256 << 
         for l in range(L):
             np.testing.assert_array_equal(gk[l].view(torch.int16).cpu().numpy(), kl[l].view(np.int16))
             np.testing.assert_array_equal(gv[l].view(torch.int16).cpu().numpy(), vl[l].view(np.int16))
+        if record:
+            delta, counts = rec[0].cpu().numpy().view(np.uint32), rec[1].cpu().numpy()
+            for r in range(rows):
+                segs = range(r * L * G, (r + 1) * L * G)
+                if res_c[r, 0] != 0:
+                    assert not counts[r * L * G:(r + 1) * L * G].any()
+                    continue
+                dw, cw = oracle.retention_record(before["pos"][r], int(before["count"][r]),
+                                                 int(before["frontier"][r]), n, state["pos"][r],
+                                                 int(state["count"][r]))
+                np.testing.assert_array_equal(counts[r * L * G:(r + 1) * L * G], cw)
+                np.testing.assert_array_equal(np.concatenate([delta[q, :counts[q]] for q in segs]), dw)
 
 
 @pytest.mark.parametrize("policy", ["head_sum_2048", "h2o_global_2048", "random_reservoir_2048",
@@ -171,6 +189,7 @@ def test_boundary_page1_full_width_vs_oracle(policy):
     tokens, so the candidate ranking, the packing and the compaction all run
     over many tiles and chunks; then a second boundary over the kept columns
     plus 9,000 new ones, with the hazard workspace forcing one row per copy
-    launch.  The GPU against the oracle, bit for bit."""
+    launch.  The GPU against the oracle, bit for bit (and the retention
+    record for head_sum)."""
     _two_boundaries(policy, rows=4, L=1, n0=65536, n1=74536, budgets=[40000, 8192, 20000, 32768], seed=43,
-                    hazard_bytes=1)
+                    hazard_bytes=1, record=policy == "head_sum_2048")
