@@ -250,7 +250,8 @@ def build_engine(specs, steps_total, world, rank, group, device):
     G, H, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
     units = pool_units_needed(specs, steps_total)
     eng = RaggedDecodeEngine(layers=LAYERS, q_heads=H, kv_heads=G, page_size=PAGE, pool_units=units,
-                             max_rows=len(specs), r2u_width=-(-(65536 + steps_total + 4096) // PAGE),
+                             max_rows=len(specs),
+                             r2u_width=-(-(max([65536] + [sp["ctx"] for sp in specs]) + steps_total + 4096) // PAGE),
                              pos_cap=32768 // PAGE, device=device, head_offset=off,
                              global_kv_heads=G_TOTAL, process_group=group)
     synth_state(eng, specs, steps_total, seed=2026 + 17)
@@ -349,6 +350,80 @@ def run_no_score(args, specs, steps_total, world, rank, group, device, q, out, s
     del eng
     torch.cuda.empty_cache()
     return B * args.steps / (ms * 1e-3)
+
+
+def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, steps=2048, warmup=8):
+    """BASELINE config 4's decode phase: one sequence after an 80,000-token
+    prompt, per-head H2O (head_sum) with 512 prefix + 4,096 recent + 24,064
+    scored tokens (28,672 resident after each boundary), 12 full layers of
+    this rank's heads (attention + H2O score, no output projection), `steps`
+    decode steps including the boundary at 81,920 tokens.  Each step without a
+    boundary replays one CUDA graph (position advance, CSR fill, the 12 fused
+    decode layers); the boundary step runs eagerly through engine.step.  The
+    same pass with scoring off at the same resident KV gives the full-cache
+    rate it is compared against.  Algorithmic bytes per step: K + V of every
+    resident token (2,048 B at 8 KV heads) + Q/O + the page-score
+    read-modify-write, per layer."""
+    import torch
+    from cache_eviction_b200 import capi, tp
+    from cache_eviction_b200.policy import EvictionConfig
+    G, H, _ = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    ctx, budget, prefix, recent = 80000, 28672, 512, 4096
+    cfg = EvictionConfig("head_sum_2048", budget, prefix, recent, seed=4)
+    specs = [dict(ctx=ctx, cfg=cfg, policy="h2o_per_head", budget=budget)]
+    scale = D ** -0.5
+    gen = torch.Generator(device=device).manual_seed(4321 + rank)
+    q = torch.randn((LAYERS, 1, H, D), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty((LAYERS, 1, H, D), dtype=torch.bfloat16, device=device)
+    sinks = [torch.randn(H, generator=gen, device=device) for _ in range(LAYERS)]
+    res = {}
+    for scored in (True, False):
+        eng = build_engine(specs, warmup + steps, world, rank, group, device)
+        if not scored:
+            eng.mode.fill_(capi.CE_MODE_NONE)
+        # the CSR buffer the graph holds stays large enough; the warm-up steps
+        # then size the decode workspace for it, so the capture allocates nothing
+        eng._ensure_capacity(warmup + steps + 16)
+        for _ in range(warmup):
+            eng.step(q, out, sinks, scale)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            eng.seq_lens_dev.add_(1)
+            eng.fill()
+            for l in range(LAYERS):
+                eng.decode_layer(l, q[l], out[l], sinks[l], scale)
+        torch.cuda.synchronize()
+        row = eng.rows[eng.active[0]]
+        resident = []
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            if eng.due():
+                eng.step(q, out, sinks, scale)
+            else:
+                row.n += 1       # the host side of engine.advance
+                graph.replay()
+            resident.append(eng.resident_tokens(eng.active[0]))
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(start.elapsed_time(end))
+        eng.check_errors()
+        bounds = len(eng.rows[eng.active[0]].events)
+        del graph, eng
+        torch.cuda.empty_cache()
+        tok = statistics.mean(resident)
+        nbytes = LAYERS * (tok * G * D * 2 * 2 + 2 * H * D * 2 + (-(-tok // PAGE)) * G * 8 * scored)
+        res["scored" if scored else "no_score"] = {
+            "tok_s": steps / (ms * 1e-3), "ms_per_step": ms / steps, "resident_tokens_mean": tok,
+            "gbs": nbytes / (ms / steps * 1e-3) / 1e9, "boundaries": bounds}
+    peak, kind = measured_peak_hbm()
+    res["scored_over_no_score"] = res["scored"]["tok_s"] / res["no_score"]["tok_s"]
+    res["hbm_frac_scored"] = res["scored"]["gbs"] / peak
+    res["peak_kind"] = kind
+    return res
 
 
 PREFILL_CHUNK = 2048
@@ -582,7 +657,7 @@ def main():
                     help="skip the config-5 eviction-step leg")
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (small cases for profiling)")
-    ap.add_argument("--legs", default="decode,e2e,noscore,prefill4,evict5,select1,evict1",
+    ap.add_argument("--legs", default="decode,e2e,noscore,decode4,prefill4,evict5,select1,evict1",
                     help="legs to run; without 'decode' only the listed microbenchmarks run "
                          "and one JSON line with their results is printed (profiling)")
     ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
@@ -609,6 +684,20 @@ def main():
     capi.load()
     if "decode" not in legs:
         res = {}
+
+        def barrier0():
+            if world > 1:
+                dist.barrier(device_ids=[device.index])
+
+        def max0(x: float) -> float:
+            if world == 1:
+                return x
+            t = torch.tensor([x], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        if "decode4" in legs:
+            res["decode_config4"] = decode4_microbench(world, rank, group, device, barrier0, max0)
         if "prefill4" in legs:
             res["prefill_config4"] = prefill_microbench(world, rank, device, prefixes=prefixes)
         if "evict5" in legs:
@@ -706,6 +795,9 @@ def main():
         e2e_value = run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
                             scale, after_layer, barrier, max_over_ranks, e2e_steps)
 
+    decode4 = None
+    if "decode4" in legs:
+        decode4 = decode4_microbench(world, rank, group, device, barrier, max_over_ranks)
     prefill4 = None
     if "prefill4" in legs:
         prefill4 = prefill_microbench(world, rank, device, cpu=(rank == 0 and args.cpu_seconds > 0),
@@ -763,6 +855,7 @@ def main():
         "evict_config5": evict5,
         "select_token_config5": select1,
         "evict_token_config5": evict1,
+        "decode_config4": decode4,
         "prefill_config4": prefill4,
     }
     if rank == 0 and world == 1 and args.cpu_seconds > 0:

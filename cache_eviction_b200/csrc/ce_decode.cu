@@ -676,18 +676,32 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams
     // once the normaliser is known (no second or third read of the records).
     const bool fits = nslots <= MAX_SLOTS;
     float m = -INFINITY, l = 0.f;
-    for (int i = lane; i < nslots; i += 32) {
-      float mk = -INFINITY, lk = 0.f;
-      if (live(i)) {
-        const float* st = rec_of(i) + REC_ROWS * D;
-        mk = st[vrow(i)];
-        lk = st[REC_ROWS + vrow(i)];
+    // Four slots of a lane per batch: their loads are issued together (a
+    // sequence spread over every CTA has ~150 slots per head).
+    constexpr int SB = 4;
+    for (int i0 = lane; i0 < nslots; i0 += 32 * SB) {
+      float mk[SB], lk[SB];
+#pragma unroll
+      for (int u = 0; u < SB; ++u) {
+        const int i = i0 + 32 * u;
+        mk[u] = -INFINITY;
+        lk[u] = 0.f;
+        if (i < nslots && live(i)) {
+          const float* st = rec_of(i) + REC_ROWS * D;
+          mk[u] = st[vrow(i)];
+          lk[u] = st[REC_ROWS + vrow(i)];
+        }
       }
-      if (fits) wts[warp][i] = mk;
-      if (mk != -INFINITY) {
-        const float mn = fmaxf(m, mk);
-        l = l * exp2f(m - mn) + lk * exp2f(mk - mn);
-        m = mn;
+#pragma unroll
+      for (int u = 0; u < SB; ++u) {
+        const int i = i0 + 32 * u;
+        if (i >= nslots) continue;
+        if (fits) wts[warp][i] = mk[u];
+        if (mk[u] != -INFINITY) {
+          const float mn = fmaxf(m, mk[u]);
+          l = l * exp2f(m - mn) + lk[u] * exp2f(mk[u] - mn);
+          m = mn;
+        }
       }
     }
 #pragma unroll
@@ -719,17 +733,34 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams
         wts[warp][i] = (L2 == -INFINITY || mk == -INFINITY) ? 0.f : exp2f(mk - L2);
       }
     __syncwarp();
-    // lane = dim group (8 dims) x slot group (4): sg = lane % 4, dg = lane / 4
+    // lane = dim group (8 dims) x slot group (4): sg = lane % 4, dg = lane / 4.
+    // Eight slots of a lane per batch, their record rows loaded together.
     const int sg = lane & 3, dg = lane >> 2;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-    for (int i = sg; i < nslots; i += 4) {
-      const float w = fits ? wts[warp][i] : weight(i);
-      if (w == 0.f) continue;
-      const float4* src = reinterpret_cast<const float4*>(rec_of(i) + vrow(i) * D + dg * 8);
-      const float4 a = src[0], c = src[1];
-      acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
-      acc[4] += w * c.x; acc[5] += w * c.y; acc[6] += w * c.z; acc[7] += w * c.w;
+    constexpr int AB = 8;
+    for (int i0 = sg; i0 < nslots; i0 += 4 * AB) {
+      float w[AB];
+      float4 a[AB], c[AB];
+#pragma unroll
+      for (int u = 0; u < AB; ++u) {
+        const int i = i0 + 4 * u;
+        w[u] = i < nslots ? (fits ? wts[warp][i] : weight(i)) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < AB; ++u) {
+        const int i = i0 + 4 * u;
+        a[u] = c[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (w[u] != 0.f) {
+          const float4* src = reinterpret_cast<const float4*>(rec_of(i) + vrow(i) * D + dg * 8);
+          a[u] = src[0];
+          c[u] = src[1];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < AB; ++u) {
+        acc[0] += w[u] * a[u].x; acc[1] += w[u] * a[u].y; acc[2] += w[u] * a[u].z; acc[3] += w[u] * a[u].w;
+        acc[4] += w[u] * c[u].x; acc[5] += w[u] * c[u].y; acc[6] += w[u] * c[u].z; acc[7] += w[u] * c[u].w;
+      }
     }
 #pragma unroll
     for (int d = 0; d < 8; ++d) {
