@@ -243,6 +243,11 @@ def config_block(world):
 
 
 # ---------------------------------------------------------------- our arm
+# Page scores of a layer on a second stream beside the next layer's attention
+# (engine overlap_scores), with --score-overlap; off by default.
+SCORE_OVERLAP = [False]
+
+
 def build_engine(specs, steps_total, world, rank, group, device):
     import torch
     from cache_eviction_b200.engine import RaggedDecodeEngine, synth_state
@@ -253,7 +258,8 @@ def build_engine(specs, steps_total, world, rank, group, device):
                              max_rows=len(specs),
                              r2u_width=-(-(max([65536] + [sp["ctx"] for sp in specs]) + steps_total + 4096) // PAGE),
                              pos_cap=32768 // PAGE, device=device, head_offset=off,
-                             global_kv_heads=G_TOTAL, process_group=group)
+                             global_kv_heads=G_TOTAL, process_group=group,
+                             overlap_scores=SCORE_OVERLAP[0])
     synth_state(eng, specs, steps_total, seed=2026 + 17)
     torch.cuda.synchronize()
     return eng
@@ -315,6 +321,7 @@ def run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
         one_step()
     compute.wait_stream(up)
     compute.wait_stream(down)                       # every download is inside the timed region
+    eng.join_scores()
     e2.record()
     torch.cuda.synchronize()
     barrier()
@@ -335,6 +342,7 @@ def run_no_score(args, specs, steps_total, world, rank, group, device, q, out, s
     B = len(specs)
     eng = build_engine(specs, steps_total, world, rank, group, device)
     eng.mode.fill_(capi.CE_MODE_NONE)
+    eng.score_flags = 0          # a plain full-cache decode: no score work or launches
     for _ in range(args.warmup):
         eng.step(q, out, sinks, scale, after_layer)
     barrier()
@@ -343,6 +351,7 @@ def run_no_score(args, specs, steps_total, world, rank, group, device, q, out, s
     s2.record()
     for _ in range(args.steps):
         eng.step(q, out, sinks, scale, after_layer)
+    eng.join_scores()
     e2.record()
     torch.cuda.synchronize()
     barrier()
@@ -381,6 +390,7 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
         eng = build_engine(specs, warmup + steps, world, rank, group, device)
         if not scored:
             eng.mode.fill_(capi.CE_MODE_NONE)
+            eng.score_flags = 0      # a plain full-cache decode: no score work or launches
         # the CSR buffer the graph holds stays large enough; the warm-up steps
         # then size the decode workspace for it, so the capture allocates nothing
         eng._ensure_capacity(warmup + steps + 16)
@@ -388,11 +398,15 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
             eng.step(q, out, sinks, scale)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
+        eng.join_scores()
+        eng.new_score_events()
         with torch.cuda.graph(graph):
             eng.seq_lens_dev.add_(1)
             eng.fill()
             for l in range(LAYERS):
                 eng.decode_layer(l, q[l], out[l], sinks[l], scale)
+            eng.join_scores()      # a capture ends with every forked stream joined
+        eng.new_score_events()
         torch.cuda.synchronize()
         row = eng.rows[eng.active[0]]
         resident = []
@@ -406,6 +420,7 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
                 row.n += 1       # the host side of engine.advance
                 graph.replay()
             resident.append(eng.resident_tokens(eng.active[0]))
+        eng.join_scores()
         end.record()
         torch.cuda.synchronize()
         barrier()
@@ -661,10 +676,13 @@ def main():
                     help="legs to run; without 'decode' only the listed microbenchmarks run "
                          "and one JSON line with their results is printed (profiling)")
     ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
+    ap.add_argument("--score-overlap", action="store_true",
+                    help="score each layer's pages on a second stream (engine overlap_scores)")
     ap.add_argument("--prefill-prefixes", default=",".join(map(str, PREFILL_PREFIXES)),
                     help="resident prefixes of the config-4 leg")
     args = ap.parse_args()
     legs = set(args.legs.split(","))
+    SCORE_OVERLAP[0] = args.score_overlap
     prefixes = tuple(int(x) for x in args.prefill_prefixes.split(","))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -772,6 +790,7 @@ def main():
                 b.record()
                 ev.append((a, b, nbytes))
                 after_layer(l, out[l])
+        eng.join_scores()          # the last layers' page scores are inside the timed region
         end.record()
         torch.cuda.synchronize()
     barrier()

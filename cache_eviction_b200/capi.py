@@ -37,6 +37,7 @@ CE_POLICY_HEAD_MAX = 4
 CE_POLICY_H2O_GLOBAL = 5
 
 CE_MODE_NONE, CE_MODE_SUM, CE_MODE_MAX = 0, 1, 2
+CE_SCORE_DEFER = 4   # score_flags bit: leave the page scores to ce_decode_scores
 CE_DTYPE_NONE, CE_DTYPE_F32, CE_DTYPE_F64, CE_DTYPE_BF16 = 0, 1, 2, 3
 
 # size of the static scratch behind ce_decode_attn_score_static
@@ -67,6 +68,8 @@ SIGNATURES = {
     "ce_decode_attn_score": (C.c_int, [P, I64, I64, P, P, I64, P, P, P, I64, P, P, P, F32, I32,
                                        I32, I32, I32, I32, P, I64, I32, P, I32, I64, I64, P,
                                        I32, P, I64, P, P]),
+    "ce_decode_scores": (C.c_int, [P, P, P, I64, I64, P, P, I32, I32, I32, I32, P, I64, I32, I32, P,
+                                   I64, P, P]),
     "ce_decode_attn_score_static": (C.c_int, [P, I64, I64, P, P, I64, P, P, P, I64, P, P, P, F32,
                                               I32, I32, I32, I32, I32, P, I64, I32, P, I32, I64,
                                               I64, P, I32, P, P]),

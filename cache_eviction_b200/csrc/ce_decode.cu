@@ -567,8 +567,9 @@ constexpr int MAX_SLOTS = 160 * NCW;   // (record, sub-part) slots one sequence 
 
 struct CombineParams {
   Params a;
-  int grid;   // CTAs the attention kernel was launched with
+  int grid;    // CTAs the attention kernel was launched with
   int P;
+  int defer;   // CE_SCORE_DEFER: keep the normalisers in lse2, add no scores here
 };
 
 // Add sequence b's page masses for KV head g into scores[g, unit]:
@@ -774,7 +775,9 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams
     if (lane == 0) {
       sh_l2[warp] = L2;
       if (p.lse_out) p.lse_out[static_cast<int64_t>(b) * H + h] = L2 * LN2;
+      if (cp.defer) p.lse2[static_cast<int64_t>(b) * H + h] = L2;
     }
+    if (cp.defer) continue;   // score_kernel adds the page masses later
     __syncthreads();
     // The task's 8 heads are exactly KV head g's group: add this sequence's
     // page masses for KV head g (pages in independent batches of 4).
@@ -782,6 +785,27 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams
     if (mode == CE_MODE_MAX && cp.P > 1 && !p.tl) mode = CE_MODE_NONE;
     if (mode == CE_MODE_SUM || mode == CE_MODE_MAX)
       score_pages(p, b, hc, mode, cp.P, sh_l2);
+    __syncthreads();
+  }
+}
+
+// The page masses of a deferred decode (CE_SCORE_DEFER): the same work as
+// the tail of combine_kernel, one task per (sequence, group of 8 query
+// heads), from the normalisers combine_kernel left in lse2.  Small enough to
+// run beside the next layer's attention kernel on another stream.
+__global__ void __launch_bounds__(CB_THREADS) score_kernel(const CombineParams cp) {
+  const Params& p = cp.a;
+  const int hgroups = p.H / GROUP;
+  const int64_t ntasks = static_cast<int64_t>(p.bs) * hgroups;
+  __shared__ float sh_l2[GROUP];
+  for (int64_t task = blockIdx.x; task < ntasks; task += gridDim.x) {
+    const int b = static_cast<int>(task / hgroups), hc = static_cast<int>(task % hgroups);
+    int mode = (p.mode_of_row && p.scores && p.ul) ? seq_mode(p, b) : CE_MODE_NONE;
+    if (mode == CE_MODE_MAX && cp.P > 1 && !p.tl) mode = CE_MODE_NONE;
+    if (seq_tokens(p, b, cp.P) <= 0 || (mode != CE_MODE_SUM && mode != CE_MODE_MAX)) continue;
+    if (threadIdx.x < GROUP) sh_l2[threadIdx.x] = p.lse2[static_cast<int64_t>(b) * p.H + hc * GROUP + threadIdx.x];
+    __syncthreads();
+    score_pages(p, b, hc, mode, cp.P, sh_l2);
     __syncthreads();
   }
 }
@@ -910,10 +934,61 @@ extern "C" int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh, c
     attn_kernel<1><<<grid, THREADS, SMEM_BYTES, st>>>(kmap, vmap, p);
   }
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("attn_kernel launch");
-  CombineParams cp{p, grid, page_size};
+  const bool defer = (score_flags & CE_SCORE_DEFER) != 0;
+  CombineParams cp{p, grid, page_size, defer ? 1 : 0};
+  // A deferred decode's page scores run beside the next layer's attention
+  // kernel (195 KB of shared memory per CTA): keep SMs at the largest carveout.
+  if (defer && !host::set_max_shared_carveout(combine_kernel)) return host::fail(CE_ERR_CUDA, "carveout attr");
   const int cb_grid = static_cast<int>(
       std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP), 4LL * grid)));
   combine_kernel<<<cb_grid, CB_THREADS, 0, st>>>(cp);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("combine_kernel launch");
+  return CE_OK;
+}
+
+extern "C" int ce_decode_scores(const int32_t* kv_indptr, const int32_t* kv_indices,
+                                const int32_t* kv_tokens, int64_t kv_capacity, int64_t pool_units,
+                                const int32_t* mode_of_row, const int64_t* rows, int32_t bs,
+                                int32_t num_q_heads, int32_t num_kv_heads, int32_t page_size,
+                                float* scores, int64_t score_sg, int32_t zero_new, int32_t score_flags,
+                                const void* workspace, int64_t workspace_bytes, int32_t* err,
+                                void* stream) {
+  if (bs < 0 || pool_units < 0 || kv_capacity < 0) return host::fail(CE_ERR_ARG, "negative size");
+  if (num_kv_heads <= 0 || num_q_heads != GROUP * num_kv_heads || NCW % num_kv_heads != 0)
+    return host::fail(CE_ERR_UNSUPPORTED, "need 8 query heads per KV head and 1/2/4/8 KV heads");
+  if (!(page_size == 16 || (page_size == 1 && num_kv_heads == 8)))
+    return host::fail(CE_ERR_UNSUPPORTED, "page_size must be 16 (or 1 with 8 KV heads)");
+  if (bs == 0 || !mode_of_row || !scores || !(score_flags & 3)) return CE_OK;
+  if (!kv_indptr || !kv_indices || !workspace) return host::fail(CE_ERR_ARG, "null pointer");
+  if (page_size > 1 && !kv_tokens) return host::fail(CE_ERR_ARG, "kv_tokens required for page_size > 1");
+  const int grid = host::sm_count();
+  if (grid <= 0) return host::fail(CE_ERR_CUDA, "no device");
+  DecodeLayout L = decode_layout(bs, kv_capacity, num_q_heads, page_size, score_flags, grid);
+  if (workspace_bytes < (int64_t)L.total) return host::fail(CE_ERR_WORKSPACE, "decode workspace too small");
+  Params p{};
+  p.kv_indptr = kv_indptr;
+  p.kv_indices = kv_indices;
+  p.kv_tokens = kv_tokens;
+  p.kv_capacity = kv_capacity;
+  p.pool_units = pool_units;
+  p.mode_of_row = mode_of_row;
+  p.rows = rows;
+  p.bs = bs;
+  p.H = num_q_heads;
+  p.G = num_kv_heads;
+  p.scores = scores;
+  p.score_sg = score_sg;
+  p.zero_new = zero_new;
+  uint8_t* ws = static_cast<uint8_t*>(const_cast<void*>(workspace));
+  p.lse2 = reinterpret_cast<float*>(ws + L.lse2);
+  p.ul = reinterpret_cast<float*>(ws + L.ul);
+  p.tl = ((score_flags & 2) && page_size > 1) ? reinterpret_cast<float*>(ws + L.tl) : nullptr;
+  p.err = err;
+  CombineParams cp{p, grid, page_size, 1};
+  if (!host::set_max_shared_carveout(score_kernel)) return host::fail(CE_ERR_CUDA, "carveout attr");
+  const int sc_grid = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP), 2LL * grid)));
+  score_kernel<<<sc_grid, CB_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(cp);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("score_kernel launch");
   return CE_OK;
 }

@@ -60,6 +60,8 @@ extern "C" int ce_decode_attn_score_static(
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
     float* scores, int64_t score_sg, int32_t zero_new, void* out, int32_t out_f32, int64_t o_sb,
     int64_t o_sh, float* lse_out, int32_t score_flags, int32_t* err, void* stream) {
+  if (score_flags & CE_SCORE_DEFER)
+    return ce::host::fail(CE_ERR_ARG, "ce_decode_attn_score_static: deferred scores need a caller workspace");
   if (bs == 0) return CE_OK;
   const int64_t need = ce_decode_workspace_bytes(bs, kv_capacity, num_q_heads, num_kv_heads,
                                                  page_size, score_flags);

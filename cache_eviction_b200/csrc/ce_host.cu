@@ -66,6 +66,20 @@ bool set_smem_attr(const void* func, int bytes) {
   return true;
 }
 
+bool set_max_shared_carveout_attr(const void* func) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(g_mu);
+  // carveout entries share the cache with bytes = -1
+  for (int i = 0; i < g_smem_n; ++i)
+    if (g_smem[i].func == func && g_smem[i].device == dev && g_smem[i].bytes == -1) return true;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           static_cast<int>(cudaSharedmemCarveoutMaxShared)) != cudaSuccess)
+    return false;
+  if (g_smem_n < 256) g_smem[g_smem_n++] = {func, dev, -1};
+  return true;
+}
+
 static bool encoder() {
   std::lock_guard<std::mutex> lock(g_mu);
   if (!g_encode) {

@@ -26,6 +26,15 @@ bool set_smem(F* func, int bytes) {
   return set_smem_attr(reinterpret_cast<const void*>(func), bytes);
 }
 
+// Prefer the largest shared-memory carveout for a kernel, once per device: a
+// small kernel that runs beside a large-shared-memory one must not leave an
+// SM configured for less shared memory than the large one needs.
+bool set_max_shared_carveout_attr(const void* func);
+template <class F>
+bool set_max_shared_carveout(F* func) {
+  return set_max_shared_carveout_attr(reinterpret_cast<const void*>(func));
+}
+
 // Tiled tensor map of `rank` dims (innermost first): dims, byte strides of
 // dims 1..rank-1, box sizes; element strides 1, zero fill out of bounds,
 // 128-byte swizzle or none.

@@ -45,7 +45,7 @@ class RaggedDecodeEngine:
                  pool_units: int, max_rows: int, r2u_width: int, pos_cap: int,
                  device="cuda", head_offset: int = 0, global_kv_heads: Optional[int] = None,
                  process_group=None, alloc_pools: bool = True, boundary_rows: int = 8,
-                 hazard_bytes: int = 512 << 20):
+                 hazard_bytes: int = 512 << 20, overlap_scores: bool = False):
         self.L, self.H, self.G, self.P = layers, q_heads, kv_heads, page_size
         self.units = pool_units
         self.device = torch.device(device)
@@ -84,14 +84,46 @@ class RaggedDecodeEngine:
         # loop (a larger batch grows it once).
         self.hazard_bytes = hazard_bytes
         self.r2u_width = r2u_width
+        # With overlap_scores a layer's H2O page scores (ce_decode_scores) run
+        # on their own stream beside the next layer's attention, from one of
+        # two decode workspaces alternating by layer (decode_layer).  Off by
+        # default: measured against scoring inside the decode call it gained
+        # 0-1 % at a batch of 64 and at batch 1 (CUDA-graph steps) and lost
+        # ~3 % end to end in a host-driven loop with per-layer copies.
+        self.overlap_scores = overlap_scores
+        # score_flags of every decode call: 0 makes the engine a plain
+        # full-cache decode (no score workspace, no score launches)
+        self.score_flags = 3
+        self._score_stream = torch.cuda.Stream(dev) if overlap_scores else None
+        self._dec_ws = [None, None]
+        self._ws_need = (None, 0)
+        self.new_score_events()
+        self._scores_pending = False
         if alloc_pools:
             kernels.reserve_boundary(dev, min(max_rows, boundary_rows), layers, kv_heads, page_size,
                                      r2u_width, pos_cap,
                                      self.global_G if process_group is not None else 0, hazard_bytes)
 
+    def new_score_events(self):
+        """Fresh ordering events for the score stream.  Also for a CUDA-graph
+        capture: a capture may not wait on an event recorded outside it, and
+        no stream may wait on an event last recorded inside one, so call this
+        (after join_scores) right before a capture and again right after."""
+        self._ws_free = [torch.cuda.Event(), torch.cuda.Event()]
+        self._attn_done = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def join_scores(self):
+        """Order the current stream after every deferred page-score launch.
+        Called before anything rewrites the CSR, the row lists or the decode
+        workspaces, and before the scores are read."""
+        if self._scores_pending:
+            torch.cuda.current_stream(self.device).wait_stream(self._score_stream)
+            self._scores_pending = False
+
     # ------------------------------------------------------------- rows
     def add_row(self, row: int, cfg: Optional[EvictionConfig], n: int, last_boundary: int = 0,
                 frontier_units: int = 0, count_units: int = 0):
+        self.join_scores()
         self.rows[row] = Row(cfg=cfg, n=n, last_boundary=last_boundary, frontier=frontier_units,
                              count=count_units)
         self.mode[row] = cfg.score_mode if cfg is not None else capi.CE_MODE_NONE
@@ -102,6 +134,7 @@ class RaggedDecodeEngine:
 
     def commit_rows(self):
         """Upload the active row list and lengths (after rows were added)."""
+        self.join_scores()
         self.rows_dev = torch.tensor(self.active, dtype=torch.int64, device=self.device)
         self.seq_lens_dev = torch.tensor([self.rows[r].n for r in self.active], dtype=torch.int64,
                                          device=self.device)
@@ -119,6 +152,7 @@ class RaggedDecodeEngine:
     def _ensure_capacity(self, extra_tokens: int = 1):
         need = sum(self.resident_units(r, extra_tokens) for r in self.active) + 16
         if self.kv_indices.numel() < need:
+            self.join_scores()
             self.kv_indices = torch.zeros(int(need * 1.25), dtype=torch.int32, device=self.device)
 
     # -------------------------------------------------------- boundaries
@@ -138,6 +172,7 @@ class RaggedDecodeEngine:
         """One batched ce_boundary over `rows`; returns the per-row results (host)."""
         if not rows:
             return []
+        self.join_scores()
         P = self.P
         hazard_bytes = self.hazard_bytes if hazard_bytes is None else hazard_bytes
         params, ncols = [], []
@@ -205,19 +240,51 @@ class RaggedDecodeEngine:
 
     # ------------------------------------------------------------ decode
     def fill(self):
+        self.join_scores()
         bs = len(self.active)
         kernels.fill(self.table, self.r2u, self.frontier, self.count, self.rows_dev,
                      self.seq_lens_dev, self.P, self.kv_indptr[:bs + 1], self.kv_indices,
                      self.kv_tokens[:bs], self.err)
 
     def decode_layer(self, layer: int, q: torch.Tensor, out: torch.Tensor, sinks, scale: float,
-                     score_flags: int = 3):
+                     score_flags: Optional[int] = None):
         bs = len(self.active)
-        return kernels.decode_attn_score(
+        score_flags = self.score_flags if score_flags is None else score_flags
+        if not (self.overlap_scores and score_flags & 3 and bs):
+            return kernels.decode_attn_score(
+                q, self.k[layer], self.v[layer], self.kv_indptr[:bs + 1], self.kv_indices,
+                self.kv_tokens[:bs], scale, self.P, sinks=sinks, mode_of_row=self.mode,
+                rows=self.rows_dev, scores=self.scores[layer], zero_new=True, out=out,
+                score_flags=score_flags, err=self.err)
+        # Attention and outputs on the current stream; this layer's page scores
+        # on the score stream once they are done, overlapping the next layer.
+        # Workspace k is reused two layers later, after its scores have run.
+        k = layer % 2
+        key = (bs, self.kv_indices.numel(), score_flags)
+        if self._ws_need[0] != key:      # the same for every layer of a step
+            self._ws_need = (key, kernels.decode_workspace_bytes(bs, key[1], self.H, self.G, self.P,
+                                                                 score_flags))
+        need = self._ws_need[1]
+        if self._dec_ws[k] is None or self._dec_ws[k].numel() < need:
+            self.join_scores()
+            self._dec_ws[k] = torch.empty(need, dtype=torch.uint8, device=self.device)
+        ws = self._dec_ws[k]
+        main = torch.cuda.current_stream(self.device)
+        main.wait_event(self._ws_free[k])
+        res = kernels.decode_attn_score(
             q, self.k[layer], self.v[layer], self.kv_indptr[:bs + 1], self.kv_indices,
             self.kv_tokens[:bs], scale, self.P, sinks=sinks, mode_of_row=self.mode,
             rows=self.rows_dev, scores=self.scores[layer], zero_new=True, out=out,
-            score_flags=score_flags, err=self.err)
+            score_flags=score_flags | capi.CE_SCORE_DEFER, err=self.err, workspace=ws)
+        self._attn_done[k].record(main)
+        side = self._score_stream
+        side.wait_event(self._attn_done[k])
+        kernels.decode_scores(self.kv_indptr[:bs + 1], self.kv_indices, self.kv_tokens[:bs], self.units,
+                              self.P, self.H, self.G, bs, self.mode, self.rows_dev, self.scores[layer], ws,
+                              zero_new=True, score_flags=score_flags, err=self.err, stream=side)
+        self._ws_free[k].record(side)
+        self._scores_pending = True
+        return res
 
     def advance(self):
         """Append one token to every active row (host lengths and the device copy)."""

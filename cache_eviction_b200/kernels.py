@@ -96,11 +96,14 @@ def fill(table, req_to_unit, frontier, count, rows, seq_lens, page_size, kv_indp
 
 def decode_attn_score(q, k_pool, v_pool, kv_indptr, kv_indices, kv_tokens, sm_scale, page_size,
                       sinks=None, mode_of_row=None, rows=None, scores=None, zero_new=True,
-                      out=None, out_f32=False, lse=None, score_flags=3, err=None):
+                      out=None, out_f32=False, lse=None, score_flags=3, err=None, workspace=None):
     """Fused decode attention + H2O score over one layer.
 
     q [bs, H, 64] bf16; pools [units, G, page, 64] bf16; scores [G, units] fp32.
-    Returns out [bs, H, 64] (bf16, or fp32 with out_f32).
+    Returns out [bs, H, 64] (bf16, or fp32 with out_f32).  With
+    capi.CE_SCORE_DEFER in score_flags the page scores are left to
+    decode_scores, which must get the same workspace (then pass one here:
+    a uint8 device tensor of at least decode_workspace_bytes()).
     """
     lib = capi.load()
     bs, H, D = q.shape
@@ -119,7 +122,11 @@ def decode_attn_score(q, k_pool, v_pool, kv_indptr, kv_indices, kv_tokens, sm_sc
     need = lib.ce_decode_workspace_bytes(bs, cap, H, G, page_size, score_flags)
     if need < 0:
         raise capi.CeError("ce_decode_workspace_bytes failed")
-    ws = WORKSPACES.get(dev, "decode", need)
+    if workspace is not None:
+        assert workspace.dtype == torch.uint8 and workspace.numel() >= need
+        ws = workspace
+    else:
+        ws = WORKSPACES.get(dev, "decode", need)
     st = lib.ce_decode_attn_score(
         _p(q), q.stride(0), q.stride(1), _p(k_pool), _p(v_pool), k_pool.shape[0], _p(kv_indptr),
         _p(kv_indices), _p(kv_tokens), cap, _p(sinks), _p(mode_of_row), _p(rows), float(sm_scale),
@@ -129,6 +136,30 @@ def decode_attn_score(q, k_pool, v_pool, kv_indptr, kv_indices, kv_tokens, sm_sc
     capi.check(st, "ce_decode_attn_score")
     _count(2 if bs else 0)
     return out
+
+
+def decode_workspace_bytes(bs, kv_capacity, H, G, page_size, score_flags=3):
+    need = capi.load().ce_decode_workspace_bytes(bs, kv_capacity, H, G, page_size, score_flags)
+    if need < 0:
+        raise capi.CeError("ce_decode_workspace_bytes failed")
+    return need
+
+
+def decode_scores(kv_indptr, kv_indices, kv_tokens, pool_units, page_size, H, G, bs, mode_of_row, rows,
+                  scores, workspace, zero_new=True, score_flags=3, err=None, stream=None):
+    """The page scores a decode_attn_score(..., CE_SCORE_DEFER) call left out,
+    from that call's workspace and CSR, on `stream` (a torch.cuda.Stream;
+    default the current stream)."""
+    lib = capi.load()
+    if bs == 0 or scores is None or mode_of_row is None:
+        return
+    assert scores.dtype == torch.float32 and scores.stride(1) == 1
+    st = lib.ce_decode_scores(_p(kv_indptr), _p(kv_indices), _p(kv_tokens), kv_indices.numel(), pool_units,
+                              _p(mode_of_row), _p(rows), bs, H, G, page_size, _p(scores), scores.stride(0),
+                              1 if zero_new else 0, score_flags & 3, _p(workspace), workspace.numel(), _p(err),
+                              _stream(workspace.device) if stream is None else C.c_void_p(stream.cuda_stream))
+    capi.check(st, "ce_decode_scores")
+    _count(1 if score_flags & 3 else 0)
 
 
 def prefill_scores(q, k_pool, qo_indptr, kv_indptr, kv_indices, kv_tokens, sm_scale, page_size,

@@ -139,8 +139,10 @@ int ce_fill(const int32_t* table, int64_t table_stride,
  *   lse_out [bs, H] fp32 natural-log normalizer incl. sink, or NULL
  *   score_flags bit0: CE_MODE_SUM rows may occur, bit1: CE_MODE_MAX rows may
  *           occur (sizes the workspace; a row whose mode has no workspace
- *           flags CE_EW_MODE and gets no score)
+ *           flags CE_EW_MODE and gets no score); CE_SCORE_DEFER: compute the
+ *           outputs and lse only, leave the scores to ce_decode_scores
  * Supported: head_dim 64, H/G == 8, page_size 1 (G == 8) or 16 (any G). */
+#define CE_SCORE_DEFER 4
 int64_t ce_decode_workspace_bytes(int32_t bs, int64_t kv_capacity,
                                   int32_t num_q_heads, int32_t num_kv_heads,
                                   int32_t page_size, int32_t score_flags);
@@ -158,13 +160,32 @@ int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh,
                          void* workspace, int64_t workspace_bytes,
                          int32_t* err, void* stream);
 
+/* ---- K1's score part, deferred ----------------------------------------------
+ * After ce_decode_attn_score(..., score_flags | CE_SCORE_DEFER, workspace, ...)
+ * adds the H2O page masses that call left out, from the normalisers and
+ * per-page log-masses it kept in its workspace.  The arguments are that
+ * call's (the same CSR, rows, modes, scores, score_flags and workspace), and
+ * the two calls must be ordered (same stream, or an event between streams);
+ * the CSR and the workspace must not be rewritten before this call has run.
+ * The scores equal those of the undeferred call bit for bit.  No reference
+ * counterpart: it lets a layer's page scoring run on a second stream beside
+ * the next layer's attention. */
+int ce_decode_scores(const int32_t* kv_indptr, const int32_t* kv_indices,
+                     const int32_t* kv_tokens, int64_t kv_capacity, int64_t pool_units,
+                     const int32_t* mode_of_row, const int64_t* rows, int32_t bs,
+                     int32_t num_q_heads, int32_t num_kv_heads, int32_t page_size,
+                     float* scores, int64_t score_sg, int32_t zero_new, int32_t score_flags,
+                     const void* workspace, int64_t workspace_bytes, int32_t* err,
+                     void* stream);
+
 /* ---- K1 without a caller workspace ------------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device
  * memory when they decode (an engine that gave all HBM to its KV pool, a host
  * that forbids allocations after start-up, a global-mode graph capture):
  * identical to ce_decode_attn_score except that its scratch is a static
  * device array of CE_DECODE_STATIC_SCRATCH_BYTES inside the library, held by
- * every GPU that loads the library until the process exits.
+ * every GPU that loads the library until the process exits, and that
+ * CE_SCORE_DEFER is refused (CE_ERR_ARG).
  *   - A call whose ce_decode_workspace_bytes() exceeds that maximum returns
  *     CE_ERR_WORKSPACE and launches nothing.
  *   - The first call on a device looks up the array's device address

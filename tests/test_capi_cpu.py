@@ -84,3 +84,26 @@ def test_live_boundary_needs_a_positive_epoch():
     args[names.index("hazard_bytes")] = 1 << 20
     assert lib.ce_boundary(*args) == capi.CE_ERR_ARG
     assert b"epoch" in lib.ce_last_error()
+
+
+def test_static_decode_refuses_deferred_scores():
+    """ce_decode_attn_score_static has no caller workspace for
+    ce_decode_scores to read, so CE_SCORE_DEFER is refused on the host before
+    any device work (the pointers below are never dereferenced)."""
+    from cache_eviction_b200 import capi
+    lib = capi.load()
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "ce_api.h").read_text(), flags=re.S)
+    params = re.search(r"\bce_decode_attn_score_static\s*\(([^)]*)\)\s*;", text).group(1).split(",")
+    names = [re.findall(r"\w+", p)[-1] for p in params]
+    ints = {"bs": 1, "num_q_heads": 64, "num_kv_heads": 8, "head_dim": 64, "page_size": 16,
+            "score_flags": 3 | capi.CE_SCORE_DEFER, "pool_units": 4, "kv_capacity": 4}
+    args = []
+    for name, p in zip(names, params):
+        if "*" in p:
+            args.append(None if name in ("err", "stream", "lse_out", "sinks", "rows") else C.c_void_p(4096))
+        elif "float" in p:
+            args.append(0.125)
+        else:
+            args.append(ints.get(name, 0))
+    assert lib.ce_decode_attn_score_static(*args) == capi.CE_ERR_ARG
+    assert b"caller workspace" in lib.ce_last_error()
