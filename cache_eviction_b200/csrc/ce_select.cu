@@ -1782,16 +1782,46 @@ __global__ void __launch_bounds__(T, LARGE ? 1 : 2) bsel_kernel(const BParams p)
 // once per KV-head segment: the fp32 sum of the layer's KV heads' unit
 // scores in ascending head order (the same additions the selection would
 // make).  Grid (column blocks, rows); rows of other policies are skipped.
-__global__ void hsum_kernel(const BParams p, float* gsum) {
+// With usum (unit_sum_kernel's per-unit sums) a column reads its unit's sum
+// instead of gathering the G head scores itself.
+__global__ void hsum_kernel(const BParams p, float* gsum, const float* usum) {
   const int i = blockIdx.y;
   const RowCtx r = row_ctx(p, i);
   if (r.q.policy != CE_POLICY_H2O_GLOBAL || !row_shape_ok(p, r) || r.N <= r.q.budget) return;
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < r.N; c += gridDim.x * blockDim.x) {
     const int u = col_unit(p, r, c);
+    const bool ok = u >= 0 && u < p.pool_units;
     for (int l = 0; l < p.L; ++l) {
       float acc = 0.f;
-      for (int gg = 0; gg < p.G; ++gg) acc += unit_score(p, l, gg, u);
+      if (usum) {
+        acc = ok ? usum[static_cast<int64_t>(l) * p.pool_units + u] : 0.f;
+      } else {
+        for (int gg = 0; gg < p.G; ++gg) acc += unit_score(p, l, gg, u);
+      }
       gsum[(static_cast<int64_t>(i) * p.L + l) * p.max_cols + c] = acc;
+    }
+  }
+}
+
+// Per-unit sums over the layer's KV heads (ascending head order, starting
+// from 0 as hsum_kernel does) for every pool unit, in one coalesced pass over
+// the score rows.  Used when the batch's rows own most of the pool, where it
+// replaces G scattered loads per column by one; returns at once when no row
+// of the batch is H2O global.
+__global__ void unit_sum_kernel(const BParams p, float* usum) {
+  __shared__ int any;
+  if (threadIdx.x == 0) {
+    any = 0;
+    for (int i = 0; i < p.R; ++i) any |= p.params[i].policy == CE_POLICY_H2O_GLOBAL;
+  }
+  __syncthreads();
+  if (!any) return;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < p.pool_units;
+       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    for (int l = 0; l < p.L; ++l) {
+      float acc = 0.f;
+      for (int gg = 0; gg < p.G; ++gg) acc += p.scores[l * p.sls + gg * p.shs + u];
+      usum[static_cast<int64_t>(l) * p.pool_units + u] = acc;
     }
   }
 }
@@ -2516,7 +2546,19 @@ extern "C" int ce_boundary(int32_t* table, int64_t table_stride, int32_t table_w
   if (cudaMemsetAsync(p.row_info, 0, sizeof(int32_t) * RI * num_rows, st) != cudaSuccess)
     return host::fail_cuda("row_info memset");
   if (!global_scores) {
-    hsum_kernel<<<dim3((max_cols + 255) / 256, num_rows), 256, 0, st>>>(p, const_cast<float*>(p.gscores));
+    // Long rows (more than 4,096 columns) that own most of the pool
+    // (pool_units <= 2 x rows x columns): per-unit head sums in the kv region
+    // (free until the selection, and at least 8 x rows x layers x max_cols
+    // bytes) save G - 1 gathers per column.  Shorter rows gather cheaply and
+    // would only pay the extra launch.
+    float* usum = nullptr;
+    if (max_cols > REG_ITEMS * T && pool_units > 0 && pool_units <= 2LL * num_rows * max_cols) {
+      usum = reinterpret_cast<float*>(p.kv);
+      const int64_t ublocks = std::min<int64_t>((pool_units + 255) / 256, 8LL * host::sm_count());
+      unit_sum_kernel<<<static_cast<unsigned>(std::max<int64_t>(1, ublocks)), 256, 0, st>>>(p, usum);
+      if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("unit_sum_kernel");
+    }
+    hsum_kernel<<<dim3((max_cols + 255) / 256, num_rows), 256, 0, st>>>(p, const_cast<float*>(p.gscores), usum);
     if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("hsum_kernel");
   }
   if (large)

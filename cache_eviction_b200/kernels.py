@@ -326,7 +326,8 @@ def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, k
         _p(record[1]) if record else None, _p(err), _stream(dev))
     capi.check(st, "ce_boundary")
     if R:
-        # bsel, bvalidate, bfinish; hsum without global scores; bzero when
+        # bsel, bvalidate, bfinish; hsum (and unit_sum for long rows that own
+        # most of the pool) without global scores; bzero when
         # live; a gather and a scatter per launch group (rows x layers fitting
         # the hazard scratch)
         width = max_width if 0 < max_width < max_cols else max_cols
@@ -334,7 +335,9 @@ def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, k
         hz = max(int(hazard_bytes), row_layer)
         rows_per = min(R, max(1, hz // row_layer))
         group = min(L, max(1, hz // (rows_per * row_layer)))
-        _count(3 + (1 if global_scores is None else 0) + (1 if live and scores.shape[2] > 0 else 0)
+        units = scores.shape[2]
+        hsum = 0 if global_scores is not None else (2 if max_cols > 4096 and 0 < units <= 2 * R * max_cols else 1)
+        _count(3 + hsum + (1 if live and units > 0 else 0)
                + 2 * ceil_div(R, rows_per) * ceil_div(L, group) + (1 if record else 0))
     return result, freed
 
