@@ -1,9 +1,9 @@
 """Generate the golden fixtures from the reference's own functions.
 
-    python tests/golden/make_golden.py [/path/to/cache-eviction]
+    python tests/golden/make_golden.py /path/to/cache-eviction
 
 Imports tonghuikang/cache-eviction's code/cache_eviction/sglang_evict_runtime.py
-and core.py from a read-only checkout (default /root/reference) and runs them on
+and core.py from a read-only checkout (the path argument) and runs them on
 CPU tensors; torch.cuda.synchronize is replaced by a no-op in this process only.
 Inputs come from tests/golden/scenarios.py (numpy, fixed seeds), so only the
 reference's outputs are stored.  The checkout is needed only to regenerate;
@@ -276,7 +276,9 @@ def gen_prefill(rt):
 
 
 def main():
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py /path/to/cache-eviction")
+    root = Path(sys.argv[1])
     rt, core = load_reference(root)
     gen_choose(rt)
     gen_reservoir(rt, core)
