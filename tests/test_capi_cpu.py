@@ -107,3 +107,20 @@ def test_static_decode_refuses_deferred_scores():
             args.append(ints.get(name, 0))
     assert lib.ce_decode_attn_score_static(*args) == capi.CE_ERR_ARG
     assert b"caller workspace" in lib.ce_last_error()
+
+
+def test_deferred_scores_check_shapes_on_the_host():
+    """ce_decode_scores validates its sizes before any device work: an
+    unsupported head layout or page size is an error status, and a call with
+    nothing to score (no mode table) is a no-op (pointers never dereferenced)."""
+    from cache_eviction_b200 import capi
+    lib = capi.load()
+    dummy = C.c_void_p(4096)
+
+    def call(H, G, page, modes=dummy):
+        return lib.ce_decode_scores(dummy, dummy, dummy, 16, 16, modes, None, 2, H, G, page, dummy, 16, 1, 3,
+                                    dummy, 1 << 20, None, None)
+    assert call(63, 8, 16) == capi.CE_ERR_UNSUPPORTED
+    assert call(64, 8, 8) == capi.CE_ERR_UNSUPPORTED
+    assert call(32, 4, 1) == capi.CE_ERR_UNSUPPORTED        # page size 1 needs 8 KV heads
+    assert call(64, 8, 16, modes=None) == capi.CE_OK
