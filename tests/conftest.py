@@ -14,3 +14,14 @@ for p in (ROOT, ROOT / "tests"):
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) and libce_b200.so")
+
+
+def pytest_sessionstart(session):
+    """A fresh checkout has no libce_b200.so yet: compile it (nvcc for sm_100a,
+    in-tree, as __graft_entry__.build does) before any test loads it.  An
+    existing library is used as it is, so a test run never rebuilds what the
+    build step made.  (The oracle builds itself on first use.)"""
+    lib = ROOT / "cache_eviction_b200" / "_lib" / "libce_b200.so"
+    if not lib.exists():
+        from cache_eviction_b200 import build
+        build.build(force=False)
