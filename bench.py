@@ -25,6 +25,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -33,14 +34,16 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-METRIC = "decode tok/s with per-head H2O eviction (ragged 64-seq batch, 8K-32K budgets)"
+METRIC = ("decode tok/s with eviction, config-3 ragged batch (64 seqs/GPU, budgets 2K-32K, "
+          "policies full/recent/random/H2O global/H2O per-head)")
 UNIT = "tok/s"
 H_TOTAL, G_TOTAL, D, PAGE, LAYERS, HIDDEN = 64, 8, 64, 16, 12, 2880
 SEQS_PER_GPU = 64
 # DRAM bytes (read + write, attn_kernel + combine_kernel) per resident token
-# from one ncu capture of the 8-sequence config-3 case
-# (profiles/decode_kernels_config3_8seq.md); the traffic of this streaming
-# kernel grows with resident tokens, so a full launch scales by its tokens.
+# from one ncu capture of the 8-sequence config-3 case (dram__bytes_read.sum +
+# dram__bytes_write.sum over the launch's resident tokens); the traffic of this
+# streaming kernel grows with resident tokens, so a full launch scales by its
+# tokens.
 TRAFFIC_BYTES_PER_RESIDENT_TOKEN = 2174.0
 BUDGETS = [2048, 4096, 8192, 16384, 32768]
 POLICY_MIX = ["full", "recent", "random", "h2o_global", "h2o_per_head"]
@@ -97,7 +100,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_gpu{gpu_index}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"ce_bench_clocks_gpu{gpu_index}_{os.getpid()}.csv"
 
     def __enter__(self):
         try:

@@ -946,6 +946,16 @@ extern "C" int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh, c
   return CE_OK;
 }
 
+int ce::host::decode_prepare_device() {
+  // cudaFuncGetAttributes loads a kernel under lazy module loading; the
+  // shared-memory attribute is the one the first launch would set.
+  cudaFuncAttributes a;
+  if (!host::set_smem(attn_kernel<16>, SMEM_BYTES) || !host::set_smem(attn_kernel<1>, SMEM_BYTES) ||
+      cudaFuncGetAttributes(&a, combine_kernel) != cudaSuccess)
+    return host::fail_cuda("decode kernels: set-up");
+  return CE_OK;
+}
+
 extern "C" int ce_decode_scores(const int32_t* kv_indptr, const int32_t* kv_indices,
                                 const int32_t* kv_tokens, int64_t kv_capacity, int64_t pool_units,
                                 const int32_t* mode_of_row, const int64_t* rows, int32_t bs,

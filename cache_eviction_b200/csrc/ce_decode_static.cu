@@ -10,10 +10,18 @@
 // still needs such a caller to pass a workspace; this entry point does not.
 //
 // Its scratch is the file-scope array below, CE_DECODE_STATIC_SCRATCH_BYTES
-// long.  Every GPU that loads libce_b200.so holds one copy of it until the
-// process exits.  The entry point checks that the call fits the array, finds
-// the array's device address and hands it to ce_decode_attn_score as the
+// long.  The entry point checks that the call fits the array, finds the
+// array's device address and hands it to ce_decode_attn_score as the
 // workspace; nothing else changes.
+//
+// When the array takes device memory: with lazy module loading (the CUDA 12
+// default, CUDA_MODULE_LOADING=LAZY) the driver places it when this file's
+// module is first used, which is the set-up below (the first call on a
+// device, or a call with bs == 0); with eager loading, when the context is
+// created.  It then stays until the process exits.  The set-up also loads the
+// decode kernels themselves.  A caller that gives the rest of HBM to its pool
+// therefore makes its set-up call first.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -25,28 +33,77 @@ namespace {
 
 // The scratch itself.  In host code this name is only a stand-in for the
 // device array (its address is not a device address); the real address comes
-// from cudaGetSymbolAddress, once per device.
+// from cudaGetSymbolAddress, once per device and context.
 static __device__ __align__(256) unsigned char g_decode_scratch[CE_DECODE_STATIC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-void* g_scratch_ptr[kMaxDevices] = {nullptr};
-std::mutex g_scratch_mu;
 
-// Device address of this device's copy of the scratch, looked up on the
-// first call made with that device current.
+// The device address found at set-up, with the context it belongs to: after
+// cudaDeviceReset the device gets a new primary context (and a new copy of the
+// array), so an address cached for the old one is looked up again.
+struct Slot {
+  void* ptr = nullptr;
+  unsigned long long context = 0;
+};
+Slot g_slot[kMaxDevices];
+std::mutex g_mu;
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current context, or 0 when there is none
+// (or the driver cannot say, in which case every call repeats the set-up).
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    looked_up = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(fn);
+    cudaGetLastError();  // a failed lookup leaves nothing pending for later launches
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of this device's copy of the scratch.  The first call made
+// with a device current (and the first after its context was replaced) runs
+// the set-up: it looks the address up, which places the array under lazy
+// loading, and loads the decode kernels.
 int scratch_address(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return ce::host::fail(CE_ERR_CUDA, "ce_decode_attn_score_static: no current device");
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+    return ce::host::fail_cuda("ce_decode_attn_score_static: no current device");
+  std::lock_guard<std::mutex> lock(g_mu);
+  Slot& slot = g_slot[dev];
+  const unsigned long long ctx = current_context_id();
+  if (!slot.ptr || ctx == 0 || ctx != slot.context) {
     void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
-    if (e != cudaSuccess || !ptr)
-      return ce::host::fail(CE_ERR_CUDA, "ce_decode_attn_score_static: cudaGetSymbolAddress failed");
-    g_scratch_ptr[dev] = ptr;
+    if (cudaGetSymbolAddress(&ptr, g_decode_scratch) != cudaSuccess || !ptr) {
+      slot = Slot{};
+      return ce::host::fail_cuda("ce_decode_attn_score_static: cudaGetSymbolAddress of the static scratch");
+    }
+    const int st = ce::host::decode_prepare_device();
+    if (st != CE_OK) {
+      slot = Slot{};
+      return st;
+    }
+    slot.ptr = ptr;
+    slot.context = current_context_id();  // the lookup made the primary context current
   }
-  *out = g_scratch_ptr[dev];
+  *out = slot.ptr;
   return CE_OK;
 }
 
@@ -62,7 +119,9 @@ extern "C" int ce_decode_attn_score_static(
     int64_t o_sh, float* lse_out, int32_t score_flags, int32_t* err, void* stream) {
   if (score_flags & CE_SCORE_DEFER)
     return ce::host::fail(CE_ERR_ARG, "ce_decode_attn_score_static: deferred scores need a caller workspace");
-  if (bs == 0) return CE_OK;
+  if (bs < 0) return ce::host::fail(CE_ERR_ARG, "ce_decode_attn_score_static: negative batch");
+  void* scratch = nullptr;
+  if (bs == 0) return scratch_address(&scratch);  // set-up only: nothing is launched
   const int64_t need = ce_decode_workspace_bytes(bs, kv_capacity, num_q_heads, num_kv_heads,
                                                  page_size, score_flags);
   if (need < 0) return ce::host::fail(CE_ERR_ARG, "ce_decode_attn_score_static: bad sizes");
@@ -71,7 +130,6 @@ extern "C" int ce_decode_attn_score_static(
                           "ce_decode_attn_score_static: this batch needs more scratch than the "
                           "static maximum (CE_DECODE_STATIC_SCRATCH_BYTES); use "
                           "ce_decode_attn_score with a caller workspace");
-  void* scratch = nullptr;
   const int st = scratch_address(&scratch);
   if (st != CE_OK) return st;
   // Nothing in the scratch has to start at zero: every byte the kernels read

@@ -46,5 +46,10 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
 bool encode_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint32_t cols,
                      uint32_t box_rows);
 
+// Loads every kernel that ce_decode_attn_score launches on the current device
+// and sets their launch attributes, which that entry point otherwise does on
+// its first call (defined in ce_decode.cu).  Returns a CE_* status.
+int decode_prepare_device();
+
 }  // namespace host
 }  // namespace ce

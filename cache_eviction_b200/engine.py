@@ -79,6 +79,7 @@ class RaggedDecodeEngine:
         self.seq_lens_dev = torch.zeros(0, dtype=torch.int64, device=dev)
         self.free_units: list = []
         self.boundary_ms: list = []
+        self.last_batch: Optional[dict] = None
         # The boundary workspace is sized up front for batches of up to
         # `boundary_rows` rows, so no device allocation falls inside the decode
         # loop (a larger batch grows it once).
@@ -221,6 +222,10 @@ class RaggedDecodeEngine:
         end.record()
         res = result.cpu().numpy()   # one readback per boundary batch, as the reference syncs
         self.boundary_ms.append(start.elapsed_time(end))
+        # what this batch was given and returned (the uniforms are the exact
+        # draws of the random rows), for callers that audit or replay it
+        self.last_batch = dict(rows=list(rows), params=params, max_cols=max_cols, uniforms=uniforms,
+                               result=res, freed=freed)
         fr = None
         for i, r in enumerate(rows):
             row = self.rows[r]

@@ -183,13 +183,19 @@ int ce_decode_scores(const int32_t* kv_indptr, const int32_t* kv_indices,
  * memory when they decode (an engine that gave all HBM to its KV pool, a host
  * that forbids allocations after start-up, a global-mode graph capture):
  * identical to ce_decode_attn_score except that its scratch is a static
- * device array of CE_DECODE_STATIC_SCRATCH_BYTES inside the library, held by
- * every GPU that loads the library until the process exits, and that
+ * device array of CE_DECODE_STATIC_SCRATCH_BYTES inside the library, and that
  * CE_SCORE_DEFER is refused (CE_ERR_ARG).
- *   - A call whose ce_decode_workspace_bytes() exceeds that maximum returns
+ *   - Set-up: the first call on a device (and the first after cudaDeviceReset
+ *     replaced its context) looks up the array's device address
+ *     (cudaGetSymbolAddress) and loads the decode kernels.  A call with
+ *     bs == 0 does only this and launches nothing.  Under lazy module loading
+ *     (the CUDA 12 default) the array's 32 MiB are placed on the device at
+ *     this point, so make the set-up call before handing the rest of HBM to a
+ *     pool, and before any stream capture; the array then stays until the
+ *     process exits (with eager loading it is placed when the context is
+ *     created).  Calls after the set-up take no device memory.
+ *   - A call whose ce_decode_workspace_bytes() exceeds the maximum returns
  *     CE_ERR_WORKSPACE and launches nothing.
- *   - The first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress); make that first call before any stream capture.
  *   - Every call on a device shares the one array: calls that may overlap on
  *     the GPU (different streams without ordering) race and must be
  *     serialised by the caller.  No part of the array needs to start at zero.
