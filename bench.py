@@ -334,37 +334,72 @@ def run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
     return B * e2e_steps / (e2e_ms * 1e-3)
 
 
+def paired_segments(run_a, run_b, steps, seg):
+    """Alternate `seg`-step segments of two passes (a then b, then b then a,
+    ...) until each has run `steps` steps, as the reference's paired off/on
+    timing does (code/cache_eviction/sglang_timing.py:69-87): box drift then
+    falls on both sides alike.  Each segment is bracketed by CUDA events on
+    the current stream.  Returns (ms of a, ms of b, pairs)."""
+    import torch
+    done, i, marks = 0, 0, []
+    while done < steps:
+        n = min(seg, steps - done)
+        order = (("a", run_a), ("b", run_b)) if i % 2 == 0 else (("b", run_b), ("a", run_a))
+        for name, fn in order:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn(n)
+            e1.record()
+            marks.append((i, name, e0, e1))
+        done += n
+        i += 1
+    torch.cuda.synchronize()
+    pairs = {}
+    for i, name, e0, e1 in marks:
+        pairs.setdefault(i, {})[name] = e0.elapsed_time(e1)
+    ms_a = sum(p["a"] for p in pairs.values())
+    ms_b = sum(p["b"] for p in pairs.values())
+    return ms_a, ms_b, list(pairs.values())
+
+
 def run_no_score(args, specs, steps_total, world, rank, group, device, q, out, sinks, scale,
                  after_layer, barrier, max_over_ranks):
-    """The device-resident pass again from a fresh state with H2O scoring off for
-    every row (mode NONE) and the same boundaries, so the resident KV matches the
-    scored pass step for step: the full-cache decode rate at the same resident
-    size, which the scored rate is compared against."""
+    """Scored against unscored decode at the same resident KV, in alternating
+    segments: two engines from the same fresh state, one with H2O scoring off
+    for every row (mode NONE, no score work at all) and the same boundaries, so
+    the resident KV matches step for step.  The unscored rate is the
+    full-cache decode rate at the same resident size that the north star
+    compares the scored rate with."""
     import torch
     from cache_eviction_b200 import capi
     B = len(specs)
-    eng = build_engine(specs, steps_total, world, rank, group, device)
-    eng.mode.fill_(capi.CE_MODE_NONE)
-    eng.score_flags = 0          # a plain full-cache decode: no score work or launches
-    for _ in range(args.warmup):
-        eng.step(q, out, sinks, scale, after_layer)
+    eng_s = build_engine(specs, steps_total, world, rank, group, device)
+    eng_u = build_engine(specs, steps_total, world, rank, group, device)
+    eng_u.mode.fill_(capi.CE_MODE_NONE)
+    eng_u.score_flags = 0        # a plain full-cache decode: no score work or launches
+    for eng in (eng_s, eng_u):
+        for _ in range(args.warmup):
+            eng.step(q, out, sinks, scale, after_layer)
+
+    def runner(eng):
+        def fn(n):
+            for _ in range(n):
+                eng.step(q, out, sinks, scale, after_layer)
+            eng.join_scores()
+        return fn
+
     barrier()
     torch.cuda.synchronize()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(args.steps):
-        eng.step(q, out, sinks, scale, after_layer)
-    eng.join_scores()
-    e2.record()
-    torch.cuda.synchronize()
+    ms_s, ms_u, pairs = paired_segments(runner(eng_s), runner(eng_u), args.steps, seg=16)
     barrier()
-    ms = max_over_ranks(s2.elapsed_time(e2))
-    del eng
+    ms_s, ms_u = max_over_ranks(ms_s), max_over_ranks(ms_u)
+    del eng_s, eng_u
     torch.cuda.empty_cache()
-    return B * args.steps / (ms * 1e-3)
+    return {"value": B * args.steps / (ms_u * 1e-3), "scored_value": B * args.steps / (ms_s * 1e-3),
+            "scored_over_no_score": ms_u / ms_s, "pairs": len(pairs), "segment_steps": 16}
 
 
-def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, steps=2048, warmup=8):
+def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, steps=2048, warmup=8, seg=64):
     """BASELINE config 4's decode phase: one sequence after an 80,000-token
     prompt, per-head H2O (head_sum) with 512 prefix + 4,096 recent + 24,064
     scored tokens (28,672 resident after each boundary), 12 full layers of
@@ -372,10 +407,11 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
     decode steps including the boundary at 81,920 tokens.  Each step without a
     boundary replays one CUDA graph (position advance, CSR fill, the 12 fused
     decode layers); the boundary step runs eagerly through engine.step.  The
-    same pass with scoring off at the same resident KV gives the full-cache
-    rate it is compared against.  Algorithmic bytes per step: K + V of every
-    resident token (2,048 B at 8 KV heads) + Q/O + the page-score
-    read-modify-write, per layer."""
+    same steps with scoring off at the same resident KV (a second engine, the
+    full-cache rate) are timed in alternating `seg`-step segments with the
+    scored ones.  Algorithmic bytes per step: K + V of every resident token
+    (2,048 B at 8 KV heads) + Q/O + the page-score read-modify-write, per
+    layer."""
     import torch
     from cache_eviction_b200 import capi, tp
     from cache_eviction_b200.policy import EvictionConfig
@@ -388,7 +424,7 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
     q = torch.randn((LAYERS, 1, H, D), generator=gen, device=device).to(torch.bfloat16)
     out = torch.empty((LAYERS, 1, H, D), dtype=torch.bfloat16, device=device)
     sinks = [torch.randn(H, generator=gen, device=device) for _ in range(LAYERS)]
-    res = {}
+    passes = {}
     for scored in (True, False):
         eng = build_engine(specs, warmup + steps, world, rank, group, device)
         if not scored:
@@ -411,36 +447,46 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
             eng.join_scores()      # a capture ends with every forked stream joined
         eng.new_score_events()
         torch.cuda.synchronize()
+        passes[scored] = dict(eng=eng, graph=graph, resident=[])
+
+    def runner(ps):
+        eng, graph = ps["eng"], ps["graph"]
         row = eng.rows[eng.active[0]]
-        resident = []
-        barrier()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(steps):
-            if eng.due():
-                eng.step(q, out, sinks, scale)
-            else:
-                row.n += 1       # the host side of engine.advance
-                graph.replay()
-            resident.append(eng.resident_tokens(eng.active[0]))
-        eng.join_scores()
-        end.record()
-        torch.cuda.synchronize()
-        barrier()
-        ms = max_over_ranks(start.elapsed_time(end))
-        eng.check_errors()
-        bounds = len(eng.rows[eng.active[0]].events)
-        del graph, eng
-        torch.cuda.empty_cache()
-        tok = statistics.mean(resident)
+
+        def fn(n):
+            for _ in range(n):
+                if eng.due():
+                    eng.step(q, out, sinks, scale)
+                else:
+                    row.n += 1       # the host side of engine.advance
+                    graph.replay()
+                ps["resident"].append(eng.resident_tokens(eng.active[0]))
+            eng.join_scores()
+        return fn
+
+    barrier()
+    torch.cuda.synchronize()
+    ms_s, ms_u, pairs = paired_segments(runner(passes[True]), runner(passes[False]), steps, seg)
+    barrier()
+    ms = {True: max_over_ranks(ms_s), False: max_over_ranks(ms_u)}
+    res = {}
+    for scored in (True, False):
+        ps = passes[scored]
+        ps["eng"].check_errors()
+        bounds = len(ps["eng"].rows[ps["eng"].active[0]].events)
+        tok = statistics.mean(ps["resident"])
         nbytes = LAYERS * (tok * G * D * 2 * 2 + 2 * H * D * 2 + (-(-tok // PAGE)) * G * 8 * scored)
         res["scored" if scored else "no_score"] = {
-            "tok_s": steps / (ms * 1e-3), "ms_per_step": ms / steps, "resident_tokens_mean": tok,
-            "gbs": nbytes / (ms / steps * 1e-3) / 1e9, "boundaries": bounds}
+            "tok_s": steps / (ms[scored] * 1e-3), "ms_per_step": ms[scored] / steps,
+            "resident_tokens_mean": tok, "gbs": nbytes / (ms[scored] / steps * 1e-3) / 1e9,
+            "boundaries": bounds}
+    del passes
+    torch.cuda.empty_cache()
     peak, kind = measured_peak_hbm()
     res["scored_over_no_score"] = res["scored"]["tok_s"] / res["no_score"]["tok_s"]
     res["hbm_frac_scored"] = res["scored"]["gbs"] / peak
     res["peak_kind"] = kind
+    res["timing"] = f"alternating {seg}-step segments of the scored and unscored passes, {len(pairs)} pairs"
     return res
 
 
@@ -870,10 +916,13 @@ def main():
                   "boundary_rows": n_bound_rows},
         "resident_tokens_mean": statistics.mean(tokens_resident),
         "no_score_same_resident": None if no_score is None else {
-                                   "value": no_score, "unit": UNIT,
-                                   "scored_over_no_score": value / no_score,
-                                   "what": "same rows, steps and boundaries with H2O scoring off "
-                                           "(full-cache decode at the same resident KV)"},
+                                   "value": no_score["value"], "unit": UNIT,
+                                   "scored_value": no_score["scored_value"],
+                                   "scored_over_no_score": no_score["scored_over_no_score"],
+                                   "pairs": no_score["pairs"], "segment_steps": no_score["segment_steps"],
+                                   "what": "scored and unscored engines (same rows, steps and boundaries, "
+                                           "H2O scoring off in the second: full-cache decode at the same "
+                                           "resident KV) timed in alternating segments"},
         "evict_config5": evict5,
         "select_token_config5": select1,
         "evict_token_config5": evict1,

@@ -561,25 +561,192 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
 }
 
-// ---- combine: records of a sequence + sink -> output, lse ----------------------
+// ---- combine: records of a sequence + sink -> output, lse, page scores --------
+//
+// One task per (sequence b, KV head g, chunk c): the chunks of a (b, g) split
+// its eight query heads' output merges and its page scoring between them, so
+// a small batch (one sequence spread over every attention CTA) still fills the
+// GPU.  Every task first rebuilds the eight heads' normalisers from the
+// sequence's record slots: one pass in which thread t merges slots t, t+256,
+// ... (each slot's eight maxima and sums are two pairs of 16-byte loads), then
+// a shared-memory reduction per head, with the sink folded in (the normaliser
+// of SGLang's stage 2 and of runtime:179-188).
 constexpr int CB_THREADS = 256;
-constexpr int MAX_SLOTS = 160 * NCW;   // (record, sub-part) slots one sequence can span
+constexpr int CB_SLOT_BATCH = 4;   // slots a thread loads before merging them
+constexpr int CB_MAX_CHUNKS = 64;
 
 struct CombineParams {
   Params a;
-  int grid;    // CTAs the attention kernel was launched with
+  int grid;     // CTAs the attention kernel was launched with
   int P;
-  int defer;   // CE_SCORE_DEFER: keep the normalisers in lse2, add no scores here
+  int defer;    // CE_SCORE_DEFER: keep the normalisers in lse2, add no scores here
+  int chunks;   // tasks per (sequence, KV head)
 };
 
-// Add sequence b's page masses for KV head g into scores[g, unit]:
+__device__ __forceinline__ void merge_ml(float& m, float& l, float m2, float l2) {
+  if (m2 == -INFINITY) return;
+  const float mn = fmaxf(m, m2);
+  l = l * exp2f(m - mn) + l2 * exp2f(m2 - mn);
+  m = mn;
+}
+
+// Record slots of sequence b for KV head g: slot i is sub-part i % subs of
+// record k0 + i / subs (an attention CTA's warps over G heads: NCW / G of them
+// per head).
+struct SeqSlots {
+  int b, g, subs, k0, nslots;
+  int64_t S, grid;
+  __device__ const float* rec(const Params& p, int i) const {
+    return p.rec + static_cast<int64_t>(b + k0 + i / subs) * REC_FLOATS;
+  }
+  __device__ int vrow(int i, int G) const { return ((i % subs) * G + g) * GROUP; }  // + head row r
+  __device__ bool live(int i) const { return cta_has_work(k0 + i / subs, S, grid); }
+};
+
+// sh_l2[r] = log2 normaliser of query head g*8 + r (record maxima, sums and
+// the sink).  sh_m / sh_l: [GROUP][CB_THREADS] scratch.
+__device__ void group_normalisers(const Params& p, const SeqSlots& q, float* sh_m, float* sh_l,
+                                  float* sh_l2) {
+  const int tid = threadIdx.x, G = p.G;
+  float m[GROUP], l[GROUP];
+#pragma unroll
+  for (int r = 0; r < GROUP; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+  }
+  for (int i0 = tid; i0 < q.nslots; i0 += CB_THREADS * CB_SLOT_BATCH) {
+    float4 ma[CB_SLOT_BATCH], mb[CB_SLOT_BATCH], la[CB_SLOT_BATCH], lb[CB_SLOT_BATCH];
+#pragma unroll
+    for (int u = 0; u < CB_SLOT_BATCH; ++u) {
+      const int i = i0 + u * CB_THREADS;
+      ma[u] = mb[u] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      la[u] = lb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < q.nslots && q.live(i)) {
+        const float4* st = reinterpret_cast<const float4*>(q.rec(p, i) + REC_ROWS * D + q.vrow(i, G));
+        ma[u] = st[0];
+        mb[u] = st[1];
+        la[u] = st[REC_ROWS / 4];
+        lb[u] = st[REC_ROWS / 4 + 1];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < CB_SLOT_BATCH; ++u) {
+      merge_ml(m[0], l[0], ma[u].x, la[u].x);
+      merge_ml(m[1], l[1], ma[u].y, la[u].y);
+      merge_ml(m[2], l[2], ma[u].z, la[u].z);
+      merge_ml(m[3], l[3], ma[u].w, la[u].w);
+      merge_ml(m[4], l[4], mb[u].x, lb[u].x);
+      merge_ml(m[5], l[5], mb[u].y, lb[u].y);
+      merge_ml(m[6], l[6], mb[u].z, lb[u].z);
+      merge_ml(m[7], l[7], mb[u].w, lb[u].w);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < GROUP; ++r) {
+    sh_m[r * CB_THREADS + tid] = m[r];
+    sh_l[r * CB_THREADS + tid] = l[r];
+  }
+  __syncthreads();
+  // warp r reduces head r over the 256 partial states
+  const int warp = tid >> 5, lane = tid & 31;
+  float mw = -INFINITY, lw = 0.f;
+#pragma unroll
+  for (int k = 0; k < CB_THREADS / 32; ++k)
+    merge_ml(mw, lw, sh_m[warp * CB_THREADS + k * 32 + lane], sh_l[warp * CB_THREADS + k * 32 + lane]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, mw, o), l2 = __shfl_xor_sync(0xffffffffu, lw, o);
+    merge_ml(mw, lw, m2, l2);
+  }
+  if (lane == 0) {
+    const int h = q.g * GROUP + warp;
+    const float sink2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
+    const float M = fmaxf(mw, sink2);
+    float den = 0.f;
+    if (M != -INFINITY) {
+      den = (mw == -INFINITY) ? 0.f : lw * exp2f(mw - M);
+      if (p.sinks) den += exp2f(sink2 - M);
+    }
+    sh_l2[warp] = (M == -INFINITY) ? -INFINITY : M + log2f(den);
+  }
+  __syncthreads();
+}
+
+// Outputs of the query heads r = c, c + C, ... (r < 8) of KV head g: each a
+// sum over the slots of 2^(m_i - L2) O_i.  The block's threads split as heads
+// x 16 dimension quads x slot groups; partial sums meet in shared memory.
+__device__ void group_outputs(const Params& p, const SeqSlots& q, int c, int C, const float* sh_l2,
+                              float4* red) {
+  const int nh = (c < GROUP) ? (GROUP - 1 - c) / C + 1 : 0;
+  if (nh == 0) return;
+  const int nhr = nh <= 1 ? 1 : nh <= 2 ? 2 : nh <= 4 ? 4 : 8;
+  const int tph = CB_THREADS / nhr;        // threads per head
+  const int sgn = tph / 16;                // slot groups per head
+  const int tid = threadIdx.x, hh = tid / tph, lt = tid % tph, dq = lt & 15, sg = lt >> 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (hh < nh) {
+    const int r = c + hh * C;
+    const float L2 = sh_l2[r];
+    constexpr int AB = 4;
+    for (int i0 = sg; i0 < q.nslots; i0 += sgn * AB) {
+      float w[AB];
+      float4 o[AB];
+#pragma unroll
+      for (int u = 0; u < AB; ++u) {
+        const int i = i0 + u * sgn;
+        w[u] = 0.f;
+        o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < q.nslots && q.live(i) && L2 != -INFINITY) {
+          const float* rc = q.rec(p, i);
+          const int v = q.vrow(i, p.G) + r;
+          const float mk = rc[REC_ROWS * D + v];
+          if (mk != -INFINITY) {
+            w[u] = exp2f(mk - L2);
+            o[u] = reinterpret_cast<const float4*>(rc + v * D)[dq];
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < AB; ++u) {
+        if (w[u] != 0.f) {
+          acc.x += w[u] * o[u].x;
+          acc.y += w[u] * o[u].y;
+          acc.z += w[u] * o[u].z;
+          acc.w += w[u] * o[u].w;
+        }
+      }
+    }
+  }
+  red[tid] = acc;
+  __syncthreads();
+  if (tid < nh * 16) {
+    const int h2 = tid >> 4, d2 = tid & 15;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < sgn; ++k) {
+      const float4 v = red[h2 * tph + k * 16 + d2];
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    const int h = q.g * GROUP + c + h2 * C;
+    store_out(p, q.b, h, d2 * 4 + 0, s.x);
+    store_out(p, q.b, h, d2 * 4 + 1, s.y);
+    store_out(p, q.b, h, d2 * 4 + 2, s.z);
+    store_out(p, q.b, h, d2 * 4 + 3, s.w);
+  }
+}
+
+// Add pages [lo, hi) of sequence b's page masses for KV head g into scores[g, unit]:
 //   SUM: sum_h 2^(page_lse - LSE_h)   MAX: sum_t max_h 2^(s_t,h - LSE_h)
-// L2 holds the group's 8 log2 normalisers.  Each thread takes 4 pages per
+// L2s holds the group's 8 log2 normalisers.  Each thread takes 4 pages per
 // round and issues all their loads before any store.
-__device__ void score_pages(const Params& p, int b, int g, int mode, int P, const float* L2s) {
+__device__ void score_pages(const Params& p, int b, int g, int mode, int P, const float* L2s, int lo,
+                            int hi) {
   const int H = p.H;
   const int tokens = seq_tokens(p, b, P);
   const int npages = (tokens + P - 1) / P;
+  hi = min(hi, npages);
   const int64_t ip = p.kv_indptr[b];
   float L2[GROUP];
 #pragma unroll
@@ -589,14 +756,14 @@ __device__ void score_pages(const Params& p, int b, int g, int mode, int P, cons
   const float* __restrict__ ul = p.ul;
   float* __restrict__ sc = p.scores + g * p.score_sg;
   constexpr int BATCH = 4;
-  for (int j0 = threadIdx.x * BATCH; j0 < npages; j0 += CB_THREADS * BATCH) {
+  for (int j0 = lo + threadIdx.x * BATCH; j0 < hi; j0 += CB_THREADS * BATCH) {
     int unit[BATCH];
     float contrib[BATCH], old[BATCH];
 #pragma unroll
     for (int q = 0; q < BATCH; ++q) {
       const int jj = j0 + q;
       unit[q] = -1;
-      if (jj < npages && ip + jj < p.kv_capacity) unit[q] = kvi[ip + jj];
+      if (jj < hi && ip + jj < p.kv_capacity) unit[q] = kvi[ip + jj];
     }
 #pragma unroll
     for (int q = 0; q < BATCH; ++q) {
@@ -633,7 +800,7 @@ __device__ void score_pages(const Params& p, int b, int g, int mode, int P, cons
 #pragma unroll
     for (int q = 0; q < BATCH; ++q) {
       const int jj = j0 + q;
-      if (jj >= npages) continue;
+      if (jj >= hi) continue;
       if (unit[q] < 0 || unit[q] >= p.pool_units) {
         if (ip + jj < p.kv_capacity) flag_error(p.err, CE_EW_INDEX);
         continue;
@@ -644,168 +811,84 @@ __device__ void score_pages(const Params& p, int b, int g, int mode, int P, cons
   }
 }
 
-// One task per (sequence b, group of 8 query heads): warp w handles head
-// hc*8 + w.  Its lanes first reduce the head's max and sum over the record
-// slots (plus the sink), then split as 8 dim groups x 4 slot groups to
-// accumulate the 64 outputs, so a sequence spread over many CTAs costs a few
-// rounds of independent loads rather than one chain per slot.
+__device__ __forceinline__ int score_mode_of(const Params& p, int b, int P) {
+  int mode = (p.mode_of_row && p.scores && p.ul) ? seq_mode(p, b) : CE_MODE_NONE;
+  if (mode == CE_MODE_MAX && P > 1 && !p.tl) mode = CE_MODE_NONE;
+  return (mode == CE_MODE_SUM || mode == CE_MODE_MAX) ? mode : CE_MODE_NONE;
+}
+
+// Chunk c of C of sequence b's pages.
+__device__ __forceinline__ void chunk_pages(const Params& p, int b, int P, int c, int C, int& lo, int& hi) {
+  const int npages = (seq_tokens(p, b, P) + P - 1) / P;
+  const int per = (npages + C - 1) / C;
+  lo = min(npages, c * per);
+  hi = min(npages, lo + per);
+}
+
 __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams cp) {
   const Params& p = cp.a;
-  const int bs = p.bs, H = p.H, G = p.G;
-  const int subs = NCW / G;
+  const int bs = p.bs, H = p.H, G = p.G, C = cp.chunks;
   const int64_t S = p.prefix[bs];
   const int64_t grid = eff_grid(S, cp.grid);
   const int hgroups = H / GROUP;
-  const int64_t ntasks = static_cast<int64_t>(bs) * hgroups;
-  __shared__ float wts[GROUP][MAX_SLOTS];
+  const int64_t ntasks = static_cast<int64_t>(bs) * hgroups * C;
+  __shared__ float sh_m[GROUP * CB_THREADS], sh_l[GROUP * CB_THREADS];
+  __shared__ float4 red[CB_THREADS];
   __shared__ float sh_l2[GROUP];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int64_t task = blockIdx.x; task < ntasks; task += gridDim.x) {
-    const int b = static_cast<int>(task / hgroups), hc = static_cast<int>(task % hgroups);
+    const int c = static_cast<int>(task % C);
+    const int64_t bg = task / C;
+    const int b = static_cast<int>(bg / hgroups), hc = static_cast<int>(bg % hgroups);
     const int64_t pre = p.prefix[b], n = p.prefix[b + 1] - pre;
     if (n <= 0) continue;   // empty sequences were written by the attention kernel
-    const int k0 = cta_of_stage(pre, S, grid), k1 = cta_of_stage(pre + n - 1, S, grid);
-    const int nslots = (k1 - k0 + 1) * subs;
-    const int h = hc * GROUP + warp, g = h / GROUP, r = h % GROUP;
-    auto rec_of = [&](int i) -> const float* {
-      return p.rec + static_cast<int64_t>(b + k0 + i / subs) * REC_FLOATS;
-    };
-    auto vrow = [&](int i) -> int { return ((i % subs) * G + g) * 8 + r; };
-    auto live = [&](int i) -> bool { return cta_has_work(k0 + i / subs, S, grid); };
-    // One pass over the slots: each lane keeps an online (max, sum) of its
-    // slots and caches their maxima in wts, from which the weights are formed
-    // once the normaliser is known (no second or third read of the records).
-    const bool fits = nslots <= MAX_SLOTS;
-    float m = -INFINITY, l = 0.f;
-    // Four slots of a lane per batch: their loads are issued together (a
-    // sequence spread over every CTA has ~150 slots per head).
-    constexpr int SB = 4;
-    for (int i0 = lane; i0 < nslots; i0 += 32 * SB) {
-      float mk[SB], lk[SB];
-#pragma unroll
-      for (int u = 0; u < SB; ++u) {
-        const int i = i0 + 32 * u;
-        mk[u] = -INFINITY;
-        lk[u] = 0.f;
-        if (i < nslots && live(i)) {
-          const float* st = rec_of(i) + REC_ROWS * D;
-          mk[u] = st[vrow(i)];
-          lk[u] = st[REC_ROWS + vrow(i)];
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < SB; ++u) {
-        const int i = i0 + 32 * u;
-        if (i >= nslots) continue;
-        if (fits) wts[warp][i] = mk[u];
-        if (mk[u] != -INFINITY) {
-          const float mn = fmaxf(m, mk[u]);
-          l = l * exp2f(m - mn) + lk[u] * exp2f(mk[u] - mn);
-          m = mn;
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
-      const float mn = fmaxf(m, m2);
-      if (mn != -INFINITY) {
-        l = l * exp2f(m - mn) + l2 * exp2f(m2 - mn);
-        m = mn;
-      }
-    }
-    const float sink2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
-    const float M = fmaxf(m, sink2);
-    float den = 0.f;
-    if (M != -INFINITY) {
-      den = (m == -INFINITY) ? 0.f : l * exp2f(m - M);
-      if (p.sinks) den += exp2f(sink2 - M);
-    }
-    const float L2 = (M == -INFINITY) ? -INFINITY : M + log2f(den);
-    auto weight = [&](int i) -> float {
-      if (L2 == -INFINITY || !live(i)) return 0.f;
-      const float mk = rec_of(i)[REC_ROWS * D + vrow(i)];
-      return mk == -INFINITY ? 0.f : exp2f(mk - L2);
-    };
-    __syncwarp();
-    if (fits)
-      for (int i = lane; i < nslots; i += 32) {
-        const float mk = wts[warp][i];
-        wts[warp][i] = (L2 == -INFINITY || mk == -INFINITY) ? 0.f : exp2f(mk - L2);
-      }
-    __syncwarp();
-    // lane = dim group (8 dims) x slot group (4): sg = lane % 4, dg = lane / 4.
-    // Eight slots of a lane per batch, their record rows loaded together.
-    const int sg = lane & 3, dg = lane >> 2;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    constexpr int AB = 8;
-    for (int i0 = sg; i0 < nslots; i0 += 4 * AB) {
-      float w[AB];
-      float4 a[AB], c[AB];
-#pragma unroll
-      for (int u = 0; u < AB; ++u) {
-        const int i = i0 + 4 * u;
-        w[u] = i < nslots ? (fits ? wts[warp][i] : weight(i)) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < AB; ++u) {
-        const int i = i0 + 4 * u;
-        a[u] = c[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (w[u] != 0.f) {
-          const float4* src = reinterpret_cast<const float4*>(rec_of(i) + vrow(i) * D + dg * 8);
-          a[u] = src[0];
-          c[u] = src[1];
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < AB; ++u) {
-        acc[0] += w[u] * a[u].x; acc[1] += w[u] * a[u].y; acc[2] += w[u] * a[u].z; acc[3] += w[u] * a[u].w;
-        acc[4] += w[u] * c[u].x; acc[5] += w[u] * c[u].y; acc[6] += w[u] * c[u].z; acc[7] += w[u] * c[u].w;
-      }
-    }
-#pragma unroll
-    for (int d = 0; d < 8; ++d) {
-      acc[d] += __shfl_xor_sync(0xffffffffu, acc[d], 1);
-      acc[d] += __shfl_xor_sync(0xffffffffu, acc[d], 2);
-    }
-    if (sg == 0) {
-#pragma unroll
-      for (int d = 0; d < 8; ++d) store_out(p, b, h, dg * 8 + d, acc[d]);
-    }
-    if (lane == 0) {
-      sh_l2[warp] = L2;
+    SeqSlots q;
+    q.b = b;
+    q.g = hc;
+    q.subs = NCW / G;
+    q.S = S;
+    q.grid = grid;
+    q.k0 = cta_of_stage(pre, S, grid);
+    q.nslots = (cta_of_stage(pre + n - 1, S, grid) - q.k0 + 1) * q.subs;
+    group_normalisers(p, q, sh_m, sh_l, sh_l2);
+    group_outputs(p, q, c, C, sh_l2, red);
+    if (c == 0 && threadIdx.x < GROUP) {
+      const int h = hc * GROUP + threadIdx.x;
+      const float L2 = sh_l2[threadIdx.x];
       if (p.lse_out) p.lse_out[static_cast<int64_t>(b) * H + h] = L2 * LN2;
       if (cp.defer) p.lse2[static_cast<int64_t>(b) * H + h] = L2;
     }
-    if (cp.defer) continue;   // score_kernel adds the page masses later
-    __syncthreads();
-    // The task's 8 heads are exactly KV head g's group: add this sequence's
-    // page masses for KV head g (pages in independent batches of 4).
-    int mode = (p.mode_of_row && p.scores && p.ul) ? seq_mode(p, b) : CE_MODE_NONE;
-    if (mode == CE_MODE_MAX && cp.P > 1 && !p.tl) mode = CE_MODE_NONE;
-    if (mode == CE_MODE_SUM || mode == CE_MODE_MAX)
-      score_pages(p, b, hc, mode, cp.P, sh_l2);
+    if (!cp.defer) {   // else score_kernel adds the page masses later
+      const int mode = score_mode_of(p, b, cp.P);
+      if (mode != CE_MODE_NONE) {
+        int lo, hi;
+        chunk_pages(p, b, cp.P, c, C, lo, hi);
+        score_pages(p, b, hc, mode, cp.P, sh_l2, lo, hi);
+      }
+    }
     __syncthreads();
   }
 }
 
 // The page masses of a deferred decode (CE_SCORE_DEFER): the same work as
-// the tail of combine_kernel, one task per (sequence, group of 8 query
-// heads), from the normalisers combine_kernel left in lse2.  Small enough to
-// run beside the next layer's attention kernel on another stream.
+// the tail of combine_kernel, one task per (sequence, KV head, chunk), from
+// the normalisers combine_kernel left in lse2.  Small enough to run beside
+// the next layer's attention kernel on another stream.
 __global__ void __launch_bounds__(CB_THREADS) score_kernel(const CombineParams cp) {
   const Params& p = cp.a;
-  const int hgroups = p.H / GROUP;
-  const int64_t ntasks = static_cast<int64_t>(p.bs) * hgroups;
+  const int hgroups = p.H / GROUP, C = cp.chunks;
+  const int64_t ntasks = static_cast<int64_t>(p.bs) * hgroups * C;
   __shared__ float sh_l2[GROUP];
   for (int64_t task = blockIdx.x; task < ntasks; task += gridDim.x) {
-    const int b = static_cast<int>(task / hgroups), hc = static_cast<int>(task % hgroups);
-    int mode = (p.mode_of_row && p.scores && p.ul) ? seq_mode(p, b) : CE_MODE_NONE;
-    if (mode == CE_MODE_MAX && cp.P > 1 && !p.tl) mode = CE_MODE_NONE;
-    if (seq_tokens(p, b, cp.P) <= 0 || (mode != CE_MODE_SUM && mode != CE_MODE_MAX)) continue;
+    const int c = static_cast<int>(task % C);
+    const int64_t bg = task / C;
+    const int b = static_cast<int>(bg / hgroups), hc = static_cast<int>(bg % hgroups);
+    const int mode = score_mode_of(p, b, cp.P);
+    if (seq_tokens(p, b, cp.P) <= 0 || mode == CE_MODE_NONE) continue;
     if (threadIdx.x < GROUP) sh_l2[threadIdx.x] = p.lse2[static_cast<int64_t>(b) * p.H + hc * GROUP + threadIdx.x];
     __syncthreads();
-    score_pages(p, b, hc, mode, cp.P, sh_l2);
+    int lo, hi;
+    chunk_pages(p, b, cp.P, c, C, lo, hi);
+    score_pages(p, b, hc, mode, cp.P, sh_l2, lo, hi);
     __syncthreads();
   }
 }
@@ -819,6 +902,16 @@ using namespace ce::decode;
 namespace {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Tasks per (sequence, KV head) of the combine and score kernels: enough for
+// about two blocks per SM when the batch alone would leave SMs idle (a
+// batch-1 decode has one task per KV head otherwise).
+int combine_chunks(int bs, int H, int sms) {
+  const int64_t base = static_cast<int64_t>(bs) * (H / GROUP);
+  if (base <= 0) return 1;
+  const int64_t c = (2LL * sms + base - 1) / base;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(c, CB_MAX_CHUNKS)));
+}
 
 struct DecodeLayout {
   size_t prefix, lse2, rec, ul, tl, total;
@@ -935,12 +1028,12 @@ extern "C" int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh, c
   }
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("attn_kernel launch");
   const bool defer = (score_flags & CE_SCORE_DEFER) != 0;
-  CombineParams cp{p, grid, page_size, defer ? 1 : 0};
+  CombineParams cp{p, grid, page_size, defer ? 1 : 0, combine_chunks(bs, num_q_heads, grid)};
   // A deferred decode's page scores run beside the next layer's attention
   // kernel (195 KB of shared memory per CTA): keep SMs at the largest carveout.
   if (defer && !host::set_max_shared_carveout(combine_kernel)) return host::fail(CE_ERR_CUDA, "carveout attr");
-  const int cb_grid = static_cast<int>(
-      std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP), 4LL * grid)));
+  const int cb_grid = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP) * cp.chunks, 4LL * grid)));
   combine_kernel<<<cb_grid, CB_THREADS, 0, st>>>(cp);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("combine_kernel launch");
   return CE_OK;
@@ -994,10 +1087,10 @@ extern "C" int ce_decode_scores(const int32_t* kv_indptr, const int32_t* kv_indi
   p.ul = reinterpret_cast<float*>(ws + L.ul);
   p.tl = ((score_flags & 2) && page_size > 1) ? reinterpret_cast<float*>(ws + L.tl) : nullptr;
   p.err = err;
-  CombineParams cp{p, grid, page_size, 1};
+  CombineParams cp{p, grid, page_size, 1, combine_chunks(bs, num_q_heads, grid)};
   if (!host::set_max_shared_carveout(score_kernel)) return host::fail(CE_ERR_CUDA, "carveout attr");
-  const int sc_grid = static_cast<int>(
-      std::max<int64_t>(1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP), 2LL * grid)));
+  const int sc_grid = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP) * cp.chunks, 2LL * grid)));
   score_kernel<<<sc_grid, CB_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(cp);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("score_kernel launch");
   return CE_OK;

@@ -251,20 +251,11 @@ class RaggedDecodeEngine:
                      self.seq_lens_dev, self.P, self.kv_indptr[:bs + 1], self.kv_indices,
                      self.kv_tokens[:bs], self.err)
 
-    def decode_layer(self, layer: int, q: torch.Tensor, out: torch.Tensor, sinks, scale: float,
-                     score_flags: Optional[int] = None):
-        bs = len(self.active)
-        score_flags = self.score_flags if score_flags is None else score_flags
-        if not (self.overlap_scores and score_flags & 3 and bs):
-            return kernels.decode_attn_score(
-                q, self.k[layer], self.v[layer], self.kv_indptr[:bs + 1], self.kv_indices,
-                self.kv_tokens[:bs], scale, self.P, sinks=sinks, mode_of_row=self.mode,
-                rows=self.rows_dev, scores=self.scores[layer], zero_new=True, out=out,
-                score_flags=score_flags, err=self.err)
-        # Attention and outputs on the current stream; this layer's page scores
-        # on the score stream once they are done, overlapping the next layer.
-        # Workspace k is reused two layers later, after its scores have run.
-        k = layer % 2
+    def _decode_workspace(self, k: int, bs: int, score_flags: int) -> torch.Tensor:
+        """Decode workspace k of this engine (k = layer % 2 with overlap_scores,
+        else 0), grown when the batch or the CSR capacity grew.  Each engine
+        owns its workspaces, so a CUDA graph captured from one engine never
+        depends on a buffer that another engine may regrow."""
         key = (bs, self.kv_indices.numel(), score_flags)
         if self._ws_need[0] != key:      # the same for every layer of a step
             self._ws_need = (key, kernels.decode_workspace_bytes(bs, key[1], self.H, self.G, self.P,
@@ -273,7 +264,24 @@ class RaggedDecodeEngine:
         if self._dec_ws[k] is None or self._dec_ws[k].numel() < need:
             self.join_scores()
             self._dec_ws[k] = torch.empty(need, dtype=torch.uint8, device=self.device)
-        ws = self._dec_ws[k]
+        return self._dec_ws[k]
+
+    def decode_layer(self, layer: int, q: torch.Tensor, out: torch.Tensor, sinks, scale: float,
+                     score_flags: Optional[int] = None):
+        bs = len(self.active)
+        score_flags = self.score_flags if score_flags is None else score_flags
+        if not (self.overlap_scores and score_flags & 3 and bs):
+            ws = self._decode_workspace(0, bs, score_flags) if bs else None
+            return kernels.decode_attn_score(
+                q, self.k[layer], self.v[layer], self.kv_indptr[:bs + 1], self.kv_indices,
+                self.kv_tokens[:bs], scale, self.P, sinks=sinks, mode_of_row=self.mode,
+                rows=self.rows_dev, scores=self.scores[layer], zero_new=True, out=out,
+                score_flags=score_flags, err=self.err, workspace=ws)
+        # Attention and outputs on the current stream; this layer's page scores
+        # on the score stream once they are done, overlapping the next layer.
+        # Workspace k is reused two layers later, after its scores have run.
+        k = layer % 2
+        ws = self._decode_workspace(k, bs, score_flags)
         main = torch.cuda.current_stream(self.device)
         main.wait_event(self._ws_free[k])
         res = kernels.decode_attn_score(

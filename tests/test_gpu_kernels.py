@@ -165,6 +165,19 @@ def test_decode_paged_vs_oracle(G):
     np.testing.assert_allclose(s_g, s_c, rtol=1e-3, atol=1e-6)
 
 
+@pytest.mark.parametrize("G,page,mode", [(8, 16, 1), (8, 16, 2), (1, 16, 1), (2, 16, 2), (8, 1, 1)])
+def test_decode_batch1_long_sequence_vs_oracle(G, page, mode):
+    """One sequence spread over every attention CTA (config 4's decode shape):
+    the combine splits each KV head's output merges and page scoring into
+    chunks, and at one KV head per GPU merges more slots than it has threads."""
+    c = _decode_case([28_700], G, page, [mode], seed=40 + G + page + mode)
+    o_g, s_g, l_g = _run_decode_gpu(c, 0.125, zero_new=True)
+    o_c, s_c, l_c = _run_decode_oracle(c, 0.125, zero_new=True)
+    assert _rel(o_g[0], o_c[0]) < 1e-3
+    np.testing.assert_allclose(l_g, l_c, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(s_g, s_c, rtol=1e-3, atol=1e-6)
+
+
 def test_decode_token_mode_vs_oracle():
     lengths = [1, 2, 37, 1500, 3001, 513]
     c = _decode_case(lengths, 8, 1, [1, 2, 1, 2, 1, 0], seed=11)
