@@ -82,19 +82,6 @@ def pool_units_needed(specs, steps):
     return total + 64
 
 
-def resident_tokens_after_steps(specs, steps):
-    """Host-side resident token count per sequence (for the CPU sample)."""
-    out = []
-    for sp in specs:
-        cfg, ctx = sp["cfg"], sp["ctx"]
-        last = (ctx // 2048) * 2048
-        if cfg is not None and last > cfg.budget:
-            out.append(cfg.budget + ctx - last)
-        else:
-            out.append(ctx)
-    return out
-
-
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
     def __init__(self, gpu_index: int):
@@ -162,64 +149,104 @@ def measured_peak_hbm():
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_decode_sample(specs, n_rows, layers_sample, seed, max_seconds=None, min_reps=1):
-    """Time the oracle's decode (attention + H2O scores) on a bounded sample.
-
-    Builds host pools for `n_rows` sequences of the workload (their resident
-    token counts, 16-token pages) and runs oracle.decode for `layers_sample`
-    layers.  Returns (seconds per sampled layer-step, sampled tokens).
-    """
+def cpu_steps(specs, warmup, steps, budget_s, seed=2026 + 17):
+    """Time the oracle (the reference's eviction path restated in C, on all
+    host cores) on the whole config-3 workload, step by step, as the GPU arm's
+    step runs it: the due boundaries (oracle.boundary, the engine's due rule
+    and parameters), one token appended to every row, the CSR (oracle.fill)
+    and decode attention + H2O scores of every row on every layer
+    (oracle.decode).  The rows start from the same synthetic state as the GPU
+    arm's (engine.synth_rows).  The twelve layers share one host K and one V
+    pool: values do not change the CPU time, and the 12 x 1.3 GB a layer each
+    would take is saved.  Stops once budget_s of host time is spent (at least
+    one timed step).  Returns (seconds per timed step, info)."""
     from oracle import oracle
+    from cache_eviction_b200.engine import synth_rows
+    from cache_eviction_b200.policy import INTERVAL
+    P, L, G, H = PAGE, LAYERS, G_TOTAL, H_TOTAL
+    total = warmup + steps
+    units = pool_units_needed(specs, total)
+    pos_cap = 32768 // P
+    width = -(-(max([65536] + [sp["ctx"] for sp in specs]) + total + 4096) // P)
+    t_setup = time.perf_counter()
+    arrays, rows, scored, _ = synth_rows(specs, total, seed, layers=L, kv_heads=G, page_size=P,
+                                         pool_units=units, max_rows=len(specs), pos_cap=pos_cap,
+                                         r2u_width=width)
     rng = np.random.default_rng(seed)
-    resident = resident_tokens_after_steps(specs, 0)
-    idx = rng.choice(len(specs), size=min(n_rows, len(specs)), replace=False)
-    lengths = [resident[i] for i in idx]
-    pages = [-(-n // PAGE) for n in lengths]
-    units = sum(pages) + 1
-    kp = rng.integers(0, 1 << 16, (units, G_TOTAL, PAGE, D), dtype=np.uint16) & 0xBFFF
-    vp = rng.integers(0, 1 << 16, (units, G_TOTAL, PAGE, D), dtype=np.uint16) & 0xBFFF
-    q = (rng.integers(0, 1 << 16, (len(idx), H_TOTAL, D), dtype=np.uint16) & 0x3FFF) | 0x3800
-    indptr = np.concatenate([[0], np.cumsum(pages)]).astype(np.int32)
-    indices = (rng.permutation(units - 1) + 1).astype(np.int32)[:sum(pages)]
-    tokens = np.array(lengths, np.int32)
-    modes = np.array([1 if specs[i]["cfg"] is not None and specs[i]["cfg"].score_mode else 0
-                      for i in idx], np.int32)
-    sinks = rng.standard_normal(H_TOTAL).astype(np.float32)
-    scores = np.zeros((G_TOTAL, units), np.float32)
-    times = []
-    t_all = time.perf_counter()
-    while True:
+    state = dict(arrays)
+    state["scores"] = np.zeros((L, G, units), np.float32)
+    for owned in scored:
+        state["scores"][:, :, owned] = rng.lognormal(0.0, 2.0, (L, G, len(owned))).astype(np.float32)
+    kp = rng.integers(0, 1 << 16, (units, G, P, D), dtype=np.uint16) & 0xBFFF
+    vp = rng.integers(0, 1 << 16, (units, G, P, D), dtype=np.uint16) & 0xBFFF
+    B = len(specs)
+    q = (rng.integers(0, 1 << 16, (L, B, H, D), dtype=np.uint16) & 0x3FFF) | 0x3800
+    sinks = rng.standard_normal((L, H)).astype(np.float32)
+    cfgs = [r[1] for r in rows]
+    n = [r[2] for r in rows]
+    last = [r[3] for r in rows]
+    modes = np.array([c.score_mode if c is not None else 0 for c in cfgs], np.int32)
+    order = np.arange(B, dtype=np.int64)
+    setup_s = time.perf_counter() - t_setup
+    times, bound_rows = [], 0
+    t0_all = time.perf_counter()
+    for s in range(total):
+        if s < warmup and times == [] and s > 0 and time.perf_counter() - t0_all > budget_s / 2:
+            continue                       # warm-up cut short: keep the budget for timed steps
         t0 = time.perf_counter()
-        for _ in range(layers_sample):
-            oracle.decode(q, kp, vp, indptr, indices, tokens, sinks, modes, 0.125, PAGE, scores)
-        times.append(time.perf_counter() - t0)
-        if len(times) >= min_reps and (max_seconds is None or time.perf_counter() - t_all > max_seconds):
+        due = [r for r in range(B) if cfgs[r] is not None and n[r] % INTERVAL == 0 and n[r] > last[r]]
+        if due:
+            params, ncols = [], []
+            for r in due:
+                b, pre, rec = cfgs[r].units(P)
+                n_u = n[r] // P
+                params.append(dict(n=n_u, budget=b, prefix=pre, recent=rec, cursor=None,
+                                   policy=cfgs[r].policy_id, seed=cfgs[r].seed))
+                ncols.append(int(state["count"][r]) + n_u - int(state["frontier"][r]))
+                last[r] = n[r]
+            max_cols = max(ncols)
+            uni = None
+            if any(cfgs[r].name == "random_2048" for r in due):
+                uni = rng.random((len(due), L, G, max_cols))
+            oracle.boundary(state, [kp] * L, [vp] * L, due, oracle.row_params(params), max_cols, live=True,
+                            uniforms=uni)
+            bound_rows += len(due)
+        for r in range(B):
+            n[r] += 1
+        indptr, indices, tokens = oracle.fill(state["table"], state["r2u"], state["frontier"], state["count"],
+                                              order, np.array(n, np.int64), page=P)
+        indices = indices.astype(np.int32)
+        for l in range(L):
+            oracle.decode(q[l], kp, vp, indptr, indices, tokens, sinks[l], modes, D ** -0.5, P,
+                          scores=state["scores"][l], zero_new=True)
+        dt = time.perf_counter() - t0
+        if s >= warmup:
+            times.append(dt)
+        if times and time.perf_counter() - t0_all > budget_s:
             break
-        if max_seconds is None:
-            break
-    return statistics.median(times) / layers_sample, int(sum(lengths)), len(idx)
+    info = {"timed_steps": len(times), "resident_tokens": int(tokens.sum()), "boundary_rows": bound_rows,
+            "setup_s": setup_s}
+    return statistics.mean(times), info
+
+
+def cpu_sample_text(info, B, steps_requested):
+    return (f"oracle (C restatement of the reference path) on the whole config-3 step: due boundaries "
+            f"(oracle.boundary), CSR fill and decode attention + H2O scores of all {B} sequences "
+            f"({info['resident_tokens']} resident tokens) on all {LAYERS} layers; "
+            f"{info['timed_steps']} of {steps_requested} steps timed in full, {info['boundary_rows']} boundary "
+            f"rows in the run; the layers share one host K/V pool")
 
 
 def reference_arm(args, world, rank):
-    """--impl reference: the CPU restatement of the reference path on host cores."""
+    """--impl reference: the reference's path (its CPU restatement, the
+    oracle) on the host cores, timed on this arm's workload step by step."""
     if rank != 0:
         return 0
     from oracle import oracle
     cores = os.cpu_count() or 1
     oracle.set_threads(cores)
     specs = workload(SEQS_PER_GPU * world)
-    resident = resident_tokens_after_steps(specs, 0)
-    total_tokens = sum(resident)
-    n_sample = 4
-    step_times = []
-    sampled = None
-    for s in range(args.warmup + args.steps):
-        t, tok, nrows = cpu_decode_sample(specs, n_sample, 1, seed=100 + s)
-        full_step = t * (total_tokens / tok) * LAYERS
-        if s >= args.warmup:
-            step_times.append(full_step)
-        sampled = (tok, nrows)
-    per_step = statistics.mean(step_times)
+    per_step, info = cpu_steps(specs, args.warmup, args.steps, budget_s=REFERENCE_BUDGET_S)
     value = len(specs) / per_step
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -227,13 +254,16 @@ def reference_arm(args, world, rank):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic", "config": config_block(world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"oracle decode (attention + H2O scores) of {sampled[1]} of "
-                                   f"{len(specs)} sequences ({sampled[0]} resident tokens), 1 of "
-                                   f"{LAYERS} layers per step, scaled by resident tokens and layers"},
+                         "sample": cpu_sample_text(info, len(specs), args.steps)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# Host seconds the reference arm spends on its warm-up and timed steps (each a
+# full step of the workload); setting up the host state comes on top.
+REFERENCE_BUDGET_S = 150.0
 
 
 def config_block(world):
@@ -933,12 +963,9 @@ def main():
         from oracle import oracle
         cores = os.cpu_count() or 1
         oracle.set_threads(cores)
-        t, tok, nrows = cpu_decode_sample(specs, 4, 1, seed=99, max_seconds=args.cpu_seconds)
-        cpu_step = t * (statistics.mean(tokens_resident) / tok) * LAYERS
-        line["cpu_baseline"] = {
-            "value": B / cpu_step, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"oracle decode of {nrows} of {B} sequences ({tok} resident tokens), 1 layer, "
-                      f"repeated for ~{args.cpu_seconds:.0f} s, scaled by resident tokens x {LAYERS} layers"}
+        per_step, info = cpu_steps(specs, 1, args.steps, budget_s=args.cpu_seconds)
+        line["cpu_baseline"] = {"value": B / per_step, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": cpu_sample_text(info, B, args.steps)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

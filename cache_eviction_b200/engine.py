@@ -330,20 +330,23 @@ class RaggedDecodeEngine:
 
 
 # -------------------------------------------------------------- synthesis
-def synth_state(engine: RaggedDecodeEngine, specs: list, steps: int, seed: int,
-                score_sigma: float = 2.0, fill_pools: bool = True):
-    """Initialise rows as if every boundary up to each context had been taken.
+def synth_rows(specs: list, steps: int, seed: int, *, layers: int, kv_heads: int, page_size: int,
+               pool_units: int, max_rows: int, pos_cap: int, r2u_width: int):
+    """Host arrays of rows initialised as if every boundary up to each context
+    had been taken (the state synth_state uploads).
 
     specs: dicts with ctx (tokens), cfg (EvictionConfig or None).  Each evicting
     row holds prefix + recent + budget-remainder residents after its last
     evicting boundary (ascending positions, per-head middle picks for per-head
     policies, shared picks for H2O global) and its tail since that boundary.
     Units are drawn from a shuffled pool; the pool holds each row's future
-    pages for `steps` more tokens.  Scores of H2O rows are lognormal(0, sigma).
+    pages for `steps` more tokens.  Returns (arrays dict with table, r2u, pos,
+    frontier, count; rows list of (row, cfg, n, last_boundary, frontier,
+    count); owned units of each H2O row; units used).
     """
     rng = np.random.default_rng(seed)
-    P, L, G = engine.P, engine.L, engine.G
-    order = rng.permutation(np.arange(1, engine.units)).astype(np.int32)
+    P, L, G = page_size, layers, kv_heads
+    order = rng.permutation(np.arange(1, pool_units)).astype(np.int32)
     cursor = 0
 
     def take(k):
@@ -354,10 +357,12 @@ def synth_state(engine: RaggedDecodeEngine, specs: list, steps: int, seed: int,
             raise RuntimeError("pool too small for the synthetic state")
         return out
 
-    table = engine.table.cpu().numpy()
-    r2u = engine.r2u.cpu().numpy()
-    pos = engine.pos.cpu().numpy()
-    scores_rows = []
+    table = np.zeros((max_rows, pos_cap), np.int32)
+    r2u = np.zeros((max_rows, r2u_width), np.int32)
+    pos = np.zeros((max_rows, L, G, pos_cap), np.int32)
+    frontier_a = np.zeros(max_rows, np.int32)
+    count_a = np.zeros(max_rows, np.int32)
+    rows, scored = [], []
     for r, sp in enumerate(specs):
         cfg, ctx = sp["cfg"], int(sp["ctx"])
         end_units = -(-(ctx + steps) // P)
@@ -394,15 +399,30 @@ def synth_state(engine: RaggedDecodeEngine, specs: list, steps: int, seed: int,
             r2u[r, :end_units] = tail
             owned = tail[:-(-ctx // P)]
             last = last if cfg is not None else 0
-        engine.add_row(r, cfg, ctx, last_boundary=last if cfg is not None else 0,
-                       frontier_units=frontier, count_units=count)
+        frontier_a[r], count_a[r] = frontier, count
+        rows.append((r, cfg, ctx, last if cfg is not None else 0, frontier, count))
         if cfg is not None and cfg.score_mode != capi.CE_MODE_NONE:
-            scores_rows.append(owned)
-    engine.table.copy_(torch.from_numpy(table))
-    engine.r2u.copy_(torch.from_numpy(r2u))
-    engine.pos.copy_(torch.from_numpy(pos))
-    if scores_rows:
-        idx = torch.from_numpy(np.concatenate(scores_rows).astype(np.int64)).to(engine.device)
+            scored.append(owned)
+    arrays = dict(table=table, r2u=r2u, pos=pos, frontier=frontier_a, count=count_a)
+    return arrays, rows, scored, cursor + 1
+
+
+def synth_state(engine: RaggedDecodeEngine, specs: list, steps: int, seed: int,
+                score_sigma: float = 2.0, fill_pools: bool = True):
+    """Initialise the engine's rows with synth_rows' state; scores of H2O rows
+    are lognormal(0, sigma), the pools N(0, 1).  Returns the units used."""
+    arrays, rows, scored, used = synth_rows(
+        specs, steps, seed, layers=engine.L, kv_heads=engine.G, page_size=engine.P,
+        pool_units=engine.units, max_rows=engine.table.shape[0], pos_cap=engine.pos_cap,
+        r2u_width=engine.r2u.shape[1])
+    for r, cfg, n, last, frontier, count in rows:
+        engine.add_row(r, cfg, n, last_boundary=last, frontier_units=frontier, count_units=count)
+    engine.table.copy_(torch.from_numpy(arrays["table"]))
+    engine.r2u.copy_(torch.from_numpy(arrays["r2u"]))
+    engine.pos.copy_(torch.from_numpy(arrays["pos"]))
+    L, G = engine.L, engine.G
+    if scored:
+        idx = torch.from_numpy(np.concatenate(scored).astype(np.int64)).to(engine.device)
         gen = torch.Generator(device=engine.device).manual_seed(seed + 7)
         vals = torch.randn((L, G, idx.numel()), generator=gen, device=engine.device) * score_sigma
         engine.scores[:, :, idx] = vals.exp_()
@@ -411,4 +431,4 @@ def synth_state(engine: RaggedDecodeEngine, specs: list, steps: int, seed: int,
         for t in engine.k + engine.v:
             t.normal_(generator=gen)
     engine.commit_rows()
-    return cursor + 1
+    return used

@@ -254,9 +254,9 @@ def after_extend(backend, q, layer, forward_batch, sinks):
         chunk = q.view(-1, layer.tp_q_head_num, layer.qk_head_dim)[lo:hi]
         if layer.layer_id == st.first_full and (e["kind"] == "replay" or st.verify and e["kind"] == "live"):
             kpool, vpool = st.pools(layer.layer_id)
-            shadow_k, shadow_v = _shadow(st, e, start + hi - lo)
-            shadow_k[start:start + hi - lo] = _token_rows(kpool, loc[lo:hi], st.page_size)
-            shadow_v[start:start + hi - lo] = _token_rows(vpool, loc[lo:hi], st.page_size)
+            shadow = e.setdefault("shadow", ShadowKV(st.kv_heads, st.dim, st.device))
+            shadow.put(start, _token_rows(kpool, loc[lo:hi], st.page_size),
+                       _token_rows(vpool, loc[lo:hi], st.page_size))
             if e["kind"] == "replay":
                 _replay_layer_difference(st, e, chunk, layer, sinks, start)
         if e["kind"] == "diagnostic":
@@ -312,18 +312,29 @@ def _token_rows(pool, loc, page):
     return pool[loc // page, :, loc % page]
 
 
-def _shadow(st, entry, length):
-    """First full layer keys and values by logical position (runtime:227-238),
-    grown by doubling; the checks that need the unevicted cache read them."""
-    current = entry["shadow_k"].shape[0] if "shadow_k" in entry else 0
-    if current < length:
-        grown = max(length, 2 * current)
-        for name in ("shadow_k", "shadow_v"):
-            new = torch.zeros((grown, st.kv_heads, st.dim), dtype=torch.bfloat16, device=st.device)
-            if name in entry:
-                new[:current] = entry[name]
-            entry[name] = new
-    return entry["shadow_k"], entry["shadow_v"]
+class ShadowKV:
+    """The first full layer's keys and values indexed by logical position:
+    the unevicted cache that the replay metric and the verify checks compare
+    against (runtime:227-238).  Storage is [capacity, G, D] bf16 per side,
+    the capacity a whole number of INTERVAL blocks, so a request's shadow is
+    reallocated at most once per 2,048 tokens."""
+
+    def __init__(self, kv_heads, dim, device):
+        self.k = torch.zeros((0, kv_heads, dim), dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros_like(self.k)
+
+    def put(self, start, k_rows, v_rows):
+        """Write the rows of positions start .. start + len(k_rows) - 1."""
+        end = start + k_rows.shape[0]
+        if end > self.k.shape[0]:
+            cap = -(-end // INTERVAL) * INTERVAL
+            for side in ("k", "v"):
+                old = getattr(self, side)
+                grown = torch.zeros((cap,) + tuple(old.shape[1:]), dtype=old.dtype, device=old.device)
+                grown[:old.shape[0]].copy_(old)
+                setattr(self, side, grown)
+        self.k[start:end].copy_(k_rows)
+        self.v[start:end].copy_(v_rows)
 
 
 def _visible(st, entry, end):
@@ -348,8 +359,8 @@ def _replay_layer_difference(st, entry, queries, layer, sinks, start):
     shadow: both outputs use the unevicted keys, the evicted one restricted to
     each head's visible positions."""
     end = start + queries.shape[0]
-    shadow_k, shadow_v = entry["shadow_k"], entry["shadow_v"]
-    error = kernels.replay_error(queries, shadow_k, shadow_v, start, layer.scaling,
+    shadow = entry["shadow"]
+    error = kernels.replay_error(queries, shadow.k, shadow.v, start, layer.scaling,
                                  visible_bits=_visible(st, entry, end), sinks=sinks, err=st.err)
     entry["layer_error"].append(error)
 
@@ -357,25 +368,30 @@ def _replay_layer_difference(st, entry, queries, layer, sinks, start):
 def _verify_decode(st, queries, out, layer, forward_batch, sinks):
     """GSTAR_EVICT_VERIFY=1, eager only (runtime:250-274): the first full
     layer's output of every live row with a shadow equals attention over each
-    head's claimed positions; the largest absolute difference is kept."""
+    head's claimed positions; the largest absolute difference is kept.  The
+    new token's key and value join the shadow first; ce_replay_error's masked
+    output over the shadow is the expected output."""
+    rows = forward_batch.req_pool_indices.tolist()
+    checked = [(i, st.entries[r]) for i, r in enumerate(rows)
+               if r in st.entries and st.entries[r]["kind"] == "live" and "shadow" in st.entries[r]]
+    if not checked:
+        return
     heads, dim = layer.tp_q_head_num, layer.qk_head_dim
     kpool, vpool = st.pools(st.first_full)
-    loc = forward_batch.out_cache_loc.long()
-    positions = forward_batch.positions.tolist()
-    o = out.view(-1, heads, dim)
-    for i, row in enumerate(forward_batch.req_pool_indices.tolist()):
-        entry = st.entries.get(row)
-        if entry is None or entry["kind"] != "live" or "shadow_k" not in entry:
-            continue
-        end = positions[i] + 1
-        shadow_k, shadow_v = _shadow(st, entry, end)
-        shadow_k[end - 1] = _token_rows(kpool, loc[i:i + 1], st.page_size)[0]
-        shadow_v[end - 1] = _token_rows(vpool, loc[i:i + 1], st.page_size)[0]
-        expected = torch.empty((1, heads, dim), dtype=torch.float32, device=st.device)
-        kernels.replay_error(queries[i:i + 1], shadow_k, shadow_v, end - 1, layer.scaling,
-                             visible_bits=_visible(st, entry, end), sinks=sinks, out_masked=expected, err=st.err)
-        error = float((o[i].float() - expected[0]).abs().max())
-        entry["verify_max_error"] = max(entry.get("verify_max_error", 0.0), error)
+    new_loc = forward_batch.out_cache_loc.long()
+    new_pos = forward_batch.positions.tolist()
+    got = out.view(-1, heads, dim).float()
+    expected = torch.empty((1, heads, dim), dtype=torch.float32, device=st.device)
+    for i, entry in checked:
+        p = int(new_pos[i])
+        shadow = entry["shadow"]
+        shadow.put(p, _token_rows(kpool, new_loc[i:i + 1], st.page_size),
+                   _token_rows(vpool, new_loc[i:i + 1], st.page_size))
+        kernels.replay_error(queries[i:i + 1], shadow.k, shadow.v, p, layer.scaling,
+                             visible_bits=_visible(st, entry, p + 1), sinks=sinks, out_masked=expected,
+                             err=st.err)
+        gap = float((got[i] - expected[0]).abs().max())
+        entry["verify_max_error"] = max(entry.get("verify_max_error", 0.0), gap)
         entry["verify_steps"] = entry.get("verify_steps", 0) + 1
 
 
@@ -388,7 +404,7 @@ def _relocation_ok(st, entry, table):
     heads = torch.arange(st.kv_heads, device=st.device)[:, None]
     stored = kpool[table.long()[None, :].expand(st.kv_heads, -1), heads]   # [G, count, P, D]
     tokens = pos[..., None] * P + torch.arange(P, device=st.device)       # [G, count, P]
-    want = entry["shadow_k"][tokens, heads[..., None]]                       # [G, count, P, D]
+    want = entry["shadow"].k[tokens, heads[..., None]]                       # [G, count, P, D]
     return bool(torch.equal(stored, want))
 
 
@@ -400,47 +416,74 @@ def _events(entry, req):
 
 
 # ------------------------------------------------------ regret diagnostic
+# A diagnostic request (runtime:549-613) evicts nothing.  At each boundary it
+# asks every "name:budget:prefix:recent" spec which positions it would keep,
+# ranked by the unevicted cache's exact per-token tables, and then measures the
+# softmax mass that each prefill query puts on the positions the spec dropped.
+# A spec's state is the same positions-first form the live path keeps in
+# State.pos: its kept positions [L, G, K] below the diagnostic frontier (None
+# while nothing was dropped), everything from the frontier on resident.
 def _diagnostic_entry(req, cfg, device, layers, heads):
-    """A prefill-only entry that scores several eviction specs against the
-    unevicted cache (runtime:549-560): per spec a resident mask, per-token
-    head_sum / head_max tables, and the per-query lost mass."""
-    specs = []
-    for item in str(cfg["policies"]).split(","):
-        name, budget, prefix, recent = item.split(":")
-        specs.append((name, int(budget), int(prefix), int(recent)))
+    """A prefill-only entry scoring several eviction specs against the
+    unevicted cache (runtime:549-560)."""
+    specs = [(name, int(budget), int(prefix), int(recent))
+             for name, budget, prefix, recent in (item.split(":") for item in str(cfg["policies"]).split(","))]
     length = len(req.origin_input_ids)
-    return {"kind": "diagnostic", "key": _identity(req), "mode": 0, "specs": specs, "error": None, "frontier": 0,
-            "seed": int(cfg.get("seed", 0)),
-            "resident": torch.ones((len(specs), layers, heads, length), dtype=torch.bool, device=device),
-            "score_sum": torch.zeros((layers, heads, length), device=device),
-            "score_max": torch.zeros((layers, heads, length), device=device),
-            "lost": torch.zeros((len(specs), length), device=device), "layers_seen": set()}
+    tables = torch.zeros((2, layers, heads, length), device=device)   # head_sum, head_max per token
+    return {"kind": "diagnostic", "key": _identity(req), "mode": 0, "specs": specs, "error": None,
+            "frontier": 0, "seed": int(cfg.get("seed", 0)), "kept": [None] * len(specs),
+            "score_sum": tables[0], "score_max": tables[1], "layers_seen": set(),
+            "lost": torch.zeros((len(specs), length), device=device)}
+
+
+def _diagnostic_draws(entry, j, n, name, pos):
+    """The ranking key of spec j's candidates at a boundary at n (the
+    reference draws its random keys with seed * 1000003 + 31 n + j)."""
+    dev = pos.device
+    L, G = pos.shape[:2]
+    if name == "random_2048":
+        gen = torch.Generator(device=dev).manual_seed((entry["seed"] * 1000003 + n * 31 + j) & 0x7FFFFFFF)
+        return torch.rand(tuple(pos.shape), generator=gen, device=dev, dtype=torch.float64)
+    if name == "random_reservoir_2048":
+        return reservoir_scores(entry["seed"], pos, torch.arange(L, device=dev), torch.arange(G, device=dev))
+    table = entry["score_max" if name == "head_max_sum_2048" else "score_sum"]
+    return torch.gather(table, 2, pos).double()
 
 
 def _diagnostic_boundary(entry, n):
-    """Every spec's per-head boundary at n, scored by the unevicted reference (runtime:563-584)."""
-    layers, heads = entry["resident"].shape[1:3]
-    device = entry["resident"].device
+    """Every spec's per-head boundary at n, ranked by the unevicted tables
+    (runtime:563-584): candidates are the spec's kept positions and the new
+    positions [frontier, n); the survivors become its kept positions."""
+    L, G = entry["score_sum"].shape[:2]
+    dev = entry["score_sum"].device
+    fresh = torch.arange(entry["frontier"], n, device=dev).expand(L, G, -1)
     for j, (name, budget, prefix, recent) in enumerate(entry["specs"]):
-        resident = entry["resident"][j, :, :, :n]
-        count = int(resident[0, 0].sum())
-        if count <= budget:
-            continue
-        pos = resident.nonzero()[:, -1].view(layers, heads, count)
-        if name == "random_2048":
-            generator = torch.Generator(device=device).manual_seed(
-                (entry["seed"] * 1000003 + n * 31 + j) & 0x7FFFFFFF)
-            score = torch.rand(pos.shape, generator=generator, device=device, dtype=torch.float64)
-        elif name == "random_reservoir_2048":
-            score = reservoir_scores(entry["seed"], pos, torch.arange(layers, device=device),
-                                     torch.arange(heads, device=device))
+        kept = entry["kept"][j]
+        if kept is None:
+            kept = torch.zeros((L, G, 0), dtype=torch.long, device=dev)
+            pos = torch.arange(0, n, device=dev).expand(L, G, -1)
         else:
-            table = entry["score_max" if name == "head_max_sum_2048" else "score_sum"][..., :n]
-            score = torch.gather(table, -1, pos).double()
-        keep, _ = choose(name, pos, n, budget, prefix, recent, score)
-        entry["resident"][j, :, :, :n] = torch.zeros_like(resident).scatter_(
-            -1, torch.gather(pos, -1, keep), True)
+            pos = torch.cat((kept, fresh), -1)
+        if pos.shape[-1] <= budget:
+            if entry["kept"][j] is not None:
+                entry["kept"][j] = pos.contiguous()
+            continue
+        cols, _ = choose(name, pos, n, budget, prefix, recent, _diagnostic_draws(entry, j, n, name, pos))
+        entry["kept"][j] = torch.gather(pos, 2, cols)
     entry["frontier"] = n
+
+
+def _diagnostic_resident(entry, j, layer_index, end):
+    """Spec j's resident positions [G, end) of one layer as booleans."""
+    G = entry["score_sum"].shape[1]
+    dev = entry["score_sum"].device
+    kept = entry["kept"][j]
+    if kept is None:
+        return torch.ones((G, end), dtype=torch.bool, device=dev)
+    resident = torch.zeros((G, end), dtype=torch.bool, device=dev)
+    resident[:, entry["frontier"]:] = True
+    resident.scatter_(1, kept[layer_index], True)
+    return resident
 
 
 def _pack_bits(mask):
@@ -478,7 +521,8 @@ def _diagnose(st, entry, index, layer, queries, keys, sinks, slots, start):
         kernels.prefill_scores(q, kpool, qo, kvp, idx, tok, layer.scaling, 1, count, end, sinks=sinks,
                                mode_of_row=i32([mode]), scores=scratch, zero_new=False, err=st.err)
         entry[table][index, :, :end] += scratch[:, slots.long()]
-    evicted = _pack_bits(~entry["resident"][:, index, :, :end])
+    evicted = _pack_bits(torch.stack([~_diagnostic_resident(entry, j, index, end)
+                                      for j in range(len(entry["specs"]))]))
     kernels.prefill_lost(q, kpool, qo, kvp, idx, tok, layer.scaling, 1, count, end, evicted,
                          entry["lost"][:, start:end], 1.0 / (heads * len(st.full_layers)),
                          sinks=sinks, err=st.err)
@@ -625,7 +669,7 @@ def _boundary(st, row, entry, n, cursor=None, allocator=None):
     elapsed = 1000 * (finished - started)
     event = {"boundary": n, "before": before, "after": after, "freed": nfreed,
              "swa_cursor": cursor, "ranking_ms": elapsed, "compaction_ms": 0.0}
-    if st.verify and "shadow_k" in entry:
+    if st.verify and "shadow" in entry:
         event["relocation_ok"] = _relocation_ok(st, entry, st.table[row, :after])
     entry["events"].append(event)
     if record is not None:
