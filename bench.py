@@ -70,15 +70,20 @@ def workload(n_seqs: int, seed: int = 2026):
 
 
 def pool_units_needed(specs, steps):
+    """Units the engine's pool needs: what each row can hold at once over
+    `steps` decode steps (units come and go through the free stack, so an
+    evicting row needs its budget plus one boundary interval of new pages,
+    not every token it ever saw), plus slack."""
     total = 1
     for sp in specs:
         cfg, ctx = sp["cfg"], sp["ctx"]
-        end = -(-(ctx + steps) // PAGE)
-        last = (ctx // 2048) * 2048
-        if cfg is not None and last > cfg.budget:
-            total += cfg.budget // PAGE + end - last // PAGE
-        else:
-            total += end
+        grown = -(-(ctx + steps) // PAGE) + 1
+        if cfg is None:
+            total += grown
+        elif (ctx // 2048) * 2048 > cfg.budget:       # evicted: budget + one interval of new pages
+            total += min(grown, cfg.budget // PAGE + 2048 // PAGE + 1)
+        else:                                         # not yet: its context until the first eviction
+            total += min(grown, -(-(max(ctx, cfg.budget) + 2048) // PAGE) + 1)
     return total + 64
 
 
@@ -169,9 +174,10 @@ def cpu_steps(specs, warmup, steps, budget_s, seed=2026 + 17):
     pos_cap = 32768 // P
     width = -(-(max([65536] + [sp["ctx"] for sp in specs]) + total + 4096) // P)
     t_setup = time.perf_counter()
-    arrays, rows, scored, _ = synth_rows(specs, total, seed, layers=L, kv_heads=G, page_size=P,
-                                         pool_units=units, max_rows=len(specs), pos_cap=pos_cap,
-                                         r2u_width=width)
+    arrays, rows, scored, free = synth_rows(specs, seed, layers=L, kv_heads=G, page_size=P,
+                                            pool_units=units, max_rows=len(specs), pos_cap=pos_cap,
+                                            r2u_width=width)
+    free = list(free)      # the host allocator: a stack of free units
     rng = np.random.default_rng(seed)
     state = dict(arrays)
     state["scores"] = np.zeros((L, G, units), np.float32)
@@ -208,11 +214,15 @@ def cpu_steps(specs, warmup, steps, budget_s, seed=2026 + 17):
             uni = None
             if any(cfgs[r].name == "random_2048" for r in due):
                 uni = rng.random((len(due), L, G, max_cols))
-            oracle.boundary(state, [kp] * L, [vp] * L, due, oracle.row_params(params), max_cols, live=True,
-                            uniforms=uni)
+            res, freed = oracle.boundary(state, [kp] * L, [vp] * L, due, oracle.row_params(params), max_cols,
+                                         live=True, uniforms=uni)
+            for i in range(len(due)):
+                free.extend(freed[i, :res[i, 3]].tolist())
             bound_rows += len(due)
         for r in range(B):
             n[r] += 1
+            if (n[r] - 1) % P == 0:
+                state["r2u"][r, (n[r] - 1) // P] = free.pop()
         indptr, indices, tokens = oracle.fill(state["table"], state["r2u"], state["frontier"], state["count"],
                                               order, np.array(n, np.int64), page=P)
         indices = indices.astype(np.int32)
@@ -293,7 +303,7 @@ def build_engine(specs, steps_total, world, rank, group, device):
                              pos_cap=32768 // PAGE, device=device, head_offset=off,
                              global_kv_heads=G_TOTAL, process_group=group,
                              overlap_scores=SCORE_OVERLAP[0])
-    synth_state(eng, specs, steps_total, seed=2026 + 17)
+    synth_state(eng, specs, seed=2026 + 17)
     torch.cuda.synchronize()
     return eng
 
@@ -470,7 +480,7 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
         eng.join_scores()
         eng.new_score_events()
         with torch.cuda.graph(graph):
-            eng.seq_lens_dev.add_(1)
+            eng.advance_device()
             eng.fill()
             for l in range(LAYERS):
                 eng.decode_layer(l, q[l], out[l], sinks[l], scale)
@@ -481,14 +491,13 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
 
     def runner(ps):
         eng, graph = ps["eng"], ps["graph"]
-        row = eng.rows[eng.active[0]]
 
         def fn(n):
             for _ in range(n):
                 if eng.due():
                     eng.step(q, out, sinks, scale)
                 else:
-                    row.n += 1       # the host side of engine.advance
+                    eng.advance_host()
                     graph.replay()
                 ps["resident"].append(eng.resident_tokens(eng.active[0]))
             eng.join_scores()

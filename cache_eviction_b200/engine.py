@@ -7,7 +7,12 @@ full-attention layer and drives the four kernels through the C ABI:
     the tail, runtime:136-152), and ce_decode_attn_score runs the fused decode
     attention + H2O score for each full layer;
   * at boundaries (a row's length hits a multiple of 2048, runtime:692-710):
-    ce_boundary selects and compacts every due row in one batched call.
+    ce_boundary selects and compacts every due row in one batched call;
+  * units come from a free-unit stack on the device (ce_pool_alloc pops one
+    for every row whose new token starts a unit, ce_pool_push returns a
+    boundary's leftovers and a retired row's units), so rows can be admitted
+    and retired between steps and the pool is sized to what is resident, as
+    SGLang's allocator serves the reference (runtime:476-482, 719-742).
 
 Rows, their policies and lengths live on the host (like SGLang's scheduler);
 eviction state (tables, positions, scores, pools) lives on the device.  With
@@ -77,7 +82,11 @@ class RaggedDecodeEngine:
         self.kv_indices = torch.zeros(1, dtype=torch.int32, device=dev)
         self.rows_dev = torch.zeros(0, dtype=torch.int64, device=dev)
         self.seq_lens_dev = torch.zeros(0, dtype=torch.int64, device=dev)
-        self.free_units: list = []
+        # free-unit stack: units[0 .. top) on the device; free_top mirrors top
+        # on the host exactly (every push and pop count is known there)
+        self.free_stack = torch.zeros(pool_units, dtype=torch.int32, device=dev)
+        self.free_top_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.free_top = 0
         self.boundary_ms: list = []
         self.last_batch: Optional[dict] = None
         # The boundary workspace is sized up front for batches of up to
@@ -132,6 +141,66 @@ class RaggedDecodeEngine:
         self.count[row] = count_units
         if row not in self.active:
             self.active.append(row)
+
+    def seed_free_units(self, units):
+        """Make `units` (host ints) the free stack's contents (bottom first)."""
+        units = np.asarray(units, dtype=np.int32)
+        if len(units) > self.units:
+            raise ValueError("more free units than the pool holds")
+        self.free_stack[:len(units)] = torch.from_numpy(units).to(self.device)
+        self.free_top_dev.fill_(len(units))
+        self.free_top = len(units)
+
+    def admit(self, row: int, cfg: Optional[EvictionConfig], n: int, prompt=None) -> torch.Tensor:
+        """A new request whose n-token prompt is in the cache: ceil(n / P) units
+        from the free stack become its req_to_unit row; prompt(units), if
+        given, then fills them (K/V, prefill scores); then, as the chunked
+        prefill would have done, the boundary at the last multiple of 2048
+        at or below n runs (live: its leftovers go back to the stack).
+        Returns the prompt's units (device int32).  Call commit_rows() after
+        the admissions and retirements of a step."""
+        k = -(-n // self.P)
+        if k > self.free_top:
+            raise RuntimeError(f"unit pool exhausted: {k} units wanted, {self.free_top} free")
+        if k > self.r2u.shape[1]:
+            raise ValueError("prompt longer than the req_to_unit width")
+        dev = self.device
+        seq = torch.arange(k, dtype=torch.int64, device=dev) * self.P + 1   # token j*P starts unit j
+        kernels.pool_alloc(self.free_stack, self.free_top_dev, self.r2u,
+                           torch.full((k,), row, dtype=torch.int64, device=dev), seq, self.P, self.err)
+        self.free_top -= k
+        units = self.r2u[row, :k].clone()
+        if prompt is not None:
+            prompt(units)
+        last = (n // INTERVAL) * INTERVAL
+        self.add_row(row, cfg, n, last_boundary=0)
+        if cfg is not None and last > 0:
+            self.rows[row].n = last
+            self.run_boundaries([row])
+            self.rows[row].n = n
+        return units
+
+    def retire(self, row: int):
+        """A finished request: its resident units (compacted table and tail)
+        return to the free stack; the row leaves the batch."""
+        self.join_scores()
+        r = self.rows.pop(row)
+        tail_end = -(-r.n // self.P)
+        owned = torch.cat([self.table[row, :r.count], self.r2u[row, r.frontier:tail_end]]).view(1, -1)
+        k = int(owned.shape[1])
+        if k:
+            counts = torch.tensor([k], dtype=torch.int32, device=self.device)
+            kernels.pool_push(self.free_stack, self.free_top_dev, owned.contiguous(), counts, self.err)
+            self.free_top += k
+        self.mode[row] = capi.CE_MODE_NONE
+        self.frontier[row] = 0
+        self.count[row] = 0
+        self.active.remove(row)
+
+    def owned_units(self, row: int) -> torch.Tensor:
+        """The units row holds now (device int32): compacted table, then tail."""
+        r = self.rows[row]
+        return torch.cat([self.table[row, :r.count], self.r2u[row, r.frontier:-(-r.n // self.P)]])
 
     def commit_rows(self):
         """Upload the active row list and lengths (after rows were added)."""
@@ -226,7 +295,7 @@ class RaggedDecodeEngine:
         # draws of the random rows), for callers that audit or replay it
         self.last_batch = dict(rows=list(rows), params=params, max_cols=max_cols, uniforms=uniforms,
                                result=res, freed=freed)
-        fr = None
+        pushed = 0
         for i, r in enumerate(rows):
             row = self.rows[r]
             status, before, after, nfreed = (int(x) for x in res[i])
@@ -234,13 +303,15 @@ class RaggedDecodeEngine:
                                    freed=nfreed))
             if status == 0:
                 row.frontier, row.count = row.n // P, after
-                if live and nfreed:
-                    if fr is None:
-                        fr = freed.cpu().numpy()
-                    self.free_units.extend(fr[i, :nfreed].tolist())
+                if live:
+                    pushed += nfreed
                     row.freed += nfreed
             elif status not in (1, 2):
                 raise RuntimeError(f"boundary for row {r} failed with status {status}")
+        if live and pushed:
+            # the leftovers go back to the free stack straight from the device result
+            kernels.pool_push(self.free_stack, self.free_top_dev, freed, result[:, 3], self.err)
+            self.free_top += pushed
         return res
 
     # ------------------------------------------------------------ decode
@@ -300,10 +371,29 @@ class RaggedDecodeEngine:
         return res
 
     def advance(self):
-        """Append one token to every active row (host lengths and the device copy)."""
+        """Append one token to every active row: host lengths, then the device
+        lengths and a unit for every row whose new token starts one."""
+        self.advance_host()
+        self.advance_device()
+
+    def advance_host(self):
+        """The host side of advance (also what a replayed CUDA graph that
+        captured advance_device needs)."""
+        need = 0
         for r in self.active:
-            self.rows[r].n += 1
+            row = self.rows[r]
+            row.n += 1
+            need += (row.n - 1) % self.P == 0
+        if need > self.free_top:
+            raise RuntimeError(f"unit pool exhausted: {need} units wanted, {self.free_top} free")
+        self.free_top -= need
+
+    def advance_device(self):
+        """Device lengths + 1 and the new units (ce_pool_alloc); capturable."""
         self.seq_lens_dev.add_(1)
+        if self.active:
+            kernels.pool_alloc(self.free_stack, self.free_top_dev, self.r2u, self.rows_dev, self.seq_lens_dev,
+                               self.P, self.err)
 
     def step(self, q_layers, out_layers, sinks, scale, after_layer=None, before_layer=None):
         """One decode step: due boundaries, one token appended, CSR, every layer.
@@ -330,7 +420,7 @@ class RaggedDecodeEngine:
 
 
 # -------------------------------------------------------------- synthesis
-def synth_rows(specs: list, steps: int, seed: int, *, layers: int, kv_heads: int, page_size: int,
+def synth_rows(specs: list, seed: int, *, layers: int, kv_heads: int, page_size: int,
                pool_units: int, max_rows: int, pos_cap: int, r2u_width: int):
     """Host arrays of rows initialised as if every boundary up to each context
     had been taken (the state synth_state uploads).
@@ -339,10 +429,9 @@ def synth_rows(specs: list, steps: int, seed: int, *, layers: int, kv_heads: int
     row holds prefix + recent + budget-remainder residents after its last
     evicting boundary (ascending positions, per-head middle picks for per-head
     policies, shared picks for H2O global) and its tail since that boundary.
-    Units are drawn from a shuffled pool; the pool holds each row's future
-    pages for `steps` more tokens.  Returns (arrays dict with table, r2u, pos,
-    frontier, count; rows list of (row, cfg, n, last_boundary, frontier,
-    count); owned units of each H2O row; units used).
+    Units are drawn from a shuffled pool.  Returns (arrays dict with table,
+    r2u, pos, frontier, count; rows list of (row, cfg, n, last_boundary,
+    frontier, count); owned units of each H2O row; the units left free).
     """
     rng = np.random.default_rng(seed)
     P, L, G = page_size, layers, kv_heads
@@ -365,7 +454,7 @@ def synth_rows(specs: list, steps: int, seed: int, *, layers: int, kv_heads: int
     rows, scored = [], []
     for r, sp in enumerate(specs):
         cfg, ctx = sp["cfg"], int(sp["ctx"])
-        end_units = -(-(ctx + steps) // P)
+        end_units = -(-ctx // P)
         frontier = count = 0
         last = (ctx // INTERVAL) * INTERVAL
         if cfg is not None and last > cfg.budget:
@@ -393,33 +482,33 @@ def synth_rows(specs: list, steps: int, seed: int, *, layers: int, kv_heads: int
             tail = take(end_units - f_u)
             r2u[r, f_u:end_units] = tail
             frontier, count = f_u, b_u
-            owned = np.concatenate([units, tail[:-(-(ctx - last) // P) if ctx > last else 0]])
+            owned = np.concatenate([units, tail])
         else:
-            tail = take(end_units)
-            r2u[r, :end_units] = tail
-            owned = tail[:-(-ctx // P)]
+            owned = take(end_units)
+            r2u[r, :end_units] = owned
             last = last if cfg is not None else 0
         frontier_a[r], count_a[r] = frontier, count
         rows.append((r, cfg, ctx, last if cfg is not None else 0, frontier, count))
         if cfg is not None and cfg.score_mode != capi.CE_MODE_NONE:
             scored.append(owned)
     arrays = dict(table=table, r2u=r2u, pos=pos, frontier=frontier_a, count=count_a)
-    return arrays, rows, scored, cursor + 1
+    return arrays, rows, scored, order[cursor:]
 
 
-def synth_state(engine: RaggedDecodeEngine, specs: list, steps: int, seed: int,
-                score_sigma: float = 2.0, fill_pools: bool = True):
-    """Initialise the engine's rows with synth_rows' state; scores of H2O rows
-    are lognormal(0, sigma), the pools N(0, 1).  Returns the units used."""
-    arrays, rows, scored, used = synth_rows(
-        specs, steps, seed, layers=engine.L, kv_heads=engine.G, page_size=engine.P,
-        pool_units=engine.units, max_rows=engine.table.shape[0], pos_cap=engine.pos_cap,
-        r2u_width=engine.r2u.shape[1])
+def synth_state(engine: RaggedDecodeEngine, specs: list, seed: int, score_sigma: float = 2.0,
+                fill_pools: bool = True):
+    """Initialise the engine's rows with synth_rows' state; the units it does
+    not use become the free stack.  Scores of H2O rows are lognormal(0,
+    sigma), the pools N(0, 1)."""
+    arrays, rows, scored, free = synth_rows(
+        specs, seed, layers=engine.L, kv_heads=engine.G, page_size=engine.P, pool_units=engine.units,
+        max_rows=engine.table.shape[0], pos_cap=engine.pos_cap, r2u_width=engine.r2u.shape[1])
     for r, cfg, n, last, frontier, count in rows:
         engine.add_row(r, cfg, n, last_boundary=last, frontier_units=frontier, count_units=count)
     engine.table.copy_(torch.from_numpy(arrays["table"]))
     engine.r2u.copy_(torch.from_numpy(arrays["r2u"]))
     engine.pos.copy_(torch.from_numpy(arrays["pos"]))
+    engine.seed_free_units(free)
     L, G = engine.L, engine.G
     if scored:
         idx = torch.from_numpy(np.concatenate(scored).astype(np.int64)).to(engine.device)
@@ -431,4 +520,3 @@ def synth_state(engine: RaggedDecodeEngine, specs: list, steps: int, seed: int,
         for t in engine.k + engine.v:
             t.normal_(generator=gen)
     engine.commit_rows()
-    return used

@@ -94,6 +94,31 @@ def fill(table, req_to_unit, frontier, count, rows, seq_lens, page_size, kv_indp
     return kv_indptr
 
 
+def pool_alloc(units, top, req_to_unit, rows, seq_lens, page_size, err=None):
+    """Pop a unit for every entry whose newest token starts one and write it
+    to req_to_unit (ce_pool_alloc); units/top: the free-unit stack."""
+    lib = capi.load()
+    bs = int(rows.numel())
+    assert units.dtype == torch.int32 and top.dtype == torch.int32 and req_to_unit.dtype == torch.int32
+    assert rows.dtype == torch.int64 and seq_lens.dtype == torch.int64
+    st = lib.ce_pool_alloc(_p(units), _p(top), _p(req_to_unit), req_to_unit.stride(0), req_to_unit.shape[1],
+                           _p(rows), _p(seq_lens), bs, page_size, _p(err), _stream(units.device))
+    capi.check(st, "ce_pool_alloc")
+    _count(1 if bs else 0)
+
+
+def pool_push(units, top, lists, counts, err=None):
+    """Push lists[r, :counts[r]] for every row r onto the free-unit stack
+    (ce_pool_push); counts may be a strided column (e.g. result[:, 3])."""
+    lib = capi.load()
+    nrows = int(lists.shape[0])
+    assert lists.dtype == torch.int32 and counts.dtype == torch.int32 and lists.stride(1) == 1
+    st = lib.ce_pool_push(_p(units), _p(top), units.numel(), _p(lists), lists.stride(0), _p(counts),
+                          counts.stride(0), nrows, _p(err), _stream(units.device))
+    capi.check(st, "ce_pool_push")
+    _count(1 if nrows else 0)
+
+
 def decode_attn_score(q, k_pool, v_pool, kv_indptr, kv_indices, kv_tokens, sm_scale, page_size,
                       sinks=None, mode_of_row=None, rows=None, scores=None, zero_new=True,
                       out=None, out_f32=False, lse=None, score_flags=3, err=None, workspace=None):

@@ -117,6 +117,31 @@ int ce_fill(const int32_t* table, int64_t table_stride,
             int64_t kv_capacity, int32_t* kv_tokens,
             int32_t* err, void* stream);
 
+/* ---- unit pool of a continuous batch ---------------------------------------
+ * A device-resident stack of free units, units[0 .. *top) (top: a device
+ * int32), standing in for SGLang's token allocator on the decode path: the
+ * new token's slot (alloc), a boundary's leftovers (allocator.free_full,
+ * runtime:476-482) and a finished request's units (release, runtime:719-742).
+ * Graph-capturable, no host sync; entries and rows are served in batch order,
+ * so assignments are deterministic.
+ *
+ * ce_pool_alloc: for every batch entry b whose newest token (position
+ * seq_lens[b] - 1) starts a unit, pop one unit and write it to
+ * req_to_unit[rows[b], (seq_lens[b] - 1) / page_size].  An empty stack (or a
+ * slot at or beyond r2u_width) flags CE_EW_CAPACITY and writes unit 0 there. */
+int ce_pool_alloc(int32_t* units, int32_t* top, int32_t* req_to_unit, int64_t r2u_stride,
+                  int64_t r2u_width, const int64_t* rows, const int64_t* seq_lens, int32_t bs,
+                  int32_t page_size, int32_t* err, void* stream);
+
+/* ce_pool_push: push lists[r * list_stride .. + counts[r * count_stride]) for
+ * r = 0 .. nrows-1, in row order, onto the stack (capacity entries).  A list
+ * longer than list_stride flags CE_EW_SHAPE and is skipped; units beyond the
+ * capacity flag CE_EW_CAPACITY.  ce_boundary's freed / result arrays can be
+ * passed directly (counts = result + 3, count_stride = 4). */
+int ce_pool_push(int32_t* units, int32_t* top, int64_t capacity, const int32_t* lists,
+                 int64_t list_stride, const int32_t* counts, int64_t count_stride, int32_t nrows,
+                 int32_t* err, void* stream);
+
 /* ---- K1: fused paged GQA decode attention + H2O score --------------------
  * Replaces SGLang decode_attention_fwd (stage 1 + stage 2, call shape
  * code/tests/test_sglang_evict.py:59-61) AND gstar_evict.after_decode /

@@ -44,7 +44,7 @@ def _engine(overlap):
     eng = RaggedDecodeEngine(layers=L, q_heads=H, kv_heads=G, page_size=P, pool_units=units,
                              max_rows=len(specs), r2u_width=width, pos_cap=512, device=DEV,
                              overlap_scores=overlap)
-    synth_state(eng, specs, STEPS, seed=5)
+    synth_state(eng, specs, seed=5)
     torch.cuda.synchronize()
     return eng
 

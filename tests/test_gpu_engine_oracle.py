@@ -116,6 +116,28 @@ class Mirror:
         np.testing.assert_array_equal(eng.kv_tokens[:bs].cpu().numpy(), tokens)
         return indptr, indices.astype(np.int32), tokens
 
+    def take_new_pages(self):
+        """The unit pool's choices for rows whose new token starts a page
+        (ce_pool_alloc), copied from the device: the allocator is SGLang's
+        side of the contract, the oracle's starts from its assignments."""
+        eng = self.eng
+        for r in eng.active:
+            t = eng.rows[r].n - 1
+            if t % P == 0:
+                self.state["r2u"][r, t // P] = int(eng.r2u[r, t // P])
+
+    def check_ownership(self):
+        """Every unit is held at most once: by one row (its compacted table
+        and tail) or by the free stack, and unit 0 (padding) by nobody."""
+        eng = self.eng
+        held = [eng.owned_units(r).cpu().numpy() for r in eng.active]
+        free = eng.free_stack[:eng.free_top].cpu().numpy()
+        assert int(eng.free_top_dev.item()) == eng.free_top
+        allu = np.concatenate(held + [free])
+        assert len(np.unique(allu)) == len(allu), "a unit is held twice"
+        assert (allu > 0).all() and (allu < eng.units).all()
+        return len(allu)
+
     def write_new_tokens(self, gen):
         """K and V of every row's newest token, into its page slot (GPU and mirror)."""
         eng = self.eng
@@ -161,9 +183,42 @@ def _kept_now_matches_oracle(eng, row):
     return True
 
 
-def _run(eng, steps, seed, check_kept_row=None):
+def _admit(eng, m, row, cfg, n, gen):
+    """Admit a request into `row` on the engine (units from the free stack,
+    random prompt K/V and lognormal page scores, then the prefill's last
+    boundary) and on the mirror: the allocator's units, the prompt's contents
+    and the scores the boundary ranks come from the device, the boundary
+    itself from the oracle.  Returns whether a boundary batch ran."""
+    def prompt(units):
+        u = units.long()
+        for l in range(eng.L):
+            for pool in (eng.k[l], eng.v[l]):
+                pool[u] = torch.randn((u.numel(), G, P, D), generator=gen, device=DEV).to(torch.bfloat16)
+        eng.scores[:, :, u] = torch.randn((eng.L, G, u.numel()), generator=gen, device=DEV).mul_(2.0).exp_()
+        torch.cuda.synchronize()
+        un = units.cpu().numpy()
+        m.state["r2u"][row, :len(un)] = un
+        m.state["frontier"][row] = 0
+        m.state["count"][row] = 0
+        for l in range(eng.L):
+            m.k[l][un] = _bits(eng.k[l][u])
+            m.v[l][un] = _bits(eng.v[l][u])
+        m.state["scores"][...] = eng.scores.cpu().numpy()
+
+    before = eng.last_batch
+    eng.admit(row, cfg, n, prompt=prompt)
+    torch.cuda.synchronize()
+    ran = eng.last_batch is not before
+    if ran:
+        m.boundary_from_engine()
+    return ran
+
+
+def _run(eng, steps, seed, check_kept_row=None, churn=None):
     """Drive engine.step for `steps` steps against the mirror; returns the
-    boundary results seen (row, status) and the count of kept-set checks."""
+    boundary results seen (row, status) and the count of kept-set checks.
+    churn: {step: [(row, spec)]} -- before that step, row retires and a new
+    request (spec: ctx, cfg) is admitted into the same row slot."""
     gen_cpu = torch.Generator().manual_seed(seed)
     gen = torch.Generator(device=DEV).manual_seed(seed)
     L, B = eng.L, len(eng.active)
@@ -173,7 +228,15 @@ def _run(eng, steps, seed, check_kept_row=None):
     m = Mirror(eng)
     m.compare_state(exact_scores=True)
     seen, kept_checks = [], 0
+    gen_admit = torch.Generator(device=DEV).manual_seed(seed + 1)
     for step in range(steps):
+        for row, spec in (churn or {}).get(step, []):
+            eng.retire(row)
+            m.state["frontier"][row] = 0
+            m.state["count"][row] = 0
+            _admit(eng, m, row, spec["cfg"], spec["ctx"], gen_admit)
+            eng.commit_rows()
+            m.check_ownership()
         due = eng.due()
         if due:
             # the boundary ranks the scores the GPU accumulated: give the
@@ -189,6 +252,7 @@ def _run(eng, steps, seed, check_kept_row=None):
             if due:
                 res = m.boundary_from_engine()
                 seen.extend((r, int(res[i, 0])) for i, r in enumerate(eng.last_batch["rows"]))
+            m.take_new_pages()
             ctx["csr"] = m.csr()
             m.write_new_tokens(gen_cpu)
 
@@ -208,6 +272,7 @@ def _run(eng, steps, seed, check_kept_row=None):
             den = np.linalg.norm(o_c.reshape(B, -1), axis=1)
             assert (num / den < 1e-3).all(), (step, l, (num / den).max())
         m.compare_state()
+        assert m.check_ownership() == eng.units - 1     # no unit lost either
         if check_kept_row is not None:
             kept_checks += _kept_now_matches_oracle(eng, check_kept_row)
     return seen, kept_checks
@@ -230,12 +295,13 @@ def test_config1_fresh_cache_256_steps():
     cfg = _cfg("head_sum_2048", 2048, 11)
     eng = _engine([dict(ctx=ctx)], steps, layers=1)
     rng = np.random.default_rng(3)
-    owned = -(-(ctx + steps) // P)
-    units = (rng.permutation(eng.units - 1) + 1)[:owned].astype(np.int32)
+    perm = (rng.permutation(eng.units - 1) + 1).astype(np.int32)
+    units, free = perm[:ctx // P], perm[ctx // P:]
     eng.add_row(0, cfg, ctx, last_boundary=2048)
-    eng.r2u[0, :owned] = torch.from_numpy(units).to(DEV)
+    eng.r2u[0, :ctx // P] = torch.from_numpy(units).to(DEV)
+    eng.seed_free_units(free)
     gen = torch.Generator(device=DEV).manual_seed(12)
-    idx = torch.from_numpy(units[:ctx // P].astype(np.int64)).to(DEV)
+    idx = torch.from_numpy(units.astype(np.int64)).to(DEV)
     eng.scores[:, :, idx] = torch.randn((1, G, idx.numel()), generator=gen, device=DEV).mul_(2.0).exp_()
     for t in eng.k + eng.v:
         t.normal_(generator=gen)
@@ -256,7 +322,7 @@ def test_config1_second_boundary_over_kept_and_new_pages():
     steps = 256
     specs = [dict(ctx=6143, cfg=_cfg("head_sum_2048", 2048, 21))]
     eng = _engine(specs, steps, layers=1)
-    synth_state(eng, specs, steps, seed=22)
+    synth_state(eng, specs, seed=22)
     seen, kept_checks = _run(eng, steps, seed=23, check_kept_row=0)
     assert seen == [(0, 0)]
     assert eng.rows[0].count == 128 and eng.rows[0].frontier == 6144 // P
@@ -278,8 +344,36 @@ def test_config3_mix_five_policies_two_layers():
              dict(ctx=6120, cfg=_cfg("random_reservoir_2048", 2048, 7)),  # 6,144 at step 25
              dict(ctx=3000, cfg=None)]
     eng = _engine(specs, steps, layers=2)
-    synth_state(eng, specs, steps, seed=31)
+    synth_state(eng, specs, seed=31)
     seen, _ = _run(eng, steps, seed=32)
     assert len(seen) == 7, seen
     assert all(status == 0 for _, status in seen), seen
     assert sorted(r for r, _ in seen) == [0, 1, 2, 3, 4, 5, 6]
+
+
+def test_continuous_batch_reuses_units_of_retired_rows():
+    """Continuous batching: mid-run, rows retire and new requests take their
+    row slots; the prompts' units come from the free stack, which holds the
+    retired rows' units and every boundary's leftovers, so freed units are
+    reused.  Every step the engine matches the oracle (CSR, outputs,
+    scores; every boundary bit for bit, the admissions' prefill boundaries
+    included) and no unit is held twice or lost."""
+    from cache_eviction_b200.engine import synth_state
+    steps = 36
+    specs = [dict(ctx=4090, cfg=_cfg("head_sum_2048", 2048, 1)),
+             dict(ctx=6140, cfg=_cfg("h2o_global_2048", 2048, 2)),
+             dict(ctx=5000, cfg=_cfg("random_2048", 2048, 3)),
+             dict(ctx=3000, cfg=None),
+             dict(ctx=8180, cfg=_cfg("head_max_sum_2048", 4096, 4))]
+    churn = {3: [(3, dict(ctx=4200, cfg=_cfg("head_sum_2048", 2048, 9)))],      # full row out, H2O row in
+             9: [(2, dict(ctx=2040, cfg=_cfg("prefix_sliding_2048", 1024, 10)))],  # boundary at 2,048 later
+             20: [(0, dict(ctx=6500, cfg=_cfg("random_2048", 4096, 11))),
+                  (1, dict(ctx=700, cfg=None))]}
+    eng = _engine(specs + [dict(ctx=6500)], steps, layers=2)
+    synth_state(eng, specs, seed=41)
+    seen, _ = _run(eng, steps, seed=42, churn=churn)
+    # the admitted prefix-sliding row crosses 2,048 at step 17; the others'
+    # own boundaries fall at 4,096 (step 6), 6,144 (step 4) and 8,192 (step 12)
+    assert sorted(r for r, _ in seen) == [0, 1, 2, 4], seen
+    assert all(status == 0 for _, status in seen), seen
+    assert sum(eng.rows[r].freed for r in eng.active) > 0
