@@ -529,6 +529,132 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
     return res
 
 
+def continuous_microbench(world, rank, group, device, barrier, max_over_ranks, steps=512, warmup=8,
+                          seed=77):
+    """Config 3 as a continuous batch: up to 64 rows decode at once; each
+    request leaves after a drawn number of new tokens (uniform 64-512) and
+    the next arriving request (context, budget and policy drawn from the
+    config-3 distribution) takes the freed row once the free units allow
+    (it waits otherwise, as a scheduler's admission would).  Admissions
+    (prompt units popped from the free stack, the prefill's last boundary
+    for all of a step's arrivals in one batch) and retirements (units pushed
+    back) run between steps inside the timed region; the arrivals' K/V pages
+    keep what the units held (the prefill that would write them is outside
+    this path) and their H2O scores are drawn lognormal.  The pool is sized
+    to what the first batch can hold at once plus 8,192 units of slack, not
+    to every token of every request served.  Value: decoded tokens / time."""
+    import torch
+    from cache_eviction_b200 import tp
+    G, H, _ = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    B = SEQS_PER_GPU * world
+    specs = workload(B, seed=seed)
+    arrivals = workload(8 * B, seed=seed + 1)
+    rng = np.random.default_rng(seed + 2)
+    units = pool_units_needed(specs, steps + warmup) + 8192
+    from cache_eviction_b200.engine import RaggedDecodeEngine, synth_state
+    eng = RaggedDecodeEngine(layers=LAYERS, q_heads=H, kv_heads=G, page_size=PAGE, pool_units=units,
+                             max_rows=B, r2u_width=-(-(65536 + steps + warmup + 4096) // PAGE),
+                             pos_cap=32768 // PAGE, device=device, head_offset=_shard_offset(rank, world),
+                             global_kv_heads=G_TOTAL, process_group=group)
+    synth_state(eng, specs, seed=seed + 3)
+    scale = D ** -0.5
+    gen = torch.Generator(device=device).manual_seed(seed + 4)
+    q = torch.randn((LAYERS, B, H, D), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty((LAYERS, B, H, D), dtype=torch.bfloat16, device=device)
+    sinks = [torch.randn(H, generator=gen, device=device) for _ in range(LAYERS)]
+    left = {r: int(rng.integers(64, 513)) for r in range(B)}
+    queue = list(arrivals)
+    stats = dict(admitted=0, retired=0, waits=0, tokens=0, units_peak=0, served_token_units=0)
+
+    def peak_units(r, rem):
+        row = eng.rows[r]
+        grown = -(-(row.n + rem) // PAGE) + 1
+        if row.cfg is None:
+            return grown
+        b_u = row.cfg.budget // PAGE
+        return min(grown, max(eng.resident_units(r), b_u) + 2048 // PAGE + 1)
+
+    def admissions():
+        free_rows = [r for r in range(B) if r not in eng.rows]
+        if not free_rows or not queue:
+            return
+        reserve = sum(max(0, peak_units(r, left[r]) - eng.resident_units(r)) for r in eng.active)
+        admitted = []
+        for r in free_rows:
+            if not queue:
+                break
+            sp = queue[0]
+            need = -(-sp["ctx"] // PAGE)
+            rem = int(rng.integers(64, 513))
+            b_u = sp["cfg"].budget // PAGE if sp["cfg"] is not None else None
+            after = -(-(sp["ctx"] + rem) // PAGE) + 1 if b_u is None else min(
+                -(-(sp["ctx"] + rem) // PAGE) + 1, b_u + 2 * (2048 // PAGE) + 1)
+            if eng.free_top - reserve < max(need, after):
+                stats["waits"] += 1
+                break
+            queue.pop(0)
+
+            def prompt(u, cfg=sp["cfg"]):
+                if cfg is not None and cfg.score_mode:
+                    eng.scores[:, :, u.long()] = torch.randn((LAYERS, G, u.numel()), generator=gen,
+                                                             device=device).mul_(2.0).exp_()
+            eng.admit(r, sp["cfg"], sp["ctx"], prompt=prompt, settle=False)
+            left[r] = rem
+            reserve += after
+            admitted.append(r)
+            stats["admitted"] += 1
+            stats["served_token_units"] += -(-(sp["ctx"] + rem) // PAGE)
+        eng.settle(admitted)
+
+    def one_step():
+        for r in list(eng.active):
+            if left[r] == 0:
+                eng.retire(r)
+                stats["retired"] += 1
+        admissions()
+        eng.commit_rows()
+        bs = len(eng.active)
+        eng.step(q[:, :bs], out[:, :bs], sinks, scale)
+        for r in eng.active:
+            left[r] -= 1
+        stats["tokens"] += bs
+        stats["units_peak"] = max(stats["units_peak"], units - eng.free_top)
+
+    for _ in range(warmup):
+        one_step()
+    for k in ("admitted", "retired", "waits", "tokens", "served_token_units"):
+        stats[k] = 0
+    barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        one_step()
+    eng.join_scores()
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end))
+    eng.check_errors()
+    all_token = stats["served_token_units"] + sum(-(-(sp["ctx"] + steps + warmup) // PAGE) for sp in specs)
+    res = {"tok_s": stats["tokens"] / (ms * 1e-3),
+           "ms_per_step": ms / steps, "decoded_tokens": stats["tokens"], "admitted": stats["admitted"],
+           "retired": stats["retired"], "admission_waits": stats["waits"],
+           "boundary_rows": sum(len(eng.rows[r].events) for r in eng.active),
+           "pool_units": units, "units_in_use_peak": stats["units_peak"],
+           "units_if_every_token_kept": all_token,
+           "what": "rows retire after 64-512 new tokens and arrivals take their rows when free units "
+                   "allow; admissions, their prefill boundaries and retirements inside the timed region"}
+    del eng
+    torch.cuda.empty_cache()
+    return res
+
+
+def _shard_offset(rank, world):
+    from cache_eviction_b200 import tp
+    return tp.shard(G_TOTAL, H_TOTAL, rank, world)[2]
+
+
 PREFILL_CHUNK = 2048
 PREFILL_PREFIXES = (0, 8192, 26624)   # resident tokens before a chunk; 26,624 + 2,048 = config 4's cache
 
@@ -760,7 +886,7 @@ def main():
                     help="skip the config-5 eviction-step leg")
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (small cases for profiling)")
-    ap.add_argument("--legs", default="decode,e2e,noscore,decode4,prefill4,evict5,select1,evict1",
+    ap.add_argument("--legs", default="decode,e2e,noscore,cb3,decode4,prefill4,evict5,select1,evict1",
                     help="legs to run; without 'decode' only the listed microbenchmarks run "
                          "and one JSON line with their results is printed (profiling)")
     ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
@@ -804,6 +930,8 @@ def main():
 
         if "decode4" in legs:
             res["decode_config4"] = decode4_microbench(world, rank, group, device, barrier0, max0)
+        if "cb3" in legs:
+            res["continuous_config3"] = continuous_microbench(world, rank, group, device, barrier0, max0)
         if "prefill4" in legs:
             res["prefill_config4"] = prefill_microbench(world, rank, device, prefixes=prefixes)
         if "evict5" in legs:
@@ -902,6 +1030,9 @@ def main():
         e2e_value = run_e2e(args, specs, steps_total, world, rank, group, device, q, out, sinks,
                             scale, after_layer, barrier, max_over_ranks, e2e_steps)
 
+    cb3 = None
+    if "cb3" in legs:
+        cb3 = continuous_microbench(world, rank, group, device, barrier, max_over_ranks)
     decode4 = None
     if "decode4" in legs:
         decode4 = decode4_microbench(world, rank, group, device, barrier, max_over_ranks)
@@ -965,6 +1096,7 @@ def main():
         "evict_config5": evict5,
         "select_token_config5": select1,
         "evict_token_config5": evict1,
+        "continuous_config3": cb3,
         "decode_config4": decode4,
         "prefill_config4": prefill4,
     }

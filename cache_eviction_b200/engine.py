@@ -151,12 +151,14 @@ class RaggedDecodeEngine:
         self.free_top_dev.fill_(len(units))
         self.free_top = len(units)
 
-    def admit(self, row: int, cfg: Optional[EvictionConfig], n: int, prompt=None) -> torch.Tensor:
+    def admit(self, row: int, cfg: Optional[EvictionConfig], n: int, prompt=None,
+              settle: bool = True) -> torch.Tensor:
         """A new request whose n-token prompt is in the cache: ceil(n / P) units
         from the free stack become its req_to_unit row; prompt(units), if
         given, then fills them (K/V, prefill scores); then, as the chunked
         prefill would have done, the boundary at the last multiple of 2048
-        at or below n runs (live: its leftovers go back to the stack).
+        at or below n runs (live: its leftovers go back to the stack) -- or,
+        with settle=False, later in settle() together with other admissions.
         Returns the prompt's units (device int32).  Call commit_rows() after
         the admissions and retirements of a step."""
         k = -(-n // self.P)
@@ -172,13 +174,25 @@ class RaggedDecodeEngine:
         units = self.r2u[row, :k].clone()
         if prompt is not None:
             prompt(units)
-        last = (n // INTERVAL) * INTERVAL
         self.add_row(row, cfg, n, last_boundary=0)
-        if cfg is not None and last > 0:
-            self.rows[row].n = last
-            self.run_boundaries([row])
-            self.rows[row].n = n
+        if settle:
+            self.settle([row])
         return units
+
+    def settle(self, rows: list):
+        """The prefill's last boundary (at the last multiple of 2048 at or
+        below each row's length) for newly admitted rows, in one batch."""
+        due = [r for r in rows if self.rows[r].cfg is not None and self.rows[r].n >= INTERVAL]
+        if not due:
+            return []
+        lengths = {r: self.rows[r].n for r in due}
+        for r in due:
+            self.rows[r].n = (lengths[r] // INTERVAL) * INTERVAL
+        try:
+            return self.run_boundaries(due)
+        finally:
+            for r in due:
+                self.rows[r].n = lengths[r]
 
     def retire(self, row: int):
         """A finished request: its resident units (compacted table and tail)
