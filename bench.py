@@ -982,6 +982,19 @@ def main():
     barrier()
     torch.cuda.synchronize()
     ev = []   # (start, end, bytes) per fused decode launch
+    proj_ev = []   # (start, after the output projection, after its all-reduce) per layer
+
+    def after_layer_timed(l, o):
+        if w_o is None:
+            return
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        torch.matmul(o.reshape(o.shape[0], -1), w_o[l], out=hidden)
+        e1.record()
+        if group is not None and world > 1:
+            dist.all_reduce(hidden, op=dist.ReduceOp.SUM, group=group)
+        e2.record()
+        proj_ev.append((e0, e1, e2))
     bound_before = len(eng.boundary_ms)
     launches0 = kernels.LAUNCHES[0]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1005,7 +1018,7 @@ def main():
                 eng.decode_layer(l, q[l], out[l], sinks[l], scale)
                 b.record()
                 ev.append((a, b, nbytes))
-                after_layer(l, out[l])
+                after_layer_timed(l, out[l])
         eng.join_scores()          # the last layers' page scores are inside the timed region
         end.record()
         torch.cuda.synchronize()
@@ -1017,6 +1030,11 @@ def main():
     avg_launch_ms = statistics.mean(dur)
     avg_bytes = statistics.mean(x for _, _, x in ev)
     achieved_gbs = avg_bytes / (avg_launch_ms * 1e-3) / 1e9
+    layer_ms = {"attention": avg_launch_ms,
+                "o_proj": statistics.mean(a.elapsed_time(b) for a, b, _ in proj_ev) if proj_ev else None,
+                "all_reduce": statistics.mean(b.elapsed_time(c) for _, b, c in proj_ev) if proj_ev else None}
+    if world > 1:
+        layer_ms = {k: (max_over_ranks(v) if v is not None else None) for k, v in layer_ms.items()}
     boundary_ms = eng.boundary_ms[bound_before:]
     n_bound_rows = sum(1 for r in eng.active for e in eng.rows[r].events)
     value = B * args.steps / (elapsed_ms * 1e-3)
@@ -1081,6 +1099,9 @@ def main():
                         "attention outputs -> pinned host, every step; copies per layer on their "
                         "own streams, overlapped with the decode"},
         "gpu_launches": launches,
+        "layer_ms": dict(layer_ms, what="per layer, by CUDA events in the timed steps (max over ranks): the "
+                                        "fused decode launch, the row-parallel output projection, and its "
+                                        "NCCL all-reduce across ranks"),
         "evict": {"boundary_batches": len(boundary_ms),
                   "boundary_ms_mean": statistics.mean(boundary_ms) if boundary_ms else None,
                   "boundary_rows": n_bound_rows},

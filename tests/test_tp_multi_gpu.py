@@ -1,13 +1,13 @@
-"""KV-head tensor parallelism on two GPUs (NCCL): a head-sharded run must
-reproduce the single-GPU run on every rank.
+"""KV-head tensor parallelism on 2, 4 and 8 GPUs (NCCL): a head-sharded run
+must reproduce the single-GPU run on every rank.
 
 Each rank builds the same 8-head state, runs it whole (tp = 1) on its GPU,
-then runs its own 4 heads (tp = 2, head offset 4 * rank) and compares:
+then runs its own 8 / tp heads (head offset rank * 8 / tp) and compares:
 decode outputs and scores of its heads (test tolerance), and boundary
 results, tables, freed units, positions, scores and K/V pools bit for bit,
 for H2O global (per-head scores all-gathered over NCCL), random (slice of the
-shared draw) and reservoir (global head index) rows.  Skipped with fewer than
-two GPUs.
+shared draw) and reservoir (global head index) rows.  Each world size is
+skipped when the box has fewer GPUs.
 """
 import os
 import socket
@@ -148,19 +148,20 @@ def _rank_main(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_two_gpu_head_sharding_matches_single_gpu():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_head_sharding_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = dict(q.get(timeout=600) for _ in range(2))
+    out = dict(q.get(timeout=600) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
-    for rank in (0, 1):
+    for rank in range(world):
         assert out[rank] == [], (rank, out[rank])
     assert all(p.exitcode == 0 for p in procs)
