@@ -455,7 +455,11 @@ __device__ bool grid_barrier(int32_t* err) {
   const unsigned int add = blockIdx.x == 0 ? 0x80000000u - (n - 1u) : 1u;
   __threadfence();
   const unsigned int old = atomicAdd(&g_grid_bar, add);
-  if ((old & 0x7fffffffu) >= n) {   // more arrivals than blocks: state left by a failed barrier
+  // Valid low bits before this arrival: j < n arrivals of other blocks, or
+  // block 0's 2^31 - (n - 1) plus j < n - 1 of them.  Anything else is state
+  // left by a barrier that gave up.
+  const unsigned int low = old & 0x7fffffffu;
+  if (low >= n && low < 0x80000000u - (n - 1u)) {
     flag_error(err, CE_EW_TIMEOUT);
     return false;
   }
