@@ -7,13 +7,11 @@
 //
 // Work split (stream-K over tokens): the concatenation of all sequences'
 // 16-token-per-warp "stages" is cut into equal contiguous ranges, one per
-// persistent CTA (one CTA per SM, launched cooperatively).  A CTA walks its
-// range sequence by sequence and leaves one partial record (per-warp running
-// max m, sum l and unnormalised O) for every sequence it touched.  Record
-// (b, cta) lives at index b + cta, which is unique because both walks are
-// monotone.  After a grid barrier the same CTAs merge each sequence's records
-// with the sink into the output and the log-sum-exp (the second phase), so a
-// decode layer is one launch.
+// persistent CTA.  A CTA walks its range sequence by sequence and leaves one
+// partial record (per-warp running max m, sum l and unnormalised O) for every
+// sequence it touched.  Record (b, cta) lives at index b + cta, which is unique
+// because both walks are monotone.  combine_kernel then merges each
+// sequence's records with the sink into the output and the log-sum-exp.
 //
 // Inside a CTA: warp 8 is the producer.  It issues one 2D bulk-tensor (TMA)
 // load per KV page for K and one for V (box = the page's G*P rows of 128 B,
@@ -28,7 +26,7 @@
 // Scores need the final normaliser.  For H2O rows the consumer stores, per KV
 // page and query head, log2 of the page's probability mass relative to the
 // running max (CE_MODE_SUM), or every token's logit (CE_MODE_MAX, which needs a
-// max over heads per token).  The second phase, after merging a sequence, adds
+// max over heads per token).  combine_kernel, after merging a sequence, adds
 //   SUM: sum_h 2^(page_lse - LSE_h)   MAX: sum_t max_h 2^(s_t,h - LSE_h)
 // into scores[g, unit] with a plain read-modify-write: a unit appears once in
 // a batch, as in the reference kernel (runtime:199-200).  LSE_h is the same
@@ -88,9 +86,6 @@ struct Params {
   float* ul;         // [kv_capacity, H] unit log-mass (log2 units) or null
   float* tl;         // [kv_capacity * P, H] token logits (page_size > 1, MAX rows) or null
   int32_t* err;
-  int P;             // tokens per page
-  int chunks;        // combine tasks per (sequence, KV head)
-  int defer;         // CE_SCORE_DEFER: keep the normalisers in lse2, add no page scores
 };
 
 __device__ __forceinline__ int stage_tokens(int G) { return 16 * (NCW / G); }
@@ -166,359 +161,6 @@ __device__ void empty_sequence(const Params& p, int b) {
     const float s2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
     p.lse2[static_cast<int64_t>(b) * p.H + h] = s2;
     if (p.lse_out) p.lse_out[static_cast<int64_t>(b) * p.H + h] = s2 * LN2;
-  }
-}
-
-// ---- combine: records of a sequence + sink -> output, lse, page scores --------
-//
-// The attention kernel's second phase (after its grid barrier) and the
-// deferred-score kernel share these.  One task per (sequence b, KV head g,
-// chunk c): the chunks of a (b, g) split its eight query heads' output merges
-// and its page scoring between them, so a small batch (one sequence spread
-// over every CTA) still uses every SM.  Every task first rebuilds the eight
-// heads' normalisers from the sequence's record slots: one pass in which
-// thread t < 256 merges slots t, t+256, ... (each slot's eight maxima and sums
-// are two pairs of 16-byte loads), then a shared-memory reduction per head,
-// with the sink folded in (the normaliser of SGLang's stage 2 and of
-// runtime:179-188).  Threads at or above CB_THREADS (the attention kernel's
-// producer warp) only take part in the block barriers.
-constexpr int CB_THREADS = 256;
-constexpr int CB_SLOT_BATCH = 4;   // slots a thread loads before merging them
-constexpr int CB_MAX_CHUNKS = 64;
-
-
-__device__ __forceinline__ void merge_ml(float& m, float& l, float m2, float l2) {
-  if (m2 == -INFINITY) return;
-  const float mn = fmaxf(m, m2);
-  l = l * exp2f(m - mn) + l2 * exp2f(m2 - mn);
-  m = mn;
-}
-
-// Record slots of sequence b for KV head g: slot i is sub-part i % subs of
-// record k0 + i / subs (an attention CTA's warps over G heads: NCW / G of them
-// per head).
-struct SeqSlots {
-  int b, g, subs, k0, nslots;
-  int64_t S, grid;
-  __device__ const float* rec(const Params& p, int i) const {
-    return p.rec + static_cast<int64_t>(b + k0 + i / subs) * REC_FLOATS;
-  }
-  __device__ int vrow(int i, int G) const { return ((i % subs) * G + g) * GROUP; }  // + head row r
-  __device__ bool live(int i) const { return cta_has_work(k0 + i / subs, S, grid); }
-};
-
-// sh_l2[r] = log2 normaliser of query head g*8 + r (record maxima, sums and
-// the sink).  sh_m / sh_l: [GROUP][CB_THREADS] scratch.
-__device__ void group_normalisers(const Params& p, const SeqSlots& q, float* sh_m, float* sh_l,
-                                  float* sh_l2) {
-  const int tid = threadIdx.x, G = p.G;
-  float m[GROUP], l[GROUP];
-#pragma unroll
-  for (int r = 0; r < GROUP; ++r) {
-    m[r] = -INFINITY;
-    l[r] = 0.f;
-  }
-  for (int i0 = tid; tid < CB_THREADS && i0 < q.nslots; i0 += CB_THREADS * CB_SLOT_BATCH) {
-    float4 ma[CB_SLOT_BATCH], mb[CB_SLOT_BATCH], la[CB_SLOT_BATCH], lb[CB_SLOT_BATCH];
-#pragma unroll
-    for (int u = 0; u < CB_SLOT_BATCH; ++u) {
-      const int i = i0 + u * CB_THREADS;
-      ma[u] = mb[u] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      la[u] = lb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (i < q.nslots && q.live(i)) {
-        const float4* st = reinterpret_cast<const float4*>(q.rec(p, i) + REC_ROWS * D + q.vrow(i, G));
-        ma[u] = st[0];
-        mb[u] = st[1];
-        la[u] = st[REC_ROWS / 4];
-        lb[u] = st[REC_ROWS / 4 + 1];
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < CB_SLOT_BATCH; ++u) {
-      merge_ml(m[0], l[0], ma[u].x, la[u].x);
-      merge_ml(m[1], l[1], ma[u].y, la[u].y);
-      merge_ml(m[2], l[2], ma[u].z, la[u].z);
-      merge_ml(m[3], l[3], ma[u].w, la[u].w);
-      merge_ml(m[4], l[4], mb[u].x, lb[u].x);
-      merge_ml(m[5], l[5], mb[u].y, lb[u].y);
-      merge_ml(m[6], l[6], mb[u].z, lb[u].z);
-      merge_ml(m[7], l[7], mb[u].w, lb[u].w);
-    }
-  }
-  if (tid < CB_THREADS) {
-#pragma unroll
-    for (int r = 0; r < GROUP; ++r) {
-      sh_m[r * CB_THREADS + tid] = m[r];
-      sh_l[r * CB_THREADS + tid] = l[r];
-    }
-  }
-  __syncthreads();
-  // warp r < 8 reduces head r over the 256 partial states
-  const int warp = tid >> 5, lane = tid & 31;
-  if (warp >= GROUP) {
-    __syncthreads();
-    return;
-  }
-  float mw = -INFINITY, lw = 0.f;
-#pragma unroll
-  for (int k = 0; k < CB_THREADS / 32; ++k)
-    merge_ml(mw, lw, sh_m[warp * CB_THREADS + k * 32 + lane], sh_l[warp * CB_THREADS + k * 32 + lane]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, mw, o), l2 = __shfl_xor_sync(0xffffffffu, lw, o);
-    merge_ml(mw, lw, m2, l2);
-  }
-  if (lane == 0) {
-    const int h = q.g * GROUP + warp;
-    const float sink2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
-    const float M = fmaxf(mw, sink2);
-    float den = 0.f;
-    if (M != -INFINITY) {
-      den = (mw == -INFINITY) ? 0.f : lw * exp2f(mw - M);
-      if (p.sinks) den += exp2f(sink2 - M);
-    }
-    sh_l2[warp] = (M == -INFINITY) ? -INFINITY : M + log2f(den);
-  }
-  __syncthreads();
-}
-
-// Outputs of the query heads r = c, c + C, ... (r < 8) of KV head g: each a
-// sum over the slots of 2^(m_i - L2) O_i.  The block's threads split as heads
-// x 16 dimension quads x slot groups; partial sums meet in shared memory.
-__device__ void group_outputs(const Params& p, const SeqSlots& q, int c, int C, const float* sh_l2,
-                              float4* red) {
-  const int nh = (c < GROUP) ? (GROUP - 1 - c) / C + 1 : 0;
-  if (nh == 0) return;
-  const int nhr = nh <= 1 ? 1 : nh <= 2 ? 2 : nh <= 4 ? 4 : 8;
-  const int tph = CB_THREADS / nhr;        // threads per head
-  const int sgn = tph / 16;                // slot groups per head
-  const int tid = threadIdx.x, hh = tid / tph, lt = tid % tph, dq = lt & 15, sg = lt >> 4;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (hh < nh) {
-    const int r = c + hh * C;
-    const float L2 = sh_l2[r];
-    constexpr int AB = 4;
-    for (int i0 = sg; i0 < q.nslots; i0 += sgn * AB) {
-      float w[AB];
-      float4 o[AB];
-#pragma unroll
-      for (int u = 0; u < AB; ++u) {
-        const int i = i0 + u * sgn;
-        w[u] = 0.f;
-        o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < q.nslots && q.live(i) && L2 != -INFINITY) {
-          const float* rc = q.rec(p, i);
-          const int v = q.vrow(i, p.G) + r;
-          const float mk = rc[REC_ROWS * D + v];
-          if (mk != -INFINITY) {
-            w[u] = exp2f(mk - L2);
-            o[u] = reinterpret_cast<const float4*>(rc + v * D)[dq];
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < AB; ++u) {
-        if (w[u] != 0.f) {
-          acc.x += w[u] * o[u].x;
-          acc.y += w[u] * o[u].y;
-          acc.z += w[u] * o[u].z;
-          acc.w += w[u] * o[u].w;
-        }
-      }
-    }
-  }
-  if (tid < CB_THREADS) red[tid] = acc;
-  __syncthreads();
-  if (tid < nh * 16) {
-    const int h2 = tid >> 4, d2 = tid & 15;
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < sgn; ++k) {
-      const float4 v = red[h2 * tph + k * 16 + d2];
-      s.x += v.x;
-      s.y += v.y;
-      s.z += v.z;
-      s.w += v.w;
-    }
-    const int h = q.g * GROUP + c + h2 * C;
-    store_out(p, q.b, h, d2 * 4 + 0, s.x);
-    store_out(p, q.b, h, d2 * 4 + 1, s.y);
-    store_out(p, q.b, h, d2 * 4 + 2, s.z);
-    store_out(p, q.b, h, d2 * 4 + 3, s.w);
-  }
-}
-
-// Add pages [lo, hi) of sequence b's page masses for KV head g into scores[g, unit]:
-//   SUM: sum_h 2^(page_lse - LSE_h)   MAX: sum_t max_h 2^(s_t,h - LSE_h)
-// L2s holds the group's 8 log2 normalisers.  Each thread takes 4 pages per
-// round and issues all their loads before any store.
-__device__ void score_pages(const Params& p, int b, int g, int mode, int P, const float* L2s, int lo,
-                            int hi) {
-  const int H = p.H;
-  const int tokens = seq_tokens(p, b, P);
-  const int npages = (tokens + P - 1) / P;
-  hi = min(hi, npages);
-  const int64_t ip = p.kv_indptr[b];
-  float L2[GROUP];
-#pragma unroll
-  for (int rr = 0; rr < GROUP; ++rr) L2[rr] = L2s[rr];
-  const bool fresh_tail = p.zero_new && ((tokens - 1) % P) == 0;
-  const int32_t* __restrict__ kvi = p.kv_indices;
-  const float* __restrict__ ul = p.ul;
-  float* __restrict__ sc = p.scores + g * p.score_sg;
-  constexpr int BATCH = 4;
-  if (threadIdx.x >= CB_THREADS) return;
-  for (int j0 = lo + threadIdx.x * BATCH; j0 < hi; j0 += CB_THREADS * BATCH) {
-    int unit[BATCH];
-    float contrib[BATCH], old[BATCH];
-#pragma unroll
-    for (int q = 0; q < BATCH; ++q) {
-      const int jj = j0 + q;
-      unit[q] = -1;
-      if (jj < hi && ip + jj < p.kv_capacity) unit[q] = kvi[ip + jj];
-    }
-#pragma unroll
-    for (int q = 0; q < BATCH; ++q) {
-      const int jj = j0 + q;
-      contrib[q] = 0.f;
-      old[q] = 0.f;
-      if (unit[q] < 0 || unit[q] >= p.pool_units) continue;
-      old[q] = sc[unit[q]];
-      const int64_t cpos = ip + jj;
-      if (mode == CE_MODE_SUM) {
-        const float4* u4 = reinterpret_cast<const float4*>(ul + cpos * H + g * GROUP);
-        const float4 a = u4[0], c = u4[1];
-        const float uv[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-        for (int rr = 0; rr < GROUP; ++rr)
-          if (uv[rr] != -INFINITY) contrib[q] += exp2f(uv[rr] - L2[rr]);
-      } else if (P == 1) {
-        const float* uv = ul + cpos * H + g * GROUP;
-        float mx = 0.f;
-#pragma unroll
-        for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
-        contrib[q] = mx;
-      } else {
-        const int vt = (jj == npages - 1) ? tokens - jj * P : P;
-        for (int tt = 0; tt < vt; ++tt) {
-          const float* uv = p.tl + (cpos * P + tt) * H + g * GROUP;
-          float mx = 0.f;
-#pragma unroll
-          for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
-          contrib[q] += mx;
-        }
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < BATCH; ++q) {
-      const int jj = j0 + q;
-      if (jj >= hi) continue;
-      if (unit[q] < 0 || unit[q] >= p.pool_units) {
-        if (ip + jj < p.kv_capacity) flag_error(p.err, CE_EW_INDEX);
-        continue;
-      }
-      const bool fresh = fresh_tail && jj == npages - 1;
-      sc[unit[q]] = fresh ? contrib[q] : old[q] + contrib[q];
-    }
-  }
-}
-
-__device__ __forceinline__ int score_mode_of(const Params& p, int b, int P) {
-  int mode = (p.mode_of_row && p.scores && p.ul) ? seq_mode(p, b) : CE_MODE_NONE;
-  if (mode == CE_MODE_MAX && P > 1 && !p.tl) mode = CE_MODE_NONE;
-  return (mode == CE_MODE_SUM || mode == CE_MODE_MAX) ? mode : CE_MODE_NONE;
-}
-
-// Chunk c of C of sequence b's pages.
-__device__ __forceinline__ void chunk_pages(const Params& p, int b, int P, int c, int C, int& lo, int& hi) {
-  const int npages = (seq_tokens(p, b, P) + P - 1) / P;
-  const int per = (npages + C - 1) / C;
-  lo = min(npages, c * per);
-  hi = min(npages, lo + per);
-}
-
-
-// ---- grid barrier -------------------------------------------------------------
-// State of the attention kernel's grid barrier, per device: zero when the
-// module loads and back to zero in its low 31 bits after every barrier, so no
-// call has to initialise it.  Block 0 adds 2^31 - (n - 1), every other block
-// adds 1: the top bit flips exactly when all n blocks have arrived.  Every
-// attention CTA takes a whole SM's shared memory and the grid is launched
-// cooperatively with one CTA per SM, so only one attention grid can be at its
-// barrier at a time on a device.
-__device__ unsigned int g_grid_bar = 0;
-
-// Called by one thread per block, after the block's writes (ordered before by
-// __syncthreads).  Returns false when the wait gave up (CE_EW_TIMEOUT) or the
-// state was not a valid one (a previous barrier that timed out).
-__device__ bool grid_barrier(int32_t* err) {
-  const unsigned int n = gridDim.x;
-  const unsigned int add = blockIdx.x == 0 ? 0x80000000u - (n - 1u) : 1u;
-  __threadfence();
-  const unsigned int old = atomicAdd(&g_grid_bar, add);
-  // Valid low bits before this arrival: j < n arrivals of other blocks, or
-  // block 0's 2^31 - (n - 1) plus j < n - 1 of them.  Anything else is state
-  // left by a barrier that gave up.
-  const unsigned int low = old & 0x7fffffffu;
-  if (low >= n && low < 0x80000000u - (n - 1u)) {
-    flag_error(err, CE_EW_TIMEOUT);
-    return false;
-  }
-  const unsigned long long t0 = global_timer_ns();
-  while (true) {
-    unsigned int cur;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(&g_grid_bar) : "memory");
-    if ((cur ^ old) & 0x80000000u) break;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      flag_error(err, CE_EW_TIMEOUT);
-      return false;
-    }
-    __nanosleep(32);
-  }
-  __threadfence();
-  return true;
-}
-
-// The combine tasks of this call, spread over the grid: block k takes tasks
-// k, k + gridDim.x, ...  scratch: shared memory for the reductions.
-__device__ void combine_phase(const Params& p, int64_t S, int64_t grid, uint8_t* scratch) {
-  const int bs = p.bs, H = p.H, G = p.G, C = p.chunks;
-  const int hgroups = H / GROUP;
-  float* sh_m = reinterpret_cast<float*>(scratch);
-  float* sh_l = sh_m + GROUP * CB_THREADS;
-  float4* red = reinterpret_cast<float4*>(sh_l + GROUP * CB_THREADS);
-  float* sh_l2 = reinterpret_cast<float*>(red + CB_THREADS);
-  const int64_t ntasks = static_cast<int64_t>(bs) * hgroups * C;
-  for (int64_t task = blockIdx.x; task < ntasks; task += gridDim.x) {
-    const int c = static_cast<int>(task % C);
-    const int64_t bg = task / C;
-    const int b = static_cast<int>(bg / hgroups), hc = static_cast<int>(bg % hgroups);
-    const int64_t pre = p.prefix[b], n = p.prefix[b + 1] - pre;
-    if (n <= 0) continue;   // empty sequences were written in the first phase
-    SeqSlots q;
-    q.b = b;
-    q.g = hc;
-    q.subs = NCW / G;
-    q.S = S;
-    q.grid = grid;
-    q.k0 = cta_of_stage(pre, S, grid);
-    q.nslots = (cta_of_stage(pre + n - 1, S, grid) - q.k0 + 1) * q.subs;
-    group_normalisers(p, q, sh_m, sh_l, sh_l2);
-    group_outputs(p, q, c, C, sh_l2, red);
-    if (c == 0 && threadIdx.x < GROUP) {
-      const int h = hc * GROUP + threadIdx.x;
-      const float L2 = sh_l2[threadIdx.x];
-      if (p.lse_out) p.lse_out[static_cast<int64_t>(b) * H + h] = L2 * LN2;
-      if (p.defer) p.lse2[static_cast<int64_t>(b) * H + h] = L2;
-    }
-    if (!p.defer) {   // else score_kernel adds the page masses later
-      const int mode = score_mode_of(p, b, p.P);
-      if (mode != CE_MODE_NONE) {
-        int lo, hi;
-        chunk_pages(p, b, p.P, c, C, lo, hi);
-        score_pages(p, b, hc, mode, p.P, sh_l2, lo, hi);
-      }
-    }
-    __syncthreads();
   }
 }
 
@@ -916,36 +558,337 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (cur_b >= 0) leave(cur_b);
   }
-  // ---- second phase: every CTA's records are written; merge them ------------
-  // The producer has drained its loads, so the stage ring is free for the
-  // reductions.  A CTA whose barrier wait gave up skips the phase (the error
-  // word says so).
-  volatile int* phase_ok = abort_flag + 1;
   __syncthreads();
-  if (tid == 0) *phase_ok = grid_barrier(p.err) ? 1 : 0;
+}
+
+// ---- combine: records of a sequence + sink -> output, lse, page scores --------
+//
+// One task per (sequence b, KV head g, chunk c): the chunks of a (b, g) split
+// its eight query heads' output merges and its page scoring between them, so
+// a small batch (one sequence spread over every attention CTA) still fills the
+// GPU.  Every task first rebuilds the eight heads' normalisers from the
+// sequence's record slots: one pass in which thread t merges slots t, t+256,
+// ... (each slot's eight maxima and sums are two pairs of 16-byte loads), then
+// a shared-memory reduction per head, with the sink folded in (the normaliser
+// of SGLang's stage 2 and of runtime:179-188).
+constexpr int CB_THREADS = 256;
+constexpr int CB_SLOT_BATCH = 4;   // slots a thread loads before merging them
+constexpr int CB_MAX_CHUNKS = 64;
+
+struct CombineParams {
+  Params a;
+  int grid;     // CTAs the attention kernel was launched with
+  int P;
+  int defer;    // CE_SCORE_DEFER: keep the normalisers in lse2, add no scores here
+  int chunks;   // tasks per (sequence, KV head)
+};
+
+__device__ __forceinline__ void merge_ml(float& m, float& l, float m2, float l2) {
+  if (m2 == -INFINITY) return;
+  const float mn = fmaxf(m, m2);
+  l = l * exp2f(m - mn) + l2 * exp2f(m2 - mn);
+  m = mn;
+}
+
+// Record slots of sequence b for KV head g: slot i is sub-part i % subs of
+// record k0 + i / subs (an attention CTA's warps over G heads: NCW / G of them
+// per head).
+struct SeqSlots {
+  int b, g, subs, k0, nslots;
+  int64_t S, grid;
+  __device__ const float* rec(const Params& p, int i) const {
+    return p.rec + static_cast<int64_t>(b + k0 + i / subs) * REC_FLOATS;
+  }
+  __device__ int vrow(int i, int G) const { return ((i % subs) * G + g) * GROUP; }  // + head row r
+  __device__ bool live(int i) const { return cta_has_work(k0 + i / subs, S, grid); }
+};
+
+// sh_l2[r] = log2 normaliser of query head g*8 + r (record maxima, sums and
+// the sink).  sh_m / sh_l: [GROUP][CB_THREADS] scratch.
+__device__ void group_normalisers(const Params& p, const SeqSlots& q, float* sh_m, float* sh_l,
+                                  float* sh_l2) {
+  const int tid = threadIdx.x, G = p.G;
+  float m[GROUP], l[GROUP];
+#pragma unroll
+  for (int r = 0; r < GROUP; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+  }
+  for (int i0 = tid; i0 < q.nslots; i0 += CB_THREADS * CB_SLOT_BATCH) {
+    float4 ma[CB_SLOT_BATCH], mb[CB_SLOT_BATCH], la[CB_SLOT_BATCH], lb[CB_SLOT_BATCH];
+#pragma unroll
+    for (int u = 0; u < CB_SLOT_BATCH; ++u) {
+      const int i = i0 + u * CB_THREADS;
+      ma[u] = mb[u] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      la[u] = lb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < q.nslots && q.live(i)) {
+        const float4* st = reinterpret_cast<const float4*>(q.rec(p, i) + REC_ROWS * D + q.vrow(i, G));
+        ma[u] = st[0];
+        mb[u] = st[1];
+        la[u] = st[REC_ROWS / 4];
+        lb[u] = st[REC_ROWS / 4 + 1];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < CB_SLOT_BATCH; ++u) {
+      merge_ml(m[0], l[0], ma[u].x, la[u].x);
+      merge_ml(m[1], l[1], ma[u].y, la[u].y);
+      merge_ml(m[2], l[2], ma[u].z, la[u].z);
+      merge_ml(m[3], l[3], ma[u].w, la[u].w);
+      merge_ml(m[4], l[4], mb[u].x, lb[u].x);
+      merge_ml(m[5], l[5], mb[u].y, lb[u].y);
+      merge_ml(m[6], l[6], mb[u].z, lb[u].z);
+      merge_ml(m[7], l[7], mb[u].w, lb[u].w);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < GROUP; ++r) {
+    sh_m[r * CB_THREADS + tid] = m[r];
+    sh_l[r * CB_THREADS + tid] = l[r];
+  }
   __syncthreads();
-  if (*phase_ok) combine_phase(p, S, grid, smem);
+  // warp r reduces head r over the 256 partial states
+  const int warp = tid >> 5, lane = tid & 31;
+  float mw = -INFINITY, lw = 0.f;
+#pragma unroll
+  for (int k = 0; k < CB_THREADS / 32; ++k)
+    merge_ml(mw, lw, sh_m[warp * CB_THREADS + k * 32 + lane], sh_l[warp * CB_THREADS + k * 32 + lane]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, mw, o), l2 = __shfl_xor_sync(0xffffffffu, lw, o);
+    merge_ml(mw, lw, m2, l2);
+  }
+  if (lane == 0) {
+    const int h = q.g * GROUP + warp;
+    const float sink2 = p.sinks ? p.sinks[h] * LOG2E : -INFINITY;
+    const float M = fmaxf(mw, sink2);
+    float den = 0.f;
+    if (M != -INFINITY) {
+      den = (mw == -INFINITY) ? 0.f : lw * exp2f(mw - M);
+      if (p.sinks) den += exp2f(sink2 - M);
+    }
+    sh_l2[warp] = (M == -INFINITY) ? -INFINITY : M + log2f(den);
+  }
+  __syncthreads();
+}
+
+// Outputs of the query heads r = c, c + C, ... (r < 8) of KV head g: each a
+// sum over the slots of 2^(m_i - L2) O_i.  The block's threads split as heads
+// x 16 dimension quads x slot groups; partial sums meet in shared memory.
+__device__ void group_outputs(const Params& p, const SeqSlots& q, int c, int C, const float* sh_l2,
+                              float4* red) {
+  const int nh = (c < GROUP) ? (GROUP - 1 - c) / C + 1 : 0;
+  if (nh == 0) return;
+  const int nhr = nh <= 1 ? 1 : nh <= 2 ? 2 : nh <= 4 ? 4 : 8;
+  const int tph = CB_THREADS / nhr;        // threads per head
+  const int sgn = tph / 16;                // slot groups per head
+  const int tid = threadIdx.x, hh = tid / tph, lt = tid % tph, dq = lt & 15, sg = lt >> 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (hh < nh) {
+    const int r = c + hh * C;
+    const float L2 = sh_l2[r];
+    constexpr int AB = 4;
+    for (int i0 = sg; i0 < q.nslots; i0 += sgn * AB) {
+      float w[AB];
+      float4 o[AB];
+#pragma unroll
+      for (int u = 0; u < AB; ++u) {
+        const int i = i0 + u * sgn;
+        w[u] = 0.f;
+        o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < q.nslots && q.live(i) && L2 != -INFINITY) {
+          const float* rc = q.rec(p, i);
+          const int v = q.vrow(i, p.G) + r;
+          const float mk = rc[REC_ROWS * D + v];
+          if (mk != -INFINITY) {
+            w[u] = exp2f(mk - L2);
+            o[u] = reinterpret_cast<const float4*>(rc + v * D)[dq];
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < AB; ++u) {
+        if (w[u] != 0.f) {
+          acc.x += w[u] * o[u].x;
+          acc.y += w[u] * o[u].y;
+          acc.z += w[u] * o[u].z;
+          acc.w += w[u] * o[u].w;
+        }
+      }
+    }
+  }
+  red[tid] = acc;
+  __syncthreads();
+  if (tid < nh * 16) {
+    const int h2 = tid >> 4, d2 = tid & 15;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < sgn; ++k) {
+      const float4 v = red[h2 * tph + k * 16 + d2];
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    const int h = q.g * GROUP + c + h2 * C;
+    store_out(p, q.b, h, d2 * 4 + 0, s.x);
+    store_out(p, q.b, h, d2 * 4 + 1, s.y);
+    store_out(p, q.b, h, d2 * 4 + 2, s.z);
+    store_out(p, q.b, h, d2 * 4 + 3, s.w);
+  }
+}
+
+// Add pages [lo, hi) of sequence b's page masses for KV head g into scores[g, unit]:
+//   SUM: sum_h 2^(page_lse - LSE_h)   MAX: sum_t max_h 2^(s_t,h - LSE_h)
+// L2s holds the group's 8 log2 normalisers.  Each thread takes 4 pages per
+// round and issues all their loads before any store.
+__device__ void score_pages(const Params& p, int b, int g, int mode, int P, const float* L2s, int lo,
+                            int hi) {
+  const int H = p.H;
+  const int tokens = seq_tokens(p, b, P);
+  const int npages = (tokens + P - 1) / P;
+  hi = min(hi, npages);
+  const int64_t ip = p.kv_indptr[b];
+  float L2[GROUP];
+#pragma unroll
+  for (int rr = 0; rr < GROUP; ++rr) L2[rr] = L2s[rr];
+  const bool fresh_tail = p.zero_new && ((tokens - 1) % P) == 0;
+  const int32_t* __restrict__ kvi = p.kv_indices;
+  const float* __restrict__ ul = p.ul;
+  float* __restrict__ sc = p.scores + g * p.score_sg;
+  constexpr int BATCH = 4;
+  for (int j0 = lo + threadIdx.x * BATCH; j0 < hi; j0 += CB_THREADS * BATCH) {
+    int unit[BATCH];
+    float contrib[BATCH], old[BATCH];
+#pragma unroll
+    for (int q = 0; q < BATCH; ++q) {
+      const int jj = j0 + q;
+      unit[q] = -1;
+      if (jj < hi && ip + jj < p.kv_capacity) unit[q] = kvi[ip + jj];
+    }
+#pragma unroll
+    for (int q = 0; q < BATCH; ++q) {
+      const int jj = j0 + q;
+      contrib[q] = 0.f;
+      old[q] = 0.f;
+      if (unit[q] < 0 || unit[q] >= p.pool_units) continue;
+      old[q] = sc[unit[q]];
+      const int64_t cpos = ip + jj;
+      if (mode == CE_MODE_SUM) {
+        const float4* u4 = reinterpret_cast<const float4*>(ul + cpos * H + g * GROUP);
+        const float4 a = u4[0], c = u4[1];
+        const float uv[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int rr = 0; rr < GROUP; ++rr)
+          if (uv[rr] != -INFINITY) contrib[q] += exp2f(uv[rr] - L2[rr]);
+      } else if (P == 1) {
+        const float* uv = ul + cpos * H + g * GROUP;
+        float mx = 0.f;
+#pragma unroll
+        for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
+        contrib[q] = mx;
+      } else {
+        const int vt = (jj == npages - 1) ? tokens - jj * P : P;
+        for (int tt = 0; tt < vt; ++tt) {
+          const float* uv = p.tl + (cpos * P + tt) * H + g * GROUP;
+          float mx = 0.f;
+#pragma unroll
+          for (int rr = 0; rr < GROUP; ++rr) mx = fmaxf(mx, exp2f(uv[rr] - L2[rr]));
+          contrib[q] += mx;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < BATCH; ++q) {
+      const int jj = j0 + q;
+      if (jj >= hi) continue;
+      if (unit[q] < 0 || unit[q] >= p.pool_units) {
+        if (ip + jj < p.kv_capacity) flag_error(p.err, CE_EW_INDEX);
+        continue;
+      }
+      const bool fresh = fresh_tail && jj == npages - 1;
+      sc[unit[q]] = fresh ? contrib[q] : old[q] + contrib[q];
+    }
+  }
+}
+
+__device__ __forceinline__ int score_mode_of(const Params& p, int b, int P) {
+  int mode = (p.mode_of_row && p.scores && p.ul) ? seq_mode(p, b) : CE_MODE_NONE;
+  if (mode == CE_MODE_MAX && P > 1 && !p.tl) mode = CE_MODE_NONE;
+  return (mode == CE_MODE_SUM || mode == CE_MODE_MAX) ? mode : CE_MODE_NONE;
+}
+
+// Chunk c of C of sequence b's pages.
+__device__ __forceinline__ void chunk_pages(const Params& p, int b, int P, int c, int C, int& lo, int& hi) {
+  const int npages = (seq_tokens(p, b, P) + P - 1) / P;
+  const int per = (npages + C - 1) / C;
+  lo = min(npages, c * per);
+  hi = min(npages, lo + per);
+}
+
+__global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams cp) {
+  const Params& p = cp.a;
+  const int bs = p.bs, H = p.H, G = p.G, C = cp.chunks;
+  const int64_t S = p.prefix[bs];
+  const int64_t grid = eff_grid(S, cp.grid);
+  const int hgroups = H / GROUP;
+  const int64_t ntasks = static_cast<int64_t>(bs) * hgroups * C;
+  __shared__ float sh_m[GROUP * CB_THREADS], sh_l[GROUP * CB_THREADS];
+  __shared__ float4 red[CB_THREADS];
+  __shared__ float sh_l2[GROUP];
+  for (int64_t task = blockIdx.x; task < ntasks; task += gridDim.x) {
+    const int c = static_cast<int>(task % C);
+    const int64_t bg = task / C;
+    const int b = static_cast<int>(bg / hgroups), hc = static_cast<int>(bg % hgroups);
+    const int64_t pre = p.prefix[b], n = p.prefix[b + 1] - pre;
+    if (n <= 0) continue;   // empty sequences were written by the attention kernel
+    SeqSlots q;
+    q.b = b;
+    q.g = hc;
+    q.subs = NCW / G;
+    q.S = S;
+    q.grid = grid;
+    q.k0 = cta_of_stage(pre, S, grid);
+    q.nslots = (cta_of_stage(pre + n - 1, S, grid) - q.k0 + 1) * q.subs;
+    group_normalisers(p, q, sh_m, sh_l, sh_l2);
+    group_outputs(p, q, c, C, sh_l2, red);
+    if (c == 0 && threadIdx.x < GROUP) {
+      const int h = hc * GROUP + threadIdx.x;
+      const float L2 = sh_l2[threadIdx.x];
+      if (p.lse_out) p.lse_out[static_cast<int64_t>(b) * H + h] = L2 * LN2;
+      if (cp.defer) p.lse2[static_cast<int64_t>(b) * H + h] = L2;
+    }
+    if (!cp.defer) {   // else score_kernel adds the page masses later
+      const int mode = score_mode_of(p, b, cp.P);
+      if (mode != CE_MODE_NONE) {
+        int lo, hi;
+        chunk_pages(p, b, cp.P, c, C, lo, hi);
+        score_pages(p, b, hc, mode, cp.P, sh_l2, lo, hi);
+      }
+    }
+    __syncthreads();
+  }
 }
 
 // The page masses of a deferred decode (CE_SCORE_DEFER): the same work as
-// the attention kernel's second phase, one task per (sequence, KV head,
-// chunk), from the normalisers that phase left in lse2.  Small enough to run beside
+// the tail of combine_kernel, one task per (sequence, KV head, chunk), from
+// the normalisers combine_kernel left in lse2.  Small enough to run beside
 // the next layer's attention kernel on another stream.
-__global__ void __launch_bounds__(CB_THREADS) score_kernel(const Params p) {
-  const int hgroups = p.H / GROUP, C = p.chunks;
+__global__ void __launch_bounds__(CB_THREADS) score_kernel(const CombineParams cp) {
+  const Params& p = cp.a;
+  const int hgroups = p.H / GROUP, C = cp.chunks;
   const int64_t ntasks = static_cast<int64_t>(p.bs) * hgroups * C;
   __shared__ float sh_l2[GROUP];
   for (int64_t task = blockIdx.x; task < ntasks; task += gridDim.x) {
     const int c = static_cast<int>(task % C);
     const int64_t bg = task / C;
     const int b = static_cast<int>(bg / hgroups), hc = static_cast<int>(bg % hgroups);
-    const int mode = score_mode_of(p, b, p.P);
-    if (seq_tokens(p, b, p.P) <= 0 || mode == CE_MODE_NONE) continue;
+    const int mode = score_mode_of(p, b, cp.P);
+    if (seq_tokens(p, b, cp.P) <= 0 || mode == CE_MODE_NONE) continue;
     if (threadIdx.x < GROUP) sh_l2[threadIdx.x] = p.lse2[static_cast<int64_t>(b) * p.H + hc * GROUP + threadIdx.x];
     __syncthreads();
     int lo, hi;
-    chunk_pages(p, b, p.P, c, C, lo, hi);
-    score_pages(p, b, hc, mode, p.P, sh_l2, lo, hi);
+    chunk_pages(p, b, cp.P, c, C, lo, hi);
+    score_pages(p, b, hc, mode, cp.P, sh_l2, lo, hi);
     __syncthreads();
   }
 }
@@ -960,19 +903,10 @@ namespace {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Combine tasks per (sequence, KV head) in the attention kernel's second
-// phase: when the batch alone has fewer (sequence, KV head) pairs than CTAs,
-// as many chunks as keep the tasks within one per CTA (a batch-1 decode has
-// one pair per KV head otherwise).
-int phase_chunks(int bs, int H, int grid) {
-  const int64_t base = static_cast<int64_t>(bs) * (H / GROUP);
-  if (base <= 0 || base >= grid) return 1;
-  return static_cast<int>(std::min<int64_t>(grid / base, CB_MAX_CHUNKS));
-}
-
-// Tasks per (sequence, KV head) of the deferred score kernel: about two
-// blocks per SM when the batch alone would leave SMs idle.
-int score_chunks(int bs, int H, int sms) {
+// Tasks per (sequence, KV head) of the combine and score kernels: enough for
+// about two blocks per SM when the batch alone would leave SMs idle (a
+// batch-1 decode has one task per KV head otherwise).
+int combine_chunks(int bs, int H, int sms) {
   const int64_t base = static_cast<int64_t>(bs) * (H / GROUP);
   if (base <= 0) return 1;
   const int64_t c = (2LL * sms + base - 1) / base;
@@ -1084,28 +1018,33 @@ extern "C" int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh, c
   p.tl = ((score_flags & 2) && page_size > 1) ? reinterpret_cast<float*>(ws + L.tl) : nullptr;
   p.err = err;
 
-  p.P = page_size;
-  p.defer = (score_flags & CE_SCORE_DEFER) ? 1 : 0;
-  p.chunks = phase_chunks(bs, num_q_heads, grid);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (page_size == 16) {
     if (!host::set_smem(attn_kernel<16>, SMEM_BYTES)) return host::fail(CE_ERR_CUDA, "smem attr");
-    if (host::launch_cooperative(attn_kernel<16>, dim3(grid), dim3(THREADS), SMEM_BYTES, st, kmap, vmap, p) !=
-        cudaSuccess)
-      return host::fail_cuda("attn_kernel launch");
+    attn_kernel<16><<<grid, THREADS, SMEM_BYTES, st>>>(kmap, vmap, p);
   } else {
     if (!host::set_smem(attn_kernel<1>, SMEM_BYTES)) return host::fail(CE_ERR_CUDA, "smem attr");
-    if (host::launch_cooperative(attn_kernel<1>, dim3(grid), dim3(THREADS), SMEM_BYTES, st, kmap, vmap, p) !=
-        cudaSuccess)
-      return host::fail_cuda("attn_kernel launch");
+    attn_kernel<1><<<grid, THREADS, SMEM_BYTES, st>>>(kmap, vmap, p);
   }
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("attn_kernel launch");
+  const bool defer = (score_flags & CE_SCORE_DEFER) != 0;
+  CombineParams cp{p, grid, page_size, defer ? 1 : 0, combine_chunks(bs, num_q_heads, grid)};
+  // A deferred decode's page scores run beside the next layer's attention
+  // kernel (195 KB of shared memory per CTA): keep SMs at the largest carveout.
+  if (defer && !host::set_max_shared_carveout(combine_kernel)) return host::fail(CE_ERR_CUDA, "carveout attr");
+  const int cb_grid = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP) * cp.chunks, 4LL * grid)));
+  combine_kernel<<<cb_grid, CB_THREADS, 0, st>>>(cp);
+  if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("combine_kernel launch");
   return CE_OK;
 }
 
 int ce::host::decode_prepare_device() {
   // cudaFuncGetAttributes loads a kernel under lazy module loading; the
   // shared-memory attribute is the one the first launch would set.
-  if (!host::set_smem(attn_kernel<16>, SMEM_BYTES) || !host::set_smem(attn_kernel<1>, SMEM_BYTES))
+  cudaFuncAttributes a;
+  if (!host::set_smem(attn_kernel<16>, SMEM_BYTES) || !host::set_smem(attn_kernel<1>, SMEM_BYTES) ||
+      cudaFuncGetAttributes(&a, combine_kernel) != cudaSuccess)
     return host::fail_cuda("decode kernels: set-up");
   return CE_OK;
 }
@@ -1148,13 +1087,11 @@ extern "C" int ce_decode_scores(const int32_t* kv_indptr, const int32_t* kv_indi
   p.ul = reinterpret_cast<float*>(ws + L.ul);
   p.tl = ((score_flags & 2) && page_size > 1) ? reinterpret_cast<float*>(ws + L.tl) : nullptr;
   p.err = err;
-  p.P = page_size;
-  p.defer = 1;
-  p.chunks = score_chunks(bs, num_q_heads, grid);
+  CombineParams cp{p, grid, page_size, 1, combine_chunks(bs, num_q_heads, grid)};
   if (!host::set_max_shared_carveout(score_kernel)) return host::fail(CE_ERR_CUDA, "carveout attr");
   const int sc_grid = static_cast<int>(std::max<int64_t>(
-      1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP) * p.chunks, 2LL * grid)));
-  score_kernel<<<sc_grid, CB_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(p);
+      1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP) * cp.chunks, 2LL * grid)));
+  score_kernel<<<sc_grid, CB_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(cp);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("score_kernel launch");
   return CE_OK;
 }

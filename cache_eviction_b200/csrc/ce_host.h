@@ -4,7 +4,6 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
-#include <utility>
 
 namespace ce {
 namespace host {
@@ -46,24 +45,6 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
 // {cols, box_rows}, 128-byte swizzle, zero fill out of bounds.
 bool encode_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint32_t cols,
                      uint32_t box_rows);
-
-// Launch `kernel` on `st` as a cooperative grid: every block is resident at
-// once (or the launch fails), so its blocks may wait for one another.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_cooperative(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                               cudaStream_t st, Args&&... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
 
 // Loads every kernel that ce_decode_attn_score launches on the current device
 // and sets their launch attributes, which that entry point otherwise does on

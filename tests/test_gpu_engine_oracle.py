@@ -249,10 +249,12 @@ def _run(eng, steps, seed, check_kept_row=None, churn=None):
             if l:
                 return
             torch.cuda.synchronize()
+            # the step already allocated the new tokens' pages (after its
+            # boundaries, whose columns end below them): take them first
+            m.take_new_pages()
             if due:
                 res = m.boundary_from_engine()
                 seen.extend((r, int(res[i, 0])) for i, r in enumerate(eng.last_batch["rows"]))
-            m.take_new_pages()
             ctx["csr"] = m.csr()
             m.write_new_tokens(gen_cpu)
 
