@@ -849,6 +849,25 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams
     q.grid = grid;
     q.k0 = cta_of_stage(pre, S, grid);
     q.nslots = (cta_of_stage(pre + n - 1, S, grid) - q.k0 + 1) * q.subs;
+    // Page scoring (else score_kernel adds the page masses later).  A chunk of
+    // at most one page per thread (small batches) issues its page's index and
+    // log-masses before the normaliser merge, which they do not depend on, so
+    // their latency hides behind it; only the old score's load (which needs
+    // the index) and the store follow the merge.
+    const int mode = cp.defer ? CE_MODE_NONE : score_mode_of(p, b, cp.P);
+    int lo = 0, hi = 0;
+    if (mode != CE_MODE_NONE) chunk_pages(p, b, cp.P, c, C, lo, hi);
+    const bool early = mode != CE_MODE_NONE && hi - lo <= CB_THREADS && (mode == CE_MODE_SUM || cp.P == 1);
+    const int jj = lo + threadIdx.x;
+    const int64_t cpos = p.kv_indptr[b] + jj;
+    int unit = -1;
+    float4 ua = make_float4(0.f, 0.f, 0.f, 0.f), ub = ua;
+    if (early && jj < hi && cpos < p.kv_capacity) {
+      unit = p.kv_indices[cpos];
+      const float4* u4 = reinterpret_cast<const float4*>(p.ul + cpos * H + hc * GROUP);
+      ua = u4[0];
+      ub = u4[1];
+    }
     group_normalisers(p, q, sh_m, sh_l, sh_l2);
     group_outputs(p, q, c, C, sh_l2, red);
     if (c == 0 && threadIdx.x < GROUP) {
@@ -857,13 +876,31 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams
       if (p.lse_out) p.lse_out[static_cast<int64_t>(b) * H + h] = L2 * LN2;
       if (cp.defer) p.lse2[static_cast<int64_t>(b) * H + h] = L2;
     }
-    if (!cp.defer) {   // else score_kernel adds the page masses later
-      const int mode = score_mode_of(p, b, cp.P);
-      if (mode != CE_MODE_NONE) {
-        int lo, hi;
-        chunk_pages(p, b, cp.P, c, C, lo, hi);
-        score_pages(p, b, hc, mode, cp.P, sh_l2, lo, hi);
+    if (early) {
+      if (jj < hi && cpos < p.kv_capacity) {
+        if (unit < 0 || unit >= p.pool_units) {
+          flag_error(p.err, CE_EW_INDEX);
+        } else {
+          float* sc = p.scores + hc * p.score_sg;
+          const float old = sc[unit];
+          const float uv[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+          float contrib = 0.f;
+          if (mode == CE_MODE_SUM) {
+#pragma unroll
+            for (int rr = 0; rr < GROUP; ++rr)
+              if (uv[rr] != -INFINITY) contrib += exp2f(uv[rr] - sh_l2[rr]);
+          } else {   // MAX at page size 1: the page is one token
+#pragma unroll
+            for (int rr = 0; rr < GROUP; ++rr) contrib = fmaxf(contrib, exp2f(uv[rr] - sh_l2[rr]));
+          }
+          const int tokens = seq_tokens(p, b, cp.P);
+          const int npages = (tokens + cp.P - 1) / cp.P;
+          const bool fresh = p.zero_new && ((tokens - 1) % cp.P) == 0 && jj == npages - 1;
+          sc[unit] = fresh ? contrib : old + contrib;
+        }
       }
+    } else if (mode != CE_MODE_NONE) {
+      score_pages(p, b, hc, mode, cp.P, sh_l2, lo, hi);
     }
     __syncthreads();
   }
