@@ -697,15 +697,17 @@ __device__ void group_outputs(const Params& p, const SeqSlots& q, int c, int C, 
         w[u] = 0.f;
         o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (i < q.nslots && q.live(i) && L2 != -INFINITY) {
+          // the slot's maximum and its output row are loaded together
           const float* rc = q.rec(p, i);
           const int v = q.vrow(i, p.G) + r;
-          const float mk = rc[REC_ROWS * D + v];
-          if (mk != -INFINITY) {
-            w[u] = exp2f(mk - L2);
-            o[u] = reinterpret_cast<const float4*>(rc + v * D)[dq];
-          }
+          w[u] = rc[REC_ROWS * D + v];
+          o[u] = reinterpret_cast<const float4*>(rc + v * D)[dq];
+        } else {
+          w[u] = -INFINITY;
         }
       }
+#pragma unroll
+      for (int u = 0; u < AB; ++u) w[u] = w[u] == -INFINITY ? 0.f : exp2f(w[u] - L2);
 #pragma unroll
       for (int u = 0; u < AB; ++u) {
         if (w[u] != 0.f) {
