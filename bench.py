@@ -655,6 +655,72 @@ def _shard_offset(rank, world):
     return tp.shard(G_TOTAL, H_TOTAL, rank, world)[2]
 
 
+def model2_microbench(world, rank, device, max_len=16384, prompt_len=1024, seg=512, seed=2):
+    """a gpt-oss-20b-shaped decoder with random bf16 weights
+    (24 layers alternating a 128-token sliding window and full attention,
+    hidden 2880, 32 experts top 4, vocabulary 201,088; cache_eviction_b200.oss20b),
+    batch 1, a 1,024-token prompt of seeded uniform token ids, greedy decoding
+    to 16,384 tokens.  Per-head H2O on the 12 full layers at budget 8192 = 512
+    prefix + 1,024 recent + 6,656 scored, against the same decoder with H2O
+    scoring off and the same boundaries (the full-cache rate at the same
+    resident KV) and against a full cache that keeps every token; the three
+    share the weights and are timed over their 15,360 generated tokens in
+    alternating 512-step segments (each step one CUDA graph; the boundary
+    steps run their boundary eagerly first).  One GPU: the model is not split
+    across ranks."""
+    import torch
+    from cache_eviction_b200.oss20b import OssConfig, OssDecoder, OssWeights
+    from cache_eviction_b200.policy import EvictionConfig
+    if world > 1:
+        return {"skipped": "config 2 runs on one GPU (the decoder is not sharded over ranks)"}
+    cfg = OssConfig()
+    t0 = time.perf_counter()
+    W = OssWeights(cfg, device, seed=seed)
+    torch.cuda.synchronize()
+    init_s = time.perf_counter() - t0
+    ev = EvictionConfig("head_sum_2048", 8192, 512, 1024, seed=seed)
+    decs = {"scored": OssDecoder(W, ev, max_len, scored=True, device=device),
+            "no_score_same_resident": OssDecoder(W, ev, max_len, scored=False, device=device),
+            "full_cache": OssDecoder(W, None, max_len, scored=False, device=device)}
+    gen = torch.Generator(device=device).manual_seed(seed + 1)
+    prompt = torch.randint(0, cfg.vocab, (prompt_len,), generator=gen, device=device)
+    for d in decs.values():
+        d.prefill(prompt)
+    torch.cuda.synchronize()
+    steps = max_len - prompt_len
+
+    def runner(d):
+        def fn(n):
+            for _ in range(n):
+                d.step()
+        return fn
+
+    ms_a, ms_b, pairs = paired_segments(runner(decs["scored"]), runner(decs["no_score_same_resident"]), steps, seg)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    runner(decs["full_cache"])(steps)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = {"scored": ms_a, "no_score_same_resident": ms_b, "full_cache": e0.elapsed_time(e1)}
+    out = {}
+    for name, d in decs.items():
+        eng = d.eng
+        eng.check_errors()
+        out[name] = {"tok_s": steps / (ms[name] * 1e-3), "ms_per_token": ms[name] / steps,
+                     "tokens": d.n, "resident_tokens_end": eng.resident_tokens(0),
+                     "boundaries": [e["boundary"] for e in eng.rows[0].events if e["status"] == 0]}
+    out["scored_over_no_score"] = out["scored"]["tok_s"] / out["no_score_same_resident"]["tok_s"]
+    out["scored_over_full_cache"] = out["scored"]["tok_s"] / out["full_cache"]["tok_s"]
+    out["weights_gb"] = sum(t.numel() * 2 for t in [W.embed, W.lm_head] +
+                            [v for lw in W.layers for v in lw.values() if v.dtype == torch.bfloat16]) / 1e9
+    out["weight_init_s"] = init_s
+    out["timing"] = (f"{steps} generated tokens per decoder; scored and unscored in alternating {seg}-step "
+                     f"segments ({len(pairs)} pairs), the full cache after them")
+    del decs, W
+    torch.cuda.empty_cache()
+    return out
+
+
 PREFILL_CHUNK = 2048
 PREFILL_PREFIXES = (0, 8192, 26624)   # resident tokens before a chunk; 26,624 + 2,048 = config 4's cache
 
@@ -886,7 +952,7 @@ def main():
                     help="skip the config-5 eviction-step leg")
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (small cases for profiling)")
-    ap.add_argument("--legs", default="decode,e2e,noscore,cb3,decode4,prefill4,evict5,select1,evict1",
+    ap.add_argument("--legs", default="decode,e2e,noscore,cb3,model2,decode4,prefill4,evict5,select1,evict1",
                     help="legs to run; without 'decode' only the listed microbenchmarks run "
                          "and one JSON line with their results is printed (profiling)")
     ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
@@ -932,6 +998,8 @@ def main():
             res["decode_config4"] = decode4_microbench(world, rank, group, device, barrier0, max0)
         if "cb3" in legs:
             res["continuous_config3"] = continuous_microbench(world, rank, group, device, barrier0, max0)
+        if "model2" in legs:
+            res["model_config2"] = model2_microbench(world, rank, device)
         if "prefill4" in legs:
             res["prefill_config4"] = prefill_microbench(world, rank, device, prefixes=prefixes)
         if "evict5" in legs:
@@ -1051,6 +1119,9 @@ def main():
     cb3 = None
     if "cb3" in legs:
         cb3 = continuous_microbench(world, rank, group, device, barrier, max_over_ranks)
+    model2 = None
+    if "model2" in legs:
+        model2 = model2_microbench(world, rank, device)
     decode4 = None
     if "decode4" in legs:
         decode4 = decode4_microbench(world, rank, group, device, barrier, max_over_ranks)
@@ -1118,6 +1189,7 @@ def main():
         "select_token_config5": select1,
         "evict_token_config5": evict1,
         "continuous_config3": cb3,
+        "model_config2": model2,
         "decode_config4": decode4,
         "prefill_config4": prefill4,
     }

@@ -45,8 +45,8 @@ def up_to_date() -> bool:
     if not LIB.exists():
         return False
     t = LIB.stat().st_mtime
-    deps = sources() + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [
-        HERE.parent / "include" / "ce_api.h", Path(__file__)]
+    deps = sources() + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(
+        (HERE.parent / "include").glob("*.h")) + [Path(__file__)]
     return all(d.stat().st_mtime <= t for d in deps if d.exists())
 
 

@@ -66,6 +66,8 @@ SIGNATURES = {
     "ce_fill": (C.c_int, [P, I64, P, I64, P, P, P, P, I32, I32, P, P, I32, I64, P, P, P]),
     "ce_pool_alloc": (C.c_int, [P, P, P, I64, I64, P, P, I32, I32, P, P]),
     "ce_pool_push": (C.c_int, [P, P, I64, P, I64, P, I64, I32, P, P]),
+    "ce_moe_gate_up": (C.c_int, [P, P, P, I32, I32, I32, I32, P, P, P]),
+    "ce_moe_down": (C.c_int, [P, P, P, P, I32, I32, I32, I32, P, P, P]),
     "ce_decode_workspace_bytes": (I64, [I32, I64, I32, I32, I32, I32]),
     "ce_decode_attn_score": (C.c_int, [P, I64, I64, P, P, I64, P, P, P, I64, P, P, P, F32, I32,
                                        I32, I32, I32, I32, P, I64, I32, P, I32, I64, I64, P,
