@@ -132,7 +132,8 @@ class OssDecoder:
             self.eng.mode.fill_(capi.CE_MODE_NONE)
             self.eng.score_flags = 0
         self.eng.commit_rows()
-        self.eng._ensure_capacity(units)
+        # the CSR buffer the graph holds must fit the longest row (max_len tokens)
+        self.eng._ensure_capacity(max_len)
         nswa = cfg.layers - len(self.full)
         ring = (cfg.window, cfg.kv_heads, 1, cfg.head_dim)
         self.ring_k = [torch.zeros(ring, dtype=torch.bfloat16, device=dev) for _ in range(nswa)]
