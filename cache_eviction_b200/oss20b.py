@@ -78,7 +78,7 @@ def moe_down(g, w2, ids, weights, x, err=None):
 
 
 class OssWeights:
-    """Random bf16 weights (uniform with std 0.02; norms at 1), on the device."""
+    """Random bf16 weights (uniform with std 0.02; norms at 1; sinks fp32), on the device."""
 
     def __init__(self, cfg: OssConfig, device, seed: int = 0):
         self.cfg = cfg
@@ -93,11 +93,12 @@ class OssWeights:
         qkv = (cfg.q_heads + 2 * cfg.kv_heads) * hd
         self.embed = mat(cfg.vocab, D)
         self.lm_head = mat(cfg.vocab, D)
-        self.ln_f = torch.ones(D, device=dev)
+        self.ln_f = torch.ones(D, dtype=torch.bfloat16, device=dev)
         self.layers = []
         for _ in range(cfg.layers):
             self.layers.append(dict(
-                ln1=torch.ones(D, device=dev), ln2=torch.ones(D, device=dev),
+                ln1=torch.ones(D, dtype=torch.bfloat16, device=dev),
+                ln2=torch.ones(D, dtype=torch.bfloat16, device=dev),
                 wqkv=mat(D, qkv), bqkv=mat(qkv), wo=mat(cfg.q_heads * hd, D),
                 sinks=torch.randn(cfg.q_heads, generator=gen, device=dev),
                 wr=mat(D, cfg.experts), br=mat(cfg.experts),
@@ -145,7 +146,7 @@ class OssDecoder:
         hd = cfg.head_dim
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd))
         ang = torch.arange(max_len + 1, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
-        self.cos, self.sin = ang.cos(), ang.sin()
+        self.rot = torch.polar(torch.ones_like(ang), ang)      # e^{i pos theta_j}, complex64
         self.tok = torch.zeros(1, dtype=torch.int64, device=dev)
         self.logits = torch.zeros((1, cfg.vocab), dtype=torch.bfloat16, device=dev)
         self.x = torch.zeros((1, cfg.hidden), dtype=torch.bfloat16, device=dev)
@@ -162,9 +163,11 @@ class OssDecoder:
         return self.eng.rows[0].n
 
     # ------------------------------------------------------------ one step
-    def _rope(self, t, cos, sin):
-        a, b = t[..., 0::2].float(), t[..., 1::2].float()
-        return torch.stack((a * cos - b * sin, b * cos + a * sin), -1).flatten(-2).to(torch.bfloat16)
+    def _rope(self, qk, rot):
+        """Rotary embedding of q and k together: adjacent pairs as complex
+        numbers times e^{i pos theta_j}.  qk [1, heads * hd] bf16 view."""
+        c = torch.view_as_complex(qk.view(-1, self.cfg.head_dim // 2, 2).float()) * rot
+        return torch.view_as_real(c).flatten(-2).to(torch.bfloat16)
 
     def _device_step(self):
         """Everything of one token on the device: position advance and page
@@ -174,7 +177,7 @@ class OssDecoder:
         eng.advance_device()
         eng.fill()
         pos = eng.seq_lens_dev[:1] - 1                        # the new token's position
-        cos, sin = self.cos[pos], self.sin[pos]               # [1, hd/2]
+        rot = self.rot.index_select(0, pos)                   # [1, hd/2] complex
         self.swa_indptr[1:].copy_(torch.clamp(eng.seq_lens_dev[:1], max=cfg.window))
         unit = eng.r2u[0].index_select(0, pos // eng.P).long()
         slot = pos % eng.P
@@ -183,10 +186,11 @@ class OssDecoder:
         fi = si = 0
         for l in range(cfg.layers):
             lw = W.layers[l]
-            h = F.rms_norm(self.x.float(), (cfg.hidden,), lw["ln1"], 1e-5).to(torch.bfloat16)
+            h = F.rms_norm(self.x, (cfg.hidden,), lw["ln1"], 1e-5)
             qkv = torch.addmm(lw["bqkv"], h, lw["wqkv"])
-            q = self._rope(qkv[:, :Hq * hd].view(1, Hq, hd), cos, sin)
-            k = self._rope(qkv[:, Hq * hd:(Hq + G) * hd].view(1, G, hd), cos, sin)
+            qk = self._rope(qkv[:, :(Hq + G) * hd], rot)       # [Hq + G, hd]
+            q = qk[:Hq].view(1, Hq, hd)
+            k = qk[Hq:].view(1, G, hd)
             v = qkv[:, (Hq + G) * hd:].view(1, G, hd)
             if cfg.full_layer(l):
                 eng.k[fi][unit, :, slot] = k
@@ -201,13 +205,13 @@ class OssDecoder:
                                           err=self.err, workspace=self.swa_ws)
                 si += 1
             self.x.addmm_(self.attn.view(1, -1), lw["wo"])
-            h = F.rms_norm(self.x.float(), (cfg.hidden,), lw["ln2"], 1e-5).to(torch.bfloat16)
-            top_v, top_i = torch.topk(torch.addmm(lw["br"], h, lw["wr"]).float(), cfg.top_k)
-            self.wts.copy_(torch.softmax(top_v[0], 0))
+            h = F.rms_norm(self.x, (cfg.hidden,), lw["ln2"], 1e-5)
+            top_v, top_i = torch.topk(torch.addmm(lw["br"], h, lw["wr"]), cfg.top_k)
+            self.wts.copy_(torch.softmax(top_v[0].float(), 0))
             self.ids.copy_(top_i[0])
             moe_gate_up(h, lw["w1"], self.ids, self.g, self.err)
             moe_down(self.g, lw["w2"], self.ids, self.wts, self.x, self.err)
-        h = F.rms_norm(self.x.float(), (cfg.hidden,), W.ln_f, 1e-5).to(torch.bfloat16)
+        h = F.rms_norm(self.x, (cfg.hidden,), W.ln_f, 1e-5)
         torch.matmul(h, W.lm_head.t(), out=self.logits)
         self.tok.copy_(torch.argmax(self.logits, -1))
 

@@ -70,7 +70,7 @@ class Restated:
         x = W.embed[tok].float()
         for l in range(cfg.layers):
             lw = W.layers[l]
-            h = bf(F.rms_norm(x, (cfg.hidden,), lw["ln1"], 1e-5))
+            h = bf(F.rms_norm(x, (cfg.hidden,), lw["ln1"].float(), 1e-5))
             qkv = bf(h @ lw["wqkv"].float() + lw["bqkv"].float())
             q = bf(self.rope(qkv[:Hq * hd].view(Hq, hd), pos))
             k = bf(self.rope(qkv[Hq * hd:(Hq + G) * hd].view(G, hd), pos))
@@ -86,7 +86,7 @@ class Restated:
             p = torch.softmax(torch.cat((s, sink), -1), -1)[..., :-1]
             o = bf(torch.einsum("gjt,tgd->gjd", p, vs).reshape(-1))
             x = bf(x + o @ lw["wo"].float())
-            h = bf(F.rms_norm(x, (cfg.hidden,), lw["ln2"], 1e-5))
+            h = bf(F.rms_norm(x, (cfg.hidden,), lw["ln2"].float(), 1e-5))
             r = bf(h @ lw["wr"].float() + lw["br"].float())     # the router's logits are bf16
             tv, ti = torch.topk(r, cfg.top_k)
             wts = torch.softmax(tv, 0)
@@ -96,7 +96,7 @@ class Restated:
                 gte = bf(F.silu(w1[:cfg.inter] @ h) * (w1[cfg.inter:] @ h))
                 y = y + wts[kk] * (w2 @ gte)
             x = bf(x + y)
-        h = bf(F.rms_norm(x, (cfg.hidden,), W.ln_f, 1e-5))
+        h = bf(F.rms_norm(x, (cfg.hidden,), W.ln_f.float(), 1e-5))
         return h @ W.lm_head.float().t()
 
 
