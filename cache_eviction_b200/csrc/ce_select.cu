@@ -498,12 +498,21 @@ __device__ __forceinline__ int large_quad(int q, const uint64_t (&key)[4], const
   return np;
 }
 
-// Qd supplies Raw (the loaded words of a quad), load(c, raw) (loads only) and
-// make(raw, key, pr) (keys and protection from the loaded words).
+// Qd supplies Raw (the loaded words of a quad, raw.pos its four positions),
+// load(c, raw) (loads only), make(raw, key, pr) (keys and protection from the
+// loaded words) and pos_at(c).  On the way, the scan checks whether the
+// positions ascend strictly with the column index (each quad in itself, and
+// against the previous quad's last position: lane - 1's quad, or one load for
+// a warp's first lane); `ascending` is the block's verdict.
 template <int LQN, int KIND, class Qd>
-__device__ int scan_quads(const Qd& qd, int nq, const LargeBuf& lb) {
+__device__ int scan_quads(const Qd& qd, int nq, const LargeBuf& lb, bool& ascending) {
   int np = 0;
-  for (int q0 = threadIdx.x; q0 < nq; q0 += LQN * T) {
+  bool ok = true;
+  const int lane = threadIdx.x & 31;
+  // the loop bound is the warp's first quad, so every lane takes every
+  // iteration and each shuffle below has the whole warp
+  for (int qw = threadIdx.x - lane; qw < nq; qw += LQN * T) {
+    const int q0 = qw + lane;
     typename Qd::Raw raw[LQN];
 #pragma unroll
     for (int u = 0; u < LQN; ++u)
@@ -511,13 +520,24 @@ __device__ int scan_quads(const Qd& qd, int nq, const LargeBuf& lb) {
 #pragma unroll
     for (int u = 0; u < LQN; ++u) {
       const int q = q0 + u * T;
-      if (q >= nq) continue;
+      const bool live = q < nq;
+      // lanes of a warp hold consecutive quads, and a live lane's lower
+      // neighbours are live: the previous quad's last position comes from
+      // lane - 1, or from memory for lane 0 (whose previous quad is the last
+      // one of the warp below)
+      const int last = live ? raw[u].pos.w : 0;
+      int prev = __shfl_up_sync(0xffffffffu, last, 1);
+      if (!live) continue;
+      if (lane == 0) prev = q > 0 ? qd.pos_at(4 * q - 1) : -1;
+      ok = ok && prev < raw[u].pos.x && raw[u].pos.x < raw[u].pos.y && raw[u].pos.y < raw[u].pos.z &&
+           raw[u].pos.z < raw[u].pos.w;
       uint64_t key[4];
       bool pr[4];
       qd.make(raw[u], key, pr);
       np += large_quad<KIND>(q, key, pr, lb);
     }
   }
+  ascending = __syncthreads_and(ok) != 0;
   return np;
 }
 
@@ -902,6 +922,7 @@ struct ChooseQuads {
       r.d1 = a1;
     }
   }
+  __device__ __forceinline__ int pos_at(int c) const { return p->pos[base + c]; }
   __device__ __forceinline__ void make(const Raw& r, uint64_t (&key)[4], bool (&pr)[4]) const {
     const int pos[4] = {r.pos.x, r.pos.y, r.pos.z, r.pos.w};
     uint64_t k[4] = {0ull, 0ull, 0ull, 0ull};
@@ -961,6 +982,7 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
   };
   large_init(N, lb);
   int np = 0, cstart = 0;
+  bool ascending = false;
   if (p.vec4) {
     // Quads per thread per batch, by the registers a quad's loaded words take.
     const int nq = N / 4;
@@ -968,20 +990,21 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
     const uint64_t head = static_cast<uint64_t>(p.head_offset + g);
     // (loader, key kind) pairs; prefix_sliding keys are all 0, whose bin is 0 in every kind
     if (q.policy == CE_POLICY_RESERVOIR)
-      np = scan_quads<16, BIN_R53>(ChooseQuads<QS_POS>{&p, base, hbase, q, head, l}, nq, lb);
+      np = scan_quads<16, BIN_R53>(ChooseQuads<QS_POS>{&p, base, hbase, q, head, l}, nq, lb, ascending);
     else if (q.policy == CE_POLICY_PREFIX_SLIDING)
-      np = scan_quads<16, BIN_K32>(ChooseQuads<QS_POS>{&p, base, hbase, q, head, l}, nq, lb);
+      np = scan_quads<16, BIN_K32>(ChooseQuads<QS_POS>{&p, base, hbase, q, head, l}, nq, lb, ascending);
     else if (q.policy == CE_POLICY_H2O_GLOBAL)
       np = p.sdt == CE_DTYPE_F64
-               ? scan_quads<2, BIN_K64>(ChooseQuads<QS_H2O_F64>{&p, base, hbase, q, head, l}, nq, lb)
-               : scan_quads<4, BIN_K32>(ChooseQuads<QS_H2O_F32>{&p, base, hbase, q, head, l}, nq, lb);
+               ? scan_quads<2, BIN_K64>(ChooseQuads<QS_H2O_F64>{&p, base, hbase, q, head, l}, nq, lb, ascending)
+               : scan_quads<4, BIN_K32>(ChooseQuads<QS_H2O_F32>{&p, base, hbase, q, head, l}, nq, lb, ascending);
     else if (p.sdt == CE_DTYPE_F64)
-      np = kind == BIN_U64 ? scan_quads<6, BIN_U64>(ChooseQuads<QS_F64>{&p, base, hbase, q, head, l}, nq, lb)
-                           : scan_quads<6, BIN_K64>(ChooseQuads<QS_F64>{&p, base, hbase, q, head, l}, nq, lb);
+      np = kind == BIN_U64 ? scan_quads<6, BIN_U64>(ChooseQuads<QS_F64>{&p, base, hbase, q, head, l}, nq, lb, ascending)
+                           : scan_quads<6, BIN_K64>(ChooseQuads<QS_F64>{&p, base, hbase, q, head, l}, nq, lb, ascending);
     else
-      np = scan_quads<8, BIN_K32>(ChooseQuads<QS_F32>{&p, base, hbase, q, head, l}, nq, lb);
+      np = scan_quads<8, BIN_K32>(ChooseQuads<QS_F32>{&p, base, hbase, q, head, l}, nq, lb, ascending);
     cstart = 4 * nq;
   }
+  if (cstart < N) ascending = false;   // tail columns are not checked
   np += kind == BIN_K32   ? large_tail<BIN_K32>(colfn, cstart, N, lb)
         : kind == BIN_K64 ? large_tail<BIN_K64>(colfn, cstart, N, lb)
         : kind == BIN_R53 ? large_tail<BIN_R53>(colfn, cstart, N, lb)
@@ -999,6 +1022,26 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
   // kept bitmap in the histogram's storage (dead once the threshold is known)
   uint32_t* kb = reinterpret_cast<uint32_t*>(lb.hist);
   large_kept_bits<true>(lb, sel, N, kb);
+  if (ascending) {
+    // positions ascend with the column: a kept column's rank is the number of
+    // kept columns before it, a prefix popcount over the kept bitmap
+    const int nwc = (N + 31) / 32;
+    int carry = 0;
+    for (int b0 = 0; b0 < nwc; b0 += T) {
+      const int w = b0 + threadIdx.x;
+      const uint32_t m0 = w < nwc ? kb[w] : 0u;
+      int tot;
+      const int ex = block_excl(__popc(m0), sh, tot);
+      int rank = carry + ex;
+      for (uint32_t m = m0; m; m &= m - 1, ++rank) {
+        if (rank < stride) out[rank] = 32 * w + __ffs(m) - 1;
+        else flag_error(err, CE_EW_CAPACITY);
+      }
+      carry += tot;
+    }
+    __syncthreads();
+    return true;
+  }
   emit_sorted(
       kept_bits(N, kb, [&](int c) { return pos[c]; },
                 [&](int c) { return *reinterpret_cast<const int4*>(pos + c); }, p.vec4 != 0),

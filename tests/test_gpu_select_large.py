@@ -193,3 +193,30 @@ def test_boundary_page1_full_width_vs_oracle(policy):
     record for head_sum)."""
     _two_boundaries(policy, rows=4, L=1, n0=65536, n1=74536, budgets=[40000, 8192, 20000, 32768], seed=43,
                     hazard_bytes=1, record=policy == "head_sum_2048")
+
+
+@pytest.mark.parametrize("N", [5000, 65536])
+@pytest.mark.parametrize("policy", ["head_sum_2048", "random_2048"])
+def test_choose_large_unordered_positions_vs_oracle(policy, N):
+    """Positions that do not ascend with the column index (each head's row a
+    permutation of the same positions, so protected counts agree): the
+    kept set must still come out ranked by position, through the bitmap
+    ranking rather than the column-order one."""
+    rng = np.random.default_rng(N + 7)
+    P, G = 2, 8
+    pos = np.stack([np.stack([rng.permutation(N).astype(np.int32) for _ in range(G)]) for _ in range(P)])
+    pos[:, :, :4] = np.arange(4, dtype=np.int32)[::-1]     # the first quad itself descends
+    score = _scores(rng, "lognormal" if policy == "head_sum_2048" else "u64", (P, G, N))
+    kern = K()
+    budget = N // 3
+    rows = [dict(n=N, budget=budget, prefix=budget // 4, recent=budget // 4, cursor=None, policy=policy,
+                 seed=3 + r) for r in range(P)]
+    kept_c, st_c, _ = oracle.choose(pos, score, oracle.row_params(rows), 1, G,
+                                    score_is_f32=score.dtype == np.float32)
+    err = kern.error_word(DEV)
+    kept_g, st_g, _ = kern.choose(torch.from_numpy(pos).to(DEV), torch.from_numpy(score).to(DEV),
+                                  kern.row_params(rows, DEV), 1, G, max_n=N + 1, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert st_g.cpu().numpy().tolist() == st_c.tolist() == [0] * P
+    np.testing.assert_array_equal(kept_g[:, :, :budget].cpu().numpy(), kept_c[:, :, :budget])
