@@ -205,7 +205,7 @@ def test_choose_large_unordered_positions_vs_oracle(policy, N):
     rng = np.random.default_rng(N + 7)
     P, G = 2, 8
     pos = np.stack([np.stack([rng.permutation(N).astype(np.int32) for _ in range(G)]) for _ in range(P)])
-    pos[:, :, :4] = np.arange(4, dtype=np.int32)[::-1]     # the first quad itself descends
+    pos[:, :, :4] = np.sort(pos[:, :, :4], -1)[..., ::-1]   # the first quad itself descends
     score = _scores(rng, "lognormal" if policy == "head_sum_2048" else "u64", (P, G, N))
     kern = K()
     budget = N // 3
