@@ -87,6 +87,17 @@ def pool_units_needed(specs, steps):
     return total + 64
 
 
+# --shard-of N (profiling): one process runs rank 0's shard of an N-GPU run
+# (its KV heads of 64 N sequences) with no collectives, so a single GPU, and
+# ncu, can see the per-rank workload of the scaling run.
+SHARD_OF = [1]
+
+
+def _shard(rank, world):
+    from cache_eviction_b200 import tp
+    return tp.shard(G_TOTAL, H_TOTAL, rank, max(world, SHARD_OF[0]))
+
+
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
     def __init__(self, gpu_index: int):
@@ -295,7 +306,7 @@ def build_engine(specs, steps_total, world, rank, group, device):
     import torch
     from cache_eviction_b200.engine import RaggedDecodeEngine, synth_state
     from cache_eviction_b200 import tp
-    G, H, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    G, H, off = _shard(rank, world)
     units = pool_units_needed(specs, steps_total)
     eng = RaggedDecodeEngine(layers=LAYERS, q_heads=H, kv_heads=G, page_size=PAGE, pool_units=units,
                              max_rows=len(specs),
@@ -455,7 +466,7 @@ def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, step
     import torch
     from cache_eviction_b200 import capi, tp
     from cache_eviction_b200.policy import EvictionConfig
-    G, H, _ = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    G, H, _ = _shard(rank, world)
     ctx, budget, prefix, recent = 80000, 28672, 512, 4096
     cfg = EvictionConfig("head_sum_2048", budget, prefix, recent, seed=4)
     specs = [dict(ctx=ctx, cfg=cfg, policy="h2o_per_head", budget=budget)]
@@ -545,7 +556,7 @@ def continuous_microbench(world, rank, group, device, barrier, max_over_ranks, s
     to every token of every request served.  Value: decoded tokens / time."""
     import torch
     from cache_eviction_b200 import tp
-    G, H, _ = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    G, H, _ = _shard(rank, world)
     B = SEQS_PER_GPU * world
     specs = workload(B, seed=seed)
     arrivals = workload(8 * B, seed=seed + 1)
@@ -652,7 +663,7 @@ def continuous_microbench(world, rank, group, device, barrier, max_over_ranks, s
 
 def _shard_offset(rank, world):
     from cache_eviction_b200 import tp
-    return tp.shard(G_TOTAL, H_TOTAL, rank, world)[2]
+    return _shard(rank, world)[2]
 
 
 def model2_microbench(world, rank, device, max_len=16384, prompt_len=1024, seg=512, seed=2):
@@ -735,7 +746,7 @@ def prefill_microbench(world, rank, device, reps=5, cpu=False, prefixes=PREFILL_
     busy while the host prepares it)."""
     import torch
     from cache_eviction_b200 import capi, kernels, tp
-    G, H, _ = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    G, H, _ = _shard(rank, world)
     out = {}
     gen = torch.Generator(device=device).manual_seed(77)
     nq = PREFILL_CHUNK
@@ -826,7 +837,7 @@ def select_token_microbench(world, rank, device, reps=3, rows=32):
     (+ uniforms) read once, kept indices written."""
     import torch
     from cache_eviction_b200 import kernels, tp
-    G, _, _ = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    G, _, _ = _shard(rank, world)
     R, N = rows, 65536
     gen = torch.Generator(device=device).manual_seed(56)
     pos = torch.arange(N, dtype=torch.int32, device=device).expand(R, G, N).contiguous()
@@ -865,7 +876,7 @@ def evict_microbench(world, rank, device, reps=3, rows=32, page=PAGE):
     algorithmic GB/s."""
     import torch
     from cache_eviction_b200 import kernels, tp
-    G, _, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    G, _, off = _shard(rank, world)
     R, N = rows, 65536 // page
     units = R * N + 1
     gen = torch.Generator(device=device).manual_seed(55)
@@ -958,10 +969,13 @@ def main():
     ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
     ap.add_argument("--score-overlap", action="store_true",
                     help="score each layer's pages on a second stream (engine overlap_scores)")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="profiling: run rank 0's shard of an N-GPU run on this one GPU, no collectives")
     ap.add_argument("--prefill-prefixes", default=",".join(map(str, PREFILL_PREFIXES)),
                     help="resident prefixes of the config-4 leg")
     args = ap.parse_args()
     legs = set(args.legs.split(","))
+    SHARD_OF[0] = args.shard_of
     SCORE_OVERLAP[0] = args.score_overlap
     prefixes = tuple(int(x) for x in args.prefill_prefixes.split(","))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1013,10 +1027,10 @@ def main():
         if world > 1:
             dist.destroy_process_group()
         return 0
-    specs = workload(args.seqs * world)
+    specs = workload(args.seqs * max(world, SHARD_OF[0]))
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else args.steps
     steps_total = args.warmup + max(args.steps, e2e_steps)
-    G, H, off = tp.shard(G_TOTAL, H_TOTAL, rank, world)
+    G, H, off = _shard(rank, world)
     B = len(specs)
     scale = D ** -0.5
 
