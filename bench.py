@@ -91,6 +91,9 @@ def pool_units_needed(specs, steps):
 # (its KV heads of 64 N sequences) with no collectives, so a single GPU, and
 # ncu, can see the per-rank workload of the scaling run.
 SHARD_OF = [1]
+# --ordered-units (profiling): each row's pages on consecutive units, for
+# telling DRAM locality effects from kernel effects
+ORDERED_UNITS = [False]
 
 
 def _shard(rank, world):
@@ -314,7 +317,7 @@ def build_engine(specs, steps_total, world, rank, group, device):
                              pos_cap=32768 // PAGE, device=device, head_offset=off,
                              global_kv_heads=G_TOTAL, process_group=group,
                              overlap_scores=SCORE_OVERLAP[0])
-    synth_state(eng, specs, seed=2026 + 17)
+    synth_state(eng, specs, seed=2026 + 17, shuffle=not ORDERED_UNITS[0])
     torch.cuda.synchronize()
     return eng
 
@@ -969,6 +972,8 @@ def main():
     ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
     ap.add_argument("--score-overlap", action="store_true",
                     help="score each layer's pages on a second stream (engine overlap_scores)")
+    ap.add_argument("--ordered-units", action="store_true",
+                    help="profiling: consecutive units for each row instead of shuffled ones")
     ap.add_argument("--shard-of", type=int, default=1,
                     help="profiling: run rank 0's shard of an N-GPU run on this one GPU, no collectives")
     ap.add_argument("--prefill-prefixes", default=",".join(map(str, PREFILL_PREFIXES)),
@@ -976,6 +981,7 @@ def main():
     args = ap.parse_args()
     legs = set(args.legs.split(","))
     SHARD_OF[0] = args.shard_of
+    ORDERED_UNITS[0] = args.ordered_units
     SCORE_OVERLAP[0] = args.score_overlap
     prefixes = tuple(int(x) for x in args.prefill_prefixes.split(","))
     world = int(os.environ.get("WORLD_SIZE", "1"))

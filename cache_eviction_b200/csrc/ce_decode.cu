@@ -238,9 +238,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == NCW) {
     // ------------------------------- producer --------------------------------
-    // Page indices are read in 32-entry windows one window ahead of use (the
-    // CTA's CSR positions only move forward), so no TMA issue waits on a
-    // dependent global load.
+    // Page indices are read in 32-entry windows (the CTA's CSR positions only
+    // move forward): the two windows in use and a third one in flight, so a
+    // window is loaded a whole window of stages before any lookup reads it
+    // and no TMA issue waits on a dependent global load.  (With one window
+    // ahead, a stage of 8 pages -- one KV head per GPU -- waited for a load
+    // every 4 stages.)
     int issued = 0;
     int b = b_start, base = base_start;
     int nst = 0, tok_b = 0;
@@ -256,7 +259,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       return (c >= 0 && c < p.kv_capacity) ? p.kv_indices[c] : -2;
     };
     int64_t w0 = -1;
-    int idx_cur = -2, idx_next = -2;
+    int idx_cur = -2, idx_next = -2, idx_ahead = -2;
     for (int64_t x = S_lo; x < S_hi; ++x) {
       while (x >= base + nst) {
         base += nst;
@@ -272,10 +275,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         w0 = c0;
         idx_cur = fetch(w0);
         idx_next = fetch(w0 + 32);
+        idx_ahead = fetch(w0 + 64);
       } else if (c0 >= w0 + 32) {
         w0 += 32;
         idx_cur = idx_next;
-        idx_next = fetch(w0 + 32);
+        idx_next = idx_ahead;
+        idx_ahead = fetch(w0 + 64);
       }
       const int s = issued % NSTAGES;
       const uint32_t ph = (issued / NSTAGES) & 1;

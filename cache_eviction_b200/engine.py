@@ -435,7 +435,7 @@ class RaggedDecodeEngine:
 
 # -------------------------------------------------------------- synthesis
 def synth_rows(specs: list, seed: int, *, layers: int, kv_heads: int, page_size: int,
-               pool_units: int, max_rows: int, pos_cap: int, r2u_width: int):
+               pool_units: int, max_rows: int, pos_cap: int, r2u_width: int, shuffle: bool = True):
     """Host arrays of rows initialised as if every boundary up to each context
     had been taken (the state synth_state uploads).
 
@@ -443,13 +443,15 @@ def synth_rows(specs: list, seed: int, *, layers: int, kv_heads: int, page_size:
     row holds prefix + recent + budget-remainder residents after its last
     evicting boundary (ascending positions, per-head middle picks for per-head
     policies, shared picks for H2O global) and its tail since that boundary.
-    Units are drawn from a shuffled pool.  Returns (arrays dict with table,
+    Units are drawn from a shuffled pool (in order with shuffle=False, so a
+    row's pages are consecutive in memory).  Returns (arrays dict with table,
     r2u, pos, frontier, count; rows list of (row, cfg, n, last_boundary,
     frontier, count); owned units of each H2O row; the units left free).
     """
     rng = np.random.default_rng(seed)
     P, L, G = page_size, layers, kv_heads
-    order = rng.permutation(np.arange(1, pool_units)).astype(np.int32)
+    order = rng.permutation(np.arange(1, pool_units)).astype(np.int32) if shuffle else \
+        np.arange(1, pool_units, dtype=np.int32)
     cursor = 0
 
     def take(k):
@@ -510,13 +512,14 @@ def synth_rows(specs: list, seed: int, *, layers: int, kv_heads: int, page_size:
 
 
 def synth_state(engine: RaggedDecodeEngine, specs: list, seed: int, score_sigma: float = 2.0,
-                fill_pools: bool = True):
+                fill_pools: bool = True, shuffle: bool = True):
     """Initialise the engine's rows with synth_rows' state; the units it does
     not use become the free stack.  Scores of H2O rows are lognormal(0,
     sigma), the pools N(0, 1)."""
     arrays, rows, scored, free = synth_rows(
         specs, seed, layers=engine.L, kv_heads=engine.G, page_size=engine.P, pool_units=engine.units,
-        max_rows=engine.table.shape[0], pos_cap=engine.pos_cap, r2u_width=engine.r2u.shape[1])
+        max_rows=engine.table.shape[0], pos_cap=engine.pos_cap, r2u_width=engine.r2u.shape[1],
+        shuffle=shuffle)
     for r, cfg, n, last, frontier, count in rows:
         engine.add_row(r, cfg, n, last_boundary=last, frontier_units=frontier, count_units=count)
     engine.table.copy_(torch.from_numpy(arrays["table"]))
