@@ -49,7 +49,8 @@ namespace decode {
 constexpr int D = 64;
 constexpr int GROUP = 8;
 constexpr int NCW = 8;                    // consumer warps
-constexpr int THREADS = (NCW + 1) * 32;   // + producer warp
+constexpr int NPW = 2;                    // producer warps (stage k is issued by warp NCW + k % NPW)
+constexpr int THREADS = (NCW + NPW) * 32;
 constexpr int ROW_BYTES = D * 2;          // 128 B per (token, head) row
 constexpr int HALF_STAGE = NCW * 16 * ROW_BYTES;  // 16 KB of K (or V) per stage
 constexpr int STAGE_BYTES = 2 * HALF_STAGE;
@@ -236,8 +237,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int b_start = start_sh[0];
   const int base_start = start_sh[1];
 
-  if (warp == NCW) {
-    // ------------------------------- producer --------------------------------
+  if (warp >= NCW) {
+    // ------------------------------- producers -------------------------------
+    // Every producer warp walks every stage (sequence and page-index window
+    // state stay warp-uniform); stage k's loads are issued by warp NCW + k % NPW,
+    // so consecutive stages' TMA issue overlaps (at one KV head per GPU a stage
+    // is 8 pages, 16 boxes).
+    const int pw = warp - NCW;
     // Page indices are read in 32-entry windows (the CTA's CSR positions only
     // move forward): the two windows in use and a third one in flight, so a
     // window is loaded a whole window of stages before any lookup reads it
@@ -284,6 +290,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const int s = issued % NSTAGES;
       const uint32_t ph = (issued / NSTAGES) & 1;
+      if (issued % NPW != pw) {
+        ++issued;
+        continue;
+      }
       if (issued >= NSTAGES) {
         bool ok = true;
         if (lane == 0) ok = mbar_wait(&empty[s], ph ^ 1, p.err);
@@ -320,10 +330,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       ++issued;
     }
-    // Drain: every issued load must land before the CTA may exit.
+    // Drain: every load this warp issued must land before the CTA may exit.
     if (lane == 0) {
       for (int it = max(0, issued - NSTAGES); it < issued; ++it)
-        mbar_wait(&full[it % NSTAGES], (it / NSTAGES) & 1, p.err);
+        if (it % NPW == pw) mbar_wait(&full[it % NSTAGES], (it / NSTAGES) & 1, p.err);
     }
   } else {
     // ------------------------------- consumers -------------------------------
