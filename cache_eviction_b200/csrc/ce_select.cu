@@ -851,7 +851,6 @@ struct ChooseParams {
   int32_t* pv;
   int32_t* seg_info;
   int32_t* err;
-  int split;  // large segments go through choose_scan_kernel + choose_pick_kernel
 };
 
 __device__ __forceinline__ float score_f(const void* s, int dt, int64_t idx) {
@@ -1082,191 +1081,6 @@ __device__ bool choose_large(const ChooseParams& p, int i, int l, int g, int s, 
   return true;
 }
 
-// ---- large segments split over CTAs -------------------------------------------
-// A large segment in one CTA needs 176 KB of shared memory (its 16-bit key
-// prefixes), so 256 page-size-1 segments run one CTA per SM in two waves, each
-// CTA's scan latency-bound.  Split instead: choose_scan_kernel streams the
-// inputs with up to four CTAs per segment (SPLIT_COLS columns each, 20 KB of
-// shared memory, two CTAs per SM) and leaves the prefixes, protected bits, one
-// 4,096-bin histogram and protected count per slice and whether positions
-// ascend in the workspace -- inside the segment's own 8-bytes-per-column cells
-// of it, 32 MB at 256 x 65,536 columns, so it stays in L2; then
-// choose_pick_kernel, one small CTA per segment, merges the slices'
-// histograms and runs the same threshold, candidate and emit steps as the
-// one-CTA path on that data.
-constexpr int SPLIT_COLS = 16384;
-
-__device__ __forceinline__ int split_count(int N) { return (N + SPLIT_COLS - 1) / SPLIT_COLS; }
-
-struct SplitData {
-  uint16_t* bin;   // [N] key prefixes
-  uint32_t* prot;  // [(N + 31) / 32] protected columns
-  int* hist;       // [S][LHIST]
-  int* np;         // [S] protected columns per slice
-  int* asc;        // [S] positions ascend within the slice and from the slice before
-};
-
-__device__ __forceinline__ SplitData split_data(const ChooseParams& p, int64_t base, int N, int S) {
-  // fits in the segment's 8 * n_cols bytes: 2N + N/8 + S * 16 KB + 8 S + padding
-  // < 8N for N > REG_ITEMS * T, with S = split_count(N)
-  uint8_t* q = reinterpret_cast<uint8_t*>(p.kv + base);
-  SplitData d;
-  d.bin = reinterpret_cast<uint16_t*>(q);
-  q += (2 * static_cast<int64_t>(N) + 15) & ~int64_t(15);
-  d.prot = reinterpret_cast<uint32_t*>(q);
-  q += ((static_cast<int64_t>(N + 31) / 32) * 4 + 15) & ~int64_t(15);
-  d.hist = reinterpret_cast<int*>(q);
-  q += static_cast<int64_t>(S) * LHIST * 4;
-  d.np = reinterpret_cast<int*>(q);
-  d.asc = d.np + S;
-  return d;
-}
-
-__device__ __forceinline__ int segment_cols(const ChooseParams& p, int i) {
-  return p.ncols ? min(p.ncols[i], p.n_cols) : p.n_cols;
-}
-
-// Grid: problems * segs * ceil(n_cols / SPLIT_COLS); segments of at most
-// REG_ITEMS * T columns are choose_seg_kernel's.
-__global__ void __launch_bounds__(T, 2) choose_scan_kernel(const ChooseParams p, int smax) {
-  __shared__ Sh sh;
-  __shared__ int hist[LHIST];
-  __shared__ uint32_t prot[SPLIT_COLS / 32];
-  const int segs = p.layers * p.heads;
-  const int seg = blockIdx.x / smax, slice = blockIdx.x % smax;
-  const int i = seg / segs, s = seg % segs;
-  const int l = s / p.heads, g = s % p.heads;
-  const int N = segment_cols(p, i);
-  if (N <= REG_ITEMS * T) return;
-  const int S = split_count(N);
-  if (slice >= S) return;
-  const ce_row_params q = p.params[i];
-  const int64_t base = static_cast<int64_t>(seg) * p.n_cols;
-  const SplitData d = split_data(p, base, N, S);
-  const int c0 = slice * SPLIT_COLS, n = min(N - c0, SPLIT_COLS);
-  for (int j = threadIdx.x; j < LHIST; j += T) hist[j] = 0;
-  for (int j = threadIdx.x; j < SPLIT_COLS / 32; j += T) prot[j] = 0u;
-  __syncthreads();
-  LargeBuf lb{};
-  lb.bin = d.bin + c0;
-  lb.prot = prot;
-  lb.hist = hist;
-  const int kind = q.policy == CE_POLICY_RESERVOIR ? BIN_R53
-                   : p.sdt == CE_DTYPE_F64 ? (q.policy == CE_POLICY_RANDOM ? BIN_U64 : BIN_K64)
-                                           : BIN_K32;
-  auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool {
-    return choose_column(p, i, l, g, base, q, c0 + c, key, pv);
-  };
-  int np = 0, cstart = 0;
-  bool ascending = false;
-  if (p.vec4) {
-    const int nq = n / 4;
-    const int64_t hbase = (static_cast<int64_t>(i) * segs + l * p.heads) * p.n_cols + c0;
-    const int64_t sb = base + c0;
-    const uint64_t head = static_cast<uint64_t>(p.head_offset + g);
-    if (q.policy == CE_POLICY_RESERVOIR)
-      np = scan_quads<8, BIN_R53>(ChooseQuads<QS_POS>{&p, sb, hbase, q, head, l}, nq, lb, ascending);
-    else if (q.policy == CE_POLICY_PREFIX_SLIDING)
-      np = scan_quads<8, BIN_K32>(ChooseQuads<QS_POS>{&p, sb, hbase, q, head, l}, nq, lb, ascending);
-    else if (q.policy == CE_POLICY_H2O_GLOBAL)
-      np = p.sdt == CE_DTYPE_F64
-               ? scan_quads<2, BIN_K64>(ChooseQuads<QS_H2O_F64>{&p, sb, hbase, q, head, l}, nq, lb, ascending)
-               : scan_quads<2, BIN_K32>(ChooseQuads<QS_H2O_F32>{&p, sb, hbase, q, head, l}, nq, lb, ascending);
-    else if (p.sdt == CE_DTYPE_F64)
-      np = kind == BIN_U64
-               ? scan_quads<3, BIN_U64>(ChooseQuads<QS_F64>{&p, sb, hbase, q, head, l}, nq, lb, ascending)
-               : scan_quads<3, BIN_K64>(ChooseQuads<QS_F64>{&p, sb, hbase, q, head, l}, nq, lb, ascending);
-    else
-      np = scan_quads<4, BIN_K32>(ChooseQuads<QS_F32>{&p, sb, hbase, q, head, l}, nq, lb, ascending);
-    cstart = 4 * nq;
-  }
-  if (cstart < n) ascending = false;   // tail columns are not checked
-  np += kind == BIN_K32   ? large_tail<BIN_K32>(colfn, cstart, n, lb)
-        : kind == BIN_K64 ? large_tail<BIN_K64>(colfn, cstart, n, lb)
-        : kind == BIN_R53 ? large_tail<BIN_R53>(colfn, cstart, n, lb)
-                          : large_tail<BIN_U64>(colfn, cstart, n, lb);
-  const int nprot = block_sum(np, sh);   // includes the barrier after the scan
-  for (int j = threadIdx.x; j < LHIST; j += T) d.hist[static_cast<int64_t>(slice) * LHIST + j] = hist[j];
-  for (int j = threadIdx.x; j < (n + 31) / 32; j += T) d.prot[c0 / 32 + j] = prot[j];
-  if (threadIdx.x == 0) {
-    d.np[slice] = nprot;
-    bool ok = ascending;
-    if (c0 > 0) ok = ok && p.pos[base + c0 - 1] < p.pos[base + c0];
-    d.asc[slice] = ok ? 1 : 0;
-  }
-}
-
-// One CTA per large segment, after choose_scan_kernel: protected count,
-// threshold (large_select over the merged histogram and the prefixes left in
-// the workspace), kept bitmap and emit.  A segment whose candidates overflow
-// takes the general path over every column.
-__global__ void __launch_bounds__(T, 2) choose_pick_kernel(const ChooseParams p) {
-  extern __shared__ uint32_t dyn[];
-  __shared__ Sh sh;
-  const int segs = p.layers * p.heads;
-  const int i = blockIdx.x / segs, s = blockIdx.x % segs;
-  const int l = s / p.heads, g = s % p.heads;
-  const int N = segment_cols(p, i);
-  if (N <= REG_ITEMS * T) return;
-  const int S = split_count(N);
-  const ce_row_params q = p.params[i];
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * p.n_cols;
-  const SplitData d = split_data(p, base, N, S);
-  int nprot = 0;
-  bool ascending = true;
-  for (int j = 0; j < S; ++j) {
-    nprot += d.np[j];
-    ascending = ascending && d.asc[j] != 0;
-  }
-  if (threadIdx.x == 0) p.seg_info[static_cast<int64_t>(i) * segs + s] = nprot;
-  if (nprot > q.budget) return;
-  const int k = (q.policy == CE_POLICY_PREFIX_SLIDING) ? 0 : q.budget - nprot;
-  // shared memory after the emit bitmaps: pick bits, then the histogram /
-  // candidate buffer
-  uint32_t* pick = dyn + 2 * p.nw;
-  int* hist = reinterpret_cast<int*>(pick + (LARGE_MAX / 32));
-  for (int j = threadIdx.x; j < LHIST; j += T) {
-    int v = 0;
-    for (int t = 0; t < S; ++t) v += d.hist[static_cast<int64_t>(t) * LHIST + j];
-    hist[j] = v;
-  }
-  for (int j = threadIdx.x; j < (N + 31) / 32; j += T) pick[j] = 0u;
-  __syncthreads();
-  LargeBuf lb;
-  lb.bin = d.bin;
-  lb.prot = d.prot;
-  lb.pick = pick;
-  lb.hist = hist;
-  lb.ckey = reinterpret_cast<uint64_t*>(hist);
-  lb.ccol = reinterpret_cast<int*>(lb.ckey + LCAND);
-  lb.cpv = lb.ccol + LCAND;
-  const int kind = q.policy == CE_POLICY_RESERVOIR ? BIN_R53
-                   : p.sdt == CE_DTYPE_F64 ? (q.policy == CE_POLICY_RANDOM ? BIN_U64 : BIN_K64)
-                                           : BIN_K32;
-  auto colfn = [&](int c, uint64_t& key, int32_t& pv) -> bool {
-    return choose_column(p, i, l, g, base, q, c, key, pv);
-  };
-  int32_t* out = p.kept + static_cast<int64_t>(blockIdx.x) * p.kept_stride;
-  LargeSel sel;
-  if (large_select(colfn, N, k, N - nprot, kind, lb, sh, sel)) {
-    uint32_t* kb = reinterpret_cast<uint32_t*>(hist);
-    large_kept_bits<true>(lb, sel, N, kb);
-    choose_emit(p, out, p.kept_stride, p.pos + base, N, kb, ascending, sh, dyn);
-    return;
-  }
-  // candidate overflow: the general path (the workspace cells are rewritten
-  // with every column's key; the prefixes are no longer needed)
-  __syncthreads();
-  uint64_t* kv = p.kv + base;
-  int32_t* pv = p.pv + base;
-  int np = 0;
-  for (int c = threadIdx.x; c < N; c += T) np += choose_column(p, i, l, g, base, q, c, kv[c], pv[c]);
-  __syncthreads();
-  choose_body(p, MemCols{kv, pv, N}, np, i, s, N, q, sh, dyn);
-}
-
-// Shared memory of choose_pick_kernel beyond the emit bitmaps.
-constexpr int PICK_EXTRA_BYTES = (LARGE_MAX / 32) * 4 + LCAND * 16;
 
 // LARGE: the launch carries the large-segment shared-memory buffer (one CTA
 // per SM); otherwise two CTAs share an SM and large segments take the
@@ -1294,7 +1108,6 @@ __global__ void __launch_bounds__(T, LARGE ? 1 : 2) choose_seg_kernel(const Choo
     choose_body(p, cols, np, i, s, N, q, sh, dyn);
     return;
   }
-  if (p.split) return;   // choose_scan_kernel + choose_pick_kernel take it
   if constexpr (LARGE) {
     if (N <= LARGE_MAX && choose_large(p, i, l, g, s, base, q, N, sh, dyn)) return;
   }
@@ -2628,11 +2441,7 @@ extern "C" int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_col
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   p.vec4 = (n_cols % 4 == 0) && (reinterpret_cast<uintptr_t>(pos) % 16 == 0) &&
            (reinterpret_cast<uintptr_t>(score) % 16 == 0);
-  // Segments of up to LARGE_MAX columns above the register path are split
-  // (choose_scan_kernel + choose_pick_kernel); choose_seg_kernel takes the rest.
-  const int pick_smem = sel_smem(nw) + PICK_EXTRA_BYTES;
-  p.split = (n_cols > REG_ITEMS * T && n_cols <= LARGE_MAX && pick_smem <= kLargeSmemMax) ? 1 : 0;
-  const bool large = !p.split && n_cols > REG_ITEMS * T && sel_smem(nw) + LARGE_BYTES <= kLargeSmemMax;
+  const bool large = n_cols > REG_ITEMS * T && sel_smem(nw) + LARGE_BYTES <= kLargeSmemMax;
   const int smem = sel_smem(nw) + (large ? LARGE_BYTES : 0);
   if (large) {
     if (!host::set_smem(choose_seg_kernel<true>, smem)) return host::fail(CE_ERR_CUDA, "smem attr");
@@ -2642,14 +2451,6 @@ extern "C" int ce_choose(const int32_t* pos, const int32_t* ncols, int32_t n_col
     choose_seg_kernel<false><<<problems * segs, T, smem, st>>>(p);
   }
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("choose_seg_kernel");
-  if (p.split) {
-    const int smax = (n_cols + SPLIT_COLS - 1) / SPLIT_COLS;
-    choose_scan_kernel<<<problems * segs * smax, T, 0, st>>>(p, smax);
-    if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("choose_scan_kernel");
-    if (!host::set_smem(choose_pick_kernel, pick_smem)) return host::fail(CE_ERR_CUDA, "smem attr");
-    choose_pick_kernel<<<problems * segs, T, pick_smem, st>>>(p);
-    if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("choose_pick_kernel");
-  }
   choose_status_kernel<<<problems, 32, 0, st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("choose_status_kernel");
   return CE_OK;

@@ -71,7 +71,9 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("N", [5000, 65536])
+# 5000: one tile; 20000: three tiles, the last partial; 12347: no 16-byte
+# quads (single-column loads); 65536: eight full tiles
+@pytest.mark.parametrize("N", [5000, 12347, 20000, 65536])
 @pytest.mark.parametrize("policy,skind,compacted", CASES)
 def test_choose_large_vs_oracle(policy, skind, compacted, N):
     rng = np.random.default_rng(N + len(policy))
