@@ -588,7 +588,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 // a shared-memory reduction per head, with the sink folded in (the normaliser
 // of SGLang's stage 2 and of runtime:179-188).
 constexpr int CB_THREADS = 256;
-constexpr int CB_SLOT_BATCH = 4;   // slots a thread loads before merging them
+// Record slots a thread loads before merging them.  In a large batch a head
+// has few slots (its sequence spans few attention CTAs): a batch of one keeps
+// the kernel at 64 registers, so four blocks share an SM and a 64-sequence
+// batch's 512 tasks run in one wave.  A small batch (a head's slots come from
+// up to every attention CTA) takes a batch of four.
+constexpr int CB_SLOT_BATCH_WIDE = 4;
 constexpr int CB_MAX_CHUNKS = 64;
 
 struct CombineParams {
@@ -621,6 +626,7 @@ struct SeqSlots {
 
 // sh_l2[r] = log2 normaliser of query head g*8 + r (record maxima, sums and
 // the sink).  sh_m / sh_l: [GROUP][CB_THREADS] scratch.
+template <int SB>
 __device__ void group_normalisers(const Params& p, const SeqSlots& q, float* sh_m, float* sh_l,
                                   float* sh_l2) {
   const int tid = threadIdx.x, G = p.G;
@@ -630,10 +636,10 @@ __device__ void group_normalisers(const Params& p, const SeqSlots& q, float* sh_
     m[r] = -INFINITY;
     l[r] = 0.f;
   }
-  for (int i0 = tid; i0 < q.nslots; i0 += CB_THREADS * CB_SLOT_BATCH) {
-    float4 ma[CB_SLOT_BATCH], mb[CB_SLOT_BATCH], la[CB_SLOT_BATCH], lb[CB_SLOT_BATCH];
+  for (int i0 = tid; i0 < q.nslots; i0 += CB_THREADS * SB) {
+    float4 ma[SB], mb[SB], la[SB], lb[SB];
 #pragma unroll
-    for (int u = 0; u < CB_SLOT_BATCH; ++u) {
+    for (int u = 0; u < SB; ++u) {
       const int i = i0 + u * CB_THREADS;
       ma[u] = mb[u] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
       la[u] = lb[u] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -646,7 +652,7 @@ __device__ void group_normalisers(const Params& p, const SeqSlots& q, float* sh_
       }
     }
 #pragma unroll
-    for (int u = 0; u < CB_SLOT_BATCH; ++u) {
+    for (int u = 0; u < SB; ++u) {
       merge_ml(m[0], l[0], ma[u].x, la[u].x);
       merge_ml(m[1], l[1], ma[u].y, la[u].y);
       merge_ml(m[2], l[2], ma[u].z, la[u].z);
@@ -691,6 +697,7 @@ __device__ void group_normalisers(const Params& p, const SeqSlots& q, float* sh_
 // Outputs of the query heads r = c, c + C, ... (r < 8) of KV head g: each a
 // sum over the slots of 2^(m_i - L2) O_i.  The block's threads split as heads
 // x 16 dimension quads x slot groups; partial sums meet in shared memory.
+template <int AB>
 __device__ void group_outputs(const Params& p, const SeqSlots& q, int c, int C, const float* sh_l2,
                               float4* red) {
   const int nh = (c < GROUP) ? (GROUP - 1 - c) / C + 1 : 0;
@@ -703,7 +710,6 @@ __device__ void group_outputs(const Params& p, const SeqSlots& q, int c, int C, 
   if (hh < nh) {
     const int r = c + hh * C;
     const float L2 = sh_l2[r];
-    constexpr int AB = 4;
     for (int i0 = sg; i0 < q.nslots; i0 += sgn * AB) {
       float w[AB];
       float4 o[AB];
@@ -843,7 +849,8 @@ __device__ __forceinline__ void chunk_pages(const Params& p, int b, int P, int c
   hi = min(npages, lo + per);
 }
 
-__global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams cp) {
+template <int SB>
+__global__ void __launch_bounds__(CB_THREADS, SB == 1 ? 4 : 2) combine_kernel(const CombineParams cp) {
   const Params& p = cp.a;
   const int bs = p.bs, H = p.H, G = p.G, C = cp.chunks;
   const int64_t S = p.prefix[bs];
@@ -886,8 +893,8 @@ __global__ void __launch_bounds__(CB_THREADS) combine_kernel(const CombineParams
       ua = u4[0];
       ub = u4[1];
     }
-    group_normalisers(p, q, sh_m, sh_l, sh_l2);
-    group_outputs(p, q, c, C, sh_l2, red);
+    group_normalisers<SB>(p, q, sh_m, sh_l, sh_l2);
+    group_outputs<SB == 1 ? 2 : 4>(p, q, c, C, sh_l2, red);
     if (c == 0 && threadIdx.x < GROUP) {
       const int h = hc * GROUP + threadIdx.x;
       const float L2 = sh_l2[threadIdx.x];
@@ -1086,10 +1093,20 @@ extern "C" int ce_decode_attn_score(const void* q, int64_t q_sb, int64_t q_sh, c
   CombineParams cp{p, grid, page_size, defer ? 1 : 0, combine_chunks(bs, num_q_heads, grid)};
   // A deferred decode's page scores run beside the next layer's attention
   // kernel (195 KB of shared memory per CTA): keep SMs at the largest carveout.
-  if (defer && !host::set_max_shared_carveout(combine_kernel)) return host::fail(CE_ERR_CUDA, "carveout attr");
-  const int cb_grid = static_cast<int>(std::max<int64_t>(
-      1, std::min<int64_t>(static_cast<int64_t>(bs) * (num_q_heads / GROUP) * cp.chunks, 4LL * grid)));
-  combine_kernel<<<cb_grid, CB_THREADS, 0, st>>>(cp);
+  const int64_t tasks = static_cast<int64_t>(bs) * (num_q_heads / GROUP) * cp.chunks;
+  const int cb_grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tasks, 4LL * grid)));
+  // Fewer (sequence, KV head) pairs than attention CTAs: each head has many
+  // record slots (up to one per CTA and warp group) and the tasks are chunks
+  // of few sequences -- the wide variant's batched loads win.
+  const bool wide = static_cast<int64_t>(bs) * (num_q_heads / GROUP) < grid;
+  if (wide) {
+    if (defer && !host::set_max_shared_carveout(combine_kernel<CB_SLOT_BATCH_WIDE>))
+      return host::fail(CE_ERR_CUDA, "carveout attr");
+    combine_kernel<CB_SLOT_BATCH_WIDE><<<cb_grid, CB_THREADS, 0, st>>>(cp);
+  } else {
+    if (defer && !host::set_max_shared_carveout(combine_kernel<1>)) return host::fail(CE_ERR_CUDA, "carveout attr");
+    combine_kernel<1><<<cb_grid, CB_THREADS, 0, st>>>(cp);
+  }
   if (cudaPeekAtLastError() != cudaSuccess) return host::fail_cuda("combine_kernel launch");
   return CE_OK;
 }
@@ -1099,7 +1116,8 @@ int ce::host::decode_prepare_device() {
   // shared-memory attribute is the one the first launch would set.
   cudaFuncAttributes a;
   if (!host::set_smem(attn_kernel<16>, SMEM_BYTES) || !host::set_smem(attn_kernel<1>, SMEM_BYTES) ||
-      cudaFuncGetAttributes(&a, combine_kernel) != cudaSuccess)
+      cudaFuncGetAttributes(&a, combine_kernel<1>) != cudaSuccess ||
+      cudaFuncGetAttributes(&a, combine_kernel<CB_SLOT_BATCH_WIDE>) != cudaSuccess)
     return host::fail_cuda("decode kernels: set-up");
   return CE_OK;
 }
