@@ -50,8 +50,17 @@ POLICY_MIX = ["full", "recent", "random", "h2o_global", "h2o_per_head"]
 SLEEP_CYCLES = 2_000_000   # ~1 ms spin ahead of a timed call
 
 
-def workload(n_seqs: int, seed: int = 2026):
-    """Seeded per-sequence (ctx, policy, budget) of BASELINE config 3."""
+def workload(n_seqs: int, seed: int = 2026, first_boundary_step=None):
+    """Seeded per-sequence (ctx, policy, budget) of BASELINE config 3.
+
+    With first_boundary_step = t0, the evicting rows' boundaries are spread
+    evenly over the 2,048 steps from step t0 on (row i of E reaches one at
+    step t0 + i * 2048 // E): each context is lowered by less than 2,048
+    tokens (raised by 2,048 if that would leave it under 2,048) so that its
+    length then sits on a multiple of 2,048.  A run timed from step t0 then
+    meets its share of the eviction work -- E boundaries per 2,048 steps,
+    rounded up -- however few steps it times; with free phases a short
+    window often saw none."""
     from cache_eviction_b200.policy import EvictionConfig, canonical, sweep_split
     rng = np.random.default_rng(seed)
     specs = []
@@ -66,6 +75,13 @@ def workload(n_seqs: int, seed: int = 2026):
             p, r = sweep_split(budget, name)
             cfg = EvictionConfig(name, budget, p, r, seed=int(rng.integers(0, 1 << 31)))
         specs.append(dict(ctx=ctx, cfg=cfg, policy=pol, budget=budget))
+    if first_boundary_step is not None:
+        from cache_eviction_b200.policy import INTERVAL
+        evicting = [sp for sp in specs if sp["cfg"] is not None]
+        for i, sp in enumerate(evicting):
+            t = int(first_boundary_step) + (i * INTERVAL) // len(evicting)
+            ctx = sp["ctx"] - (sp["ctx"] + t) % INTERVAL
+            sp["ctx"] = ctx if ctx >= 2048 else ctx + INTERVAL
     return specs
 
 
@@ -269,7 +285,7 @@ def reference_arm(args, world, rank):
     from oracle import oracle
     cores = os.cpu_count() or 1
     oracle.set_threads(cores)
-    specs = workload(SEQS_PER_GPU * world)
+    specs = workload(SEQS_PER_GPU * world, first_boundary_step=args.warmup)
     per_step, info = cpu_steps(specs, args.warmup, args.steps, budget_s=REFERENCE_BUDGET_S)
     value = len(specs) / per_step
     line = {
@@ -1033,7 +1049,7 @@ def main():
         if world > 1:
             dist.destroy_process_group()
         return 0
-    specs = workload(args.seqs * max(world, SHARD_OF[0]))
+    specs = workload(args.seqs * max(world, SHARD_OF[0]), first_boundary_step=args.warmup)
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else args.steps
     steps_total = args.warmup + max(args.steps, e2e_steps)
     G, H, off = _shard(rank, world)
@@ -1084,6 +1100,7 @@ def main():
         e2.record()
         proj_ev.append((e0, e1, e2))
     bound_before = len(eng.boundary_ms)
+    events_before = sum(len(eng.rows[r].events) for r in eng.active)
     launches0 = kernels.LAUNCHES[0]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     tokens_resident = []
@@ -1124,7 +1141,7 @@ def main():
     if world > 1:
         layer_ms = {k: (max_over_ranks(v) if v is not None else None) for k, v in layer_ms.items()}
     boundary_ms = eng.boundary_ms[bound_before:]
-    n_bound_rows = sum(1 for r in eng.active for e in eng.rows[r].events)
+    n_bound_rows = sum(len(eng.rows[r].events) for r in eng.active) - events_before
     value = B * args.steps / (elapsed_ms * 1e-3)
     clock_info = clocks.summary()
     del eng
