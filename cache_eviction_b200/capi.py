@@ -63,6 +63,7 @@ SIGNATURES = {
     "ce_version": (C.c_char_p, []),
     "ce_status_string": (C.c_char_p, [C.c_int]),
     "ce_last_error": (C.c_char_p, []),
+    "ce_prepare_device": (C.c_int, []),
     "ce_fill": (C.c_int, [P, I64, P, I64, P, P, P, P, I32, I32, P, P, I32, I64, P, P, P]),
     "ce_pool_alloc": (C.c_int, [P, P, P, I64, I64, P, P, I32, I32, P, P]),
     "ce_pool_push": (C.c_int, [P, P, I64, P, I64, P, I64, I32, P, P]),

@@ -85,6 +85,12 @@ __global__ void __launch_bounds__(THREADS) fill_kernel(const Params p) {
 }  // namespace fill
 }  // namespace ce
 
+int ce::host::fill_prepare_device() {
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, ce::fill::fill_kernel) != cudaSuccess) return host::fail_cuda("fill kernel: set-up");
+  return CE_OK;
+}
+
 extern "C" int ce_fill(const int32_t* table, int64_t table_stride, const int32_t* req_to_unit,
                        int64_t r2u_stride, const int32_t* frontier, const int32_t* count,
                        const int64_t* rows, const int64_t* seq_lens, int32_t bs,

@@ -136,3 +136,11 @@ extern "C" const char* ce_status_string(int status) {
 }
 
 extern "C" const char* ce_last_error(void) { return ce::host::last_error(); }
+
+extern "C" int ce_prepare_device(void) {
+  int st = ce::host::decode_prepare_device();
+  if (st == CE_OK) st = ce::host::select_prepare_device();
+  if (st == CE_OK) st = ce::host::fill_prepare_device();
+  if (st == CE_OK) st = ce::host::pool_prepare_device();
+  return st;
+}

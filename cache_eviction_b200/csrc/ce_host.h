@@ -51,5 +51,11 @@ bool encode_rows_map(CUtensorMap* map, const void* base, uint64_t rows, uint32_t
 // its first call (defined in ce_decode.cu).  Returns a CE_* status.
 int decode_prepare_device();
 
+// The same for the selection / boundary kernels (ce_select.cu), the CSR
+// kernel (ce_fill.cu) and the unit-pool kernels (ce_pool.cu).
+int select_prepare_device();
+int fill_prepare_device();
+int pool_prepare_device();
+
 }  // namespace host
 }  // namespace ce

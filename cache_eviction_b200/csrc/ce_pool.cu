@@ -122,6 +122,14 @@ __global__ void __launch_bounds__(THREADS) push_kernel(int32_t* units, int32_t* 
 
 using namespace ce;
 
+int ce::host::pool_prepare_device() {
+  cudaFuncAttributes a;
+  if (cudaFuncGetAttributes(&a, pool::alloc_kernel) != cudaSuccess ||
+      cudaFuncGetAttributes(&a, pool::push_kernel) != cudaSuccess)
+    return host::fail_cuda("unit pool kernels: set-up");
+  return CE_OK;
+}
+
 extern "C" int ce_pool_alloc(int32_t* units, int32_t* top, int32_t* req_to_unit, int64_t r2u_stride,
                              int64_t r2u_width, const int64_t* rows, const int64_t* seq_lens, int32_t bs,
                              int32_t page_size, int32_t* err, void* stream) {

@@ -2354,6 +2354,24 @@ __global__ void reservoir_kernel(const int32_t* pos, int layers, int heads, int 
 using namespace ce;
 using namespace ce::sel;
 
+int ce::host::select_prepare_device() {
+  // cudaFuncGetAttributes loads a kernel under lazy module loading.
+  cudaFuncAttributes a;
+  const void* fns[] = {
+      reinterpret_cast<const void*>(bsel_kernel<true>), reinterpret_cast<const void*>(bsel_kernel<false>),
+      reinterpret_cast<const void*>(bvalidate_kernel), reinterpret_cast<const void*>(bgather_kernel<true>),
+      reinterpret_cast<const void*>(bgather_kernel<false>), reinterpret_cast<const void*>(bscatter_kernel<true>),
+      reinterpret_cast<const void*>(bscatter_kernel<false>), reinterpret_cast<const void*>(bfinish_kernel),
+      reinterpret_cast<const void*>(bzero_kernel), reinterpret_cast<const void*>(hsum_kernel),
+      reinterpret_cast<const void*>(unit_sum_kernel), reinterpret_cast<const void*>(brecord_kernel),
+      reinterpret_cast<const void*>(choose_seg_kernel<true>), reinterpret_cast<const void*>(choose_seg_kernel<false>),
+      reinterpret_cast<const void*>(choose_status_kernel), reinterpret_cast<const void*>(gather_scores_kernel),
+      reinterpret_cast<const void*>(reservoir_kernel)};
+  for (const void* f : fns)
+    if (cudaFuncGetAttributes(&a, f) != cudaSuccess) return host::fail_cuda("selection kernels: set-up");
+  return CE_OK;
+}
+
 namespace {
 size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
 

@@ -110,6 +110,8 @@ class RaggedDecodeEngine:
         self.new_score_events()
         self._scores_pending = False
         if alloc_pools:
+            # kernels loaded now rather than inside the first step that needs them
+            kernels.prepare_device(dev)
             kernels.reserve_boundary(dev, min(max_rows, boundary_rows), layers, kv_heads, page_size,
                                      r2u_width, pos_cap,
                                      self.global_G if process_group is not None else 0, hazard_bytes)

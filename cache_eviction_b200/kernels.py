@@ -367,6 +367,13 @@ def boundary(table, req_to_unit, frontier, count, pos, scores, k_ptrs, v_ptrs, k
     return result, freed
 
 
+def prepare_device(device):
+    """Load the library's decode, boundary, CSR and pool kernels on `device`
+    (ce_prepare_device), so that no later call pays the module load."""
+    with torch.cuda.device(torch.device(device)):
+        capi.check(capi.load().ce_prepare_device(), "ce_prepare_device")
+
+
 def reserve_boundary(device, rows, layers, kv_heads, page_size, max_cols, max_width, global_heads,
                      hazard_bytes):
     """Allocate the ce_boundary workspace for the given batch bounds ahead of use."""

@@ -99,6 +99,14 @@ const char* ce_status_string(int status);
 /* Detail of the last failing call made by this host thread. */
 const char* ce_last_error(void);
 
+/* Load the decode, selection / boundary, CSR and unit-pool kernels on the
+ * current device and set their launch attributes, which their entry points
+ * otherwise do on first use.  Under lazy module loading (the CUDA 12 default)
+ * a first ce_boundary call spends ~5 ms loading its kernels; a server calls
+ * this once per device at start-up so no decode step pays that.  Launches
+ * nothing and allocates no workspace. */
+int ce_prepare_device(void);
+
 /* ---- K4: ragged CSR page table -------------------------------------------
  * Replaces gstar_evict.fill (runtime:136-152) and the two
  * create_flashinfer_kv_indices_triton launches it makes.  For batch entry b

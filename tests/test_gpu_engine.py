@@ -110,3 +110,10 @@ def test_deferred_scores_equal_inline_scores(page):
     assert torch.equal(o1, o2)
     assert torch.equal(s_inline, s_defer)
     assert not torch.equal(s_inline, base)
+
+
+def test_prepare_device_loads_kernels():
+    """ce_prepare_device succeeds (and is idempotent) on the current device."""
+    from cache_eviction_b200 import kernels
+    kernels.prepare_device(DEV)
+    kernels.prepare_device(DEV)
