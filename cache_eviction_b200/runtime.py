@@ -81,6 +81,9 @@ class State:
         rows, width = self.req_to_token.shape
         device = self.req_to_token.device
         self.device = device
+        if device.type == "cuda":
+            # the library's kernels are loaded now, not inside the first boundary
+            kernels.prepare_device(device)
         self.page_size = int(getattr(backend, "page_size", 1) or 1)
         self.full_layers = sorted(i for i, (_, swa) in self.pool.layers_mapping.items() if not swa)
         self.index = {layer: i for i, layer in enumerate(self.full_layers)}
