@@ -178,6 +178,25 @@ def test_decode_batch1_long_sequence_vs_oracle(G, page, mode):
     np.testing.assert_allclose(s_g, s_c, rtol=1e-3, atol=1e-6)
 
 
+@pytest.mark.parametrize("G,page,n", [(8, 16, 40), (2, 16, 90), (1, 16, 160), (8, 1, 40)])
+def test_decode_large_batch_vs_oracle(G, page, n):
+    """Batches with at least as many (sequence, KV head) pairs as attention
+    CTAs (the combine's one-slot, 64-register variant) at 8, 2 and 1 KV heads
+    and page size 1: ragged lengths, some spanning several CTAs, an empty and
+    a one-token sequence."""
+    rng = np.random.default_rng(70 + G + page)
+    lengths = rng.integers(1, 2500 if page == 16 else 900, n).tolist()
+    lengths[3], lengths[7], lengths[11] = 0, 1, 9000 if page == 16 else 3000
+    modes = rng.integers(0, 3, n).tolist()
+    c = _decode_case(lengths, G, page, modes, seed=70 + G + page)
+    o_g, s_g, l_g = _run_decode_gpu(c, 0.125, zero_new=True)
+    o_c, s_c, l_c = _run_decode_oracle(c, 0.125, zero_new=True)
+    for i in range(n):
+        assert _rel(o_g[i], o_c[i]) < 1e-3, (i, _rel(o_g[i], o_c[i]))
+    np.testing.assert_allclose(l_g, l_c, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(s_g, s_c, rtol=1e-3, atol=1e-6)
+
+
 def test_decode_token_mode_vs_oracle():
     lengths = [1, 2, 37, 1500, 3001, 513]
     c = _decode_case(lengths, 8, 1, [1, 2, 1, 2, 1, 0], seed=11)
