@@ -88,6 +88,12 @@ class RaggedDecodeEngine:
         self.free_top_dev = torch.zeros(1, dtype=torch.int32, device=dev)
         self.free_top = 0
         self.boundary_ms: list = []
+        # advance() calls until some evicting row reaches a boundary (None:
+        # unknown), so due() scans the rows only when one can be due
+        self._due_in = None
+        # exact CSR need at some advance count (_ensure_capacity); None: unknown
+        self._cap_base = None
+        self._advances = 0
         self.last_batch: Optional[dict] = None
         # The boundary workspace is sized up front for batches of up to
         # `boundary_rows` rows, so no device allocation falls inside the decode
@@ -138,6 +144,7 @@ class RaggedDecodeEngine:
         self.join_scores()
         self.rows[row] = Row(cfg=cfg, n=n, last_boundary=last_boundary, frontier=frontier_units,
                              count=count_units)
+        self._due_in = self._cap_base = None
         self.mode[row] = cfg.score_mode if cfg is not None else capi.CE_MODE_NONE
         self.frontier[row] = frontier_units
         self.count[row] = count_units
@@ -195,12 +202,14 @@ class RaggedDecodeEngine:
         finally:
             for r in due:
                 self.rows[r].n = lengths[r]
+            self._due_in = self._cap_base = None
 
     def retire(self, row: int):
         """A finished request: its resident units (compacted table and tail)
         return to the free stack; the row leaves the batch."""
         self.join_scores()
         r = self.rows.pop(row)
+        self._due_in = self._cap_base = None
         tail_end = -(-r.n // self.P)
         owned = torch.cat([self.table[row, :r.count], self.r2u[row, r.frontier:tail_end]]).view(1, -1)
         k = int(owned.shape[1])
@@ -236,21 +245,40 @@ class RaggedDecodeEngine:
         return row.count * self.P + row.n - row.frontier * self.P
 
     def _ensure_capacity(self, extra_tokens: int = 1):
+        # A row gains at most one unit per P tokens, so from the last exact
+        # count the need is bounded without a pass over the rows; the pass
+        # (512 rows at eight ranks) runs only when the bound nears capacity.
+        if self._cap_base is not None:
+            need0, adv0, e0, nrows = self._cap_base
+            grown = max(0, self._advances - adv0 + extra_tokens - e0)
+            if need0 + nrows * (grown // self.P + 1) <= self.kv_indices.numel():
+                return
         need = sum(self.resident_units(r, extra_tokens) for r in self.active) + 16
+        self._cap_base = (need, self._advances, extra_tokens, len(self.active))
         if self.kv_indices.numel() < need:
             self.join_scores()
             self.kv_indices = torch.zeros(int(need * 1.25), dtype=torch.int32, device=self.device)
 
     # -------------------------------------------------------- boundaries
     def due(self) -> list:
-        """Rows whose length sits on a boundary not yet taken (runtime:706)."""
-        out = []
+        """Rows whose length sits on a boundary not yet taken (runtime:706).
+        Every row grows by one token per advance(), so the scan also notes how
+        many advances it is until the next row can be due; until then due()
+        returns at once (a 512-row scan per step was host time the GPU waited
+        for at eight ranks)."""
+        if self._due_in is not None and self._due_in > 0:
+            return []
+        out, nxt = [], INTERVAL
         for r in self.active:
             row = self.rows[r]
             if row.cfg is None:
                 continue
-            if row.n % INTERVAL == 0 and row.n > row.last_boundary:
+            k = row.n % INTERVAL
+            if k == 0 and row.n > row.last_boundary:
                 out.append(r)
+            else:
+                nxt = min(nxt, INTERVAL - k if k else INTERVAL)
+        self._due_in = None if out else nxt
         return out
 
     def run_boundaries(self, rows: list, cursors: Optional[dict] = None, live: bool = True,
@@ -328,6 +356,7 @@ class RaggedDecodeEngine:
             # the leftovers go back to the free stack straight from the device result
             kernels.pool_push(self.free_stack, self.free_top_dev, freed, result[:, 3], self.err)
             self.free_top += pushed
+        self._due_in = self._cap_base = None
         return res
 
     # ------------------------------------------------------------ decode
@@ -400,6 +429,9 @@ class RaggedDecodeEngine:
             row = self.rows[r]
             row.n += 1
             need += (row.n - 1) % self.P == 0
+        self._advances += 1
+        if self._due_in is not None:
+            self._due_in -= 1
         if need > self.free_top:
             raise RuntimeError(f"unit pool exhausted: {need} units wanted, {self.free_top} free")
         self.free_top -= need
