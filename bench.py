@@ -1,6 +1,6 @@
 """Decode throughput of the eviction hot path on B200 (one JSON line on rank 0).
 
-Workload ("ragged continuous batch"): 64 sequences per GPU
+Workload (benchmark config 3, "ragged continuous batch"): 64 sequences per GPU
 with contexts log-uniform over 2K-64K tokens in 16-token pages, per-sequence
 budgets from {2K, 4K, 8K, 16K, 32K} (P = R = B/4, recent: R = 3B/4) and
 policies mixed over full / recent / random / H2O global / H2O per-head, on the
@@ -51,7 +51,7 @@ SLEEP_CYCLES = 2_000_000   # ~1 ms spin ahead of a timed call
 
 
 def workload(n_seqs: int, seed: int = 2026, first_boundary_step=None):
-    """Seeded per-sequence (ctx, policy, budget) of BASELINE config 3.
+    """Seeded per-sequence (ctx, policy, budget) of benchmark config 3.
 
     With first_boundary_step = t0, the evicting rows' boundaries are spread
     evenly over the 2,048 steps from step t0 on (row i of E reaches one at
@@ -498,7 +498,7 @@ def run_no_score(args, specs, steps_total, world, rank, group, device, q, out, s
 
 
 def decode4_microbench(world, rank, group, device, barrier, max_over_ranks, steps=2048, warmup=8, seg=64):
-    """BASELINE config 4's decode phase: one sequence after an 80,000-token
+    """benchmark config 4's decode phase: one sequence after an 80,000-token
     prompt, per-head H2O (head_sum) with 512 prefix + 4,096 recent + 24,064
     scored tokens (28,672 resident after each boundary), 12 full layers of
     this rank's heads (attention + H2O score, no output projection), `steps`
@@ -714,7 +714,7 @@ def _shard_offset(rank, world):
 
 
 def model2_microbench(world, rank, device, max_len=16384, prompt_len=1024, seg=512, seed=2):
-    """a gpt-oss-20b-shaped decoder with random bf16 weights
+    """benchmark config 2: a gpt-oss-20b-shaped decoder with random bf16 weights
     (24 layers alternating a 128-token sliding window and full attention,
     hidden 2880, 32 experts top 4, vocabulary 201,088; cache_eviction_b200.oss20b),
     batch 1, a 1,024-token prompt of seeded uniform token ids, greedy decoding
@@ -784,7 +784,7 @@ PREFILL_PREFIXES = (0, 8192, 26624)   # resident tokens before a chunk; 26,624 +
 
 
 def prefill_microbench(world, rank, device, reps=5, cpu=False, prefixes=PREFILL_PREFIXES):
-    """one 2,048-token prefill chunk of one layer scored by
+    """benchmark config 4: one 2,048-token prefill chunk of one layer scored by
     ce_prefill_scores against a resident prefix of 0 / 8,192 / 26,624 tokens
     (16-token pages, this rank's KV heads, no eviction inside the chunk).
     Algorithmic work per call: two Q.K^T passes over the visible (query, key)
@@ -914,7 +914,7 @@ def select_token_microbench(world, rank, device, reps=3, rows=32):
 
 
 def evict_microbench(world, rank, device, reps=3, rows=32, page=PAGE):
-    """one eviction step (select + compaction) over 32 rows x
+    """benchmark config 5: one eviction step (select + compaction) over 32 rows x
     this rank's KV heads x 65,536-token contexts (4096 pages of 16 tokens, or
     with page=1 the reference's own token slots), fp32 scores lognormal(0, 2),
     P = R = B/4, for H2O global / H2O per-head / random at budgets 2K..32K

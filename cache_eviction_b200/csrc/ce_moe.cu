@@ -1,5 +1,5 @@
 // Batch-1 mixture-of-experts GEMVs for the gpt-oss-20b-shaped decoder of
-// BASELINE config 2 (a model harness around the eviction path, not part of
+// benchmark config 2 (a model harness around the eviction path, not part of
 // the reference's overlay).  The router's top-k expert ids stay on the
 // device, so a whole decode step can be one CUDA graph:
 //

@@ -1,6 +1,6 @@
 """A gpt-oss-20b-shaped decoder with random weights, around the eviction engine.
 
-24 layers alternating a 128-token sliding window (even
+benchmark config 2: 24 layers alternating a 128-token sliding window (even
 layers) and full attention (odd layers), 64 query / 8 KV heads of 64, hidden
 2880, attention sinks, a mixture of 32 SwiGLU experts (top 4, width 2880) per
 layer and a 201,088-token vocabulary, all bf16 and randomly initialised (no

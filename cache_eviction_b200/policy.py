@@ -25,7 +25,7 @@ POLICY_IDS = {"prefix_sliding_2048": capi.CE_POLICY_PREFIX_SLIDING,
               "head_sum_2048": capi.CE_POLICY_HEAD_SUM,
               "head_max_sum_2048": capi.CE_POLICY_HEAD_MAX,
               "h2o_global_2048": capi.CE_POLICY_H2O_GLOBAL}
-# short names used by the ragged-batch configuration (BASELINE configs 3 and 5)
+# short names used by the ragged-batch configuration (benchmark configs 3 and 5)
 ALIASES = {"recent": "prefix_sliding_2048", "random": "random_2048",
            "reservoir": "random_reservoir_2048", "h2o_per_head": "head_sum_2048",
            "h2o_max": "head_max_sum_2048", "h2o_global": "h2o_global_2048"}

@@ -1,5 +1,5 @@
 /* Model-harness entry points of libce_b200.so (batch-1 mixture-of-experts
- * GEMVs for the gpt-oss-20b-shaped decoder of BASELINE config 2).  They are
+ * GEMVs for the gpt-oss-20b-shaped decoder of benchmark config 2).  They are
  * not part of the eviction overlay: the reference runs that model inside
  * SGLang, whose MoE layers have no counterpart here.  Conventions as in
  * ce_api.h (device pointers, a cudaStream_t as void*, int status). */

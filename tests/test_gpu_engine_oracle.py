@@ -19,7 +19,7 @@ the same uniforms ("bit-exact given identical scores and draws").  The test
 writes each new token's K and V into its page before the layers run, as the
 serving loop does.
 
-Workloads: BASELINE config 1 (one layer, 64 query / 8 KV heads, batch 1, a
+Workloads: benchmark config 1 (one layer, 64 query / 8 KV heads, batch 1, a
 4,096-token cache, per-head H2O at budget 2048 = 512 + 512 + 1024, 256 decode
 steps), once from a never-evicted cache and once from a cache evicted at
 4,096 whose next boundary works over kept plus new pages; with config 1 the

@@ -1,4 +1,4 @@
-"""The gpt-oss-20b-shaped decoder of BASELINE config 2 (cache_eviction_b200.oss20b)
+"""The gpt-oss-20b-shaped decoder of benchmark config 2 (cache_eviction_b200.oss20b)
 on a small configuration of the same architecture (4 layers alternating a
 16-token sliding window and full attention, 64 query / 8 KV heads of 64,
 hidden 256, 8 SwiGLU experts top 2, vocabulary 1,000), against a plain
