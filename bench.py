@@ -1010,9 +1010,11 @@ def main():
                     help="skip the config-5 eviction-step leg")
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (small cases for profiling)")
-    ap.add_argument("--legs", default="decode,e2e,noscore,cb3,model2,decode4,prefill4,evict5,select1,evict1",
-                    help="legs to run; without 'decode' only the listed microbenchmarks run "
-                         "and one JSON line with their results is printed (profiling)")
+    ap.add_argument("--legs", default=None,
+                    help="legs to run (default: every leg on one GPU; the config-3 headline, its "
+                         "end-to-end pass and the paired unscored pass on several -- the other legs "
+                         "are one-GPU shapes); without 'decode' only the listed microbenchmarks "
+                         "run and one JSON line with their results is printed (profiling)")
     ap.add_argument("--evict-rows", type=int, default=32, help="rows of the config-5 leg")
     ap.add_argument("--score-overlap", action="store_true",
                     help="score each layer's pages on a second stream (engine overlap_scores)")
@@ -1023,6 +1025,10 @@ def main():
     ap.add_argument("--prefill-prefixes", default=",".join(map(str, PREFILL_PREFIXES)),
                     help="resident prefixes of the config-4 leg")
     args = ap.parse_args()
+    if args.legs is None:
+        several = int(os.environ.get("WORLD_SIZE", "1")) > 1
+        args.legs = ("decode,e2e,noscore" if several else
+                     "decode,e2e,noscore,cb3,model2,decode4,prefill4,evict5,select1,evict1")
     legs = set(args.legs.split(","))
     SHARD_OF[0] = args.shard_of
     ORDERED_UNITS[0] = args.ordered_units
