@@ -13,9 +13,10 @@
 // because both walks are monotone.  combine_kernel then merges each
 // sequence's records with the sink into the output and the log-sum-exp.
 //
-// Inside a CTA: warp 8 is the producer.  It issues one 2D bulk-tensor (TMA)
-// load per KV page for K and one for V (box = the page's G*P rows of 128 B,
-// 128-byte swizzle) into a ring of shared-memory stages guarded by mbarriers.
+// Inside a CTA: warps 8..11 are the producers (stage k is issued by warp
+// 8 + k % 4).  They issue one 2D bulk-tensor (TMA) load per KV page for K and
+// one for V (box = the page's G*P rows of 128 B, 128-byte swizzle) into a
+// ring of shared-memory stages guarded by mbarriers.
 // Warps 0..7 consume: warp w owns KV head g = w % G and 16 tokens of the
 // stage; they copy their K and V fragments to registers and release the stage
 // before doing any math.  S^T = K Q^T and O^T += V^T P^T run on m16n8k16 bf16
