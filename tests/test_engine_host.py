@@ -95,3 +95,23 @@ def test_csr_capacity_bound_never_undershoots():
         eng._ensure_capacity(0)
         exact = sum(eng.resident_units(r, 0) for r in eng.active) + 16
         assert eng.kv_indices.numel() >= exact, step
+
+
+def test_workload_spreads_boundaries_over_the_timed_window():
+    """bench.workload(first_boundary_step=W): the evicting rows reach their
+    boundaries one by one from step W on, evenly spaced, so a window of K
+    timed steps holds ceil(K * E / 2048) of them; contexts stay >= 2,048 and
+    move by less than 2,048 tokens."""
+    import math
+    import bench
+    free = bench.workload(64)
+    for W in (3, 5, 8):
+        specs = bench.workload(64, first_boundary_step=W)
+        evicting = [(a, b) for a, b in zip(free, specs) if b["cfg"] is not None]
+        E = len(evicting)
+        steps = sorted((-b["ctx"]) % INTERVAL for _, b in evicting)
+        assert steps[0] == W
+        for a, b in evicting:
+            assert b["ctx"] >= 2048 and abs(a["ctx"] - b["ctx"]) < INTERVAL
+        for K in (1, 20, 64, 512):
+            assert sum(W <= s < W + K for s in steps) == math.ceil(K * E / INTERVAL), (W, K)
